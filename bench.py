@@ -1,0 +1,658 @@
+#!/usr/bin/env python3
+"""Benchmark of the W8A8 matmul hot path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload prefill1b|decode270m|lmhead4b]
+
+Workloads (synthetic seeded data, no checkpoints):
+  prefill1b   configs[1], the default: Gemma-3-1B-shaped prefill, M=512
+              tokens, 26 layers.  One step = every layer's quantize_acts +
+              Q/K/V, O, up/gate, down int8 GEMMs (gemma.c:5034-5391), inputs
+              1% outlier channels x20.  Metric unit: int8 TOPS (2*M*N*K).
+              At N>1 every rank runs its own replica (weak scaling).
+  decode270m  configs[0]: Gemma-3-270m decode, batch 1: 18 layers of
+              quantize_act + Q/K/V multi-GEMV, O, gate/up multi-GEMV, down,
+              then the 262144-row lm_head GEMV.  Unit: HBM GB/s.
+  lmhead4b    configs[2]: lm_head GEMV 262144 x 2560, batch 1, rows sharded
+              over the ranks and all-gathered with NCCL (strong scaling).
+
+`value` is measured with inputs resident in HBM, one CUDA graph replay per
+step, CUDA events on the launching stream, max over ranks.  `e2e` is the same
+metric through the host-pointer C ABI (gcu_quantize_acts / gcu_gemm_int8 /
+gcu_gemv_int8 on pinned host buffers, copies inside the timed region).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "gemma.c_b200"))
+
+METRIC = "W8A8 matmul: decode GEMV HBM GB/s, prefill GEMM int8 TOPS (% roofline)"
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+class Clocks:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+def dist_setup(args):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# workloads
+# ---------------------------------------------------------------------------
+class Prefill:
+    """1B-shaped W8A8 prefill, M tokens, all layers."""
+    name = "prefill1b"
+
+    def __init__(self, m=512, cfg="1b", seed=0):
+        import synth
+        self.cfg = synth.CONFIGS[cfg]
+        self.m = m
+        self.groups = synth.layer_groups(self.cfg)
+        self.layers = self.cfg["layers"]
+        self.ops = synth.layer_ops(self.cfg, m) * self.layers
+        self.seed = seed
+
+    def config(self):
+        return {"workload": "prefill1b (configs[1]): Gemma-3-1B-shaped W8A8 prefill GEMM set",
+                "tokens_m": self.m, "layers": self.layers, "d_model": self.cfg["dim"], "ffn": self.cfg["ffn"],
+                "calls_per_layer": "quantize_acts x4 + GEMM {QKV fused, O, up+gate fused, down}",
+                "inputs": "1% outlier channels x20; per-layer weights+activations ~1.3 GB > L2 (no flush)"}
+
+    def build(self, device):
+        import torch
+        import synth
+        gen = torch.Generator(device=device).manual_seed(1234 + self.seed)
+        m = self.m
+        self.L = []
+        for _ in range(self.layers):
+            layer = []
+            for k, jobs in self.groups:
+                x = synth.activations_torch(m, k, gen, device, outliers=True)
+                q = torch.empty((m, k), dtype=torch.int8, device=device)
+                s = torch.empty(m, dtype=torch.float32, device=device)
+                ws = []
+                for _, n in jobs:
+                    w, sc = synth.weight_torch(n, k, gen, device)
+                    ws.append((w, sc))
+                layer.append({"x": x, "q": q, "s": s, "k": k, "w": ws})
+            self.L.append(layer)
+        # output buffers (fp32) per group, shared by the layers
+        self.out = [[torch.empty((m, n), dtype=torch.float32, device=device) for _, n in jobs]
+                    for _, jobs in self.groups]
+
+    def step(self, gcu, stream=None, ev=None):
+        """Enqueue one step. `ev(kind)` brackets each launch when profiling."""
+        m = self.m
+        for layer in self.L:
+            for gi, g in enumerate(layer):
+                if ev:
+                    ev("quant", 5 * m * g["k"] + 4 * m, 0)
+                gcu.dev_quantize_acts(g["q"], g["s"], g["x"], m, g["k"], stream=stream)
+                if ev:
+                    ev(None)
+                jobs = [(w, sc, o) for (w, sc), o in zip(g["w"], self.out[gi])]
+                if ev:
+                    nsum = sum(w.shape[0] for w, _ in g["w"])
+                    k = g["k"]
+                    ev("gemm", nsum * k + 4 * nsum + m * k + 4 * m + 4 * m * nsum, 2 * m * nsum * k)
+                if len(jobs) == 1:
+                    w, sc, o = jobs[0]
+                    gcu.dev_gemm_int8(o, w, sc, g["q"], g["s"], m, w.shape[0], g["k"], stream=stream)
+                else:
+                    gcu.dev_gemm_int8_multi(jobs, g["q"], g["s"], m, g["k"], stream=stream)
+                if ev:
+                    ev(None)
+
+    launches_per_step = property(lambda self: self.layers * 2 * len(self.groups))
+
+    # ---- end to end through the host-pointer ABI --------------------------
+    def build_host(self):
+        import numpy as np
+        import torch
+        self.H = []
+        for layer in self.L:
+            hl = []
+            for g in layer:
+                x = torch.empty(g["x"].shape, dtype=torch.float32, pin_memory=True)
+                x.copy_(g["x"].cpu())
+                ws = []
+                for w, sc in g["w"]:
+                    wh = w.cpu().numpy()
+                    sh = sc.cpu().numpy()
+                    ws.append((wh, sh))
+                hl.append({"x": x.numpy(), "k": g["k"], "w": ws,
+                           "q": torch.empty((self.m, g["k"]), dtype=torch.int8, pin_memory=True).numpy(),
+                           "s": torch.empty(self.m, dtype=torch.float32, pin_memory=True).numpy()})
+            self.H.append(hl)
+        self.Hout = [[torch.empty((self.m, n), dtype=torch.float32, pin_memory=True).numpy() for _, n in jobs]
+                     for _, jobs in self.groups]
+        self.h2d = self.d2h = 0
+        for hl in self.H:
+            for gi, g in enumerate(hl):
+                mk = self.m * g["k"]
+                self.h2d += 4 * mk + (mk + 4 * self.m) * len(g["w"])
+                self.d2h += mk + 4 * self.m + sum(4 * self.m * w.shape[0] for w, _ in g["w"])
+        return self.H
+
+    def register_host(self, gcu):
+        for hl in self.H:
+            for g in hl:
+                for w, s in g["w"]:
+                    gcu.register_weight(w, s)
+
+    def step_host(self, gcu):
+        lib = gcu.lib()
+        m = self.m
+        for hl in self.H:
+            for gi, g in enumerate(hl):
+                k = g["k"]
+                rc = lib.gcu_quantize_acts(g["q"].ctypes.data, g["s"].ctypes.data, g["x"].ctypes.data, 0, m, k)
+                if rc:
+                    raise RuntimeError(lib.gcu_last_error().decode())
+                for (w, s), o in zip(g["w"], self.Hout[gi]):
+                    rc = lib.gcu_gemm_int8(o.ctypes.data, 0, w.ctypes.data, 0, s.ctypes.data, g["q"].ctypes.data,
+                                           0, g["s"].ctypes.data, m, w.shape[0], k)
+                    if rc:
+                        raise RuntimeError(lib.gcu_last_error().decode())
+
+    # ---- CPU reference ---------------------------------------------------------
+    def cpu_sample(self, R, layers):
+        """Time `layers` layers of the same calls in the reference's own
+        quantize_acts + gemm_int8 (OpenMP over all threads)."""
+        import numpy as np
+        import synth
+        data = []
+        for li in range(layers):
+            layer = []
+            for gi, (k, jobs) in enumerate(self.groups):
+                x = synth.activations(9000 + 10 * li + gi, self.m, k, outliers=True)
+                ws = [synth.weight(9500 + 10 * li + 3 * gi + j, n, k) for j, (_, n) in enumerate(jobs)]
+                outs = [np.empty((self.m, n), np.float32) for _, n in jobs]
+                layer.append((x, ws, outs))
+            data.append(layer)
+        ops = synth.layer_ops(self.cfg, self.m) * layers
+
+        def run():
+            for layer in data:
+                for x, ws, outs in layer:
+                    q, s = R.quantize_acts(x)
+                    for (w, sc), o in zip(ws, outs):
+                        R.gemm_int8(w, sc, q, s, dst=o)
+        return ops, run
+
+
+class Decode:
+    """Gemma-3-270m decode, batch 1, plus the lm_head."""
+    name = "decode270m"
+
+    def __init__(self, cfg="270m", seed=0):
+        import synth
+        self.cfg = synth.CONFIGS[cfg]
+        self.groups = synth.layer_groups(self.cfg)
+        self.layers = self.cfg["layers"]
+        self.bytes = (synth.layer_weight_bytes(self.cfg) * self.layers +
+                      self.cfg["vocab"] * (self.cfg["dim"] + 4))
+        self.seed = seed
+
+    def config(self):
+        return {"workload": "decode270m (configs[0]): Gemma-3-270m W8A8 decode, batch 1, 18 layers + lm_head",
+                "vocab": self.cfg["vocab"], "d_model": self.cfg["dim"],
+                "inputs": "271 MB of weights per token > L2 (no flush)"}
+
+    def build(self, device):
+        import torch
+        import synth
+        gen = torch.Generator(device=device).manual_seed(99 + self.seed)
+        self.L = []
+        for _ in range(self.layers):
+            layer = []
+            for k, jobs in self.groups:
+                layer.append({"x": synth.activations_torch(1, k, gen, device),
+                              "q": torch.empty(k, dtype=torch.int8, device=device),
+                              "s": torch.empty(1, dtype=torch.float32, device=device), "k": k,
+                              "w": [synth.weight_torch(n, k, gen, device) for _, n in jobs],
+                              "o": [torch.empty(n, dtype=torch.float32, device=device) for _, n in jobs]})
+            self.L.append(layer)
+        d = self.cfg["dim"]
+        self.head = {"x": synth.activations_torch(1, d, gen, device), "q": torch.empty(d, dtype=torch.int8, device=device),
+                     "s": torch.empty(1, dtype=torch.float32, device=device),
+                     "w": synth.weight_torch(self.cfg["vocab"], d, gen, device),
+                     "o": torch.empty(self.cfg["vocab"], dtype=torch.float32, device=device)}
+
+    def step(self, gcu, stream=None, ev=None):
+        for layer in self.L:
+            for g in layer:
+                k = g["k"]
+                if ev:
+                    ev("quant", 5 * k + 4, 0)
+                gcu.dev_quantize_acts(g["q"], g["s"], g["x"], 1, k, stream=stream)
+                if ev:
+                    ev(None)
+                    nsum = sum(w.shape[0] for w, _ in g["w"])
+                    ev("gemv", nsum * (k + 8) + k + 4, 2 * nsum * k)
+                gcu.dev_gemv_int8_multi([(w, sc, o) for (w, sc), o in zip(g["w"], g["o"])], g["q"], g["s"], k,
+                                        stream=stream)
+                if ev:
+                    ev(None)
+        h = self.head
+        d = self.cfg["dim"]
+        if ev:
+            ev("quant", 5 * d + 4, 0)
+        gcu.dev_quantize_acts(h["q"], h["s"], h["x"], 1, d, stream=stream)
+        if ev:
+            ev(None)
+            n = self.cfg["vocab"]
+            ev("gemv", n * (d + 8) + d + 4, 2 * n * d)
+        gcu.dev_gemv_int8(h["o"], h["w"][0], h["w"][1], h["q"], h["s"], self.cfg["vocab"], d, stream=stream)
+        if ev:
+            ev(None)
+
+    launches_per_step = property(lambda self: self.layers * 2 * len(self.groups) + 2)
+
+
+class LmHead:
+    """lm_head GEMV 262144 x 2560, rows sharded over ranks."""
+    name = "lmhead4b"
+
+    def __init__(self, world, rank, vocab=262144, dim=2560, batch=1):
+        self.world, self.rank = world, rank
+        self.n, self.k, self.b = vocab, dim, batch
+        self.bytes = vocab * (dim + 4) + batch * (dim + 4) + 4 * batch * vocab
+
+    def config(self):
+        return {"workload": f"lmhead4b (configs[2]): lm_head GEMV {self.n} x {self.k}, batch {self.b}, "
+                            f"rows sharded over {self.world} GPU(s) + NCCL all-gather",
+                "inputs": "672 MB of weights > L2 (no flush)"}
+
+    def build(self, device):
+        import torch
+        import synth
+        gen = torch.Generator(device=device).manual_seed(7 + self.rank)
+        nl = self.n // self.world
+        self.w, self.ws = synth.weight_torch(nl, self.k, gen, device)
+        x = synth.activations_torch(self.b, self.k, torch.Generator(device=device).manual_seed(5), device)
+        self.q = torch.empty((self.b, self.k), dtype=torch.int8, device=device)
+        self.s = torch.empty(self.b, dtype=torch.float32, device=device)
+        self.x = x
+        self.y = torch.empty((self.b, self.n), dtype=torch.float32, device=device)
+        self.work = torch.empty((self.b, self.n), dtype=torch.float32, device=device)
+
+    def step(self, gcu, stream=None, ev=None):
+        gcu.dev_quantize_acts(self.q, self.s, self.x, self.b, self.k, stream=stream)
+        if self.world == 1:
+            if ev:
+                ev("gemv", self.bytes, 2 * self.b * self.n * self.k)
+            gcu.dev_gemm_int8(self.y, self.w, self.ws, self.q, self.s, self.b, self.n, self.k, stream=stream)
+            if ev:
+                ev(None)
+        else:
+            gcu.dev_gemm_int8_rowshard(self.y, self.work, self.w, self.ws, self.q, self.s, self.b, self.n,
+                                       self.k, stream=stream)
+
+    launches_per_step = property(lambda self: 2)
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    world, rank, local = dist_setup(args)
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    import gcu
+    gcu.init(local)
+    peaks = load_peaks()
+    if args.workload == "prefill1b":
+        wl = Prefill(seed=rank)
+    elif args.workload == "decode270m":
+        wl = Decode(seed=rank)
+    else:
+        wl = LmHead(world, rank)
+        if world > 1:
+            uid = bytearray(128)
+            if rank == 0:
+                uid = bytearray(gcu.comm_unique_id())
+            import torch.distributed as dist
+            obj = [bytes(uid)]
+            dist.broadcast_object_list(obj, src=0)
+            gcu.comm_init(rank, world, obj[0])
+    wl.build(device)
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.Stream(device)
+    # eager warm-up (allocates the split-K workspace before capture)
+    with torch.cuda.stream(stream):
+        wl.step(gcu)
+    stream.synchronize()
+    gcu.check_device()
+
+    use_graph = not (isinstance(wl, LmHead) and world > 1)
+    graph = None
+    if use_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            wl.step(gcu)
+    torch.cuda.synchronize()
+
+    def one():
+        if graph is not None:
+            graph.replay()
+        else:
+            with torch.cuda.stream(stream):
+                wl.step(gcu)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            one()
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = Clocks(local)
+    clocks.start()
+    time.sleep(0.3)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps):
+            one()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = e0.elapsed_time(e1) / args.steps
+    ms = max_over_ranks(ms, world)
+    clk = clocks.stop()
+    gcu.check_device()
+
+    # per-kernel durations: the same step, eager, each launch bracketed by
+    # CUDA events on the launching stream
+    prof = {}
+    pending = []
+
+    def ev(kind, nbytes=0, ops=0):
+        if kind is None:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record(stream)
+            pending[-1][3] = e
+        else:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record(stream)
+            pending.append([kind, nbytes, ops, None, e])
+
+    psteps = max(1, min(args.steps, 5))
+    with torch.cuda.stream(stream):
+        for _ in range(psteps):
+            wl.step(gcu, ev=ev)
+    torch.cuda.synchronize()
+    for kind, nbytes, ops, e_end, e_start in pending:
+        d = prof.setdefault(kind, {"launches": 0, "ms": 0.0, "bytes": 0, "ops": 0})
+        d["launches"] += 1
+        d["ms"] += e_start.elapsed_time(e_end)
+        d["bytes"] += nbytes
+        d["ops"] += ops
+
+    out = {"metric": METRIC, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": ms, "higher_is_better": True, "vs_baseline": None, "data": "synthetic",
+           "impl": "ours"}
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+    if isinstance(wl, Prefill):
+        out.update(value=wl.ops * world / (ms * 1e-3) / 1e12, unit="int8 TOPS", dtype="int8 (int32 accum, fp32 out)",
+                   scaling="weak")
+        cfg = wl.config()
+        cfg.update(parallelism=f"replicas x{world}" if world > 1 else "single GPU")
+    elif isinstance(wl, Decode):
+        out.update(value=wl.bytes * world / (ms * 1e-3) / 1e9, unit="GB/s", dtype="int8 (int32 accum, fp32 out)",
+                   scaling="weak")
+        cfg = wl.config()
+        cfg.update(parallelism=f"replicas x{world}" if world > 1 else "single GPU")
+    else:
+        out.update(value=wl.bytes / (ms * 1e-3) / 1e9, unit="GB/s", dtype="int8 (int32 accum, fp32 out)",
+                   scaling="strong")
+        cfg = wl.config()
+        cfg.update(parallelism=f"row-shard x{world} + all-gather" if world > 1 else "single GPU")
+    out["config"] = cfg
+    out["clocks"] = clk
+    out["gpu_launches"] = wl.launches_per_step * args.steps
+
+    # roofline of the dominant kernel
+    if prof:
+        dom = max(prof, key=lambda k: prof[k]["ms"])
+        d = prof[dom]
+        t = d["ms"] * 1e-3
+        t_hbm = d["bytes"] / (peaks["hbm_gbs"] * 1e9)
+        t_tc = d["ops"] / (int8_peak * 1e12) if d["ops"] else 0.0
+        if t_tc > t_hbm:
+            ach = d["ops"] / t / 1e12
+            roof = {"bound": "tensor", "achieved": ach, "peak": int8_peak, "unit": "TOPS",
+                    "peak_src": f"2 x {peaks['src']} bf16 dense"}
+        else:
+            ach = d["bytes"] / t / 1e9
+            roof = {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                    "peak_src": f"{peaks['src']} copy bandwidth"}
+        roof.update(frac=roof["achieved"] / roof["peak"], kernel=dom, launches=d["launches"],
+                    avg_launch_us=d["ms"] * 1e3 / d["launches"],
+                    bytes_per_launch=d["bytes"] / d["launches"], ops_per_launch=d["ops"] / d["launches"],
+                    roofline_time_frac=max(t_hbm, t_tc) / t, traffic=None)
+        tr = os.path.join(ROOT, "profiles", f"traffic_{wl.name}.json")
+        if os.path.exists(tr):
+            roof["traffic"] = json.load(open(tr)).get(dom)
+        out["roofline"] = roof
+        out["kernels"] = {k: {"launches": v["launches"], "share": v["ms"] / sum(x["ms"] for x in prof.values()),
+                              "avg_us": v["ms"] * 1e3 / v["launches"]} for k, v in prof.items()}
+
+    # end to end through the host-pointer ABI
+    if isinstance(wl, Prefill) and not args.no_e2e:
+        wl.build_host()
+        wl.register_host(gcu)
+        wl.step_host(gcu)  # warm-up
+        torch.cuda.synchronize()
+        barrier(world)
+        esteps = max(1, min(args.steps, 3))
+        t0 = time.perf_counter()
+        for _ in range(esteps):
+            wl.step_host(gcu)
+        t1 = time.perf_counter()
+        e_ms = (t1 - t0) * 1e3 / esteps
+        e_ms = max_over_ranks(e_ms, world)
+        out["e2e"] = {"value": wl.ops * world / (e_ms * 1e-3) / 1e12, "unit": "int8 TOPS", "ms_per_step": e_ms,
+                      "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h,
+                      "path": "gcu_quantize_acts + gcu_gemm_int8 host-pointer ABI, registered weights, "
+                              "pinned host activations, wall clock around synchronous calls"}
+
+    # CPU baseline on rank 0 at N=1 (bounded sample)
+    if world == 1 and not args.no_cpu and isinstance(wl, Prefill):
+        out["cpu_baseline"] = cpu_baseline(wl, args.cpu_seconds)
+
+    if graph is not None:
+        del graph
+    if isinstance(wl, LmHead) and world > 1:
+        gcu.comm_destroy()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def cpu_baseline(wl, seconds):
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    threads = os.cpu_count() or 1
+    variant = oracle.ref_variant()
+    if variant is not None:
+        R = oracle.Ref(variant, threads=threads)
+        kind = "reference"
+        desc = f"gemma.c quantize_acts+gemm_int8 (-O3 -ffast-math -fopenmp, {variant}/{R.isa})"
+    else:
+        return {"value": None, "unit": "int8 TOPS", "cores": threads, "kind": "reference",
+                "sample": "reference build not runnable on this host"}
+    ops, run = wl.cpu_sample(R, 1)
+    run()  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        run()
+        n += 1
+        if time.perf_counter() - t0 > seconds or n >= 50:
+            break
+    dt = (time.perf_counter() - t0) / n
+    return {"value": ops / dt / 1e12, "unit": "int8 TOPS", "cores": threads, "kind": kind,
+            "sample": f"1 of {wl.layers} layers of the same step (M={wl.m}), {n} reps, {desc}",
+            "ms_per_layer": dt * 1e3}
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the reference's own CPU implementation of the path
+# ---------------------------------------------------------------------------
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    variant = oracle.ref_variant()
+    if variant is None:
+        print(json.dumps({"impl": "reference", "unavailable": "no runnable build of gemma.c's matmul functions "
+                          "for this host CPU in oracle/_ref"}))
+        return
+    threads = os.cpu_count() or 1
+    R = oracle.Ref(variant, threads=threads)
+    wl = Prefill()
+    ops, run = wl.cpu_sample(R, 1)
+    for _ in range(args.warmup):
+        run()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        run()
+    dt = (time.perf_counter() - t0) / args.steps
+    v = ops / dt / 1e12
+    out = {"metric": METRIC, "value": v, "unit": "int8 TOPS", "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "int8 (int32 accum, fp32 out)", "data": "synthetic", "impl": "reference",
+           "config": dict(wl.config(), parallelism="CPU, OpenMP", sample="1 of 26 layers per step"),
+           "cpu_baseline": {"value": v, "unit": "int8 TOPS", "cores": threads, "kind": "reference",
+                            "sample": f"1 layer (M=512) of gemma.c quantize_acts+gemm_int8 per step, "
+                                      f"{variant}/{R.isa} build"},
+           "e2e": {"value": v, "unit": "int8 TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="prefill1b", choices=["prefill1b", "decode270m", "lmhead4b"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,658 @@
+// gcu_api.cu -- runtime of libgcu.so: errors, per-thread streams and staging,
+// the weight registry, and the exported host- and device-pointer entry points
+// declared in include/gcu.h.
+//
+// The host entry points keep gemma.c's calling convention: host pointers in,
+// results in host memory on return (gemma.c:2590, 2656, 2770, 2818, 3943).
+// Weights are uploaded once at registration; any interior pointer of a
+// registered range (gemma.c:5080-5086 passes w->i8.q + hd*hdim*dim) maps to
+// the same offset of the device copy.
+#include "gcu_internal.cuh"
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <shared_mutex>
+#include <unordered_map>
+#include <vector>
+
+#define GCU_EXPORT extern "C" __attribute__((visibility("default")))
+
+namespace gcu {
+
+int launch_gemm_tc_jobs(const int8_t *src, long sstr, const float *ssc, int m, int k,
+                        const GemmArgs *jobs, int njobs, cudaStream_t st, int force_bn,
+                        int force_split);
+
+// ---------------------------------------------------------------------------
+// errors
+// ---------------------------------------------------------------------------
+static thread_local char t_err[256] = {0};
+
+int set_error(const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_err, sizeof(t_err), fmt, ap);
+  va_end(ap);
+  return 1;
+}
+
+int check_cuda(cudaError_t e, const char *what) {
+  return set_error("%s: %s", what, cudaGetErrorString(e));
+}
+
+// ---------------------------------------------------------------------------
+// per-device state
+// ---------------------------------------------------------------------------
+__device__ unsigned int g_dev_err;
+
+static thread_local int t_device = -1;
+
+static int current_device() {
+  if (t_device < 0) {
+    int d = 0;
+    if (cudaGetDevice(&d) != cudaSuccess) d = 0;
+    t_device = d;
+  }
+  return t_device;
+}
+
+struct DeviceInfo {
+  int sms = 0;
+  unsigned int *err = nullptr;
+};
+static std::mutex g_dev_mu;
+static std::unordered_map<int, DeviceInfo> g_dev;
+
+static DeviceInfo &device_info() {
+  const int d = current_device();
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DeviceInfo &di = g_dev[d];
+  if (di.sms == 0) {
+    cudaDeviceGetAttribute(&di.sms, cudaDevAttrMultiProcessorCount, d);
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_dev_err) == cudaSuccess) di.err = (unsigned int *)p;
+  }
+  return di;
+}
+
+int num_sms() { return device_info().sms; }
+unsigned int *dev_error_word() { return device_info().err; }
+
+// ---------------------------------------------------------------------------
+// per-thread context: stream and device buffers for the host entry points
+// ---------------------------------------------------------------------------
+struct DevBuf {
+  void *p = nullptr;
+  size_t cap = 0;
+  int get(size_t bytes, void **out) {
+    if (bytes > cap) {
+      if (p) cudaFree(p);
+      p = nullptr;
+      cap = 0;
+      size_t want = bytes + bytes / 4 + 256;
+      GCU_CUDA(cudaMalloc(&p, want));
+      cap = want;
+    }
+    *out = p;
+    return 0;
+  }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    cap = 0;
+  }
+};
+
+struct ThreadCtx {
+  int device = -1;
+  cudaStream_t stream = nullptr;
+  DevBuf in, in2, out, sc, sc2, wtmp, wstmp;
+  ~ThreadCtx() {
+    // process teardown may already have unloaded the driver: leak quietly
+  }
+};
+static thread_local ThreadCtx t_ctx;
+
+static int ctx(ThreadCtx **out) {
+  const int d = current_device();
+  ThreadCtx &c = t_ctx;
+  if (c.device != d || c.stream == nullptr) {
+    GCU_CUDA(cudaSetDevice(d));
+    GCU_CUDA(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking));
+    c.device = d;
+  }
+  *out = &c;
+  return 0;
+}
+
+// ---------------------------------------------------------------------------
+// split-K workspace, one per (device, stream): launches on one stream are
+// ordered, so they can share it; different streams never do.
+// ---------------------------------------------------------------------------
+struct Workspace {
+  void *ws = nullptr;
+  size_t ws_cap = 0;
+  int *cnt = nullptr;
+  int cnt_cap = 0;
+};
+static std::mutex g_ws_mu;
+static std::map<std::pair<int, cudaStream_t>, Workspace> g_ws;
+
+int gemm_workspace(size_t bytes, void **ws, int **counters, int ncounters, cudaStream_t st) {
+  std::lock_guard<std::mutex> lk(g_ws_mu);
+  Workspace &w = g_ws[{current_device(), st}];
+  if (bytes > w.ws_cap) {
+    if (w.ws) {
+      GCU_CUDA(cudaStreamSynchronize(st));
+      cudaFree(w.ws);
+    }
+    w.ws = nullptr;
+    w.ws_cap = 0;
+    size_t want = bytes < ((size_t)16 << 20) ? ((size_t)16 << 20) : bytes;
+    GCU_CUDA(cudaMalloc(&w.ws, want));
+    w.ws_cap = want;
+  }
+  if (ncounters > w.cnt_cap) {
+    if (w.cnt) {
+      GCU_CUDA(cudaStreamSynchronize(st));
+      cudaFree(w.cnt);
+    }
+    w.cnt = nullptr;
+    w.cnt_cap = 0;
+    int want = ncounters < 4096 ? 4096 : ncounters;
+    GCU_CUDA(cudaMalloc(&w.cnt, (size_t)want * sizeof(int)));
+    GCU_CUDA(cudaMemsetAsync(w.cnt, 0, (size_t)want * sizeof(int), st));
+    w.cnt_cap = want;
+  }
+  *ws = w.ws;
+  *counters = w.cnt;
+  return 0;
+}
+
+// ---------------------------------------------------------------------------
+// weight registry
+// ---------------------------------------------------------------------------
+struct WeightEntry {
+  uintptr_t q0, q1;  // host range of the int8 values
+  uintptr_t s0, s1;  // host range of the scales
+  int8_t *dq;
+  float *ds;
+  int rows, k;
+};
+static std::shared_mutex g_reg_mu;
+// keyed by (device, host begin)
+static std::map<std::pair<int, uintptr_t>, WeightEntry> g_q;
+static std::map<std::pair<int, uintptr_t>, uintptr_t> g_s;  // scales begin -> q begin
+static size_t g_reg_bytes = 0;
+
+// device address for host range [p, p+bytes) inside a registered weight
+static const void *lookup_q(const void *p, size_t bytes) {
+  const int d = current_device();
+  const uintptr_t a = (uintptr_t)p;
+  std::shared_lock<std::shared_mutex> lk(g_reg_mu);
+  auto it = g_q.upper_bound({d, a});
+  if (it == g_q.begin()) return nullptr;
+  --it;
+  if (it->first.first != d) return nullptr;
+  const WeightEntry &e = it->second;
+  if (a < e.q0 || a + bytes > e.q1) return nullptr;
+  return e.dq + (a - e.q0);
+}
+static const float *lookup_s(const float *p, size_t count) {
+  const int d = current_device();
+  const uintptr_t a = (uintptr_t)p;
+  std::shared_lock<std::shared_mutex> lk(g_reg_mu);
+  auto it = g_s.upper_bound({d, a});
+  if (it == g_s.begin()) return nullptr;
+  --it;
+  if (it->first.first != d) return nullptr;
+  const WeightEntry &e = g_q.at({d, it->second});
+  if (a < e.s0 || a + count * sizeof(float) > e.s1) return nullptr;
+  return e.ds + (a - e.s0) / sizeof(float);
+}
+
+// Device pointer of a weight operand: registered copy, else a transient
+// upload into the thread's buffer (correct, but pays the copy every call).
+static int weight_dev(ThreadCtx *c, DevBuf &buf, const void *host, size_t bytes,
+                      const void **dev) {
+  if ((*dev = lookup_q(host, bytes)) != nullptr) return 0;
+  void *p;
+  if (buf.get(bytes, &p)) return 1;
+  GCU_CUDA(cudaMemcpyAsync(p, host, bytes, cudaMemcpyHostToDevice, c->stream));
+  *dev = p;
+  return 0;
+}
+static int scales_dev(ThreadCtx *c, DevBuf &buf, const float *host, size_t count,
+                      const float **dev) {
+  if ((*dev = lookup_s(host, count)) != nullptr) return 0;
+  void *p;
+  if (buf.get(count * sizeof(float), &p)) return 1;
+  GCU_CUDA(cudaMemcpyAsync(p, host, count * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+  *dev = (const float *)p;
+  return 0;
+}
+
+static int sync_and_check(ThreadCtx *c) {
+  GCU_CUDA(cudaStreamSynchronize(c->stream));
+  unsigned int *ew = dev_error_word();
+  unsigned int code = 0;
+  if (ew) {
+    GCU_CUDA(cudaMemcpy(&code, ew, sizeof(code), cudaMemcpyDeviceToHost));
+    if (code) {
+      unsigned int zero = 0;
+      cudaMemcpy(ew, &zero, sizeof(zero), cudaMemcpyHostToDevice);
+      return set_error("device-side wait gave up (code %u)", code);
+    }
+  }
+  return 0;
+}
+
+static inline cudaStream_t as_stream(void *s) { return static_cast<cudaStream_t>(s); }
+
+// Enqueue y = gemm on device operands, choosing the kernel by m.
+static int dev_gemm(float *dst, long dstr, const int8_t *mat, long mstr, const float *matsc,
+                    const int8_t *src, long sstr, const float *ssc, int m, int n, int k,
+                    cudaStream_t st) {
+  if (m <= 8) {
+    if (mstr != k)
+      return set_error("gemm: m <= 8 needs dense weight rows (mstr %ld, k %d)", mstr, k);
+    GemvJobs jobs{};
+    jobs.w[0] = mat;
+    jobs.ws[0] = matsc;
+    jobs.y[0] = dst;
+    jobs.row_end[0] = n;
+    jobs.njobs = 1;
+    return launch_gemv(jobs, src, sstr, ssc, m, dstr, k, st);
+  }
+  GemmArgs a{dst, dstr, mat, mstr, matsc, src, sstr, ssc, m, n, k};
+  return launch_gemm_tc(a, st, 0, 0);
+}
+
+}  // namespace gcu
+
+using namespace gcu;
+
+// ===========================================================================
+// exported entry points
+// ===========================================================================
+GCU_EXPORT const char *gcu_version(void) { return "gcu 0.1 sm_100a"; }
+
+GCU_EXPORT const char *gcu_last_error(void) { return t_err; }
+
+GCU_EXPORT int gcu_init(int device) {
+  int n = 0;
+  GCU_CUDA(cudaGetDeviceCount(&n));
+  if (device < 0 || device >= n) return set_error("gcu_init: device %d of %d", device, n);
+  GCU_CUDA(cudaSetDevice(device));
+  t_device = device;
+  device_info();
+  return 0;
+}
+
+GCU_EXPORT int gcu_check_device(void) {
+  GCU_CUDA(cudaDeviceSynchronize());
+  unsigned int *ew = dev_error_word();
+  if (!ew) return 0;
+  unsigned int code = 0;
+  GCU_CUDA(cudaMemcpy(&code, ew, sizeof(code), cudaMemcpyDeviceToHost));
+  if (code) {
+    unsigned int zero = 0;
+    cudaMemcpy(ew, &zero, sizeof(zero), cudaMemcpyHostToDevice);
+    set_error("device-side wait gave up (code %u)", code);
+    return 1;
+  }
+  return 0;
+}
+
+GCU_EXPORT int gcu_register_weight(const int8_t *q, const float *scales, int rows, int k) {
+  if (!q || !scales || rows <= 0 || k <= 0) return set_error("gcu_register_weight: bad arguments");
+  const int d = current_device();
+  GCU_CUDA(cudaSetDevice(d));
+  {
+    std::shared_lock<std::shared_mutex> lk(g_reg_mu);
+    if (g_q.count({d, (uintptr_t)q})) return 0;  // already registered
+  }
+  const size_t qb = (size_t)rows * k, sb = (size_t)rows * sizeof(float);
+  WeightEntry e{(uintptr_t)q, (uintptr_t)q + qb, (uintptr_t)scales, (uintptr_t)scales + sb,
+                nullptr, nullptr, rows, k};
+  GCU_CUDA(cudaMalloc(&e.dq, qb));
+  if (cudaMalloc(&e.ds, sb) != cudaSuccess) {
+    cudaFree(e.dq);
+    return set_error("gcu_register_weight: out of device memory");
+  }
+  cudaError_t r1 = cudaMemcpy(e.dq, q, qb, cudaMemcpyHostToDevice);
+  cudaError_t r2 = cudaMemcpy(e.ds, scales, sb, cudaMemcpyHostToDevice);
+  if (r1 != cudaSuccess || r2 != cudaSuccess) {
+    cudaFree(e.dq);
+    cudaFree(e.ds);
+    return check_cuda(r1 != cudaSuccess ? r1 : r2, "gcu_register_weight upload");
+  }
+  std::unique_lock<std::shared_mutex> lk(g_reg_mu);
+  g_q[{d, e.q0}] = e;
+  g_s[{d, e.s0}] = e.q0;
+  g_reg_bytes += qb + sb;
+  return 0;
+}
+
+GCU_EXPORT int gcu_unregister_weight(const int8_t *q) {
+  const int d = current_device();
+  std::unique_lock<std::shared_mutex> lk(g_reg_mu);
+  auto it = g_q.find({d, (uintptr_t)q});
+  if (it == g_q.end()) return set_error("gcu_unregister_weight: not registered");
+  WeightEntry e = it->second;
+  g_q.erase(it);
+  g_s.erase({d, e.s0});
+  g_reg_bytes -= (size_t)e.rows * e.k + (size_t)e.rows * sizeof(float);
+  cudaDeviceSynchronize();
+  cudaFree(e.dq);
+  cudaFree(e.ds);
+  return 0;
+}
+
+GCU_EXPORT size_t gcu_registered_bytes(void) {
+  std::shared_lock<std::shared_mutex> lk(g_reg_mu);
+  return g_reg_bytes;
+}
+
+GCU_EXPORT int gcu_shutdown(void) {
+  cudaDeviceSynchronize();
+  {
+    std::unique_lock<std::shared_mutex> lk(g_reg_mu);
+    for (auto &kv : g_q) {
+      cudaFree(kv.second.dq);
+      cudaFree(kv.second.ds);
+    }
+    g_q.clear();
+    g_s.clear();
+    g_reg_bytes = 0;
+  }
+  {
+    std::lock_guard<std::mutex> lk(g_ws_mu);
+    for (auto &kv : g_ws) {
+      cudaFree(kv.second.ws);
+      cudaFree(kv.second.cnt);
+    }
+    g_ws.clear();
+  }
+  ThreadCtx &c = t_ctx;
+  c.in.release();
+  c.in2.release();
+  c.out.release();
+  c.sc.release();
+  c.sc2.release();
+  c.wtmp.release();
+  c.wstmp.release();
+  if (c.stream) cudaStreamDestroy(c.stream);
+  c.stream = nullptr;
+  c.device = -1;
+  return 0;
+}
+
+// ---- host-pointer entry points ---------------------------------------------
+
+GCU_EXPORT int gcu_quantize_acts(int8_t *dst, float *dsc, const float *src, int sstr, int m,
+                                 int n) {
+  if (m <= 0 || n <= 0) return 0;
+  if (!dst || !dsc || !src) return set_error("gcu_quantize_acts: null pointer");
+  if (sstr == 0) sstr = n;
+  if (sstr < n) return set_error("gcu_quantize_acts: sstr %d < n %d", sstr, n);
+  ThreadCtx *c;
+  if (ctx(&c)) return 1;
+  const size_t in_elems = (size_t)(m - 1) * sstr + n;
+  void *din, *dout, *dsc_d;
+  if (c->in.get(in_elems * 4, &din) || c->out.get((size_t)m * n, &dout) ||
+      c->sc.get((size_t)m * 4, &dsc_d))
+    return 1;
+  GCU_CUDA(cudaMemcpyAsync(din, src, in_elems * 4, cudaMemcpyHostToDevice, c->stream));
+  if (launch_quantize_rows((int8_t *)dout, (float *)dsc_d, (const float *)din, sstr, m, n,
+                           c->stream))
+    return 1;
+  GCU_CUDA(cudaMemcpyAsync(dst, dout, (size_t)m * n, cudaMemcpyDeviceToHost, c->stream));
+  GCU_CUDA(cudaMemcpyAsync(dsc, dsc_d, (size_t)m * 4, cudaMemcpyDeviceToHost, c->stream));
+  GCU_CUDA(cudaStreamSynchronize(c->stream));
+  return 0;
+}
+
+GCU_EXPORT float gcu_quantize_act(int8_t *dst, const float *vec, int dim) {
+  float sc = NAN;
+  if (gcu_quantize_acts(dst, &sc, vec, 0, 1, dim)) return NAN;
+  return sc;
+}
+
+static int host_gemv_jobs(const gcu_gemv_job *jobs, int njobs, const int8_t *vec, float vsc,
+                          int n) {
+  if (njobs <= 0) return 0;
+  if (njobs > GCU_MAX_JOBS) return set_error("gemv_int8_multi: at most %d jobs", GCU_MAX_JOBS);
+  if (!vec || n <= 0) return set_error("gemv_int8: bad vector");
+  ThreadCtx *c;
+  if (ctx(&c)) return 1;
+  GemvJobs J{};
+  int rows = 0;
+  size_t out_elems = 0;
+  for (int j = 0; j < njobs; ++j) out_elems += jobs[j].m > 0 ? jobs[j].m : 0;
+  void *dx, *dy, *dxs;
+  if (c->in.get((size_t)n + 16, &dx) || c->out.get(out_elems * 4 + 16, &dy) ||
+      c->sc.get(16, &dxs))
+    return 1;
+  // weights of unregistered jobs share one transient buffer: size it once
+  size_t wt = 0, st = 0;
+  for (int j = 0; j < njobs; ++j) {
+    if (!lookup_q(jobs[j].w, (size_t)jobs[j].m * n)) wt += (size_t)jobs[j].m * n + 16;
+    if (!lookup_s(jobs[j].sc, (size_t)jobs[j].m)) st += (size_t)jobs[j].m * 4 + 16;
+  }
+  void *wbase = nullptr, *sbase = nullptr;
+  if (wt && c->wtmp.get(wt, &wbase)) return 1;
+  if (st && c->wstmp.get(st, &sbase)) return 1;
+  size_t woff = 0, soff = 0, yoff = 0;
+  for (int j = 0; j < njobs; ++j) {
+    const int m = jobs[j].m;
+    if (m <= 0) continue;
+    const void *dw = lookup_q(jobs[j].w, (size_t)m * n);
+    if (!dw) {
+      void *p = (char *)wbase + woff;
+      GCU_CUDA(cudaMemcpyAsync(p, jobs[j].w, (size_t)m * n, cudaMemcpyHostToDevice, c->stream));
+      woff += ((size_t)m * n + 15) / 16 * 16;
+      dw = p;
+    }
+    const float *ds = lookup_s(jobs[j].sc, (size_t)m);
+    if (!ds) {
+      void *p = (char *)sbase + soff;
+      GCU_CUDA(cudaMemcpyAsync(p, jobs[j].sc, (size_t)m * 4, cudaMemcpyHostToDevice, c->stream));
+      soff += ((size_t)m * 4 + 15) / 16 * 16;
+      ds = (const float *)p;
+    }
+    J.w[J.njobs] = (const int8_t *)dw;
+    J.ws[J.njobs] = ds;
+    J.y[J.njobs] = (float *)dy + yoff;
+    rows += m;
+    J.row_end[J.njobs] = rows;
+    J.njobs++;
+    yoff += m;
+  }
+  GCU_CUDA(cudaMemcpyAsync(dx, vec, (size_t)n, cudaMemcpyHostToDevice, c->stream));
+  GCU_CUDA(cudaMemcpyAsync(dxs, &vsc, 4, cudaMemcpyHostToDevice, c->stream));
+  if (launch_gemv(J, (const int8_t *)dx, 0, (const float *)dxs, 1, 0, n, c->stream)) return 1;
+  yoff = 0;
+  for (int j = 0; j < njobs; ++j) {
+    if (jobs[j].m <= 0) continue;
+    GCU_CUDA(cudaMemcpyAsync(jobs[j].dst, (float *)dy + yoff, (size_t)jobs[j].m * 4,
+                             cudaMemcpyDeviceToHost, c->stream));
+    yoff += jobs[j].m;
+  }
+  // vsc lives on this stack frame: the copies must finish before returning
+  GCU_CUDA(cudaStreamSynchronize(c->stream));
+  return 0;
+}
+
+GCU_EXPORT int gcu_gemv_int8(float *dst, const int8_t *mat, const float *matsc, const int8_t *vec,
+                             float vsc, int m, int n) {
+  gcu_gemv_job j{mat, matsc, dst, m};
+  return host_gemv_jobs(&j, 1, vec, vsc, n);
+}
+
+GCU_EXPORT int gcu_gemv_int8_multi(const gcu_gemv_job *jobs, int njobs, const int8_t *vec,
+                                   float vsc, int n) {
+  return host_gemv_jobs(jobs, njobs, vec, vsc, n);
+}
+
+GCU_EXPORT int gcu_gemm_int8(float *dst, int dstr, const int8_t *mat, int mstr,
+                             const float *matsc, const int8_t *src, int sstr, const float *ssc,
+                             int m, int n, int k) {
+  if (m <= 0 || n <= 0) return 0;
+  if (k <= 0 || !dst || !mat || !matsc || !src || !ssc) return set_error("gemm_int8: bad arguments");
+  if (dstr == 0) dstr = n;
+  if (mstr == 0) mstr = k;
+  if (sstr == 0) sstr = k;
+  ThreadCtx *c;
+  if (ctx(&c)) return 1;
+  const int k16 = (k + 15) / 16 * 16;  // device row stride of packed operands
+  const int n4 = (n + 3) / 4 * 4;      // device row stride of the output
+  // activations: pack to rows of k16 bytes (TMA wants 16-byte strides)
+  void *dsrc, *dssc, *dout;
+  if (c->in.get((size_t)m * k16, &dsrc) || c->sc.get((size_t)m * 4, &dssc) ||
+      c->out.get((size_t)m * n4 * 4, &dout))
+    return 1;
+  GCU_CUDA(cudaMemcpy2DAsync(dsrc, k16, src, sstr, k, m, cudaMemcpyHostToDevice, c->stream));
+  GCU_CUDA(cudaMemcpyAsync(dssc, ssc, (size_t)m * 4, cudaMemcpyHostToDevice, c->stream));
+  // weights: registered copy if the whole strided range is inside one
+  const size_t wbytes = (size_t)(n - 1) * mstr + k;
+  const void *dmat = lookup_q(mat, wbytes);
+  const float *dms = nullptr;
+  if (scales_dev(c, c->wstmp, matsc, (size_t)n, &dms)) return 1;
+  long dmstr = mstr;
+  // the GEMV kernel (m <= 8) reads dense rows; the tensor-core kernel any
+  // 16-byte-aligned stride
+  const bool dense_ok = dmat && (m <= 8 ? mstr == k
+                                        : ((uintptr_t)dmat % 16 == 0) && (mstr % 16 == 0));
+  if (!dense_ok) {
+    // pack the weight rows into a dense, 16-byte-strided device buffer
+    void *p;
+    const int ws = (m <= 8) ? k : k16;
+    if (c->wtmp.get((size_t)n * ws, &p)) return 1;
+    if (dmat) {
+      GCU_CUDA(cudaMemcpy2DAsync(p, ws, dmat, mstr, k, n, cudaMemcpyDeviceToDevice, c->stream));
+    } else {
+      GCU_CUDA(cudaMemcpy2DAsync(p, ws, mat, mstr, k, n, cudaMemcpyHostToDevice, c->stream));
+    }
+    dmat = p;
+    dmstr = ws;
+  }
+  if (m <= 8) {
+    // the GEMV kernel reads x rows at stride k16 and k-length weight rows
+    if (dev_gemm((float *)dout, n4, (const int8_t *)dmat, dmstr, dms, (const int8_t *)dsrc, k16,
+                 (const float *)dssc, m, n, k, c->stream))
+      return 1;
+  } else {
+    if (k16 != k && dmstr % 16 != 0) return set_error("gemm_int8: internal stride error");
+    GemmArgs a{(float *)dout, n4, (const int8_t *)dmat, dmstr, dms,
+               (const int8_t *)dsrc, k16, (const float *)dssc, m, n, k};
+    if (launch_gemm_tc(a, c->stream, 0, 0)) return 1;
+  }
+  GCU_CUDA(cudaMemcpy2DAsync(dst, (size_t)dstr * 4, dout, (size_t)n4 * 4, (size_t)n * 4, m,
+                             cudaMemcpyDeviceToHost, c->stream));
+  return sync_and_check(c);
+}
+
+// ---- device-pointer entry points ---------------------------------------------
+
+GCU_EXPORT int gcu_dev_quantize_acts(int8_t *dst, float *dsc, const float *src, int sstr, int m,
+                                     int n, void *stream) {
+  if (sstr == 0) sstr = n;
+  return launch_quantize_rows(dst, dsc, src, sstr, m, n, as_stream(stream));
+}
+
+GCU_EXPORT int gcu_dev_gemv_int8(float *dst, const int8_t *mat, const float *matsc,
+                                 const int8_t *vec, const float *vsc, int m, int n, void *stream) {
+  GemvJobs J{};
+  J.w[0] = mat;
+  J.ws[0] = matsc;
+  J.y[0] = dst;
+  J.row_end[0] = m;
+  J.njobs = 1;
+  return launch_gemv(J, vec, 0, vsc, 1, 0, n, as_stream(stream));
+}
+
+GCU_EXPORT int gcu_dev_gemv_int8_multi(const gcu_gemv_job *jobs, int njobs, const int8_t *vec,
+                                       const float *vsc, int n, void *stream) {
+  if (njobs > GCU_MAX_JOBS) return set_error("gemv_int8_multi: at most %d jobs", GCU_MAX_JOBS);
+  GemvJobs J{};
+  int rows = 0;
+  for (int j = 0; j < njobs; ++j) {
+    if (jobs[j].m <= 0) continue;
+    J.w[J.njobs] = (const int8_t *)jobs[j].w;
+    J.ws[J.njobs] = jobs[j].sc;
+    J.y[J.njobs] = jobs[j].dst;
+    rows += jobs[j].m;
+    J.row_end[J.njobs] = rows;
+    J.njobs++;
+  }
+  return launch_gemv(J, vec, 0, vsc, 1, 0, n, as_stream(stream));
+}
+
+GCU_EXPORT int gcu_dev_gemm_int8(float *dst, int dstr, const int8_t *mat, int mstr,
+                                 const float *matsc, const int8_t *src, int sstr,
+                                 const float *ssc, int m, int n, int k, void *stream) {
+  if (m <= 0 || n <= 0) return 0;
+  if (dstr == 0) dstr = n;
+  if (mstr == 0) mstr = k;
+  if (sstr == 0) sstr = k;
+  return dev_gemm(dst, dstr, mat, mstr, matsc, src, sstr, ssc, m, n, k, as_stream(stream));
+}
+
+GCU_EXPORT int gcu_dev_gemm_int8_multi(const gcu_gemv_job *jobs, int njobs, const int8_t *src,
+                                       int sstr, const float *ssc, int m, int k, void *stream) {
+  if (m <= 0) return 0;
+  if (sstr == 0) sstr = k;
+  if (njobs <= 0) return 0;
+  if (m <= 8) {
+    if (njobs > GCU_MAX_JOBS) return set_error("gemm_int8_multi: at most %d jobs", GCU_MAX_JOBS);
+    GemvJobs J{};
+    int rows = 0;
+    for (int j = 0; j < njobs; ++j) {
+      J.w[j] = (const int8_t *)jobs[j].w;
+      J.ws[j] = jobs[j].sc;
+      J.y[j] = jobs[j].dst;
+      rows += jobs[j].m;
+      J.row_end[j] = rows;
+    }
+    J.njobs = njobs;
+    if (njobs > 1) {
+      // each job's output is (m, rows_j): one launch per job keeps the
+      // per-job row stride
+      for (int j = 0; j < njobs; ++j) {
+        GemvJobs one{};
+        one.w[0] = J.w[j];
+        one.ws[0] = J.ws[j];
+        one.y[0] = J.y[j];
+        one.row_end[0] = jobs[j].m;
+        one.njobs = 1;
+        if (launch_gemv(one, src, sstr, ssc, m, jobs[j].m, k, as_stream(stream))) return 1;
+      }
+      return 0;
+    }
+    return launch_gemv(J, src, sstr, ssc, m, jobs[0].m, k, as_stream(stream));
+  }
+  if (njobs > 4) return set_error("gemm_int8_multi: at most 4 jobs on the tensor-core path");
+  GemmArgs a[4];
+  for (int j = 0; j < njobs; ++j)
+    a[j] = GemmArgs{jobs[j].dst, jobs[j].m, (const int8_t *)jobs[j].w, k, jobs[j].sc,
+                    src, sstr, ssc, m, jobs[j].m, k};
+  return launch_gemm_tc_jobs(src, sstr, ssc, m, k, a, njobs, as_stream(stream), 0, 0);
+}
+
+// Tuning hook (not in gcu.h): force the tensor-core kernel's tile width
+// (128/256) and K split for one call.  Used by the benchmark's sweeps.
+GCU_EXPORT int gcu_dev_gemm_int8_tuned(float *dst, int dstr, const int8_t *mat, int mstr,
+                                       const float *matsc, const int8_t *src, int sstr,
+                                       const float *ssc, int m, int n, int k, int bn, int split,
+                                       void *stream) {
+  if (dstr == 0) dstr = n;
+  if (mstr == 0) mstr = k;
+  if (sstr == 0) sstr = k;
+  GemmArgs a{dst, dstr, mat, mstr, matsc, src, sstr, ssc, m, n, k};
+  return launch_gemm_tc(a, as_stream(stream), bn, split);
+}

@@ -1,0 +1,519 @@
+// k_gemm.cu -- K3: int8 NT GEMM on the 5th-generation tensor cores.
+//
+// Device restatement of gemm_int8 (gemma.c:3937-4054):
+//   dst[i*dstr + j] = (float)(sum_l src[i,l] * mat[j,l]) * (ssc[i] * matsc[j])
+// The int32 sums are exact, so the tiling, the split of K and the order of
+// accumulation cannot change a bit; the epilogue is the reference -ffast-math
+// build's (float)acc * (xs*ws) with round-to-nearest multiplies.
+//
+// Design (one CTA per SM, persistent over work units):
+//   warp 0      TMA producer: 128-byte-swizzled A (128 x 128 B) and B
+//               (BN x 128 B) tiles into a STAGES-deep shared-memory ring
+//   warp 1      allocates TMEM, issues tcgen05.mma.cta_group::1.kind::i8
+//               (M=128, N=BN, K=32) from one thread, commits stage releases
+//   warps 2-5   epilogue: tcgen05.ld the int32 accumulators (two TMEM
+//               buffers, so the next tile's MMAs overlap this epilogue),
+//               dequantize, stage through swizzled shared memory and TMA-store
+//               fp32 rows; or, when K is split, write int32 partials and let
+//               the last split of a tile reduce them
+// No cluster multicast is used anywhere (every load reads this GPU's memory).
+// Every wait is bounded (globaltimer); on timeout the kernel records an error
+// code, drains its copies, frees TMEM and returns.
+#include "gcu_internal.cuh"
+
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+namespace gcu {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 128;  // K bytes per stage (one 128-byte swizzle row)
+constexpr int kThreads = 192;
+constexpr int kMaxJobs = 4;
+constexpr int kEpiStageBytes = 32 * 128;  // 32 rows x 32 fp32
+
+template <int BN>
+struct Cfg {
+  static constexpr int STAGES = BN == 256 ? 4 : 5;
+  static constexpr int A_BYTES = BM * BK;
+  static constexpr int B_BYTES = BN * BK;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
+  static constexpr int BAR_OFF = EPI_OFF + 4 * 2 * kEpiStageBytes;
+  static constexpr int NBARS = 2 * STAGES + 5;
+  static constexpr int SMEM = 1024 + BAR_OFF + NBARS * 8 + 16;
+};
+
+struct alignas(64) TcJob {
+  CUtensorMap tmB;  // weights [n][k] int8, box BN x 128
+  CUtensorMap tmD;  // output [m][n] fp32 (row stride dstr), box 32 x 32
+  const float *matsc;
+  float *dst;
+  long dstr;
+  int n;
+  int tn_begin;  // first global n-tile of this job
+  int tma_store;
+};
+
+struct alignas(64) TcParams {
+  CUtensorMap tmA;  // activations [m][k] int8, box 128 x 128
+  TcJob jobs[kMaxJobs];
+  int njobs;
+  int m, k;
+  int tiles_m, tiles_n, splits, kb_total, kb_per_split, units;
+  const float *ssc;
+  int32_t *ws;    // split-K partials [tile][split][BM][BN]
+  int *counters;  // split-K arrival counters [tile]
+  unsigned int *err;
+};
+
+__device__ __forceinline__ float dequant(int acc, float xs, float ws) {
+  return __fmul_rn(__int2float_rn(acc), __fmul_rn(xs, ws));
+}
+
+struct Unit {
+  int m_t, s, job, n_t, tile;
+};
+
+__device__ __forceinline__ Unit decode_unit(const TcParams &p, int u) {
+  Unit w;
+  w.m_t = u % p.tiles_m;
+  const int rest = u / p.tiles_m;
+  w.s = rest % p.splits;
+  const int ntg = rest / p.splits;
+  int j = 0;
+#pragma unroll
+  for (int t = 1; t < kMaxJobs; ++t)
+    if (t < p.njobs && ntg >= p.jobs[t].tn_begin) j = t;
+  w.job = j;
+  w.n_t = ntg - p.jobs[j].tn_begin;
+  w.tile = w.m_t * p.tiles_n + ntg;
+  return w;
+}
+
+// Dequantize 32 accumulators of one row and write them: either into the
+// warp's swizzled staging buffer for a TMA store, or straight to global.
+template <bool TMA>
+__device__ __forceinline__ void emit_chunk(const TcParams &p, const TcJob &job, const int (&acc)[32],
+                                           float xs, int row, int col0, int lane, uint8_t *stage,
+                                           int tile_row0) {
+  float out[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const int col = col0 + i;
+    const float ws = col < job.n ? __ldg(job.matsc + col) : 0.0f;
+    out[i] = dequant(acc[i], xs, ws);
+  }
+  if (TMA) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      float4 v = make_float4(out[4 * c], out[4 * c + 1], out[4 * c + 2], out[4 * c + 3]);
+      *reinterpret_cast<float4 *>(stage + lane * 128 + ((c ^ (lane & 7)) << 4)) = v;
+    }
+    ptx::fence_proxy_async_smem();
+    __syncwarp();
+    // boxes starting below the last row (M tail) hold nothing to store
+    if (lane == 0 && tile_row0 < p.m) {
+      ptx::tma_store_2d(&job.tmD, stage, col0, tile_row0);
+      ptx::bulk_commit();
+    }
+  } else {
+    if (row < p.m) {
+      float *d = job.dst + (size_t)row * job.dstr;
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < job.n) d[col0 + i] = out[i];
+    }
+  }
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_tc(const __grid_constant__ TcParams p) {
+  using C = Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *smA = smem;
+  uint8_t *smB = smem + C::STAGES * C::A_BYTES;
+  uint8_t *epi = smem + C::EPI_OFF;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
+  uint64_t *full = bars;
+  uint64_t *empty = bars + C::STAGES;
+  uint64_t *tfull = bars + 2 * C::STAGES;
+  uint64_t *tempty = tfull + 2;
+  uint64_t *mma_done = tempty + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
+  __shared__ int s_last;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(&tfull[b], 1);
+      ptx::mbar_init(&tempty[b], 4 * 32);
+    }
+    ptx::mbar_init(mma_done, 1);
+    ptx::fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    ptx::prefetch_tmap(&p.tmA);
+    for (int j = 0; j < p.njobs; ++j) {
+      ptx::prefetch_tmap(&p.jobs[j].tmB);
+      if (p.jobs[j].tma_store) ptx::prefetch_tmap(&p.jobs[j].tmD);
+    }
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, C::TMEM_COLS);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol_a = ptx::policy_evict_last();
+      const uint64_t pol_b = ptx::policy_evict_first();
+      int it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+        const Unit w = decode_unit(p, u);
+        const int kb0 = w.s * p.kb_per_split;
+        const int kb1 = min(kb0 + p.kb_per_split, p.kb_total);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int st = it % C::STAGES;
+          const uint32_t round = it / C::STAGES;
+          if (!ptx::mbar_wait(&empty[st], (round & 1) ^ 1, p.err, DEV_TIMEOUT_EMPTY)) {
+            ok = false;
+            break;
+          }
+          ptx::mbar_arrive_expect_tx(&full[st], C::STAGE_BYTES);
+          ptx::tma_load_2d(&p.tmA, &full[st], smA + st * C::A_BYTES, kb * BK, w.m_t * BM, pol_a);
+          ptx::tma_load_2d(&p.jobs[w.job].tmB, &full[st], smB + st * C::B_BYTES, kb * BK,
+                           w.n_t * BN, pol_b);
+        }
+      }
+      // drain: the last load issued into each stage must have landed before
+      // the CTA may exit (immediate in normal operation)
+      for (int d = 1; d <= C::STAGES && d <= it; ++d) {
+        const int j = it - d;
+        ptx::mbar_wait(&full[j % C::STAGES], (j / C::STAGES) & 1, p.err, DEV_TIMEOUT_DRAIN);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = ptx::idesc_i8(BM, BN);
+      int it = 0, t = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x, ++t) {
+        const Unit w = decode_unit(p, u);
+        const int kb0 = w.s * p.kb_per_split;
+        const int kb1 = min(kb0 + p.kb_per_split, p.kb_total);
+        const int buf = t & 1;
+        const uint32_t use = t >> 1;
+        if (!ptx::mbar_wait(&tempty[buf], (use & 1) ^ 1, p.err, DEV_TIMEOUT_TMEM)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int st = it % C::STAGES;
+          const uint32_t round = it / C::STAGES;
+          if (!ptx::mbar_wait(&full[st], round & 1, p.err, DEV_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t a0 = ptx::smem_u32(smA + st * C::A_BYTES);
+          const uint32_t b0 = ptx::smem_u32(smB + st * C::B_BYTES);
+#pragma unroll
+          for (int j = 0; j < BK / 32; ++j)
+            ptx::mma_i8(d_tmem, ptx::smem_desc_k128(a0 + 32 * j), ptx::smem_desc_k128(b0 + 32 * j),
+                        idesc, (kb > kb0 || j > 0) ? 1u : 0u);
+          ptx::mma_commit(&empty[st]);
+        }
+        ptx::mma_commit(&tfull[buf]);
+      }
+      // all MMAs of this CTA complete before TMEM may be freed
+      ptx::mma_commit(mma_done);
+      ptx::mbar_wait(mma_done, 0, p.err, DEV_TIMEOUT_DRAIN);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    uint8_t *stage0 = epi + (warp - 2) * 2 * kEpiStageBytes;
+    int t = 0, nstore = 0;
+    for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++t) {
+      const Unit w = decode_unit(p, u);
+      const TcJob &job = p.jobs[w.job];
+      const int buf = t & 1;
+      const uint32_t use = t >> 1;
+      if (!ptx::mbar_wait(&tfull[buf], use & 1, p.err, DEV_TIMEOUT_TMEM)) break;
+      ptx::tc_fence_after();
+      const int tile_row0 = w.m_t * BM + q * 32;
+      const int row = tile_row0 + lane;
+      const float xs = row < p.m ? __ldg(p.ssc + row) : 0.0f;
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
+      if (p.splits == 1) {
+#pragma unroll 1
+        for (int ch = 0; ch < BN / 32; ++ch) {
+          uint32_t r[32];
+          ptx::tmem_ld_32x32(taddr + ch * 32, r);
+          ptx::tmem_ld_wait();
+          const int col0 = w.n_t * BN + ch * 32;
+          if (col0 >= job.n) continue;
+          if (job.tma_store) {
+            uint8_t *stage = stage0 + (nstore & 1) * kEpiStageBytes;
+            if (lane == 0) ptx::bulk_wait_read<1>();
+            __syncwarp();
+            emit_chunk<true>(p, job, reinterpret_cast<const int(&)[32]>(r), xs, row, col0, lane,
+                             stage, tile_row0);
+            ++nstore;
+          } else {
+            emit_chunk<false>(p, job, reinterpret_cast<const int(&)[32]>(r), xs, row, col0, lane,
+                              nullptr, tile_row0);
+          }
+        }
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(&tempty[buf]);
+      } else {
+        // split K: int32 partial of this split -> workspace
+        int32_t *part = p.ws + ((size_t)w.tile * p.splits + w.s) * (BM * BN) +
+                        (size_t)(q * 32 + lane) * BN;
+#pragma unroll 1
+        for (int ch = 0; ch < BN / 32; ++ch) {
+          uint32_t r[32];
+          ptx::tmem_ld_32x32(taddr + ch * 32, r);
+          ptx::tmem_ld_wait();
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            __stcg(reinterpret_cast<int4 *>(part + ch * 32) + c,
+                   make_int4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]));
+        }
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(&tempty[buf]);
+        __threadfence();
+        ptx::named_bar_sync(1, 128);
+        if (threadIdx.x == 64) {
+          const int prev = atomicAdd(p.counters + w.tile, 1);
+          s_last = (prev == p.splits - 1);
+        }
+        ptx::named_bar_sync(1, 128);
+        if (s_last) {
+          __threadfence();
+          const int32_t *base = p.ws + (size_t)w.tile * p.splits * (BM * BN) +
+                                (size_t)(q * 32 + lane) * BN;
+#pragma unroll 1
+          for (int ch = 0; ch < BN / 32; ++ch) {
+            const int col0 = w.n_t * BN + ch * 32;
+            if (col0 >= job.n) continue;
+            int acc[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc[i] = 0;
+            for (int s = 0; s < p.splits; ++s) {
+              const int4 *src = reinterpret_cast<const int4 *>(base + (size_t)s * (BM * BN) + ch * 32);
+#pragma unroll
+              for (int c = 0; c < 8; ++c) {
+                const int4 v = __ldcg(src + c);
+                acc[4 * c] += v.x;
+                acc[4 * c + 1] += v.y;
+                acc[4 * c + 2] += v.z;
+                acc[4 * c + 3] += v.w;
+              }
+            }
+            if (job.tma_store) {
+              uint8_t *stage = stage0 + (nstore & 1) * kEpiStageBytes;
+              if (lane == 0) ptx::bulk_wait_read<1>();
+              __syncwarp();
+              emit_chunk<true>(p, job, acc, xs, row, col0, lane, stage, tile_row0);
+              ++nstore;
+            } else {
+              emit_chunk<false>(p, job, acc, xs, row, col0, lane, nullptr, tile_row0);
+            }
+          }
+          ptx::named_bar_sync(1, 128);
+          if (threadIdx.x == 64) p.counters[w.tile] = 0;  // ready for the next launch
+        }
+      }
+    }
+    if (lane == 0) ptx::bulk_wait<0>();
+    __syncwarp();
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+int get_encode() {
+  std::call_once(g_encode_once, [] {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (!g_encode) return set_error("cuTensorMapEncodeTiled unavailable");
+  return 0;
+}
+
+int make_map_i8(CUtensorMap *m, const int8_t *base, int k, int rows, long stride, int box_rows) {
+  cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)stride};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t *>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error("tensor map (int8 %dx%d stride %ld) failed: %d", rows, k, stride, (int)r);
+  return 0;
+}
+
+int make_map_f32(CUtensorMap *m, float *base, int n, int rows, long stride_elems) {
+  cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)stride_elems * 4};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error("tensor map (f32 %dx%d) failed: %d", rows, n, (int)r);
+  return 0;
+}
+
+template <int BN>
+int launch_bn(TcParams &p, cudaStream_t st) {
+  using C = Cfg<BN>;
+  // the shared-memory opt-in is per device; set it once, outside any capture
+  static std::mutex mu;
+  static uint64_t done_mask = 0;
+  int dev = 0;
+  GCU_CUDA(cudaGetDevice(&dev));
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!(done_mask & (1ull << (dev & 63)))) {
+      GCU_CUDA(cudaFuncSetAttribute(k_gemm_i8_tc<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    C::SMEM));
+      done_mask |= 1ull << (dev & 63);
+    }
+  }
+  int grid = p.units < num_sms() ? p.units : num_sms();
+  k_gemm_i8_tc<BN><<<grid, kThreads, C::SMEM, st>>>(p);
+  GCU_CUDA(cudaGetLastError());
+  return 0;
+}
+
+double wave_eff(long units, int sms) {
+  long waves = (units + sms - 1) / sms;
+  return (double)units / (double)(waves * sms);
+}
+
+}  // namespace
+
+// Multi-job entry: jobs share A (src); job j has its own weights and output.
+int launch_gemm_tc_jobs(const int8_t *src, long sstr, const float *ssc, int m, int k,
+                        const GemmArgs *jobs, int njobs, cudaStream_t st, int force_bn,
+                        int force_split) {
+  if (njobs < 1 || njobs > kMaxJobs) return set_error("gemm: 1..%d jobs (got %d)", kMaxJobs, njobs);
+  if (m <= 0 || k <= 0) return 0;
+  if (get_encode()) return 1;
+  if ((uintptr_t)src % 16 || sstr % 16)
+    return set_error("gemm: activation rows must be 16-byte aligned (stride %ld)", sstr);
+  const int sms = num_sms();
+  const int tiles_m = (m + BM - 1) / BM;
+  int ntot128 = 0, ntot256 = 0;
+  for (int j = 0; j < njobs; ++j) {
+    ntot128 += (jobs[j].n + 127) / 128;
+    ntot256 += (jobs[j].n + 255) / 256;
+    if ((uintptr_t)jobs[j].mat % 16 || jobs[j].mstr % 16)
+      return set_error("gemm: weight rows must be 16-byte aligned (stride %ld)", jobs[j].mstr);
+  }
+  int bn = force_bn;
+  if (bn != 128 && bn != 256) {
+    const double e256 = wave_eff((long)tiles_m * ntot256, sms);
+    const double e128 = wave_eff((long)tiles_m * ntot128, sms);
+    bn = (e256 >= 0.85 || e256 >= e128) ? 256 : 128;
+  }
+  const int tiles_n = bn == 256 ? ntot256 : ntot128;
+  const int tiles = tiles_m * tiles_n;
+  const int kb_total = (k + BK - 1) / BK;
+  int splits = 1;
+  if (force_split > 0) {
+    splits = force_split;
+  } else if (tiles * 2 <= sms) {
+    splits = sms / tiles;
+    if (splits > kb_total / 2) splits = kb_total / 2;
+    if (splits > 16) splits = 16;
+    if (splits < 1) splits = 1;
+  }
+  if (splits > kb_total) splits = kb_total;
+  const int kb_per = (kb_total + splits - 1) / splits;
+  splits = (kb_total + kb_per - 1) / kb_per;
+
+  static_assert(sizeof(TcParams) <= 4096, "kernel parameters exceed 4 KB");
+  TcParams p;
+  memset(&p, 0, sizeof(p));
+  if (make_map_i8(&p.tmA, src, k, m, sstr, BM)) return 1;
+  int tn = 0;
+  for (int j = 0; j < njobs; ++j) {
+    TcJob &J = p.jobs[j];
+    if (make_map_i8(&J.tmB, jobs[j].mat, k, jobs[j].n, jobs[j].mstr, bn)) return 1;
+    J.tma_store = ((uintptr_t)jobs[j].dst % 16 == 0) && (jobs[j].dstr % 4 == 0);
+    if (J.tma_store && make_map_f32(&J.tmD, jobs[j].dst, jobs[j].n, m, jobs[j].dstr)) return 1;
+    J.matsc = jobs[j].matsc;
+    J.dst = jobs[j].dst;
+    J.dstr = jobs[j].dstr;
+    J.n = jobs[j].n;
+    J.tn_begin = tn;
+    tn += (jobs[j].n + bn - 1) / bn;
+  }
+  p.njobs = njobs;
+  p.m = m;
+  p.k = k;
+  p.tiles_m = tiles_m;
+  p.tiles_n = tiles_n;
+  p.splits = splits;
+  p.kb_total = kb_total;
+  p.kb_per_split = kb_per;
+  p.units = tiles * splits;
+  p.ssc = ssc;
+  p.err = dev_error_word();
+  if (splits > 1) {
+    void *ws = nullptr;
+    int *cnt = nullptr;
+    if (gemm_workspace((size_t)tiles * splits * BM * bn * sizeof(int32_t), &ws, &cnt, tiles, st))
+      return 1;
+    p.ws = static_cast<int32_t *>(ws);
+    p.counters = cnt;
+  }
+  return bn == 256 ? launch_bn<256>(p, st) : launch_bn<128>(p, st);
+}
+
+int launch_gemm_tc(const GemmArgs &a, cudaStream_t st, int force_bn, int force_split) {
+  return launch_gemm_tc_jobs(a.src, a.sstr, a.ssc, a.m, a.k, &a, 1, st, force_bn, force_split);
+}
+
+}  // namespace gcu

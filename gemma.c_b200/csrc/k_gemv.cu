@@ -1,0 +1,239 @@
+// k_gemv.cu -- K2: HBM-streaming int8 GEMV (decode) and small-batch GEMV.
+//
+// Device restatement of gemv_int8_row / gemv_int8 / gemv_int8_multi
+// (gemma.c:2754-2837), extended to mb <= 8 activation rows so that the same
+// kernel serves gemm_int8 calls with few tokens (batch-8 decode):
+//   y[b][i] = (float)(sum_k W[i,k] * x[b,k]) * (xs[b] * ws[i])
+// The int32 sum is exact (|sum| <= 15360*127^2 < 2^31) so any order gives
+// the reference's bits; the epilogue is the -ffast-math build's
+// (float)acc * (xs*ws) with explicit round-to-nearest multiplies.
+//
+// Roofline: HBM.  Each weight byte is read once (rows*k bytes + 4 per row
+// of scales); x (mb*k bytes) is staged once per CTA in shared memory.
+//
+// Layout of the work: a weight row is split over LPR lanes, each lane
+// streaming 16-byte chunks (ld.global.nc, no L1 allocation) of R rows at a
+// time with U chunks per row in flight, accumulating with dp4a; LPR-lane
+// shuffles reduce.  CTAs are persistent-ish (grid = SMs x occupancy) and
+// stride over row groups.
+#include "gcu_internal.cuh"
+
+#include <mutex>
+
+namespace gcu {
+namespace {
+
+constexpr int kThreads = 256;
+
+__device__ __forceinline__ int dot16(const int4 &w, const int4 &x, int acc) {
+  acc = __dp4a(w.x, x.x, acc);
+  acc = __dp4a(w.y, x.y, acc);
+  acc = __dp4a(w.z, x.z, acc);
+  acc = __dp4a(w.w, x.w, acc);
+  return acc;
+}
+
+__device__ __forceinline__ float dequant(int acc, float xs, float ws) {
+  return __fmul_rn(__int2float_rn(acc), __fmul_rn(xs, ws));
+}
+
+__device__ __forceinline__ void job_of(const GemvJobs &jobs, int row, int &j, int &local) {
+  j = 0;
+#pragma unroll
+  for (int t = 0; t < GCU_MAX_JOBS - 1; ++t)
+    if (t < jobs.njobs - 1 && row >= jobs.row_end[t]) j = t + 1;
+  local = row - (j > 0 ? jobs.row_end[j - 1] : 0);
+}
+
+// Vector kernel: k % 16 == 0, every weight row and x row 16-byte aligned.
+template <int MB, int LPR, int R, int U>
+__global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs,
+                                                       const int8_t *__restrict__ x,
+                                                       long xstride,
+                                                       const float *__restrict__ xs,
+                                                       int mb, long ystride, int k,
+                                                       int total_rows) {
+  extern __shared__ int4 xsm[];  // [MB][C] 16-byte chunks of x
+  const int C = k >> 4;
+  for (int i = threadIdx.x; i < MB * C; i += kThreads) {
+    const int b = i / C, c = i - b * C;
+    int4 v = make_int4(0, 0, 0, 0);
+    if (b < mb) v = *reinterpret_cast<const int4 *>(x + (size_t)b * xstride + (size_t)c * 16);
+    xsm[i] = v;
+  }
+  float xsc[MB];
+#pragma unroll
+  for (int b = 0; b < MB; ++b) xsc[b] = b < mb ? xs[b] : 0.0f;
+  __syncthreads();
+
+  const int lane = threadIdx.x & 31;
+  const int slot = lane / LPR, sub = lane % LPR;
+  constexpr int kRowsPerWarp = (32 / LPR) * R;
+  const int nwarps = gridDim.x * (kThreads / 32);
+  for (int base = (blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5)) * kRowsPerWarp;
+       base < total_rows; base += nwarps * kRowsPerWarp) {
+    const int8_t *wp[R];
+    bool valid[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int row = base + slot * R + r;
+      valid[r] = row < total_rows;
+      int j, local;
+      job_of(jobs, valid[r] ? row : total_rows - 1, j, local);
+      wp[r] = jobs.w[j] + (size_t)local * k;
+    }
+    int acc[R][MB];
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int b = 0; b < MB; ++b) acc[r][b] = 0;
+
+    for (int c0 = sub; c0 < C; c0 += LPR * U) {
+      int4 wv[U][R];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int c = c0 + u * LPR;
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+          wv[u][r] = (c < C && valid[r]) ? ptx::ld_stream_v4(wp[r] + (size_t)c * 16)
+                                         : make_int4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int c = c0 + u * LPR;
+        if (c < C) {
+#pragma unroll
+          for (int b = 0; b < MB; ++b) {
+            const int4 xv = xsm[b * C + c];
+#pragma unroll
+            for (int r = 0; r < R; ++r) acc[r][b] = dot16(wv[u][r], xv, acc[r][b]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int o = LPR / 2; o > 0; o >>= 1)
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int b = 0; b < MB; ++b) acc[r][b] += __shfl_xor_sync(0xffffffffu, acc[r][b], o);
+
+    if (sub == 0) {
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        if (!valid[r]) continue;
+        int j, local;
+        job_of(jobs, base + slot * R + r, j, local);
+        const float ws = jobs.ws[j][local];
+#pragma unroll
+        for (int b = 0; b < MB; ++b)
+          if (b < mb) jobs.y[j][(size_t)b * ystride + local] = dequant(acc[r][b], xsc[b], ws);
+      }
+    }
+  }
+}
+
+// Generic kernel: any k, any alignment.  One warp per weight row, byte loads.
+__global__ void __launch_bounds__(kThreads) k_gemv_any(const GemvJobs jobs,
+                                                       const int8_t *__restrict__ x,
+                                                       long xstride,
+                                                       const float *__restrict__ xs,
+                                                       int mb, long ystride, int k,
+                                                       int total_rows) {
+  const int lane = threadIdx.x & 31;
+  const int nwarps = gridDim.x * (kThreads / 32);
+  for (int row = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); row < total_rows;
+       row += nwarps) {
+    int j, local;
+    job_of(jobs, row, j, local);
+    const int8_t *w = jobs.w[j] + (size_t)local * k;
+    int acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int l = lane; l < k; l += 32) {
+      const int wv = w[l];
+#pragma unroll
+      for (int b = 0; b < 8; ++b)
+        if (b < mb) acc[b] += wv * (int)x[(size_t)b * xstride + l];
+    }
+#pragma unroll
+    for (int b = 0; b < 8; ++b)
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc[b] += __shfl_xor_sync(0xffffffffu, acc[b], o);
+    if (lane == 0) {
+      const float ws = jobs.ws[j][local];
+      for (int b = 0; b < mb; ++b)
+        jobs.y[j][(size_t)b * ystride + local] = dequant(acc[b], xs[b], ws);
+    }
+  }
+}
+
+template <int MB, int LPR>
+int launch_v16(const GemvJobs &jobs, const int8_t *x, long xstride, const float *xs, int mb,
+               long ystride, int k, int total_rows, cudaStream_t st) {
+  constexpr int R = 2;
+  constexpr int U = (MB >= 4) ? 2 : 4;
+  auto kern = k_gemv_v16<MB, LPR, R, U>;
+  const size_t smem = (size_t)MB * k;
+  static std::once_flag once;
+  static int regs = 0;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    cudaFuncAttributes fa;
+    attr_err = cudaFuncGetAttributes(&fa, kern);
+    regs = fa.numRegs;
+  });
+  GCU_CUDA(attr_err);
+  if (smem > 48 * 1024)
+    GCU_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  // resident CTAs per SM from registers (64K per SM) and shared memory
+  // (228 KB per SM, 1 KB reserved per CTA), at most 2048 threads per SM
+  int by_regs = 65536 / ((regs > 0 ? regs : 64) * kThreads);
+  int by_smem = (int)((228 * 1024) / (smem + 1024));
+  int blocks_per_sm = by_regs < by_smem ? by_regs : by_smem;
+  if (blocks_per_sm > 2048 / kThreads) blocks_per_sm = 2048 / kThreads;
+  if (blocks_per_sm < 1) blocks_per_sm = 1;
+  constexpr int rows_per_block = (32 / LPR) * R * (kThreads / 32);
+  long need = ((long)total_rows + rows_per_block - 1) / rows_per_block;
+  long cap = (long)num_sms() * blocks_per_sm;
+  const int grid = (int)(need < cap ? need : cap);
+  kern<<<grid, kThreads, smem, st>>>(jobs, x, xstride, xs, mb, ystride, k, total_rows);
+  GCU_CUDA(cudaGetLastError());
+  return 0;
+}
+
+template <int MB>
+int launch_mb(const GemvJobs &jobs, const int8_t *x, long xstride, const float *xs, int mb,
+              long ystride, int k, int total_rows, cudaStream_t st) {
+  const int C = k / 16;
+  if (C >= 128) return launch_v16<MB, 32>(jobs, x, xstride, xs, mb, ystride, k, total_rows, st);
+  if (C >= 64) return launch_v16<MB, 16>(jobs, x, xstride, xs, mb, ystride, k, total_rows, st);
+  return launch_v16<MB, 8>(jobs, x, xstride, xs, mb, ystride, k, total_rows, st);
+}
+
+}  // namespace
+
+int launch_gemv(const GemvJobs &jobs, const int8_t *x, long xstride, const float *xs, int mb,
+                long ystride, int k, cudaStream_t st) {
+  if (jobs.njobs <= 0 || mb <= 0) return 0;
+  if (mb > 8) return set_error("gemv: at most 8 activation rows (got %d)", mb);
+  const int total_rows = jobs.row_end[jobs.njobs - 1];
+  if (total_rows <= 0) return 0;
+  if (k <= 0) return set_error("gemv: k must be positive (got %d)", k);
+  const int mb_pad = mb == 1 ? 1 : mb == 2 ? 2 : mb <= 4 ? 4 : 8;
+  bool vec = (k % 16 == 0) && ((uintptr_t)x % 16 == 0) && (mb == 1 || xstride % 16 == 0) &&
+             (size_t)mb_pad * k <= 200 * 1024;
+  for (int j = 0; j < jobs.njobs && vec; ++j) vec = ((uintptr_t)jobs.w[j] % 16 == 0);
+  if (vec) {
+    if (mb == 1) return launch_mb<1>(jobs, x, xstride, xs, mb, ystride, k, total_rows, st);
+    if (mb == 2) return launch_mb<2>(jobs, x, xstride, xs, mb, ystride, k, total_rows, st);
+    if (mb <= 4) return launch_mb<4>(jobs, x, xstride, xs, mb, ystride, k, total_rows, st);
+    return launch_mb<8>(jobs, x, xstride, xs, mb, ystride, k, total_rows, st);
+  }
+  long need = ((long)total_rows + 7) / 8;
+  long cap = (long)num_sms() * 8;
+  const int grid = (int)(need < cap ? need : cap);
+  k_gemv_any<<<grid, kThreads, 0, st>>>(jobs, x, xstride, xs, mb, ystride, k, total_rows);
+  GCU_CUDA(cudaGetLastError());
+  return 0;
+}
+
+}  // namespace gcu

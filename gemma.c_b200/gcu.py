@@ -1,0 +1,246 @@
+"""Python host binding of libgcu.so (ctypes over the C ABI in include/gcu.h).
+
+The functions mirror gemma.c's hot-path interface -- same names, same
+argument meaning (gemma.c:2590 quantize_act, 2656 quantize_acts, 2770
+gemv_int8, 2818 gemv_int8_multi, 3943 gemm_int8) -- on numpy host arrays,
+plus ``dev_*`` variants on CUDA tensors (torch is only the allocator and
+stream provider here).  There is no CPU fallback: importing this module
+without a built libgcu.so raises, and calls fail loudly on error.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libgcu.so")
+
+_i8p = ctypes.POINTER(ctypes.c_int8)
+_f32p = ctypes.POINTER(ctypes.c_float)
+_vp = ctypes.c_void_p
+_int = ctypes.c_int
+
+
+class GemvJob(ctypes.Structure):
+    """gcu_gemv_job == gemma.c:2795 GemvJob (floatx = float)."""
+    _fields_ = [("w", ctypes.c_void_p), ("sc", ctypes.c_void_p), ("dst", ctypes.c_void_p), ("m", ctypes.c_int)]
+
+
+class GcuError(RuntimeError):
+    pass
+
+
+# every symbol include/gcu.h declares, with (restype, argtypes)
+SIGNATURES = {
+    "gcu_init": (_int, [_int]),
+    "gcu_shutdown": (_int, []),
+    "gcu_last_error": (ctypes.c_char_p, []),
+    "gcu_check_device": (_int, []),
+    "gcu_version": (ctypes.c_char_p, []),
+    "gcu_register_weight": (_int, [_vp, _vp, _int, _int]),
+    "gcu_unregister_weight": (_int, [_vp]),
+    "gcu_registered_bytes": (ctypes.c_size_t, []),
+    "gcu_quantize_act": (ctypes.c_float, [_vp, _vp, _int]),
+    "gcu_quantize_acts": (_int, [_vp, _vp, _vp, _int, _int, _int]),
+    "gcu_gemv_int8": (_int, [_vp, _vp, _vp, _vp, ctypes.c_float, _int, _int]),
+    "gcu_gemv_int8_multi": (_int, [ctypes.POINTER(GemvJob), _int, _vp, ctypes.c_float, _int]),
+    "gcu_gemm_int8": (_int, [_vp, _int, _vp, _int, _vp, _vp, _int, _vp, _int, _int, _int]),
+    "gcu_dev_quantize_acts": (_int, [_vp, _vp, _vp, _int, _int, _int, _vp]),
+    "gcu_dev_gemv_int8": (_int, [_vp, _vp, _vp, _vp, _vp, _int, _int, _vp]),
+    "gcu_dev_gemv_int8_multi": (_int, [ctypes.POINTER(GemvJob), _int, _vp, _vp, _int, _vp]),
+    "gcu_dev_gemm_int8": (_int, [_vp, _int, _vp, _int, _vp, _vp, _int, _vp, _int, _int, _int, _vp]),
+    "gcu_dev_gemm_int8_multi": (_int, [ctypes.POINTER(GemvJob), _int, _vp, _int, _vp, _int, _int, _vp]),
+    "gcu_comm_unique_id": (_int, [ctypes.c_char_p]),
+    "gcu_comm_init": (_int, [_int, _int, ctypes.c_char_p]),
+    "gcu_comm_destroy": (_int, []),
+    "gcu_dev_gemm_int8_rowshard": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _int, _vp]),
+}
+# exported but not part of the public header (benchmark sweeps)
+EXTRA = {
+    "gcu_dev_gemm_int8_tuned": (_int, [_vp, _int, _vp, _int, _vp, _vp, _int, _vp, _int, _int, _int,
+                                       _int, _int, _vp]),
+}
+
+
+def build() -> None:
+    """Compile libgcu.so in-tree (nvcc, sm_100a)."""
+    subprocess.run(["make", "-s", "-C", HERE, "-j4"], check=True)
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise GcuError(f"libgcu.so not built ({LIB_PATH}); run make -C gemma.c_b200")
+        l = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in {**SIGNATURES, **EXTRA}.items():
+            f = getattr(l, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = l
+    return _lib
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise GcuError(f"{what}: {lib().gcu_last_error().decode()}")
+
+
+def _p(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+def init(device: int = 0) -> None:
+    _check(lib().gcu_init(device), "gcu_init")
+
+
+def shutdown() -> None:
+    _check(lib().gcu_shutdown(), "gcu_shutdown")
+
+
+def check_device() -> None:
+    _check(lib().gcu_check_device(), "device")
+
+
+def register_weight(q: np.ndarray, scales: np.ndarray) -> None:
+    """Upload a QTensor (int8 [rows][k] + fp32 [rows]) once; the arrays must
+    stay alive and unchanged while registered."""
+    assert q.dtype == np.int8 and q.ndim == 2 and q.flags["C_CONTIGUOUS"]
+    assert scales.dtype == np.float32 and scales.shape == (q.shape[0],)
+    _check(lib().gcu_register_weight(_p(q), _p(scales), q.shape[0], q.shape[1]), "register_weight")
+
+
+def unregister_weight(q: np.ndarray) -> None:
+    _check(lib().gcu_unregister_weight(_p(q)), "unregister_weight")
+
+
+# --------------------------------------------------------------------------
+# host-pointer API (gemma.c semantics; numpy in, numpy out)
+# --------------------------------------------------------------------------
+
+def quantize_act(vec: np.ndarray):
+    """gemma.c:2590 -> (int8 codes, fp32 scale)."""
+    vec = np.ascontiguousarray(vec, np.float32)
+    dst = np.empty(vec.shape[0], np.int8)
+    sc = lib().gcu_quantize_act(_p(dst), _p(vec), vec.shape[0])
+    if np.isnan(sc):
+        raise GcuError("quantize_act: " + lib().gcu_last_error().decode())
+    return dst, np.float32(sc)
+
+
+def quantize_acts(src: np.ndarray, n: int | None = None, sstr: int = 0):
+    """gemma.c:2656 on an (m, sstr) fp32 array -> int8 (m, n), fp32 (m,)."""
+    src = np.ascontiguousarray(src, np.float32)
+    m = src.shape[0]
+    n = src.shape[1] if n is None else n
+    dst = np.empty((m, n), np.int8)
+    dsc = np.empty(m, np.float32)
+    _check(lib().gcu_quantize_acts(_p(dst), _p(dsc), _p(src), sstr, m, n), "quantize_acts")
+    return dst, dsc
+
+
+def gemv_int8(mat, matsc, vec, vsc, dst=None):
+    """gemma.c:2770: mat (m, n) int8, returns fp32 (m,)."""
+    m, n = mat.shape
+    if dst is None:
+        dst = np.empty(m, np.float32)
+    _check(lib().gcu_gemv_int8(_p(dst), _p(mat), _p(matsc), _p(vec), float(vsc), m, n), "gemv_int8")
+    return dst
+
+
+def gemv_int8_multi(mats, scs, vec, vsc, outs=None):
+    """gemma.c:2818: several (rows_j, n) weights sharing vec."""
+    if outs is None:
+        outs = [np.empty(w.shape[0], np.float32) for w in mats]
+    jobs = (GemvJob * len(mats))()
+    for j, (w, s, o) in enumerate(zip(mats, scs, outs)):
+        jobs[j] = GemvJob(_p(w), _p(s), _p(o), w.shape[0])
+    _check(lib().gcu_gemv_int8_multi(jobs, len(mats), _p(vec), float(vsc), vec.shape[0]), "gemv_int8_multi")
+    return outs
+
+
+def gemm_int8(mat, matsc, src, ssc, dst=None, dstr=0, mstr=0, sstr=0, m=None, n=None, k=None):
+    """gemma.c:3943 NT GEMM; with strides, pass flat buffers and m, n, k."""
+    if m is None:
+        m, k = src.shape
+        n = mat.shape[0]
+    if dst is None:
+        dst = np.zeros((m, n), np.float32)
+    _check(lib().gcu_gemm_int8(_p(dst), dstr, _p(mat), mstr, _p(matsc), _p(src), sstr, _p(ssc), m, n, k),
+           "gemm_int8")
+    return dst
+
+
+# --------------------------------------------------------------------------
+# device-pointer API on torch CUDA tensors (enqueued on torch's current stream)
+# --------------------------------------------------------------------------
+
+def _stream(stream=None) -> int:
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def dev_quantize_acts(dst, dsc, src, m, n, sstr=0, stream=None):
+    _check(lib().gcu_dev_quantize_acts(dst.data_ptr(), dsc.data_ptr(), src.data_ptr(), sstr, m, n,
+                                       _stream(stream)), "dev_quantize_acts")
+
+
+def dev_gemv_int8(dst, mat, matsc, vec, vsc, m, n, stream=None):
+    _check(lib().gcu_dev_gemv_int8(dst.data_ptr(), mat.data_ptr(), matsc.data_ptr(), vec.data_ptr(),
+                                   vsc.data_ptr(), m, n, _stream(stream)), "dev_gemv_int8")
+
+
+def dev_gemv_int8_multi(jobs_t, vec, vsc, n, stream=None):
+    """jobs_t: list of (w, sc, dst) device tensors."""
+    jobs = (GemvJob * len(jobs_t))()
+    for j, (w, s, o) in enumerate(jobs_t):
+        jobs[j] = GemvJob(w.data_ptr(), s.data_ptr(), o.data_ptr(), w.shape[0])
+    _check(lib().gcu_dev_gemv_int8_multi(jobs, len(jobs_t), vec.data_ptr(), vsc.data_ptr(), n,
+                                         _stream(stream)), "dev_gemv_int8_multi")
+
+
+def dev_gemm_int8(dst, mat, matsc, src, ssc, m, n, k, dstr=0, mstr=0, sstr=0, stream=None):
+    _check(lib().gcu_dev_gemm_int8(dst.data_ptr(), dstr, mat.data_ptr(), mstr, matsc.data_ptr(),
+                                   src.data_ptr(), sstr, ssc.data_ptr(), m, n, k, _stream(stream)),
+           "dev_gemm_int8")
+
+
+def dev_gemm_int8_multi(jobs_t, src, ssc, m, k, sstr=0, stream=None):
+    jobs = (GemvJob * len(jobs_t))()
+    for j, (w, s, o) in enumerate(jobs_t):
+        jobs[j] = GemvJob(w.data_ptr(), s.data_ptr(), o.data_ptr(), w.shape[0])
+    _check(lib().gcu_dev_gemm_int8_multi(jobs, len(jobs_t), src.data_ptr(), sstr, ssc.data_ptr(), m, k,
+                                         _stream(stream)), "dev_gemm_int8_multi")
+
+
+def dev_gemm_int8_tuned(dst, mat, matsc, src, ssc, m, n, k, bn, split, stream=None):
+    _check(lib().gcu_dev_gemm_int8_tuned(dst.data_ptr(), 0, mat.data_ptr(), 0, matsc.data_ptr(),
+                                         src.data_ptr(), 0, ssc.data_ptr(), m, n, k, bn, split,
+                                         _stream(stream)), "dev_gemm_int8_tuned")
+
+
+def comm_unique_id() -> bytes:
+    buf = ctypes.create_string_buffer(128)
+    _check(lib().gcu_comm_unique_id(buf), "comm_unique_id")
+    return buf.raw
+
+
+def comm_init(rank: int, world: int, uid: bytes) -> None:
+    _check(lib().gcu_comm_init(rank, world, uid), "comm_init")
+
+
+def comm_destroy() -> None:
+    _check(lib().gcu_comm_destroy(), "comm_destroy")
+
+
+def dev_gemm_int8_rowshard(dst, work, mat_local, matsc_local, src, ssc, m, n, k, stream=None):
+    _check(lib().gcu_dev_gemm_int8_rowshard(dst.data_ptr(), work.data_ptr(), mat_local.data_ptr(),
+                                            matsc_local.data_ptr(), src.data_ptr(), ssc.data_ptr(),
+                                            m, n, k, _stream(stream)), "dev_gemm_int8_rowshard")

@@ -1,0 +1,142 @@
+"""Seeded synthetic inputs and the workload shapes of the benchmark configs.
+
+No model files or datasets exist for this path, so inputs are synthetic with
+the shapes and value distributions of the Gemma-3 configs:
+
+* weights  fp32 N(0, 0.02), quantized per output row the way the exporter
+  does it (model.py:151-161 Linear.quantize via export.py:430-457):
+  s = max(amax, 1e-8) / 127, q = round-half-even(w / s), clamp +-127;
+* activations fp32 N(0, 1), optionally with 1% outlier channels x20.
+
+Small tensors come from a counter-based splitmix64 -> Box-Muller generator
+(seed 0x5EED0000 + tensor id), identical on every machine up to the last
+float64 ulp of libm's log/cos; large benchmark tensors are drawn on the GPU
+with torch's seeded generator.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+SEED_BASE = 0x5EED0000
+_GOLDEN = np.uint64(0x9E3779B97F4A7C15)
+_M1 = np.uint64(0xBF58476D1CE4E5B9)
+_M2 = np.uint64(0x94D049BB133111EB)
+
+
+def splitmix64(seed: int, count: int) -> np.ndarray:
+    """The first `count` outputs of splitmix64 started at state `seed`."""
+    with np.errstate(over="ignore"):
+        i = np.arange(1, count + 1, dtype=np.uint64)
+        z = np.uint64(seed) + i * _GOLDEN
+        z = (z ^ (z >> np.uint64(30))) * _M1
+        z = (z ^ (z >> np.uint64(27))) * _M2
+        return z ^ (z >> np.uint64(31))
+
+
+def normal(tensor_id: int, shape, std: float = 1.0) -> np.ndarray:
+    """fp32 N(0, std^2) of the given shape from seed SEED_BASE + tensor_id."""
+    n = int(np.prod(shape))
+    pairs = (n + 1) // 2
+    u = splitmix64(SEED_BASE + tensor_id, 2 * pairs)
+    u1 = ((u[0::2] >> np.uint64(11)).astype(np.float64) + 1.0) * (1.0 / 9007199254740992.0)
+    u2 = (u[1::2] >> np.uint64(11)).astype(np.float64) * (1.0 / 9007199254740992.0)
+    r = np.sqrt(-2.0 * np.log(u1))
+    z = np.empty(2 * pairs, np.float64)
+    z[0::2] = r * np.cos(2.0 * math.pi * u2)
+    z[1::2] = r * np.sin(2.0 * math.pi * u2)
+    return (z[:n] * std).astype(np.float32).reshape(shape)
+
+
+def outlier_columns(tensor_id: int, k: int, frac: float = 0.01) -> np.ndarray:
+    """ceil(frac*k) distinct seeded column indices."""
+    c = int(math.ceil(frac * k))
+    h = splitmix64(SEED_BASE + 0x10000 + tensor_id, k)
+    return np.sort(np.argsort(h, kind="stable")[:c])
+
+
+def activations(tensor_id: int, m: int, k: int, outliers: bool = False) -> np.ndarray:
+    x = normal(tensor_id, (m, k), 1.0)
+    if outliers:
+        x[:, outlier_columns(tensor_id, k)] *= 20.0
+    return x
+
+
+def quantize_weight_rows(w: np.ndarray):
+    """Exporter quantizer (model.py:151-161) in numpy fp32 arithmetic."""
+    w = np.asarray(w, np.float32)
+    amax = np.maximum(np.abs(w).max(axis=1), np.float32(1e-8)).astype(np.float32)
+    s = (amax / np.float32(127.0)).astype(np.float32)
+    q = np.clip(np.rint(w / s[:, None]), -127, 127).astype(np.int8)
+    return q, s
+
+
+def weight(tensor_id: int, rows: int, k: int, std: float = 0.02):
+    """Seeded N(0, std) weight quantized per row -> (int8 [rows][k], fp32 [rows])."""
+    return quantize_weight_rows(normal(tensor_id, (rows, k), std))
+
+
+# --------------------------------------------------------------------------
+# GPU generation for the large benchmark tensors (torch is the allocator)
+# --------------------------------------------------------------------------
+
+def weight_torch(rows: int, k: int, gen, device, std: float = 0.02, chunk_rows: int = 16384):
+    """Same quantizer on the GPU, row chunk by row chunk (bounded temporaries)."""
+    import torch
+    q = torch.empty((rows, k), dtype=torch.int8, device=device)
+    s = torch.empty((rows,), dtype=torch.float32, device=device)
+    for r0 in range(0, rows, chunk_rows):
+        r1 = min(rows, r0 + chunk_rows)
+        w = torch.randn((r1 - r0, k), generator=gen, device=device, dtype=torch.float32) * std
+        amax = w.abs().amax(1, keepdim=True).clamp_min(1e-8)
+        sc = amax / 127.0
+        q[r0:r1] = torch.round(w / sc).clamp(-127, 127).to(torch.int8)
+        s[r0:r1] = sc.squeeze(1)
+        del w
+    return q, s
+
+
+def activations_torch(m: int, k: int, gen, device, outliers: bool = False, cols=None):
+    import torch
+    x = torch.randn((m, k), generator=gen, device=device, dtype=torch.float32)
+    if outliers:
+        if cols is None:
+            c = int(math.ceil(0.01 * k))
+            cols = torch.randperm(k, generator=gen, device=device)[:c]
+        x[:, cols] *= 20.0
+    return x
+
+
+# --------------------------------------------------------------------------
+# the Gemma-3 shapes of the benchmark configs
+# --------------------------------------------------------------------------
+# per layer: (name, rows n, reduction k); "qkv"/"gu" groups share one input
+CONFIGS = {
+    "270m": dict(layers=18, dim=640, q=1024, kv=256, ffn=2048, vocab=262144),
+    "1b": dict(layers=26, dim=1152, q=1024, kv=256, ffn=6912, vocab=262144),
+    "4b": dict(layers=34, dim=2560, q=2048, kv=1024, ffn=10240, vocab=262144),
+    "12b": dict(layers=48, dim=3840, q=4096, kv=2048, ffn=15360, vocab=262144),
+    "siglip": dict(layers=27, dim=1152, q=1152, kv=1152, ffn=4304, vocab=0),
+}
+
+
+def layer_groups(cfg: dict):
+    """The W8A8 calls of one layer, in gemma.c's order (gemma.c:4768-4930 /
+    5034-5391): each group is (input width k, [(name, rows)...]) sharing one
+    quantized input."""
+    d, q, kv, f = cfg["dim"], cfg["q"], cfg["kv"], cfg["ffn"]
+    return [
+        (d, [("wq", q), ("wk", kv), ("wv", kv)]),
+        (q, [("wo", d)]),
+        (d, [("w1_up", f), ("w2_gate", f)]),
+        (f, [("w3_down", d)]),
+    ]
+
+
+def layer_ops(cfg: dict, m: int) -> int:
+    return sum(2 * m * n * k for k, jobs in layer_groups(cfg) for _, n in jobs)
+
+
+def layer_weight_bytes(cfg: dict) -> int:
+    return sum(n * k + 4 * n for k, jobs in layer_groups(cfg) for _, n in jobs)

@@ -1,0 +1,154 @@
+/*
+ * gcu.h -- C ABI of libgcu.so, the B200 (sm_100a) W8A8 matmul hot path of
+ * Gemma.c.
+ *
+ * The reference keeps the path in five `static` functions of gemma.c; this
+ * library exports one entry point per function with the same argument
+ * meaning, plus device-pointer variants for callers whose activations already
+ * live in GPU memory.  Everything is plain C: pointers, ints, floats.
+ *
+ * Conventions shared by every entry point:
+ *   - return 0 on success and 1 on error (gemma.c's gemm_int8 convention,
+ *     gemma.c:3977-3982); gcu_last_error() then holds a message.  The
+ *     message is thread local, like gemma.c's g_err (gemma.c:577).
+ *   - "host" entry points take HOST pointers exactly as gemma.c passes them
+ *     and return when the result is in host memory.  Weights should be
+ *     registered once (gcu_register_weight) so calls find their device copy;
+ *     an unregistered weight is uploaded for that call only.
+ *   - "dev" entry points take DEVICE pointers and a cudaStream_t (as void*,
+ *     NULL = the legacy default stream) and only enqueue work.
+ *   - every entry point may be called concurrently from several host threads
+ *     (gemma.c calls gemm_int8 from inside OpenMP regions, gemma.c:5045-5091);
+ *     each thread gets its own stream and staging buffers.
+ *   - weight layout is gemma.c's QTensor (gemma.c:1102-1131): int8 values
+ *     row-major [rows][k] followed by one fp32 scale per row.
+ */
+#ifndef GCU_H
+#define GCU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GCU_MAX_JOBS 8
+
+/* ---- lifecycle ---------------------------------------------------------- */
+
+/* Select the CUDA device the calling thread uses (default 0). Idempotent. */
+int gcu_init(int device);
+/* Free every registered weight, stream and buffer of this process. */
+int gcu_shutdown(void);
+/* Thread-local message of the last failed call ("" if none). */
+const char *gcu_last_error(void);
+/* Wait for the device and return 1 if a kernel recorded a device-side error
+ * (a bounded wait that gave up), clearing it; 0 otherwise. */
+int gcu_check_device(void);
+/* Library version string. */
+const char *gcu_version(void);
+
+/* ---- weight registry ------------------------------------------------------
+ * Replaces nothing in gemma.c: it is the hook a maintainer adds after the
+ * weights are read or mapped (read_qtensor / mmap_qtensor, gemma.c:1134-1171;
+ * setup_gemma_model, gemma.c:6867).  q points at rows*k int8 values, scales
+ * at rows floats.  Any pointer INSIDE a registered range (gemma.c passes
+ * w->i8.q + hd*hdim*dim, gemma.c:5080-5086) resolves to the device copy. */
+int gcu_register_weight(const int8_t *q, const float *scales, int rows, int k);
+int gcu_unregister_weight(const int8_t *q);
+/* Bytes of device memory held by registered weights. */
+size_t gcu_registered_bytes(void);
+
+/* ---- host-pointer entry points (gemma.c signatures) ----------------------- */
+
+/* gemma.c:2590 quantize_act: per-vector symmetric int8 of vec[0..dim);
+ * returns the scale (the reference returns floatx).  On error returns NaN. */
+float gcu_quantize_act(int8_t *dst, const float *vec, int dim);
+
+/* gemma.c:2656 quantize_acts: m rows of src (row stride sstr floats, 0 = n)
+ * to dense int8 dst (m, n) and scales dsc (m). */
+int gcu_quantize_acts(int8_t *dst, float *dsc, const float *src, int sstr,
+                      int m, int n);
+
+/* gemma.c:2770 gemv_int8: dst[i] = dequant(dot(mat row i, vec)), i < m,
+ * reduction length n (note: m = rows, n = k, as in the reference). */
+int gcu_gemv_int8(float *dst, const int8_t *mat, const float *matsc,
+                  const int8_t *vec, float vsc, int m, int n);
+
+/* gemma.c:2795 GemvJob (floatx = float). */
+typedef struct {
+  const void *w;
+  const float *sc;
+  float *dst;
+  int m;
+} gcu_gemv_job;
+
+/* gemma.c:2818 gemv_int8_multi: up to GCU_MAX_JOBS GEMVs sharing vec. */
+int gcu_gemv_int8_multi(const gcu_gemv_job *jobs, int njobs, const int8_t *vec,
+                        float vsc, int n);
+
+/* gemma.c:3943 gemm_int8: NT GEMM
+ *   dst[i*dstr + j] = (float)sum_l src[i*sstr+l]*mat[j*mstr+l] * (ssc[i]*matsc[j])
+ * for i < m (tokens), j < n (weight rows), l < k; strides 0 = dense. */
+int gcu_gemm_int8(float *dst, int dstr, const int8_t *mat, int mstr,
+                  const float *matsc, const int8_t *src, int sstr,
+                  const float *ssc, int m, int n, int k);
+
+/* ---- device-pointer entry points ------------------------------------------
+ * Same arithmetic as the host entry points; all pointers are device
+ * pointers; work is enqueued on `stream` and not waited for. */
+
+/* quantize_acts on device data. */
+int gcu_dev_quantize_acts(int8_t *dst, float *dsc, const float *src, int sstr,
+                          int m, int n, void *stream);
+
+/* gemv_int8 on device data; vsc points at the one device-resident scale
+ * written by gcu_dev_quantize_acts. */
+int gcu_dev_gemv_int8(float *dst, const int8_t *mat, const float *matsc,
+                      const int8_t *vec, const float *vsc, int m, int n,
+                      void *stream);
+
+/* gemv_int8_multi on device data (jobs hold device pointers; the job array
+ * itself is host memory). */
+int gcu_dev_gemv_int8_multi(const gcu_gemv_job *jobs, int njobs,
+                            const int8_t *vec, const float *vsc, int n,
+                            void *stream);
+
+/* gemm_int8 on device data. m <= 8 runs the streaming GEMV kernel, larger m
+ * the tcgen05 tensor-core kernel; both give the same bits. */
+int gcu_dev_gemm_int8(float *dst, int dstr, const int8_t *mat, int mstr,
+                      const float *matsc, const int8_t *src, int sstr,
+                      const float *ssc, int m, int n, int k, void *stream);
+
+/* One A operand against several weights in one launch, e.g. the prefill
+ * Q/K/V projections (gemma.c:5045-5091) or up/gate (gemma.c:5367-5372):
+ * job j writes dst_j (m, rows_j) dense.  Weights must be dense [rows_j][k]. */
+int gcu_dev_gemm_int8_multi(const gcu_gemv_job *jobs, int njobs,
+                            const int8_t *src, int sstr, const float *ssc,
+                            int m, int k, void *stream);
+
+/* ---- row-sharded entry points (NCCL over NVLink) ---------------------------
+ * No counterpart in the reference, which is single-process (README.md:614).
+ * Rank r of `world` owns weight rows [r*n/world, (r+1)*n/world) of an n-row
+ * matrix (n divisible by world) and computes that slice; the slices are
+ * all-gathered so every rank ends with the full output. */
+
+/* 128-byte NCCL unique id, created on one rank and given to all. */
+int gcu_comm_unique_id(unsigned char id[128]);
+int gcu_comm_init(int rank, int world, const unsigned char id[128]);
+int gcu_comm_destroy(void);
+
+/* dst (m, n) dense = sharded gemm_int8 with this rank's rows mat_local
+ * (n/world rows) and scales matsc_local.  `work` is device scratch of
+ * m*n floats used as the all-gather buffer.  m <= 8 uses the GEMV kernel. */
+int gcu_dev_gemm_int8_rowshard(float *dst, float *work,
+                               const int8_t *mat_local,
+                               const float *matsc_local, const int8_t *src,
+                               const float *ssc, int m, int n, int k,
+                               void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GCU_H */

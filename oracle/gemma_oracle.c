@@ -1,0 +1,165 @@
+/*
+ * gemma_oracle.c -- CPU restatement of Gemma.c's W8A8 matmul hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the checker the CUDA library is
+ * compared against; nothing in the product links it.  Only tests/, the
+ * smoke() entry point and bench.py's cpu_baseline leg load it.
+ *
+ * Parity pinning: the reference ships no tests or golden vectors, so this
+ * restatement is pinned against the reference's own functions compiled from
+ * gemma.c by oracle/Makefile (target `ref`, output in oracle/_ref/), through
+ * the committed fixtures in tests/golden/ and a randomized cross-check.
+ *
+ * Arithmetic follows the reference built the way its Makefile builds it
+ * (-O3 -ffast-math -march=native).  Under -ffast-math gcc rewrites three
+ * expressions of the source, and this file states the rewritten forms:
+ *   scale = amax * (1/127)      for `amax / 127.0f`        (gemma.c:2615)
+ *   inv   = 127 / amax          for `1.0f / scale`         (gemma.c:2616)
+ *   y     = (float)acc * (xs*ws) for `acc * xs * ws`       (gemma.c:2762, 3862)
+ * This file must itself be compiled WITHOUT fast-math and without FMA
+ * contraction (-O3 -ffp-contract=off), so the C text is the arithmetic.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+/* Per-vector symmetric int8 quantization, gemma.c:2586-2650 (quantize_act).
+ * Round half away from zero by truncating v +/- 0.5 (gemma.c:2628-2631 and
+ * 2642-2645), clamp to [-127, 127].  amax == 0 gives scale 1, inv 1. */
+float orc_quantize_act(int8_t *dst, const float *vec, int dim) {
+  float amax = 0.0f;
+  for (int d = 0; d < dim; d++) {
+    float a = fabsf(vec[d]);
+    amax = a > amax ? a : amax;
+  }
+  float scale = amax > 0.0f ? amax * (1.0f / 127.0f) : 1.0f;
+  float inv = amax > 0.0f ? 127.0f / amax : 1.0f;
+  for (int d = 0; d < dim; d++) {
+    float v = vec[d] * inv;
+    float t = v + (signbit(v) ? -0.5f : 0.5f);
+    int q = (int)t; /* C conversion truncates toward zero */
+    dst[d] = (int8_t)(q > 127 ? 127 : (q < -127 ? -127 : q));
+  }
+  return scale;
+}
+
+/* Row loop of quantize_acts, gemma.c:2652-2674: sstr == 0 means dense rows
+ * of n; dst is always dense (m, n). */
+void orc_quantize_acts(int8_t *dst, float *dsc, const float *src, int sstr,
+                       int m, int n) {
+  if (sstr == 0)
+    sstr = n;
+  for (int i = 0; i < m; i++)
+    dsc[i] = orc_quantize_act(dst + (size_t)i * n, src + (size_t)i * sstr, n);
+}
+
+/* int32 accumulators of the NT product acc[i][j] = sum_l src[i,l]*mat[j,l]
+ * (the quantity gemm_int8_kernel_dot/_widen/_accum and gemv_int8_row sum,
+ * gemma.c:2758-2761, 3617-3661, 3675-3845).  Integer addition is exact and
+ * order independent, so any summation order gives the same bits. */
+void orc_acc_int8(int32_t *acc, const int8_t *mat, int mstr,
+                  const int8_t *src, int sstr, int m, int n, int k) {
+  if (mstr == 0)
+    mstr = k;
+  if (sstr == 0)
+    sstr = k;
+  for (int i = 0; i < m; i++) {
+    const int8_t *a = src + (size_t)i * sstr;
+    for (int j = 0; j < n; j++) {
+      const int8_t *b = mat + (size_t)j * mstr;
+      int32_t s = 0;
+      for (int l = 0; l < k; l++)
+        s += (int32_t)a[l] * (int32_t)b[l];
+      acc[(size_t)i * n + j] = s;
+    }
+  }
+}
+
+/* Dequant epilogue: (float)acc * (xs * ws), gemma.c:2762 / 3859-3862 in the
+ * form the -ffast-math build evaluates. */
+static inline float orc_dequant(int32_t acc, float xs, float ws) {
+  return (float)acc * (xs * ws);
+}
+
+/* gemv_int8, gemma.c:2765-2788: dst[i] = dot(mat row i, vec) dequantized.
+ * m = rows of mat (outputs), n = reduction length. */
+void orc_gemv_int8(float *dst, const int8_t *mat, const float *matsc,
+                   const int8_t *vec, float vsc, int m, int n) {
+  for (int i = 0; i < m; i++) {
+    const int8_t *w = mat + (size_t)i * n;
+    int32_t s = 0;
+    for (int l = 0; l < n; l++)
+      s += (int32_t)w[l] * (int32_t)vec[l];
+    dst[i] = orc_dequant(s, vsc, matsc[i]);
+  }
+}
+
+/* GemvJob, gemma.c:2795-2800 (floatx = float). */
+typedef struct {
+  const void *w;
+  const float *sc;
+  float *dst;
+  int m;
+} OrcGemvJob;
+
+/* gemv_int8_multi, gemma.c:2814-2837: every job shares vec, vsc and n. */
+void orc_gemv_int8_multi(const OrcGemvJob *jobs, int njobs,
+                         const int8_t *vec, float vsc, int n) {
+  for (int j = 0; j < njobs; j++)
+    orc_gemv_int8(jobs[j].dst, (const int8_t *)jobs[j].w, jobs[j].sc, vec,
+                  vsc, jobs[j].m, n);
+}
+
+/* gemm_int8, gemma.c:3937-4054: NT GEMM with per-row (ssc) and per-column
+ * (matsc) scales.  Strides of 0 mean dense (dstr = n, mstr = sstr = k).
+ * Returns 0 like the reference on success. */
+int orc_gemm_int8(float *dst, int dstr, const int8_t *mat, int mstr,
+                  const float *matsc, const int8_t *src, int sstr,
+                  const float *ssc, int m, int n, int k) {
+  if (dstr == 0)
+    dstr = n;
+  if (mstr == 0)
+    mstr = k;
+  if (sstr == 0)
+    sstr = k;
+  for (int i = 0; i < m; i++) {
+    const int8_t *a = src + (size_t)i * sstr;
+    for (int j = 0; j < n; j++) {
+      const int8_t *b = mat + (size_t)j * mstr;
+      int32_t s = 0;
+      for (int l = 0; l < k; l++)
+        s += (int32_t)a[l] * (int32_t)b[l];
+      dst[(size_t)i * dstr + j] = orc_dequant(s, ssc[i], matsc[j]);
+    }
+  }
+  return 0;
+}
+
+/* Per-output-row weight quantizer of the exporter, model.py:151-161
+ * (Linear.quantize, called by export.py:430-457 on the transposed weight, so
+ * each gemma.c row n gets one scale) and model.py:97-107 (Embedding.quantize,
+ * lm_head).  fp32 throughout: s = max(amax, 1e-8) / 127 (IEEE division),
+ * q = round-half-to-even(w / s) (torch.round), clamp to [-127, 127]. */
+void orc_quantize_weight_rows(int8_t *q, float *scales, const float *w, int n,
+                              int k) {
+  for (int j = 0; j < n; j++) {
+    const float *row = w + (size_t)j * k;
+    float amax = 0.0f;
+    for (int l = 0; l < k; l++) {
+      float a = fabsf(row[l]);
+      amax = a > amax ? a : amax;
+    }
+    if (amax < 1e-8f)
+      amax = 1e-8f;
+    float s = amax / 127.0f;
+    scales[j] = s;
+    for (int l = 0; l < k; l++) {
+      float r = nearbyintf(row[l] / s); /* default mode: half to even */
+      if (r > 127.0f)
+        r = 127.0f;
+      if (r < -127.0f)
+        r = -127.0f;
+      q[(size_t)j * k + l] = (int8_t)r;
+    }
+  }
+}

@@ -1,0 +1,294 @@
+"""ctypes bindings to the CPU checkers (test infrastructure only).
+
+Two libraries live here:
+
+* ``liboracle.so`` -- the C restatement of Gemma.c's W8A8 hot path
+  (``gemma_oracle.c``; each function cites the gemma.c lines it follows).
+* ``_ref/libgemma_ref_<isa>.so`` -- the reference's own ``quantize_act``,
+  ``quantize_acts``, ``gemv_int8``, ``gemv_int8_multi`` and ``gemm_int8``
+  compiled from gemma.c (gemma.c:2586-2837, 3937-4054) with its Makefile's
+  -O3 -ffast-math -fopenmp flags.  Present wherever ``make -C oracle ref`` ran
+  (the build machine); it is shipped as a built file, the source is not.
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline leg may
+import this module.  The product (gemma.c_b200) never does.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REF_DIR = os.path.join(HERE, "_ref")
+
+_i8p = ctypes.POINTER(ctypes.c_int8)
+_f32p = ctypes.POINTER(ctypes.c_float)
+_i32p = ctypes.POINTER(ctypes.c_int32)
+
+
+class GemvJob(ctypes.Structure):
+    """gemma.c:2795 GemvJob with floatx = float."""
+    _fields_ = [("w", ctypes.c_void_p), ("sc", _f32p), ("dst", _f32p), ("m", ctypes.c_int)]
+
+
+def _ptr(a: np.ndarray, t):
+    assert a.flags["C_CONTIGUOUS"] or a.ndim == 0
+    return a.ctypes.data_as(t)
+
+
+def build() -> None:
+    """Compile liboracle.so (the restatement). Needs only gcc."""
+    subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
+
+
+def build_ref(ref_dir: str = "/root/reference") -> bool:
+    """Compile the reference harness when the reference sources are present."""
+    if not os.path.isfile(os.path.join(ref_dir, "gemma.c")):
+        return False
+    subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF_DIR={ref_dir}"], check=True)
+    return True
+
+
+_orc = None
+
+
+def orc() -> ctypes.CDLL:
+    global _orc
+    if _orc is None:
+        path = os.path.join(HERE, "liboracle.so")
+        if not os.path.exists(path):
+            build()
+        lib = ctypes.CDLL(path)
+        lib.orc_quantize_act.restype = ctypes.c_float
+        lib.orc_quantize_act.argtypes = [_i8p, _f32p, ctypes.c_int]
+        lib.orc_quantize_acts.restype = None
+        lib.orc_quantize_acts.argtypes = [_i8p, _f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+        lib.orc_acc_int8.restype = None
+        lib.orc_acc_int8.argtypes = [_i32p, _i8p, ctypes.c_int, _i8p, ctypes.c_int,
+                                     ctypes.c_int, ctypes.c_int, ctypes.c_int]
+        lib.orc_gemv_int8.restype = None
+        lib.orc_gemv_int8.argtypes = [_f32p, _i8p, _f32p, _i8p, ctypes.c_float, ctypes.c_int, ctypes.c_int]
+        lib.orc_gemv_int8_multi.restype = None
+        lib.orc_gemv_int8_multi.argtypes = [ctypes.POINTER(GemvJob), ctypes.c_int, _i8p,
+                                            ctypes.c_float, ctypes.c_int]
+        lib.orc_gemm_int8.restype = ctypes.c_int
+        lib.orc_gemm_int8.argtypes = [_f32p, ctypes.c_int, _i8p, ctypes.c_int, _f32p, _i8p,
+                                      ctypes.c_int, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+        lib.orc_quantize_weight_rows.restype = None
+        lib.orc_quantize_weight_rows.argtypes = [_i8p, _f32p, _f32p, ctypes.c_int, ctypes.c_int]
+        _orc = lib
+    return _orc
+
+
+# --------------------------------------------------------------------------
+# restatement wrappers (numpy in, numpy out)
+# --------------------------------------------------------------------------
+
+def quantize_act(vec: np.ndarray):
+    vec = np.ascontiguousarray(vec, dtype=np.float32)
+    dst = np.empty(vec.shape[0], np.int8)
+    sc = orc().orc_quantize_act(_ptr(dst, _i8p), _ptr(vec, _f32p), vec.shape[0])
+    return dst, np.float32(sc)
+
+
+def quantize_acts(src: np.ndarray, n: int | None = None, sstr: int = 0):
+    """src is (m, sstr) fp32 (sstr >= n); returns int8 (m, n) and fp32 (m,)."""
+    src = np.ascontiguousarray(src, dtype=np.float32)
+    m = src.shape[0]
+    n = src.shape[1] if n is None else n
+    dst = np.empty((m, n), np.int8)
+    dsc = np.empty(m, np.float32)
+    orc().orc_quantize_acts(_ptr(dst, _i8p), _ptr(dsc, _f32p), _ptr(src, _f32p), sstr, m, n)
+    return dst, dsc
+
+
+def acc_int8(mat: np.ndarray, src: np.ndarray) -> np.ndarray:
+    """int32 accumulators acc[i, j] = sum_l src[i, l] * mat[j, l] (dense)."""
+    mat = np.ascontiguousarray(mat, np.int8)
+    src = np.ascontiguousarray(src, np.int8)
+    m, k = src.shape
+    n = mat.shape[0]
+    acc = np.empty((m, n), np.int32)
+    orc().orc_acc_int8(_ptr(acc, _i32p), _ptr(mat, _i8p), k, _ptr(src, _i8p), k, m, n, k)
+    return acc
+
+
+def gemv_int8(mat, matsc, vec, vsc):
+    mat = np.ascontiguousarray(mat, np.int8)
+    matsc = np.ascontiguousarray(matsc, np.float32)
+    vec = np.ascontiguousarray(vec, np.int8)
+    m, n = mat.shape
+    dst = np.empty(m, np.float32)
+    orc().orc_gemv_int8(_ptr(dst, _f32p), _ptr(mat, _i8p), _ptr(matsc, _f32p), _ptr(vec, _i8p),
+                        float(vsc), m, n)
+    return dst
+
+
+def gemv_int8_multi(mats, scs, vec, vsc):
+    vec = np.ascontiguousarray(vec, np.int8)
+    mats = [np.ascontiguousarray(w, np.int8) for w in mats]
+    scs = [np.ascontiguousarray(s, np.float32) for s in scs]
+    outs = [np.empty(w.shape[0], np.float32) for w in mats]
+    jobs = (GemvJob * len(mats))()
+    for j, (w, s, o) in enumerate(zip(mats, scs, outs)):
+        jobs[j] = GemvJob(w.ctypes.data, _ptr(s, _f32p), _ptr(o, _f32p), w.shape[0])
+    orc().orc_gemv_int8_multi(jobs, len(mats), _ptr(vec, _i8p), float(vsc), vec.shape[0])
+    return outs
+
+
+def gemm_int8(mat, matsc, src, ssc, dst=None, dstr=0, mstr=0, sstr=0, m=None, n=None, k=None):
+    """NT GEMM; with strides the arrays are flat buffers and m, n, k are given."""
+    mat = np.ascontiguousarray(mat, np.int8)
+    src = np.ascontiguousarray(src, np.int8)
+    matsc = np.ascontiguousarray(matsc, np.float32)
+    ssc = np.ascontiguousarray(ssc, np.float32)
+    if m is None:
+        m, k = src.shape
+        n = mat.shape[0]
+    if dst is None:
+        dst = np.zeros((m, n), np.float32)
+    orc().orc_gemm_int8(_ptr(dst, _f32p), dstr, _ptr(mat, _i8p), mstr, _ptr(matsc, _f32p),
+                        _ptr(src, _i8p), sstr, _ptr(ssc, _f32p), m, n, k)
+    return dst
+
+
+def quantize_weight_rows(w: np.ndarray):
+    w = np.ascontiguousarray(w, np.float32)
+    n, k = w.shape
+    q = np.empty((n, k), np.int8)
+    s = np.empty(n, np.float32)
+    orc().orc_quantize_weight_rows(_ptr(q, _i8p), _ptr(s, _f32p), _ptr(w, _f32p), n, k)
+    return q, s
+
+
+# --------------------------------------------------------------------------
+# the compiled reference (gemma.c's own functions)
+# --------------------------------------------------------------------------
+
+def cpu_flags() -> set:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("flags"):
+                    return set(line.split(":", 1)[1].split())
+    except OSError:
+        pass
+    return set()
+
+
+def ref_variant() -> str | None:
+    """Best reference build this host can run: native (the build machine),
+    v4 (AVX-512) or v3 (AVX2+FMA)."""
+    flags = cpu_flags()
+    avail = {v: os.path.join(REF_DIR, f"libgemma_ref_{v}.so") for v in ("native", "v4", "v3")}
+    if os.path.isfile("/root/reference/gemma.c") and os.path.exists(avail["native"]):
+        return "native"
+    if {"avx512f", "avx512bw", "avx512cd", "avx512dq", "avx512vl"} <= flags and os.path.exists(avail["v4"]):
+        return "v4"
+    if {"avx2", "fma", "bmi2"} <= flags and os.path.exists(avail["v3"]):
+        return "v3"
+    return None
+
+
+_refs: dict = {}
+
+
+def ref(variant: str | None = None) -> ctypes.CDLL | None:
+    variant = variant or ref_variant()
+    if variant is None:
+        return None
+    if variant in _refs:
+        return _refs[variant]
+    path = os.path.join(REF_DIR, f"libgemma_ref_{variant}.so")
+    if not os.path.exists(path):
+        return None
+    lib = ctypes.CDLL(path)
+    lib.ref_quantize_act.restype = ctypes.c_float
+    lib.ref_quantize_act.argtypes = [_i8p, _f32p, ctypes.c_int]
+    lib.ref_quantize_acts.restype = None
+    lib.ref_quantize_acts.argtypes = [_i8p, _f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    lib.ref_gemv_int8.restype = None
+    lib.ref_gemv_int8.argtypes = [_f32p, _i8p, _f32p, _i8p, ctypes.c_float, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    lib.ref_gemv_int8_multi.restype = None
+    lib.ref_gemv_int8_multi.argtypes = [ctypes.POINTER(GemvJob), ctypes.c_int, _i8p, ctypes.c_float,
+                                        ctypes.c_int, ctypes.c_int]
+    lib.ref_gemm_int8.restype = ctypes.c_int
+    lib.ref_gemm_int8.argtypes = [_f32p, ctypes.c_int, _i8p, ctypes.c_int, _f32p, _i8p, ctypes.c_int,
+                                  _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    lib.ref_setup.restype = None
+    lib.ref_isa.restype = ctypes.c_char_p
+    lib.ref_gemv_job_size.restype = ctypes.c_int
+    assert lib.ref_gemv_job_size() == ctypes.sizeof(GemvJob)
+    lib.ref_setup()
+    _refs[variant] = lib
+    return lib
+
+
+class Ref:
+    """numpy-level calls into the compiled reference."""
+
+    def __init__(self, variant: str | None = None, threads: int | None = None):
+        self.lib = ref(variant)
+        if self.lib is None:
+            raise RuntimeError("reference build not available (run make -C oracle ref)")
+        self.variant = variant or ref_variant()
+        self.threads = threads or os.cpu_count() or 1
+
+    @property
+    def isa(self) -> str:
+        return self.lib.ref_isa().decode()
+
+    def quantize_act(self, vec):
+        vec = np.ascontiguousarray(vec, np.float32)
+        dst = np.empty(vec.shape[0], np.int8)
+        sc = self.lib.ref_quantize_act(_ptr(dst, _i8p), _ptr(vec, _f32p), vec.shape[0])
+        return dst, np.float32(sc)
+
+    def quantize_acts(self, src, n=None, sstr=0):
+        src = np.ascontiguousarray(src, np.float32)
+        m = src.shape[0]
+        n = src.shape[1] if n is None else n
+        dst = np.empty((m, n), np.int8)
+        dsc = np.empty(m, np.float32)
+        self.lib.ref_quantize_acts(_ptr(dst, _i8p), _ptr(dsc, _f32p), _ptr(src, _f32p), sstr, m, n,
+                                   self.threads)
+        return dst, dsc
+
+    def gemv_int8(self, mat, matsc, vec, vsc, dst=None):
+        mat = np.ascontiguousarray(mat, np.int8)
+        m, n = mat.shape
+        if dst is None:
+            dst = np.empty(m, np.float32)
+        self.lib.ref_gemv_int8(_ptr(dst, _f32p), _ptr(mat, _i8p), _ptr(np.ascontiguousarray(matsc, np.float32), _f32p),
+                               _ptr(np.ascontiguousarray(vec, np.int8), _i8p), float(vsc), m, n, self.threads)
+        return dst
+
+    def gemv_int8_multi(self, mats, scs, vec, vsc, outs=None):
+        vec = np.ascontiguousarray(vec, np.int8)
+        if outs is None:
+            outs = [np.empty(w.shape[0], np.float32) for w in mats]
+        jobs = (GemvJob * len(mats))()
+        for j, (w, s, o) in enumerate(zip(mats, scs, outs)):
+            jobs[j] = GemvJob(w.ctypes.data, _ptr(s, _f32p), _ptr(o, _f32p), w.shape[0])
+        self.lib.ref_gemv_int8_multi(jobs, len(mats), _ptr(vec, _i8p), float(vsc), vec.shape[0], self.threads)
+        return outs
+
+    def gemm_int8(self, mat, matsc, src, ssc, dst=None, dstr=0, mstr=0, sstr=0, m=None, n=None, k=None,
+                  omp: bool = True):
+        mat = np.ascontiguousarray(mat, np.int8)
+        src = np.ascontiguousarray(src, np.int8)
+        if m is None:
+            m, k = src.shape
+            n = mat.shape[0]
+        if dst is None:
+            dst = np.zeros((m, n), np.float32)
+        rc = self.lib.ref_gemm_int8(_ptr(dst, _f32p), dstr, _ptr(mat, _i8p), mstr,
+                                    _ptr(np.ascontiguousarray(matsc, np.float32), _f32p), _ptr(src, _i8p), sstr,
+                                    _ptr(np.ascontiguousarray(ssc, np.float32), _f32p), m, n, k,
+                                    self.threads if omp else 1)
+        if rc != 0:
+            raise RuntimeError("reference gemm_int8 returned %d" % rc)
+        return dst
