@@ -12,6 +12,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -80,6 +81,14 @@ static DeviceInfo &device_info() {
 }
 
 int num_sms() { return device_info().sms; }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char *e = getenv("GCU_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
 unsigned int *dev_error_word() { return device_info().err; }
 
 // ---------------------------------------------------------------------------

@@ -28,6 +28,29 @@ int check_cuda(cudaError_t e, const char *what);
 
 int num_sms();
 
+// Programmatic dependent launch: every kernel is launched with programmatic
+// stream serialization, does its setup (barrier init, TMEM allocation,
+// descriptor prefetch), then waits on griddepcontrol.wait before touching
+// global memory, so its prologue overlaps the previous kernel's tail.
+// GCU_PDL=0 in the environment turns the attribute off.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                            cudaStream_t st, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 // ---------------------------------------------------------------------------
 // device error word.  Kernels never trap: a bounded wait that gives up sets
 // a code here and the kernel returns; the host reads it after synchronising.
@@ -89,6 +112,17 @@ namespace ptx {
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// wait until the grids this one depends on have completed and their memory
+// is visible (no-op without a programmatic dependency)
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+// allow the dependent grid to be scheduled (it still waits for our completion
+// in its griddep_wait before reading anything we write)
+__device__ __forceinline__ void griddep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 __device__ __forceinline__ uint64_t globaltimer() {

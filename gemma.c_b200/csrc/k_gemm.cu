@@ -30,19 +30,21 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 128;  // K bytes per stage (one 128-byte swizzle row)
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;  // two per TMEM lane quarter, each half the chunks
+constexpr int kEpiThreads = 32 * kEpiWarps;
+constexpr int kThreads = 64 + kEpiThreads;
 constexpr int kMaxJobs = 4;
 constexpr int kEpiStageBytes = 32 * 128;  // 32 rows x 32 fp32
 
 template <int BN>
 struct Cfg {
-  static constexpr int STAGES = BN == 256 ? 4 : 5;
+  static constexpr int STAGES = BN == 256 ? 4 : BN == 128 ? 5 : 7;
   static constexpr int A_BYTES = BM * BK;
   static constexpr int B_BYTES = BN * BK;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
-  static constexpr int BAR_OFF = EPI_OFF + 4 * 2 * kEpiStageBytes;
+  static constexpr int BAR_OFF = EPI_OFF + kEpiWarps * kEpiStageBytes;
   static constexpr int NBARS = 2 * STAGES + 5;
   static constexpr int SMEM = 1024 + BAR_OFF + NBARS * 8 + 16;
 };
@@ -96,17 +98,16 @@ __device__ __forceinline__ Unit decode_unit(const TcParams &p, int u) {
 
 // Dequantize 32 accumulators of one row and write them: either into the
 // warp's swizzled staging buffer for a TMA store, or straight to global.
+// Lane i of the warp holds the weight scale of column col0 + i in `ws_lane`
+// (loaded before the accumulator was ready); shuffles broadcast it.
 template <bool TMA>
 __device__ __forceinline__ void emit_chunk(const TcParams &p, const TcJob &job, const int (&acc)[32],
-                                           float xs, int row, int col0, int lane, uint8_t *stage,
-                                           int tile_row0) {
+                                           float xs, float ws_lane, int row, int col0, int lane,
+                                           uint8_t *stage, int tile_row0) {
   float out[32];
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const int col = col0 + i;
-    const float ws = col < job.n ? __ldg(job.matsc + col) : 0.0f;
-    out[i] = dequant(acc[i], xs, ws);
-  }
+  for (int i = 0; i < 32; ++i)
+    out[i] = dequant(acc[i], xs, __shfl_sync(0xffffffffu, ws_lane, i));
   if (TMA) {
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
@@ -158,7 +159,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_tc(const __grid_constan
     }
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(&tfull[b], 1);
-      ptx::mbar_init(&tempty[b], 4 * 32);
+      ptx::mbar_init(&tempty[b], kEpiThreads);
     }
     ptx::mbar_init(mma_done, 1);
     ptx::fence_mbar_init();
@@ -178,6 +179,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_tc(const __grid_constan
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // everything above overlapped the previous kernel; global memory from here
+  ptx::griddep_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -246,6 +249,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_tc(const __grid_constan
         }
         ptx::mma_commit(&tfull[buf]);
       }
+      // the next kernel may start its prologue while our epilogue drains
+      ptx::griddep_launch();
       // all MMAs of this CTA complete before TMEM may be freed
       ptx::mma_commit(mma_done);
       ptx::mbar_wait(mma_done, 0, p.err, DEV_TIMEOUT_DRAIN);
@@ -253,97 +258,116 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_tc(const __grid_constan
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    uint8_t *stage0 = epi + (warp - 2) * 2 * kEpiStageBytes;
-    int t = 0, nstore = 0;
+    const int half = (warp - 2) >> 2;  // this warp takes chunks with (ch & 1) == half
+    uint8_t *stage = epi + (warp - 2) * kEpiStageBytes;
+    constexpr int NCH = BN / 32;  // 32-column chunks per tile
+    int t = 0;
     for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++t) {
       const Unit w = decode_unit(p, u);
       const TcJob &job = p.jobs[w.job];
       const int buf = t & 1;
       const uint32_t use = t >> 1;
-      if (!ptx::mbar_wait(&tfull[buf], use & 1, p.err, DEV_TIMEOUT_TMEM)) break;
-      ptx::tc_fence_after();
       const int tile_row0 = w.m_t * BM + q * 32;
       const int row = tile_row0 + lane;
+      const int n0 = w.n_t * BN;
+      // operand scales of this tile, fetched while its MMAs still run: the
+      // row's activation scale, and lane i holds column (32*ch + i)'s weight
+      // scale for chunk ch
       const float xs = row < p.m ? __ldg(p.ssc + row) : 0.0f;
+      float wsl[NCH];
+#pragma unroll
+      for (int ch = 0; ch < NCH; ++ch) {
+        const int col = n0 + ch * 32 + lane;
+        wsl[ch] = col < job.n ? __ldg(job.matsc + col) : 0.0f;
+      }
+      if (!ptx::mbar_wait(&tfull[buf], use & 1, p.err, DEV_TIMEOUT_TMEM)) break;
+      ptx::tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
       if (p.splits == 1) {
-#pragma unroll 1
-        for (int ch = 0; ch < BN / 32; ++ch) {
+#pragma unroll
+        for (int ch = 0; ch < NCH; ++ch) {
+          if ((ch & 1) != half) continue;
+          __syncwarp();
           uint32_t r[32];
           ptx::tmem_ld_32x32(taddr + ch * 32, r);
           ptx::tmem_ld_wait();
-          const int col0 = w.n_t * BN + ch * 32;
+          const int col0 = n0 + ch * 32;
           if (col0 >= job.n) continue;
           if (job.tma_store) {
-            uint8_t *stage = stage0 + (nstore & 1) * kEpiStageBytes;
-            if (lane == 0) ptx::bulk_wait_read<1>();
+            if (lane == 0) ptx::bulk_wait_read<0>();
             __syncwarp();
-            emit_chunk<true>(p, job, reinterpret_cast<const int(&)[32]>(r), xs, row, col0, lane,
-                             stage, tile_row0);
-            ++nstore;
+            emit_chunk<true>(p, job, reinterpret_cast<const int(&)[32]>(r), xs, wsl[ch], row, col0,
+                             lane, stage, tile_row0);
           } else {
-            emit_chunk<false>(p, job, reinterpret_cast<const int(&)[32]>(r), xs, row, col0, lane,
-                              nullptr, tile_row0);
+            emit_chunk<false>(p, job, reinterpret_cast<const int(&)[32]>(r), xs, wsl[ch], row, col0,
+                              lane, nullptr, tile_row0);
           }
         }
         ptx::tc_fence_before();
         ptx::mbar_arrive(&tempty[buf]);
       } else {
-        // split K: int32 partial of this split -> workspace
-        int32_t *part = p.ws + ((size_t)w.tile * p.splits + w.s) * (BM * BN) +
-                        (size_t)(q * 32 + lane) * BN;
-#pragma unroll 1
-        for (int ch = 0; ch < BN / 32; ++ch) {
+        // split K: this split's int32 partial goes to the workspace in a
+        // layout where each warp store is 512 contiguous bytes:
+        // [quarter q][chunk][8 x int4][lane]
+        constexpr size_t kPartInt4 = (size_t)BM * BN / 4;
+        int4 *part = reinterpret_cast<int4 *>(p.ws) + ((size_t)w.tile * p.splits + w.s) * kPartInt4 +
+                     (size_t)q * NCH * 8 * 32 + lane;
+#pragma unroll
+        for (int ch = 0; ch < NCH; ++ch) {
+          if ((ch & 1) != half) continue;
+          __syncwarp();
           uint32_t r[32];
           ptx::tmem_ld_32x32(taddr + ch * 32, r);
           ptx::tmem_ld_wait();
 #pragma unroll
           for (int c = 0; c < 8; ++c)
-            __stcg(reinterpret_cast<int4 *>(part + ch * 32) + c,
+            __stcg(part + (ch * 8 + c) * 32,
                    make_int4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]));
         }
         ptx::tc_fence_before();
         ptx::mbar_arrive(&tempty[buf]);
         __threadfence();
-        ptx::named_bar_sync(1, 128);
+        ptx::named_bar_sync(1, kEpiThreads);
         if (threadIdx.x == 64) {
           const int prev = atomicAdd(p.counters + w.tile, 1);
           s_last = (prev == p.splits - 1);
         }
-        ptx::named_bar_sync(1, 128);
+        ptx::named_bar_sync(1, kEpiThreads);
         if (s_last) {
+          // the last split to finish sums every partial (integer adds are
+          // exact, so the order of arrival does not matter)
           __threadfence();
-          const int32_t *base = p.ws + (size_t)w.tile * p.splits * (BM * BN) +
-                                (size_t)(q * 32 + lane) * BN;
-#pragma unroll 1
-          for (int ch = 0; ch < BN / 32; ++ch) {
-            const int col0 = w.n_t * BN + ch * 32;
+          const int4 *base = reinterpret_cast<const int4 *>(p.ws) + (size_t)w.tile * p.splits * kPartInt4 +
+                             (size_t)q * NCH * 8 * 32 + lane;
+#pragma unroll
+          for (int ch = 0; ch < NCH; ++ch) {
+            if ((ch & 1) != half) continue;
+            const int col0 = n0 + ch * 32;
             if (col0 >= job.n) continue;
             int acc[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) acc[i] = 0;
             for (int s = 0; s < p.splits; ++s) {
-              const int4 *src = reinterpret_cast<const int4 *>(base + (size_t)s * (BM * BN) + ch * 32);
+              const int4 *src = base + (size_t)s * kPartInt4 + ch * 8 * 32;
 #pragma unroll
               for (int c = 0; c < 8; ++c) {
-                const int4 v = __ldcg(src + c);
+                const int4 v = __ldcg(src + c * 32);
                 acc[4 * c] += v.x;
                 acc[4 * c + 1] += v.y;
                 acc[4 * c + 2] += v.z;
                 acc[4 * c + 3] += v.w;
               }
             }
+            __syncwarp();
             if (job.tma_store) {
-              uint8_t *stage = stage0 + (nstore & 1) * kEpiStageBytes;
-              if (lane == 0) ptx::bulk_wait_read<1>();
+              if (lane == 0) ptx::bulk_wait_read<0>();
               __syncwarp();
-              emit_chunk<true>(p, job, acc, xs, row, col0, lane, stage, tile_row0);
-              ++nstore;
-            } else {
-              emit_chunk<false>(p, job, acc, xs, row, col0, lane, nullptr, tile_row0);
+              emit_chunk<true>(p, job, acc, xs, wsl[ch], row, col0, lane, stage, tile_row0);
+              } else {
+              emit_chunk<false>(p, job, acc, xs, wsl[ch], row, col0, lane, nullptr, tile_row0);
             }
           }
-          ptx::named_bar_sync(1, 128);
+          ptx::named_bar_sync(1, kEpiThreads);
           if (threadIdx.x == 64) p.counters[w.tile] = 0;  // ready for the next launch
         }
       }
@@ -421,7 +445,7 @@ int launch_bn(TcParams &p, cudaStream_t st) {
     }
   }
   int grid = p.units < num_sms() ? p.units : num_sms();
-  k_gemm_i8_tc<BN><<<grid, kThreads, C::SMEM, st>>>(p);
+  GCU_CUDA(launch_k(k_gemm_i8_tc<BN>, grid, kThreads, C::SMEM, st, p));
   GCU_CUDA(cudaGetLastError());
   return 0;
 }
@@ -444,28 +468,31 @@ int launch_gemm_tc_jobs(const int8_t *src, long sstr, const float *ssc, int m, i
     return set_error("gemm: activation rows must be 16-byte aligned (stride %ld)", sstr);
   const int sms = num_sms();
   const int tiles_m = (m + BM - 1) / BM;
-  int ntot128 = 0, ntot256 = 0;
+  int ntot64 = 0, ntot128 = 0, ntot256 = 0;
   for (int j = 0; j < njobs; ++j) {
+    ntot64 += (jobs[j].n + 63) / 64;
     ntot128 += (jobs[j].n + 127) / 128;
     ntot256 += (jobs[j].n + 255) / 256;
     if ((uintptr_t)jobs[j].mat % 16 || jobs[j].mstr % 16)
       return set_error("gemm: weight rows must be 16-byte aligned (stride %ld)", jobs[j].mstr);
   }
   int bn = force_bn;
-  if (bn != 128 && bn != 256) {
+  if (bn != 64 && bn != 128 && bn != 256) {
     const double e256 = wave_eff((long)tiles_m * ntot256, sms);
     const double e128 = wave_eff((long)tiles_m * ntot128, sms);
     bn = (e256 >= 0.85 || e256 >= e128) ? 256 : 128;
   }
-  const int tiles_n = bn == 256 ? ntot256 : ntot128;
+  const int tiles_n = bn == 256 ? ntot256 : bn == 128 ? ntot128 : ntot64;
   const int tiles = tiles_m * tiles_n;
   const int kb_total = (k + BK - 1) / BK;
   int splits = 1;
   if (force_split > 0) {
     splits = force_split;
-  } else if (tiles * 2 <= sms) {
+  } else if (tiles * 2 <= sms && kb_total >= 16) {
+    // too few tiles to occupy the SMs and a long K: split it, keeping at
+    // least 8 K blocks per split so the partial round trip stays small
     splits = sms / tiles;
-    if (splits > kb_total / 2) splits = kb_total / 2;
+    if (splits > kb_total / 8) splits = kb_total / 8;
     if (splits > 16) splits = 16;
     if (splits < 1) splits = 1;
   }
@@ -509,7 +536,9 @@ int launch_gemm_tc_jobs(const int8_t *src, long sstr, const float *ssc, int m, i
     p.ws = static_cast<int32_t *>(ws);
     p.counters = cnt;
   }
-  return bn == 256 ? launch_bn<256>(p, st) : launch_bn<128>(p, st);
+  if (bn == 256) return launch_bn<256>(p, st);
+  if (bn == 128) return launch_bn<128>(p, st);
+  return launch_bn<64>(p, st);
 }
 
 int launch_gemm_tc(const GemmArgs &a, cudaStream_t st, int force_bn, int force_split) {

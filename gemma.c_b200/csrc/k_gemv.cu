@@ -55,6 +55,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs,
                                                        int total_rows) {
   extern __shared__ int4 xsm[];  // [MB][C] 16-byte chunks of x
   const int C = k >> 4;
+  ptx::griddep_wait();
   for (int i = threadIdx.x; i < MB * C; i += kThreads) {
     const int b = i / C, c = i - b * C;
     int4 v = make_int4(0, 0, 0, 0);
@@ -131,6 +132,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs,
       }
     }
   }
+  ptx::griddep_launch();
 }
 
 // Generic kernel: any k, any alignment.  One warp per weight row, byte loads.
@@ -142,6 +144,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv_any(const GemvJobs jobs,
                                                        int total_rows) {
   const int lane = threadIdx.x & 31;
   const int nwarps = gridDim.x * (kThreads / 32);
+  ptx::griddep_wait();
   for (int row = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); row < total_rows;
        row += nwarps) {
     int j, local;
@@ -164,6 +167,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv_any(const GemvJobs jobs,
         jobs.y[j][(size_t)b * ystride + local] = dequant(acc[b], xs[b], ws);
     }
   }
+  ptx::griddep_launch();
 }
 
 template <int MB, int LPR>
@@ -195,7 +199,7 @@ int launch_v16(const GemvJobs &jobs, const int8_t *x, long xstride, const float 
   long need = ((long)total_rows + rows_per_block - 1) / rows_per_block;
   long cap = (long)num_sms() * blocks_per_sm;
   const int grid = (int)(need < cap ? need : cap);
-  kern<<<grid, kThreads, smem, st>>>(jobs, x, xstride, xs, mb, ystride, k, total_rows);
+  GCU_CUDA(launch_k(kern, grid, kThreads, smem, st, jobs, x, xstride, xs, mb, ystride, k, total_rows));
   GCU_CUDA(cudaGetLastError());
   return 0;
 }
@@ -231,7 +235,7 @@ int launch_gemv(const GemvJobs &jobs, const int8_t *x, long xstride, const float
   long need = ((long)total_rows + 7) / 8;
   long cap = (long)num_sms() * 8;
   const int grid = (int)(need < cap ? need : cap);
-  k_gemv_any<<<grid, kThreads, 0, st>>>(jobs, x, xstride, xs, mb, ystride, k, total_rows);
+  GCU_CUDA(launch_k(k_gemv_any, grid, kThreads, 0, st, jobs, x, xstride, xs, mb, ystride, k, total_rows));
   GCU_CUDA(cudaGetLastError());
   return 0;
 }

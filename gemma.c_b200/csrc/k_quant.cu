@@ -59,6 +59,7 @@ __global__ void __launch_bounds__(1024) k_quant_rows_v4(int8_t *__restrict__ dst
                                                         long sstr, int m, int n) {
   __shared__ float red[32];
   const int n4 = n >> 2;
+  ptx::griddep_wait();
   for (int row = blockIdx.x; row < m; row += gridDim.x) {
     const float4 *x = reinterpret_cast<const float4 *>(src + (size_t)row * sstr);
     float4 v[VPT];
@@ -90,6 +91,7 @@ __global__ void __launch_bounds__(1024) k_quant_rows_v4(int8_t *__restrict__ dst
     }
     if (threadIdx.x == 0) dsc[row] = scale;
   }
+  ptx::griddep_launch();
 }
 
 // Any alignment and length: two passes over global memory.
@@ -98,6 +100,7 @@ __global__ void __launch_bounds__(256) k_quant_rows_any(int8_t *__restrict__ dst
                                                         const float *__restrict__ src,
                                                         long sstr, int m, int n) {
   __shared__ float red[32];
+  ptx::griddep_wait();
   for (int row = blockIdx.x; row < m; row += gridDim.x) {
     const float *x = src + (size_t)row * sstr;
     float amax = 0.0f;
@@ -109,6 +112,7 @@ __global__ void __launch_bounds__(256) k_quant_rows_any(int8_t *__restrict__ dst
     for (int i = threadIdx.x; i < n; i += blockDim.x) q[i] = (int8_t)quant_one(x[i], inv);
     if (threadIdx.x == 0) dsc[row] = scale;
   }
+  ptx::griddep_launch();
 }
 
 }  // namespace
@@ -127,13 +131,13 @@ int launch_quantize_rows(int8_t *dst, float *dsc, const float *src, long sstr,
     threads = ((threads + 31) / 32) * 32;
     if (threads < 32) threads = 32;
     switch (vpt) {
-      case 1: k_quant_rows_v4<1><<<grid, threads, 0, st>>>(dst, dsc, src, sstr, m, n); break;
-      case 2: k_quant_rows_v4<2><<<grid, threads, 0, st>>>(dst, dsc, src, sstr, m, n); break;
-      case 4: k_quant_rows_v4<4><<<grid, threads, 0, st>>>(dst, dsc, src, sstr, m, n); break;
-      default: k_quant_rows_v4<8><<<grid, threads, 0, st>>>(dst, dsc, src, sstr, m, n); break;
+      case 1: GCU_CUDA(launch_k(k_quant_rows_v4<1>, grid, threads, 0, st, dst, dsc, src, sstr, m, n)); break;
+      case 2: GCU_CUDA(launch_k(k_quant_rows_v4<2>, grid, threads, 0, st, dst, dsc, src, sstr, m, n)); break;
+      case 4: GCU_CUDA(launch_k(k_quant_rows_v4<4>, grid, threads, 0, st, dst, dsc, src, sstr, m, n)); break;
+      default: GCU_CUDA(launch_k(k_quant_rows_v4<8>, grid, threads, 0, st, dst, dsc, src, sstr, m, n)); break;
     }
   } else {
-    k_quant_rows_any<<<grid, 256, 0, st>>>(dst, dsc, src, sstr, m, n);
+    GCU_CUDA(launch_k(k_quant_rows_any, grid, 256, 0, st, dst, dsc, src, sstr, m, n));
   }
   GCU_CUDA(cudaGetLastError());
   return 0;

@@ -220,7 +220,7 @@ def _dev(a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
-@pytest.mark.parametrize("bn,split", [(128, 1), (256, 1), (128, 3), (256, 2), (128, 7)])
+@pytest.mark.parametrize("bn,split", [(128, 1), (256, 1), (128, 3), (256, 2), (128, 7), (64, 1), (64, 3)])
 def test_gemm_tile_and_split_variants(bn, split):
     m, n, k = 384, 1000, 2304
     w, ws = synth.weight(7000 + bn + split, n, k)
