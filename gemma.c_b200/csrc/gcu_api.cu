@@ -24,10 +24,6 @@
 
 namespace gcu {
 
-int launch_gemm_tc_jobs(const int8_t *src, long sstr, const float *ssc, int m, int k,
-                        const GemmArgs *jobs, int njobs, cudaStream_t st, int force_bn,
-                        int force_split);
-
 // ---------------------------------------------------------------------------
 // errors
 // ---------------------------------------------------------------------------

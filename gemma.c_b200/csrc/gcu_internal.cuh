@@ -97,6 +97,21 @@ struct GemmArgs {
 int launch_gemm_tc(const GemmArgs &a, cudaStream_t st, int force_bn,
                    int force_split);
 
+// Caller-owned split-K scratch: when given, the launcher uses it instead of
+// the runtime's allocated workspace, fails if the plan needs more than
+// ws_bytes / ncounters, and zeroes the counters it uses on `st` first.
+struct ExtWorkspace {
+  void *ws;
+  size_t ws_bytes;
+  int *counters;
+  int ncounters;
+};
+// Tensor-core GEMM over up to 4 jobs sharing the A operand `src`.
+int launch_gemm_tc_jobs(const int8_t *src, long sstr, const float *ssc, int m,
+                        int k, const GemmArgs *jobs, int njobs, cudaStream_t st,
+                        int force_bn, int force_split,
+                        const ExtWorkspace *ext = nullptr);
+
 // split-K workspace and tile counters (device memory owned by the runtime)
 int gemm_workspace(size_t bytes, void **ws, int **counters, int ncounters,
                    cudaStream_t st);

@@ -460,7 +460,7 @@ double wave_eff(long units, int sms) {
 // Multi-job entry: jobs share A (src); job j has its own weights and output.
 int launch_gemm_tc_jobs(const int8_t *src, long sstr, const float *ssc, int m, int k,
                         const GemmArgs *jobs, int njobs, cudaStream_t st, int force_bn,
-                        int force_split) {
+                        int force_split, const ExtWorkspace *ext) {
   if (njobs < 1 || njobs > kMaxJobs) return set_error("gemm: 1..%d jobs (got %d)", kMaxJobs, njobs);
   if (m <= 0 || k <= 0) return 0;
   if (get_encode()) return 1;
@@ -529,10 +529,20 @@ int launch_gemm_tc_jobs(const int8_t *src, long sstr, const float *ssc, int m, i
   p.ssc = ssc;
   p.err = dev_error_word();
   if (splits > 1) {
+    const size_t need = (size_t)tiles * splits * BM * bn * sizeof(int32_t);
     void *ws = nullptr;
     int *cnt = nullptr;
-    if (gemm_workspace((size_t)tiles * splits * BM * bn * sizeof(int32_t), &ws, &cnt, tiles, st))
+    if (ext) {
+      if (need > ext->ws_bytes || tiles > ext->ncounters)
+        return set_error("gemm: split-K needs %zu bytes of scratch and %d counters; the caller's "
+                         "scratch holds %zu bytes and %d counters",
+                         need, tiles, ext->ws_bytes, ext->ncounters);
+      GCU_CUDA(cudaMemsetAsync(ext->counters, 0, (size_t)tiles * sizeof(int), st));
+      ws = ext->ws;
+      cnt = ext->counters;
+    } else if (gemm_workspace(need, &ws, &cnt, tiles, st)) {
       return 1;
+    }
     p.ws = static_cast<int32_t *>(ws);
     p.counters = cnt;
   }

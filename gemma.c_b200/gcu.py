@@ -53,6 +53,7 @@ SIGNATURES = {
     "gcu_dev_gemv_int8_multi": (_int, [ctypes.POINTER(GemvJob), _int, _vp, _vp, _int, _vp]),
     "gcu_dev_gemm_int8": (_int, [_vp, _int, _vp, _int, _vp, _vp, _int, _vp, _int, _int, _int, _vp]),
     "gcu_dev_gemm_int8_multi": (_int, [ctypes.POINTER(GemvJob), _int, _vp, _int, _vp, _int, _int, _vp]),
+    "gcu_dev_gemm_int8_noalloc": (_int, [_vp, _int, _vp, _int, _vp, _vp, _int, _vp, _int, _int, _int, _vp]),
     "gcu_comm_unique_id": (_int, [ctypes.c_char_p]),
     "gcu_comm_init": (_int, [_int, _int, ctypes.c_char_p]),
     "gcu_comm_destroy": (_int, []),
@@ -210,6 +211,14 @@ def dev_gemm_int8(dst, mat, matsc, src, ssc, m, n, k, dstr=0, mstr=0, sstr=0, st
     _check(lib().gcu_dev_gemm_int8(dst.data_ptr(), dstr, mat.data_ptr(), mstr, matsc.data_ptr(),
                                    src.data_ptr(), sstr, ssc.data_ptr(), m, n, k, _stream(stream)),
            "dev_gemm_int8")
+
+
+def dev_gemm_int8_noalloc(dst, mat, matsc, src, ssc, m, n, k, dstr=0, mstr=0, sstr=0, stream=None):
+    """gemm_int8 on device tensors with no device allocation: split-K scratch
+    comes from a fixed array inside libgcu.so (see include/gcu.h)."""
+    _check(lib().gcu_dev_gemm_int8_noalloc(dst.data_ptr(), dstr, mat.data_ptr(), mstr, matsc.data_ptr(),
+                                           src.data_ptr(), sstr, ssc.data_ptr(), m, n, k, _stream(stream)),
+           "dev_gemm_int8_noalloc")
 
 
 def dev_gemm_int8_multi(jobs_t, src, ssc, m, k, sstr=0, stream=None):

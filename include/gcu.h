@@ -121,6 +121,22 @@ int gcu_dev_gemm_int8(float *dst, int dstr, const int8_t *mat, int mstr,
                       const float *matsc, const int8_t *src, int sstr,
                       const float *ssc, int m, int n, int k, void *stream);
 
+/* gemm_int8 on device data that allocates no device memory.  No counterpart
+ * in the reference (its CPU gemm_int8 grows thread-local host scratch,
+ * gemma.c:3117-3150).  For callers that may not allocate once they are
+ * running -- processes that size all GPU memory at start-up, or that cannot
+ * afford the device synchronisation cudaMalloc/cudaFree may cause -- the
+ * split-K scratch comes from a fixed 8 MiB array inside libgcu.so (held on
+ * every GPU that loads the library).  Same arguments and bits as
+ * gcu_dev_gemm_int8; returns 1 with a message when the split-K plan needs
+ * more than that array.  The first call on a device looks the array's
+ * address up (make it before any stream capture).  Calls share the array:
+ * calls that overlap on the GPU race and must be serialised by the caller. */
+int gcu_dev_gemm_int8_noalloc(float *dst, int dstr, const int8_t *mat,
+                              int mstr, const float *matsc, const int8_t *src,
+                              int sstr, const float *ssc, int m, int n, int k,
+                              void *stream);
+
 /* One A operand against several weights in one launch, e.g. the prefill
  * Q/K/V projections (gemma.c:5045-5091) or up/gate (gemma.c:5367-5372):
  * job j writes dst_j (m, rows_j) dense.  Weights must be dense [rows_j][k]. */
