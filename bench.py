@@ -176,28 +176,27 @@ class Prefill:
         self.out = [[torch.empty((m, n), dtype=torch.float32, device=device) for _, n in jobs]
                     for _, jobs in self.groups]
 
-    def step(self, gcu, stream=None, ev=None):
-        """Enqueue one step. `ev(kind)` brackets each launch when profiling."""
+    kinds = ("quant", "gemm")
+
+    def step(self, gcu, stream=None, want=None):
+        """Enqueue one step.  `want(kind, bytes, ops)` filters the launches
+        (and accounts their algorithmic work) for per-kernel timing."""
         m = self.m
         for layer in self.L:
             for gi, g in enumerate(layer):
-                if ev:
-                    ev("quant", 5 * m * g["k"] + 4 * m, 0)
-                gcu.dev_quantize_acts(g["q"], g["s"], g["x"], m, g["k"], stream=stream)
-                if ev:
-                    ev(None)
+                k = g["k"]
+                if want is None or want("quant", 5 * m * k + 4 * m, 0):
+                    gcu.dev_quantize_acts(g["q"], g["s"], g["x"], m, k, stream=stream)
                 jobs = [(w, sc, o) for (w, sc), o in zip(g["w"], self.out[gi])]
-                if ev:
-                    nsum = sum(w.shape[0] for w, _ in g["w"])
-                    k = g["k"]
-                    ev("gemm", nsum * k + 4 * nsum + m * k + 4 * m + 4 * m * nsum, 2 * m * nsum * k)
+                nsum = sum(w.shape[0] for w, _ in g["w"])
+                if want is not None and not want("gemm", nsum * k + 4 * nsum + m * k + 4 * m + 4 * m * nsum,
+                                                 2 * m * nsum * k):
+                    continue
                 if len(jobs) == 1:
                     w, sc, o = jobs[0]
-                    gcu.dev_gemm_int8(o, w, sc, g["q"], g["s"], m, w.shape[0], g["k"], stream=stream)
+                    gcu.dev_gemm_int8(o, w, sc, g["q"], g["s"], m, w.shape[0], k, stream=stream)
                 else:
-                    gcu.dev_gemm_int8_multi(jobs, g["q"], g["s"], m, g["k"], stream=stream)
-                if ev:
-                    ev(None)
+                    gcu.dev_gemm_int8_multi(jobs, g["q"], g["s"], m, k, stream=stream)
 
     launches_per_step = property(lambda self: self.layers * 2 * len(self.groups))
 
@@ -315,33 +314,25 @@ class Decode:
                      "w": synth.weight_torch(self.cfg["vocab"], d, gen, device),
                      "o": torch.empty(self.cfg["vocab"], dtype=torch.float32, device=device)}
 
-    def step(self, gcu, stream=None, ev=None):
+    kinds = ("quant", "gemv")
+
+    def step(self, gcu, stream=None, want=None):
         for layer in self.L:
             for g in layer:
                 k = g["k"]
-                if ev:
-                    ev("quant", 5 * k + 4, 0)
-                gcu.dev_quantize_acts(g["q"], g["s"], g["x"], 1, k, stream=stream)
-                if ev:
-                    ev(None)
-                    nsum = sum(w.shape[0] for w, _ in g["w"])
-                    ev("gemv", nsum * (k + 8) + k + 4, 2 * nsum * k)
-                gcu.dev_gemv_int8_multi([(w, sc, o) for (w, sc), o in zip(g["w"], g["o"])], g["q"], g["s"], k,
-                                        stream=stream)
-                if ev:
-                    ev(None)
+                if want is None or want("quant", 5 * k + 4, 0):
+                    gcu.dev_quantize_acts(g["q"], g["s"], g["x"], 1, k, stream=stream)
+                nsum = sum(w.shape[0] for w, _ in g["w"])
+                if want is None or want("gemv", nsum * (k + 8) + k + 4, 2 * nsum * k):
+                    gcu.dev_gemv_int8_multi([(w, sc, o) for (w, sc), o in zip(g["w"], g["o"])], g["q"], g["s"],
+                                            k, stream=stream)
         h = self.head
         d = self.cfg["dim"]
-        if ev:
-            ev("quant", 5 * d + 4, 0)
-        gcu.dev_quantize_acts(h["q"], h["s"], h["x"], 1, d, stream=stream)
-        if ev:
-            ev(None)
-            n = self.cfg["vocab"]
-            ev("gemv", n * (d + 8) + d + 4, 2 * n * d)
-        gcu.dev_gemv_int8(h["o"], h["w"][0], h["w"][1], h["q"], h["s"], self.cfg["vocab"], d, stream=stream)
-        if ev:
-            ev(None)
+        n = self.cfg["vocab"]
+        if want is None or want("quant", 5 * d + 4, 0):
+            gcu.dev_quantize_acts(h["q"], h["s"], h["x"], 1, d, stream=stream)
+        if want is None or want("gemv", n * (d + 8) + d + 4, 2 * n * d):
+            gcu.dev_gemv_int8(h["o"], h["w"][0], h["w"][1], h["q"], h["s"], n, d, stream=stream)
 
     launches_per_step = property(lambda self: self.layers * 2 * len(self.groups) + 2)
 
@@ -373,14 +364,14 @@ class LmHead:
         self.y = torch.empty((self.b, self.n), dtype=torch.float32, device=device)
         self.work = torch.empty((self.b, self.n), dtype=torch.float32, device=device)
 
-    def step(self, gcu, stream=None, ev=None):
-        gcu.dev_quantize_acts(self.q, self.s, self.x, self.b, self.k, stream=stream)
+    kinds = ("quant", "gemv")
+
+    def step(self, gcu, stream=None, want=None):
+        if want is None or want("quant", 5 * self.b * self.k + 4 * self.b, 0):
+            gcu.dev_quantize_acts(self.q, self.s, self.x, self.b, self.k, stream=stream)
         if self.world == 1:
-            if ev:
-                ev("gemv", self.bytes, 2 * self.b * self.n * self.k)
-            gcu.dev_gemm_int8(self.y, self.w, self.ws, self.q, self.s, self.b, self.n, self.k, stream=stream)
-            if ev:
-                ev(None)
+            if want is None or want("gemv", self.bytes, 2 * self.b * self.n * self.k):
+                gcu.dev_gemm_int8(self.y, self.w, self.ws, self.q, self.s, self.b, self.n, self.k, stream=stream)
         else:
             gcu.dev_gemm_int8_rowshard(self.y, self.work, self.w, self.ws, self.q, self.s, self.b, self.n,
                                        self.k, stream=stream)
@@ -462,32 +453,39 @@ def run_ours(args):
     clk = clocks.stop()
     gcu.check_device()
 
-    # per-kernel durations: the same step, eager, each launch bracketed by
-    # CUDA events on the launching stream
+    # per-kernel-class durations: the step's launches of one kernel class
+    # only (same inputs, same order), captured as a CUDA graph and replayed
+    # `steps` times between CUDA events on the launching stream; the
+    # average launch duration includes the graph's inter-kernel gap
     prof = {}
-    pending = []
+    if use_graph:
+        for kind in wl.kinds:
+            acc = {"launches": 0, "bytes": 0, "ops": 0}
 
-    def ev(kind, nbytes=0, ops=0):
-        if kind is None:
-            e = torch.cuda.Event(enable_timing=True)
-            e.record(stream)
-            pending[-1][3] = e
-        else:
-            e = torch.cuda.Event(enable_timing=True)
-            e.record(stream)
-            pending.append([kind, nbytes, ops, None, e])
+            def want(k, nbytes, ops, kind=kind, acc=acc):
+                if k != kind:
+                    return False
+                acc["launches"] += 1
+                acc["bytes"] += nbytes
+                acc["ops"] += ops
+                return True
 
-    psteps = max(1, min(args.steps, 5))
-    with torch.cuda.stream(stream):
-        for _ in range(psteps):
-            wl.step(gcu, ev=ev)
-    torch.cuda.synchronize()
-    for kind, nbytes, ops, e_end, e_start in pending:
-        d = prof.setdefault(kind, {"launches": 0, "ms": 0.0, "bytes": 0, "ops": 0})
-        d["launches"] += 1
-        d["ms"] += e_start.elapsed_time(e_end)
-        d["bytes"] += nbytes
-        d["ops"] += ops
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                wl.step(gcu, want=want)
+            with torch.cuda.stream(stream):
+                for _ in range(2):
+                    g.replay()
+                k0 = torch.cuda.Event(enable_timing=True)
+                k1 = torch.cuda.Event(enable_timing=True)
+                k0.record(stream)
+                for _ in range(args.steps):
+                    g.replay()
+                k1.record(stream)
+            torch.cuda.synchronize()
+            prof[kind] = {"launches": acc["launches"] * args.steps, "ms": k0.elapsed_time(k1),
+                          "bytes": acc["bytes"] * args.steps, "ops": acc["ops"] * args.steps}
+            del g
 
     out = {"metric": METRIC, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
            "ms_per_step": ms, "higher_is_better": True, "vs_baseline": None, "data": "synthetic",
