@@ -649,15 +649,15 @@ GCU_EXPORT int gcu_dev_gemm_int8_multi(const gcu_gemv_job *jobs, int njobs, cons
   return launch_gemm_tc_jobs(src, sstr, ssc, m, k, a, njobs, as_stream(stream), 0, 0);
 }
 
-// Tuning hook (not in gcu.h): force the tensor-core kernel's tile width
-// (128/256) and K split for one call.  Used by the benchmark's sweeps.
+// Tuning hook (not in gcu.h): force the tensor-core kernel's tile shape
+// ((128*mb) x bn) and K split for one call.  Used by the benchmark's sweeps.
 GCU_EXPORT int gcu_dev_gemm_int8_tuned(float *dst, int dstr, const int8_t *mat, int mstr,
                                        const float *matsc, const int8_t *src, int sstr,
                                        const float *ssc, int m, int n, int k, int bn, int split,
-                                       void *stream) {
+                                       int mb, void *stream) {
   if (dstr == 0) dstr = n;
   if (mstr == 0) mstr = k;
   if (sstr == 0) sstr = k;
   GemmArgs a{dst, dstr, mat, mstr, matsc, src, sstr, ssc, m, n, k};
-  return launch_gemm_tc(a, as_stream(stream), bn, split);
+  return launch_gemm_tc(a, as_stream(stream), bn, split, mb);
 }

@@ -94,8 +94,10 @@ struct GemmArgs {
   const float *ssc;
   int m, n, k;
 };
+// force_bn / force_mb / force_split = 0 let the planner choose the tile
+// shape ((128*mb) x bn) and the K split.
 int launch_gemm_tc(const GemmArgs &a, cudaStream_t st, int force_bn,
-                   int force_split);
+                   int force_split, int force_mb = 0);
 
 // Caller-owned split-K scratch: when given, the launcher uses it instead of
 // the runtime's allocated workspace, fails if the plan needs more than
@@ -110,7 +112,7 @@ struct ExtWorkspace {
 int launch_gemm_tc_jobs(const int8_t *src, long sstr, const float *ssc, int m,
                         int k, const GemmArgs *jobs, int njobs, cudaStream_t st,
                         int force_bn, int force_split,
-                        const ExtWorkspace *ext = nullptr);
+                        const ExtWorkspace *ext = nullptr, int force_mb = 0);
 
 // split-K workspace and tile counters (device memory owned by the runtime)
 int gemm_workspace(size_t bytes, void **ws, int **counters, int ncounters,

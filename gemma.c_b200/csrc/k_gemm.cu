@@ -6,16 +6,21 @@
 // accumulation cannot change a bit; the epilogue is the reference -ffast-math
 // build's (float)acc * (xs*ws) with round-to-nearest multiplies.
 //
-// Design (one CTA per SM, persistent over work units):
-//   warp 0      TMA producer: 128-byte-swizzled A (128 x 128 B) and B
+// Design (one CTA per SM, persistent over work units).  A CTA tile is
+// (128*MB) x BN outputs, MB in {1, 2}: with MB = 2 every B stage feeds two
+// M=128 MMAs, which halves the operand bytes each SM pulls per output --
+// the limit for the small-M (prefill) shapes, whose A/B panels are re-read
+// from L2 by every tile.
+//   warp 0      TMA producer: 128-byte-swizzled A ((128*MB) x 128 B) and B
 //               (BN x 128 B) tiles into a STAGES-deep shared-memory ring
 //   warp 1      allocates TMEM, issues tcgen05.mma.cta_group::1.kind::i8
 //               (M=128, N=BN, K=32) from one thread, commits stage releases
-//   warps 2-5   epilogue: tcgen05.ld the int32 accumulators (two TMEM
-//               buffers, so the next tile's MMAs overlap this epilogue),
-//               dequantize, stage through swizzled shared memory and TMA-store
-//               fp32 rows; or, when K is split, write int32 partials and let
-//               the last split of a tile reduce them
+//   warps 2-9   epilogue, two warps per TMEM lane quarter: tcgen05.ld the
+//               int32 accumulators (two TMEM buffers when they fit, so the
+//               next tile's MMAs overlap this epilogue), dequantize, stage
+//               through swizzled shared memory and TMA-store fp32 rows; or,
+//               when K is split, write int32 partials and let the last split
+//               of a tile reduce them
 // No cluster multicast is used anywhere (every load reads this GPU's memory).
 // Every wait is bounded (globaltimer); on timeout the kernel records an error
 // code, drains its copies, frees TMEM and returns.
@@ -36,17 +41,34 @@ constexpr int kThreads = 64 + kEpiThreads;
 constexpr int kMaxJobs = 4;
 constexpr int kEpiStageBytes = 32 * 128;  // 32 rows x 32 fp32
 
-template <int BN>
+constexpr int kSmemMax = 232448;  // opt-in shared memory per CTA on sm_100
+
+__host__ __device__ constexpr int pow2_at_least(int v) {
+  int p = 32;
+  while (p < v) p <<= 1;
+  return p;
+}
+
+template <int BN, int MB>
 struct Cfg {
-  static constexpr int STAGES = BN == 256 ? 4 : BN == 128 ? 5 : 7;
-  static constexpr int A_BYTES = BM * BK;
+  static constexpr int TILE_M = BM * MB;
+  static constexpr int A_BYTES = TILE_M * BK;
   static constexpr int B_BYTES = BN * BK;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int ACC_COLS = MB * BN;  // TMEM columns of one tile
+  static constexpr int NBUF = 2 * ACC_COLS <= 512 ? 2 : 1;
+  static constexpr int TMEM_COLS = pow2_at_least(NBUF * ACC_COLS);
+  static constexpr int EPI_BYTES = kEpiWarps * kEpiStageBytes;
+  static constexpr int FIXED = 1024 + EPI_BYTES + 512;
+  static constexpr int STAGES_FIT = (kSmemMax - FIXED) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
-  static constexpr int BAR_OFF = EPI_OFF + kEpiWarps * kEpiStageBytes;
+  static constexpr int BAR_OFF = EPI_OFF + EPI_BYTES;
   static constexpr int NBARS = 2 * STAGES + 5;
   static constexpr int SMEM = 1024 + BAR_OFF + NBARS * 8 + 16;
+  static_assert(STAGES >= 2, "tile too large for shared memory");
+  static_assert(SMEM + 64 <= kSmemMax, "shared memory budget");
+  static_assert(ACC_COLS <= 512 && BN % 32 == 0 && BN <= 256, "tile shape");
 };
 
 struct alignas(64) TcJob {
@@ -67,7 +89,7 @@ struct alignas(64) TcParams {
   int m, k;
   int tiles_m, tiles_n, splits, kb_total, kb_per_split, units;
   const float *ssc;
-  int32_t *ws;    // split-K partials [tile][split][BM][BN]
+  int32_t *ws;    // split-K partials [tile][split][TILE_M][BN]
   int *counters;  // split-K arrival counters [tile]
   unsigned int *err;
 };
@@ -131,9 +153,9 @@ __device__ __forceinline__ void emit_chunk(const TcParams &p, const TcJob &job, 
   }
 }
 
-template <int BN>
+template <int BN, int MB>
 __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_tc(const __grid_constant__ TcParams p) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, MB>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -201,7 +223,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_tc(const __grid_constan
             break;
           }
           ptx::mbar_arrive_expect_tx(&full[st], C::STAGE_BYTES);
-          ptx::tma_load_2d(&p.tmA, &full[st], smA + st * C::A_BYTES, kb * BK, w.m_t * BM, pol_a);
+          ptx::tma_load_2d(&p.tmA, &full[st], smA + st * C::A_BYTES, kb * BK, w.m_t * C::TILE_M,
+                           pol_a);
           ptx::tma_load_2d(&p.jobs[w.job].tmB, &full[st], smB + st * C::B_BYTES, kb * BK,
                            w.n_t * BN, pol_b);
         }
@@ -223,14 +246,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_tc(const __grid_constan
         const Unit w = decode_unit(p, u);
         const int kb0 = w.s * p.kb_per_split;
         const int kb1 = min(kb0 + p.kb_per_split, p.kb_total);
-        const int buf = t & 1;
-        const uint32_t use = t >> 1;
+        const int buf = t % C::NBUF;
+        const uint32_t use = t / C::NBUF;
         if (!ptx::mbar_wait(&tempty[buf], (use & 1) ^ 1, p.err, DEV_TIMEOUT_TMEM)) {
           ok = false;
           break;
         }
         ptx::tc_fence_after();
-        const uint32_t d_tmem = tmem_base + buf * BN;
+        const uint32_t d_tmem = tmem_base + buf * C::ACC_COLS;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int st = it % C::STAGES;
           const uint32_t round = it / C::STAGES;
@@ -243,8 +266,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_tc(const __grid_constan
           const uint32_t b0 = ptx::smem_u32(smB + st * C::B_BYTES);
 #pragma unroll
           for (int j = 0; j < BK / 32; ++j)
-            ptx::mma_i8(d_tmem, ptx::smem_desc_k128(a0 + 32 * j), ptx::smem_desc_k128(b0 + 32 * j),
-                        idesc, (kb > kb0 || j > 0) ? 1u : 0u);
+#pragma unroll
+            for (int mb = 0; mb < MB; ++mb)  // M block mb: A rows 128*mb.., TMEM columns BN*mb..
+              ptx::mma_i8(d_tmem + mb * BN, ptx::smem_desc_k128(a0 + mb * BM * BK + 32 * j),
+                          ptx::smem_desc_k128(b0 + 32 * j), idesc, (kb > kb0 || j > 0) ? 1u : 0u);
           ptx::mma_commit(&empty[st]);
         }
         ptx::mma_commit(&tfull[buf]);
@@ -257,17 +282,21 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_tc(const __grid_constan
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int half = (warp - 2) >> 2;  // this warp takes chunks with (ch & 1) == half
+    const int q = warp & 3;            // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;  // second warp of the quarter?
+    // MB == 2: the two warps of a quarter take one M block each, all chunks;
+    // MB == 1: they share the M block and take alternate chunks
+    const int mblk = MB == 2 ? half : 0;
     uint8_t *stage = epi + (warp - 2) * kEpiStageBytes;
     constexpr int NCH = BN / 32;  // 32-column chunks per tile
+    auto mine = [&](int ch) { return MB == 2 || (ch & 1) == half; };
     int t = 0;
     for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++t) {
       const Unit w = decode_unit(p, u);
       const TcJob &job = p.jobs[w.job];
-      const int buf = t & 1;
-      const uint32_t use = t >> 1;
-      const int tile_row0 = w.m_t * BM + q * 32;
+      const int buf = t % C::NBUF;
+      const uint32_t use = t / C::NBUF;
+      const int tile_row0 = w.m_t * C::TILE_M + mblk * BM + q * 32;
       const int row = tile_row0 + lane;
       const int n0 = w.n_t * BN;
       // operand scales of this tile, fetched while its MMAs still run: the
@@ -282,11 +311,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_tc(const __grid_constan
       }
       if (!ptx::mbar_wait(&tfull[buf], use & 1, p.err, DEV_TIMEOUT_TMEM)) break;
       ptx::tc_fence_after();
-      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
+      const uint32_t taddr =
+          tmem_base + ((uint32_t)(q * 32) << 16) + buf * C::ACC_COLS + mblk * BN;
       if (p.splits == 1) {
 #pragma unroll
         for (int ch = 0; ch < NCH; ++ch) {
-          if ((ch & 1) != half) continue;
+          if (!mine(ch)) continue;
           __syncwarp();
           uint32_t r[32];
           ptx::tmem_ld_32x32(taddr + ch * 32, r);
@@ -308,13 +338,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_tc(const __grid_constan
       } else {
         // split K: this split's int32 partial goes to the workspace in a
         // layout where each warp store is 512 contiguous bytes:
-        // [quarter q][chunk][8 x int4][lane]
-        constexpr size_t kPartInt4 = (size_t)BM * BN / 4;
+        // [M block][quarter q][chunk][8 x int4][lane]
+        constexpr size_t kPartInt4 = (size_t)C::TILE_M * BN / 4;
+        const size_t my_off = (size_t)(mblk * 4 + q) * NCH * 8 * 32 + lane;
         int4 *part = reinterpret_cast<int4 *>(p.ws) + ((size_t)w.tile * p.splits + w.s) * kPartInt4 +
-                     (size_t)q * NCH * 8 * 32 + lane;
+                     my_off;
 #pragma unroll
         for (int ch = 0; ch < NCH; ++ch) {
-          if ((ch & 1) != half) continue;
+          if (!mine(ch)) continue;
           __syncwarp();
           uint32_t r[32];
           ptx::tmem_ld_32x32(taddr + ch * 32, r);
@@ -337,11 +368,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_tc(const __grid_constan
           // the last split to finish sums every partial (integer adds are
           // exact, so the order of arrival does not matter)
           __threadfence();
-          const int4 *base = reinterpret_cast<const int4 *>(p.ws) + (size_t)w.tile * p.splits * kPartInt4 +
-                             (size_t)q * NCH * 8 * 32 + lane;
+          const int4 *base =
+              reinterpret_cast<const int4 *>(p.ws) + (size_t)w.tile * p.splits * kPartInt4 + my_off;
 #pragma unroll
           for (int ch = 0; ch < NCH; ++ch) {
-            if ((ch & 1) != half) continue;
+            if (!mine(ch)) continue;
             const int col0 = n0 + ch * 32;
             if (col0 >= job.n) continue;
             int acc[32];
@@ -363,7 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_tc(const __grid_constan
               if (lane == 0) ptx::bulk_wait_read<0>();
               __syncwarp();
               emit_chunk<true>(p, job, acc, xs, wsl[ch], row, col0, lane, stage, tile_row0);
-              } else {
+            } else {
               emit_chunk<false>(p, job, acc, xs, wsl[ch], row, col0, lane, nullptr, tile_row0);
             }
           }
@@ -428,9 +459,9 @@ int make_map_f32(CUtensorMap *m, float *base, int n, int rows, long stride_elems
   return 0;
 }
 
-template <int BN>
-int launch_bn(TcParams &p, cudaStream_t st) {
-  using C = Cfg<BN>;
+template <int BN, int MB>
+int launch_cfg(TcParams &p, cudaStream_t st) {
+  using C = Cfg<BN, MB>;
   // the shared-memory opt-in is per device; set it once, outside any capture
   static std::mutex mu;
   static uint64_t done_mask = 0;
@@ -439,20 +470,52 @@ int launch_bn(TcParams &p, cudaStream_t st) {
   {
     std::lock_guard<std::mutex> lk(mu);
     if (!(done_mask & (1ull << (dev & 63)))) {
-      GCU_CUDA(cudaFuncSetAttribute(k_gemm_i8_tc<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    C::SMEM));
+      GCU_CUDA(cudaFuncSetAttribute(k_gemm_i8_tc<BN, MB>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
       done_mask |= 1ull << (dev & 63);
     }
   }
   int grid = p.units < num_sms() ? p.units : num_sms();
-  GCU_CUDA(launch_k(k_gemm_i8_tc<BN>, grid, kThreads, C::SMEM, st, p));
+  GCU_CUDA(launch_k(k_gemm_i8_tc<BN, MB>, grid, kThreads, C::SMEM, st, p));
   GCU_CUDA(cudaGetLastError());
   return 0;
 }
 
-double wave_eff(long units, int sms) {
-  long waves = (units + sms - 1) / sms;
-  return (double)units / (double)(waves * sms);
+// Tile shapes the kernel is instantiated for: BN x (128*MB).
+struct Shape {
+  int bn, mb;
+};
+constexpr Shape kShapes[] = {{64, 1}, {128, 1}, {256, 1}, {128, 2}, {192, 2}, {256, 2}};
+
+int split_for(int tiles, int kb_total, int sms) {
+  // split K only when the tiles cannot occupy the SMs and K is long, keeping
+  // at least 8 K blocks per split so the partial round trip stays small
+  if (tiles * 2 > sms || kb_total < 16) return 1;
+  int s = sms / tiles;
+  if (s > kb_total / 8) s = kb_total / 8;
+  if (s > 16) s = 16;
+  return s < 1 ? 1 : s;
+}
+
+// Estimated microseconds of one launch with this tile shape.  Measured on
+// B200: a CTA's TMA ring ingests about 100 GB/s, the SMs together about
+// 9 TB/s from L2; the int8 tensor rate is about 22 TOPS per SM; the last
+// tile's epilogue and a split-K round trip are not overlapped.
+double estimate_us(int m, int ntn, int kb_total, int bn, int mb, int splits, int sms) {
+  const double tile_m = 128.0 * mb;
+  const long tiles = (long)((m + 128 * mb - 1) / (128 * mb)) * ntn;
+  const long units = tiles * splits;
+  const int kb_unit = (kb_total + splits - 1) / splits;
+  const double stage = (tile_m + bn) * 128.0;
+  const double t_load = kb_unit * stage / 1.0e5;
+  const double t_mma = kb_unit * 2.0 * tile_m * bn * 128.0 / 2.2e7;
+  const double t_unit = t_load > t_mma ? t_load : t_mma;
+  const long waves = (units + sms - 1) / sms;
+  const double t_l2 = (double)units * kb_unit * stage / 9.0e6;
+  const double t_main = waves * t_unit > t_l2 ? waves * t_unit : t_l2;
+  const double t_out = tile_m * bn * 4.0 / 1.0e5;
+  const double t_split = splits > 1 ? tile_m * bn * 4.0 * (1 + splits) / 1.0e5 : 0.0;
+  return t_main + t_out + t_split;
 }
 
 }  // namespace
@@ -460,42 +523,47 @@ double wave_eff(long units, int sms) {
 // Multi-job entry: jobs share A (src); job j has its own weights and output.
 int launch_gemm_tc_jobs(const int8_t *src, long sstr, const float *ssc, int m, int k,
                         const GemmArgs *jobs, int njobs, cudaStream_t st, int force_bn,
-                        int force_split, const ExtWorkspace *ext) {
+                        int force_split, const ExtWorkspace *ext, int force_mb) {
   if (njobs < 1 || njobs > kMaxJobs) return set_error("gemm: 1..%d jobs (got %d)", kMaxJobs, njobs);
   if (m <= 0 || k <= 0) return 0;
   if (get_encode()) return 1;
   if ((uintptr_t)src % 16 || sstr % 16)
     return set_error("gemm: activation rows must be 16-byte aligned (stride %ld)", sstr);
   const int sms = num_sms();
-  const int tiles_m = (m + BM - 1) / BM;
-  int ntot64 = 0, ntot128 = 0, ntot256 = 0;
-  for (int j = 0; j < njobs; ++j) {
-    ntot64 += (jobs[j].n + 63) / 64;
-    ntot128 += (jobs[j].n + 127) / 128;
-    ntot256 += (jobs[j].n + 255) / 256;
+  for (int j = 0; j < njobs; ++j)
     if ((uintptr_t)jobs[j].mat % 16 || jobs[j].mstr % 16)
       return set_error("gemm: weight rows must be 16-byte aligned (stride %ld)", jobs[j].mstr);
-  }
-  int bn = force_bn;
-  if (bn != 64 && bn != 128 && bn != 256) {
-    const double e256 = wave_eff((long)tiles_m * ntot256, sms);
-    const double e128 = wave_eff((long)tiles_m * ntot128, sms);
-    bn = (e256 >= 0.85 || e256 >= e128) ? 256 : 128;
-  }
-  const int tiles_n = bn == 256 ? ntot256 : bn == 128 ? ntot128 : ntot64;
-  const int tiles = tiles_m * tiles_n;
+  auto ntiles_n = [&](int bn_) {
+    int t = 0;
+    for (int j = 0; j < njobs; ++j) t += (jobs[j].n + bn_ - 1) / bn_;
+    return t;
+  };
   const int kb_total = (k + BK - 1) / BK;
-  int splits = 1;
-  if (force_split > 0) {
-    splits = force_split;
-  } else if (tiles * 2 <= sms && kb_total >= 16) {
-    // too few tiles to occupy the SMs and a long K: split it, keeping at
-    // least 8 K blocks per split so the partial round trip stays small
-    splits = sms / tiles;
-    if (splits > kb_total / 8) splits = kb_total / 8;
-    if (splits > 16) splits = 16;
-    if (splits < 1) splits = 1;
+  int bn = 0, mb = 0;
+  if (force_bn > 0) {
+    bn = force_bn;
+    mb = force_mb > 0 ? force_mb : 1;
+    bool known = false;
+    for (const Shape &sh : kShapes) known |= (sh.bn == bn && sh.mb == mb);
+    if (!known) return set_error("gemm: no %d x %d tile variant", 128 * mb, bn);
+  } else {
+    double best = 1e30;
+    for (const Shape &sh : kShapes) {
+      const int tiles_ = (m + 128 * sh.mb - 1) / (128 * sh.mb) * ntiles_n(sh.bn);
+      const int sp = split_for(tiles_, kb_total, sms);
+      const double t = estimate_us(m, ntiles_n(sh.bn), kb_total, sh.bn, sh.mb, sp, sms);
+      if (t < best - 1e-9) {
+        best = t;
+        bn = sh.bn;
+        mb = sh.mb;
+      }
+    }
   }
+  const int tile_m = BM * mb;
+  const int tiles_m = (m + tile_m - 1) / tile_m;
+  const int tiles_n = ntiles_n(bn);
+  const int tiles = tiles_m * tiles_n;
+  int splits = force_split > 0 ? force_split : split_for(tiles, kb_total, sms);
   if (splits > kb_total) splits = kb_total;
   const int kb_per = (kb_total + splits - 1) / splits;
   splits = (kb_total + kb_per - 1) / kb_per;
@@ -503,7 +571,7 @@ int launch_gemm_tc_jobs(const int8_t *src, long sstr, const float *ssc, int m, i
   static_assert(sizeof(TcParams) <= 4096, "kernel parameters exceed 4 KB");
   TcParams p;
   memset(&p, 0, sizeof(p));
-  if (make_map_i8(&p.tmA, src, k, m, sstr, BM)) return 1;
+  if (make_map_i8(&p.tmA, src, k, m, sstr, tile_m)) return 1;
   int tn = 0;
   for (int j = 0; j < njobs; ++j) {
     TcJob &J = p.jobs[j];
@@ -529,7 +597,7 @@ int launch_gemm_tc_jobs(const int8_t *src, long sstr, const float *ssc, int m, i
   p.ssc = ssc;
   p.err = dev_error_word();
   if (splits > 1) {
-    const size_t need = (size_t)tiles * splits * BM * bn * sizeof(int32_t);
+    const size_t need = (size_t)tiles * splits * tile_m * bn * sizeof(int32_t);
     void *ws = nullptr;
     int *cnt = nullptr;
     if (ext) {
@@ -546,13 +614,20 @@ int launch_gemm_tc_jobs(const int8_t *src, long sstr, const float *ssc, int m, i
     p.ws = static_cast<int32_t *>(ws);
     p.counters = cnt;
   }
-  if (bn == 256) return launch_bn<256>(p, st);
-  if (bn == 128) return launch_bn<128>(p, st);
-  return launch_bn<64>(p, st);
+  if (mb == 2) {
+    if (bn == 128) return launch_cfg<128, 2>(p, st);
+    if (bn == 192) return launch_cfg<192, 2>(p, st);
+    return launch_cfg<256, 2>(p, st);
+  }
+  if (bn == 256) return launch_cfg<256, 1>(p, st);
+  if (bn == 128) return launch_cfg<128, 1>(p, st);
+  return launch_cfg<64, 1>(p, st);
 }
 
-int launch_gemm_tc(const GemmArgs &a, cudaStream_t st, int force_bn, int force_split) {
-  return launch_gemm_tc_jobs(a.src, a.sstr, a.ssc, a.m, a.k, &a, 1, st, force_bn, force_split);
+int launch_gemm_tc(const GemmArgs &a, cudaStream_t st, int force_bn, int force_split,
+                   int force_mb) {
+  return launch_gemm_tc_jobs(a.src, a.sstr, a.ssc, a.m, a.k, &a, 1, st, force_bn, force_split,
+                             nullptr, force_mb);
 }
 
 }  // namespace gcu

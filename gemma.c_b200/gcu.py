@@ -62,7 +62,7 @@ SIGNATURES = {
 # exported but not part of the public header (benchmark sweeps)
 EXTRA = {
     "gcu_dev_gemm_int8_tuned": (_int, [_vp, _int, _vp, _int, _vp, _vp, _int, _vp, _int, _int, _int,
-                                       _int, _int, _vp]),
+                                       _int, _int, _int, _vp]),
 }
 
 
@@ -229,9 +229,10 @@ def dev_gemm_int8_multi(jobs_t, src, ssc, m, k, sstr=0, stream=None):
                                          _stream(stream)), "dev_gemm_int8_multi")
 
 
-def dev_gemm_int8_tuned(dst, mat, matsc, src, ssc, m, n, k, bn, split, stream=None):
+def dev_gemm_int8_tuned(dst, mat, matsc, src, ssc, m, n, k, bn, split, mb=1, stream=None):
+    """Force the tile shape ((128*mb) x bn) and K split (benchmark sweeps)."""
     _check(lib().gcu_dev_gemm_int8_tuned(dst.data_ptr(), 0, mat.data_ptr(), 0, matsc.data_ptr(),
-                                         src.data_ptr(), 0, ssc.data_ptr(), m, n, k, bn, split,
+                                         src.data_ptr(), 0, ssc.data_ptr(), m, n, k, bn, split, mb,
                                          _stream(stream)), "dev_gemm_int8_tuned")
 
 

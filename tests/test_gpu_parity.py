@@ -220,13 +220,16 @@ def _dev(a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
-@pytest.mark.parametrize("bn,split", [(128, 1), (256, 1), (128, 3), (256, 2), (128, 7), (64, 1), (64, 3)])
-def test_gemm_tile_and_split_variants(bn, split):
+@pytest.mark.parametrize("bn,split,mb", [(128, 1, 1), (256, 1, 1), (128, 3, 1), (256, 2, 1), (128, 7, 1),
+                                         (64, 1, 1), (64, 3, 1), (128, 1, 2), (192, 1, 2), (256, 1, 2),
+                                         (192, 3, 2), (128, 2, 2)])
+def test_gemm_tile_and_split_variants(bn, split, mb):
+    # m = 384 leaves a half-empty last 256-row tile for mb = 2
     m, n, k = 384, 1000, 2304
     w, ws = synth.weight(7000 + bn + split, n, k)
     xq, xs = O.quantize_acts(synth.activations(7100, m, k, outliers=True))
     y = torch.empty((m, n), dtype=torch.float32, device="cuda")
-    gcu.dev_gemm_int8_tuned(y, _dev(w), _dev(ws), _dev(xq), _dev(xs), m, n, k, bn, split)
+    gcu.dev_gemm_int8_tuned(y, _dev(w), _dev(ws), _dev(xq), _dev(xs), m, n, k, bn, split, mb)
     torch.cuda.synchronize()
     gcu.check_device()
     assert_bits(y.cpu().numpy(), O.gemm_int8(w, ws, xq, xs))
