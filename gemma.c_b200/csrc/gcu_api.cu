@@ -649,6 +649,22 @@ GCU_EXPORT int gcu_dev_gemm_int8_multi(const gcu_gemv_job *jobs, int njobs, cons
   return launch_gemm_tc_jobs(src, sstr, ssc, m, k, a, njobs, as_stream(stream), 0, 0);
 }
 
+// Tuning hook (not in gcu.h): the multi-job GEMM with a forced tile shape
+// ((128*mb) x bn) and K split.  Used by the benchmark's sweeps.
+GCU_EXPORT int gcu_dev_gemm_int8_multi_tuned(const gcu_gemv_job *jobs, int njobs, const int8_t *src,
+                                             int sstr, const float *ssc, int m, int k, int bn,
+                                             int split, int mb, void *stream) {
+  if (m <= 0 || njobs <= 0) return 0;
+  if (sstr == 0) sstr = k;
+  if (njobs > 4) return set_error("gemm_int8_multi: at most 4 jobs on the tensor-core path");
+  GemmArgs a[4];
+  for (int j = 0; j < njobs; ++j)
+    a[j] = GemmArgs{jobs[j].dst, jobs[j].m, (const int8_t *)jobs[j].w, k, jobs[j].sc,
+                    src, sstr, ssc, m, jobs[j].m, k};
+  return launch_gemm_tc_jobs(src, sstr, ssc, m, k, a, njobs, as_stream(stream), bn, split, nullptr,
+                             mb);
+}
+
 // Tuning hook (not in gcu.h): force the tensor-core kernel's tile shape
 // ((128*mb) x bn) and K split for one call.  Used by the benchmark's sweeps.
 GCU_EXPORT int gcu_dev_gemm_int8_tuned(float *dst, int dstr, const int8_t *mat, int mstr,

@@ -28,7 +28,11 @@
 
 #include <cudaTypedefs.h>
 
+#include <cstdio>
+#include <cstdlib>
+#include <map>
 #include <mutex>
+#include <tuple>
 
 namespace gcu {
 namespace {
@@ -520,6 +524,132 @@ double estimate_us(int m, int ntn, int kb_total, int bn, int mb, int splits, int
 
 }  // namespace
 
+namespace {
+
+struct Plan {
+  int bn, mb, splits;  // CTA tile (128*mb) x bn, K split
+};
+
+int ntiles_n(const GemmArgs *jobs, int njobs, int bn) {
+  int t = 0;
+  for (int j = 0; j < njobs; ++j) t += (jobs[j].n + bn - 1) / bn;
+  return t;
+}
+
+// Enqueue one launch of plan `pl` (everything after the tile choice).
+int run_plan(const Plan &pl, const int8_t *src, long sstr, const float *ssc, int m, int k,
+             const GemmArgs *jobs, int njobs, cudaStream_t st, const ExtWorkspace *ext);
+
+// Planner's pick without running anything: the cost model above.
+Plan model_plan(int m, int k, const GemmArgs *jobs, int njobs, int sms) {
+  const int kb_total = (k + BK - 1) / BK;
+  Plan best{128, 1, 1};
+  double best_t = 1e30;
+  for (const Shape &sh : kShapes) {
+    const int tiles = (m + 128 * sh.mb - 1) / (128 * sh.mb) * ntiles_n(jobs, njobs, sh.bn);
+    const int sp = split_for(tiles, kb_total, sms);
+    const double t = estimate_us(m, ntiles_n(jobs, njobs, sh.bn), kb_total, sh.bn, sh.mb, sp, sms);
+    if (t < best_t - 1e-9) {
+      best_t = t;
+      best = Plan{sh.bn, sh.mb, sp};
+    }
+  }
+  return best;
+}
+
+// Measured pick (opt-in, GCU_AUTOTUNE=1): the first call of a shape
+// (outside stream capture) times every tile shape, with and without a K
+// split, on the caller's stream and caches the fastest per device.  Every
+// candidate computes the same exact int32 sums, so the output is the same
+// whichever wins.  It times repeated calls on the same operands, i.e. with
+// the weights warm in L2, which misjudges a model whose weights stream from
+// HBM once per token; the calibrated cost model is therefore the default.
+struct TuneKey {
+  int dev, m, k, njobs, n[kMaxJobs];
+  bool operator<(const TuneKey &o) const {
+    return std::tie(dev, m, k, njobs, n[0], n[1], n[2], n[3]) <
+           std::tie(o.dev, o.m, o.k, o.njobs, o.n[0], o.n[1], o.n[2], o.n[3]);
+  }
+};
+std::mutex g_tune_mu;
+std::map<TuneKey, Plan> g_tune;
+
+bool autotune_enabled() {
+  static const bool on = [] {
+    const char *e = getenv("GCU_AUTOTUNE");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
+
+int tuned_plan(Plan *out, const int8_t *src, long sstr, const float *ssc, int m, int k,
+               const GemmArgs *jobs, int njobs, cudaStream_t st, int sms) {
+  TuneKey key{};
+  GCU_CUDA(cudaGetDevice(&key.dev));
+  key.m = m;
+  key.k = k;
+  key.njobs = njobs;
+  for (int j = 0; j < njobs; ++j) key.n[j] = jobs[j].n;
+  {
+    std::lock_guard<std::mutex> lk(g_tune_mu);
+    auto it = g_tune.find(key);
+    if (it != g_tune.end()) {
+      *out = it->second;
+      return 0;
+    }
+  }
+  const int kb_total = (k + BK - 1) / BK;
+  Plan cand[2 * sizeof(kShapes) / sizeof(kShapes[0])];
+  int nc = 0;
+  for (const Shape &sh : kShapes) {
+    const int tiles = (m + 128 * sh.mb - 1) / (128 * sh.mb) * ntiles_n(jobs, njobs, sh.bn);
+    const int sp = split_for(tiles, kb_total, sms);
+    cand[nc++] = Plan{sh.bn, sh.mb, 1};
+    if (sp > 1) cand[nc++] = Plan{sh.bn, sh.mb, sp};
+  }
+  cudaEvent_t e0, e1;
+  GCU_CUDA(cudaEventCreate(&e0));
+  if (cudaEventCreate(&e1) != cudaSuccess) {
+    cudaEventDestroy(e0);
+    return set_error("gemm autotune: cudaEventCreate failed");
+  }
+  float best_ms = 1e30f;
+  Plan best = model_plan(m, k, jobs, njobs, sms);
+  int rc = 0;
+  for (int c = 0; c < nc && rc == 0; ++c) {
+    rc = run_plan(cand[c], src, sstr, ssc, m, k, jobs, njobs, st, nullptr);  // warm
+    if (rc) break;
+    cudaEventRecord(e0, st);
+    for (int r = 0; r < 3 && rc == 0; ++r)
+      rc = run_plan(cand[c], src, sstr, ssc, m, k, jobs, njobs, st, nullptr);
+    cudaEventRecord(e1, st);
+    if (cudaEventSynchronize(e1) != cudaSuccess) {
+      rc = set_error("gemm autotune: event synchronize failed");
+      break;
+    }
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, e0, e1);
+    if (ms < best_ms) {
+      best_ms = ms;
+      best = cand[c];
+    }
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (rc) return rc;
+  {
+    std::lock_guard<std::mutex> lk(g_tune_mu);
+    g_tune[key] = best;
+  }
+  if (getenv("GCU_DEBUG"))
+    fprintf(stderr, "gcu: gemm m=%d k=%d n0=%d jobs=%d -> tile %dx%d split %d (%.2f us)\n", m, k,
+            key.n[0], njobs, 128 * best.mb, best.bn, best.splits, best_ms * 1000.0f / 3.0f);
+  *out = best;
+  return 0;
+}
+
+}  // namespace
+
 // Multi-job entry: jobs share A (src); job j has its own weights and output.
 int launch_gemm_tc_jobs(const int8_t *src, long sstr, const float *ssc, int m, int k,
                         const GemmArgs *jobs, int njobs, cudaStream_t st, int force_bn,
@@ -533,37 +663,39 @@ int launch_gemm_tc_jobs(const int8_t *src, long sstr, const float *ssc, int m, i
   for (int j = 0; j < njobs; ++j)
     if ((uintptr_t)jobs[j].mat % 16 || jobs[j].mstr % 16)
       return set_error("gemm: weight rows must be 16-byte aligned (stride %ld)", jobs[j].mstr);
-  auto ntiles_n = [&](int bn_) {
-    int t = 0;
-    for (int j = 0; j < njobs; ++j) t += (jobs[j].n + bn_ - 1) / bn_;
-    return t;
-  };
   const int kb_total = (k + BK - 1) / BK;
-  int bn = 0, mb = 0;
+  Plan pl;
   if (force_bn > 0) {
-    bn = force_bn;
-    mb = force_mb > 0 ? force_mb : 1;
+    pl.bn = force_bn;
+    pl.mb = force_mb > 0 ? force_mb : 1;
     bool known = false;
-    for (const Shape &sh : kShapes) known |= (sh.bn == bn && sh.mb == mb);
-    if (!known) return set_error("gemm: no %d x %d tile variant", 128 * mb, bn);
-  } else {
-    double best = 1e30;
-    for (const Shape &sh : kShapes) {
-      const int tiles_ = (m + 128 * sh.mb - 1) / (128 * sh.mb) * ntiles_n(sh.bn);
-      const int sp = split_for(tiles_, kb_total, sms);
-      const double t = estimate_us(m, ntiles_n(sh.bn), kb_total, sh.bn, sh.mb, sp, sms);
-      if (t < best - 1e-9) {
-        best = t;
-        bn = sh.bn;
-        mb = sh.mb;
-      }
-    }
+    for (const Shape &sh : kShapes) known |= (sh.bn == pl.bn && sh.mb == pl.mb);
+    if (!known) return set_error("gemm: no %d x %d tile variant", 128 * pl.mb, pl.bn);
+    const int tiles = (m + 128 * pl.mb - 1) / (128 * pl.mb) * ntiles_n(jobs, njobs, pl.bn);
+    pl.splits = force_split > 0 ? force_split : split_for(tiles, kb_total, sms);
+    return run_plan(pl, src, sstr, ssc, m, k, jobs, njobs, st, ext);
   }
+  pl = model_plan(m, k, jobs, njobs, sms);
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  GCU_CUDA(cudaStreamIsCapturing(st, &cap));
+  if (!ext && autotune_enabled() && cap == cudaStreamCaptureStatusNone &&
+      tuned_plan(&pl, src, sstr, ssc, m, k, jobs, njobs, st, sms))
+    return 1;
+  if (force_split > 0) pl.splits = force_split;
+  return run_plan(pl, src, sstr, ssc, m, k, jobs, njobs, st, ext);
+}
+
+namespace {
+
+int run_plan(const Plan &pl, const int8_t *src, long sstr, const float *ssc, int m, int k,
+             const GemmArgs *jobs, int njobs, cudaStream_t st, const ExtWorkspace *ext) {
+  const int bn = pl.bn, mb = pl.mb;
+  const int kb_total = (k + BK - 1) / BK;
   const int tile_m = BM * mb;
   const int tiles_m = (m + tile_m - 1) / tile_m;
-  const int tiles_n = ntiles_n(bn);
+  const int tiles_n = ntiles_n(jobs, njobs, bn);
   const int tiles = tiles_m * tiles_n;
-  int splits = force_split > 0 ? force_split : split_for(tiles, kb_total, sms);
+  int splits = pl.splits < 1 ? 1 : pl.splits;
   if (splits > kb_total) splits = kb_total;
   const int kb_per = (kb_total + splits - 1) / splits;
   splits = (kb_total + kb_per - 1) / kb_per;
@@ -623,6 +755,8 @@ int launch_gemm_tc_jobs(const int8_t *src, long sstr, const float *ssc, int m, i
   if (bn == 128) return launch_cfg<128, 1>(p, st);
   return launch_cfg<64, 1>(p, st);
 }
+
+}  // namespace
 
 int launch_gemm_tc(const GemmArgs &a, cudaStream_t st, int force_bn, int force_split,
                    int force_mb) {

@@ -61,6 +61,8 @@ SIGNATURES = {
 }
 # exported but not part of the public header (benchmark sweeps)
 EXTRA = {
+    "gcu_dev_gemm_int8_multi_tuned": (_int, [ctypes.POINTER(GemvJob), _int, _vp, _int, _vp, _int, _int, _int,
+                                             _int, _int, _vp]),
     "gcu_dev_gemm_int8_tuned": (_int, [_vp, _int, _vp, _int, _vp, _vp, _int, _vp, _int, _int, _int,
                                        _int, _int, _int, _vp]),
 }
@@ -234,6 +236,15 @@ def dev_gemm_int8_tuned(dst, mat, matsc, src, ssc, m, n, k, bn, split, mb=1, str
     _check(lib().gcu_dev_gemm_int8_tuned(dst.data_ptr(), 0, mat.data_ptr(), 0, matsc.data_ptr(),
                                          src.data_ptr(), 0, ssc.data_ptr(), m, n, k, bn, split, mb,
                                          _stream(stream)), "dev_gemm_int8_tuned")
+
+
+def dev_gemm_int8_multi_tuned(jobs_t, src, ssc, m, k, bn, split, mb=1, stream=None):
+    """Multi-job GEMM with a forced tile shape and K split (benchmark sweeps)."""
+    jobs = (GemvJob * len(jobs_t))()
+    for j, (w, s, o) in enumerate(jobs_t):
+        jobs[j] = GemvJob(w.data_ptr(), s.data_ptr(), o.data_ptr(), w.shape[0])
+    _check(lib().gcu_dev_gemm_int8_multi_tuned(jobs, len(jobs_t), src.data_ptr(), 0, ssc.data_ptr(), m, k, bn,
+                                               split, mb, _stream(stream)), "dev_gemm_int8_multi_tuned")
 
 
 def comm_unique_id() -> bytes:
