@@ -139,8 +139,9 @@ class Prefill:
     """1B-shaped W8A8 prefill, M tokens, all layers."""
     name = "prefill1b"
 
-    def __init__(self, m=512, cfg="1b", seed=0):
+    def __init__(self, m=512, cfg="1b", seed=0, fused=False):
         import synth
+        self.fused = fused
         self.cfg = synth.CONFIGS[cfg]
         self.m = m
         self.groups = synth.layer_groups(self.cfg)
@@ -151,7 +152,9 @@ class Prefill:
     def config(self):
         return {"workload": "prefill1b (configs[1]): Gemma-3-1B-shaped W8A8 prefill GEMM set",
                 "tokens_m": self.m, "layers": self.layers, "d_model": self.cfg["dim"], "ffn": self.cfg["ffn"],
-                "calls_per_layer": "quantize_acts x4 + GEMM {QKV fused, O, up+gate fused, down}",
+                "calls_per_layer": ("4 x quantize_acts->GEMM pairs, each one launch" if self.fused else
+                                    "quantize_acts x4 + GEMM {QKV, O, up+gate, down}") +
+                                   " (Q/K/V and up/gate as multi-weight launches)",
                 "inputs": "1% outlier channels x20; per-layer weights+activations ~1.3 GB > L2 (no flush)"}
 
     def build(self, device):
@@ -176,7 +179,9 @@ class Prefill:
         self.out = [[torch.empty((m, n), dtype=torch.float32, device=device) for _, n in jobs]
                     for _, jobs in self.groups]
 
-    kinds = ("quant", "gemm")
+    @property
+    def kinds(self):
+        return ("qgemm",) if self.fused else ("quant", "gemm")
 
     def step(self, gcu, stream=None, want=None):
         """Enqueue one step.  `want(kind, bytes, ops)` filters the launches
@@ -185,6 +190,14 @@ class Prefill:
         for layer in self.L:
             for gi, g in enumerate(layer):
                 k = g["k"]
+                if self.fused:
+                    nsum = sum(w.shape[0] for w, _ in g["w"])
+                    qb = 5 * m * k + 4 * m
+                    gb = nsum * k + 4 * nsum + m * k + 4 * m + 4 * m * nsum
+                    if want is None or want("qgemm", qb + gb, 2 * m * nsum * k):
+                        gcu.dev_quantize_gemm_int8_multi([(w, sc, o) for (w, sc), o in zip(g["w"], self.out[gi])],
+                                                         g["q"], g["s"], g["x"], m, k, stream=stream)
+                    continue
                 if want is None or want("quant", 5 * m * k + 4 * m, 0):
                     gcu.dev_quantize_acts(g["q"], g["s"], g["x"], m, k, stream=stream)
                 jobs = [(w, sc, o) for (w, sc), o in zip(g["w"], self.out[gi])]
@@ -198,6 +211,7 @@ class Prefill:
                 else:
                     gcu.dev_gemm_int8_multi(jobs, g["q"], g["s"], m, k, stream=stream)
 
+    # the quantize kernel and the GEMM are two launches either way at m > 8
     launches_per_step = property(lambda self: self.layers * 2 * len(self.groups))
 
     # ---- end to end through the host-pointer ABI --------------------------
@@ -280,8 +294,9 @@ class Decode:
     """Gemma-3-270m decode, batch 1, plus the lm_head."""
     name = "decode270m"
 
-    def __init__(self, cfg="270m", seed=0):
+    def __init__(self, cfg="270m", seed=0, fused=True):
         import synth
+        self.fused = fused
         self.cfg = synth.CONFIGS[cfg]
         self.groups = synth.layer_groups(self.cfg)
         self.layers = self.cfg["layers"]
@@ -292,7 +307,9 @@ class Decode:
     def config(self):
         return {"workload": "decode270m (configs[0]): Gemma-3-270m W8A8 decode, batch 1, 18 layers + lm_head",
                 "vocab": self.cfg["vocab"], "d_model": self.cfg["dim"],
-                "inputs": "271 MB of weights per token > L2 (no flush)"}
+                "inputs": "271 MB of weights per token > L2 (no flush)",
+                "calls": "quantize_act->gemv pairs fused into one launch each" if self.fused else
+                         "quantize_act and gemv_int8(_multi) as separate launches"}
 
     def build(self, device):
         import torch
@@ -314,9 +331,26 @@ class Decode:
                      "w": synth.weight_torch(self.cfg["vocab"], d, gen, device),
                      "o": torch.empty(self.cfg["vocab"], dtype=torch.float32, device=device)}
 
-    kinds = ("quant", "gemv")
+    @property
+    def kinds(self):
+        return ("qgemv",) if self.fused else ("quant", "gemv")
 
     def step(self, gcu, stream=None, want=None):
+        if self.fused:
+            for layer in self.L:
+                for g in layer:
+                    k = g["k"]
+                    nsum = sum(w.shape[0] for w, _ in g["w"])
+                    if want is None or want("qgemv", nsum * (k + 8) + 6 * k + 8, 2 * nsum * k):
+                        gcu.dev_quantize_gemm_int8_multi([(w, sc, o) for (w, sc), o in zip(g["w"], g["o"])],
+                                                         g["q"], g["s"], g["x"], 1, k, stream=stream)
+            h = self.head
+            d = self.cfg["dim"]
+            n = self.cfg["vocab"]
+            if want is None or want("qgemv", n * (d + 8) + 6 * d + 8, 2 * n * d):
+                gcu.dev_quantize_gemm_int8_multi([(h["w"][0], h["w"][1], h["o"])], h["q"], h["s"], h["x"], 1, d,
+                                                 stream=stream)
+            return
         for layer in self.L:
             for g in layer:
                 k = g["k"]
@@ -334,7 +368,7 @@ class Decode:
         if want is None or want("gemv", n * (d + 8) + d + 4, 2 * n * d):
             gcu.dev_gemv_int8(h["o"], h["w"][0], h["w"][1], h["q"], h["s"], n, d, stream=stream)
 
-    launches_per_step = property(lambda self: self.layers * 2 * len(self.groups) + 2)
+    launches_per_step = property(lambda self: (self.layers * len(self.groups) + 1) * (1 if self.fused else 2))
 
 
 class LmHead:
@@ -377,6 +411,7 @@ class LmHead:
                                        self.k, stream=stream)
 
     launches_per_step = property(lambda self: 2)
+    fused = False
 
 
 # ---------------------------------------------------------------------------
@@ -391,9 +426,9 @@ def run_ours(args):
     gcu.init(local)
     peaks = load_peaks()
     if args.workload == "prefill1b":
-        wl = Prefill(seed=rank)
+        wl = Prefill(seed=rank, fused=args.fused)
     elif args.workload == "decode270m":
-        wl = Decode(seed=rank)
+        wl = Decode(seed=rank, fused=not args.unfused)
     else:
         wl = LmHead(world, rank)
         if world > 1:
@@ -641,6 +676,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="prefill1b", choices=["prefill1b", "decode270m", "lmhead4b"])
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--unfused", action="store_true",
+                    help="decode: quantize and GEMV as separate launches (the reference's call split)")
+    ap.add_argument("--fused", action="store_true",
+                    help="prefill: issue each quantize+GEMM pair through gcu_dev_quantize_gemm_int8_multi")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()

@@ -649,6 +649,58 @@ GCU_EXPORT int gcu_dev_gemm_int8_multi(const gcu_gemv_job *jobs, int njobs, cons
   return launch_gemm_tc_jobs(src, sstr, ssc, m, k, a, njobs, as_stream(stream), 0, 0);
 }
 
+GCU_EXPORT int gcu_dev_quantize_gemm_int8_multi(const gcu_gemv_job *jobs, int njobs, int8_t *q,
+                                                float *s, const float *x, int xstr, int m, int k,
+                                                void *stream) {
+  if (m <= 0) return 0;
+  if (k <= 0 || !q || !s || !x) return set_error("quantize_gemm_int8: bad arguments");
+  if (xstr == 0) xstr = k;
+  if (njobs <= 0) return launch_quantize_rows(q, s, x, xstr, m, k, as_stream(stream));
+  cudaStream_t st = as_stream(stream);
+  if (m <= 8) {
+    if (njobs > GCU_MAX_JOBS) return set_error("quantize_gemm_int8: at most %d jobs", GCU_MAX_JOBS);
+    GemvJobs J{};
+    int rows = 0;
+    for (int j = 0; j < njobs; ++j) {
+      J.w[j] = (const int8_t *)jobs[j].w;
+      J.ws[j] = jobs[j].sc;
+      J.y[j] = jobs[j].dst;
+      rows += jobs[j].m;
+      J.row_end[j] = rows;
+    }
+    J.njobs = njobs;
+    if (m == 1 || njobs == 1)
+      return launch_quantize_gemv(J, x, xstr, q, s, m, njobs == 1 ? jobs[0].m : 0, k, st);
+    // several rows and several jobs: each job's output has its own row stride
+    if (launch_quantize_rows(q, s, x, xstr, m, k, st)) return 1;
+    for (int j = 0; j < njobs; ++j) {
+      GemvJobs one{};
+      one.w[0] = J.w[j];
+      one.ws[0] = J.ws[j];
+      one.y[0] = J.y[j];
+      one.row_end[0] = jobs[j].m;
+      one.njobs = 1;
+      if (launch_gemv(one, q, k, s, m, jobs[j].m, k, st)) return 1;
+    }
+    return 0;
+  }
+  if (njobs > 4) return set_error("quantize_gemm_int8: at most 4 jobs on the tensor-core path");
+  GemmArgs a[4];
+  for (int j = 0; j < njobs; ++j)
+    a[j] = GemmArgs{jobs[j].dst, jobs[j].m, (const int8_t *)jobs[j].w, k, jobs[j].sc,
+                    q, k, s, m, jobs[j].m, k};
+  if (k % 16 || (uintptr_t)q % 16)
+    return set_error("quantize_gemm_int8: m > 8 needs k %% 16 == 0 and a 16-byte aligned q "
+                     "(the tensor-core kernel reads q with TMA); got k = %d", k);
+  // Quantize kernel then tensor-core GEMM: the GEMM's prologue overlaps the
+  // quantize kernel through programmatic dependent launch.  (Quantizing
+  // inside the GEMM, one warp per row behind a grid barrier, measured slower
+  // on B200 for the prefill shapes: a 148-CTA grid cannot keep enough loads
+  // in flight for 512 rows.)
+  if (launch_quantize_rows(q, s, x, xstr, m, k, st)) return 1;
+  return launch_gemm_tc_jobs(q, k, s, m, k, a, njobs, st, 0, 0);
+}
+
 // Tuning hook (not in gcu.h): the multi-job GEMM with a forced tile shape
 // ((128*mb) x bn) and K split.  Used by the benchmark's sweeps.
 GCU_EXPORT int gcu_dev_gemm_int8_multi_tuned(const gcu_gemv_job *jobs, int njobs, const int8_t *src,

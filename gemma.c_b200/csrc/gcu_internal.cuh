@@ -83,6 +83,12 @@ int launch_gemv(const GemvJobs &jobs, const int8_t *x, long xstride,
                 const float *xs, int mb, long ystride, int k,
                 cudaStream_t st);
 
+// quantize_acts + GEMV in one launch (mb <= 8 rows of fp32 xf); writes the
+// codes (qout, dense [mb][k]) and scales (sout) as quantize_acts would.
+int launch_quantize_gemv(const GemvJobs &jobs, const float *xf, long xfstride,
+                         int8_t *qout, float *sout, int mb, long ystride, int k,
+                         cudaStream_t st);
+
 struct GemmArgs {
   float *dst;
   long dstr;
@@ -233,6 +239,7 @@ __device__ __forceinline__ void bulk_wait() {
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;"
@@ -333,6 +340,36 @@ __host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
 
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ---- quantize arithmetic of gemma.c:2586-2650 under -ffast-math ------------
+// scale = amax * (1/127), inv = 127 / amax (IEEE division); 1, 1 for amax 0;
+// q = trunc(x*inv + copysign(0.5, x*inv)) clamped to [-127, 127].  Explicit
+// round-to-nearest intrinsics keep nvcc from contracting into FMAs.
+__device__ __forceinline__ int quant_one(float x, float inv) {
+  const float t = __fmul_rn(x, inv);
+  const float s = __fadd_rn(t, copysignf(0.5f, t));
+  int q = __float2int_rz(s);
+  q = q > 127 ? 127 : q;
+  q = q < -127 ? -127 : q;
+  return q;
+}
+__device__ __forceinline__ void quant_scale(float amax, float &scale, float &inv) {
+  if (amax > 0.0f) {
+    scale = __fmul_rn(amax, 1.0f / 127.0f);
+    inv = __fdiv_rn(127.0f, amax);
+  } else {
+    scale = 1.0f;
+    inv = 1.0f;
+  }
+}
+__device__ __forceinline__ float absmax4(const float4 &v, float m) {
+  return fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+}
+// four quantized values packed little-endian into one 32-bit word
+__device__ __forceinline__ int quant_pack4(const float4 &v, float inv) {
+  return (quant_one(v.x, inv) & 0xff) | ((quant_one(v.y, inv) & 0xff) << 8) |
+         ((quant_one(v.z, inv) & 0xff) << 16) | ((quant_one(v.w, inv) & 0xff) << 24);
 }
 
 // streaming 16-byte global load that does not allocate in L1

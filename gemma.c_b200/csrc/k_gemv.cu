@@ -45,27 +45,82 @@ __device__ __forceinline__ void job_of(const GemvJobs &jobs, int row, int &j, in
   local = row - (j > 0 ? jobs.row_end[j - 1] : 0);
 }
 
+// Activation source of the GEMV: already-quantized int8 rows with their
+// scales, or (fused) fp32 rows that every CTA quantizes itself while staging
+// them -- gemma.c's quantize_act + gemv_int8 pair in one launch.  CTA 0 also
+// writes the codes and scales out, as quantize_act would.
+struct GemvX {
+  const int8_t *x;   // int8 rows (not fused)
+  long xstride;      // elements between rows (int8 or fp32)
+  const float *xs;   // their scales (not fused)
+  const float *xf;   // fp32 rows (fused)
+  int8_t *qout;      // fused: codes out [mb][k] dense (may be null)
+  float *sout;       // fused: scales out [mb] (may be null)
+};
+
+__device__ __forceinline__ float block_max256(float v, float *red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = red[0];
+#pragma unroll
+  for (int w = 1; w < kThreads / 32; ++w) r = fmaxf(r, red[w]);
+  __syncthreads();
+  return r;
+}
+
 // Vector kernel: k % 16 == 0, every weight row and x row 16-byte aligned.
-template <int MB, int LPR, int R, int U>
-__global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs,
-                                                       const int8_t *__restrict__ x,
-                                                       long xstride,
-                                                       const float *__restrict__ xs,
-                                                       int mb, long ystride, int k,
-                                                       int total_rows) {
+template <int MB, int LPR, int R, int U, bool FQ>
+__global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, const GemvX X, int mb,
+                                                       long ystride, int k, int total_rows) {
   extern __shared__ int4 xsm[];  // [MB][C] 16-byte chunks of x
+  __shared__ float red[kThreads / 32];
+  __shared__ float s_scale[MB];
   const int C = k >> 4;
   ptx::griddep_wait();
-  for (int i = threadIdx.x; i < MB * C; i += kThreads) {
-    const int b = i / C, c = i - b * C;
-    int4 v = make_int4(0, 0, 0, 0);
-    if (b < mb) v = *reinterpret_cast<const int4 *>(x + (size_t)b * xstride + (size_t)c * 16);
-    xsm[i] = v;
-  }
   float xsc[MB];
+  if (FQ) {
+    for (int b = 0; b < MB; ++b) {
+      if (b >= mb) {  // uniform: padding rows are zero
+        for (int i = threadIdx.x; i < C; i += kThreads) xsm[b * C + i] = make_int4(0, 0, 0, 0);
+        continue;
+      }
+      const float4 *xr = reinterpret_cast<const float4 *>(X.xf + (size_t)b * X.xstride);
+      float amax = 0.0f;
+      for (int i = threadIdx.x; i < 4 * C; i += kThreads) amax = ptx::absmax4(__ldg(xr + i), amax);
+      amax = block_max256(amax, red);
+      float scale, inv;
+      ptx::quant_scale(amax, scale, inv);
+      for (int i = threadIdx.x; i < C; i += kThreads) {
+        int4 v;
+        v.x = ptx::quant_pack4(__ldg(xr + 4 * i), inv);
+        v.y = ptx::quant_pack4(__ldg(xr + 4 * i + 1), inv);
+        v.z = ptx::quant_pack4(__ldg(xr + 4 * i + 2), inv);
+        v.w = ptx::quant_pack4(__ldg(xr + 4 * i + 3), inv);
+        xsm[b * C + i] = v;
+        if (blockIdx.x == 0 && X.qout)
+          *reinterpret_cast<int4 *>(X.qout + (size_t)b * k + (size_t)i * 16) = v;
+      }
+      if (threadIdx.x == 0) {
+        s_scale[b] = scale;
+        if (blockIdx.x == 0 && X.sout) X.sout[b] = scale;
+      }
+    }
+    __syncthreads();
 #pragma unroll
-  for (int b = 0; b < MB; ++b) xsc[b] = b < mb ? xs[b] : 0.0f;
-  __syncthreads();
+    for (int b = 0; b < MB; ++b) xsc[b] = b < mb ? s_scale[b] : 0.0f;
+  } else {
+    for (int i = threadIdx.x; i < MB * C; i += kThreads) {
+      const int b = i / C, c = i - b * C;
+      int4 v = make_int4(0, 0, 0, 0);
+      if (b < mb) v = *reinterpret_cast<const int4 *>(X.x + (size_t)b * X.xstride + (size_t)c * 16);
+      xsm[i] = v;
+    }
+#pragma unroll
+    for (int b = 0; b < MB; ++b) xsc[b] = b < mb ? X.xs[b] : 0.0f;
+    __syncthreads();
+  }
 
   const int lane = threadIdx.x & 31;
   const int slot = lane / LPR, sub = lane % LPR;
@@ -170,12 +225,12 @@ __global__ void __launch_bounds__(kThreads) k_gemv_any(const GemvJobs jobs,
   ptx::griddep_launch();
 }
 
-template <int MB, int LPR>
-int launch_v16(const GemvJobs &jobs, const int8_t *x, long xstride, const float *xs, int mb,
-               long ystride, int k, int total_rows, cudaStream_t st) {
+template <int MB, int LPR, bool FQ>
+int launch_v16(const GemvJobs &jobs, const GemvX &X, int mb, long ystride, int k, int total_rows,
+               cudaStream_t st) {
   constexpr int R = 2;
   constexpr int U = (MB >= 4) ? 2 : 4;
-  auto kern = k_gemv_v16<MB, LPR, R, U>;
+  auto kern = k_gemv_v16<MB, LPR, R, U, FQ>;
   const size_t smem = (size_t)MB * k;
   static std::once_flag once;
   static int regs = 0;
@@ -199,18 +254,27 @@ int launch_v16(const GemvJobs &jobs, const int8_t *x, long xstride, const float 
   long need = ((long)total_rows + rows_per_block - 1) / rows_per_block;
   long cap = (long)num_sms() * blocks_per_sm;
   const int grid = (int)(need < cap ? need : cap);
-  GCU_CUDA(launch_k(kern, grid, kThreads, smem, st, jobs, x, xstride, xs, mb, ystride, k, total_rows));
+  GCU_CUDA(launch_k(kern, grid, kThreads, smem, st, jobs, X, mb, ystride, k, total_rows));
   GCU_CUDA(cudaGetLastError());
   return 0;
 }
 
-template <int MB>
-int launch_mb(const GemvJobs &jobs, const int8_t *x, long xstride, const float *xs, int mb,
-              long ystride, int k, int total_rows, cudaStream_t st) {
+template <int MB, bool FQ>
+int launch_mb(const GemvJobs &jobs, const GemvX &X, int mb, long ystride, int k, int total_rows,
+              cudaStream_t st) {
   const int C = k / 16;
-  if (C >= 128) return launch_v16<MB, 32>(jobs, x, xstride, xs, mb, ystride, k, total_rows, st);
-  if (C >= 64) return launch_v16<MB, 16>(jobs, x, xstride, xs, mb, ystride, k, total_rows, st);
-  return launch_v16<MB, 8>(jobs, x, xstride, xs, mb, ystride, k, total_rows, st);
+  if (C >= 128) return launch_v16<MB, 32, FQ>(jobs, X, mb, ystride, k, total_rows, st);
+  if (C >= 64) return launch_v16<MB, 16, FQ>(jobs, X, mb, ystride, k, total_rows, st);
+  return launch_v16<MB, 8, FQ>(jobs, X, mb, ystride, k, total_rows, st);
+}
+
+template <bool FQ>
+int launch_vec(const GemvJobs &jobs, const GemvX &X, int mb, long ystride, int k, int total_rows,
+               cudaStream_t st) {
+  if (mb == 1) return launch_mb<1, FQ>(jobs, X, mb, ystride, k, total_rows, st);
+  if (mb == 2) return launch_mb<2, FQ>(jobs, X, mb, ystride, k, total_rows, st);
+  if (mb <= 4) return launch_mb<4, FQ>(jobs, X, mb, ystride, k, total_rows, st);
+  return launch_mb<8, FQ>(jobs, X, mb, ystride, k, total_rows, st);
 }
 
 }  // namespace
@@ -227,10 +291,8 @@ int launch_gemv(const GemvJobs &jobs, const int8_t *x, long xstride, const float
              (size_t)mb_pad * k <= 200 * 1024;
   for (int j = 0; j < jobs.njobs && vec; ++j) vec = ((uintptr_t)jobs.w[j] % 16 == 0);
   if (vec) {
-    if (mb == 1) return launch_mb<1>(jobs, x, xstride, xs, mb, ystride, k, total_rows, st);
-    if (mb == 2) return launch_mb<2>(jobs, x, xstride, xs, mb, ystride, k, total_rows, st);
-    if (mb <= 4) return launch_mb<4>(jobs, x, xstride, xs, mb, ystride, k, total_rows, st);
-    return launch_mb<8>(jobs, x, xstride, xs, mb, ystride, k, total_rows, st);
+    GemvX X{x, xstride, xs, nullptr, nullptr, nullptr};
+    return launch_vec<false>(jobs, X, mb, ystride, k, total_rows, st);
   }
   long need = ((long)total_rows + 7) / 8;
   long cap = (long)num_sms() * 8;
@@ -238,6 +300,27 @@ int launch_gemv(const GemvJobs &jobs, const int8_t *x, long xstride, const float
   GCU_CUDA(launch_k(k_gemv_any, grid, kThreads, 0, st, jobs, x, xstride, xs, mb, ystride, k, total_rows));
   GCU_CUDA(cudaGetLastError());
   return 0;
+}
+
+// Fused quantize_acts + GEMV: xf holds mb fp32 rows (row stride xfstride
+// floats); the codes and scales are also written to qout / sout.
+int launch_quantize_gemv(const GemvJobs &jobs, const float *xf, long xfstride, int8_t *qout,
+                         float *sout, int mb, long ystride, int k, cudaStream_t st) {
+  if (jobs.njobs <= 0 || mb <= 0) return 0;
+  if (mb > 8) return set_error("quantize+gemv: at most 8 activation rows (got %d)", mb);
+  const int total_rows = jobs.row_end[jobs.njobs - 1];
+  const int mb_pad = mb == 1 ? 1 : mb == 2 ? 2 : mb <= 4 ? 4 : 8;
+  bool vec = (k % 16 == 0) && ((uintptr_t)xf % 16 == 0) && (mb == 1 || xfstride % 4 == 0) &&
+             ((uintptr_t)qout % 16 == 0) && (size_t)mb_pad * k <= 200 * 1024;
+  for (int j = 0; j < jobs.njobs && vec; ++j) vec = ((uintptr_t)jobs.w[j] % 16 == 0);
+  if (!vec) {
+    // unaligned or odd k: the two kernels back to back
+    if (launch_quantize_rows(qout, sout, xf, xfstride, mb, k, st)) return 1;
+    return launch_gemv(jobs, qout, k, sout, mb, ystride, k, st);
+  }
+  if (total_rows <= 0) return launch_quantize_rows(qout, sout, xf, xfstride, mb, k, st);
+  GemvX X{nullptr, xfstride, nullptr, xf, qout, sout};
+  return launch_vec<true>(jobs, X, mb, ystride, k, total_rows, st);
 }
 
 }  // namespace gcu

@@ -17,14 +17,7 @@
 namespace gcu {
 namespace {
 
-__device__ __forceinline__ int quant_one(float x, float inv) {
-  const float t = __fmul_rn(x, inv);
-  const float s = __fadd_rn(t, copysignf(0.5f, t));
-  int q = __float2int_rz(s);
-  q = q > 127 ? 127 : q;
-  q = q < -127 ? -127 : q;
-  return q;
-}
+using ptx::quant_one;
 
 __device__ __forceinline__ float block_max(float v, float *red) {
 #pragma unroll
@@ -42,13 +35,7 @@ __device__ __forceinline__ float block_max(float v, float *red) {
 }
 
 __device__ __forceinline__ void scale_of(float amax, float &scale, float &inv) {
-  if (amax > 0.0f) {
-    scale = __fmul_rn(amax, 1.0f / 127.0f);
-    inv = __fdiv_rn(127.0f, amax);
-  } else {
-    scale = 1.0f;
-    inv = 1.0f;
-  }
+  ptx::quant_scale(amax, scale, inv);
 }
 
 // Vector path: src rows 16-byte aligned, n % 4 == 0.  VPT float4 per thread.

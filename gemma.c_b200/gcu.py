@@ -54,6 +54,8 @@ SIGNATURES = {
     "gcu_dev_gemm_int8": (_int, [_vp, _int, _vp, _int, _vp, _vp, _int, _vp, _int, _int, _int, _vp]),
     "gcu_dev_gemm_int8_multi": (_int, [ctypes.POINTER(GemvJob), _int, _vp, _int, _vp, _int, _int, _vp]),
     "gcu_dev_gemm_int8_noalloc": (_int, [_vp, _int, _vp, _int, _vp, _vp, _int, _vp, _int, _int, _int, _vp]),
+    "gcu_dev_quantize_gemm_int8_multi": (_int, [ctypes.POINTER(GemvJob), _int, _vp, _vp, _vp, _int, _int, _int,
+                                                _vp]),
     "gcu_comm_unique_id": (_int, [ctypes.c_char_p]),
     "gcu_comm_init": (_int, [_int, _int, ctypes.c_char_p]),
     "gcu_comm_destroy": (_int, []),
@@ -213,6 +215,16 @@ def dev_gemm_int8(dst, mat, matsc, src, ssc, m, n, k, dstr=0, mstr=0, sstr=0, st
     _check(lib().gcu_dev_gemm_int8(dst.data_ptr(), dstr, mat.data_ptr(), mstr, matsc.data_ptr(),
                                    src.data_ptr(), sstr, ssc.data_ptr(), m, n, k, _stream(stream)),
            "dev_gemm_int8")
+
+
+def dev_quantize_gemm_int8_multi(jobs_t, q, s, x, m, k, xstr=0, stream=None):
+    """quantize_acts(x) -> (q, s) and every job's gemm_int8 on it, in one launch.
+    jobs_t: list of (w, sc, dst) device tensors."""
+    jobs = (GemvJob * len(jobs_t))()
+    for j, (w, sc, o) in enumerate(jobs_t):
+        jobs[j] = GemvJob(w.data_ptr(), sc.data_ptr(), o.data_ptr(), w.shape[0])
+    _check(lib().gcu_dev_quantize_gemm_int8_multi(jobs, len(jobs_t), q.data_ptr(), s.data_ptr(), x.data_ptr(),
+                                                  xstr, m, k, _stream(stream)), "dev_quantize_gemm_int8_multi")
 
 
 def dev_gemm_int8_noalloc(dst, mat, matsc, src, ssc, m, n, k, dstr=0, mstr=0, sstr=0, stream=None):

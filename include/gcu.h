@@ -144,6 +144,19 @@ int gcu_dev_gemm_int8_multi(const gcu_gemv_job *jobs, int njobs,
                             const int8_t *src, int sstr, const float *ssc,
                             int m, int k, void *stream);
 
+/* quantize_acts followed by gemm_int8 / gemv_int8_multi on its result, in one
+ * launch: gemma.c always calls them as a pair on the same activations
+ * (gemma.c:4768-4773, 4911-4915, 5034-5091, 5365-5372, 5389-5391).  x holds
+ * m fp32 rows (row stride xstr floats, 0 = k); the int8 codes go to q (dense
+ * [m][k]) and the scales to s, exactly as gcu_dev_quantize_acts writes them,
+ * and job j's output to its dst (m, rows_j) dense.  m <= 8: one launch, the
+ * streaming GEMV kernel quantizes x while staging it; m > 8 (k % 16 == 0):
+ * the quantize kernel and the tensor-core GEMM back to back (the GEMM's
+ * prologue overlaps the quantize kernel).  Same bits as separate calls. */
+int gcu_dev_quantize_gemm_int8_multi(const gcu_gemv_job *jobs, int njobs,
+                                     int8_t *q, float *s, const float *x,
+                                     int xstr, int m, int k, void *stream);
+
 /* ---- row-sharded entry points (NCCL over NVLink) ---------------------------
  * No counterpart in the reference, which is single-process (README.md:614).
  * Rank r of `world` owns weight rows [r*n/world, (r+1)*n/world) of an n-row

@@ -311,3 +311,40 @@ def test_error_reported_for_unsupported_device_call():
     y = torch.empty((2, 16), device="cuda")
     with pytest.raises(gcu.GcuError, match="dense weight rows"):
         gcu.dev_gemm_int8(y, w, sc, x, xs, 2, 16, 32, mstr=64)
+
+
+# ---------------------------------------------------------------- fused quantize + matmul
+
+@pytest.mark.parametrize("m,k,rows", [(1, 640, (1024, 256, 256)), (1, 2560, (262144,)), (4, 1152, (2048,)),
+                                      (3, 1152, (512, 256)), (300, 1152, (1024, 256, 256)),
+                                      (512, 1152, (6912, 6912)), (512, 6912, (1152,)), (1000, 2560, (640,)),
+                                      (6, 40, (48,)), (77, 4304, (100, 60))])
+def test_fused_quantize_gemm(m, k, rows):
+    x = synth.activations(9100 + m + k, m, k, outliers=True)
+    ws_np = [big_weight(9200 + i + k, n, k) for i, n in enumerate(rows)]
+    q = torch.full((m, k), 99, dtype=torch.int8, device="cuda")
+    s = torch.zeros(m, dtype=torch.float32, device="cuda")
+    outs = [torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda") for n in rows]
+    jobs = [(_dev(w), _dev(sc), o) for (w, sc), o in zip(ws_np, outs)]
+    xt = _dev(x)
+    for _ in range(2):  # the grid barrier and counters are reused by the second call
+        gcu.dev_quantize_gemm_int8_multi(jobs, q, s, xt, m, k)
+        torch.cuda.synchronize()
+    gcu.check_device()
+    xq, xs = O.quantize_acts(x)
+    assert np.array_equal(q.cpu().numpy(), xq)
+    assert_bits(s.cpu().numpy(), xs)
+    for (w, sc), o in zip(ws_np, outs):
+        assert_bits(o.cpu().numpy(), O.gemm_int8(w, sc, xq, xs))
+
+
+def test_fused_quantize_gemm_rejects_odd_k_on_tensor_cores():
+    m, k = 130, 40
+    x = torch.zeros((m, k), dtype=torch.float32, device="cuda")
+    q = torch.empty((m, k), dtype=torch.int8, device="cuda")
+    s = torch.empty(m, dtype=torch.float32, device="cuda")
+    w = torch.zeros((48, k), dtype=torch.int8, device="cuda")
+    sc = torch.ones(48, device="cuda")
+    o = torch.empty((m, 48), device="cuda")
+    with pytest.raises(gcu.GcuError, match="k % 16 == 0"):
+        gcu.dev_quantize_gemm_int8_multi([(w, sc, o)], q, s, x, m, k)
