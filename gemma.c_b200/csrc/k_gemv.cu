@@ -37,6 +37,43 @@ __device__ __forceinline__ float dequant(int acc, float xs, float ws) {
   return __fmul_rn(__int2float_rn(acc), __fmul_rn(xs, ws));
 }
 
+// Butterfly reduce-scatter of V per-lane partial sums over the LPR lanes of a
+// row group (lane bit o of `sub`): each step the upper lane keeps the upper
+// half of the values and the lower lane the lower half, each adding the half
+// its partner sends -- V/2 shuffles per step instead of V.  On return v[0..]
+// holds max(V/LPR, 1) complete sums with original indices idx, idx+1, ...;
+// when V < LPR the remaining steps are plain xor-adds (lanes then share sums).
+template <int V, int O>
+struct ReduceScatter {
+  static __device__ __forceinline__ void run(int *v, int sub, int &idx) {
+    constexpr int H = V / 2;
+    const bool up = (sub & O) != 0;
+#pragma unroll
+    for (int i = 0; i < H; ++i) {
+      const int send = up ? v[i] : v[i + H];
+      const int keep = up ? v[i + H] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, O);
+    }
+    if (up) idx += H;
+    ReduceScatter<H, O / 2>::run(v, sub, idx);
+  }
+};
+template <int O>
+struct ReduceScatter<1, O> {
+  static __device__ __forceinline__ void run(int *v, int sub, int &idx) {
+    v[0] += __shfl_xor_sync(0xffffffffu, v[0], O);
+    ReduceScatter<1, O / 2>::run(v, sub, idx);
+  }
+};
+template <int V>
+struct ReduceScatter<V, 0> {
+  static __device__ __forceinline__ void run(int *, int, int &) {}
+};
+template <>
+struct ReduceScatter<1, 0> {
+  static __device__ __forceinline__ void run(int *, int, int &) {}
+};
+
 __device__ __forceinline__ void job_of(const GemvJobs &jobs, int row, int &j, int &local) {
   j = 0;
 #pragma unroll
@@ -77,6 +114,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, cons
   extern __shared__ int4 xsm[];  // [MB][C] 16-byte chunks of x
   __shared__ float red[kThreads / 32];
   __shared__ float s_scale[MB];
+  __shared__ float s_xsc[MB];  // activation scales, indexed by reduced-sum slot
   const int C = k >> 4;
   ptx::griddep_wait();
   float xsc[MB];
@@ -121,6 +159,8 @@ __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, cons
     for (int b = 0; b < MB; ++b) xsc[b] = b < mb ? X.xs[b] : 0.0f;
     __syncthreads();
   }
+  if (threadIdx.x < MB) s_xsc[threadIdx.x] = xsc[threadIdx.x];
+  __syncthreads();
 
   const int lane = threadIdx.x & 31;
   const int slot = lane / LPR, sub = lane % LPR;
@@ -167,23 +207,25 @@ __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, cons
         }
       }
     }
+    // reduce the R*MB sums over the LPR lanes; slot index vi = r*MB + b
+    constexpr int V = R * MB;
+    constexpr int KEEP = V >= LPR ? V / LPR : 1;
+    int *v = &acc[0][0];
+    int idx = 0;
+    ReduceScatter<V, LPR / 2>::run(v, sub, idx);
+    // when V < LPR several lanes hold the same sum: the lowest one writes
+    const bool writer = V >= LPR || (sub & (LPR / V - 1)) == 0;
+    if (writer) {
 #pragma unroll
-    for (int o = LPR / 2; o > 0; o >>= 1)
-#pragma unroll
-      for (int r = 0; r < R; ++r)
-#pragma unroll
-        for (int b = 0; b < MB; ++b) acc[r][b] += __shfl_xor_sync(0xffffffffu, acc[r][b], o);
-
-    if (sub == 0) {
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        if (!valid[r]) continue;
-        int j, local;
-        job_of(jobs, base + slot * R + r, j, local);
-        const float ws = jobs.ws[j][local];
-#pragma unroll
-        for (int b = 0; b < MB; ++b)
-          if (b < mb) jobs.y[j][(size_t)b * ystride + local] = dequant(acc[r][b], xsc[b], ws);
+      for (int t = 0; t < KEEP; ++t) {
+        const int vi = idx + t;
+        const int r = vi / MB, b = vi - r * MB;
+        const int row = base + slot * R + r;
+        if (row < total_rows && b < mb) {
+          int j, local;
+          job_of(jobs, row, j, local);
+          jobs.y[j][(size_t)b * ystride + local] = dequant(v[t], s_xsc[b], jobs.ws[j][local]);
+        }
       }
     }
   }
@@ -263,7 +305,9 @@ template <int MB, bool FQ>
 int launch_mb(const GemvJobs &jobs, const GemvX &X, int mb, long ystride, int k, int total_rows,
               cudaStream_t st) {
   const int C = k / 16;
-  if (C >= 128) return launch_v16<MB, 32, FQ>(jobs, X, mb, ystride, k, total_rows, st);
+  // many activation rows: narrower lane groups keep the reduction short
+  if (MB >= 8) return launch_v16<MB, 8, FQ>(jobs, X, mb, ystride, k, total_rows, st);
+  if (C >= 128 && MB <= 2) return launch_v16<MB, 32, FQ>(jobs, X, mb, ystride, k, total_rows, st);
   if (C >= 64) return launch_v16<MB, 16, FQ>(jobs, X, mb, ystride, k, total_rows, st);
   return launch_v16<MB, 8, FQ>(jobs, X, mb, ystride, k, total_rows, st);
 }
