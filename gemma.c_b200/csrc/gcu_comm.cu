@@ -3,15 +3,21 @@
 // The reference is single-process (README.md:614); this is the one place the
 // library adds communication.  Every output row of gemm_int8 / gemv_int8 is
 // independent, so rank r computes rows [r*n/world, (r+1)*n/world) of the
-// output from its slice of the weight and an NCCL all-gather over NVLink
-// assembles the full output on every rank.  NCCL is opened with dlopen on
-// first use so the single-GPU entry points never depend on it.
+// output from its slice of the weight and the slices are all-gathered over
+// NVLink.  For the decode shapes (m <= 8) the all-gather is fused into the
+// GEMV: each rank stores its outputs straight into every rank's symmetric
+// buffer (CUDA IPC mappings exchanged at gcu_comm_init) and a bounded
+// flag barrier ends the launch (see PeerOut).  Larger m, or a node without
+// peer access, uses an NCCL all-gather.  NCCL is opened with dlopen on first
+// use so the single-GPU entry points never depend on it.
 #include "gcu_internal.cuh"
 
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <cstring>
 #include <mutex>
+#include <vector>
 
 #define GCU_EXPORT extern "C" __attribute__((visibility("default")))
 
@@ -54,12 +60,112 @@ int nccl_err(ncclResult_t r, const char *what) {
   return set_error("%s: %s", what, g_nccl.getErrorString ? g_nccl.getErrorString(r) : "nccl error");
 }
 
+// symmetric buffer: two halves of kSymHalf bytes, plus 4 flag words
+constexpr size_t kSymHalf = (size_t)8 << 20;
+
 struct Comm {
   ncclComm_t comm = nullptr;
   int rank = 0, world = 1;
+  bool p2p = false;
+  float *sym = nullptr;
+  int *flags = nullptr;
+  void *peer_sym[8] = {};
+  int *peer_flags[8] = {};
 };
 Comm g_comm;
 std::mutex g_comm_mu;
+
+// Allocate this rank's symmetric buffer, exchange IPC handles over NCCL and
+// map every peer's.  Any failure leaves p2p off on all ranks (they agree
+// through a second all-gather), and the NCCL all-gather path is used.
+int setup_p2p(Comm &c) {
+  if (c.world < 2 || c.world > 8) return 0;
+  cudaIpcMemHandle_t h[2];
+  int ok = 1;
+  if (cudaMalloc(&c.sym, 2 * kSymHalf) != cudaSuccess ||
+      cudaMalloc(&c.flags, 256) != cudaSuccess || cudaMemset(c.flags, 0, 256) != cudaSuccess ||
+      cudaIpcGetMemHandle(&h[0], c.sym) != cudaSuccess ||
+      cudaIpcGetMemHandle(&h[1], c.flags) != cudaSuccess)
+    ok = 0;
+  cudaGetLastError();
+  // all-gather {ok, handles} through NCCL
+  const size_t rec = sizeof(int) * 4 + sizeof(h);
+  unsigned char *dbuf = nullptr;
+  cudaStream_t st = nullptr;
+  std::vector<unsigned char> hbuf(rec * c.world);
+  memcpy(hbuf.data() + rec * c.rank, &ok, sizeof(int));
+  memcpy(hbuf.data() + rec * c.rank + 4 * sizeof(int), h, sizeof(h));
+  GCU_CUDA(cudaMalloc(&dbuf, rec * c.world));
+  GCU_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+  GCU_CUDA(cudaMemcpy(dbuf + rec * c.rank, hbuf.data() + rec * c.rank, rec, cudaMemcpyHostToDevice));
+  ncclResult_t r = g_nccl.allGather(dbuf + rec * c.rank, dbuf, rec, ncclUint8, c.comm, st);
+  if (r != ncclSuccess) {
+    cudaFree(dbuf);
+    cudaStreamDestroy(st);
+    return nccl_err(r, "ncclAllGather (ipc handles)");
+  }
+  GCU_CUDA(cudaStreamSynchronize(st));
+  GCU_CUDA(cudaMemcpy(hbuf.data(), dbuf, rec * c.world, cudaMemcpyDeviceToHost));
+  int all_ok = 1;
+  for (int p = 0; p < c.world; ++p) {
+    int okp;
+    memcpy(&okp, hbuf.data() + rec * p, sizeof(int));
+    all_ok &= okp;
+  }
+  for (int p = 0; p < c.world && all_ok; ++p) {
+    if (p == c.rank) {
+      c.peer_sym[p] = c.sym;
+      c.peer_flags[p] = c.flags;
+      continue;
+    }
+    cudaIpcMemHandle_t hp[2];
+    memcpy(hp, hbuf.data() + rec * p + 4 * sizeof(int), sizeof(hp));
+    void *a = nullptr, *b = nullptr;
+    if (cudaIpcOpenMemHandle(&a, hp[0], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess ||
+        cudaIpcOpenMemHandle(&b, hp[1], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      all_ok = 0;
+      break;
+    }
+    c.peer_sym[p] = a;
+    c.peer_flags[p] = static_cast<int *>(b);
+  }
+  // agree: p2p only if every rank mapped every peer
+  memcpy(hbuf.data() + rec * c.rank, &all_ok, sizeof(int));
+  GCU_CUDA(cudaMemcpy(dbuf + rec * c.rank, hbuf.data() + rec * c.rank, sizeof(int), cudaMemcpyHostToDevice));
+  r = g_nccl.allGather(dbuf + rec * c.rank, dbuf, rec, ncclUint8, c.comm, st);
+  if (r == ncclSuccess) {
+    GCU_CUDA(cudaStreamSynchronize(st));
+    GCU_CUDA(cudaMemcpy(hbuf.data(), dbuf, rec * c.world, cudaMemcpyDeviceToHost));
+    for (int p = 0; p < c.world; ++p) {
+      int okp;
+      memcpy(&okp, hbuf.data() + rec * p, sizeof(int));
+      all_ok &= okp;
+    }
+  } else {
+    all_ok = 0;
+  }
+  cudaFree(dbuf);
+  cudaStreamDestroy(st);
+  c.p2p = all_ok != 0;
+  return 0;
+}
+
+void teardown_p2p(Comm &c) {
+  for (int p = 0; p < c.world && p < 8; ++p) {
+    if (p != c.rank) {
+      if (c.peer_sym[p]) cudaIpcCloseMemHandle(c.peer_sym[p]);
+      if (c.peer_flags[p]) cudaIpcCloseMemHandle(c.peer_flags[p]);
+    }
+    c.peer_sym[p] = nullptr;
+    c.peer_flags[p] = nullptr;
+  }
+  if (c.sym) cudaFree(c.sym);
+  if (c.flags) cudaFree(c.flags);
+  c.sym = nullptr;
+  c.flags = nullptr;
+  c.p2p = false;
+}
 
 }  // namespace
 }  // namespace gcu
@@ -89,12 +195,20 @@ GCU_EXPORT int gcu_comm_init(int rank, int world, const unsigned char id[128]) {
   g_comm.comm = c;
   g_comm.rank = rank;
   g_comm.world = world;
+  // all ranks synchronise here anyway (the NCCL init above is collective)
+  if (setup_p2p(g_comm)) return 1;
   return 0;
 }
+
+// 1 if the row-shard entry point runs its all-gather as peer stores fused
+// into the GEMV (every rank mapped every other rank's buffer), else 0.
+GCU_EXPORT int gcu_comm_fused_allgather(void) { return g_comm.p2p ? 1 : 0; }
 
 GCU_EXPORT int gcu_comm_destroy(void) {
   std::lock_guard<std::mutex> lk(g_comm_mu);
   if (!g_comm.comm) return 0;
+  cudaDeviceSynchronize();
+  teardown_p2p(g_comm);
   ncclResult_t r = g_nccl.commDestroy(g_comm.comm);
   g_comm.comm = nullptr;
   if (r != ncclSuccess) return nccl_err(r, "ncclCommDestroy");
@@ -110,6 +224,31 @@ GCU_EXPORT int gcu_dev_gemm_int8_rowshard(float *dst, float *work, const int8_t 
   if (m <= 0) return 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int nl = n / world;
+  if (m <= 8 && g_comm.p2p && (size_t)m * n * sizeof(float) <= kSymHalf && nl % 4 == 0 &&
+      (uintptr_t)dst % 16 == 0) {
+    // GEMV with the all-gather fused into its epilogue (peer stores)
+    GemvJobs J{};
+    J.w[0] = mat_local;
+    J.ws[0] = matsc_local;
+    J.y[0] = g_comm.sym + (size_t)rank * nl;  // column offset of this rank's slice
+    J.row_end[0] = nl;
+    J.njobs = 1;
+    PeerOut po{};
+    for (int p = 0; p < world; ++p) {
+      po.delta[p] = (long long)((char *)g_comm.peer_sym[p] - (char *)g_comm.sym);
+      po.flag_peer[p] = g_comm.peer_flags[p];
+    }
+    po.flag_local = g_comm.flags;
+    po.sym = g_comm.sym;
+    po.half_elems = (long)(kSymHalf / sizeof(float));
+    po.dst = dst;
+    po.count = (long)m * n;
+    po.n = n;
+    po.n_local = nl;
+    po.err = dev_error_word();
+    po.world = world;
+    return launch_gemv_p2p(J, src, k, ssc, m, n, k, po, st);
+  }
   // this rank's (m, nl) block, at its slot of the gather buffer
   float *mine = (m == 1 ? dst : work) + (size_t)rank * m * nl;
   if (m <= 8) {

@@ -61,6 +61,7 @@ enum DevErr : unsigned int {
   DEV_TIMEOUT_EMPTY = 2,  // producer waited too long for a free stage
   DEV_TIMEOUT_TMEM = 3,   // accumulator hand-off between MMA and epilogue
   DEV_TIMEOUT_DRAIN = 4,  // draining in-flight copies after an error
+  DEV_TIMEOUT_PEER = 6,   // a rank of a fused all-gather never signalled
 };
 unsigned int *dev_error_word();  // device address of the error word
 
@@ -82,6 +83,30 @@ struct GemvJobs {
 int launch_gemv(const GemvJobs &jobs, const int8_t *x, long xstride,
                 const float *xs, int mb, long ystride, int k,
                 cudaStream_t st);
+
+// Row-sharded GEMV whose epilogue is the all-gather.  Each rank writes its
+// output slice into half (epoch & 1) of its own symmetric buffer; the last
+// CTA of the grid then signals every rank ("slice ready") and waits,
+// bounded, until all ranks have signalled for this launch; then all CTAs
+// pull every rank's slice over NVLink (16-byte loads from the peers' CUDA
+// IPC mappings) straight into the caller's dst.  The halves alternate by a
+// device-side launch epoch: a rank one launch ahead writes the other half,
+// and it cannot get two ahead before this rank has finished pulling.
+struct PeerOut {
+  long long delta[8];  // bytes from this rank's symmetric buffer to rank p's
+  int *flag_peer[8];   // rank p's arrival counter
+  int *flag_local;     // [0] arrivals (world per launch), [1] launch epoch,
+                       // [2] finished CTAs, [3] release epoch
+  float *sym;          // this rank's symmetric buffer (two halves)
+  long half_elems;     // floats per half
+  float *dst;          // caller's output, [rows][n] floats
+  long count;          // rows * n
+  int n, n_local;      // row length and per-rank slice width (multiple of 4)
+  unsigned int *err;
+  int world;
+};
+int launch_gemv_p2p(const GemvJobs &jobs, const int8_t *x, long xstride, const float *xs,
+                    int mb, long ystride, int k, const PeerOut &po, cudaStream_t st);
 
 // quantize_acts + GEMV in one launch (mb <= 8 rows of fp32 xf); writes the
 // codes (qout, dense [mb][k]) and scales (sout) as quantize_acts would.

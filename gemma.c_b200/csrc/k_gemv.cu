@@ -108,15 +108,23 @@ __device__ __forceinline__ float block_max256(float v, float *red) {
 }
 
 // Vector kernel: k % 16 == 0, every weight row and x row 16-byte aligned.
-template <int MB, int LPR, int R, int U, bool FQ>
+template <int MB, int LPR, int R, int U, bool FQ, bool P2P>
 __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, const GemvX X, int mb,
-                                                       long ystride, int k, int total_rows) {
+                                                       long ystride, int k, int total_rows,
+                                                       const PeerOut po) {
   extern __shared__ int4 xsm[];  // [MB][C] 16-byte chunks of x
   __shared__ float red[kThreads / 32];
   __shared__ float s_scale[MB];
   __shared__ float s_xsc[MB];  // activation scales, indexed by reduced-sum slot
   const int C = k >> 4;
   ptx::griddep_wait();
+  // fused all-gather: this launch's epoch picks the symmetric buffer half
+  int epoch0 = 0;
+  long half_off = 0;
+  if (P2P) {
+    epoch0 = *reinterpret_cast<volatile int *>(po.flag_local + 1);
+    half_off = (epoch0 & 1) ? po.half_elems : 0;
+  }
   float xsc[MB];
   if (FQ) {
     for (int b = 0; b < MB; ++b) {
@@ -224,9 +232,58 @@ __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, cons
         if (row < total_rows && b < mb) {
           int j, local;
           job_of(jobs, row, j, local);
-          jobs.y[j][(size_t)b * ystride + local] = dequant(v[t], s_xsc[b], jobs.ws[j][local]);
+          const float val = dequant(v[t], s_xsc[b], jobs.ws[j][local]);
+          jobs.y[j][(size_t)b * ystride + local + half_off] = val;
         }
       }
+    }
+  }
+  if (P2P) {
+    // This CTA's slice stores reach this GPU's L2 (gpu scope); the CTA that
+    // signals the peers then releases everything it observed at system scope
+    // (fences are cumulative), so only one system-scope fence per launch.
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      volatile int *vf = po.flag_local;
+      const uint64_t t0 = ptx::globaltimer();
+      if (atomicAdd(po.flag_local + 2, 1) == (int)gridDim.x - 1) {
+        // last CTA of this rank: arrive at every rank, wait for every rank
+        po.flag_local[2] = 0;
+        __threadfence_system();
+        for (int pr = 0; pr < po.world; ++pr) atomicAdd_system(po.flag_peer[pr], 1);
+        const int target = (epoch0 + 1) * po.world;
+        while (vf[0] < target) {
+          if (ptx::globaltimer() - t0 > 2000000000ull) {
+            atomicCAS(po.err, 0u, (unsigned int)DEV_TIMEOUT_PEER);
+            break;
+          }
+        }
+        __threadfence_system();  // acquire: the peers' slices are ready
+        vf[1] = epoch0 + 1;      // next launch uses the other half
+        __threadfence();
+        atomicExch(po.flag_local + 3, epoch0 + 1);  // release this grid's CTAs
+      } else {
+        while (vf[3] != epoch0 + 1) {
+          if (ptx::globaltimer() - t0 > 4000000000ull) {
+            atomicCAS(po.err, 0u, (unsigned int)DEV_TIMEOUT_PEER);
+            break;
+          }
+          __nanosleep(64);
+        }
+        __threadfence();
+      }
+    }
+    __syncthreads();
+    // every rank's slice is ready in its half: pull them all into dst, 16
+    // bytes at a time (a 4-float group never straddles two ranks' slices)
+    const long groups = po.count >> 2;
+    for (long g = (long)blockIdx.x * kThreads + threadIdx.x; g < groups; g += (long)gridDim.x * kThreads) {
+      const long i = g << 2;
+      const int owner = (int)((i % po.n) / po.n_local);
+      const float4 *srcp = reinterpret_cast<const float4 *>(
+          reinterpret_cast<const char *>(po.sym + half_off + i) + po.delta[owner]);
+      reinterpret_cast<float4 *>(po.dst)[g] = __ldcg(srcp);
     }
   }
   ptx::griddep_launch();
@@ -267,12 +324,14 @@ __global__ void __launch_bounds__(kThreads) k_gemv_any(const GemvJobs jobs,
   ptx::griddep_launch();
 }
 
-template <int MB, int LPR, bool FQ>
+template <int MB, int LPR, bool FQ, bool P2P = false>
 int launch_v16(const GemvJobs &jobs, const GemvX &X, int mb, long ystride, int k, int total_rows,
-               cudaStream_t st) {
+               cudaStream_t st, const PeerOut *po = nullptr) {
   constexpr int R = 2;
   constexpr int U = (MB >= 4) ? 2 : 4;
-  auto kern = k_gemv_v16<MB, LPR, R, U, FQ>;
+  auto kern = k_gemv_v16<MB, LPR, R, U, FQ, P2P>;
+  PeerOut pz{};
+  const PeerOut &pout = po ? *po : pz;
   const size_t smem = (size_t)MB * k;
   static std::once_flag once;
   static int regs = 0;
@@ -296,20 +355,21 @@ int launch_v16(const GemvJobs &jobs, const GemvX &X, int mb, long ystride, int k
   long need = ((long)total_rows + rows_per_block - 1) / rows_per_block;
   long cap = (long)num_sms() * blocks_per_sm;
   const int grid = (int)(need < cap ? need : cap);
-  GCU_CUDA(launch_k(kern, grid, kThreads, smem, st, jobs, X, mb, ystride, k, total_rows));
+  GCU_CUDA(launch_k(kern, grid, kThreads, smem, st, jobs, X, mb, ystride, k, total_rows, pout));
   GCU_CUDA(cudaGetLastError());
   return 0;
 }
 
-template <int MB, bool FQ>
+template <int MB, bool FQ, bool P2P = false>
 int launch_mb(const GemvJobs &jobs, const GemvX &X, int mb, long ystride, int k, int total_rows,
-              cudaStream_t st) {
+              cudaStream_t st, const PeerOut *po = nullptr) {
   const int C = k / 16;
   // many activation rows: narrower lane groups keep the reduction short
-  if (MB >= 8) return launch_v16<MB, 8, FQ>(jobs, X, mb, ystride, k, total_rows, st);
-  if (C >= 128 && MB <= 2) return launch_v16<MB, 32, FQ>(jobs, X, mb, ystride, k, total_rows, st);
-  if (C >= 64) return launch_v16<MB, 16, FQ>(jobs, X, mb, ystride, k, total_rows, st);
-  return launch_v16<MB, 8, FQ>(jobs, X, mb, ystride, k, total_rows, st);
+  if (MB >= 8) return launch_v16<MB, 8, FQ, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
+  if (C >= 128 && MB <= 2)
+    return launch_v16<MB, 32, FQ, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
+  if (C >= 64) return launch_v16<MB, 16, FQ, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
+  return launch_v16<MB, 8, FQ, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
 }
 
 template <bool FQ>
@@ -344,6 +404,21 @@ int launch_gemv(const GemvJobs &jobs, const int8_t *x, long xstride, const float
   GCU_CUDA(launch_k(k_gemv_any, grid, kThreads, 0, st, jobs, x, xstride, xs, mb, ystride, k, total_rows));
   GCU_CUDA(cudaGetLastError());
   return 0;
+}
+
+// Row-sharded GEMV with the all-gather fused into its epilogue (see PeerOut).
+int launch_gemv_p2p(const GemvJobs &jobs, const int8_t *x, long xstride, const float *xs, int mb,
+                    long ystride, int k, const PeerOut &po, cudaStream_t st) {
+  if (jobs.njobs != 1 || mb <= 0 || mb > 8) return set_error("gemv p2p: one job, 1..8 rows");
+  const int total_rows = jobs.row_end[0];
+  const bool vec = (k % 16 == 0) && ((uintptr_t)x % 16 == 0) && (mb == 1 || xstride % 16 == 0) &&
+                   ((uintptr_t)jobs.w[0] % 16 == 0) && (size_t)8 * k <= 200 * 1024 && total_rows > 0;
+  if (!vec) return set_error("gemv p2p: needs k %% 16 == 0 and 16-byte aligned operands");
+  GemvX X{x, xstride, xs, nullptr, nullptr, nullptr};
+  if (mb == 1) return launch_mb<1, false, true>(jobs, X, mb, ystride, k, total_rows, st, &po);
+  if (mb == 2) return launch_mb<2, false, true>(jobs, X, mb, ystride, k, total_rows, st, &po);
+  if (mb <= 4) return launch_mb<4, false, true>(jobs, X, mb, ystride, k, total_rows, st, &po);
+  return launch_mb<8, false, true>(jobs, X, mb, ystride, k, total_rows, st, &po);
 }
 
 // Fused quantize_acts + GEMV: xf holds mb fp32 rows (row stride xfstride

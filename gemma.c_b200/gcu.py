@@ -59,6 +59,7 @@ SIGNATURES = {
     "gcu_comm_unique_id": (_int, [ctypes.c_char_p]),
     "gcu_comm_init": (_int, [_int, _int, ctypes.c_char_p]),
     "gcu_comm_destroy": (_int, []),
+    "gcu_comm_fused_allgather": (_int, []),
     "gcu_dev_gemm_int8_rowshard": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _int, _vp]),
 }
 # exported but not part of the public header (benchmark sweeps)
@@ -267,6 +268,10 @@ def comm_unique_id() -> bytes:
 
 def comm_init(rank: int, world: int, uid: bytes) -> None:
     _check(lib().gcu_comm_init(rank, world, uid), "comm_init")
+
+
+def comm_fused_allgather() -> bool:
+    return bool(lib().gcu_comm_fused_allgather())
 
 
 def comm_destroy() -> None:

@@ -167,10 +167,17 @@ int gcu_dev_quantize_gemm_int8_multi(const gcu_gemv_job *jobs, int njobs,
 int gcu_comm_unique_id(unsigned char id[128]);
 int gcu_comm_init(int rank, int world, const unsigned char id[128]);
 int gcu_comm_destroy(void);
+/* 1 if gcu_dev_gemm_int8_rowshard fuses its all-gather into the GEMV as
+ * NVLink peer stores (m <= 8, every rank mapped every peer's buffer through
+ * CUDA IPC at gcu_comm_init); 0 if it uses an NCCL all-gather. */
+int gcu_comm_fused_allgather(void);
 
 /* dst (m, n) dense = sharded gemm_int8 with this rank's rows mat_local
  * (n/world rows) and scales matsc_local.  `work` is device scratch of
- * m*n floats used as the all-gather buffer.  m <= 8 uses the GEMV kernel. */
+ * m*n floats used as the NCCL all-gather buffer.  m <= 8 uses the GEMV
+ * kernel, with the all-gather fused into it when gcu_comm_fused_allgather()
+ * is 1.  Every rank must make the same sequence of calls; calls of one rank
+ * are ordered by its stream. */
 int gcu_dev_gemm_int8_rowshard(float *dst, float *work,
                                const int8_t *mat_local,
                                const float *matsc_local, const int8_t *src,

@@ -40,12 +40,19 @@ def _rank(rank, world, port, q):
         obj = [gcu.comm_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
         gcu.comm_init(rank, world, obj[0])
-        for m, n, k in [(1, 8192, 2560), (4, 4096, 640), (300, 2048, 1152)]:
-            w, ws = synth.weight(700 + m, n, k)
-            xq, xs = O.quantize_acts(synth.activations(800 + m, m, k))
+        ok = gcu.comm_fused_allgather()  # NVLink peers: the fused path must be on
+        dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+        # several calls in a row alternate the two halves of the symmetric
+        # buffer; m <= 8 runs the fused GEMV + peer-store all-gather, m = 300
+        # the tensor-core GEMM + NCCL all-gather
+        for it, (m, n, k) in enumerate([(1, 8192, 2560), (4, 4096, 640), (1, 8192, 2560), (8, 2048, 1152),
+                                        (300, 2048, 1152), (1, 262144, 640), (1, 8192, 2560)]):
+            w, ws = synth.weight(700 + m + it, n, k) if n * k <= 8 << 20 else (
+                np.random.default_rng(it).integers(-127, 128, (n, k), dtype=np.int8),
+                np.random.default_rng(it + 1).random(n, dtype=np.float32) * 1e-3)
+            xq, xs = O.quantize_acts(synth.activations(800 + m + it, m, k))
             sl = shard.row_slice(n, rank, world)
-            dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
-            y = torch.empty((m, n), dtype=torch.float32, device="cuda")
+            y = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
             work = torch.empty((m, n), dtype=torch.float32, device="cuda")
             gcu.dev_gemm_int8_rowshard(y, work, dev(w[sl]), dev(ws[sl]), dev(xq), dev(xs), m, n, k)
             torch.cuda.synchronize()
