@@ -382,7 +382,7 @@ class LmHead:
 
     def config(self):
         import gcu
-        ag = "fused NVLink peer-store all-gather" if (self.world > 1 and gcu.comm_fused_allgather()) else \
+        ag = "all-gather fused into the GEMV (NVLink peer loads)" if (self.world > 1 and gcu.comm_fused_allgather()) else \
             "NCCL all-gather"
         return {"workload": f"lmhead4b (configs[2]): lm_head GEMV {self.n} x {self.k}, batch {self.b}, "
                             f"rows sharded over {self.world} GPU(s) + {ag}",
