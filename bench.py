@@ -668,7 +668,8 @@ def run_reference(args):
     out = {"metric": METRIC, "value": v, "unit": "int8 TOPS", "n_gpus": world, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
            "vs_baseline": None, "dtype": "int8 (int32 accum, fp32 out)", "data": "synthetic", "impl": "reference",
-           "config": dict(wl.config(), parallelism="CPU, OpenMP", sample="1 of 26 layers per step"),
+           "config": dict(wl.config(), parallelism="CPU, OpenMP", sample="1 of 26 layers per step",
+                          calls_per_layer="gemma.c quantize_acts x4 + gemm_int8 per weight (7)"),
            "cpu_baseline": {"value": v, "unit": "int8 TOPS", "cores": threads, "kind": "reference",
                             "sample": f"1 layer (M=512) of gemma.c quantize_acts+gemm_int8 per step, "
                                       f"{variant}/{R.isa} build"},
