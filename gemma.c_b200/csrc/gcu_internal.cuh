@@ -242,6 +242,16 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap *m,
       "l"(m), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
       : "memory");
 }
+// L2 prefetch of one tile through a tensor map (no data reaches the CTA)
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap *m, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(m), "r"(x),
+               "r"(y)
+               : "memory");
+}
+// L2 prefetch of `bytes` (a multiple of 16) from a 16-byte aligned address
+__device__ __forceinline__ void bulk_prefetch_l2(const void *p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap *m,
                                              const void *src, int x, int y) {
   asm volatile(

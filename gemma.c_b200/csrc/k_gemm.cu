@@ -46,6 +46,7 @@ constexpr int kMaxJobs = 4;
 constexpr int kEpiStageBytes = 32 * 128;  // 32 rows x 32 fp32
 
 constexpr int kSmemMax = 232448;  // opt-in shared memory per CTA on sm_100
+constexpr int kPrefetchBytes = 256 * 1024;  // B bytes a CTA warms in L2 before its wait
 
 __host__ __device__ constexpr int pow2_at_least(int v) {
   int p = 32;
@@ -205,6 +206,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_tc(const __grid_constan
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // The weights do not depend on the previous kernel on the stream: warm L2
+  // with this CTA's first B tiles while that kernel finishes.  An L2 prefetch
+  // brings nothing into the CTA, and L2 is where every write to device memory
+  // lands, so it cannot expose a stale value.
+  Unit w_first{};
+  if (warp == 0 && lane == 0 && (int)blockIdx.x < p.units) {
+    w_first = decode_unit(p, blockIdx.x);
+    const int kb0 = w_first.s * p.kb_per_split;
+    const int kb1 = min(kb0 + p.kb_per_split, p.kb_total);
+    const int kbn = min(kb1 - kb0, max(C::STAGES, kPrefetchBytes / C::B_BYTES));
+    for (int kb = kb0; kb < kb0 + kbn; ++kb)
+      ptx::tma_prefetch_l2_2d(&p.jobs[w_first.job].tmB, kb * BK, w_first.n_t * BN);
+  }
   // everything above overlapped the previous kernel; global memory from here
   ptx::griddep_wait();
 
@@ -216,7 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_tc(const __grid_constan
       int it = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
-        const Unit w = decode_unit(p, u);
+        const Unit w = u == (int)blockIdx.x ? w_first : decode_unit(p, u);
         const int kb0 = w.s * p.kb_per_split;
         const int kb1 = min(kb0 + p.kb_per_split, p.kb_total);
         for (int kb = kb0; kb < kb1; ++kb, ++it) {

@@ -24,6 +24,8 @@ namespace gcu {
 namespace {
 
 constexpr int kThreads = 256;
+// weight sets up to this size are prefetched into L2 before the dependency wait
+constexpr long kPrefetchMaxBytes = 32L << 20;
 
 __device__ __forceinline__ int dot16(const int4 &w, const int4 &x, int acc) {
   acc = __dp4a(w.x, x.x, acc);
@@ -117,6 +119,21 @@ __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, cons
   __shared__ float s_scale[MB];
   __shared__ float s_xsc[MB];  // activation scales, indexed by reduced-sum slot
   const int C = k >> 4;
+  constexpr int kRowsPerWarp = (32 / LPR) * R;
+  const int lane = threadIdx.x & 31;
+  // The next launch on the stream may start its prologue now; its own wait
+  // still orders it after this grid completes.
+  ptx::griddep_launch();
+  // Small weight sets: warm L2 with this warp's first rows while the previous
+  // kernel finishes (an L2 prefetch cannot expose a stale value).
+  if ((long)total_rows * k <= kPrefetchMaxBytes) {
+    const int row = (blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5)) * kRowsPerWarp + lane;
+    if (lane < kRowsPerWarp && row < total_rows) {
+      int j, local;
+      job_of(jobs, row, j, local);
+      ptx::bulk_prefetch_l2(jobs.w[j] + (size_t)local * k, (uint32_t)k);
+    }
+  }
   ptx::griddep_wait();
   // fused all-gather: this launch's epoch picks the symmetric buffer half
   int epoch0 = 0;
@@ -170,9 +187,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, cons
   if (threadIdx.x < MB) s_xsc[threadIdx.x] = xsc[threadIdx.x];
   __syncthreads();
 
-  const int lane = threadIdx.x & 31;
   const int slot = lane / LPR, sub = lane % LPR;
-  constexpr int kRowsPerWarp = (32 / LPR) * R;
   const int nwarps = gridDim.x * (kThreads / 32);
   for (int base = (blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5)) * kRowsPerWarp;
        base < total_rows; base += nwarps * kRowsPerWarp) {
@@ -286,7 +301,6 @@ __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, cons
       reinterpret_cast<float4 *>(po.dst)[g] = __ldcg(srcp);
     }
   }
-  ptx::griddep_launch();
 }
 
 // Generic kernel: any k, any alignment.  One warp per weight row, byte loads.
@@ -298,6 +312,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv_any(const GemvJobs jobs,
                                                        int total_rows) {
   const int lane = threadIdx.x & 31;
   const int nwarps = gridDim.x * (kThreads / 32);
+  ptx::griddep_launch();
   ptx::griddep_wait();
   for (int row = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); row < total_rows;
        row += nwarps) {
@@ -321,7 +336,6 @@ __global__ void __launch_bounds__(kThreads) k_gemv_any(const GemvJobs jobs,
         jobs.y[j][(size_t)b * ystride + local] = dequant(acc[b], xs[b], ws);
     }
   }
-  ptx::griddep_launch();
 }
 
 template <int MB, int LPR, bool FQ, bool P2P = false>

@@ -10,8 +10,15 @@
 // cannot contract them into an FMA; the division is IEEE (no fast math).
 //
 // HBM-bound: 4 bytes read + 1 byte written per element, 4 bytes per row.
-// One CTA per row keeps the row in registers between the max pass and the
-// quantize pass, so each element is read from HBM once.
+// Each row stays in registers between the max pass and the quantize pass, so
+// every element is read from HBM once.  Rows up to 16384 elements: WPR warps
+// per row, 8/WPR rows per 256-thread CTA, every load of a lane issued before
+// the first use (one barrier when WPR > 1, none otherwise).  Longer rows: one
+// CTA per row.
+//
+// Every kernel lets the next launch on the stream start (griddepcontrol
+// launch_dependents) as soon as it begins: the dependent's own wait still
+// orders it after this grid's completion, so only its prologue overlaps.
 #include "gcu_internal.cuh"
 
 namespace gcu {
@@ -38,7 +45,58 @@ __device__ __forceinline__ void scale_of(float amax, float &scale, float &inv) {
   ptx::quant_scale(amax, scale, inv);
 }
 
-// Vector path: src rows 16-byte aligned, n % 4 == 0.  VPT float4 per thread.
+// Warp path: src rows 16-byte aligned, n % 4 == 0, n/4 <= 32*WPR*VPT.  Lane
+// `lane` of warp `wi` in the row's group holds float4 (i*WPR + wi)*32 + lane,
+// so each warp load instruction reads 512 contiguous bytes.
+template <int VPT, int WPR>
+__global__ void __launch_bounds__(256) k_quant_warps(int8_t *__restrict__ dst,
+                                                     float *__restrict__ dsc,
+                                                     const float *__restrict__ src,
+                                                     long sstr, int m, int n) {
+  constexpr int kRows = 8 / WPR;
+  __shared__ float red[8];
+  ptx::griddep_launch();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = warp / WPR, wi = warp - grp * WPR;
+  const int row = blockIdx.x * kRows + grp;
+  const bool live = row < m;  // uniform per warp
+  const int n4 = n >> 2;
+  ptx::griddep_wait();
+  float4 v[VPT];
+  float amax = 0.0f;
+  if (live) {
+    const float4 *x = reinterpret_cast<const float4 *>(src + (size_t)row * sstr);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int idx = (i * WPR + wi) * 32 + lane;
+      if (idx < n4) {
+        v[i] = __ldcs(x + idx);
+        amax = ptx::absmax4(v[i], amax);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if (WPR > 1) {
+    if (lane == 0) red[warp] = amax;
+    __syncthreads();
+#pragma unroll
+    for (int w = 0; w < WPR; ++w) amax = fmaxf(amax, red[grp * WPR + w]);
+  }
+  if (!live) return;
+  float scale, inv;
+  scale_of(amax, scale, inv);
+  int *q = reinterpret_cast<int *>(dst + (size_t)row * n);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int idx = (i * WPR + wi) * 32 + lane;
+    if (idx < n4) q[idx] = ptx::quant_pack4(v[i], inv);
+  }
+  if (wi == 0 && lane == 0) dsc[row] = scale;
+}
+
+// Vector path for long rows: src rows 16-byte aligned, n % 4 == 0.  VPT
+// float4 per thread, one CTA per row.
 template <int VPT>
 __global__ void __launch_bounds__(1024) k_quant_rows_v4(int8_t *__restrict__ dst,
                                                         float *__restrict__ dsc,
@@ -46,6 +104,7 @@ __global__ void __launch_bounds__(1024) k_quant_rows_v4(int8_t *__restrict__ dst
                                                         long sstr, int m, int n) {
   __shared__ float red[32];
   const int n4 = n >> 2;
+  ptx::griddep_launch();
   ptx::griddep_wait();
   for (int row = blockIdx.x; row < m; row += gridDim.x) {
     const float4 *x = reinterpret_cast<const float4 *>(src + (size_t)row * sstr);
@@ -78,7 +137,6 @@ __global__ void __launch_bounds__(1024) k_quant_rows_v4(int8_t *__restrict__ dst
     }
     if (threadIdx.x == 0) dsc[row] = scale;
   }
-  ptx::griddep_launch();
 }
 
 // Any alignment and length: two passes over global memory.
@@ -87,6 +145,7 @@ __global__ void __launch_bounds__(256) k_quant_rows_any(int8_t *__restrict__ dst
                                                         const float *__restrict__ src,
                                                         long sstr, int m, int n) {
   __shared__ float red[32];
+  ptx::griddep_launch();
   ptx::griddep_wait();
   for (int row = blockIdx.x; row < m; row += gridDim.x) {
     const float *x = src + (size_t)row * sstr;
@@ -99,7 +158,17 @@ __global__ void __launch_bounds__(256) k_quant_rows_any(int8_t *__restrict__ dst
     for (int i = threadIdx.x; i < n; i += blockDim.x) q[i] = (int8_t)quant_one(x[i], inv);
     if (threadIdx.x == 0) dsc[row] = scale;
   }
-  ptx::griddep_launch();
+}
+
+template <int WPR>
+cudaError_t launch_warps(int vpt, int grid, int8_t *dst, float *dsc, const float *src, long sstr, int m,
+                 int n, cudaStream_t st) {
+  switch (vpt) {
+    case 2: return launch_k(k_quant_warps<2, WPR>, grid, 256, 0, st, dst, dsc, src, sstr, m, n);
+    case 4: return launch_k(k_quant_warps<4, WPR>, grid, 256, 0, st, dst, dsc, src, sstr, m, n);
+    case 8: return launch_k(k_quant_warps<8, WPR>, grid, 256, 0, st, dst, dsc, src, sstr, m, n);
+    default: return launch_k(k_quant_warps<16, WPR>, grid, 256, 0, st, dst, dsc, src, sstr, m, n);
+  }
 }
 
 }  // namespace
@@ -111,7 +180,26 @@ int launch_quantize_rows(int8_t *dst, float *dsc, const float *src, long sstr,
   const bool vec = ((uintptr_t)src % 16 == 0) && (sstr % 4 == 0) && (n % 4 == 0) &&
                    ((uintptr_t)dst % 4 == 0);
   const int n4 = n / 4;
-  if (vec && n4 <= 8 * 1024) {
+  if (vec && n4 <= 8 * 32 * 16) {
+    // fewest warps per row that hold the row in 16 float4 per lane, then more
+    // while the grid is under two CTAs per SM and each lane keeps >= 2 loads
+    int wpr = 1;
+    while (wpr < 8 && n4 > 32 * 16 * wpr) wpr *= 2;
+    const int sms = num_sms();
+    while (wpr < 8 && (long)m * wpr < 16L * sms && n4 >= 32 * 2 * (2 * wpr)) wpr *= 2;
+    const int need = (n4 + 32 * wpr - 1) / (32 * wpr);
+    const int vpt = need <= 2 ? 2 : need <= 4 ? 4 : need <= 8 ? 8 : 16;
+    const long rows_per_cta = 8 / wpr;
+    const int wgrid = (int)((m + rows_per_cta - 1) / rows_per_cta);
+    cudaError_t e;
+    switch (wpr) {
+      case 1: e = launch_warps<1>(vpt, wgrid, dst, dsc, src, sstr, m, n, st); break;
+      case 2: e = launch_warps<2>(vpt, wgrid, dst, dsc, src, sstr, m, n, st); break;
+      case 4: e = launch_warps<4>(vpt, wgrid, dst, dsc, src, sstr, m, n, st); break;
+      default: e = launch_warps<8>(vpt, wgrid, dst, dsc, src, sstr, m, n, st); break;
+    }
+    GCU_CUDA(e);
+  } else if (vec && n4 <= 8 * 1024) {
     int vpt = (n4 + 1023) / 1024;
     vpt = vpt <= 1 ? 1 : vpt <= 2 ? 2 : vpt <= 4 ? 4 : 8;
     int threads = (n4 + vpt - 1) / vpt;
