@@ -62,6 +62,7 @@ enum DevErr : unsigned int {
   DEV_TIMEOUT_TMEM = 3,   // accumulator hand-off between MMA and epilogue
   DEV_TIMEOUT_DRAIN = 4,  // draining in-flight copies after an error
   DEV_TIMEOUT_PEER = 6,   // a rank of a fused all-gather never signalled
+  DEV_TIMEOUT_SPLIT = 7,  // a split-K CTA waited too long for the other splits
 };
 unsigned int *dev_error_word();  // device address of the error word
 
@@ -177,6 +178,12 @@ __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int *p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
 // ---- mbarrier --------------------------------------------------------------

@@ -65,9 +65,11 @@ int scratch_address(void **out) {
 
 using namespace gcu;
 
-GCU_EXPORT int gcu_dev_gemm_int8_noalloc(float *dst, int dstr, const int8_t *mat, int mstr,
-                                         const float *matsc, const int8_t *src, int sstr,
-                                         const float *ssc, int m, int n, int k, void *stream) {
+namespace {
+
+int noalloc_gemm(float *dst, int dstr, const int8_t *mat, int mstr, const float *matsc,
+                 const int8_t *src, int sstr, const float *ssc, int m, int n, int k, void *stream,
+                 int force_bn, int force_split, int force_mb) {
   if (m <= 0 || n <= 0) return 0;
   if (k <= 0) return set_error("gemm_int8_noalloc: k must be positive (got %d)", k);
   if (dstr == 0) dstr = n;
@@ -92,5 +94,24 @@ GCU_EXPORT int gcu_dev_gemm_int8_noalloc(float *dst, int dstr, const int8_t *mat
                    reinterpret_cast<int *>(static_cast<unsigned char *>(base) + kMaxScratchBytes),
                    kMaxCounters};
   GemmArgs a{dst, dstr, mat, mstr, matsc, src, sstr, ssc, m, n, k};
-  return launch_gemm_tc_jobs(src, sstr, ssc, m, k, &a, 1, st, 0, 0, &ext);
+  return launch_gemm_tc_jobs(src, sstr, ssc, m, k, &a, 1, st, force_bn, force_split, &ext,
+                             force_mb);
+}
+
+}  // namespace
+
+GCU_EXPORT int gcu_dev_gemm_int8_noalloc(float *dst, int dstr, const int8_t *mat, int mstr,
+                                         const float *matsc, const int8_t *src, int sstr,
+                                         const float *ssc, int m, int n, int k, void *stream) {
+  return noalloc_gemm(dst, dstr, mat, mstr, matsc, src, sstr, ssc, m, n, k, stream, 0, 0, 0);
+}
+
+// Same with a forced tile shape ((128*mb) x bn) and K split, for tests that
+// need a given amount of scratch whatever the planner would pick (not part
+// of the public header).
+GCU_EXPORT int gcu_dev_gemm_int8_noalloc_tuned(float *dst, int dstr, const int8_t *mat, int mstr,
+                                               const float *matsc, const int8_t *src, int sstr,
+                                               const float *ssc, int m, int n, int k, int bn,
+                                               int split, int mb, void *stream) {
+  return noalloc_gemm(dst, dstr, mat, mstr, matsc, src, sstr, ssc, m, n, k, stream, bn, split, mb);
 }

@@ -95,7 +95,8 @@ struct alignas(64) TcParams {
   int tiles_m, tiles_n, splits, kb_total, kb_per_split, units;
   const float *ssc;
   int32_t *ws;    // split-K partials [tile][split][TILE_M][BN]
-  int *counters;  // split-K arrival counters [tile]
+  int *counters;  // split-K counters: arrivals [tile], then finished reductions [tile]
+  int dist;       // split-K with every unit in one wave: the splits share the reduction
   unsigned int *err;
 };
 
@@ -154,6 +155,96 @@ __device__ __forceinline__ void emit_chunk(const TcParams &p, const TcJob &job, 
 #pragma unroll
       for (int i = 0; i < 32; ++i)
         if (col0 + i < job.n) d[col0 + i] = out[i];
+    }
+  }
+}
+
+// Distributed split-K reduction, run by the 256 epilogue threads of split
+// w.s once every split of tile w.tile has written its int32 partial.  The
+// tile's 32x32 blocks b = w.s, w.s + splits, ... are this split's share;
+// partials use the writer's layout [row block][chunk][8 x int4][lane], so
+// thread `et` sums int4 `et` of a block (row 32*rb + lane, columns
+// 32*ch + 4*(et/32) ...) across the splits and stores its four fp32 outputs
+// directly.  Up to four blocks per round and four splits per load batch: at
+// most 16 int4 loads in flight per thread.
+struct ShareScales {
+  float xs[4];
+  float ws[4][4];
+};
+
+template <typename C, int BN>
+__device__ __forceinline__ void share_scales(const TcParams &p, const TcJob &job, const Unit &w,
+                                             int r0, int my_nb, ShareScales &sc) {
+  constexpr int NCH = BN / 32;
+  const int et = threadIdx.x - 64;
+  const int lane = et & 31, c = et >> 5;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int b = w.s + (r0 + i) * p.splits;
+    const int rb = b / NCH, ch = b - rb * NCH;
+    const int row = w.m_t * C::TILE_M + rb * 32 + lane;
+    const int col = w.n_t * BN + ch * 32 + 4 * c;
+    const bool ok = r0 + i < my_nb;
+    sc.xs[i] = ok && row < p.m ? __ldg(p.ssc + row) : 0.0f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) sc.ws[i][e] = ok && col + e < job.n ? __ldg(job.matsc + col + e) : 0.0f;
+  }
+}
+
+template <typename C, int BN>
+__device__ __forceinline__ void reduce_share(const TcParams &p, const TcJob &job, const Unit &w,
+                                             size_t part_int4, int my_nb, ShareScales &sc) {
+  constexpr int NCH = BN / 32;
+  const int et = threadIdx.x - 64;
+  const int lane = et & 31, c = et >> 5;
+  const int4 *tbase = reinterpret_cast<const int4 *>(p.ws) + (size_t)w.tile * p.splits * part_int4;
+  for (int r0 = 0; r0 < my_nb; r0 += 4) {
+    if (r0 > 0) share_scales<C, BN>(p, job, w, r0, my_nb, sc);
+    int4 acc[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[i] = make_int4(0, 0, 0, 0);
+    for (int sg = 0; sg < p.splits; sg += 4) {
+      int4 v[4][4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const size_t boff = (size_t)(w.s + (r0 + i) * p.splits) * 256 + et;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          v[i][j] = (r0 + i < my_nb && sg + j < p.splits)
+                        ? __ldcg(tbase + (size_t)(sg + j) * part_int4 + boff)
+                        : make_int4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          acc[i].x += v[i][j].x;
+          acc[i].y += v[i][j].y;
+          acc[i].z += v[i][j].z;
+          acc[i].w += v[i][j].w;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (r0 + i >= my_nb) break;
+      const int b = w.s + (r0 + i) * p.splits;
+      const int rb = b / NCH, ch = b - rb * NCH;
+      const int row = w.m_t * C::TILE_M + rb * 32 + lane;
+      const int col = w.n_t * BN + ch * 32 + 4 * c;
+      if (row >= p.m || col >= job.n) continue;
+      const float4 o = make_float4(dequant(acc[i].x, sc.xs[i], sc.ws[i][0]),
+                                   dequant(acc[i].y, sc.xs[i], sc.ws[i][1]),
+                                   dequant(acc[i].z, sc.xs[i], sc.ws[i][2]),
+                                   dequant(acc[i].w, sc.xs[i], sc.ws[i][3]));
+      float *d = job.dst + (size_t)row * job.dstr + col;
+      if (job.tma_store && col + 3 < job.n) {  // 16-byte aligned rows
+        *reinterpret_cast<float4 *>(d) = o;
+      } else {
+        d[0] = o.x;
+        if (col + 1 < job.n) d[1] = o.y;
+        if (col + 2 < job.n) d[2] = o.z;
+        if (col + 3 < job.n) d[3] = o.w;
+      }
     }
   }
 }
@@ -377,6 +468,39 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_tc(const __grid_constan
         ptx::mbar_arrive(&tempty[buf]);
         __threadfence();
         ptx::named_bar_sync(1, kEpiThreads);
+        if (p.dist) {
+          // Every unit runs in this one wave, so all splits of the tile are
+          // resident: wait until each has published its partial, then every
+          // split reduces its own share of the tile's 32x32 blocks.  The
+          // scales of the first round are fetched before the wait.
+          constexpr int NB = C::TILE_M / 32 * NCH;
+          const int my_nb = (NB - w.s + p.splits - 1) / p.splits;
+          ShareScales sc;
+          share_scales<C, BN>(p, job, w, 0, my_nb, sc);
+          if (threadIdx.x == 64) {
+            atomicAdd(p.counters + w.tile, 1);
+            const uint64_t t0 = ptx::globaltimer();
+            while (ptx::ld_acquire_gpu(p.counters + w.tile) < p.splits) {
+              if (ptx::globaltimer() - t0 > 2000000000ull) {
+                atomicCAS(p.err, 0u, (unsigned int)DEV_TIMEOUT_SPLIT);
+                break;
+              }
+              __nanosleep(32);
+            }
+          }
+          ptx::named_bar_sync(1, kEpiThreads);
+          reduce_share<C, BN>(p, job, w, kPartInt4, my_nb, sc);
+          ptx::named_bar_sync(1, kEpiThreads);
+          if (threadIdx.x == 64) {
+            // the last split done reading resets both counters for the next launch
+            int *done = p.counters + p.tiles_m * p.tiles_n + w.tile;
+            if (atomicAdd(done, 1) == p.splits - 1) {
+              p.counters[w.tile] = 0;
+              *done = 0;
+            }
+          }
+          continue;
+        }
         if (threadIdx.x == 64) {
           const int prev = atomicAdd(p.counters + w.tile, 1);
           s_last = (prev == p.splits - 1);
@@ -515,10 +639,15 @@ int split_for(int tiles, int kb_total, int sms) {
   return s < 1 ? 1 : s;
 }
 
-// Estimated microseconds of one launch with this tile shape.  Measured on
-// B200: a CTA's TMA ring ingests about 100 GB/s, the SMs together about
-// 9 TB/s from L2; the int8 tensor rate is about 22 TOPS per SM; the last
-// tile's epilogue and a split-K round trip are not overlapped.
+// Estimated microseconds of one launch with this tile shape.  The constants
+// were fitted to per-CTA timelines (globaltimer / clock64 stamps) and to a
+// sweep of every tile shape and split over the BASELINE shapes on B200:
+//   - a CTA's TMA ring ingests ~100 GB/s from L2; all SMs together ~12 TB/s
+//   - kind::i8 MMA sustains ~26 TOPS per SM
+//   - the fp32 epilogue drains ~70 GB/s per CTA after ~0.5 us of latency
+//   - a split-K round trip costs about half a partial write per split
+// With two TMEM accumulators the epilogue of a tile overlaps the next tile's
+// main loop; with one (MB*BN > 256) it does not.
 double estimate_us(int m, int ntn, int kb_total, int bn, int mb, int splits, int sms) {
   const double tile_m = 128.0 * mb;
   const long tiles = (long)((m + 128 * mb - 1) / (128 * mb)) * ntn;
@@ -526,14 +655,18 @@ double estimate_us(int m, int ntn, int kb_total, int bn, int mb, int splits, int
   const int kb_unit = (kb_total + splits - 1) / splits;
   const double stage = (tile_m + bn) * 128.0;
   const double t_load = kb_unit * stage / 1.0e5;
-  const double t_mma = kb_unit * 2.0 * tile_m * bn * 128.0 / 2.2e7;
+  const double t_mma = kb_unit * 2.0 * tile_m * bn * 128.0 / 2.6e7;
   const double t_unit = t_load > t_mma ? t_load : t_mma;
   const long waves = (units + sms - 1) / sms;
-  const double t_l2 = (double)units * kb_unit * stage / 9.0e6;
-  const double t_main = waves * t_unit > t_l2 ? waves * t_unit : t_l2;
-  const double t_out = tile_m * bn * 4.0 / 1.0e5;
-  const double t_split = splits > 1 ? tile_m * bn * 4.0 * (1 + splits) / 1.0e5 : 0.0;
-  return t_main + t_out + t_split;
+  const double out_bytes = tile_m * bn * 4.0;
+  const double t_drain = out_bytes / 7.0e4;
+  const double t_out = 0.5 + t_drain;
+  const bool two_acc = 2 * mb * bn <= 512;
+  double t_main = two_acc ? waves * (t_unit > t_drain ? t_unit : t_drain) : waves * (t_unit + t_out);
+  const double t_l2 = (double)units * kb_unit * stage / 1.2e7;
+  if (t_l2 > t_main) t_main = t_l2;
+  const double t_split = splits > 1 ? 0.5 * out_bytes * splits / 7.0e4 : 0.0;
+  return t_main + (two_acc ? t_out : 0.0) + t_split;
 }
 
 }  // namespace
@@ -747,18 +880,21 @@ int run_plan(const Plan &pl, const int8_t *src, long sstr, const float *ssc, int
     void *ws = nullptr;
     int *cnt = nullptr;
     if (ext) {
-      if (need > ext->ws_bytes || tiles > ext->ncounters)
+      if (need > ext->ws_bytes || 2 * tiles > ext->ncounters)
         return set_error("gemm: split-K needs %zu bytes of scratch and %d counters; the caller's "
                          "scratch holds %zu bytes and %d counters",
-                         need, tiles, ext->ws_bytes, ext->ncounters);
-      GCU_CUDA(cudaMemsetAsync(ext->counters, 0, (size_t)tiles * sizeof(int), st));
+                         need, 2 * tiles, ext->ws_bytes, ext->ncounters);
+      GCU_CUDA(cudaMemsetAsync(ext->counters, 0, (size_t)2 * tiles * sizeof(int), st));
       ws = ext->ws;
       cnt = ext->counters;
-    } else if (gemm_workspace(need, &ws, &cnt, tiles, st)) {
+    } else if (gemm_workspace(need, &ws, &cnt, 2 * tiles, st)) {
       return 1;
     }
     p.ws = static_cast<int32_t *>(ws);
     p.counters = cnt;
+    // one wave (grid = min(units, SMs), one CTA per SM): every split of a
+    // tile is resident together and they can share the reduction
+    p.dist = p.units <= num_sms();
   }
   if (mb == 2) {
     if (bn == 128) return launch_cfg<128, 2>(p, st);

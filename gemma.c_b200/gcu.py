@@ -68,6 +68,8 @@ EXTRA = {
                                              _int, _int, _vp]),
     "gcu_dev_gemm_int8_tuned": (_int, [_vp, _int, _vp, _int, _vp, _vp, _int, _vp, _int, _int, _int,
                                        _int, _int, _int, _vp]),
+    "gcu_dev_gemm_int8_noalloc_tuned": (_int, [_vp, _int, _vp, _int, _vp, _vp, _int, _vp, _int, _int,
+                                               _int, _int, _int, _int, _vp]),
 }
 
 
@@ -249,6 +251,13 @@ def dev_gemm_int8_tuned(dst, mat, matsc, src, ssc, m, n, k, bn, split, mb=1, str
     _check(lib().gcu_dev_gemm_int8_tuned(dst.data_ptr(), 0, mat.data_ptr(), 0, matsc.data_ptr(),
                                          src.data_ptr(), 0, ssc.data_ptr(), m, n, k, bn, split, mb,
                                          _stream(stream)), "dev_gemm_int8_tuned")
+
+
+def dev_gemm_int8_noalloc_tuned(dst, mat, matsc, src, ssc, m, n, k, bn, split, mb=1, stream=None):
+    """dev_gemm_int8_noalloc with a forced tile shape and K split (tests)."""
+    _check(lib().gcu_dev_gemm_int8_noalloc_tuned(dst.data_ptr(), 0, mat.data_ptr(), 0, matsc.data_ptr(),
+                                                 src.data_ptr(), 0, ssc.data_ptr(), m, n, k, bn, split, mb,
+                                                 _stream(stream)), "dev_gemm_int8_noalloc_tuned")
 
 
 def dev_gemm_int8_multi_tuned(jobs_t, src, ssc, m, k, bn, split, mb=1, stream=None):

@@ -235,6 +235,26 @@ def test_gemm_tile_and_split_variants(bn, split, mb):
     assert_bits(y.cpu().numpy(), O.gemm_int8(w, ws, xq, xs))
 
 
+@pytest.mark.parametrize("m,n,bn,split,mb", [
+    (128, 1000, 64, 9, 1),    # one wave, more splits than 32x32 blocks per tile
+    (384, 1000, 256, 8, 1),   # one wave, splits summed in two batches of four
+    (40, 1000, 128, 4, 1),    # rows past m in every tile
+    (384, 999, 128, 3, 1),    # odd row stride: plain stores instead of TMA
+    (384, 999, 128, 9, 1),    # more units than SMs: the last split reduces
+])
+def test_gemm_split_k_reductions(m, n, bn, split, mb):
+    k = 2304
+    w, ws = synth.weight(7200 + n + split, n, k)
+    xq, xs = O.quantize_acts(synth.activations(7300 + m, m, k, outliers=True))
+    y = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    for _ in range(2):  # the second call checks the counters were reset
+        y.fill_(float("nan"))
+        gcu.dev_gemm_int8_tuned(y, _dev(w), _dev(ws), _dev(xq), _dev(xs), m, n, k, bn, split, mb)
+        torch.cuda.synchronize()
+        gcu.check_device()
+        assert_bits(y.cpu().numpy(), O.gemm_int8(w, ws, xq, xs))
+
+
 def test_device_chain_quantize_then_multi_gemm():
     # prefill Q/K/V as one launch over three weights sharing the input
     m, dim = 512, 1152

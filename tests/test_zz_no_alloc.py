@@ -53,9 +53,20 @@ def test_noalloc_matches_allocating_entry_point(m, n, k):
 
 
 def test_noalloc_rejects_plans_beyond_the_array():
-    # M=512, N=1152, K=6912 splits K four ways and needs 9 MiB of partials
+    # M=512, N=1152, K=6912 in 128x128 tiles split four ways needs 9 MiB of
+    # partials (the plan is forced: the planner's own pick may need less)
     m, n, k = 512, 1152, 6912
     w, ws, q, s = _operands(m, n, k, seed=5)
     out = torch.empty((m, n), dtype=torch.float32, device="cuda")
     with pytest.raises(gcu.GcuError, match="split-K needs"):
-        gcu.dev_gemm_int8_noalloc(out, w, ws, q, s, m, n, k)
+        gcu.dev_gemm_int8_noalloc_tuned(out, w, ws, q, s, m, n, k, 128, 4, 1)
+    # the same plan within the array: 256 rows need 4.5 MiB
+    m = 256
+    w, ws, q, s = _operands(m, n, k, seed=6)
+    ref = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    gcu.dev_gemm_int8(ref, w, ws, q, s, m, n, k)
+    out = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+    gcu.dev_gemm_int8_noalloc_tuned(out, w, ws, q, s, m, n, k, 128, 4, 1)
+    torch.cuda.synchronize()
+    gcu.check_device()
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), ref.cpu().numpy().view(np.uint32))
