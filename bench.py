@@ -2,7 +2,7 @@
 """Benchmark of the W8A8 matmul hot path on B200 (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload prefill1b|decode270m|lmhead4b]
+                    [--workload prefill1b|decode270m|lmhead4b|prefill4b|prefill12b|decode12b]
 
 Workloads (synthetic seeded data, no checkpoints):
   prefill1b   configs[1], the default: Gemma-3-1B-shaped prefill, M=512
@@ -14,7 +14,15 @@ Workloads (synthetic seeded data, no checkpoints):
               quantize_act + Q/K/V multi-GEMV, O, gate/up multi-GEMV, down,
               then the 262144-row lm_head GEMV.  Unit: HBM GB/s.
   lmhead4b    configs[2]: lm_head GEMV 262144 x 2560, batch 1, rows sharded
-              over the ranks and all-gathered with NCCL (strong scaling).
+              over the ranks and all-gathered (strong scaling).
+  prefill4b   configs[3]: SigLIP-So400m tower (27 layers, M=4096), the
+              image projector (M=256) and the Gemma-3-4B text stack (34
+              layers, M=2048).  Unit: int8 TOPS; N>1 runs replicas.
+  prefill12b  configs[4] prefill: Gemma-3-12B, M=4096, 48 layers; at N>1 the
+              FFN rows are sharded over the ranks and every FFN output is
+              all-gathered (strong scaling).
+  decode12b   configs[4] decode: Gemma-3-12B, batch 1, 48 layers + lm_head;
+              at N>1 the FFN and lm_head rows are sharded (strong scaling).
 
 `value` is measured with inputs resident in HBM, one CUDA graph replay per
 step, CUDA events on the launching stream, max over ranks.  `e2e` is the same
@@ -135,100 +143,159 @@ def max_over_ranks(v: float, world: int) -> float:
 # ---------------------------------------------------------------------------
 # workloads
 # ---------------------------------------------------------------------------
-class Prefill:
-    """1B-shaped W8A8 prefill, M tokens, all layers."""
-    name = "prefill1b"
+PREFILL = {
+    # name: (BASELINE configs index, title, stacks(synth) -> [(label, groups, M, layers)], FFN row-sharded)
+    "prefill1b": (1, "Gemma-3-1B-shaped W8A8 prefill GEMM set",
+                  lambda S: [("text", S.layer_groups(S.CONFIGS["1b"]), 512, 26)], False),
+    "prefill4b": (3, "Gemma-3-4B-shaped W8A8 prefill with a SigLIP-So400m vision tower",
+                  lambda S: [("vision", S.vision_layer_groups(S.CONFIGS["siglip"]), 4096, 27),
+                             ("projector", S.projector_groups(S.CONFIGS["siglip"], S.CONFIGS["4b"]), 256, 1),
+                             ("text", S.layer_groups(S.CONFIGS["4b"]), 2048, 34)], False),
+    "prefill12b": (4, "Gemma-3-12B-shaped W8A8 prefill matmul set, FFN rows sharded over the GPUs",
+                   lambda S: [("text", S.layer_groups(S.CONFIGS["12b"]), 4096, 48)], True),
+}
 
-    def __init__(self, m=512, cfg="1b", seed=0, fused=False):
+
+def is_ffn(name):
+    return name.startswith("w1") or name.startswith("w2") or name.startswith("w3")
+
+
+class Prefill:
+    """Prefill GEMM sets (configs[1], [3], [4]): stacks of identical layers,
+    each layer the quantize_acts -> GEMM pairs of gemma.c (5034-5391 text,
+    4497-4633 vision, 4714-4716 projector).  Sharded workloads split the FFN
+    weights' rows over the ranks and all-gather each FFN output
+    (gcu_dev_gemm_int8_rowshard); Q/K/V/O stay replicated."""
+
+    def __init__(self, name="prefill1b", seed=0, fused=False, world=1, rank=0):
         import synth
-        self.fused = fused
-        self.cfg = synth.CONFIGS[cfg]
-        self.m = m
-        self.groups = synth.layer_groups(self.cfg)
-        self.layers = self.cfg["layers"]
-        self.ops = synth.layer_ops(self.cfg, m) * self.layers
+        self.name = name
+        self.index, self.title, stacks, shard = PREFILL[name]
+        self.stacks = stacks(synth)
+        self.fused, self.world, self.rank = fused, world, rank
+        self.shard = shard and world > 1
+        self.needs_comm = self.shard
+        self.m = self.stacks[-1][2]
+        self.layers = sum(st[3] for st in self.stacks)
+        self.ops = sum(synth.groups_ops(g, m) * nl for _, g, m, nl in self.stacks)
         self.seed = seed
+        # single-stack workloads keep the flat view the host path uses
+        self.groups = self.stacks[-1][1]
 
     def config(self):
-        return {"workload": "prefill1b (configs[1]): Gemma-3-1B-shaped W8A8 prefill GEMM set",
-                "tokens_m": self.m, "layers": self.layers, "d_model": self.cfg["dim"], "ffn": self.cfg["ffn"],
-                "calls_per_layer": ("4 x quantize_acts->GEMM pairs, each one launch" if self.fused else
-                                    "quantize_acts x4 + GEMM {QKV, O, up+gate, down}") +
-                                   " (Q/K/V and up/gate as multi-weight launches)",
-                "inputs": "1% outlier channels x20; per-layer weights+activations ~1.3 GB > L2 (no flush)"}
+        c = {"workload": f"{self.name} (configs[{self.index}]): {self.title}",
+             "stacks": [{"stack": lb, "tokens_m": m, "layers": nl,
+                         "gemms": [[n, k] for k, jobs in g for _, n in jobs]} for lb, g, m, nl in self.stacks],
+             "calls_per_layer": ("quantize_acts->GEMM pairs, each one launch" if self.fused else
+                                 "quantize_acts + one GEMM launch per group") +
+                                " (weights sharing an input as one multi-weight launch)",
+             "inputs": "1% outlier channels x20; per-layer weights+activations exceed L2 (no flush)"}
+        if self.name == "prefill1b":
+            c.update(tokens_m=self.m, layers=self.layers, d_model=self.groups[0][0], ffn=self.groups[3][0])
+        if self.shard:
+            c["sharding"] = (f"FFN rows over {self.world} GPUs, outputs all-gathered; "
+                             "Q/K/V/O replicated (counted once in value)")
+        return c
 
     def build(self, device):
         import torch
         import synth
         gen = torch.Generator(device=device).manual_seed(1234 + self.seed)
-        m = self.m
-        self.L = []
-        for _ in range(self.layers):
-            layer = []
-            for k, jobs in self.groups:
-                x = synth.activations_torch(m, k, gen, device, outliers=True)
-                q = torch.empty((m, k), dtype=torch.int8, device=device)
-                s = torch.empty(m, dtype=torch.float32, device=device)
-                ws = []
-                for _, n in jobs:
-                    w, sc = synth.weight_torch(n, k, gen, device)
-                    ws.append((w, sc))
-                layer.append({"x": x, "q": q, "s": s, "k": k, "w": ws})
-            self.L.append(layer)
-        # output buffers (fp32) per group, shared by the layers
-        self.out = [[torch.empty((m, n), dtype=torch.float32, device=device) for _, n in jobs]
-                    for _, jobs in self.groups]
+        wgen = torch.Generator(device=device).manual_seed(4321)  # identical weights on every rank
+        self.L, self.out, self.work = [], [], []
+        for _, groups, m, nl in self.stacks:
+            stack = []
+            for _ in range(nl):
+                layer = []
+                for k, jobs in groups:
+                    x = synth.activations_torch(m, k, gen, device, outliers=True)
+                    q = torch.empty((m, k), dtype=torch.int8, device=device)
+                    s = torch.empty(m, dtype=torch.float32, device=device)
+                    sh = self.shard and all(is_ffn(nm) for nm, _ in jobs)
+                    ws = []
+                    for _, n in jobs:
+                        if sh:
+                            nl_rows = n // self.world
+                            w, sc = synth.weight_torch(n, k, wgen, device)
+                            r0 = self.rank * nl_rows
+                            w, sc = w[r0:r0 + nl_rows].contiguous(), sc[r0:r0 + nl_rows].contiguous()
+                        else:
+                            w, sc = synth.weight_torch(n, k, gen, device)
+                        ws.append((w, sc))
+                    layer.append({"x": x, "q": q, "s": s, "k": k, "w": ws, "shard": sh,
+                                  "n": [n for _, n in jobs]})
+                stack.append(layer)
+            self.L.append(stack)
+            # output buffers (fp32) per group, shared by the stack's layers
+            self.out.append([[torch.empty((m, n), dtype=torch.float32, device=device) for _, n in jobs]
+                             for _, jobs in groups])
+            self.work.append([[torch.empty((m, n), dtype=torch.float32, device=device) for _, n in jobs]
+                              if self.shard and all(is_ffn(nm) for nm, _ in jobs) else None
+                              for _, jobs in groups])
 
     @property
     def kinds(self):
+        if self.shard:
+            return ("quant", "gemm", "gemm_allgather")
         return ("qgemm",) if self.fused else ("quant", "gemm")
 
     def step(self, gcu, stream=None, want=None):
         """Enqueue one step.  `want(kind, bytes, ops)` filters the launches
         (and accounts their algorithmic work) for per-kernel timing."""
-        m = self.m
-        for layer in self.L:
-            for gi, g in enumerate(layer):
-                k = g["k"]
-                if self.fused:
+        for si, (_, _, m, _) in enumerate(self.stacks):
+            for layer in self.L[si]:
+                for gi, g in enumerate(layer):
+                    k = g["k"]
+                    outs = self.out[si][gi]
+                    if g["shard"]:
+                        if want is None or want("quant", 5 * m * k + 4 * m, 0):
+                            gcu.dev_quantize_acts(g["q"], g["s"], g["x"], m, k, stream=stream)
+                        for (w, sc), o, wk in zip(g["w"], outs, self.work[si][gi]):
+                            nl, n = w.shape[0], o.shape[1]
+                            if want is None or want("gemm_allgather", nl * k + 4 * nl + m * k + 4 * m + 4 * m * n,
+                                                    2 * m * nl * k):
+                                gcu.dev_gemm_int8_rowshard(o, wk, w, sc, g["q"], g["s"], m, n, k, stream=stream)
+                        continue
                     nsum = sum(w.shape[0] for w, _ in g["w"])
-                    qb = 5 * m * k + 4 * m
-                    gb = nsum * k + 4 * nsum + m * k + 4 * m + 4 * m * nsum
-                    if want is None or want("qgemm", qb + gb, 2 * m * nsum * k):
-                        gcu.dev_quantize_gemm_int8_multi([(w, sc, o) for (w, sc), o in zip(g["w"], self.out[gi])],
-                                                         g["q"], g["s"], g["x"], m, k, stream=stream)
-                    continue
-                if want is None or want("quant", 5 * m * k + 4 * m, 0):
-                    gcu.dev_quantize_acts(g["q"], g["s"], g["x"], m, k, stream=stream)
-                jobs = [(w, sc, o) for (w, sc), o in zip(g["w"], self.out[gi])]
-                nsum = sum(w.shape[0] for w, _ in g["w"])
-                if want is not None and not want("gemm", nsum * k + 4 * nsum + m * k + 4 * m + 4 * m * nsum,
-                                                 2 * m * nsum * k):
-                    continue
-                if len(jobs) == 1:
-                    w, sc, o = jobs[0]
-                    gcu.dev_gemm_int8(o, w, sc, g["q"], g["s"], m, w.shape[0], k, stream=stream)
-                else:
-                    gcu.dev_gemm_int8_multi(jobs, g["q"], g["s"], m, k, stream=stream)
+                    jobs = [(w, sc, o) for (w, sc), o in zip(g["w"], outs)]
+                    if self.fused:
+                        qb = 5 * m * k + 4 * m
+                        gb = nsum * k + 4 * nsum + m * k + 4 * m + 4 * m * nsum
+                        if want is None or want("qgemm", qb + gb, 2 * m * nsum * k):
+                            gcu.dev_quantize_gemm_int8_multi(jobs, g["q"], g["s"], g["x"], m, k, stream=stream)
+                        continue
+                    if want is None or want("quant", 5 * m * k + 4 * m, 0):
+                        gcu.dev_quantize_acts(g["q"], g["s"], g["x"], m, k, stream=stream)
+                    if want is not None and not want("gemm", nsum * k + 4 * nsum + m * k + 4 * m + 4 * m * nsum,
+                                                     2 * m * nsum * k):
+                        continue
+                    if len(jobs) == 1:
+                        w, sc, o = jobs[0]
+                        gcu.dev_gemm_int8(o, w, sc, g["q"], g["s"], m, w.shape[0], k, stream=stream)
+                    else:
+                        gcu.dev_gemm_int8_multi(jobs, g["q"], g["s"], m, k, stream=stream)
 
-    # the quantize kernel and the GEMM are two launches either way at m > 8
-    launches_per_step = property(lambda self: self.layers * 2 * len(self.groups))
+    @property
+    def launches_per_step(self):
+        n = 0
+        for si, (_, groups, _, nl) in enumerate(self.stacks):
+            for k, jobs in groups:
+                sh = self.shard and all(is_ffn(nm) for nm, _ in jobs)
+                n += nl * ((1 + len(jobs)) if sh else (1 if self.fused else 2))
+        return n
 
     # ---- end to end through the host-pointer ABI --------------------------
     def build_host(self):
-        import numpy as np
         import torch
         self.H = []
-        for layer in self.L:
+        for layer in self.L[-1]:
             hl = []
             for g in layer:
                 x = torch.empty(g["x"].shape, dtype=torch.float32, pin_memory=True)
                 x.copy_(g["x"].cpu())
                 ws = []
                 for w, sc in g["w"]:
-                    wh = w.cpu().numpy()
-                    sh = sc.cpu().numpy()
-                    ws.append((wh, sh))
+                    ws.append((w.cpu().numpy(), sc.cpu().numpy()))
                 hl.append({"x": x.numpy(), "k": g["k"], "w": ws,
                            "q": torch.empty((self.m, g["k"]), dtype=torch.int8, pin_memory=True).numpy(),
                            "s": torch.empty(self.m, dtype=torch.float32, pin_memory=True).numpy()})
@@ -266,20 +333,22 @@ class Prefill:
 
     # ---- CPU reference ---------------------------------------------------------
     def cpu_sample(self, R, layers):
-        """Time `layers` layers of the same calls in the reference's own
+        """Time `layers` layers of every stack with the reference's own
         quantize_acts + gemm_int8 (OpenMP over all threads)."""
         import numpy as np
         import synth
         data = []
-        for li in range(layers):
-            layer = []
-            for gi, (k, jobs) in enumerate(self.groups):
-                x = synth.activations(9000 + 10 * li + gi, self.m, k, outliers=True)
-                ws = [synth.weight(9500 + 10 * li + 3 * gi + j, n, k) for j, (_, n) in enumerate(jobs)]
-                outs = [np.empty((self.m, n), np.float32) for _, n in jobs]
-                layer.append((x, ws, outs))
-            data.append(layer)
-        ops = synth.layer_ops(self.cfg, self.m) * layers
+        ops = 0
+        for si, (_, groups, m, _) in enumerate(self.stacks):
+            for li in range(layers):
+                layer = []
+                for gi, (k, jobs) in enumerate(groups):
+                    x = synth.activations(9000 + 100 * si + 10 * li + gi, m, k, outliers=True)
+                    ws = [synth.weight(9500 + 100 * si + 10 * li + 3 * gi + j, n, k) for j, (_, n) in enumerate(jobs)]
+                    outs = [np.empty((m, n), np.float32) for _, n in jobs]
+                    layer.append((x, ws, outs))
+                data.append(layer)
+            ops += synth.groups_ops(groups, m) * layers
 
         def run():
             for layer in data:
@@ -290,13 +359,28 @@ class Prefill:
         return ops, run
 
 
-class Decode:
-    """Gemma-3-270m decode, batch 1, plus the lm_head."""
-    name = "decode270m"
+DECODE = {
+    # name: (configs index, model, layer count, FFN + lm_head rows sharded)
+    "decode270m": (0, "270m", False),
+    "decode12b": (4, "12b", True),
+}
 
-    def __init__(self, cfg="270m", seed=0, fused=True):
+
+class Decode:
+    """Decode, batch 1 (configs[0], and configs[4]'s decode half): every
+    layer's quantize_act -> Q/K/V, O, gate/up, down GEMVs, then the
+    262144-row lm_head.  Sharded workloads split the FFN and lm_head rows
+    over the ranks with the all-gather fused into the GEMV when the peers are
+    mapped (gcu_dev_gemm_int8_rowshard); Q/K/V/O stay replicated."""
+
+    def __init__(self, name="decode270m", seed=0, fused=True, world=1, rank=0):
         import synth
+        self.name = name
+        self.index, cfg, shard = DECODE[name]
         self.fused = fused
+        self.world, self.rank = world, rank
+        self.shard = shard and world > 1
+        self.needs_comm = self.shard
         self.cfg = synth.CONFIGS[cfg]
         self.groups = synth.layer_groups(self.cfg)
         self.layers = self.cfg["layers"]
@@ -305,49 +389,93 @@ class Decode:
         self.seed = seed
 
     def config(self):
-        return {"workload": "decode270m (configs[0]): Gemma-3-270m W8A8 decode, batch 1, 18 layers + lm_head",
-                "vocab": self.cfg["vocab"], "d_model": self.cfg["dim"],
-                "inputs": "271 MB of weights per token > L2 (no flush)",
-                "calls": "quantize_act->gemv pairs fused into one launch each" if self.fused else
-                         "quantize_act and gemv_int8(_multi) as separate launches"}
+        import gcu
+        c = {"workload": f"{self.name} (configs[{self.index}]): Gemma-3-{self.name[6:]} W8A8 decode, batch 1, "
+                         f"{self.layers} layers + lm_head",
+             "vocab": self.cfg["vocab"], "d_model": self.cfg["dim"],
+             "inputs": f"{self.bytes / 1e6:.0f} MB of weights per token > L2 (no flush)",
+             "calls": "quantize_act->gemv pairs fused into one launch each" if self.fused else
+                      "quantize_act and gemv_int8(_multi) as separate launches"}
+        if self.shard:
+            ag = "fused into the GEMV (NVLink peer loads)" if gcu.comm_fused_allgather() else "NCCL"
+            c["sharding"] = (f"FFN and lm_head rows over {self.world} GPUs, all-gather {ag}; "
+                             "Q/K/V/O replicated (counted once in value)")
+        return c
 
     def build(self, device):
         import torch
         import synth
         gen = torch.Generator(device=device).manual_seed(99 + self.seed)
+        wgen = torch.Generator(device=device).manual_seed(4321)
+
+        def weight(n, k, sharded):
+            if not sharded:
+                return synth.weight_torch(n, k, gen, device)
+            nl = n // self.world
+            w, sc = synth.weight_torch(n, k, wgen, device)
+            r0 = self.rank * nl
+            return w[r0:r0 + nl].contiguous(), sc[r0:r0 + nl].contiguous()
+
         self.L = []
         for _ in range(self.layers):
             layer = []
             for k, jobs in self.groups:
+                sh = self.shard and all(is_ffn(nm) for nm, _ in jobs)
                 layer.append({"x": synth.activations_torch(1, k, gen, device),
                               "q": torch.empty(k, dtype=torch.int8, device=device),
-                              "s": torch.empty(1, dtype=torch.float32, device=device), "k": k,
-                              "w": [synth.weight_torch(n, k, gen, device) for _, n in jobs],
-                              "o": [torch.empty(n, dtype=torch.float32, device=device) for _, n in jobs]})
+                              "s": torch.empty(1, dtype=torch.float32, device=device), "k": k, "shard": sh,
+                              "w": [weight(n, k, sh) for _, n in jobs],
+                              "o": [torch.empty(n, dtype=torch.float32, device=device) for _, n in jobs],
+                              "work": [torch.empty(n, dtype=torch.float32, device=device) for _, n in jobs]
+                              if sh else None})
             self.L.append(layer)
         d = self.cfg["dim"]
         self.head = {"x": synth.activations_torch(1, d, gen, device), "q": torch.empty(d, dtype=torch.int8, device=device),
                      "s": torch.empty(1, dtype=torch.float32, device=device),
-                     "w": synth.weight_torch(self.cfg["vocab"], d, gen, device),
-                     "o": torch.empty(self.cfg["vocab"], dtype=torch.float32, device=device)}
+                     "w": weight(self.cfg["vocab"], d, self.shard),
+                     "o": torch.empty(self.cfg["vocab"], dtype=torch.float32, device=device),
+                     "work": torch.empty(self.cfg["vocab"], dtype=torch.float32, device=device)}
 
     @property
     def kinds(self):
-        return ("qgemv",) if self.fused else ("quant", "gemv")
+        base = ("qgemv",) if self.fused else ("quant", "gemv")
+        if self.shard:
+            return tuple(dict.fromkeys(base + ("quant", "gemv_allgather")))
+        return base
+
+    def _sharded(self, gcu, x, q, s, k, ws, outs, works, stream, want):
+        if want is None or want("quant", 5 * k + 4, 0):
+            gcu.dev_quantize_acts(q, s, x, 1, k, stream=stream)
+        for (w, sc), o, wk in zip(ws, outs, works):
+            nl, n = w.shape[0], o.shape[0]
+            if want is None or want("gemv_allgather", nl * (k + 8) + k + 4 + 4 * n, 2 * nl * k):
+                gcu.dev_gemm_int8_rowshard(o, wk, w, sc, q, s, 1, n, k, stream=stream)
 
     def step(self, gcu, stream=None, want=None):
-        if self.fused:
+        h = self.head
+        d = self.cfg["dim"]
+        n = self.cfg["vocab"]
+        if self.fused or self.shard:
             for layer in self.L:
                 for g in layer:
                     k = g["k"]
+                    if g["shard"]:
+                        self._sharded(gcu, g["x"], g["q"], g["s"], k, g["w"], g["o"], g["work"], stream, want)
+                        continue
                     nsum = sum(w.shape[0] for w, _ in g["w"])
-                    if want is None or want("qgemv", nsum * (k + 8) + 6 * k + 8, 2 * nsum * k):
-                        gcu.dev_quantize_gemm_int8_multi([(w, sc, o) for (w, sc), o in zip(g["w"], g["o"])],
-                                                         g["q"], g["s"], g["x"], 1, k, stream=stream)
-            h = self.head
-            d = self.cfg["dim"]
-            n = self.cfg["vocab"]
-            if want is None or want("qgemv", n * (d + 8) + 6 * d + 8, 2 * n * d):
+                    if self.fused:
+                        if want is None or want("qgemv", nsum * (k + 8) + 6 * k + 8, 2 * nsum * k):
+                            gcu.dev_quantize_gemm_int8_multi([(w, sc, o) for (w, sc), o in zip(g["w"], g["o"])],
+                                                             g["q"], g["s"], g["x"], 1, k, stream=stream)
+                        continue
+                    if want is None or want("quant", 5 * k + 4, 0):
+                        gcu.dev_quantize_acts(g["q"], g["s"], g["x"], 1, k, stream=stream)
+                    if want is None or want("gemv", nsum * (k + 8) + k + 4, 2 * nsum * k):
+                        gcu.dev_gemv_int8_multi([(w, sc, o) for (w, sc), o in zip(g["w"], g["o"])], g["q"],
+                                                g["s"], k, stream=stream)
+            if self.shard:
+                self._sharded(gcu, h["x"], h["q"], h["s"], d, [h["w"]], [h["o"]], [h["work"]], stream, want)
+            elif want is None or want("qgemv", n * (d + 8) + 6 * d + 8, 2 * n * d):
                 gcu.dev_quantize_gemm_int8_multi([(h["w"][0], h["w"][1], h["o"])], h["q"], h["s"], h["x"], 1, d,
                                                  stream=stream)
             return
@@ -360,15 +488,22 @@ class Decode:
                 if want is None or want("gemv", nsum * (k + 8) + k + 4, 2 * nsum * k):
                     gcu.dev_gemv_int8_multi([(w, sc, o) for (w, sc), o in zip(g["w"], g["o"])], g["q"], g["s"],
                                             k, stream=stream)
-        h = self.head
-        d = self.cfg["dim"]
-        n = self.cfg["vocab"]
         if want is None or want("quant", 5 * d + 4, 0):
             gcu.dev_quantize_acts(h["q"], h["s"], h["x"], 1, d, stream=stream)
         if want is None or want("gemv", n * (d + 8) + d + 4, 2 * n * d):
             gcu.dev_gemv_int8(h["o"], h["w"][0], h["w"][1], h["q"], h["s"], n, d, stream=stream)
 
-    launches_per_step = property(lambda self: (self.layers * len(self.groups) + 1) * (1 if self.fused else 2))
+    @property
+    def launches_per_step(self):
+        if not self.shard:
+            return (self.layers * len(self.groups) + 1) * (1 if self.fused else 2)
+        n = 2  # lm_head: quantize + sharded GEMV
+        for k, jobs in self.groups:
+            if all(is_ffn(nm) for nm, _ in jobs):
+                n += self.layers * (1 + len(jobs))
+            else:
+                n += self.layers * (1 if self.fused else 2)
+        return n
 
 
 class LmHead:
@@ -377,6 +512,7 @@ class LmHead:
 
     def __init__(self, world, rank, vocab=262144, dim=2560, batch=1):
         self.world, self.rank = world, rank
+        self.needs_comm = world > 1
         self.n, self.k, self.b = vocab, dim, batch
         self.bytes = vocab * (dim + 4) + batch * (dim + 4) + 4 * batch * vocab
 
@@ -431,20 +567,20 @@ def run_ours(args):
     import gcu
     gcu.init(local)
     peaks = load_peaks()
-    if args.workload == "prefill1b":
-        wl = Prefill(seed=rank, fused=args.fused)
-    elif args.workload == "decode270m":
-        wl = Decode(seed=rank, fused=not args.unfused)
+    if args.workload in PREFILL:
+        wl = Prefill(args.workload, seed=rank, fused=args.fused, world=world, rank=rank)
+    elif args.workload in DECODE:
+        wl = Decode(args.workload, seed=rank, fused=not args.unfused, world=world, rank=rank)
     else:
         wl = LmHead(world, rank)
-        if world > 1:
-            uid = bytearray(128)
-            if rank == 0:
-                uid = bytearray(gcu.comm_unique_id())
-            import torch.distributed as dist
-            obj = [bytes(uid)]
-            dist.broadcast_object_list(obj, src=0)
-            gcu.comm_init(rank, world, obj[0])
+    if wl.needs_comm:
+        uid = bytearray(128)
+        if rank == 0:
+            uid = bytearray(gcu.comm_unique_id())
+        import torch.distributed as dist
+        obj = [bytes(uid)]
+        dist.broadcast_object_list(obj, src=0)
+        gcu.comm_init(rank, world, obj[0])
     wl.build(device)
     torch.cuda.synchronize()
 
@@ -455,9 +591,10 @@ def run_ours(args):
     stream.synchronize()
     gcu.check_device()
 
-    # the sharded lm_head is graph-captured when its all-gather is the fused
-    # peer-store kernel (no NCCL call inside the step)
-    use_graph = not (isinstance(wl, LmHead) and world > 1 and not gcu.comm_fused_allgather())
+    # a sharded step is graph-captured only when every all-gather is the fused
+    # peer-load GEMV (no NCCL call inside the step): sharded decode with the
+    # peers mapped, never sharded prefill (m > 8 all-gathers through NCCL)
+    use_graph = not wl.needs_comm or (not isinstance(wl, Prefill) and gcu.comm_fused_allgather())
     graph = None
     if use_graph:
         graph = torch.cuda.CUDAGraph()
@@ -534,16 +671,20 @@ def run_ours(args):
            "ms_per_step": ms, "higher_is_better": True, "vs_baseline": None, "data": "synthetic",
            "impl": "ours"}
     int8_peak = 2.0 * peaks["bf16_tflops"]
+    # replicas: every rank runs the whole workload (weak scaling, value sums
+    # them); sharded: the ranks share one workload (strong scaling)
+    copies = 1 if wl.needs_comm else world
+    par = (f"row-shard x{world}" if wl.needs_comm else f"replicas x{world}") if world > 1 else "single GPU"
     if isinstance(wl, Prefill):
-        out.update(value=wl.ops * world / (ms * 1e-3) / 1e12, unit="int8 TOPS", dtype="int8 (int32 accum, fp32 out)",
-                   scaling="weak")
+        out.update(value=wl.ops * copies / (ms * 1e-3) / 1e12, unit="int8 TOPS",
+                   dtype="int8 (int32 accum, fp32 out)", scaling="strong" if wl.needs_comm else "weak")
         cfg = wl.config()
-        cfg.update(parallelism=f"replicas x{world}" if world > 1 else "single GPU")
+        cfg.update(parallelism=par)
     elif isinstance(wl, Decode):
-        out.update(value=wl.bytes * world / (ms * 1e-3) / 1e9, unit="GB/s", dtype="int8 (int32 accum, fp32 out)",
-                   scaling="weak")
+        out.update(value=wl.bytes * copies / (ms * 1e-3) / 1e9, unit="GB/s", dtype="int8 (int32 accum, fp32 out)",
+                   scaling="strong" if wl.needs_comm else "weak")
         cfg = wl.config()
-        cfg.update(parallelism=f"replicas x{world}" if world > 1 else "single GPU")
+        cfg.update(parallelism=par)
     else:
         out.update(value=wl.bytes / (ms * 1e-3) / 1e9, unit="GB/s", dtype="int8 (int32 accum, fp32 out)",
                    scaling="strong")
@@ -580,7 +721,7 @@ def run_ours(args):
                               "avg_us": v["ms"] * 1e3 / v["launches"]} for k, v in prof.items()}
 
     # end to end through the host-pointer ABI
-    if isinstance(wl, Prefill) and not args.no_e2e:
+    if isinstance(wl, Prefill) and wl.name == "prefill1b" and not args.no_e2e:
         wl.build_host()
         wl.register_host(gcu)
         wl.step_host(gcu)  # warm-up
@@ -599,12 +740,12 @@ def run_ours(args):
                               "pinned host activations, wall clock around synchronous calls"}
 
     # CPU baseline on rank 0 at N=1 (bounded sample)
-    if world == 1 and not args.no_cpu and isinstance(wl, Prefill):
+    if world == 1 and not args.no_cpu and isinstance(wl, Prefill) and wl.name == "prefill1b":
         out["cpu_baseline"] = cpu_baseline(wl, args.cpu_seconds)
 
     if graph is not None:
         del graph
-    if isinstance(wl, LmHead) and world > 1:
+    if wl.needs_comm:
         gcu.comm_destroy()
     if rank == 0:
         print(json.dumps(out), flush=True)
@@ -683,7 +824,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="prefill1b", choices=["prefill1b", "decode270m", "lmhead4b"])
+    ap.add_argument("--workload", default="prefill1b", choices=list(PREFILL) + list(DECODE) + ["lmhead4b"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--unfused", action="store_true",
                     help="decode: quantize and GEMV as separate launches (the reference's call split)")

@@ -112,9 +112,19 @@ struct DevBuf {
   }
 };
 
+// Host entry points that move several MB split their rows into chunks and
+// pipeline them: chunk i's host->device copy (stream s_in), its kernel
+// (stream), and its device->host copy (s_out) overlap chunk i+1's, so the
+// two PCIe directions and the GPU work at the same time.
+constexpr int kMaxChunks = 4;
+constexpr size_t kChunkMinBytes = 4u << 20;  // smaller transfers go in one piece
+
 struct ThreadCtx {
   int device = -1;
-  cudaStream_t stream = nullptr;
+  cudaStream_t stream = nullptr;  // kernels (and everything of unchunked calls)
+  cudaStream_t s_in = nullptr, s_out = nullptr;
+  cudaEvent_t ev_in[kMaxChunks] = {}, ev_done[kMaxChunks] = {};
+  unsigned int *h_err = nullptr;  // pinned landing slot of the device error word
   DevBuf in, in2, out, sc, sc2, wtmp, wstmp;
   ~ThreadCtx() {
     // process teardown may already have unloaded the driver: leak quietly
@@ -128,10 +138,31 @@ static int ctx(ThreadCtx **out) {
   if (c.device != d || c.stream == nullptr) {
     GCU_CUDA(cudaSetDevice(d));
     GCU_CUDA(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking));
+    GCU_CUDA(cudaStreamCreateWithFlags(&c.s_in, cudaStreamNonBlocking));
+    GCU_CUDA(cudaStreamCreateWithFlags(&c.s_out, cudaStreamNonBlocking));
+    for (int i = 0; i < kMaxChunks; ++i) {
+      GCU_CUDA(cudaEventCreateWithFlags(&c.ev_in[i], cudaEventDisableTiming));
+      GCU_CUDA(cudaEventCreateWithFlags(&c.ev_done[i], cudaEventDisableTiming));
+    }
+    GCU_CUDA(cudaHostAlloc(reinterpret_cast<void **>(&c.h_err), sizeof(unsigned int),
+                           cudaHostAllocDefault));
     c.device = d;
   }
   *out = &c;
   return 0;
+}
+
+// Rows per pipeline chunk for a call moving `bytes_per_row` bytes per row in
+// its larger direction: one chunk below kChunkMinBytes, else up to
+// kMaxChunks chunks, rounded up to a multiple of `align` rows.
+static int chunk_rows(int m, size_t bytes_per_row, int align) {
+  const size_t total = (size_t)m * bytes_per_row;
+  if (total < kChunkMinBytes || m < 2 * align) return m;
+  size_t chunks = total / (kChunkMinBytes / 4);
+  if (chunks > (size_t)kMaxChunks) chunks = kMaxChunks;
+  int rows = (int)((m + chunks - 1) / chunks);
+  rows = (rows + align - 1) / align * align;
+  return rows < m ? rows : m;
 }
 
 // ---------------------------------------------------------------------------
@@ -241,20 +272,25 @@ static int scales_dev(ThreadCtx *c, DevBuf &buf, const float *host, size_t count
   return 0;
 }
 
-static int sync_and_check(ThreadCtx *c) {
-  GCU_CUDA(cudaStreamSynchronize(c->stream));
+// Wait for `st`, the last stream of a host call, and report a device-side
+// error word set by its kernels.  The word is read back on `st` itself, so
+// the wait covers it (no extra synchronous copy).
+static int sync_and_check(ThreadCtx *c, cudaStream_t st) {
   unsigned int *ew = dev_error_word();
-  unsigned int code = 0;
   if (ew) {
-    GCU_CUDA(cudaMemcpy(&code, ew, sizeof(code), cudaMemcpyDeviceToHost));
-    if (code) {
-      unsigned int zero = 0;
-      cudaMemcpy(ew, &zero, sizeof(zero), cudaMemcpyHostToDevice);
-      return set_error("device-side wait gave up (code %u)", code);
-    }
+    *c->h_err = 0;
+    GCU_CUDA(cudaMemcpyAsync(c->h_err, ew, sizeof(unsigned int), cudaMemcpyDeviceToHost, st));
+  }
+  GCU_CUDA(cudaStreamSynchronize(st));
+  const unsigned int code = ew ? *c->h_err : 0u;
+  if (code) {
+    unsigned int zero = 0;
+    cudaMemcpy(ew, &zero, sizeof(zero), cudaMemcpyHostToDevice);
+    return set_error("device-side wait gave up (code %u)", code);
   }
   return 0;
 }
+static int sync_and_check(ThreadCtx *c) { return sync_and_check(c, c->stream); }
 
 static inline cudaStream_t as_stream(void *s) { return static_cast<cudaStream_t>(s); }
 
@@ -391,8 +427,18 @@ GCU_EXPORT int gcu_shutdown(void) {
   c.sc2.release();
   c.wtmp.release();
   c.wstmp.release();
-  if (c.stream) cudaStreamDestroy(c.stream);
-  c.stream = nullptr;
+  if (c.stream) {
+    cudaStreamDestroy(c.stream);
+    cudaStreamDestroy(c.s_in);
+    cudaStreamDestroy(c.s_out);
+    for (int i = 0; i < kMaxChunks; ++i) {
+      cudaEventDestroy(c.ev_in[i]);
+      cudaEventDestroy(c.ev_done[i]);
+    }
+    cudaFreeHost(c.h_err);
+  }
+  c.stream = c.s_in = c.s_out = nullptr;
+  c.h_err = nullptr;
   c.device = -1;
   return 0;
 }
@@ -412,13 +458,31 @@ GCU_EXPORT int gcu_quantize_acts(int8_t *dst, float *dsc, const float *src, int 
   if (c->in.get(in_elems * 4, &din) || c->out.get((size_t)m * n, &dout) ||
       c->sc.get((size_t)m * 4, &dsc_d))
     return 1;
-  GCU_CUDA(cudaMemcpyAsync(din, src, in_elems * 4, cudaMemcpyHostToDevice, c->stream));
-  if (launch_quantize_rows((int8_t *)dout, (float *)dsc_d, (const float *)din, sstr, m, n,
-                           c->stream))
-    return 1;
-  GCU_CUDA(cudaMemcpyAsync(dst, dout, (size_t)m * n, cudaMemcpyDeviceToHost, c->stream));
-  GCU_CUDA(cudaMemcpyAsync(dsc, dsc_d, (size_t)m * 4, cudaMemcpyDeviceToHost, c->stream));
-  GCU_CUDA(cudaStreamSynchronize(c->stream));
+  const int rows = chunk_rows(m, (size_t)sstr * 4, 1);
+  const bool piped = rows < m;
+  cudaStream_t s_in = piped ? c->s_in : c->stream, s_out = piped ? c->s_out : c->stream;
+  for (int r0 = 0, i = 0; r0 < m; r0 += rows, ++i) {
+    const int mr = m - r0 < rows ? m - r0 : rows;
+    const size_t off = (size_t)r0 * sstr;
+    const size_t elems = (size_t)(mr - 1) * sstr + n;
+    GCU_CUDA(cudaMemcpyAsync((float *)din + off, src + off, elems * 4, cudaMemcpyHostToDevice, s_in));
+    if (piped) {
+      GCU_CUDA(cudaEventRecord(c->ev_in[i], s_in));
+      GCU_CUDA(cudaStreamWaitEvent(c->stream, c->ev_in[i], 0));
+    }
+    if (launch_quantize_rows((int8_t *)dout + (size_t)r0 * n, (float *)dsc_d + r0,
+                             (const float *)din + off, sstr, mr, n, c->stream))
+      return 1;
+    if (piped) {
+      GCU_CUDA(cudaEventRecord(c->ev_done[i], c->stream));
+      GCU_CUDA(cudaStreamWaitEvent(s_out, c->ev_done[i], 0));
+    }
+    GCU_CUDA(cudaMemcpyAsync(dst + (size_t)r0 * n, (int8_t *)dout + (size_t)r0 * n, (size_t)mr * n,
+                             cudaMemcpyDeviceToHost, s_out));
+    GCU_CUDA(cudaMemcpyAsync(dsc + r0, (float *)dsc_d + r0, (size_t)mr * 4, cudaMemcpyDeviceToHost,
+                             s_out));
+  }
+  GCU_CUDA(cudaStreamSynchronize(s_out));
   return 0;
 }
 
@@ -521,8 +585,14 @@ GCU_EXPORT int gcu_gemm_int8(float *dst, int dstr, const int8_t *mat, int mstr,
   if (c->in.get((size_t)m * k16, &dsrc) || c->sc.get((size_t)m * 4, &dssc) ||
       c->out.get((size_t)m * n4 * 4, &dout))
     return 1;
-  GCU_CUDA(cudaMemcpy2DAsync(dsrc, k16, src, sstr, k, m, cudaMemcpyHostToDevice, c->stream));
-  GCU_CUDA(cudaMemcpyAsync(dssc, ssc, (size_t)m * 4, cudaMemcpyHostToDevice, c->stream));
+  // row chunks of whole 128-row tiles when the output is large: chunk i's
+  // output copy overlaps the GEMM and input copy of chunk i+1
+  const int rows = m <= 8 ? m : chunk_rows(m, (size_t)n * 4, 128);
+  const bool piped = rows < m;
+  if (!piped) {
+    GCU_CUDA(cudaMemcpy2DAsync(dsrc, k16, src, sstr, k, m, cudaMemcpyHostToDevice, c->stream));
+    GCU_CUDA(cudaMemcpyAsync(dssc, ssc, (size_t)m * 4, cudaMemcpyHostToDevice, c->stream));
+  }
   // weights: registered copy if the whole strided range is inside one
   const size_t wbytes = (size_t)(n - 1) * mstr + k;
   const void *dmat = lookup_q(mat, wbytes);
@@ -551,15 +621,35 @@ GCU_EXPORT int gcu_gemm_int8(float *dst, int dstr, const int8_t *mat, int mstr,
     if (dev_gemm((float *)dout, n4, (const int8_t *)dmat, dmstr, dms, (const int8_t *)dsrc, k16,
                  (const float *)dssc, m, n, k, c->stream))
       return 1;
-  } else {
-    if (k16 != k && dmstr % 16 != 0) return set_error("gemm_int8: internal stride error");
-    GemmArgs a{(float *)dout, n4, (const int8_t *)dmat, dmstr, dms,
-               (const int8_t *)dsrc, k16, (const float *)dssc, m, n, k};
-    if (launch_gemm_tc(a, c->stream, 0, 0)) return 1;
+    GCU_CUDA(cudaMemcpy2DAsync(dst, (size_t)dstr * 4, dout, (size_t)n4 * 4, (size_t)n * 4, m,
+                               cudaMemcpyDeviceToHost, c->stream));
+    return sync_and_check(c);
   }
-  GCU_CUDA(cudaMemcpy2DAsync(dst, (size_t)dstr * 4, dout, (size_t)n4 * 4, (size_t)n * 4, m,
-                             cudaMemcpyDeviceToHost, c->stream));
-  return sync_and_check(c);
+  if (k16 != k && dmstr % 16 != 0) return set_error("gemm_int8: internal stride error");
+  cudaStream_t s_out = piped ? c->s_out : c->stream;
+  for (int r0 = 0, i = 0; r0 < m; r0 += rows, ++i) {
+    const int mr = m - r0 < rows ? m - r0 : rows;
+    if (piped) {
+      // this chunk's activation rows, on the input stream
+      GCU_CUDA(cudaMemcpy2DAsync((int8_t *)dsrc + (size_t)r0 * k16, k16, src + (size_t)r0 * sstr,
+                                 sstr, k, mr, cudaMemcpyHostToDevice, c->s_in));
+      GCU_CUDA(cudaMemcpyAsync((float *)dssc + r0, ssc + r0, (size_t)mr * 4,
+                               cudaMemcpyHostToDevice, c->s_in));
+      GCU_CUDA(cudaEventRecord(c->ev_in[i], c->s_in));
+      GCU_CUDA(cudaStreamWaitEvent(c->stream, c->ev_in[i], 0));
+    }
+    GemmArgs a{(float *)dout + (size_t)r0 * n4, n4, (const int8_t *)dmat, dmstr, dms,
+               (const int8_t *)dsrc + (size_t)r0 * k16, k16, (const float *)dssc + r0, mr, n, k};
+    if (launch_gemm_tc(a, c->stream, 0, 0)) return 1;
+    if (piped) {
+      GCU_CUDA(cudaEventRecord(c->ev_done[i], c->stream));
+      GCU_CUDA(cudaStreamWaitEvent(s_out, c->ev_done[i], 0));
+    }
+    GCU_CUDA(cudaMemcpy2DAsync(dst + (size_t)r0 * dstr, (size_t)dstr * 4,
+                               (float *)dout + (size_t)r0 * n4, (size_t)n4 * 4, (size_t)n * 4, mr,
+                               cudaMemcpyDeviceToHost, s_out));
+  }
+  return sync_and_check(c, s_out);
 }
 
 // ---- device-pointer entry points ---------------------------------------------

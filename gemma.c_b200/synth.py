@@ -134,8 +134,29 @@ def layer_groups(cfg: dict):
     ]
 
 
+def vision_layer_groups(cfg: dict):
+    """The W8A8 calls of one SigLIP encoder layer (gemma.c:4497-4633): Q/K/V
+    share one quantized input, then O, fc1 and fc2 (an ungated MLP)."""
+    d, f = cfg["dim"], cfg["ffn"]
+    return [
+        (d, [("wq", d), ("wk", d), ("wv", d)]),
+        (d, [("wo", d)]),
+        (d, [("w1_fc1", f)]),
+        (f, [("w2_fc2", d)]),
+    ]
+
+
+def projector_groups(vision: dict, text: dict):
+    """The image-token projection into the text stream (gemma.c:4714-4716)."""
+    return [(vision["dim"], [("proj", text["dim"])])]
+
+
+def groups_ops(groups, m: int) -> int:
+    return sum(2 * m * n * k for k, jobs in groups for _, n in jobs)
+
+
 def layer_ops(cfg: dict, m: int) -> int:
-    return sum(2 * m * n * k for k, jobs in layer_groups(cfg) for _, n in jobs)
+    return groups_ops(layer_groups(cfg), m)
 
 
 def layer_weight_bytes(cfg: dict) -> int:

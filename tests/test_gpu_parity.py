@@ -69,11 +69,22 @@ def test_quantize_golden(golden):
 
 
 @pytest.mark.parametrize("m,k", [(1, 640), (1, 15360), (4, 1152), (64, 2560), (37, 6912), (3, 33),
-                                 (2, 40000), (512, 1024)])
+                                 (2, 40000), (512, 1024), (700, 2048), (509, 6912)])
 def test_quantize_random(m, k):
     x = synth.activations(1000 + k + m, m, k, outliers=True)
     q, s = gcu.quantize_acts(x)
     q0, s0 = O.quantize_acts(x)
+    assert np.array_equal(q, q0)
+    assert_bits(s, s0)
+
+
+def test_quantize_host_strided_pipelined():
+    # > 4 MB of input: the host call copies, quantizes and copies back in row
+    # chunks on separate streams; rows are read at a stride of 2053 floats
+    m, n, sstr = 611, 2000, 2053
+    full = synth.activations(1500, m, sstr, outliers=True)
+    q, s = gcu.quantize_acts(full, n=n, sstr=sstr)
+    q0, s0 = O.quantize_acts(np.ascontiguousarray(full[:, :n]))
     assert np.array_equal(q, q0)
     assert_bits(s, s0)
 
@@ -168,6 +179,22 @@ def test_gemm_random(m, n, k):
     finally:
         gcu.unregister_weight(w)
     assert_bits(y, O.gemm_int8(w, ws, xq, xs))
+
+
+@pytest.mark.parametrize("m,n,k,pad", [(600, 2500, 640, 0), (300, 4000, 640, 5), (129, 9000, 128, 3)])
+def test_gemm_host_pipelined(m, n, k, pad):
+    # > 4 MB of output: the host call runs 128-row chunks whose copies overlap
+    # the GEMM of the next chunk; a padded dst stride keeps the gaps untouched
+    w, ws = synth.weight(5600 + n, n, k)
+    xq, xs = O.quantize_acts(synth.activations(5700 + m, m, k, outliers=True))
+    dst = np.full((m, n + pad), -7.0, np.float32)
+    gcu.register_weight(w, ws)
+    try:
+        gcu.gemm_int8(w.reshape(-1), ws, xq.reshape(-1), xs, dst=dst, dstr=n + pad, m=m, n=n, k=k)
+    finally:
+        gcu.unregister_weight(w)
+    assert_bits(dst[:, :n], O.gemm_int8(w, ws, xq, xs))
+    assert (dst[:, n:] == -7.0).all()
 
 
 def test_gemm_prefill_qkv_head_blocks():
@@ -311,6 +338,41 @@ def test_full_size_gemm_sampled_rows():
     assert np.array_equal(q[rows].cpu().numpy(), xq)
     ref = O.gemm_int8(w.cpu().numpy(), ws.cpu().numpy(), xq, xs)
     assert_bits(y[rows].cpu().numpy(), ref)
+
+
+# every distinct GEMM of BASELINE configs[3] (Gemma-3-4B text at M=2048 and
+# the SigLIP-So400m tower at M=4096, projector at M=256) and configs[4]
+# (Gemma-3-12B at M=4096, FFN row slices of 2/4/8 GPUs), at full size
+FULL_SHAPES = [
+    (2048, (2048, 1024, 1024), 2560), (2048, (2560,), 2048), (2048, (10240, 10240), 2560),
+    (2048, (2560,), 10240),
+    (4096, (1152, 1152, 1152), 1152), (4096, (1152,), 1152), (4096, (4304,), 1152), (4096, (1152,), 4304),
+    (256, (2560,), 1152),
+    (4096, (4096, 2048, 2048), 3840), (4096, (3840,), 4096), (4096, (15360, 15360), 3840),
+    (4096, (3840,), 15360),
+    (4096, (7680, 7680), 3840), (4096, (1920, 1920), 3840), (4096, (1920,), 15360), (4096, (480,), 15360),
+]
+
+
+@pytest.mark.parametrize("m,ns,k", FULL_SHAPES)
+def test_full_size_config_shapes_sampled_rows(m, ns, k):
+    # the quantize kernel and one multi-weight launch at full size; the oracle
+    # recomputes a seeded sample of rows of every output
+    gen = torch.Generator(device="cuda").manual_seed(m + k + sum(ns))
+    ws_t = [synth.weight_torch(n, k, gen, "cuda") for n in ns]
+    x = synth.activations_torch(m, k, gen, "cuda", outliers=True)
+    q = torch.empty((m, k), dtype=torch.int8, device="cuda")
+    s = torch.empty(m, dtype=torch.float32, device="cuda")
+    ys = [torch.empty((m, n), dtype=torch.float32, device="cuda") for n in ns]
+    gcu.dev_quantize_gemm_int8_multi([(w, sc, y) for (w, sc), y in zip(ws_t, ys)], q, s, x, m, k)
+    torch.cuda.synchronize()
+    gcu.check_device()
+    rows = np.sort(np.random.default_rng(m + k).choice(m, 8, replace=False))
+    xq, xs = O.quantize_acts(x[rows].cpu().numpy())
+    assert np.array_equal(q[rows].cpu().numpy(), xq)
+    assert_bits(s[rows].cpu().numpy(), xs)
+    for (w, sc), y in zip(ws_t, ys):
+        assert_bits(y[rows].cpu().numpy(), O.gemm_int8(w.cpu().numpy(), sc.cpu().numpy(), xq, xs))
 
 
 def test_scale_linearity_property():
