@@ -181,10 +181,11 @@ int launch_quantize_rows(int8_t *dst, float *dsc, const float *src, long sstr,
                    ((uintptr_t)dst % 4 == 0);
   const int n4 = n / 4;
   if (vec && n4 <= 8 * 32 * 16) {
-    // fewest warps per row that hold the row in 16 float4 per lane, then more
+    // fewest warps per row that hold the row in 8 float4 per lane (16 past
+    // 8192 elements; fewer registers keep more CTAs resident), then more
     // while the grid is under two CTAs per SM and each lane keeps >= 2 loads
     int wpr = 1;
-    while (wpr < 8 && n4 > 32 * 16 * wpr) wpr *= 2;
+    while (wpr < 8 && n4 > 32 * 8 * wpr) wpr *= 2;
     const int sms = num_sms();
     while (wpr < 8 && (long)m * wpr < 16L * sms && n4 >= 32 * 2 * (2 * wpr)) wpr *= 2;
     const int need = (n4 + 32 * wpr - 1) / (32 * wpr);
