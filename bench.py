@@ -440,16 +440,17 @@ class Decode:
     def kinds(self):
         base = ("qgemv",) if self.fused else ("quant", "gemv")
         if self.shard:
-            return tuple(dict.fromkeys(base + ("quant", "gemv_allgather")))
+            return base + ("qgemv_allgather",)
         return base
 
     def _sharded(self, gcu, x, q, s, k, ws, outs, works, stream, want):
-        if want is None or want("quant", 5 * k + 4, 0):
-            gcu.dev_quantize_acts(q, s, x, 1, k, stream=stream)
-        for (w, sc), o, wk in zip(ws, outs, works):
-            nl, n = w.shape[0], o.shape[0]
-            if want is None or want("gemv_allgather", nl * (k + 8) + k + 4 + 4 * n, 2 * nl * k):
-                gcu.dev_gemm_int8_rowshard(o, wk, w, sc, q, s, 1, n, k, stream=stream)
+        # quantize + every sharded weight of the group + their all-gathers:
+        # one launch when the peers are mapped
+        nl = sum(w.shape[0] for w, _ in ws)
+        n = sum(o.shape[0] for o in outs)
+        if want is None or want("qgemv_allgather", nl * (k + 8) + 6 * k + 8 + 4 * n, 2 * nl * k):
+            gcu.dev_quantize_gemm_int8_rowshard_multi([(w, sc, o, o.shape[0]) for (w, sc), o in zip(ws, outs)],
+                                                      q, s, x, 1, k, work=works[0], stream=stream)
 
     def step(self, gcu, stream=None, want=None):
         h = self.head
@@ -497,10 +498,10 @@ class Decode:
     def launches_per_step(self):
         if not self.shard:
             return (self.layers * len(self.groups) + 1) * (1 if self.fused else 2)
-        n = 2  # lm_head: quantize + sharded GEMV
+        n = 1  # lm_head: one fused quantize + sharded GEMV
         for k, jobs in self.groups:
             if all(is_ffn(nm) for nm, _ in jobs):
-                n += self.layers * (1 + len(jobs))
+                n += self.layers
             else:
                 n += self.layers * (1 if self.fused else 2)
         return n

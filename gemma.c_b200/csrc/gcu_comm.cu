@@ -215,6 +215,23 @@ GCU_EXPORT int gcu_comm_destroy(void) {
   return 0;
 }
 
+// The fused all-gather's view of this rank's symmetric buffer and flags.
+static PeerOut peer_out(int m) {
+  PeerOut po{};
+  for (int p = 0; p < g_comm.world; ++p) {
+    po.delta[p] = (long long)((char *)g_comm.peer_sym[p] - (char *)g_comm.sym);
+    po.flag_peer[p] = g_comm.peer_flags[p];
+  }
+  po.flag_local = g_comm.flags;
+  po.sym = g_comm.sym;
+  po.half_elems = (long)(kSymHalf / sizeof(float));
+  po.mb = m;
+  po.rank = g_comm.rank;
+  po.world = g_comm.world;
+  po.err = dev_error_word();
+  return po;
+}
+
 GCU_EXPORT int gcu_dev_gemm_int8_rowshard(float *dst, float *work, const int8_t *mat_local,
                                           const float *matsc_local, const int8_t *src,
                                           const float *ssc, int m, int n, int k, void *stream) {
@@ -226,28 +243,18 @@ GCU_EXPORT int gcu_dev_gemm_int8_rowshard(float *dst, float *work, const int8_t 
   const int nl = n / world;
   if (m <= 8 && g_comm.p2p && (size_t)m * n * sizeof(float) <= kSymHalf && nl % 4 == 0 &&
       (uintptr_t)dst % 16 == 0) {
-    // GEMV with the all-gather fused into its epilogue (peer stores)
+    // GEMV with the all-gather fused into it (NVLink loads from the peers)
     GemvJobs J{};
     J.w[0] = mat_local;
     J.ws[0] = matsc_local;
-    J.y[0] = g_comm.sym + (size_t)rank * nl;  // column offset of this rank's slice
     J.row_end[0] = nl;
     J.njobs = 1;
-    PeerOut po{};
-    for (int p = 0; p < world; ++p) {
-      po.delta[p] = (long long)((char *)g_comm.peer_sym[p] - (char *)g_comm.sym);
-      po.flag_peer[p] = g_comm.peer_flags[p];
-    }
-    po.flag_local = g_comm.flags;
-    po.sym = g_comm.sym;
-    po.half_elems = (long)(kSymHalf / sizeof(float));
-    po.dst = dst;
-    po.count = (long)m * n;
-    po.n = n;
-    po.n_local = nl;
-    po.err = dev_error_word();
-    po.world = world;
-    return launch_gemv_p2p(J, src, k, ssc, m, n, k, po, st);
+    PeerOut po = peer_out(m);
+    po.njobs = 1;
+    po.n[0] = n;
+    po.n_local[0] = nl;
+    po.dst[0] = dst;
+    return launch_gemv_p2p(J, src, k, ssc, nullptr, nullptr, nullptr, m, k, po, st);
   }
   // this rank's (m, nl) block, at its slot of the gather buffer
   float *mine = (m == 1 ? dst : work) + (size_t)rank * m * nl;
@@ -272,5 +279,57 @@ GCU_EXPORT int gcu_dev_gemm_int8_rowshard(float *dst, float *work, const int8_t 
       GCU_CUDA(cudaMemcpy2DAsync(dst + (size_t)g * nl, (size_t)n * 4, work + (size_t)g * m * nl,
                                  (size_t)nl * 4, (size_t)nl * 4, m, cudaMemcpyDeviceToDevice, st));
   }
+  return 0;
+}
+
+GCU_EXPORT int gcu_dev_quantize_gemm_int8_rowshard_multi(const gcu_gemv_job *jobs, int njobs,
+                                                         int8_t *q, float *s, const float *x,
+                                                         int xstr, int m, int k, float *work,
+                                                         void *stream) {
+  if (!g_comm.comm) return set_error("gcu_dev_quantize_gemm_int8_rowshard_multi: gcu_comm_init first");
+  if (njobs < 1 || njobs > GCU_MAX_JOBS)
+    return set_error("quantize_gemm_rowshard_multi: 1..%d jobs (got %d)", GCU_MAX_JOBS, njobs);
+  if (m <= 0) return 0;
+  if (k <= 0) return set_error("quantize_gemm_rowshard_multi: k must be positive (got %d)", k);
+  if (xstr == 0) xstr = k;
+  const int world = g_comm.world;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  size_t total = 0;
+  bool fused = m <= 8 && g_comm.p2p && k % 16 == 0;
+  for (int j = 0; j < njobs; ++j) {
+    const int n = jobs[j].m;
+    if (n <= 0 || n % world) return set_error("quantize_gemm_rowshard_multi: job %d rows %d not a positive "
+                                              "multiple of world %d", j, n, world);
+    total += (size_t)m * n * sizeof(float);
+    fused = fused && (n / world) % 4 == 0 && (uintptr_t)jobs[j].dst % 16 == 0;
+  }
+  fused = fused && total <= kSymHalf;
+  if (fused) {
+    GemvJobs J{};
+    PeerOut po = peer_out(m);
+    long off = 0;
+    int rows = 0;
+    for (int j = 0; j < njobs; ++j) {
+      const int n = jobs[j].m, nl = n / world;
+      J.w[j] = static_cast<const int8_t *>(jobs[j].w);
+      J.ws[j] = jobs[j].sc;
+      rows += nl;
+      J.row_end[j] = rows;
+      po.off[j] = off;
+      po.n[j] = n;
+      po.n_local[j] = nl;
+      po.dst[j] = jobs[j].dst;
+      off += (long)m * n;
+    }
+    J.njobs = njobs;
+    po.njobs = njobs;
+    return launch_gemv_p2p(J, nullptr, xstr, nullptr, x, q, s, m, k, po, st);
+  }
+  // quantize once, then every job through the row-shard entry point
+  if (launch_quantize_rows(q, s, x, xstr, m, k, st)) return 1;
+  for (int j = 0; j < njobs; ++j)
+    if (gcu_dev_gemm_int8_rowshard(jobs[j].dst, work, static_cast<const int8_t *>(jobs[j].w), jobs[j].sc,
+                                   q, s, m, jobs[j].m, k, stream))
+      return 1;
   return 0;
 }

@@ -85,29 +85,35 @@ int launch_gemv(const GemvJobs &jobs, const int8_t *x, long xstride,
                 const float *xs, int mb, long ystride, int k,
                 cudaStream_t st);
 
-// Row-sharded GEMV whose epilogue is the all-gather.  Each rank writes its
-// output slice into half (epoch & 1) of its own symmetric buffer; the last
-// CTA of the grid then signals every rank ("slice ready") and waits,
-// bounded, until all ranks have signalled for this launch; then all CTAs
-// pull every rank's slice over NVLink (16-byte loads from the peers' CUDA
-// IPC mappings) straight into the caller's dst.  The halves alternate by a
-// device-side launch epoch: a rank one launch ahead writes the other half,
-// and it cannot get two ahead before this rank has finished pulling.
+// Row-sharded GEMV whose epilogue is the all-gather.  Every rank holds a
+// symmetric buffer (two halves, mapped by every peer through CUDA IPC) laid
+// out identically: job j's (mb, n_j) output at float offset off[j] of a half,
+// rank r's column slice at r * n_local[j].  Each rank stores its slices into
+// half (epoch & 1) of its own buffer; the last CTA of the grid to finish
+// signals every rank ("slices ready"); every CTA waits, bounded, until all
+// ranks have signalled for this launch, then pulls its share of every rank's
+// slices over NVLink (16-byte loads from the peers' mappings) into the
+// caller's dst.  The halves alternate by a device-side launch epoch: a rank
+// one launch ahead writes the other half, and it cannot get two ahead before
+// this rank has finished pulling.
 struct PeerOut {
   long long delta[8];  // bytes from this rank's symmetric buffer to rank p's
   int *flag_peer[8];   // rank p's arrival counter
   int *flag_local;     // [0] arrivals (world per launch), [1] launch epoch,
-                       // [2] finished CTAs, [3] release epoch
+                       // [2] finished CTAs of this launch
   float *sym;          // this rank's symmetric buffer (two halves)
   long half_elems;     // floats per half
-  float *dst;          // caller's output, [rows][n] floats
-  long count;          // rows * n
-  int n, n_local;      // row length and per-rank slice width (multiple of 4)
+  long off[GCU_MAX_JOBS];                    // job region offsets in a half
+  int n[GCU_MAX_JOBS], n_local[GCU_MAX_JOBS];  // full / per-rank columns (n_local % 4 == 0)
+  float *dst[GCU_MAX_JOBS];                  // caller's outputs, [mb][n_j] dense
+  int njobs, mb, rank, world;
   unsigned int *err;
-  int world;
 };
+// x/xs: quantized activations, or xf (fp32, quantized in the launch into
+// qout/sout as quantize_acts would) when xf is not null.
 int launch_gemv_p2p(const GemvJobs &jobs, const int8_t *x, long xstride, const float *xs,
-                    int mb, long ystride, int k, const PeerOut &po, cudaStream_t st);
+                    const float *xf, int8_t *qout, float *sout, int mb, int k,
+                    const PeerOut &po, cudaStream_t st);
 
 // quantize_acts + GEMV in one launch (mb <= 8 rows of fp32 xf); writes the
 // codes (qout, dense [mb][k]) and scales (sout) as quantize_acts would.
@@ -180,6 +186,11 @@ __device__ __forceinline__ uint64_t globaltimer() {
   return t;
 }
 
+__device__ __forceinline__ int ld_acquire_sys(const int *p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 __device__ __forceinline__ int ld_acquire_gpu(const int *p) {
   int v;
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");

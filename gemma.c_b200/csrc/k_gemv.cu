@@ -248,57 +248,54 @@ __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, cons
           int j, local;
           job_of(jobs, row, j, local);
           const float val = dequant(v[t], s_xsc[b], jobs.ws[j][local]);
-          jobs.y[j][(size_t)b * ystride + local + half_off] = val;
+          if (P2P) {
+            // this rank's slice of job j in the current half
+            po.sym[half_off + po.off[j] + (size_t)b * po.n[j] + (size_t)po.rank * po.n_local[j] + local] = val;
+          } else {
+            jobs.y[j][(size_t)b * ystride + local] = val;
+          }
         }
       }
     }
   }
   if (P2P) {
-    // This CTA's slice stores reach this GPU's L2 (gpu scope); the CTA that
-    // signals the peers then releases everything it observed at system scope
-    // (fences are cumulative), so only one system-scope fence per launch.
+    // This CTA's slice stores reach this GPU's L2 (gpu scope) before it
+    // counts itself; the CTA that counts last then releases everything it
+    // observed at system scope (fences are cumulative), so one system-scope
+    // fence per launch covers every CTA's stores.
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) {
-      volatile int *vf = po.flag_local;
       const uint64_t t0 = ptx::globaltimer();
       if (atomicAdd(po.flag_local + 2, 1) == (int)gridDim.x - 1) {
-        // last CTA of this rank: arrive at every rank, wait for every rank
+        // last CTA of this rank: every CTA of the launch has read the epoch
+        // and pushed its rows; arrive at every rank
         po.flag_local[2] = 0;
+        po.flag_local[1] = epoch0 + 1;  // the next launch uses the other half
         __threadfence_system();
         for (int pr = 0; pr < po.world; ++pr) atomicAdd_system(po.flag_peer[pr], 1);
-        const int target = (epoch0 + 1) * po.world;
-        while (vf[0] < target) {
-          if (ptx::globaltimer() - t0 > 2000000000ull) {
-            atomicCAS(po.err, 0u, (unsigned int)DEV_TIMEOUT_PEER);
-            break;
-          }
+      }
+      const int target = (epoch0 + 1) * po.world;
+      while (ptx::ld_acquire_sys(po.flag_local) < target) {
+        if (ptx::globaltimer() - t0 > 2000000000ull) {
+          atomicCAS(po.err, 0u, (unsigned int)DEV_TIMEOUT_PEER);
+          break;
         }
-        __threadfence_system();  // acquire: the peers' slices are ready
-        vf[1] = epoch0 + 1;      // next launch uses the other half
-        __threadfence();
-        atomicExch(po.flag_local + 3, epoch0 + 1);  // release this grid's CTAs
-      } else {
-        while (vf[3] != epoch0 + 1) {
-          if (ptx::globaltimer() - t0 > 4000000000ull) {
-            atomicCAS(po.err, 0u, (unsigned int)DEV_TIMEOUT_PEER);
-            break;
-          }
-          __nanosleep(64);
-        }
-        __threadfence();
+        __nanosleep(32);
       }
     }
     __syncthreads();
-    // every rank's slice is ready in its half: pull them all into dst, 16
+    // every rank's slices are ready in its own half: pull them into dst, 16
     // bytes at a time (a 4-float group never straddles two ranks' slices)
-    const long groups = po.count >> 2;
-    for (long g = (long)blockIdx.x * kThreads + threadIdx.x; g < groups; g += (long)gridDim.x * kThreads) {
-      const long i = g << 2;
-      const int owner = (int)((i % po.n) / po.n_local);
-      const float4 *srcp = reinterpret_cast<const float4 *>(
-          reinterpret_cast<const char *>(po.sym + half_off + i) + po.delta[owner]);
-      reinterpret_cast<float4 *>(po.dst)[g] = __ldcg(srcp);
+    for (int j = 0; j < po.njobs; ++j) {
+      const long groups = ((long)po.mb * po.n[j]) >> 2;
+      const float *reg = po.sym + half_off + po.off[j];
+      float4 *d = reinterpret_cast<float4 *>(po.dst[j]);
+      for (long g = (long)blockIdx.x * kThreads + threadIdx.x; g < groups; g += (long)gridDim.x * kThreads) {
+        const long i = g << 2;
+        const int owner = (int)((i % po.n[j]) / po.n_local[j]);
+        d[g] = __ldcg(reinterpret_cast<const float4 *>(reinterpret_cast<const char *>(reg + i) + po.delta[owner]));
+      }
     }
   }
 }
@@ -421,18 +418,32 @@ int launch_gemv(const GemvJobs &jobs, const int8_t *x, long xstride, const float
 }
 
 // Row-sharded GEMV with the all-gather fused into its epilogue (see PeerOut).
-int launch_gemv_p2p(const GemvJobs &jobs, const int8_t *x, long xstride, const float *xs, int mb,
-                    long ystride, int k, const PeerOut &po, cudaStream_t st) {
-  if (jobs.njobs != 1 || mb <= 0 || mb > 8) return set_error("gemv p2p: one job, 1..8 rows");
-  const int total_rows = jobs.row_end[0];
-  const bool vec = (k % 16 == 0) && ((uintptr_t)x % 16 == 0) && (mb == 1 || xstride % 16 == 0) &&
-                   ((uintptr_t)jobs.w[0] % 16 == 0) && (size_t)8 * k <= 200 * 1024 && total_rows > 0;
-  if (!vec) return set_error("gemv p2p: needs k %% 16 == 0 and 16-byte aligned operands");
+int launch_gemv_p2p(const GemvJobs &jobs, const int8_t *x, long xstride, const float *xs,
+                    const float *xf, int8_t *qout, float *sout, int mb, int k, const PeerOut &po,
+                    cudaStream_t st) {
+  if (jobs.njobs <= 0 || jobs.njobs != po.njobs || mb <= 0 || mb > 8 || po.mb != mb)
+    return set_error("gemv p2p: 1..%d jobs and 1..8 rows", GCU_MAX_JOBS);
+  const int total_rows = jobs.row_end[jobs.njobs - 1];
+  bool vec = (k % 16 == 0) && (size_t)8 * k <= 200 * 1024 && total_rows > 0;
+  if (xf)
+    vec = vec && ((uintptr_t)xf % 16 == 0) && (mb == 1 || xstride % 4 == 0) && ((uintptr_t)qout % 16 == 0);
+  else
+    vec = vec && ((uintptr_t)x % 16 == 0) && (mb == 1 || xstride % 16 == 0);
+  for (int j = 0; j < jobs.njobs && vec; ++j)
+    vec = ((uintptr_t)jobs.w[j] % 16 == 0) && ((uintptr_t)po.dst[j] % 16 == 0) && po.n_local[j] % 4 == 0;
+  if (!vec) return set_error("gemv p2p: needs k %% 16 == 0, 16-byte aligned operands and outputs");
+  if (xf) {
+    GemvX X{nullptr, xstride, nullptr, xf, qout, sout};
+    if (mb == 1) return launch_mb<1, true, true>(jobs, X, mb, 0, k, total_rows, st, &po);
+    if (mb == 2) return launch_mb<2, true, true>(jobs, X, mb, 0, k, total_rows, st, &po);
+    if (mb <= 4) return launch_mb<4, true, true>(jobs, X, mb, 0, k, total_rows, st, &po);
+    return launch_mb<8, true, true>(jobs, X, mb, 0, k, total_rows, st, &po);
+  }
   GemvX X{x, xstride, xs, nullptr, nullptr, nullptr};
-  if (mb == 1) return launch_mb<1, false, true>(jobs, X, mb, ystride, k, total_rows, st, &po);
-  if (mb == 2) return launch_mb<2, false, true>(jobs, X, mb, ystride, k, total_rows, st, &po);
-  if (mb <= 4) return launch_mb<4, false, true>(jobs, X, mb, ystride, k, total_rows, st, &po);
-  return launch_mb<8, false, true>(jobs, X, mb, ystride, k, total_rows, st, &po);
+  if (mb == 1) return launch_mb<1, false, true>(jobs, X, mb, 0, k, total_rows, st, &po);
+  if (mb == 2) return launch_mb<2, false, true>(jobs, X, mb, 0, k, total_rows, st, &po);
+  if (mb <= 4) return launch_mb<4, false, true>(jobs, X, mb, 0, k, total_rows, st, &po);
+  return launch_mb<8, false, true>(jobs, X, mb, 0, k, total_rows, st, &po);
 }
 
 // Fused quantize_acts + GEMV: xf holds mb fp32 rows (row stride xfstride

@@ -61,6 +61,8 @@ SIGNATURES = {
     "gcu_comm_destroy": (_int, []),
     "gcu_comm_fused_allgather": (_int, []),
     "gcu_dev_gemm_int8_rowshard": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _int, _vp]),
+    "gcu_dev_quantize_gemm_int8_rowshard_multi": (_int, [ctypes.POINTER(GemvJob), _int, _vp, _vp, _vp, _int,
+                                                         _int, _int, _vp, _vp]),
 }
 # exported but not part of the public header (benchmark sweeps)
 EXTRA = {
@@ -291,3 +293,16 @@ def dev_gemm_int8_rowshard(dst, work, mat_local, matsc_local, src, ssc, m, n, k,
     _check(lib().gcu_dev_gemm_int8_rowshard(dst.data_ptr(), work.data_ptr(), mat_local.data_ptr(),
                                             matsc_local.data_ptr(), src.data_ptr(), ssc.data_ptr(),
                                             m, n, k, _stream(stream)), "dev_gemm_int8_rowshard")
+
+
+def dev_quantize_gemm_int8_rowshard_multi(jobs_t, q, s, x, m, k, work=None, xstr=0, stream=None):
+    """quantize_acts(x) -> (q, s) and the row-sharded GEMM of every job on it.
+    jobs_t: list of (w_local, sc_local, dst, rows) with rows the FULL row count."""
+    jobs = (GemvJob * len(jobs_t))()
+    for j, (w, sc, o, rows) in enumerate(jobs_t):
+        jobs[j] = GemvJob(w.data_ptr(), sc.data_ptr(), o.data_ptr(), rows)
+    _check(lib().gcu_dev_quantize_gemm_int8_rowshard_multi(jobs, len(jobs_t), q.data_ptr(), s.data_ptr(),
+                                                           x.data_ptr(), xstr, m, k,
+                                                           work.data_ptr() if work is not None else None,
+                                                           _stream(stream)),
+           "dev_quantize_gemm_int8_rowshard_multi")

@@ -168,8 +168,9 @@ int gcu_comm_unique_id(unsigned char id[128]);
 int gcu_comm_init(int rank, int world, const unsigned char id[128]);
 int gcu_comm_destroy(void);
 /* 1 if gcu_dev_gemm_int8_rowshard fuses its all-gather into the GEMV as
- * NVLink peer stores (m <= 8, every rank mapped every peer's buffer through
- * CUDA IPC at gcu_comm_init); 0 if it uses an NCCL all-gather. */
+ * NVLink loads from the peers' buffers (m <= 8, every rank mapped every
+ * peer's buffer through CUDA IPC at gcu_comm_init); 0 if it uses an NCCL
+ * all-gather. */
 int gcu_comm_fused_allgather(void);
 
 /* dst (m, n) dense = sharded gemm_int8 with this rank's rows mat_local
@@ -183,6 +184,25 @@ int gcu_dev_gemm_int8_rowshard(float *dst, float *work,
                                const float *matsc_local, const int8_t *src,
                                const float *ssc, int m, int n, int k,
                                void *stream);
+
+/* quantize_acts on x (m <= 8 fp32 rows, row stride xstr floats, 0 = k) and
+ * the row-sharded gemm_int8 of every job on the result, e.g. a layer's
+ * up/gate pair (gemma.c:4911-4915) with its FFN rows split over the ranks.
+ * Job j: w / sc hold this rank's rows_j/world rows of weight j and their
+ * scales, dst its full (m, rows_j) output, and the job's `m` field is the
+ * FULL row count rows_j (a multiple of world).  q / s receive the codes and
+ * scales as gcu_dev_quantize_acts writes them.  With the peers mapped
+ * (gcu_comm_fused_allgather() == 1), m <= 8, k % 16 == 0, every slice a
+ * multiple of 4 rows, 16-byte aligned dst and m * sum(rows_j) floats within
+ * 8 MiB, this is ONE launch: the GEMV quantizes x while staging it, and one
+ * cross-rank signal followed by NVLink loads completes the all-gather of all
+ * jobs.  Otherwise it runs gcu_dev_quantize_acts and then
+ * gcu_dev_gemm_int8_rowshard per job, using `work` (m * max rows_j floats)
+ * as that call's scratch.  No counterpart in the reference. */
+int gcu_dev_quantize_gemm_int8_rowshard_multi(const gcu_gemv_job *jobs, int njobs,
+                                              int8_t *q, float *s, const float *x,
+                                              int xstr, int m, int k, float *work,
+                                              void *stream);
 
 #ifdef __cplusplus
 }
