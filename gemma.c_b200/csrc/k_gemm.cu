@@ -76,6 +76,37 @@ struct Cfg {
   static_assert(ACC_COLS <= 512 && BN % 32 == 0 && BN <= 256, "tile shape");
 };
 
+// A CTA pair (thread-block cluster of two) computes a 256 x BN tile with
+// tcgen05.mma.cta_group::2: CTA r of the pair holds A rows [128r, 128r+128)
+// and B rows [r*BN/2, (r+1)*BN/2) of every stage, and its TMEM holds the
+// accumulator of its 128 rows x all BN columns.  Per output, each SM pulls
+// a third less operand data than a one-CTA 128 x BN tile, and a 128 x BN
+// accumulator leaves room for two TMEM buffers.
+constexpr int kPairMB = 4;  // Plan::mb value of the pair kernel
+
+template <int BN>
+struct PairCfg {
+  static constexpr int BH = BN / 2;  // B rows per CTA
+  static constexpr int TILE_M = 2 * BM;
+  static constexpr int A_BYTES = BM * BK;
+  static constexpr int B_BYTES = BH * BK;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int ACC_COLS = BN;
+  static constexpr int NBUF = 2 * ACC_COLS <= 512 ? 2 : 1;
+  static constexpr int TMEM_COLS = pow2_at_least(NBUF * ACC_COLS);
+  static constexpr int EPI_BYTES = kEpiWarps * kEpiStageBytes;
+  static constexpr int FIXED = 1024 + EPI_BYTES + 512;
+  static constexpr int STAGES_FIT = (kSmemMax - FIXED) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
+  static constexpr int BAR_OFF = EPI_OFF + EPI_BYTES;
+  static constexpr int NBARS = 3 * STAGES + 5;
+  static constexpr int SMEM = 1024 + BAR_OFF + NBARS * 8 + 16;
+  static_assert(STAGES >= 2, "tile too large for shared memory");
+  static_assert(SMEM + 64 <= kSmemMax, "shared memory budget");
+  static_assert(BH % 8 == 0 && BN <= 256 && BN % 32 == 0, "pair tile shape");
+};
+
 struct alignas(64) TcJob {
   CUtensorMap tmB;  // weights [n][k] int8, box BN x 128
   CUtensorMap tmD;  // output [m][n] fp32 (row stride dstr), box 32 x 32
@@ -557,6 +588,223 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_tc(const __grid_constan
   }
 }
 
+// The CTA-pair kernel.  Warp roles as in k_gemm_i8_tc; in addition the
+// second CTA's warp 1 forwards "my stage is full" to the first CTA (a remote
+// mbarrier arrival), whose warp 1 issues the pair's MMAs once both halves of
+// a stage have landed.  Commits arrive on the stage and accumulator barriers
+// of both CTAs; each CTA's epilogue reads its own TMEM rows and hands the
+// buffer back to the first CTA.  No split K.
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_pair(const __grid_constant__ TcParams p) {
+  using C = PairCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *smA = smem;
+  uint8_t *smB = smem + C::STAGES * C::A_BYTES;
+  uint8_t *epi = smem + C::EPI_OFF;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
+  uint64_t *full = bars;                    // this CTA's half of a stage landed
+  uint64_t *empty = bars + C::STAGES;       // the pair's MMAs are done with a stage
+  uint64_t *pfull = bars + 2 * C::STAGES;   // first CTA: the second CTA's half landed
+  uint64_t *tfull = bars + 3 * C::STAGES;   // accumulator buffer ready (both CTAs)
+  uint64_t *tempty = tfull + 2;             // first CTA: buffer drained by both CTAs
+  uint64_t *mma_done = tempty + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t crank = ptx::cluster_ctarank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&empty[s], 1);
+      ptx::mbar_init(&pfull[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(&tfull[b], 1);
+      ptx::mbar_init(&tempty[b], 2 * kEpiWarps);
+    }
+    ptx::mbar_init(mma_done, 1);
+    ptx::fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    ptx::prefetch_tmap(&p.tmA);
+    for (int j = 0; j < p.njobs; ++j) {
+      ptx::prefetch_tmap(&p.jobs[j].tmB);
+      if (p.jobs[j].tma_store) ptx::prefetch_tmap(&p.jobs[j].tmD);
+    }
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+    ptx::tmem_relinquish_pair();
+  }
+  ptx::tc_fence_before();
+  ptx::cluster_sync();  // both CTAs' barriers exist before any remote arrival
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  // warm L2 with this CTA's first B half-tiles (see k_gemm_i8_tc)
+  Unit w_first{};
+  if (warp == 0 && lane == 0 && pair < p.units) {
+    w_first = decode_unit(p, pair);
+    const int kbn = min(p.kb_total, max(C::STAGES, kPrefetchBytes / C::B_BYTES));
+    for (int kb = 0; kb < kbn; ++kb)
+      ptx::tma_prefetch_l2_2d(&p.jobs[w_first.job].tmB, kb * BK, w_first.n_t * BN + crank * C::BH);
+  }
+  ptx::griddep_wait();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol_a = ptx::policy_evict_last();
+      const uint64_t pol_b = ptx::policy_evict_first();
+      int it = 0;
+      bool ok = true;
+      for (int u = pair; u < p.units && ok; u += npairs) {
+        const Unit w = u == pair ? w_first : decode_unit(p, u);
+        for (int kb = 0; kb < p.kb_total; ++kb, ++it) {
+          const int st = it % C::STAGES;
+          const uint32_t round = it / C::STAGES;
+          if (!ptx::mbar_wait(&empty[st], (round & 1) ^ 1, p.err, DEV_TIMEOUT_EMPTY)) {
+            ok = false;
+            break;
+          }
+          ptx::mbar_arrive_expect_tx(&full[st], C::STAGE_BYTES);
+          ptx::tma_load_2d(&p.tmA, &full[st], smA + st * C::A_BYTES, kb * BK,
+                           w.m_t * C::TILE_M + crank * BM, pol_a);
+          ptx::tma_load_2d(&p.jobs[w.job].tmB, &full[st], smB + st * C::B_BYTES, kb * BK,
+                           w.n_t * BN + crank * C::BH, pol_b);
+        }
+      }
+      for (int d = 1; d <= C::STAGES && d <= it; ++d) {
+        const int j = it - d;
+        ptx::mbar_wait(&full[j % C::STAGES], (j / C::STAGES) & 1, p.err, DEV_TIMEOUT_DRAIN);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && crank == 0) {
+      // -------------------------------------------------------- MMA issuer
+      constexpr uint32_t idesc = ptx::idesc_i8(2 * BM, BN);
+      int it = 0, t = 0;
+      bool ok = true;
+      for (int u = pair; u < p.units && ok; u += npairs, ++t) {
+        const int buf = t % C::NBUF;
+        const uint32_t use = t / C::NBUF;
+        if (!ptx::mbar_wait_cluster(&tempty[buf], (use & 1) ^ 1, p.err, DEV_TIMEOUT_TMEM)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * C::ACC_COLS;
+        for (int kb = 0; kb < p.kb_total; ++kb, ++it) {
+          const int st = it % C::STAGES;
+          const uint32_t round = it / C::STAGES;
+          if (!ptx::mbar_wait(&full[st], round & 1, p.err, DEV_TIMEOUT_FULL) ||
+              !ptx::mbar_wait_cluster(&pfull[st], round & 1, p.err, DEV_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t a0 = ptx::smem_u32(smA + st * C::A_BYTES);
+          const uint32_t b0 = ptx::smem_u32(smB + st * C::B_BYTES);
+#pragma unroll
+          for (int j = 0; j < BK / 32; ++j)
+            ptx::mma_i8_pair(d_tmem, ptx::smem_desc_k128(a0 + 32 * j), ptx::smem_desc_k128(b0 + 32 * j),
+                             idesc, (kb > 0 || j > 0) ? 1u : 0u);
+          ptx::mma_commit_pair(&empty[st]);
+        }
+        ptx::mma_commit_pair(&tfull[buf]);
+      }
+      ptx::griddep_launch();
+      ptx::mma_commit_pair(mma_done);
+      ptx::mbar_wait(mma_done, 0, p.err, DEV_TIMEOUT_DRAIN);
+    } else if (lane == 0) {
+      // ------------------------------------------- forwarder (second CTA)
+      const uint32_t pfull0 = ptx::mapa(ptx::smem_u32(pfull), 0);
+      int it = 0;
+      bool ok = true;
+      for (int u = pair; u < p.units && ok; u += npairs) {
+        for (int kb = 0; kb < p.kb_total; ++kb, ++it) {
+          const int st = it % C::STAGES;
+          if (!ptx::mbar_wait(&full[st], (it / C::STAGES) & 1, p.err, DEV_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          ptx::mbar_arrive_remote_relaxed(pfull0 + st * 8);
+        }
+      }
+      ptx::griddep_launch();
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    uint8_t *stage = epi + (warp - 2) * kEpiStageBytes;
+    constexpr int NCH = BN / 32;
+    const uint32_t tempty0 = ptx::mapa(ptx::smem_u32(tempty), 0);
+    int t = 0;
+    for (int u = pair; u < p.units; u += npairs, ++t) {
+      const Unit w = decode_unit(p, u);
+      const TcJob &job = p.jobs[w.job];
+      const int buf = t % C::NBUF;
+      const uint32_t use = t / C::NBUF;
+      const int tile_row0 = w.m_t * C::TILE_M + crank * BM + q * 32;
+      const int row = tile_row0 + lane;
+      const int n0 = w.n_t * BN;
+      const float xs = row < p.m ? __ldg(p.ssc + row) : 0.0f;
+      float wsl[NCH];
+#pragma unroll
+      for (int ch = 0; ch < NCH; ++ch) {
+        const int col = n0 + ch * 32 + lane;
+        wsl[ch] = col < job.n ? __ldg(job.matsc + col) : 0.0f;
+      }
+      if (!ptx::mbar_wait(&tfull[buf], use & 1, p.err, DEV_TIMEOUT_TMEM)) break;
+      ptx::tc_fence_after();
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * C::ACC_COLS;
+#pragma unroll
+      for (int ch = 0; ch < NCH; ++ch) {
+        if ((ch & 1) != half) continue;
+        __syncwarp();
+        uint32_t r[32];
+        ptx::tmem_ld_32x32(taddr + ch * 32, r);
+        ptx::tmem_ld_wait();
+        const int col0 = n0 + ch * 32;
+        if (col0 >= job.n) continue;
+        if (job.tma_store) {
+          if (lane == 0) ptx::bulk_wait_read<0>();
+          __syncwarp();
+          emit_chunk<true>(p, job, reinterpret_cast<const int(&)[32]>(r), xs, wsl[ch], row, col0, lane,
+                           stage, tile_row0);
+        } else {
+          emit_chunk<false>(p, job, reinterpret_cast<const int(&)[32]>(r), xs, wsl[ch], row, col0,
+                            lane, nullptr, tile_row0);
+        }
+      }
+      // this warp's TMEM reads are done: hand its part of the buffer back
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (crank == 0)
+          ptx::mbar_arrive(&tempty[buf]);
+        else
+          ptx::mbar_arrive_remote(tempty0 + buf * 8);
+      }
+    }
+    if (lane == 0) ptx::bulk_wait<0>();
+    __syncwarp();
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::cluster_sync();  // the other CTA is done with this CTA's barriers and TMEM
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
@@ -623,11 +871,51 @@ int launch_cfg(TcParams &p, cudaStream_t st) {
   return 0;
 }
 
+template <int BN>
+int launch_pair(TcParams &p, cudaStream_t st) {
+  using C = PairCfg<BN>;
+  static std::mutex mu;
+  static uint64_t done_mask = 0;
+  int dev = 0;
+  GCU_CUDA(cudaGetDevice(&dev));
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!(done_mask & (1ull << (dev & 63)))) {
+      GCU_CUDA(cudaFuncSetAttribute(k_gemm_i8_pair<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    C::SMEM));
+      done_mask |= 1ull << (dev & 63);
+    }
+  }
+  const int max_pairs = num_sms() / 2;
+  const int pairs = p.units < max_pairs ? p.units : max_pairs;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  GCU_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_i8_pair<BN>, p));
+  GCU_CUDA(cudaGetLastError());
+  return 0;
+}
+
 // Tile shapes the kernel is instantiated for: BN x (128*MB).
 struct Shape {
   int bn, mb;
 };
-constexpr Shape kShapes[] = {{64, 1}, {128, 1}, {256, 1}, {128, 2}, {192, 2}, {256, 2}};
+constexpr Shape kShapes[] = {{64, 1},        {128, 1},       {256, 1},      {128, 2}, {192, 2},
+                             {256, 2},       {128, kPairMB}, {192, kPairMB}, {256, kPairMB}};
+
+// rows of one tile: 128*mb for one CTA, 256 for a CTA pair
+constexpr int tile_rows(int mb) { return mb == kPairMB ? 2 * BM : BM * mb; }
 
 int split_for(int tiles, int kb_total, int sms) {
   // split K only when the tiles cannot occupy the SMs and K is long, keeping
@@ -643,19 +931,35 @@ int split_for(int tiles, int kb_total, int sms) {
 // were fitted to per-CTA timelines (globaltimer / clock64 stamps) and to a
 // sweep of every tile shape and split over the BASELINE shapes on B200:
 //   - a CTA's TMA ring ingests ~100 GB/s from L2; all SMs together ~12 TB/s
-//   - kind::i8 MMA sustains ~26 TOPS per SM
+//   - kind::i8 MMA sustains ~22 TOPS per SM (clocks drop under load)
+//   - a CTA pair's ring moves ~78 GB/s per CTA (each stage waits for the
+//     other CTA's half to be forwarded), plus ~3 us of pair set-up and tail
 //   - the fp32 epilogue drains ~70 GB/s per CTA after ~0.5 us of latency
 //   - a split-K round trip costs about half a partial write per split
 // With two TMEM accumulators the epilogue of a tile overlaps the next tile's
 // main loop; with one (MB*BN > 256) it does not.
 double estimate_us(int m, int ntn, int kb_total, int bn, int mb, int splits, int sms) {
+  if (mb == kPairMB) {
+    // per CTA of a pair: 128 rows x bn outputs from 128 + bn/2 operand rows
+    const long tiles = (long)((m + 255) / 256) * ntn;
+    const double stage = (128.0 + bn / 2) * 128.0;
+    const double t_load = kb_total * stage / 0.78e5;
+    const double t_mma = kb_total * 2.0 * 128.0 * bn * 128.0 / 2.2e7;
+    const double t_unit = t_load > t_mma ? t_load : t_mma;
+    const long waves = (tiles + sms / 2 - 1) / (sms / 2);
+    const double t_drain = 128.0 * bn * 4.0 / 7.0e4;
+    double t_main = waves * (t_unit > t_drain ? t_unit : t_drain);
+    const double t_l2 = (double)tiles * 2 * kb_total * stage / 1.2e7;
+    if (t_l2 > t_main) t_main = t_l2;
+    return t_main + 3.0 + t_drain;
+  }
   const double tile_m = 128.0 * mb;
   const long tiles = (long)((m + 128 * mb - 1) / (128 * mb)) * ntn;
   const long units = tiles * splits;
   const int kb_unit = (kb_total + splits - 1) / splits;
   const double stage = (tile_m + bn) * 128.0;
   const double t_load = kb_unit * stage / 1.0e5;
-  const double t_mma = kb_unit * 2.0 * tile_m * bn * 128.0 / 2.6e7;
+  const double t_mma = kb_unit * 2.0 * tile_m * bn * 128.0 / 2.2e7;
   const double t_unit = t_load > t_mma ? t_load : t_mma;
   const long waves = (units + sms - 1) / sms;
   const double out_bytes = tile_m * bn * 4.0;
@@ -693,8 +997,8 @@ Plan model_plan(int m, int k, const GemmArgs *jobs, int njobs, int sms) {
   Plan best{128, 1, 1};
   double best_t = 1e30;
   for (const Shape &sh : kShapes) {
-    const int tiles = (m + 128 * sh.mb - 1) / (128 * sh.mb) * ntiles_n(jobs, njobs, sh.bn);
-    const int sp = split_for(tiles, kb_total, sms);
+    const int tiles = (m + tile_rows(sh.mb) - 1) / tile_rows(sh.mb) * ntiles_n(jobs, njobs, sh.bn);
+    const int sp = sh.mb == kPairMB ? 1 : split_for(tiles, kb_total, sms);
     const double t = estimate_us(m, ntiles_n(jobs, njobs, sh.bn), kb_total, sh.bn, sh.mb, sp, sms);
     if (t < best_t - 1e-9) {
       best_t = t;
@@ -749,10 +1053,10 @@ int tuned_plan(Plan *out, const int8_t *src, long sstr, const float *ssc, int m,
   Plan cand[2 * sizeof(kShapes) / sizeof(kShapes[0])];
   int nc = 0;
   for (const Shape &sh : kShapes) {
-    const int tiles = (m + 128 * sh.mb - 1) / (128 * sh.mb) * ntiles_n(jobs, njobs, sh.bn);
+    const int tiles = (m + tile_rows(sh.mb) - 1) / tile_rows(sh.mb) * ntiles_n(jobs, njobs, sh.bn);
     const int sp = split_for(tiles, kb_total, sms);
     cand[nc++] = Plan{sh.bn, sh.mb, 1};
-    if (sp > 1) cand[nc++] = Plan{sh.bn, sh.mb, sp};
+    if (sp > 1 && sh.mb != kPairMB) cand[nc++] = Plan{sh.bn, sh.mb, sp};
   }
   cudaEvent_t e0, e1;
   GCU_CUDA(cudaEventCreate(&e0));
@@ -790,7 +1094,7 @@ int tuned_plan(Plan *out, const int8_t *src, long sstr, const float *ssc, int m,
   }
   if (getenv("GCU_DEBUG"))
     fprintf(stderr, "gcu: gemm m=%d k=%d n0=%d jobs=%d -> tile %dx%d split %d (%.2f us)\n", m, k,
-            key.n[0], njobs, 128 * best.mb, best.bn, best.splits, best_ms * 1000.0f / 3.0f);
+            key.n[0], njobs, tile_rows(best.mb), best.bn, best.splits, best_ms * 1000.0f / 3.0f);
   *out = best;
   return 0;
 }
@@ -817,9 +1121,10 @@ int launch_gemm_tc_jobs(const int8_t *src, long sstr, const float *ssc, int m, i
     pl.mb = force_mb > 0 ? force_mb : 1;
     bool known = false;
     for (const Shape &sh : kShapes) known |= (sh.bn == pl.bn && sh.mb == pl.mb);
-    if (!known) return set_error("gemm: no %d x %d tile variant", 128 * pl.mb, pl.bn);
-    const int tiles = (m + 128 * pl.mb - 1) / (128 * pl.mb) * ntiles_n(jobs, njobs, pl.bn);
+    if (!known) return set_error("gemm: no %d x %d tile variant", tile_rows(pl.mb), pl.bn);
+    const int tiles = (m + tile_rows(pl.mb) - 1) / tile_rows(pl.mb) * ntiles_n(jobs, njobs, pl.bn);
     pl.splits = force_split > 0 ? force_split : split_for(tiles, kb_total, sms);
+    if (pl.mb == kPairMB && pl.splits > 1) return set_error("gemm: the CTA-pair tiles take no K split");
     return run_plan(pl, src, sstr, ssc, m, k, jobs, njobs, st, ext);
   }
   pl = model_plan(m, k, jobs, njobs, sms);
@@ -837,12 +1142,13 @@ namespace {
 int run_plan(const Plan &pl, const int8_t *src, long sstr, const float *ssc, int m, int k,
              const GemmArgs *jobs, int njobs, cudaStream_t st, const ExtWorkspace *ext) {
   const int bn = pl.bn, mb = pl.mb;
+  const bool pair = mb == kPairMB;
   const int kb_total = (k + BK - 1) / BK;
-  const int tile_m = BM * mb;
+  const int tile_m = tile_rows(mb);
   const int tiles_m = (m + tile_m - 1) / tile_m;
   const int tiles_n = ntiles_n(jobs, njobs, bn);
   const int tiles = tiles_m * tiles_n;
-  int splits = pl.splits < 1 ? 1 : pl.splits;
+  int splits = pl.splits < 1 || pair ? 1 : pl.splits;
   if (splits > kb_total) splits = kb_total;
   const int kb_per = (kb_total + splits - 1) / splits;
   splits = (kb_total + kb_per - 1) / kb_per;
@@ -850,11 +1156,12 @@ int run_plan(const Plan &pl, const int8_t *src, long sstr, const float *ssc, int
   static_assert(sizeof(TcParams) <= 4096, "kernel parameters exceed 4 KB");
   TcParams p;
   memset(&p, 0, sizeof(p));
-  if (make_map_i8(&p.tmA, src, k, m, sstr, tile_m)) return 1;
+  // a pair's CTAs each load 128 A rows and bn/2 B rows per stage
+  if (make_map_i8(&p.tmA, src, k, m, sstr, pair ? BM : tile_m)) return 1;
   int tn = 0;
   for (int j = 0; j < njobs; ++j) {
     TcJob &J = p.jobs[j];
-    if (make_map_i8(&J.tmB, jobs[j].mat, k, jobs[j].n, jobs[j].mstr, bn)) return 1;
+    if (make_map_i8(&J.tmB, jobs[j].mat, k, jobs[j].n, jobs[j].mstr, pair ? bn / 2 : bn)) return 1;
     J.tma_store = ((uintptr_t)jobs[j].dst % 16 == 0) && (jobs[j].dstr % 4 == 0);
     if (J.tma_store && make_map_f32(&J.tmD, jobs[j].dst, jobs[j].n, m, jobs[j].dstr)) return 1;
     J.matsc = jobs[j].matsc;
@@ -895,6 +1202,11 @@ int run_plan(const Plan &pl, const int8_t *src, long sstr, const float *ssc, int
     // one wave (grid = min(units, SMs), one CTA per SM): every split of a
     // tile is resident together and they can share the reduction
     p.dist = p.units <= num_sms();
+  }
+  if (pair) {
+    if (bn == 128) return launch_pair<128>(p, st);
+    if (bn == 192) return launch_pair<192>(p, st);
+    return launch_pair<256>(p, st);
   }
   if (mb == 2) {
     if (bn == 128) return launch_cfg<128, 2>(p, st);

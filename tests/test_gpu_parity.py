@@ -249,7 +249,8 @@ def _dev(a):
 
 @pytest.mark.parametrize("bn,split,mb", [(128, 1, 1), (256, 1, 1), (128, 3, 1), (256, 2, 1), (128, 7, 1),
                                          (64, 1, 1), (64, 3, 1), (128, 1, 2), (192, 1, 2), (256, 1, 2),
-                                         (192, 3, 2), (128, 2, 2)])
+                                         (192, 3, 2), (128, 2, 2),
+                                         (128, 1, 4), (192, 1, 4), (256, 1, 4)])  # mb 4: CTA-pair tiles
 def test_gemm_tile_and_split_variants(bn, split, mb):
     # m = 384 leaves a half-empty last 256-row tile for mb = 2
     m, n, k = 384, 1000, 2304
