@@ -167,11 +167,13 @@ class Prefill:
     weights' rows over the ranks and all-gather each FFN output
     (gcu_dev_gemm_int8_rowshard); Q/K/V/O stay replicated."""
 
-    def __init__(self, name="prefill1b", seed=0, fused=False, world=1, rank=0):
+    def __init__(self, name="prefill1b", seed=0, fused=False, world=1, rank=0, layers=0):
         import synth
         self.name = name
         self.index, self.title, stacks, shard = PREFILL[name]
         self.stacks = stacks(synth)
+        if layers > 0:  # profiling captures of a small case: every stack cut to `layers` layers
+            self.stacks = [(lb, g, m, min(nl, layers)) for lb, g, m, nl in self.stacks]
         self.fused, self.world, self.rank = fused, world, rank
         self.shard = shard and world > 1
         self.needs_comm = self.shard
@@ -373,7 +375,7 @@ class Decode:
     over the ranks with the all-gather fused into the GEMV when the peers are
     mapped (gcu_dev_gemm_int8_rowshard); Q/K/V/O stay replicated."""
 
-    def __init__(self, name="decode270m", seed=0, fused=True, world=1, rank=0):
+    def __init__(self, name="decode270m", seed=0, fused=True, world=1, rank=0, layers=0):
         import synth
         self.name = name
         self.index, cfg, shard = DECODE[name]
@@ -383,7 +385,7 @@ class Decode:
         self.needs_comm = self.shard
         self.cfg = synth.CONFIGS[cfg]
         self.groups = synth.layer_groups(self.cfg)
-        self.layers = self.cfg["layers"]
+        self.layers = min(self.cfg["layers"], layers) if layers > 0 else self.cfg["layers"]
         self.bytes = (synth.layer_weight_bytes(self.cfg) * self.layers +
                       self.cfg["vocab"] * (self.cfg["dim"] + 4))
         self.seed = seed
@@ -569,9 +571,9 @@ def run_ours(args):
     gcu.init(local)
     peaks = load_peaks()
     if args.workload in PREFILL:
-        wl = Prefill(args.workload, seed=rank, fused=args.fused, world=world, rank=rank)
+        wl = Prefill(args.workload, seed=rank, fused=args.fused, world=world, rank=rank, layers=args.layers)
     elif args.workload in DECODE:
-        wl = Decode(args.workload, seed=rank, fused=not args.unfused, world=world, rank=rank)
+        wl = Decode(args.workload, seed=rank, fused=not args.unfused, world=world, rank=rank, layers=args.layers)
     else:
         wl = LmHead(world, rank)
     if wl.needs_comm:
@@ -691,6 +693,8 @@ def run_ours(args):
                    scaling="strong")
         cfg = wl.config()
         cfg.update(parallelism=f"row-shard x{world}" if world > 1 else "single GPU")
+    if args.layers > 0:
+        cfg["reduced"] = f"--layers {args.layers}: a profiling case, not the benchmark workload"
     out["config"] = cfg
     out["clocks"] = clk
     out["gpu_launches"] = wl.launches_per_step * args.steps
@@ -833,6 +837,9 @@ def main():
                     help="prefill: issue each quantize+GEMM pair through gcu_dev_quantize_gemm_int8_multi")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--layers", type=int, default=0,
+                    help="cut every stack to this many layers (small cases for ncu captures; the line "
+                         "then describes a reduced workload and is not a benchmark value)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
