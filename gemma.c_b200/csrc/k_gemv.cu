@@ -151,19 +151,48 @@ __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, cons
       }
       const float4 *xr = reinterpret_cast<const float4 *>(X.xf + (size_t)b * X.xstride);
       float amax = 0.0f;
-      for (int i = threadIdx.x; i < 4 * C; i += kThreads) amax = ptx::absmax4(__ldg(xr + i), amax);
-      amax = block_max256(amax, red);
       float scale, inv;
-      ptx::quant_scale(amax, scale, inv);
-      for (int i = threadIdx.x; i < C; i += kThreads) {
-        int4 v;
-        v.x = ptx::quant_pack4(__ldg(xr + 4 * i), inv);
-        v.y = ptx::quant_pack4(__ldg(xr + 4 * i + 1), inv);
-        v.z = ptx::quant_pack4(__ldg(xr + 4 * i + 2), inv);
-        v.w = ptx::quant_pack4(__ldg(xr + 4 * i + 3), inv);
-        xsm[b * C + i] = v;
-        if (blockIdx.x == 0 && X.qout)
-          *reinterpret_cast<int4 *>(X.qout + (size_t)b * k + (size_t)i * 16) = v;
+      if (4 * C <= 4 * kThreads) {
+        // k <= 4096: each thread keeps its (at most four) float4 of the row
+        // in registers across the max, one read of x
+        float4 xv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int idx = threadIdx.x + i * kThreads;
+          if (idx < 4 * C) {
+            xv[i] = __ldg(xr + idx);
+            amax = ptx::absmax4(xv[i], amax);
+          }
+        }
+        amax = block_max256(amax, red);
+        ptx::quant_scale(amax, scale, inv);
+        // float4 idx -> 32-bit word idx of the row's codes (word 4c + j of
+        // 16-byte chunk c holds elements 16c + 4j .. 16c + 4j + 3)
+        int *xw = reinterpret_cast<int *>(xsm + b * C);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int idx = threadIdx.x + i * kThreads;
+          if (idx < 4 * C) {
+            const int w = ptx::quant_pack4(xv[i], inv);
+            xw[idx] = w;
+            if (blockIdx.x == 0 && X.qout)
+              reinterpret_cast<int *>(X.qout + (size_t)b * k)[idx] = w;
+          }
+        }
+      } else {
+        for (int i = threadIdx.x; i < 4 * C; i += kThreads) amax = ptx::absmax4(__ldg(xr + i), amax);
+        amax = block_max256(amax, red);
+        ptx::quant_scale(amax, scale, inv);
+        for (int i = threadIdx.x; i < C; i += kThreads) {
+          int4 v;
+          v.x = ptx::quant_pack4(__ldg(xr + 4 * i), inv);
+          v.y = ptx::quant_pack4(__ldg(xr + 4 * i + 1), inv);
+          v.z = ptx::quant_pack4(__ldg(xr + 4 * i + 2), inv);
+          v.w = ptx::quant_pack4(__ldg(xr + 4 * i + 3), inv);
+          xsm[b * C + i] = v;
+          if (blockIdx.x == 0 && X.qout)
+            *reinterpret_cast<int4 *>(X.qout + (size_t)b * k + (size_t)i * 16) = v;
+        }
       }
       if (threadIdx.x == 0) {
         s_scale[b] = scale;
