@@ -1,0 +1,196 @@
+// k_producers.cu -- the producers of the matmul inputs, fused with K1.
+//
+// gemma.c quantizes two kinds of activation right after computing them:
+//   - every block input right after its RMSNorm: rmsnorm (gemma.c:2509-2524)
+//     at 4754 / 5026, then quantize_act / quantize_acts at 4768 / 5034;
+//   - the down projection's input right after the GeGLU gate: gelu with
+//     `mul` (gemma.c:4139-4170) at 4921 / 5379, then quantize at 4927 / 5389.
+// Each kernel here computes the producer on a row held in registers and
+// quantizes the result in the same pass, so the fp32 activation is read once
+// and the int8 codes (plus, optionally, the fp32 values) written once.
+//
+//   rmsnorm:  sq = sum x^2, rms = 1 / sqrt(sq / n + eps), xn = (x*rms)*(w+1)
+//   geglu:    h = (0.5*x) * (1 + tanh(c*(x + ((0.044715*x)*x)*x))) * up,
+//             c = sqrt(2/pi), tanhf is CUDA's
+// The quantize step is K1's exact arithmetic on those values.  The sum of
+// squares is reduced in a different order than gemma.c's vectorized loop
+// and tanhf is a different library's, so the fp32 values match the
+// reference to within ~1e-6 relative, not bit for bit; a code can then
+// differ by one where a value sits that close to a rounding boundary.
+//
+// HBM-bound: one read of the input row(s) (and the norm weight, from L2),
+// one int8 write (plus the optional fp32 write).  Same work split as K1's
+// warp path: WPR warps per row, 8/WPR rows per 256-thread CTA.
+#include "gcu_internal.cuh"
+
+#define GCU_EXPORT extern "C" __attribute__((visibility("default")))
+
+namespace gcu {
+namespace {
+
+enum Producer { RMSNORM = 0, GEGLU = 1 };
+
+template <int WPR, bool MAX>
+__device__ __forceinline__ float row_reduce(float v, float *red, int warp, int grp, int lane) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float u = __shfl_xor_sync(0xffffffffu, v, o);
+    v = MAX ? fmaxf(v, u) : v + u;
+  }
+  if (WPR == 1) return v;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float r = red[grp * WPR];
+#pragma unroll
+  for (int w = 1; w < WPR; ++w) r = MAX ? fmaxf(r, red[grp * WPR + w]) : r + red[grp * WPR + w];
+  __syncthreads();  // red is written again by the next reduction
+  return r;
+}
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float c = 0.79788456080287f;  // sqrt(2 / pi)
+  const float t = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, x), x), x);
+  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(__fmul_rn(c, __fadd_rn(x, t)))));
+}
+
+// a: the row source (x, or the gate), b: the norm weight [n] (RMSNORM) or the
+// up rows (GEGLU, same stride as a); out: optional fp32 result rows [m][n].
+template <int VPT, int WPR, Producer P>
+__global__ void __launch_bounds__(256) k_producer_quant(int8_t *__restrict__ dst, float *__restrict__ dsc,
+                                                        float *__restrict__ out, const float *__restrict__ a,
+                                                        const float *__restrict__ b, float eps, long astr,
+                                                        int m, int n) {
+  constexpr int kRows = 8 / WPR;
+  __shared__ float red[8];
+  ptx::griddep_launch();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = warp / WPR, wi = warp - grp * WPR;
+  const int row = blockIdx.x * kRows + grp;
+  const bool live = row < m;  // uniform per warp
+  const int n4 = n >> 2;
+  ptx::griddep_wait();
+  float4 v[VPT];
+  if (live) {
+    const float4 *ar = reinterpret_cast<const float4 *>(a + (size_t)row * astr);
+    const float4 *br = reinterpret_cast<const float4 *>(P == GEGLU ? b + (size_t)row * astr : b);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int idx = (i * WPR + wi) * 32 + lane;
+      if (idx < n4) {
+        v[i] = __ldcs(ar + idx);
+        if (P == GEGLU) {
+          const float4 u = __ldcs(br + idx);
+          v[i] = make_float4(__fmul_rn(gelu_tanh(v[i].x), u.x), __fmul_rn(gelu_tanh(v[i].y), u.y),
+                             __fmul_rn(gelu_tanh(v[i].z), u.z), __fmul_rn(gelu_tanh(v[i].w), u.w));
+        }
+      }
+    }
+  }
+  if (P == RMSNORM) {
+    float sq = 0.0f;
+    if (live) {
+#pragma unroll
+      for (int i = 0; i < VPT; ++i)
+        if ((i * WPR + wi) * 32 + lane < n4)
+          sq += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+    }
+    sq = row_reduce<WPR, false>(sq, red, warp, grp, lane);
+    const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sq, (float)n), eps)));
+    if (live) {
+      const float4 *wr = reinterpret_cast<const float4 *>(b);
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int idx = (i * WPR + wi) * 32 + lane;
+        if (idx < n4) {
+          const float4 w = __ldg(wr + idx);
+          v[i] = make_float4(__fmul_rn(__fmul_rn(v[i].x, rms), __fadd_rn(w.x, 1.0f)),
+                             __fmul_rn(__fmul_rn(v[i].y, rms), __fadd_rn(w.y, 1.0f)),
+                             __fmul_rn(__fmul_rn(v[i].z, rms), __fadd_rn(w.z, 1.0f)),
+                             __fmul_rn(__fmul_rn(v[i].w, rms), __fadd_rn(w.w, 1.0f)));
+        }
+      }
+    }
+  }
+  float amax = 0.0f;
+  if (live) {
+#pragma unroll
+    for (int i = 0; i < VPT; ++i)
+      if ((i * WPR + wi) * 32 + lane < n4) amax = ptx::absmax4(v[i], amax);
+  }
+  amax = row_reduce<WPR, true>(amax, red, warp, grp, lane);
+  if (!live) return;
+  float scale, inv;
+  ptx::quant_scale(amax, scale, inv);
+  int *q = reinterpret_cast<int *>(dst + (size_t)row * n);
+  float4 *o = out ? reinterpret_cast<float4 *>(out + (size_t)row * n) : nullptr;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int idx = (i * WPR + wi) * 32 + lane;
+    if (idx < n4) {
+      q[idx] = ptx::quant_pack4(v[i], inv);
+      if (o) o[idx] = v[i];
+    }
+  }
+  if (wi == 0 && lane == 0) dsc[row] = scale;
+}
+
+template <Producer P, int WPR>
+cudaError_t launch_wpr(int vpt, int grid, int8_t *dst, float *dsc, float *out, const float *a,
+                       const float *b, float eps, long astr, int m, int n, cudaStream_t st) {
+  switch (vpt) {
+    case 2: return launch_k(k_producer_quant<2, WPR, P>, grid, 256, 0, st, dst, dsc, out, a, b, eps, astr, m, n);
+    case 4: return launch_k(k_producer_quant<4, WPR, P>, grid, 256, 0, st, dst, dsc, out, a, b, eps, astr, m, n);
+    case 8: return launch_k(k_producer_quant<8, WPR, P>, grid, 256, 0, st, dst, dsc, out, a, b, eps, astr, m, n);
+    default: return launch_k(k_producer_quant<16, WPR, P>, grid, 256, 0, st, dst, dsc, out, a, b, eps, astr, m, n);
+  }
+}
+
+template <Producer P>
+int launch_producer(int8_t *dst, float *dsc, float *out, const float *a, const float *b, float eps,
+                    long astr, int m, int n, cudaStream_t st, const char *what) {
+  if (m <= 0) return 0;
+  if (n <= 0 || n % 4 || n > 16384)
+    return set_error("%s: row length %d must be a positive multiple of 4 up to 16384", what, n);
+  if (astr < n || astr % 4) return set_error("%s: row stride %ld must be >= %d and a multiple of 4", what, astr, n);
+  if (!dst || !dsc || !a || !b) return set_error("%s: null pointer", what);
+  if ((uintptr_t)a % 16 || (uintptr_t)b % 16 || (uintptr_t)dst % 4 || (out && (uintptr_t)out % 16))
+    return set_error("%s: rows must be 16-byte aligned (codes 4-byte)", what);
+  const int n4 = n / 4;
+  // the quantize kernel's split: fewest warps per row holding 8 float4 per
+  // lane (16 past 8192 elements), more while the grid is small
+  int wpr = 1;
+  while (wpr < 8 && n4 > 32 * 8 * wpr) wpr *= 2;
+  const int sms = num_sms();
+  while (wpr < 8 && (long)m * wpr < 16L * sms && n4 >= 32 * 2 * (2 * wpr)) wpr *= 2;
+  const int need = (n4 + 32 * wpr - 1) / (32 * wpr);
+  const int vpt = need <= 2 ? 2 : need <= 4 ? 4 : need <= 8 ? 8 : 16;
+  const long rows_per_cta = 8 / wpr;
+  const int grid = (int)((m + rows_per_cta - 1) / rows_per_cta);
+  cudaError_t e;
+  switch (wpr) {
+    case 1: e = launch_wpr<P, 1>(vpt, grid, dst, dsc, out, a, b, eps, astr, m, n, st); break;
+    case 2: e = launch_wpr<P, 2>(vpt, grid, dst, dsc, out, a, b, eps, astr, m, n, st); break;
+    case 4: e = launch_wpr<P, 4>(vpt, grid, dst, dsc, out, a, b, eps, astr, m, n, st); break;
+    default: e = launch_wpr<P, 8>(vpt, grid, dst, dsc, out, a, b, eps, astr, m, n, st); break;
+  }
+  GCU_CUDA(e);
+  GCU_CUDA(cudaGetLastError());
+  return 0;
+}
+
+}  // namespace
+}  // namespace gcu
+
+using namespace gcu;
+
+GCU_EXPORT int gcu_dev_rmsnorm_quantize(int8_t *q, float *s, float *xn, const float *x, int xstr,
+                                        const float *weight, float eps, int m, int dim, void *stream) {
+  return launch_producer<RMSNORM>(q, s, xn, x, weight, eps, xstr == 0 ? dim : xstr, m, dim,
+                                  static_cast<cudaStream_t>(stream), "rmsnorm_quantize");
+}
+
+GCU_EXPORT int gcu_dev_geglu_quantize(int8_t *q, float *s, float *h, const float *gate,
+                                      const float *up, int m, int dim, void *stream) {
+  return launch_producer<GEGLU>(q, s, h, gate, up, 0.0f, dim, m, dim, static_cast<cudaStream_t>(stream),
+                                "geglu_quantize");
+}

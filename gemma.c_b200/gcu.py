@@ -63,6 +63,8 @@ SIGNATURES = {
     "gcu_dev_gemm_int8_rowshard": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _int, _vp]),
     "gcu_dev_quantize_gemm_int8_rowshard_multi": (_int, [ctypes.POINTER(GemvJob), _int, _vp, _vp, _vp, _int,
                                                          _int, _int, _vp, _vp]),
+    "gcu_dev_rmsnorm_quantize": (_int, [_vp, _vp, _vp, _vp, _int, _vp, ctypes.c_float, _int, _int, _vp]),
+    "gcu_dev_geglu_quantize": (_int, [_vp, _vp, _vp, _vp, _vp, _int, _int, _vp]),
 }
 # exported but not part of the public header (benchmark sweeps)
 EXTRA = {
@@ -306,3 +308,18 @@ def dev_quantize_gemm_int8_rowshard_multi(jobs_t, q, s, x, m, k, work=None, xstr
                                                            work.data_ptr() if work is not None else None,
                                                            _stream(stream)),
            "dev_quantize_gemm_int8_rowshard_multi")
+
+
+def dev_rmsnorm_quantize(q, s, x, weight, eps, m, dim, out=None, xstr=0, stream=None):
+    """gemma.c's rmsnorm then quantize_acts, fused: codes -> q, scales -> s,
+    the normalized rows -> out (optional)."""
+    _check(lib().gcu_dev_rmsnorm_quantize(q.data_ptr(), s.data_ptr(), out.data_ptr() if out is not None else None,
+                                          x.data_ptr(), xstr, weight.data_ptr(), float(eps), m, dim,
+                                          _stream(stream)), "dev_rmsnorm_quantize")
+
+
+def dev_geglu_quantize(q, s, gate, up, m, dim, out=None, stream=None):
+    """gemma.c's gelu(gate) * up then quantize_acts, fused."""
+    _check(lib().gcu_dev_geglu_quantize(q.data_ptr(), s.data_ptr(), out.data_ptr() if out is not None else None,
+                                        gate.data_ptr(), up.data_ptr(), m, dim, _stream(stream)),
+           "dev_geglu_quantize")

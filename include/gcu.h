@@ -157,6 +157,28 @@ int gcu_dev_quantize_gemm_int8_multi(const gcu_gemv_job *jobs, int njobs,
                                      int8_t *q, float *s, const float *x,
                                      int xstr, int m, int k, void *stream);
 
+/* ---- producers fused with quantize_acts -------------------------------------
+ * gemma.c quantizes each block input right after its RMSNorm (rmsnorm,
+ * gemma.c:2509-2524, at 4754 / 5026, then quantize_act(s) at 4768 / 5034) and
+ * the down projection's input right after the GeGLU gate (gelu with `mul`,
+ * gemma.c:4139-4170, at 4921 / 5379, then 4927 / 5389).  These compute the
+ * producer and quantize its result in one pass over device memory: codes to
+ * q (dense [m][dim]) and scales to s as gcu_dev_quantize_acts writes them,
+ * and the fp32 result to `out` unless it is NULL.  dim % 4 == 0, dim <= 16384,
+ * 16-byte aligned rows.  The quantize step is bit-exact on the computed
+ * values; those values agree with gemma.c's to ~1e-6 relative (a different
+ * summation order for the sum of squares, CUDA's tanhf), so a code can
+ * differ by one where a value sits that close to a rounding boundary.
+ * No single counterpart in the reference (each fuses two of its calls). */
+
+/* out = (x * rms) * (weight + 1), rms = 1 / sqrtf(mean(x^2) + eps); x rows at
+ * stride xstr floats (0 = dim), weight [dim]. */
+int gcu_dev_rmsnorm_quantize(int8_t *q, float *s, float *out, const float *x, int xstr,
+                             const float *weight, float eps, int m, int dim, void *stream);
+/* out = gelu_tanh(gate) * up, gate and up dense [m][dim]. */
+int gcu_dev_geglu_quantize(int8_t *q, float *s, float *out, const float *gate, const float *up,
+                           int m, int dim, void *stream);
+
 /* ---- row-sharded entry points (NCCL over NVLink) ---------------------------
  * No counterpart in the reference, which is single-process (README.md:614).
  * Rank r of `world` owns weight rows [r*n/world, (r+1)*n/world) of an n-row

@@ -163,3 +163,47 @@ void orc_quantize_weight_rows(int8_t *q, float *scales, const float *w, int n,
     }
   }
 }
+
+/* gemma-style RMSNorm of each row followed by quantize_act, the pair gemma.c
+ * runs on every block input: rmsnorm (gemma.c:2509-2524) at 4754 / 5026,
+ * then quantize_act / quantize_acts at 4768 / 5034.  Sequential fp32 sum of
+ * squares (the reference's -ffast-math build vectorizes it, so its last bits
+ * may differ), rms = 1 / sqrtf(sum / dim + eps), xn = (x * rms) * (w + 1).
+ * xn (optional) receives the normalized rows, q / s the codes and scales. */
+void orc_rmsnorm_quantize(int8_t *q, float *s, float *xn, const float *x, const float *w,
+                          float eps, int m, int dim) {
+  for (int i = 0; i < m; i++) {
+    const float *row = x + (size_t)i * dim;
+    float sq = 0.0f;
+    for (int d = 0; d < dim; d++)
+      sq += row[d] * row[d];
+    const float rms = 1.0f / sqrtf(sq / (float)dim + eps);
+    float tmp[16384];
+    for (int d = 0; d < dim; d++)
+      tmp[d] = row[d] * rms * (w[d] + 1.0f);
+    if (xn)
+      memcpy(xn + (size_t)i * dim, tmp, (size_t)dim * sizeof(float));
+    s[i] = orc_quantize_act(q + (size_t)i * dim, tmp, dim);
+  }
+}
+
+/* GeGLU gate followed by quantize_act: h = gelu_tanh(gate) * up
+ * (gemma.c:4139-4170, gelu with `mul`, called at 4921 / 5379), then
+ * quantize_act / quantize_acts on h (the down projection's input).
+ * gelu_tanh(x) = 0.5 x (1 + tanhf(sqrt(2/pi) (x + 0.044715 x^3))) in the
+ * reference's operation order; tanhf is this C library's. */
+void orc_geglu_quantize(int8_t *q, float *s, float *h, const float *gate, const float *up,
+                        int m, int dim) {
+  const float c = 0.79788456080287f;
+  for (int i = 0; i < m; i++) {
+    float tmp[16384];
+    for (int d = 0; d < dim; d++) {
+      const float x = gate[(size_t)i * dim + d];
+      const float g = 0.5f * x * (1.0f + tanhf(c * (x + 0.044715f * x * x * x)));
+      tmp[d] = g * up[(size_t)i * dim + d];
+    }
+    if (h)
+      memcpy(h + (size_t)i * dim, tmp, (size_t)dim * sizeof(float));
+    s[i] = orc_quantize_act(q + (size_t)i * dim, tmp, dim);
+  }
+}

@@ -79,6 +79,11 @@ def orc() -> ctypes.CDLL:
                                       ctypes.c_int, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int]
         lib.orc_quantize_weight_rows.restype = None
         lib.orc_quantize_weight_rows.argtypes = [_i8p, _f32p, _f32p, ctypes.c_int, ctypes.c_int]
+        lib.orc_rmsnorm_quantize.restype = None
+        lib.orc_rmsnorm_quantize.argtypes = [_i8p, _f32p, _f32p, _f32p, _f32p, ctypes.c_float,
+                                             ctypes.c_int, ctypes.c_int]
+        lib.orc_geglu_quantize.restype = None
+        lib.orc_geglu_quantize.argtypes = [_i8p, _f32p, _f32p, _f32p, _f32p, ctypes.c_int, ctypes.c_int]
         _orc = lib
     return _orc
 
@@ -164,6 +169,32 @@ def quantize_weight_rows(w: np.ndarray):
     return q, s
 
 
+def rmsnorm_quantize(x: np.ndarray, w: np.ndarray, eps: float):
+    """(m, dim) fp32 rows -> RMSNorm'd rows, their int8 codes and scales."""
+    x = np.ascontiguousarray(x, np.float32)
+    m, dim = x.shape
+    w = np.ascontiguousarray(w, np.float32)
+    xn = np.empty((m, dim), np.float32)
+    q = np.empty((m, dim), np.int8)
+    s = np.empty(m, np.float32)
+    orc().orc_rmsnorm_quantize(_ptr(q, _i8p), _ptr(s, _f32p), _ptr(xn, _f32p), _ptr(x, _f32p),
+                               _ptr(w, _f32p), eps, m, dim)
+    return xn, q, s
+
+
+def geglu_quantize(gate: np.ndarray, up: np.ndarray):
+    """(m, dim) gate and up rows -> gelu_tanh(gate) * up, its codes and scales."""
+    gate = np.ascontiguousarray(gate, np.float32)
+    up = np.ascontiguousarray(up, np.float32)
+    m, dim = gate.shape
+    h = np.empty((m, dim), np.float32)
+    q = np.empty((m, dim), np.int8)
+    s = np.empty(m, np.float32)
+    orc().orc_geglu_quantize(_ptr(q, _i8p), _ptr(s, _f32p), _ptr(h, _f32p), _ptr(gate, _f32p),
+                             _ptr(up, _f32p), m, dim)
+    return h, q, s
+
+
 # --------------------------------------------------------------------------
 # the compiled reference (gemma.c's own functions)
 # --------------------------------------------------------------------------
@@ -219,6 +250,10 @@ def ref(variant: str | None = None) -> ctypes.CDLL | None:
     lib.ref_gemm_int8.argtypes = [_f32p, ctypes.c_int, _i8p, ctypes.c_int, _f32p, _i8p, ctypes.c_int,
                                   _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]
     lib.ref_setup.restype = None
+    lib.ref_rmsnorm.restype = None
+    lib.ref_rmsnorm.argtypes = [_f32p, _f32p, _f32p, ctypes.c_int, ctypes.c_float]
+    lib.ref_gelu_mul.restype = None
+    lib.ref_gelu_mul.argtypes = [_f32p, _f32p, _f32p, ctypes.c_int, ctypes.c_int]
     lib.ref_isa.restype = ctypes.c_char_p
     lib.ref_gemv_job_size.restype = ctypes.c_int
     assert lib.ref_gemv_job_size() == ctypes.sizeof(GemvJob)
@@ -256,6 +291,25 @@ class Ref:
         self.lib.ref_quantize_acts(_ptr(dst, _i8p), _ptr(dsc, _f32p), _ptr(src, _f32p), sstr, m, n,
                                    self.threads)
         return dst, dsc
+
+    def rmsnorm_quantize(self, x, w, eps):
+        """gemma.c's rmsnorm on each row, then its quantize_acts."""
+        x = np.ascontiguousarray(x, np.float32)
+        w = np.ascontiguousarray(w, np.float32)
+        xn = np.empty_like(x)
+        for i in range(x.shape[0]):
+            self.lib.ref_rmsnorm(_ptr(xn[i], _f32p), _ptr(x[i], _f32p), _ptr(w, _f32p), x.shape[1], eps)
+        q, s = self.quantize_acts(xn)
+        return xn, q, s
+
+    def geglu_quantize(self, gate, up):
+        """gemma.c's gelu with `mul` (gate * up), then its quantize_acts."""
+        gate = np.ascontiguousarray(gate, np.float32)
+        up = np.ascontiguousarray(up, np.float32)
+        h = np.empty_like(gate)
+        self.lib.ref_gelu_mul(_ptr(h, _f32p), _ptr(gate, _f32p), _ptr(up, _f32p), gate.shape[0], gate.shape[1])
+        q, s = self.quantize_acts(h)
+        return h, q, s
 
     def gemv_int8(self, mat, matsc, vec, vsc, dst=None):
         mat = np.ascontiguousarray(mat, np.int8)

@@ -50,6 +50,17 @@ int ref_gemm_int8(float *dst, int dstr, const int8_t *mat, int mstr,
                    threads > 1, threads, NULL);
 }
 
+/* gemma.c:2509: gemma-style RMSNorm of one row (dst may equal src). */
+void ref_rmsnorm(float *dst, const float *src, const float *weight, int dim, float eps) {
+  rmsnorm(dst, src, weight, dim, eps, NULL);
+}
+
+/* gemma.c:4150: dst[i] = gelu_tanh(src[i] + bias) * mul[i] over rows x dim,
+ * here without bias and with `mul` (the GeGLU gate * up of 4921, 5379). */
+void ref_gelu_mul(float *dst, const float *src, const float *mul, int rows, int dim) {
+  gelu(dst, src, rows, dim, NULL, mul, false, 1, NULL);
+}
+
 /* gemma.c:484: GEMM_MC / GEMM_NC / GEMM_KC tile sizes from the environment. */
 void ref_setup(void) { setup_runtime_config(); }
 

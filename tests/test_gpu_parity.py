@@ -376,6 +376,68 @@ def test_full_size_config_shapes_sampled_rows(m, ns, k):
         assert_bits(y[rows].cpu().numpy(), O.gemm_int8(w.cpu().numpy(), sc.cpu().numpy(), xq, xs))
 
 
+def _rel(a, b):
+    return float(np.abs(np.asarray(a, np.float64) - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+@pytest.mark.parametrize("m,dim,xpad", [(1, 640, 0), (4, 1152, 0), (37, 2560, 8), (5, 3840, 0),
+                                        (3, 15360, 0), (300, 1152, 4), (2, 40, 0)])
+def test_rmsnorm_quantize_fused(m, dim, xpad):
+    # the fused kernel's fp32 output within BASELINE's 1e-5 relative of the
+    # reference's rmsnorm; its codes and scales are exactly quantize_acts of
+    # that output; against the reference the codes differ by at most one
+    xstr = dim + xpad
+    x = synth.activations(3300 + dim, m, xstr, outliers=True)
+    w = (synth.activations(3301 + dim, 1, dim)[0] * 0.1).astype(np.float32)
+    xt, wt = _dev(x), _dev(w)
+    q = torch.empty((m, dim), dtype=torch.int8, device="cuda")
+    s = torch.empty(m, dtype=torch.float32, device="cuda")
+    xn = torch.empty((m, dim), dtype=torch.float32, device="cuda")
+    gcu.dev_rmsnorm_quantize(q, s, xt, wt, 1e-6, m, dim, out=xn, xstr=xstr)
+    torch.cuda.synchronize()
+    gcu.check_device()
+    xn_g, q_g, s_g = xn.cpu().numpy(), q.cpu().numpy(), s.cpu().numpy()
+    q_e, s_e = O.quantize_acts(xn_g)
+    assert np.array_equal(q_g, q_e) and np.array_equal(bits(s_g), bits(s_e))
+    xn_o, q_o, s_o = O.rmsnorm_quantize(np.ascontiguousarray(x[:, :dim]), w, 1e-6)
+    assert _rel(xn_g, xn_o) < 1e-5 and _rel(s_g, s_o) < 1e-5
+    assert np.abs(q_g.astype(int) - q_o).max() <= 1 and (q_g != q_o).mean() < 1e-3
+
+
+@pytest.mark.parametrize("m,dim", [(1, 2048), (2, 6912), (8, 10240), (512, 6912), (3, 15360), (5, 40)])
+def test_geglu_quantize_fused(m, dim):
+    g = synth.activations(3400 + dim, m, dim)
+    u = synth.activations(3401 + dim, m, dim)
+    q = torch.empty((m, dim), dtype=torch.int8, device="cuda")
+    s = torch.empty(m, dtype=torch.float32, device="cuda")
+    h = torch.empty((m, dim), dtype=torch.float32, device="cuda")
+    gcu.dev_geglu_quantize(q, s, _dev(g), _dev(u), m, dim, out=h)
+    torch.cuda.synchronize()
+    gcu.check_device()
+    h_g, q_g, s_g = h.cpu().numpy(), q.cpu().numpy(), s.cpu().numpy()
+    q_e, s_e = O.quantize_acts(h_g)
+    assert np.array_equal(q_g, q_e) and np.array_equal(bits(s_g), bits(s_e))
+    h_o, q_o, s_o = O.geglu_quantize(g, u)
+    assert _rel(h_g, h_o) < 1e-5 and _rel(s_g, s_o) < 1e-5
+    assert np.abs(q_g.astype(int) - q_o).max() <= 1 and (q_g != q_o).mean() < 1e-3
+    # without the optional fp32 output the codes are the same
+    q2 = torch.empty_like(q)
+    s2 = torch.empty_like(s)
+    gcu.dev_geglu_quantize(q2, s2, _dev(g), _dev(u), m, dim)
+    torch.cuda.synchronize()
+    assert torch.equal(q2, q) and torch.equal(s2, s)
+
+
+def test_producers_reject_unsupported_rows():
+    x = torch.zeros((2, 18), dtype=torch.float32, device="cuda")
+    q = torch.empty((2, 18), dtype=torch.int8, device="cuda")
+    s = torch.empty(2, dtype=torch.float32, device="cuda")
+    with pytest.raises(gcu.GcuError, match="multiple of 4"):
+        gcu.dev_rmsnorm_quantize(q, s, x, x[0], 1e-6, 2, 18)
+    with pytest.raises(gcu.GcuError, match="multiple of 4"):
+        gcu.dev_geglu_quantize(q, s, x, x, 2, 18)
+
+
 def test_scale_linearity_property():
     # doubling every weight scale doubles every output exactly
     m, n, k = 256, 2048, 2048

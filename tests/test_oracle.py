@@ -125,6 +125,46 @@ def test_oracle_matches_reference_random():
         assert np.array_equal(bits(y1), bits(y2))
 
 
+def rel_err(a, b):
+    return float(np.abs(np.asarray(a, np.float64) - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+@pytest.mark.skipif(ref_lib is None, reason="reference build not present on this host")
+@pytest.mark.parametrize("m,dim", [(4, 640), (3, 1152), (2, 2560), (2, 3840), (2, 15360), (5, 40)])
+def test_producer_restatements_match_reference(m, dim):
+    # rmsnorm and gelu*up then quantize_acts: the restatement sums squares in
+    # order and uses this libm's tanhf; gemma.c's -ffast-math build
+    # vectorizes the sum, so fp32 values agree within BASELINE's 1e-5
+    # relative tolerance (1e-6 in practice) and the codes all but identically
+    R = O.Ref(threads=4)
+    x = synth.activations(70 + dim, m, dim, outliers=True)
+    w = (synth.activations(71 + dim, 1, dim)[0] * 0.1).astype(np.float32)
+    xn0, q0, s0 = R.rmsnorm_quantize(x, w, 1e-6)
+    xn1, q1, s1 = O.rmsnorm_quantize(x, w, 1e-6)
+    assert rel_err(xn1, xn0) < 1e-5
+    assert rel_err(s1, s0) < 1e-5
+    assert np.abs(q1.astype(int) - q0).max() <= 1 and (q1 != q0).mean() < 1e-3
+    g = synth.activations(72 + dim, m, dim)
+    u = synth.activations(73 + dim, m, dim)
+    h0, qg0, sg0 = R.geglu_quantize(g, u)
+    h1, qg1, sg1 = O.geglu_quantize(g, u)
+    assert rel_err(h1, h0) < 1e-5
+    assert rel_err(sg1, sg0) < 1e-5
+    assert np.abs(qg1.astype(int) - qg0).max() <= 1 and (qg1 != qg0).mean() < 1e-3
+
+
+def test_producer_quantize_step_is_quantize_act():
+    # the restated producers quantize exactly as quantize_acts does
+    x = synth.activations(80, 3, 1152, outliers=True)
+    w = (synth.activations(81, 1, 1152)[0] * 0.1).astype(np.float32)
+    xn, q, s = O.rmsnorm_quantize(x, w, 1e-6)
+    q2, s2 = O.quantize_acts(xn)
+    assert np.array_equal(q, q2) and np.array_equal(bits(s), bits(s2))
+    h, qg, sg = O.geglu_quantize(x, x * 0.5)
+    q3, s3 = O.quantize_acts(h)
+    assert np.array_equal(qg, q3) and np.array_equal(bits(sg), bits(s3))
+
+
 def test_synth_generator_is_deterministic():
     a = synth.normal(3, (1000,))
     b = synth.normal(3, (1000,))
