@@ -63,6 +63,7 @@ enum DevErr : unsigned int {
   DEV_TIMEOUT_DRAIN = 4,  // draining in-flight copies after an error
   DEV_TIMEOUT_PEER = 6,   // a rank of a fused all-gather never signalled
   DEV_TIMEOUT_SPLIT = 7,  // a split-K CTA waited too long for the other splits
+  DEV_TIMEOUT_SELFTEST = 8,  // gcu_selftest_bounded_wait's wait (nothing ever completes it)
 };
 unsigned int *dev_error_word();  // device address of the error word
 
@@ -195,6 +196,23 @@ __device__ __forceinline__ int ld_acquire_gpu(const int *p) {
   int v;
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
+}
+
+// Spin until *flag >= target, acquiring at system scope (SYS: the flag is
+// written by other GPUs) or gpu scope, for at most budget_ns after t0.
+// Returns false, with `code` recorded in the error word, on timeout.
+template <bool SYS>
+__device__ __forceinline__ bool flag_wait_geq(const int *flag, int target, uint64_t t0,
+                                              unsigned int *err, unsigned int code,
+                                              uint64_t budget_ns = 2000000000ull) {
+  while ((SYS ? ld_acquire_sys(flag) : ld_acquire_gpu(flag)) < target) {
+    if (globaltimer() - t0 > budget_ns) {
+      atomicCAS(err, 0u, code);
+      return false;
+    }
+    __nanosleep(32);
+  }
+  return true;
 }
 
 // ---- mbarrier --------------------------------------------------------------

@@ -510,14 +510,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_tc(const __grid_constan
           share_scales<C, BN>(p, job, w, 0, my_nb, sc);
           if (threadIdx.x == 64) {
             atomicAdd(p.counters + w.tile, 1);
-            const uint64_t t0 = ptx::globaltimer();
-            while (ptx::ld_acquire_gpu(p.counters + w.tile) < p.splits) {
-              if (ptx::globaltimer() - t0 > 2000000000ull) {
-                atomicCAS(p.err, 0u, (unsigned int)DEV_TIMEOUT_SPLIT);
-                break;
-              }
-              __nanosleep(32);
-            }
+            ptx::flag_wait_geq<false>(p.counters + w.tile, p.splits, ptx::globaltimer(), p.err,
+                                      DEV_TIMEOUT_SPLIT);
           }
           ptx::named_bar_sync(1, kEpiThreads);
           reduce_share<C, BN>(p, job, w, kPartInt4, my_nb, sc);

@@ -304,14 +304,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, cons
         __threadfence_system();
         for (int pr = 0; pr < po.world; ++pr) atomicAdd_system(po.flag_peer[pr], 1);
       }
-      const int target = (epoch0 + 1) * po.world;
-      while (ptx::ld_acquire_sys(po.flag_local) < target) {
-        if (ptx::globaltimer() - t0 > 2000000000ull) {
-          atomicCAS(po.err, 0u, (unsigned int)DEV_TIMEOUT_PEER);
-          break;
-        }
-        __nanosleep(32);
-      }
+      ptx::flag_wait_geq<true>(po.flag_local, (epoch0 + 1) * po.world, t0, po.err, DEV_TIMEOUT_PEER);
     }
     __syncthreads();
     // every rank's slices are ready in its own half: pull them into dst, 16

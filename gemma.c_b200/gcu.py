@@ -66,8 +66,9 @@ SIGNATURES = {
     "gcu_dev_rmsnorm_quantize": (_int, [_vp, _vp, _vp, _vp, _int, _vp, ctypes.c_float, _int, _int, _vp]),
     "gcu_dev_geglu_quantize": (_int, [_vp, _vp, _vp, _vp, _vp, _int, _int, _vp]),
 }
-# exported but not part of the public header (benchmark sweeps)
+# exported but not part of the public header (benchmark sweeps, self-test)
 EXTRA = {
+    "gcu_selftest_bounded_wait": (_int, [_int, _int, ctypes.POINTER(ctypes.c_ulonglong), _vp]),
     "gcu_dev_gemm_int8_multi_tuned": (_int, [ctypes.POINTER(GemvJob), _int, _vp, _int, _vp, _int, _int, _int,
                                              _int, _int, _vp]),
     "gcu_dev_gemm_int8_tuned": (_int, [_vp, _int, _vp, _int, _vp, _vp, _int, _vp, _int, _int, _int,
@@ -118,6 +119,17 @@ def shutdown() -> None:
 
 def check_device() -> None:
     _check(lib().gcu_check_device(), "device")
+
+
+def selftest_bounded_wait(mode: int, budget_us: int, stream=None) -> int:
+    """Run one device-side wait (mode 0: an mbarrier, 1: a global flag) on
+    something that never completes, with a budget of `budget_us`; returns the
+    nanoseconds the kernel waited.  Leaves the timeout code in the device error
+    word for the next check to report."""
+    ns = ctypes.c_ulonglong(0)
+    _check(lib().gcu_selftest_bounded_wait(mode, budget_us, ctypes.byref(ns), _stream(stream)),
+           "selftest_bounded_wait")
+    return ns.value
 
 
 def register_weight(q: np.ndarray, scales: np.ndarray) -> None:
