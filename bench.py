@@ -2,7 +2,8 @@
 """Benchmark of the W8A8 matmul hot path on B200 (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload prefill1b|decode270m|lmhead4b|prefill4b|prefill12b|decode12b]
+                    [--workload prefill1b|decode270m|lmhead4b|prefill4b|prefill12b|decode12b|
+                                upload1b|upload4b]
 
 Workloads (synthetic seeded data, no checkpoints):
   prefill1b   configs[1], the default: Gemma-3-1B-shaped prefill, M=512
@@ -23,6 +24,9 @@ Workloads (synthetic seeded data, no checkpoints):
               all-gathered (strong scaling).
   decode12b   configs[4] decode: Gemma-3-12B, batch 1, 48 layers + lm_head;
               at N>1 the FFN and lm_head rows are sharded (strong scaling).
+  upload1b    not a BASELINE metric: gcu_register_model of a synthetic `-q`
+  upload4b    model image (1B text / 4B text + SigLIP), GB/s of matmul
+              weights into HBM against the measured PCIe copy rate.
 
 `value` is measured with inputs resident in HBM, one CUDA graph replay per
 step, CUDA events on the launching stream, max over ranks.  `e2e` is the same
@@ -786,6 +790,157 @@ def cpu_baseline(wl, seconds):
 
 
 # ---------------------------------------------------------------------------
+# model upload (gcu_register_model): a `-q` model image -> one HBM arena
+# ---------------------------------------------------------------------------
+UPLOAD = {"upload1b": ("Gemma-3-1B text decoder", "TEXT_1B", None),
+          "upload4b": ("Gemma-3-4B text decoder + SigLIP tower", "TEXT_4B", "VISION_SIGLIP")}
+
+
+def run_upload(args):
+    """One step = gcu_register_model of a synthetic `-q` image (timed on the
+    host clock around the synchronous call: parse, arena allocation, packed
+    pinned copies, registry insert), then gcu_unregister_arena (untimed).
+    Two sources: the image resident in process memory, and a FRESH mmap of
+    the same file in the page cache every step (gemma.c's mmap path,
+    gemma.c:1946-2043: each step pays the page faults).  Beside them: the
+    per-weight gcu_register_weight loop, a plain pinned cudaMemcpy (the
+    PCIe roofline) and the reference's own read_gemma_model of the file."""
+    import mmap
+    import tempfile
+
+    import numpy as np
+    import torch
+
+    import binfmt
+    import gcu
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    gcu.init(0)
+    torch.cuda.set_device(0)
+    title, tkey, vkey = UPLOAD[args.workload]
+    text, vision = getattr(binfmt, tkey), (getattr(binfmt, vkey) if vkey else None)
+    buf, _ = binfmt.image(text, vision, seed=1, fast=True)
+    recs = gcu.bin_qtensors(buf)
+    wbytes = sum(r["rows"] * r["k"] + 4 * r["rows"] for r in recs)
+
+    arenas = []
+
+    def step_resident():
+        arenas.append(gcu.register_model(buf))
+
+    def drop():
+        while arenas:
+            gcu.unregister_arena(arenas.pop())
+
+    for _ in range(args.warmup):
+        step_resident()
+        drop()
+    ts = []
+    clocks = Clocks(0)
+    clocks.start()
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        step_resident()
+        ts.append(time.perf_counter() - t0)
+        drop()
+    clk = clocks.stop()
+    t_res = statistics.median(ts)
+
+    # fresh mapping of the page-cached file per step
+    tmpdir = tempfile.mkdtemp(prefix="gcu_upload_")
+    path = os.path.join(tmpdir, "model.bin")
+    buf.tofile(path)
+    ts = []
+    for i in range(args.warmup + args.steps):
+        with open(path, "rb") as f:
+            mm = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ)
+        img = np.frombuffer(mm, np.uint8)
+        t0 = time.perf_counter()
+        a = gcu.register_model(img)
+        t1 = time.perf_counter()
+        gcu.unregister_arena(a)
+        del img
+        mm.close()
+        if i >= args.warmup:
+            ts.append(t1 - t0)
+    t_mmap = statistics.median(ts)
+
+    # per-weight registration (one cudaMalloc + two pageable copies each)
+    def per_weight():
+        views = [binfmt.qtensor_arrays(buf, r) for r in recs]
+        for q, s in views:
+            gcu.lib().gcu_register_weight(q.ctypes.data, s.ctypes.data, q.shape[0], q.shape[1])
+        for q, _ in views:
+            gcu.lib().gcu_unregister_weight(q.ctypes.data)
+    per_weight()
+    ts = []
+    for _ in range(max(1, min(args.steps, 3))):
+        views = [binfmt.qtensor_arrays(buf, r) for r in recs]
+        t0 = time.perf_counter()
+        for q, s in views:
+            gcu.lib().gcu_register_weight(q.ctypes.data, s.ctypes.data, q.shape[0], q.shape[1])
+        ts.append(time.perf_counter() - t0)
+        for q, _ in views:
+            gcu.lib().gcu_unregister_weight(q.ctypes.data)
+    t_pw = statistics.median(ts)
+
+    # PCIe roofline: one pinned 256 MB host->device copy, CUDA events
+    hb = torch.empty(256 << 20, dtype=torch.uint8, pin_memory=True)
+    db = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    for _ in range(3):
+        db.copy_(hb, non_blocking=True)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(5):
+        db.copy_(hb, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    pcie = 5 * hb.numel() / (e0.elapsed_time(e1) * 1e-3) / 1e9
+    del hb, db
+
+    ref = None
+    if not args.no_cpu:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle
+        variant = oracle.ref_variant()
+        lib = oracle.ref(variant) if variant else None
+        if lib is not None and hasattr(lib, "ref_read_model_seconds"):
+            R = oracle.Ref(variant, threads=1)
+            R.read_model_seconds(path)
+            tr = statistics.median(R.read_model_seconds(path) for _ in range(3))
+            ref = {"value": wbytes / tr / 1e9, "unit": "GB/s", "cores": 1, "kind": "reference",
+                   "sample": f"gemma.c read_gemma_model of the same {buf.nbytes / 1e9:.2f} GB file (page cache warm), "
+                             f"host memory only, median of 3",
+                   "seconds": tr}
+    os.unlink(path)
+    os.rmdir(tmpdir)
+
+    v = wbytes / t_mmap / 1e9
+    out = {"metric": "model registration: matmul weights of a -q model image -> HBM (GB/s)",
+           "value": v, "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": t_mmap * 1e3, "higher_is_better": True, "scaling": "none", "vs_baseline": None,
+           "dtype": "u8 (int8 weights + fp32 scales, byte copy)", "data": "synthetic", "impl": "ours",
+           "config": {"workload": f"{args.workload}: {title}, {len(recs)} QTensors, {wbytes / 1e9:.3f} GB of "
+                                  f"weights in a {buf.nbytes / 1e9:.3f} GB image",
+                      "source": "fresh mmap of the page-cached file per step (value); resident buffer "
+                                "(resident_gbs)",
+                      "timing": "host clock around the synchronous gcu_register_model, median of steps"},
+           "resident_gbs": wbytes / t_res / 1e9,
+           "per_weight_gbs": wbytes / t_pw / 1e9,
+           "roofline": {"bound": "pcie", "achieved": v, "peak": pcie, "unit": "GB/s", "frac": v / pcie,
+                        "peak_src": "pinned 256 MB cudaMemcpy host->device measured in this run",
+                        "resident_frac": wbytes / t_res / 1e9 / pcie, "traffic": None},
+           "clocks": clk, "gpu_launches": 0,
+           "copy_engine": "no kernels: cudaMemcpyAsync of 8 MB packed pinned slots"}
+    if ref is not None:
+        out["cpu_baseline"] = ref
+    print(json.dumps(out), flush=True)
+
+
+# ---------------------------------------------------------------------------
 # reference arm: the reference's own CPU implementation of the path
 # ---------------------------------------------------------------------------
 def run_reference(args):
@@ -829,7 +984,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="prefill1b", choices=list(PREFILL) + list(DECODE) + ["lmhead4b"])
+    ap.add_argument("--workload", default="prefill1b",
+                    choices=list(PREFILL) + list(DECODE) + ["lmhead4b"] + list(UPLOAD))
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--unfused", action="store_true",
                     help="decode: quantize and GEMV as separate launches (the reference's call split)")
@@ -843,7 +999,13 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.workload in UPLOAD:
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the model-upload line carries the reference's "
+                              "read_gemma_model timing as its cpu_baseline"}))
+        else:
+            run_upload(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

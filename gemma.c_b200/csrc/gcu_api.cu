@@ -218,12 +218,64 @@ struct WeightEntry {
   int8_t *dq;
   float *ds;
   int rows, k;
+  int arena;  // 0: dq/ds are the entry's own allocations; else the arena holding them
+};
+// one device allocation holding many registered weights (gcu_register_qtensors)
+struct Arena {
+  int device;
+  void *base;
+  size_t bytes;
+  std::vector<uintptr_t> keys;  // q begins of its entries
 };
 static std::shared_mutex g_reg_mu;
 // keyed by (device, host begin)
 static std::map<std::pair<int, uintptr_t>, WeightEntry> g_q;
 static std::map<std::pair<int, uintptr_t>, uintptr_t> g_s;  // scales begin -> q begin
+static std::map<int, Arena> g_arenas;
+static int g_next_arena = 1;
 static size_t g_reg_bytes = 0;
+
+int calling_device() { return current_device(); }
+
+// true if [p, p+bytes) meets a registered range of kind Q (int8) or S
+// (scales) on device d; the caller holds g_reg_mu
+static bool overlaps_locked(int d, uintptr_t a, size_t bytes, bool q) {
+  if (q) {
+    auto it = g_q.lower_bound({d, a + bytes});
+    if (it == g_q.begin()) return false;
+    --it;
+    return it->first.first == d && it->second.q1 > a;
+  }
+  auto it = g_s.lower_bound({d, a + bytes});
+  if (it == g_s.begin()) return false;
+  --it;
+  return it->first.first == d && g_q.at({d, it->second}).s1 > a;
+}
+
+int registry_add_arena(const RegRec *recs, int n, void *base, size_t bytes, int *arena_id) {
+  const int d = current_device();
+  std::unique_lock<std::shared_mutex> lk(g_reg_mu);
+  for (int i = 0; i < n; ++i) {
+    const size_t qb = (size_t)recs[i].rows * recs[i].k, sb = (size_t)recs[i].rows * sizeof(float);
+    if (overlaps_locked(d, recs[i].q, qb, true) || overlaps_locked(d, recs[i].s, sb, false))
+      return set_error("register_qtensors: tensor %d overlaps a registered weight", i);
+  }
+  const int id = g_next_arena++;
+  Arena &ar = g_arenas[id];
+  ar = Arena{d, base, bytes, {}};
+  for (int i = 0; i < n; ++i) {
+    const RegRec &r = recs[i];
+    const size_t qb = (size_t)r.rows * r.k, sb = (size_t)r.rows * sizeof(float);
+    WeightEntry e{r.q, r.q + qb, r.s, r.s + sb, (int8_t *)base + r.dq_off,
+                  (float *)((char *)base + r.ds_off), r.rows, r.k, id};
+    g_q[{d, e.q0}] = e;
+    g_s[{d, e.s0}] = e.q0;
+    ar.keys.push_back(e.q0);
+  }
+  g_reg_bytes += bytes;
+  if (arena_id) *arena_id = id;
+  return 0;
+}
 
 // device address for host range [p, p+bytes) inside a registered weight
 static const void *lookup_q(const void *p, size_t bytes) {
@@ -358,8 +410,13 @@ GCU_EXPORT int gcu_register_weight(const int8_t *q, const float *scales, int row
     if (g_q.count({d, (uintptr_t)q})) return 0;  // already registered
   }
   const size_t qb = (size_t)rows * k, sb = (size_t)rows * sizeof(float);
+  {
+    std::shared_lock<std::shared_mutex> lk(g_reg_mu);
+    if (overlaps_locked(d, (uintptr_t)q, qb, true) || overlaps_locked(d, (uintptr_t)scales, sb, false))
+      return set_error("gcu_register_weight: overlaps a registered weight");
+  }
   WeightEntry e{(uintptr_t)q, (uintptr_t)q + qb, (uintptr_t)scales, (uintptr_t)scales + sb,
-                nullptr, nullptr, rows, k};
+                nullptr, nullptr, rows, k, 0};
   GCU_CUDA(cudaMalloc(&e.dq, qb));
   if (cudaMalloc(&e.ds, sb) != cudaSuccess) {
     cudaFree(e.dq);
@@ -384,6 +441,8 @@ GCU_EXPORT int gcu_unregister_weight(const int8_t *q) {
   std::unique_lock<std::shared_mutex> lk(g_reg_mu);
   auto it = g_q.find({d, (uintptr_t)q});
   if (it == g_q.end()) return set_error("gcu_unregister_weight: not registered");
+  if (it->second.arena)
+    return set_error("gcu_unregister_weight: part of arena %d (gcu_unregister_arena)", it->second.arena);
   WeightEntry e = it->second;
   g_q.erase(it);
   g_s.erase({d, e.s0});
@@ -391,6 +450,28 @@ GCU_EXPORT int gcu_unregister_weight(const int8_t *q) {
   cudaDeviceSynchronize();
   cudaFree(e.dq);
   cudaFree(e.ds);
+  return 0;
+}
+
+GCU_EXPORT int gcu_unregister_arena(int arena) {
+  std::unique_lock<std::shared_mutex> lk(g_reg_mu);
+  auto it = g_arenas.find(arena);
+  if (it == g_arenas.end()) return set_error("gcu_unregister_arena: no arena %d", arena);
+  Arena ar = it->second;
+  g_arenas.erase(it);
+  for (uintptr_t key : ar.keys) {
+    auto e = g_q.find({ar.device, key});
+    if (e == g_q.end()) continue;
+    g_s.erase({ar.device, e->second.s0});
+    g_q.erase(e);
+  }
+  g_reg_bytes -= ar.bytes;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(ar.device);
+  cudaDeviceSynchronize();
+  cudaFree(ar.base);
+  cudaSetDevice(prev);
   return 0;
 }
 
@@ -404,11 +485,14 @@ GCU_EXPORT int gcu_shutdown(void) {
   {
     std::unique_lock<std::shared_mutex> lk(g_reg_mu);
     for (auto &kv : g_q) {
+      if (kv.second.arena) continue;
       cudaFree(kv.second.dq);
       cudaFree(kv.second.ds);
     }
+    for (auto &kv : g_arenas) cudaFree(kv.second.base);
     g_q.clear();
     g_s.clear();
+    g_arenas.clear();
     g_reg_bytes = 0;
   }
   {
@@ -419,6 +503,7 @@ GCU_EXPORT int gcu_shutdown(void) {
     }
     g_ws.clear();
   }
+  release_staging();
   ThreadCtx &c = t_ctx;
   c.in.release();
   c.in2.release();

@@ -68,6 +68,22 @@ enum DevErr : unsigned int {
 unsigned int *dev_error_word();  // device address of the error word
 
 // ---------------------------------------------------------------------------
+// weight registry (gcu_api.cu)
+// ---------------------------------------------------------------------------
+int calling_device();  // the calling thread's device (gcu_init)
+// a weight whose device copy lives at byte offsets dq_off / ds_off of an arena
+struct RegRec {
+  uintptr_t q, s;  // host int8 values / scales
+  int rows, k;
+  size_t dq_off, ds_off;
+};
+// Register n weights held by the device allocation `base` (`bytes`), which
+// the registry then owns; fails, owning nothing, if any overlaps a weight
+// already registered.
+int registry_add_arena(const RegRec *recs, int n, void *base, size_t bytes, int *arena_id);
+void release_staging();  // free the model uploader's pinned slots (gcu_model.cu)
+
+// ---------------------------------------------------------------------------
 // kernel launchers (defined in k_*.cu)
 // ---------------------------------------------------------------------------
 int launch_quantize_rows(int8_t *dst, float *dsc, const float *src, long sstr,

@@ -29,6 +29,18 @@ class GemvJob(ctypes.Structure):
     _fields_ = [("w", ctypes.c_void_p), ("sc", ctypes.c_void_p), ("dst", ctypes.c_void_p), ("m", ctypes.c_int)]
 
 
+class QTensor(ctypes.Structure):
+    """gcu_qtensor: one matmul weight of a model image (gemma.c:1102 QTensor
+    plus its shape and which weight it is)."""
+    _fields_ = [("q", ctypes.c_void_p), ("scales", ctypes.c_void_p), ("rows", ctypes.c_int),
+                ("k", ctypes.c_int), ("kind", ctypes.c_int), ("layer", ctypes.c_int)]
+
+
+# gcu_qt_kind
+QT_KINDS = ("lm_head", "wq", "wk", "wv", "wo", "w1", "w2", "w3",
+            "vwq", "vwk", "vwv", "vwo", "vw1", "vw2", "vproj")
+
+
 class GcuError(RuntimeError):
     pass
 
@@ -43,6 +55,10 @@ SIGNATURES = {
     "gcu_register_weight": (_int, [_vp, _vp, _int, _int]),
     "gcu_unregister_weight": (_int, [_vp]),
     "gcu_registered_bytes": (ctypes.c_size_t, []),
+    "gcu_bin_qtensors": (_int, [_vp, ctypes.c_size_t, _int, ctypes.POINTER(QTensor), _int]),
+    "gcu_register_qtensors": (_int, [ctypes.POINTER(QTensor), _int, ctypes.POINTER(_int)]),
+    "gcu_register_model": (_int, [_vp, ctypes.c_size_t, _int, ctypes.POINTER(_int)]),
+    "gcu_unregister_arena": (_int, [_int]),
     "gcu_quantize_act": (ctypes.c_float, [_vp, _vp, _int]),
     "gcu_quantize_acts": (_int, [_vp, _vp, _vp, _int, _int, _int]),
     "gcu_gemv_int8": (_int, [_vp, _vp, _vp, _vp, ctypes.c_float, _int, _int]),
@@ -142,6 +158,51 @@ def register_weight(q: np.ndarray, scales: np.ndarray) -> None:
 
 def unregister_weight(q: np.ndarray) -> None:
     _check(lib().gcu_unregister_weight(_p(q)), "unregister_weight")
+
+
+def bin_qtensors(image: np.ndarray, allow_mm: bool = True) -> list[dict]:
+    """The matmul QTensors of a `-q` model image (uint8 array): kind, layer,
+    rows, k and the BYTE OFFSETS of the int8 values and scales in the image.
+    Host only."""
+    assert image.dtype == np.uint8 and image.flags["C_CONTIGUOUS"]
+    n = lib().gcu_bin_qtensors(_p(image), image.nbytes, int(allow_mm), None, 0)
+    if n < 0:
+        raise GcuError(f"bin_qtensors: {lib().gcu_last_error().decode()}")
+    recs = (QTensor * max(n, 1))()
+    lib().gcu_bin_qtensors(_p(image), image.nbytes, int(allow_mm), recs, n)
+    base = _p(image)
+    return [{"kind": QT_KINDS[r.kind], "layer": r.layer, "rows": r.rows, "k": r.k,
+             "q_off": r.q - base, "s_off": r.scales - base} for r in recs[:n]]
+
+
+def register_model(image: np.ndarray, allow_mm: bool = True) -> int:
+    """Upload every matmul weight of a model image as one arena; returns its
+    handle.  The image must stay alive and unchanged while registered."""
+    assert image.dtype == np.uint8 and image.flags["C_CONTIGUOUS"]
+    arena = _int(0)
+    _check(lib().gcu_register_model(_p(image), image.nbytes, int(allow_mm), ctypes.byref(arena)),
+           "register_model")
+    return arena.value
+
+
+def register_qtensors(tensors) -> int:
+    """Upload (q, scales) pairs of numpy arrays as one arena; returns its handle."""
+    recs = (QTensor * len(tensors))()
+    for r, (q, sc) in zip(recs, tensors):
+        assert q.dtype == np.int8 and q.ndim == 2 and q.flags["C_CONTIGUOUS"]
+        assert sc.dtype == np.float32 and sc.shape == (q.shape[0],)
+        r.q, r.scales, r.rows, r.k, r.kind, r.layer = _p(q), _p(sc), q.shape[0], q.shape[1], 0, -1
+    arena = _int(0)
+    _check(lib().gcu_register_qtensors(recs, len(tensors), ctypes.byref(arena)), "register_qtensors")
+    return arena.value
+
+
+def unregister_arena(arena: int) -> None:
+    _check(lib().gcu_unregister_arena(arena), "unregister_arena")
+
+
+def registered_bytes() -> int:
+    return lib().gcu_registered_bytes()
 
 
 # --------------------------------------------------------------------------

@@ -60,6 +60,48 @@ int gcu_unregister_weight(const int8_t *q);
 /* Bytes of device memory held by registered weights. */
 size_t gcu_registered_bytes(void);
 
+/* ---- model images: every matmul weight of a `-q` .bin at once -------------
+ * A W8A8 model file (export.py -q; header "GEMA" "f32" 'Q', gemma.c:1915-1940)
+ * holds, after its configs (gemma.c:723-865) and tokenizer (gemma.c:905-990),
+ * every QTensor back to back in mmap_text_decoder's / mmap_vision_encoder's
+ * order (gemma.c:1470-1560, 1765-1875).  These entry points find the
+ * QTensors the matmul path uses in such an image (the mmap gemma.c made,
+ * GemmaModel.mm_data / mm_sz, gemma.c:2005-2018, or the file read into memory)
+ * and upload them as ONE device allocation: host threads pack pinned staging
+ * slots in the device layout while the copy engine drains earlier slots. */
+typedef enum {
+  GCU_QT_LM_HEAD = 0, /* text embedding, tied lm_head (gemma.c:1398-1406) */
+  GCU_QT_WQ, GCU_QT_WK, GCU_QT_WV, GCU_QT_WO, /* text attention, per layer */
+  GCU_QT_W1, GCU_QT_W2, GCU_QT_W3,            /* text FFN up, gate, down */
+  GCU_QT_VWQ, GCU_QT_VWK, GCU_QT_VWV, GCU_QT_VWO, /* SigLIP attention */
+  GCU_QT_VW1, GCU_QT_VW2,                         /* SigLIP fc1, fc2 */
+  GCU_QT_VPROJ                                    /* multimodal projection */
+} gcu_qt_kind;
+
+typedef struct {
+  const int8_t *q;      /* int8 [rows][k] */
+  const float *scales;  /* fp32 [rows] */
+  int rows, k;
+  int kind;             /* gcu_qt_kind */
+  int layer;            /* layer index, -1 for LM_HEAD and VPROJ */
+} gcu_qtensor;
+
+/* List the matmul QTensors of a model image of `size` bytes: the text
+ * decoder's, plus the vision encoder's when the file is multimodal and
+ * allow_mm is set (gemma.c's allow_mm, 1970-1983).  Fills up to cap records
+ * (out may be NULL) and returns how many there are, or -1 with a message for
+ * an image that is not a well-formed f32 W8A8 model or is truncated.  Host
+ * only: needs no GPU. */
+int gcu_bin_qtensors(const void *image, size_t size, int allow_mm, gcu_qtensor *out, int cap);
+/* Register n QTensors (any host memory) as one device allocation; *arena
+ * (may be NULL) receives its handle.  Each tensor then resolves like a
+ * gcu_register_weight one.  Tensors already registered are an error. */
+int gcu_register_qtensors(const gcu_qtensor *list, int n, int *arena);
+/* gcu_bin_qtensors + gcu_register_qtensors on a model image. */
+int gcu_register_model(const void *image, size_t size, int allow_mm, int *arena);
+/* Drop an arena's tensors from the registry and free its device memory. */
+int gcu_unregister_arena(int arena);
+
 /* ---- host-pointer entry points (gemma.c signatures) ----------------------- */
 
 /* gemma.c:2590 quantize_act: per-vector symmetric int8 of vec[0..dim);

@@ -255,6 +255,13 @@ def ref(variant: str | None = None) -> ctypes.CDLL | None:
     lib.ref_gelu_mul.restype = None
     lib.ref_gelu_mul.argtypes = [_f32p, _f32p, _f32p, ctypes.c_int, ctypes.c_int]
     lib.ref_isa.restype = ctypes.c_char_p
+    if hasattr(lib, "ref_read_model_seconds"):
+        lib.ref_read_model_seconds.restype = ctypes.c_double
+        lib.ref_read_model_seconds.argtypes = [ctypes.c_char_p, ctypes.c_int]
+    if hasattr(lib, "ref_bin_layout"):
+        lib.ref_bin_layout.restype = ctypes.c_int
+        lib.ref_bin_layout.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(ctypes.c_longlong),
+                                       ctypes.c_int]
     lib.ref_gemv_job_size.restype = ctypes.c_int
     assert lib.ref_gemv_job_size() == ctypes.sizeof(GemvJob)
     lib.ref_setup()
@@ -291,6 +298,27 @@ class Ref:
         self.lib.ref_quantize_acts(_ptr(dst, _i8p), _ptr(dsc, _f32p), _ptr(src, _f32p), sstr, m, n,
                                    self.threads)
         return dst, dsc
+
+    def bin_layout(self, path: str, allow_mm: bool = True):
+        """The matmul QTensors gemma.c's mmap_gemma_model finds in a model
+        file, as gcu_bin_qtensors lists them (offsets from the file start)."""
+        kinds = ("lm_head", "wq", "wk", "wv", "wo", "w1", "w2", "w3",
+                 "vwq", "vwk", "vwv", "vwo", "vw1", "vw2", "vproj")
+        n = self.lib.ref_bin_layout(path.encode(), int(allow_mm), None, 0)
+        if n < 0:
+            raise RuntimeError(f"the reference refused {path}")
+        rec = (ctypes.c_longlong * (6 * max(n, 1)))()
+        self.lib.ref_bin_layout(path.encode(), int(allow_mm), rec, n)
+        return [{"kind": kinds[rec[6 * i]], "layer": int(rec[6 * i + 1]), "rows": int(rec[6 * i + 4]),
+                 "k": int(rec[6 * i + 5]), "q_off": int(rec[6 * i + 2]), "s_off": int(rec[6 * i + 3])}
+                for i in range(n)]
+
+    def read_model_seconds(self, path: str, allow_mm: bool = True) -> float:
+        """Seconds gemma.c's read_gemma_model takes to load the file."""
+        t = self.lib.ref_read_model_seconds(path.encode(), int(allow_mm))
+        if t < 0:
+            raise RuntimeError(f"the reference refused {path}")
+        return t
 
     def rmsnorm_quantize(self, x, w, eps):
         """gemma.c's rmsnorm on each row, then its quantize_acts."""

@@ -80,3 +80,77 @@ const char *ref_isa(void) {
   return "portable";
 #endif
 }
+
+/* gemma.c:1946 mmap_gemma_model, walked like its users do: every QTensor of
+ * the matmul path as six numbers (kind, layer, int8 offset, scales offset,
+ * rows, k), offsets from the mapping's base, in the order mmap_text_decoder
+ * (gemma.c:1470) and mmap_vision_encoder (gemma.c:1765) lay them out.  The
+ * kind numbers are gcu.h's gcu_qt_kind.  Returns the count, or -1 when the
+ * reference refuses the file. */
+int ref_bin_layout(const char *path, int allow_mm, long long *rec, int cap) {
+  GemmaModel *m = mmap_gemma_model(path, allow_mm != 0);
+  if (m == NULL || !m->quant) {
+    if (m) munmap_gemma_model(m);
+    return -1;
+  }
+  const uint8_t *base = (const uint8_t *)m->mm_data;
+  int n = 0;
+#define REF_PUT(KIND, LAYER, QT, ROWS, K)                            \
+  do {                                                               \
+    if (n < cap) {                                                   \
+      long long *r = rec + 6 * n;                                    \
+      r[0] = (KIND);                                                 \
+      r[1] = (LAYER);                                                \
+      r[2] = (long long)((const uint8_t *)(QT)->i8.q - base);        \
+      r[3] = (long long)((const uint8_t *)(QT)->i8.scales - base);   \
+      r[4] = (ROWS);                                                 \
+      r[5] = (K);                                                    \
+    }                                                                \
+    n++;                                                             \
+  } while (0)
+  const TextDecoder *dec = m->decoder;
+  const TextConfig *tc = dec->config;
+  const int q_sz = tc->n_heads * tc->hdim, kv_sz = tc->nkv * tc->hdim;
+  REF_PUT(0, -1, dec->emb, tc->nvocab, tc->dim);
+  for (int l = 0; l < tc->nl; l++) {
+    const TextDecoderLayer *L = dec->layers[l];
+    REF_PUT(1, l, L->wq, q_sz, tc->dim);
+    REF_PUT(2, l, L->wk, kv_sz, tc->dim);
+    REF_PUT(3, l, L->wv, kv_sz, tc->dim);
+    REF_PUT(4, l, L->wo, tc->dim, q_sz);
+    REF_PUT(5, l, L->w1, tc->mlp_dim, tc->dim);
+    REF_PUT(6, l, L->w2, tc->mlp_dim, tc->dim);
+    REF_PUT(7, l, L->w3, tc->dim, tc->mlp_dim);
+  }
+  if (m->encoder) {
+    const VisionEncoder *enc = m->encoder;
+    const VisionConfig *vc = enc->config;
+    for (int l = 0; l < vc->nl; l++) {
+      const VisionEncoderLayer *L = enc->layers[l];
+      REF_PUT(8, l, L->wq, vc->dim, vc->dim);
+      REF_PUT(9, l, L->wk, vc->dim, vc->dim);
+      REF_PUT(10, l, L->wv, vc->dim, vc->dim);
+      REF_PUT(11, l, L->wo, vc->dim, vc->dim);
+      REF_PUT(12, l, L->w1, vc->mlp_dim, vc->dim);
+      REF_PUT(13, l, L->w2, vc->dim, vc->mlp_dim);
+    }
+    REF_PUT(14, -1, enc->proj, tc->dim, vc->dim);
+  }
+#undef REF_PUT
+  munmap_gemma_model(m);
+  return n;
+}
+
+/* gemma.c:2045 read_gemma_model: the reference's own load of a model file
+ * into host memory (every tensor fread into its own buffer).  Returns the
+ * seconds it took (CLOCK_MONOTONIC, the free afterwards not counted), or -1
+ * when the reference refuses the file. */
+double ref_read_model_seconds(const char *path, int allow_mm) {
+  struct timespec t0, t1;
+  clock_gettime(CLOCK_MONOTONIC, &t0);
+  GemmaModel *m = read_gemma_model(path, allow_mm != 0);
+  clock_gettime(CLOCK_MONOTONIC, &t1);
+  if (m == NULL) return -1.0;
+  free_gemma_model(m);
+  return (double)(t1.tv_sec - t0.tv_sec) + 1e-9 * (double)(t1.tv_nsec - t0.tv_nsec);
+}
