@@ -322,20 +322,43 @@ class Prefill:
                 for w, s in g["w"]:
                     gcu.register_weight(w, s)
 
-    def step_host(self, gcu):
+    def step_host(self, gcu, rec=None):
+        """One step through the host-pointer ABI in gemma.c's call order.
+        rec(kind, seconds, h2d_bytes, d2h_bytes), when given, times each call."""
         lib = gcu.lib()
         m = self.m
+        clock = time.perf_counter
         for hl in self.H:
             for gi, g in enumerate(hl):
                 k = g["k"]
+                t0 = clock()
                 rc = lib.gcu_quantize_acts(g["q"].ctypes.data, g["s"].ctypes.data, g["x"].ctypes.data, 0, m, k)
                 if rc:
                     raise RuntimeError(lib.gcu_last_error().decode())
+                if rec:
+                    rec(f"quantize_acts {m}x{k}", clock() - t0, 4 * m * k, m * k + 4 * m)
                 for (w, s), o in zip(g["w"], self.Hout[gi]):
+                    t0 = clock()
                     rc = lib.gcu_gemm_int8(o.ctypes.data, 0, w.ctypes.data, 0, s.ctypes.data, g["q"].ctypes.data,
                                            0, g["s"].ctypes.data, m, w.shape[0], k)
                     if rc:
                         raise RuntimeError(lib.gcu_last_error().decode())
+                    if rec:
+                        rec(f"gemm_int8 {m}x{w.shape[0]}x{k}", clock() - t0, m * k + 4 * m, 4 * m * w.shape[0])
+
+    def host_call_breakdown(self, gcu):
+        """Per call kind of one (untimed) host step: calls, average us, bytes
+        each way per call and the bytes/second the call achieved."""
+        acc = {}
+
+        def rec(kind, dt, h2d, d2h):
+            a = acc.setdefault(kind, [0, 0.0, h2d, d2h])
+            a[0] += 1
+            a[1] += dt
+        self.step_host(gcu, rec)
+        return {kind: {"calls": n, "avg_us": round(t / n * 1e6, 1), "h2d_mb": round(h / 1e6, 3),
+                       "d2h_mb": round(d / 1e6, 3), "gbs": round((h + d) * n / t / 1e9, 1)}
+                for kind, (n, t, h, d) in acc.items()}
 
     # ---- CPU reference ---------------------------------------------------------
     def cpu_sample(self, R, layers):
@@ -746,7 +769,8 @@ def run_ours(args):
         out["e2e"] = {"value": wl.ops * world / (e_ms * 1e-3) / 1e12, "unit": "int8 TOPS", "ms_per_step": e_ms,
                       "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h,
                       "path": "gcu_quantize_acts + gcu_gemm_int8 host-pointer ABI, registered weights, "
-                              "pinned host activations, wall clock around synchronous calls"}
+                              "pinned host activations, wall clock around synchronous calls",
+                      "calls": wl.host_call_breakdown(gcu)}
 
     # CPU baseline on rank 0 at N=1 (bounded sample)
     if world == 1 and not args.no_cpu and isinstance(wl, Prefill) and wl.name == "prefill1b":

@@ -152,6 +152,15 @@ static int ctx(ThreadCtx **out) {
   return 0;
 }
 
+// Copy `height` rows of `width` bytes between pitched buffers; one linear
+// copy when both sides are dense (a pitched copy may be run row by row).
+static cudaError_t copy_rows(void *dst, size_t dpitch, const void *src, size_t spitch, size_t width,
+                             size_t height, cudaMemcpyKind kind, cudaStream_t st) {
+  if (height == 1 || (dpitch == width && spitch == width))
+    return cudaMemcpyAsync(dst, src, width * height, kind, st);
+  return cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, height, kind, st);
+}
+
 // Rows per pipeline chunk for a call moving `bytes_per_row` bytes per row in
 // its larger direction: one chunk below kChunkMinBytes, else up to
 // kMaxChunks chunks, rounded up to a multiple of `align` rows.
@@ -675,7 +684,7 @@ GCU_EXPORT int gcu_gemm_int8(float *dst, int dstr, const int8_t *mat, int mstr,
   const int rows = m <= 8 ? m : chunk_rows(m, (size_t)n * 4, 128);
   const bool piped = rows < m;
   if (!piped) {
-    GCU_CUDA(cudaMemcpy2DAsync(dsrc, k16, src, sstr, k, m, cudaMemcpyHostToDevice, c->stream));
+    GCU_CUDA(copy_rows(dsrc, k16, src, sstr, k, m, cudaMemcpyHostToDevice, c->stream));
     GCU_CUDA(cudaMemcpyAsync(dssc, ssc, (size_t)m * 4, cudaMemcpyHostToDevice, c->stream));
   }
   // weights: registered copy if the whole strided range is inside one
@@ -694,9 +703,9 @@ GCU_EXPORT int gcu_gemm_int8(float *dst, int dstr, const int8_t *mat, int mstr,
     const int ws = (m <= 8) ? k : k16;
     if (c->wtmp.get((size_t)n * ws, &p)) return 1;
     if (dmat) {
-      GCU_CUDA(cudaMemcpy2DAsync(p, ws, dmat, mstr, k, n, cudaMemcpyDeviceToDevice, c->stream));
+      GCU_CUDA(copy_rows(p, ws, dmat, mstr, k, n, cudaMemcpyDeviceToDevice, c->stream));
     } else {
-      GCU_CUDA(cudaMemcpy2DAsync(p, ws, mat, mstr, k, n, cudaMemcpyHostToDevice, c->stream));
+      GCU_CUDA(copy_rows(p, ws, mat, mstr, k, n, cudaMemcpyHostToDevice, c->stream));
     }
     dmat = p;
     dmstr = ws;
@@ -706,7 +715,7 @@ GCU_EXPORT int gcu_gemm_int8(float *dst, int dstr, const int8_t *mat, int mstr,
     if (dev_gemm((float *)dout, n4, (const int8_t *)dmat, dmstr, dms, (const int8_t *)dsrc, k16,
                  (const float *)dssc, m, n, k, c->stream))
       return 1;
-    GCU_CUDA(cudaMemcpy2DAsync(dst, (size_t)dstr * 4, dout, (size_t)n4 * 4, (size_t)n * 4, m,
+    GCU_CUDA(copy_rows(dst, (size_t)dstr * 4, dout, (size_t)n4 * 4, (size_t)n * 4, m,
                                cudaMemcpyDeviceToHost, c->stream));
     return sync_and_check(c);
   }
@@ -716,7 +725,7 @@ GCU_EXPORT int gcu_gemm_int8(float *dst, int dstr, const int8_t *mat, int mstr,
     const int mr = m - r0 < rows ? m - r0 : rows;
     if (piped) {
       // this chunk's activation rows, on the input stream
-      GCU_CUDA(cudaMemcpy2DAsync((int8_t *)dsrc + (size_t)r0 * k16, k16, src + (size_t)r0 * sstr,
+      GCU_CUDA(copy_rows((int8_t *)dsrc + (size_t)r0 * k16, k16, src + (size_t)r0 * sstr,
                                  sstr, k, mr, cudaMemcpyHostToDevice, c->s_in));
       GCU_CUDA(cudaMemcpyAsync((float *)dssc + r0, ssc + r0, (size_t)mr * 4,
                                cudaMemcpyHostToDevice, c->s_in));
@@ -730,7 +739,7 @@ GCU_EXPORT int gcu_gemm_int8(float *dst, int dstr, const int8_t *mat, int mstr,
       GCU_CUDA(cudaEventRecord(c->ev_done[i], c->stream));
       GCU_CUDA(cudaStreamWaitEvent(s_out, c->ev_done[i], 0));
     }
-    GCU_CUDA(cudaMemcpy2DAsync(dst + (size_t)r0 * dstr, (size_t)dstr * 4,
+    GCU_CUDA(copy_rows(dst + (size_t)r0 * dstr, (size_t)dstr * 4,
                                (float *)dout + (size_t)r0 * n4, (size_t)n4 * 4, (size_t)n * 4, mr,
                                cudaMemcpyDeviceToHost, s_out));
   }
