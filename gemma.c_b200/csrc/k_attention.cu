@@ -1,0 +1,542 @@
+// k_attention.cu -- the fp32 attention around the W8A8 matmuls.
+//
+// gemma.c keeps attention in fp32 (gemma.c:5221).  Two forms:
+//   decode  (gemma.c:4836-4848): one query token; att_scores_gqa
+//           (2868-2896), att_finalize = q_scale, tanh softcap, softmax
+//           (4117-4133), att_values_gqa (2902-2985) over the cache window
+//           [spos, spos+attlen), the query heads of one kv head together;
+//   prefill (gemma.c:5160-5295): a chunk of ntok tokens, causal (with the
+//           sliding window of local layers) or dense, the queries already
+//           rotated and scaled.
+// Both use gemma.c's own exp (fast_expf, gemma.c:4066-4089; a cephes-style
+// polynomial restated in dev_fast_expf below) so the softmax weights follow
+// its arithmetic; the dot products are summed in a different order than the
+// reference's vectorized loops, so results agree to fp32 reassociation.
+//
+// Cache layout is gemma.c's (gemma.c:4806-4808, 5136-5137): kv head hk's
+// position t at cache + hk*kv_stride + t*hdim, K and V in separate arrays.
+//
+// decode: HBM-bound on the K/V window (2 * nkv * attlen * hdim * 4 bytes).
+//   Grid (splits, nkv): a CTA streams one kv head's slice of the window once,
+//   scoring every query head of the group against each key row (the row is
+//   loaded once per group, as att_scores_gqa keeps it in L1), then the
+//   softmax weights and the weighted V rows of the same slice.  With one
+//   split the CTA normalises and writes xo itself; otherwise it leaves an
+//   unnormalised partial (sum, row max, weight sum) that k_attn_combine
+//   merges in split order.
+// prefill: fp32 FMA-bound.  CTA = (head, 16-query tile); two passes over the
+//   key tiles the tile's rows can see: the first finds each row's maximum
+//   score, the second forms fast_expf(s - max) exactly as softmax does and
+//   accumulates the weights and the weighted V rows in registers.
+#include "gcu_internal.cuh"
+
+#include <algorithm>
+#include <cmath>
+#include <mutex>
+
+#define GCU_EXPORT extern "C" __attribute__((visibility("default")))
+
+namespace gcu {
+namespace {
+
+constexpr int kMaxGroup = 8;  // query heads per kv head
+
+// gemma.c:4066-4089 (fast_expf): clamp, split x*log2(e) into an integer and
+// a remainder (log 2 in two parts), a degree-6 polynomial for exp(r), scale
+// by 2^n through the exponent bits; exactly 0 below -87.33654.
+// The reference is built with -ffast-math on FMA hardware, where the
+// multiply-adds contract; they are left to contract here too.
+__device__ __forceinline__ float dev_fast_expf(float x) {
+  float xl = x < -87.33654f ? -87.33654f : x;
+  xl = xl > 88.0f ? 88.0f : xl;
+  const float fx = floorf(xl * 1.44269504088896341f + 0.5f);
+  float r = xl - fx * 0.693359375f;
+  r -= fx * -2.12194440e-4f;
+  const float z = r * r;
+  float y = 1.9875691500e-4f;
+  y = y * r + 1.3981999507e-3f;
+  y = y * r + 8.3334519073e-3f;
+  y = y * r + 4.1665795894e-2f;
+  y = y * r + 1.6666665459e-1f;
+  y = y * r + 5.0000001201e-1f;
+  y = y * z + r + 1.0f;
+  y *= __int_as_float(((int)fx + 127) << 23);
+  return x < -87.33654f ? 0.0f : y;
+}
+
+// the optional tanh softcap (gemma.c:4124-4129, 5245-5250)
+__device__ __forceinline__ float softcap(float s, float sc) {
+  return sc != 0.0f ? tanhf(s / sc) * sc : s;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+struct DecodeArgs {
+  float *xo;
+  const float *xq, *kc, *vc;
+  long kv_stride;
+  int n_heads, nkv, spos, attlen, chunk, splits;
+  float asc, sc_att;
+  float *part;  // [splits][n_heads][HD] sums, then [splits][n_heads] max, then weight sums
+};
+
+// query heads [h0, h1) of kv head hk (gqa_head_of, gemma.c:2861-2863)
+__device__ __forceinline__ int gqa_head_of(int hk, int n_heads, int nkv) {
+  return (hk * n_heads + nkv - 1) / nkv;
+}
+
+// ---------------------------------------------------------------------------
+// decode
+// ---------------------------------------------------------------------------
+constexpr int kDecThreads = 256;
+constexpr int kMaxChunk = 1024;  // window positions per CTA
+
+template <int PL>
+__device__ __forceinline__ void load_lane(float (&v)[PL], const float *p) {
+  if constexpr (PL == 8) {
+    const float4 a = __ldg(reinterpret_cast<const float4 *>(p));
+    const float4 b = __ldg(reinterpret_cast<const float4 *>(p + 4));
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else if constexpr (PL == 4) {
+    const float4 a = __ldg(reinterpret_cast<const float4 *>(p));
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  } else {
+    const float2 a = __ldg(reinterpret_cast<const float2 *>(p));
+    v[0] = a.x; v[1] = a.y;
+  }
+}
+
+// smem: scores / weights [G][chunk], then (HD < 256) [R][G][HD] partials
+template <int HD>
+__global__ void __launch_bounds__(kDecThreads) k_attn_decode(DecodeArgs a) {
+  extern __shared__ float sm[];
+  __shared__ float red[kDecThreads / 32][kMaxGroup];
+  __shared__ float stat[2][kMaxGroup];  // row max, weight sum
+  constexpr int PL = HD / 32;
+  constexpr int R = kDecThreads / HD;  // thread rows in the value phase
+  ptx::griddep_launch();
+  const int split = blockIdx.x, hk = blockIdx.y;
+  const int h0 = gqa_head_of(hk, a.n_heads, a.nkv);
+  const int G = gqa_head_of(hk + 1, a.n_heads, a.nkv) - h0;
+  const int c0 = split * a.chunk;
+  const int n = min(a.attlen, c0 + a.chunk) - c0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float *kh = a.kc + (size_t)hk * a.kv_stride + (size_t)(a.spos + c0) * HD;
+  const float *vh = a.vc + (size_t)hk * a.kv_stride + (size_t)(a.spos + c0) * HD;
+  ptx::griddep_wait();
+
+  // scores: each warp takes every 8th position; a K row is read once for
+  // all G query heads of the group (att_scores_gqa's order of work)
+  float q[kMaxGroup][PL];
+#pragma unroll
+  for (int g = 0; g < kMaxGroup; ++g)
+    if (g < G) load_lane<PL>(q[g], a.xq + (size_t)(h0 + g) * HD + lane * PL);
+  float wmax[kMaxGroup];
+#pragma unroll
+  for (int g = 0; g < kMaxGroup; ++g) wmax[g] = -INFINITY;
+  for (int t = warp; t < n; t += kDecThreads / 32) {
+    float k[PL];
+    load_lane<PL>(k, kh + (size_t)t * HD + lane * PL);
+#pragma unroll
+    for (int g = 0; g < kMaxGroup; ++g) {
+      if (g < G) {
+        float d = 0.0f;
+#pragma unroll
+        for (int i = 0; i < PL; ++i) d += q[g][i] * k[i];
+        d = warp_sum(d);
+        const float s = softcap(d * a.asc, a.sc_att);  // att_finalize: *asc, then the cap
+        wmax[g] = fmaxf(wmax[g], s);
+        if (lane == 0) sm[g * a.chunk + t] = s;
+      }
+    }
+  }
+  if (lane == 0)
+#pragma unroll
+    for (int g = 0; g < kMaxGroup; ++g) red[warp][g] = wmax[g];
+  __syncthreads();
+  if (threadIdx.x < G) {
+    float m = red[0][threadIdx.x];
+    for (int w = 1; w < kDecThreads / 32; ++w) m = fmaxf(m, red[w][threadIdx.x]);
+    stat[0][threadIdx.x] = m;
+  }
+  __syncthreads();
+
+  // softmax weights fast_expf(s - max) (gemma.c:4094-4105) and their sums
+  for (int g = 0; g < G; ++g) {
+    const float m = stat[0][g];
+    float l = 0.0f;
+    for (int t = threadIdx.x; t < n; t += kDecThreads) {
+      const float p = dev_fast_expf(sm[g * a.chunk + t] - m);
+      sm[g * a.chunk + t] = p;
+      l += p;
+    }
+    l = warp_sum(l);
+    if (lane == 0) red[warp][g] = l;
+  }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    float l = 0.0f;
+    for (int w = 0; w < kDecThreads / 32; ++w) l += red[w][threadIdx.x];
+    stat[1][threadIdx.x] = l;
+  }
+
+  // values: thread (r, d) sums weight * V[t][d] over t = r, r + R, ...
+  const int d = threadIdx.x % HD, r = threadIdx.x / HD;
+  float acc[kMaxGroup];
+#pragma unroll
+  for (int g = 0; g < kMaxGroup; ++g) acc[g] = 0.0f;
+  int t = r;
+  for (; t + 3 * R < n; t += 4 * R) {
+    const float v0 = __ldg(vh + (size_t)t * HD + d), v1 = __ldg(vh + (size_t)(t + R) * HD + d);
+    const float v2 = __ldg(vh + (size_t)(t + 2 * R) * HD + d), v3 = __ldg(vh + (size_t)(t + 3 * R) * HD + d);
+#pragma unroll
+    for (int g = 0; g < kMaxGroup; ++g) {
+      if (g < G) {
+        const float *p = sm + g * a.chunk + t;
+        acc[g] += p[0] * v0;
+        acc[g] += p[R] * v1;
+        acc[g] += p[2 * R] * v2;
+        acc[g] += p[3 * R] * v3;
+      }
+    }
+  }
+  for (; t < n; t += R) {
+    const float v = __ldg(vh + (size_t)t * HD + d);
+#pragma unroll
+    for (int g = 0; g < kMaxGroup; ++g)
+      if (g < G) acc[g] += sm[g * a.chunk + t] * v;
+  }
+  if constexpr (R > 1) {
+    float *rs = sm + kMaxGroup * a.chunk;  // [R][G][HD]
+    __syncthreads();                       // every thread is done with the weights' smem neighbours
+#pragma unroll
+    for (int g = 0; g < kMaxGroup; ++g)
+      if (g < G) rs[(r * kMaxGroup + g) * HD + d] = acc[g];
+    __syncthreads();
+    if (r != 0) return;
+#pragma unroll
+    for (int g = 0; g < kMaxGroup; ++g) {
+      if (g < G) {
+        float s = rs[g * HD + d];
+        for (int rr = 1; rr < R; ++rr) s += rs[(rr * kMaxGroup + g) * HD + d];
+        acc[g] = s;
+      }
+    }
+  } else {
+    __syncthreads();  // stat[1] is written
+  }
+  if (a.splits == 1) {
+#pragma unroll
+    for (int g = 0; g < kMaxGroup; ++g)
+      if (g < G) a.xo[(size_t)(h0 + g) * HD + d] = acc[g] / stat[1][g];
+    return;
+  }
+  float *po = a.part + (size_t)split * a.n_heads * HD;
+  float *pm = a.part + (size_t)a.splits * a.n_heads * HD + (size_t)split * a.n_heads;
+  float *pl = pm + (size_t)a.splits * a.n_heads;
+#pragma unroll
+  for (int g = 0; g < kMaxGroup; ++g) {
+    if (g < G) {
+      po[(size_t)(h0 + g) * HD + d] = acc[g];
+      if (d == 0) {
+        pm[h0 + g] = stat[0][g];
+        pl[h0 + g] = stat[1][g];
+      }
+    }
+  }
+}
+
+// merge the splits of one head in split order: m = max over splits,
+// xo = sum_s e_s * O_s / sum_s e_s * l_s with e_s = fast_expf(m_s - m)
+template <int HD>
+__global__ void __launch_bounds__(HD) k_attn_combine(float *xo, const float *part, int n_heads, int splits) {
+  ptx::griddep_launch();
+  const int h = blockIdx.x, d = threadIdx.x;
+  const float *pm = part + (size_t)splits * n_heads * HD;
+  const float *pl = pm + (size_t)splits * n_heads;
+  ptx::griddep_wait();
+  float m = -INFINITY;
+  for (int s = 0; s < splits; ++s) m = fmaxf(m, pm[(size_t)s * n_heads + h]);
+  float o = 0.0f, l = 0.0f;
+  for (int s = 0; s < splits; ++s) {
+    const float e = dev_fast_expf(pm[(size_t)s * n_heads + h] - m);
+    l += e * pl[(size_t)s * n_heads + h];
+    o += e * part[((size_t)s * n_heads + h) * HD + d];
+  }
+  xo[(size_t)h * HD + d] = o / l;
+}
+
+// ---------------------------------------------------------------------------
+// prefill
+// ---------------------------------------------------------------------------
+constexpr int kPreThreads = 256;
+constexpr int kBQ = 16;  // queries per CTA
+constexpr int kBK = 64;  // keys per tile
+
+struct PrefillArgs {
+  float *xo;
+  int xostr;
+  const float *xq, *kc, *vc;
+  long kv_stride;
+  int n_heads, nkv, spos, ntok, slide, mask;
+  float sc_att;
+};
+
+template <int HD>
+struct PreSmem {
+  static constexpr int KS = HD + 4;  // padded K / Q row: conflict-free 16-byte reads
+  static constexpr size_t q = 0;
+  static constexpr size_t k = q + (size_t)kBQ * KS;
+  static constexpr size_t v = k + (size_t)kBK * KS;
+  static constexpr size_t p = v + (size_t)kBK * HD;
+  static constexpr size_t floats = p + (size_t)kBQ * kBK;
+  static constexpr size_t bytes = floats * sizeof(float);
+};
+
+// the window of token i (gemma.c:5187-5199 / 5232-5236): [t0, t1]
+__device__ __forceinline__ void row_window(const PrefillArgs &a, int i, int &t0, int &t1) {
+  const int pos = a.spos + i;
+  if (a.mask) {
+    t0 = (a.slide > 0 && pos >= a.slide) ? pos + 1 - a.slide : 0;
+    t1 = pos;
+  } else {
+    t0 = 0;
+    t1 = a.spos + a.ntok - 1;
+  }
+}
+
+// rows [k0, k0 + kBK) of one kv head's cache into smem (row stride `ld`),
+// rows at or past `kend` zero
+template <int HD>
+__device__ __forceinline__ void load_tile(float *dst, int ld, const float *src, int k0, int kend) {
+  constexpr int V4 = HD / 4;
+  for (int idx = threadIdx.x; idx < kBK * V4; idx += kPreThreads) {
+    const int row = idx / V4, c = idx - row * V4;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (k0 + row < kend) v = __ldg(reinterpret_cast<const float4 *>(src + (size_t)(k0 + row) * HD) + c);
+    *reinterpret_cast<float4 *>(dst + row * ld + c * 4) = v;
+  }
+}
+
+// s[c] = q(row qi) . k(row kq + 16c), c < 4, from smem
+template <int HD>
+__device__ __forceinline__ void tile_scores(const float *qs, const float *ks, int qi, int kq, float (&s)[4]) {
+  constexpr int KS = PreSmem<HD>::KS;
+  s[0] = s[1] = s[2] = s[3] = 0.0f;
+  const float *qr = qs + qi * KS;
+#pragma unroll 8
+  for (int d = 0; d < HD; d += 4) {
+    const float4 q = *reinterpret_cast<const float4 *>(qr + d);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const float4 k = *reinterpret_cast<const float4 *>(ks + (kq + 16 * c) * KS + d);
+      s[c] += q.x * k.x;
+      s[c] += q.y * k.y;
+      s[c] += q.z * k.z;
+      s[c] += q.w * k.w;
+    }
+  }
+}
+
+// CTA (query tile, head).  Thread (qi, kq) = (tid / 16, tid % 16) scores
+// row qi against keys kq + 16c of each tile and, in the value phase, owns
+// columns kq*4 + 64c of row qi.
+template <int HD>
+__global__ void __launch_bounds__(kPreThreads) k_attn_prefill(PrefillArgs a) {
+  extern __shared__ __align__(16) float smem[];
+  using S = PreSmem<HD>;
+  float *qs = smem + S::q, *ks = smem + S::k, *vs = smem + S::v, *ps = smem + S::p;
+  ptx::griddep_launch();
+  const int h = blockIdx.y, i0 = blockIdx.x * kBQ;
+  const int nrows = min(kBQ, a.ntok - i0);
+  const int hk = h * a.nkv / a.n_heads;  // gemma.c:5172
+  const float *kh = a.kc + (size_t)hk * a.kv_stride, *vh = a.vc + (size_t)hk * a.kv_stride;
+  const int qi = threadIdx.x >> 4, kq = threadIdx.x & 15;
+  int t0, t1, lo, hi, unused;
+  row_window(a, i0 + min(qi, nrows - 1), t0, t1);
+  row_window(a, i0, lo, unused);              // windows only move right with i
+  row_window(a, i0 + nrows - 1, unused, hi);
+  const int kend = hi + 1;
+  ptx::griddep_wait();
+
+  for (int idx = threadIdx.x; idx < kBQ * HD / 4; idx += kPreThreads) {
+    const int row = idx / (HD / 4), c = idx - row * (HD / 4);
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (row < nrows)
+      v = __ldg(reinterpret_cast<const float4 *>(a.xq + ((size_t)h * a.ntok + i0 + row) * HD) + c);
+    *reinterpret_cast<float4 *>(qs + row * S::KS + c * 4) = v;
+  }
+
+  // pass 1: the maximum capped score of each row over its window
+  float m = -INFINITY;
+  for (int k0 = lo; k0 < kend; k0 += kBK) {
+    __syncthreads();  // the previous tile (and the Q tile's stores) are done
+    load_tile<HD>(ks, S::KS, kh, k0, kend);
+    __syncthreads();
+    float s[4];
+    tile_scores<HD>(qs, ks, qi, kq, s);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int t = k0 + kq + 16 * c;
+      if (t >= t0 && t <= t1) m = fmaxf(m, softcap(s[c], a.sc_att));
+    }
+  }
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+
+  // pass 2: weights fast_expf(s - max) (gemma.c:4094-4105), their sum, and
+  // the weighted V rows
+  float l = 0.0f;
+  float4 acc[HD / 64];
+#pragma unroll
+  for (int c = 0; c < HD / 64; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int k0 = lo; k0 < kend; k0 += kBK) {
+    __syncthreads();
+    load_tile<HD>(ks, S::KS, kh, k0, kend);
+    load_tile<HD>(vs, HD, vh, k0, kend);
+    __syncthreads();
+    float s[4];
+    tile_scores<HD>(qs, ks, qi, kq, s);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int t = k0 + kq + 16 * c;
+      const float p = (t >= t0 && t <= t1) ? dev_fast_expf(softcap(s[c], a.sc_att) - m) : 0.0f;
+      ps[qi * kBK + kq + 16 * c] = p;
+      l += p;
+    }
+    __syncthreads();
+    const int jn = min(kBK, kend - k0);
+    const float *pr = ps + qi * kBK;
+    for (int j = 0; j < jn; ++j) {
+      const float p = pr[j];
+      const float *vr = vs + j * HD + kq * 4;
+#pragma unroll
+      for (int c = 0; c < HD / 64; ++c) {
+        const float4 v = *reinterpret_cast<const float4 *>(vr + 64 * c);
+        acc[c].x += p * v.x;
+        acc[c].y += p * v.y;
+        acc[c].z += p * v.z;
+        acc[c].w += p * v.w;
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+  if (qi >= nrows) return;
+  float *out = a.xo + (size_t)(i0 + qi) * a.xostr + (size_t)h * HD + kq * 4;
+#pragma unroll
+  for (int c = 0; c < HD / 64; ++c)
+    *reinterpret_cast<float4 *>(out + 64 * c) =
+        make_float4(acc[c].x / l, acc[c].y / l, acc[c].z / l, acc[c].w / l);
+}
+
+template <int HD>
+cudaError_t launch_decode(const DecodeArgs &a, cudaStream_t st) {
+  constexpr int R = kDecThreads / HD;
+  const size_t smem = ((size_t)kMaxGroup * a.chunk + (R > 1 ? (size_t)R * kMaxGroup * HD : 0)) * sizeof(float);
+  cudaError_t e = launch_k(k_attn_decode<HD>, dim3(a.splits, a.nkv), dim3(kDecThreads), smem, st, a);
+  if (e != cudaSuccess || a.splits == 1) return e;
+  return launch_k(k_attn_combine<HD>, dim3(a.n_heads), dim3(HD), 0, st, a.xo, (const float *)a.part, a.n_heads,
+                  a.splits);
+}
+
+template <int HD>
+cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t st) {
+  // the shared-memory opt-in is per device: once for each device this runs on
+  static std::mutex mu;
+  static unsigned long long done_mask = 0;
+  {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lk(mu);
+    if (!(done_mask & (1ull << (dev & 63)))) {
+      e = cudaFuncSetAttribute(k_attn_prefill<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)PreSmem<HD>::bytes);
+      if (e != cudaSuccess) return e;
+      done_mask |= 1ull << (dev & 63);
+    }
+  }
+  const dim3 grid((a.ntok + kBQ - 1) / kBQ, a.n_heads);
+  return launch_k(k_attn_prefill<HD>, grid, dim3(kPreThreads), PreSmem<HD>::bytes, st, a);
+}
+
+bool aligned16(const void *p) { return ((uintptr_t)p & 15) == 0; }
+
+int check_heads(const char *what, int n_heads, int nkv, int hdim) {
+  if (hdim != 64 && hdim != 128 && hdim != 256)
+    return set_error("%s: head size %d (64, 128 or 256 supported)", what, hdim);
+  if (n_heads < 1 || nkv < 1 || nkv > n_heads)
+    return set_error("%s: %d query heads over %d kv heads", what, n_heads, nkv);
+  if ((n_heads + nkv - 1) / nkv > kMaxGroup)
+    return set_error("%s: more than %d query heads per kv head", what, kMaxGroup);
+  return 0;
+}
+
+}  // namespace
+}  // namespace gcu
+
+using namespace gcu;
+
+GCU_EXPORT int gcu_dev_attention_decode(float *xo, const float *xq, const float *k_cache, const float *v_cache,
+                                        long kv_stride, int n_heads, int nkv, int hdim, int spos, int attlen,
+                                        float asc, float sc_att, void *stream) {
+  if (check_heads("attention_decode", n_heads, nkv, hdim)) return 1;
+  if (!xo || !xq || !k_cache || !v_cache) return set_error("attention_decode: null pointer");
+  if (!aligned16(xo) || !aligned16(xq) || !aligned16(k_cache) || !aligned16(v_cache) || kv_stride % 4)
+    return set_error("attention_decode: buffers must be 16-byte aligned, kv_stride a multiple of 4");
+  if (spos < 0 || attlen < 1 || kv_stride < (long)(spos + attlen) * hdim)
+    return set_error("attention_decode: window [%d, %d) outside a cache of %ld floats per head", spos,
+                     spos + attlen, kv_stride);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  DecodeArgs a{xo, xq, k_cache, v_cache, kv_stride, n_heads, nkv, spos, attlen, 0, 1, asc, sc_att, nullptr};
+  // splits of the window: enough CTAs to stream it at full bandwidth, at
+  // least 64 positions each, at most kMaxChunk
+  const int target = 2 * num_sms();
+  int splits = attlen <= 64 ? 1 : std::min((attlen + 63) / 64, std::max(1, (target + nkv - 1) / nkv));
+  splits = std::max(splits, (attlen + kMaxChunk - 1) / kMaxChunk);
+  a.chunk = (attlen + splits - 1) / splits;
+  a.splits = (attlen + a.chunk - 1) / a.chunk;
+  if (a.splits > 1) {
+    void *ws;
+    int *cnt;
+    if (gemm_workspace((size_t)a.splits * n_heads * (hdim + 2) * sizeof(float), &ws, &cnt, 0, st)) return 1;
+    a.part = static_cast<float *>(ws);
+  }
+  cudaError_t e = hdim == 256 ? launch_decode<256>(a, st) : hdim == 128 ? launch_decode<128>(a, st)
+                                                                        : launch_decode<64>(a, st);
+  GCU_CUDA(e);
+  return 0;
+}
+
+GCU_EXPORT int gcu_dev_attention_prefill(float *xo, int xostr, const float *xq, const float *k_cache,
+                                         const float *v_cache, long kv_stride, int n_heads, int nkv, int hdim,
+                                         int spos, int ntok, int slide, float sc_att, int mask, void *stream) {
+  if (ntok == 0) return 0;
+  if (check_heads("attention_prefill", n_heads, nkv, hdim)) return 1;
+  if (!xo || !xq || !k_cache || !v_cache) return set_error("attention_prefill: null pointer");
+  if (xostr == 0) xostr = n_heads * hdim;
+  if (!aligned16(xo) || !aligned16(xq) || !aligned16(k_cache) || !aligned16(v_cache) || kv_stride % 4 ||
+      xostr % 4 || xostr < n_heads * hdim)
+    return set_error("attention_prefill: buffers must be 16-byte aligned, strides multiples of 4 floats "
+                     "(xostr >= n_heads*hdim)");
+  if (spos < 0 || ntok < 0 || slide < 0 || kv_stride < (long)(spos + ntok) * hdim)
+    return set_error("attention_prefill: chunk [%d, %d) outside a cache of %ld floats per head", spos, spos + ntok,
+                     kv_stride);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  PrefillArgs a{xo, xostr, xq, k_cache, v_cache, kv_stride, n_heads, nkv, spos, ntok, slide, mask ? 1 : 0, sc_att};
+  cudaError_t e = hdim == 256 ? launch_prefill<256>(a, st) : hdim == 128 ? launch_prefill<128>(a, st)
+                                                                         : launch_prefill<64>(a, st);
+  GCU_CUDA(e);
+  return 0;
+}

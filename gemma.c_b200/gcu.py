@@ -81,6 +81,10 @@ SIGNATURES = {
                                                          _int, _int, _vp, _vp]),
     "gcu_dev_rmsnorm_quantize": (_int, [_vp, _vp, _vp, _vp, _int, _vp, ctypes.c_float, _int, _int, _vp]),
     "gcu_dev_geglu_quantize": (_int, [_vp, _vp, _vp, _vp, _vp, _int, _int, _vp]),
+    "gcu_dev_attention_decode": (_int, [_vp, _vp, _vp, _vp, ctypes.c_long, _int, _int, _int, _int, _int,
+                                        ctypes.c_float, ctypes.c_float, _vp]),
+    "gcu_dev_attention_prefill": (_int, [_vp, _int, _vp, _vp, _vp, ctypes.c_long, _int, _int, _int, _int, _int,
+                                         _int, ctypes.c_float, _int, _vp]),
 }
 # exported but not part of the public header (benchmark sweeps, self-test)
 EXTRA = {
@@ -396,3 +400,25 @@ def dev_geglu_quantize(q, s, gate, up, m, dim, out=None, stream=None):
     _check(lib().gcu_dev_geglu_quantize(q.data_ptr(), s.data_ptr(), out.data_ptr() if out is not None else None,
                                         gate.data_ptr(), up.data_ptr(), m, dim, _stream(stream)),
            "dev_geglu_quantize")
+
+
+def dev_attention_decode(xo, xq, kc, vc, spos, attlen, asc, sc_att=0.0, stream=None):
+    """gemma.c:4836-4848 on CUDA tensors: xq (n_heads, hdim); kc, vc
+    (nkv, clen, hdim) caches; writes xo (n_heads, hdim)."""
+    n_heads, hdim = xq.shape
+    nkv, clen, _ = kc.shape
+    _check(lib().gcu_dev_attention_decode(xo.data_ptr(), xq.data_ptr(), kc.data_ptr(), vc.data_ptr(), clen * hdim,
+                                          n_heads, nkv, hdim, spos, attlen, asc, sc_att, _stream(stream)),
+           "dev_attention_decode")
+
+
+def dev_attention_prefill(xo, xq, kc, vc, spos, slide=0, sc_att=0.0, mask=True, xostr=0, stream=None):
+    """gemma.c:5160-5295 on CUDA tensors: xq (n_heads, ntok, hdim) rotated and
+    scaled; kc, vc (nkv, clen, hdim) holding the chunk at [spos, spos+ntok);
+    writes xo rows (ntok, >= n_heads*hdim)."""
+    n_heads, ntok, hdim = xq.shape
+    nkv, clen, _ = kc.shape
+    _check(lib().gcu_dev_attention_prefill(xo.data_ptr(), xostr, xq.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+                                           clen * hdim, n_heads, nkv, hdim, spos, ntok, slide, sc_att, int(mask),
+                                           _stream(stream)),
+           "dev_attention_prefill")

@@ -63,6 +63,20 @@ def activations(tensor_id: int, m: int, k: int, outliers: bool = False) -> np.nd
     return x
 
 
+def attention_inputs(tensor_id: int, n_heads: int, nkv: int, hdim: int, clen: int, ntok: int = 0):
+    """Seeded attention operands: K and V caches (nkv, clen, hdim) of N(0, 1)
+    and the queries, (n_heads, hdim) N(0, 1) for a decode step (the kernel
+    applies the attention scale) or (n_heads, ntok, hdim) N(0, 1/hdim) for a
+    prefill chunk (queries arrive already scaled, gemma.c:5121-5133)."""
+    kc = normal(tensor_id, (nkv, clen, hdim))
+    vc = normal(tensor_id + 1, (nkv, clen, hdim))
+    if ntok:
+        xq = normal(tensor_id + 2, (n_heads, ntok, hdim), 1.0 / math.sqrt(hdim))
+    else:
+        xq = normal(tensor_id + 2, (n_heads, hdim))
+    return xq, kc, vc
+
+
 def quantize_weight_rows(w: np.ndarray):
     """Exporter quantizer (model.py:151-161) in numpy fp32 arithmetic."""
     w = np.asarray(w, np.float32)

@@ -221,6 +221,32 @@ int gcu_dev_rmsnorm_quantize(int8_t *q, float *s, float *out, const float *x, in
 int gcu_dev_geglu_quantize(int8_t *q, float *s, float *out, const float *gate, const float *up,
                            int m, int dim, void *stream);
 
+/* ---- attention (fp32) between the Q/K/V and O matmuls ----------------------
+ * gemma.c's KV cache layout (gemma.c:4806-4808): kv head hk's position t at
+ * cache + hk*kv_stride + t*hdim (kv_stride = clen*hdim), K and V separate;
+ * each cache holds nkv*kv_stride floats.  hdim 64, 128 or 256, at most 8
+ * query heads per kv head, 16-byte aligned buffers.  fp32 arithmetic with
+ * gemma.c's fast_expf softmax; results agree with the reference to fp32
+ * reassociation (the reference's dot products are vectorized). */
+
+/* gemma.c:4836-4848 (att_scores_gqa, att_finalize, att_values_gqa): one
+ * decode step of one layer.  xq [n_heads][hdim] (normed and rotated), the
+ * window [spos, spos+attlen) of the cache, scores scaled by asc
+ * (1/sqrt(q_scale)) then soft-capped by sc_att (0 = off).  xo [n_heads][hdim]. */
+int gcu_dev_attention_decode(float *xo, const float *xq, const float *k_cache, const float *v_cache,
+                             long kv_stride, int n_heads, int nkv, int hdim, int spos, int attlen,
+                             float asc, float sc_att, void *stream);
+/* gemma.c:5160-5295: a prefill chunk of ntok tokens at positions
+ * [spos, spos+ntok) whose keys and values are already in the cache.  xq
+ * [n_heads][ntok][hdim], rotated and scaled by the attention scale
+ * (gemma.c:5121-5133).  mask = 1: causal, and a sliding window of `slide`
+ * positions when slide > 0 (gemma.c's tc->swa[l] layers); mask = 0: every
+ * token sees [0, spos+ntok).  Token i of head h goes to xo + i*xostr + h*hdim
+ * (xostr 0 = n_heads*hdim, gemma.c's xo rows). */
+int gcu_dev_attention_prefill(float *xo, int xostr, const float *xq, const float *k_cache,
+                              const float *v_cache, long kv_stride, int n_heads, int nkv, int hdim,
+                              int spos, int ntok, int slide, float sc_att, int mask, void *stream);
+
 /* ---- row-sharded entry points (NCCL over NVLink) ---------------------------
  * No counterpart in the reference, which is single-process (README.md:614).
  * Rank r of `world` owns weight rows [r*n/world, (r+1)*n/world) of an n-row

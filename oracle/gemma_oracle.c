@@ -207,3 +207,126 @@ void orc_geglu_quantize(int8_t *q, float *s, float *h, const float *gate, const 
     s[i] = orc_quantize_act(q + (size_t)i * dim, tmp, dim);
   }
 }
+
+/* ---- attention (fp32), the layer around the matmuls ------------------------
+ * gemma.c keeps attention in fp32 ("typically people don't quantize this",
+ * gemma.c:5221).  These restate its two forms with plain loops; the reference
+ * vectorizes its dot products under -ffast-math, so agreement is to within
+ * fp32 reassociation, not bit for bit. */
+
+/* gemma.c:4066-4089 fast_expf: cephes-style exp, 0 below -87.33654. */
+static float orc_fast_expf(float x) {
+  float xl = x < -87.33654f ? -87.33654f : x;
+  xl = xl > 88.0f ? 88.0f : xl;
+  float fx = floorf(xl * 1.44269504088896341f + 0.5f);
+  float r = xl - fx * 0.693359375f;
+  r -= fx * -2.12194440e-4f;
+  float z = r * r;
+  float y = 1.9875691500e-4f;
+  y = y * r + 1.3981999507e-3f;
+  y = y * r + 8.3334519073e-3f;
+  y = y * r + 4.1665795894e-2f;
+  y = y * r + 1.6666665459e-1f;
+  y = y * r + 5.0000001201e-1f;
+  y = y * z + r + 1.0f;
+  union {
+    int i;
+    float f;
+  } u;
+  u.i = ((int)fx + 127) << 23;
+  y *= u.f;
+  return x < -87.33654f ? 0.0f : y;
+}
+
+/* gemma.c:4091-4112 softmax of one row in place. */
+static void orc_softmax(float *row, int n) {
+  float max = -3.402823466e38f;
+  for (int i = 0; i < n; i++) max = row[i] > max ? row[i] : max;
+  float sum = 0.0f;
+  for (int i = 0; i < n; i++) {
+    row[i] = orc_fast_expf(row[i] - max);
+    sum += row[i];
+  }
+  for (int i = 0; i < n; i++) row[i] = row[i] / sum;
+}
+
+/* the optional tanh softcap, gemma.c:4124-4129 / 5245-5250 */
+static void orc_softcap(float *row, int n, float sc) {
+  if (sc == 0.0f) return;
+  for (int i = 0; i < n; i++) row[i] = tanhf(row[i] / sc) * sc;
+}
+
+static float orc_dot(const float *a, const float *b, int n) {
+  float s = 0.0f;
+  for (int i = 0; i < n; i++) s += a[i] * b[i];
+  return s;
+}
+
+/* One decode step's attention for one layer, gemma.c:4836-4848:
+ * att_scores_gqa (2868-2896), att_finalize per head (4117-4133),
+ * att_values_gqa (2902-2985).  Query head h reads kv head hk when
+ * gqa_head_of(hk) <= h < gqa_head_of(hk+1), gqa_head_of(hk) =
+ * (hk*n_heads + nkv - 1) / nkv (gemma.c:2861-2863).  Head hk's cache row t
+ * is at cache + hk*kv_stride + t*hdim; the window is [spos, spos+attlen).
+ * att: scratch of n_heads*attlen floats. */
+void orc_attention_decode(float *xo, const float *xq, const float *kc, const float *vc,
+                          long kv_stride, int n_heads, int nkv, int hdim, int spos, int attlen,
+                          float asc, float sc_att, float *att) {
+  for (int hk = 0; hk < nkv; hk++) {
+    const int h0 = (hk * n_heads + nkv - 1) / nkv;
+    const int h1 = ((hk + 1) * n_heads + nkv - 1) / nkv;
+    const float *kh = kc + (size_t)hk * kv_stride + (size_t)spos * hdim;
+    const float *vh = vc + (size_t)hk * kv_stride + (size_t)spos * hdim;
+    for (int h = h0; h < h1; h++) {
+      float *a = att + (size_t)h * attlen;
+      for (int t = 0; t < attlen; t++) a[t] = orc_dot(kh + (size_t)t * hdim, xq + (size_t)h * hdim, hdim);
+      for (int t = 0; t < attlen; t++) a[t] *= asc;
+      orc_softcap(a, attlen, sc_att);
+      orc_softmax(a, attlen);
+      for (int d = 0; d < hdim; d++) {
+        float acc = 0.0f;
+        for (int t = 0; t < attlen; t++) acc += a[t] * vh[(size_t)t * hdim + d];
+        xo[(size_t)h * hdim + d] = acc;
+      }
+    }
+  }
+}
+
+/* A prefill chunk's attention for one layer, gemma.c:5160-5295.  xq
+ * [n_heads][ntok][hdim] is already rotated and scaled by the attention
+ * scale (gemma.c:5121-5133); this chunk's keys and values are in the cache at
+ * [spos, spos+ntok).  Query head h reads kv head h*nkv/n_heads (gemma.c:5172).
+ * mask != 0 (the blockwise-causal path): token i (position spos+i) attends to
+ * [spos_i, spos+i], spos_i = spos+i+1-slide when the layer slides (slide > 0)
+ * and spos+i >= slide, else 0.  mask == 0 (the dense path): every token
+ * attends to [0, spos+ntok).  The softcap is applied to the scores that enter
+ * the softmax.  Token i's output row is xo + i*xostr + h*hdim.  att: scratch
+ * of spos+ntok floats. */
+void orc_attention_prefill(float *xo, int xostr, const float *xq, const float *kc, const float *vc,
+                           long kv_stride, int n_heads, int nkv, int hdim, int spos, int ntok,
+                           int slide, float sc_att, int mask, float *att) {
+  for (int h = 0; h < n_heads; h++) {
+    const int hk = h * nkv / n_heads;
+    const float *kh = kc + (size_t)hk * kv_stride;
+    const float *vh = vc + (size_t)hk * kv_stride;
+    for (int i = 0; i < ntok; i++) {
+      const int pos = spos + i;
+      int t0 = 0, t1 = spos + ntok - 1;
+      if (mask) {
+        t0 = (slide > 0 && pos >= slide) ? pos + 1 - slide : 0;
+        t1 = pos;
+      }
+      const int n = t1 - t0 + 1;
+      const float *q = xq + ((size_t)h * ntok + i) * hdim;
+      for (int t = 0; t < n; t++) att[t] = orc_dot(q, kh + (size_t)(t0 + t) * hdim, hdim);
+      orc_softcap(att, n, sc_att);
+      orc_softmax(att, n);
+      float *o = xo + (size_t)i * xostr + (size_t)h * hdim;
+      for (int d = 0; d < hdim; d++) {
+        float acc = 0.0f;
+        for (int t = 0; t < n; t++) acc += att[t] * vh[(size_t)(t0 + t) * hdim + d];
+        o[d] = acc;
+      }
+    }
+  }
+}

@@ -84,6 +84,12 @@ def orc() -> ctypes.CDLL:
                                              ctypes.c_int, ctypes.c_int]
         lib.orc_geglu_quantize.restype = None
         lib.orc_geglu_quantize.argtypes = [_i8p, _f32p, _f32p, _f32p, _f32p, ctypes.c_int, ctypes.c_int]
+        lib.orc_attention_decode.restype = None
+        lib.orc_attention_decode.argtypes = [_f32p, _f32p, _f32p, _f32p, ctypes.c_long] + [ctypes.c_int] * 5 + \
+            [ctypes.c_float, ctypes.c_float, _f32p]
+        lib.orc_attention_prefill.restype = None
+        lib.orc_attention_prefill.argtypes = [_f32p, ctypes.c_int, _f32p, _f32p, _f32p, ctypes.c_long] + \
+            [ctypes.c_int] * 6 + [ctypes.c_float, ctypes.c_int, _f32p]
         _orc = lib
     return _orc
 
@@ -195,6 +201,42 @@ def geglu_quantize(gate: np.ndarray, up: np.ndarray):
     return h, q, s
 
 
+def _cache(kc, vc):
+    """(nkv, clen, hdim) K and V caches -> contiguous arrays and the head stride."""
+    kc = np.ascontiguousarray(kc, np.float32)
+    vc = np.ascontiguousarray(vc, np.float32)
+    assert kc.shape == vc.shape and kc.ndim == 3
+    return kc, vc, kc.shape[1] * kc.shape[2]
+
+
+def attention_decode(xq, kc, vc, spos, attlen, asc, sc_att=0.0):
+    """gemma.c:4836-4848: xq (n_heads, hdim); caches (nkv, clen, hdim);
+    the window [spos, spos+attlen).  Returns xo (n_heads, hdim)."""
+    xq = np.ascontiguousarray(xq, np.float32)
+    kc, vc, stride = _cache(kc, vc)
+    n_heads, hdim = xq.shape
+    xo = np.empty((n_heads, hdim), np.float32)
+    att = np.empty(n_heads * attlen, np.float32)
+    orc().orc_attention_decode(_ptr(xo, _f32p), _ptr(xq, _f32p), _ptr(kc, _f32p), _ptr(vc, _f32p), stride,
+                               n_heads, kc.shape[0], hdim, spos, attlen, asc, sc_att, _ptr(att, _f32p))
+    return xo
+
+
+def attention_prefill(xq, kc, vc, spos, slide=0, sc_att=0.0, mask=True):
+    """gemma.c:5160-5295: xq (n_heads, ntok, hdim), rotated and scaled;
+    caches (nkv, clen, hdim) holding this chunk at [spos, spos+ntok).
+    Returns xo (ntok, n_heads*hdim)."""
+    xq = np.ascontiguousarray(xq, np.float32)
+    kc, vc, stride = _cache(kc, vc)
+    n_heads, ntok, hdim = xq.shape
+    xo = np.empty((ntok, n_heads * hdim), np.float32)
+    att = np.empty(spos + ntok, np.float32)
+    orc().orc_attention_prefill(_ptr(xo, _f32p), n_heads * hdim, _ptr(xq, _f32p), _ptr(kc, _f32p),
+                                _ptr(vc, _f32p), stride, n_heads, kc.shape[0], hdim, spos, ntok, slide,
+                                sc_att, int(mask), _ptr(att, _f32p))
+    return xo
+
+
 # --------------------------------------------------------------------------
 # the compiled reference (gemma.c's own functions)
 # --------------------------------------------------------------------------
@@ -255,6 +297,13 @@ def ref(variant: str | None = None) -> ctypes.CDLL | None:
     lib.ref_gelu_mul.restype = None
     lib.ref_gelu_mul.argtypes = [_f32p, _f32p, _f32p, ctypes.c_int, ctypes.c_int]
     lib.ref_isa.restype = ctypes.c_char_p
+    if hasattr(lib, "ref_attention_decode"):
+        lib.ref_attention_decode.restype = None
+        lib.ref_attention_decode.argtypes = [_f32p, _f32p, _f32p, _f32p, ctypes.c_long] + [ctypes.c_int] * 5 + \
+            [ctypes.c_float, ctypes.c_float, _f32p, ctypes.c_int]
+        lib.ref_attention_prefill.restype = ctypes.c_int
+        lib.ref_attention_prefill.argtypes = [_f32p, ctypes.c_int, _f32p, _f32p, _f32p, ctypes.c_long] + \
+            [ctypes.c_int] * 6 + [ctypes.c_float, ctypes.c_int, _f32p]
     if hasattr(lib, "ref_read_model_seconds"):
         lib.ref_read_model_seconds.restype = ctypes.c_double
         lib.ref_read_model_seconds.argtypes = [ctypes.c_char_p, ctypes.c_int]
@@ -312,6 +361,33 @@ class Ref:
         return [{"kind": kinds[rec[6 * i]], "layer": int(rec[6 * i + 1]), "rows": int(rec[6 * i + 4]),
                  "k": int(rec[6 * i + 5]), "q_off": int(rec[6 * i + 2]), "s_off": int(rec[6 * i + 3])}
                 for i in range(n)]
+
+    def attention_decode(self, xq, kc, vc, spos, attlen, asc, sc_att=0.0):
+        """gemma.c's decode attention (att_scores_gqa, att_finalize,
+        att_values_gqa) on the same arguments as oracle.attention_decode."""
+        xq = np.ascontiguousarray(xq, np.float32)
+        kc, vc, stride = _cache(kc, vc)
+        n_heads, hdim = xq.shape
+        xo = np.empty((n_heads, hdim), np.float32)
+        att = np.empty(spos + n_heads * attlen, np.float32)
+        self.lib.ref_attention_decode(_ptr(xo, _f32p), _ptr(xq, _f32p), _ptr(kc, _f32p), _ptr(vc, _f32p), stride,
+                                      n_heads, kc.shape[0], hdim, spos, attlen, asc, sc_att, _ptr(att, _f32p),
+                                      self.threads)
+        return xo
+
+    def attention_prefill(self, xq, kc, vc, spos, slide=0, sc_att=0.0, mask=True):
+        """gemma.c's prefill attention loop on the same arguments as
+        oracle.attention_prefill."""
+        xq = np.ascontiguousarray(xq, np.float32)
+        kc, vc, stride = _cache(kc, vc)
+        n_heads, ntok, hdim = xq.shape
+        xo = np.empty((ntok, n_heads * hdim), np.float32)
+        att = np.zeros(n_heads * ntok * (spos + ntok), np.float32)
+        if self.lib.ref_attention_prefill(_ptr(xo, _f32p), n_heads * hdim, _ptr(xq, _f32p), _ptr(kc, _f32p),
+                                          _ptr(vc, _f32p), stride, n_heads, kc.shape[0], hdim, spos, ntok, slide,
+                                          sc_att, int(mask), _ptr(att, _f32p)):
+            raise RuntimeError("reference attention_prefill failed")
+        return xo
 
     def read_model_seconds(self, path: str, allow_mm: bool = True) -> float:
         """Seconds gemma.c's read_gemma_model takes to load the file."""

@@ -154,3 +154,88 @@ double ref_read_model_seconds(const char *path, int allow_mm) {
   free_gemma_model(m);
   return (double)(t1.tv_sec - t0.tv_sec) + 1e-9 * (double)(t1.tv_nsec - t0.tv_nsec);
 }
+
+/* gemma.c:4836-4848: one decode step's attention, through the reference's
+ * own att_scores_gqa, att_finalize and att_values_gqa, with its buffer
+ * layout (att row h starts at att + spos + h*attlen; the cache rows of kv
+ * head hk at kc/vc + hk*kv_stride).  att: spos + n_heads*attlen floats. */
+void ref_attention_decode(float *xo, const float *xq, const float *kc, const float *vc,
+                          long kv_stride, int n_heads, int nkv, int hdim, int spos, int attlen,
+                          float asc, float sc_att, float *att, int threads) {
+  att_scores_gqa(att + spos, attlen, xq, kc + (size_t)spos * hdim, (int)kv_stride, nkv, n_heads,
+                 attlen, hdim, threads, NULL);
+  for (int h = 0; h < n_heads; h++)
+    att_finalize(att + (size_t)h * attlen + spos, attlen, asc, sc_att, NULL);
+  att_values_gqa(xo, att + spos, attlen, vc + (size_t)spos * hdim, (int)kv_stride, nkv, n_heads,
+                 attlen, hdim, threads, NULL);
+}
+
+/* gemma.c:5160-5295: a prefill chunk's attention, the per (head, query
+ * block) loop of forward_text_chunk restated around the reference's own
+ * gemm_fpx, softmax and gemm_fpx_nn.  xq [n_heads][ntok][hdim] (rotated and
+ * scaled); slide > 0 marks a sliding-window layer (tc->swa[l], tc->slide);
+ * xo row i of head h at xo + i*xostr + h*hdim.  att: n_heads*ntok*(spos+ntok)
+ * floats.  Single-threaded calls, as each OpenMP task of the reference is. */
+int ref_attention_prefill(float *xo, int xostr, const float *xq, const float *kc, const float *vc,
+                          long kv_stride, int n_heads, int nkv, int hdim, int spos, int ntok,
+                          int slide, float sc_att, int mask, float *att) {
+  const bool sliding = slide > 0;
+  const int epos = spos + ntok - 1, max_k = epos + 1;
+  const int qk = g_rt.qk_blk;
+  const int n_qb = mask ? (ntok + qk - 1) / qk : 1;
+  for (int qidx = 0; qidx < n_heads * n_qb; qidx++) {
+    const int h = qidx / n_qb, qbi = qidx % n_qb;
+    const int h_kv = h * nkv / n_heads;
+    float *att_h = att + (size_t)h * ntok * max_k;
+    const float *xv_head = vc + (size_t)h_kv * kv_stride;
+    float *xo_head = xo + (size_t)h * hdim;
+    if (mask) {
+      const int q_start = qbi * qk;
+      const float *qb = xq + (size_t)h * ntok * hdim + (size_t)q_start * hdim;
+      const int q_end = min(q_start + qk, ntok);
+      const int qabs_e = spos + q_end;
+      int qabs_s = spos + q_start;
+      if (sliding && qabs_s >= slide)
+        qabs_s = qabs_s + 1 - slide;
+      else
+        qabs_s = 0;
+      const int spos_b = qabs_s / qk * qk;
+      for (int k_start = spos_b; k_start < qabs_e; k_start += qk) {
+        const float *kb = kc + (size_t)h_kv * kv_stride + (size_t)k_start * hdim;
+        const int k_end = min(k_start + qk, max_k);
+        float *att_b = att_h + (size_t)q_start * max_k + k_start;
+        if (gemm_fpx(att_b, max_k, kb, 0, qb, 0, q_end - q_start, k_end - k_start, hdim, false, 1, NULL))
+          return 1;
+        for (int qi = q_start; qi < q_end; qi++) {
+          const int pos_i = spos + qi;
+          const int spos_i = (sliding && pos_i >= slide) ? (pos_i + 1 - slide) : 0;
+          for (int ki = k_start; ki < k_end; ki++)
+            if (ki > pos_i || ki < spos_i) att_h[(size_t)qi * max_k + ki] = 0.0f;
+        }
+      }
+      for (int qi = q_start; qi < q_end; qi++) {
+        float *att_row = att_h + (size_t)qi * max_k;
+        const int pos_i = spos + qi;
+        const int spos_i = (sliding && pos_i >= slide) ? (pos_i + 1 - slide) : 0;
+        if (sc_att != 0.0f)
+          for (int t = spos_i; t <= pos_i; t++) att_row[t] = tanhf(att_row[t] / sc_att) * sc_att;
+        softmax(att_row + spos_i, att_row + spos_i, pos_i - spos_i + 1, NULL);
+      }
+      gemm_fpx_nn(xo_head + (size_t)q_start * xostr, xostr, xv_head + (size_t)spos_b * hdim, 0,
+                  att_h + (size_t)q_start * max_k + spos_b, max_k, q_end - q_start, hdim, qabs_e - spos_b,
+                  false, 1, NULL);
+    } else {
+      const float *xq_head = xq + (size_t)h * ntok * hdim;
+      const float *xk_head = kc + (size_t)h_kv * kv_stride;
+      if (gemm_fpx(att_h, max_k, xk_head, 0, xq_head, 0, ntok, max_k, hdim, false, 1, NULL)) return 1;
+      for (int qi = 0; qi < ntok; qi++) {
+        float *att_row = att_h + (size_t)qi * max_k;
+        if (sc_att != 0.0f)
+          for (int t = 0; t < max_k; t++) att_row[t] = tanhf(att_row[t] / sc_att) * sc_att;
+        softmax(att_row, att_row, max_k, NULL);
+      }
+      gemm_fpx_nn(xo_head, xostr, xv_head, 0, att_h, max_k, ntok, hdim, max_k, false, 1, NULL);
+    }
+  }
+  return 0;
+}

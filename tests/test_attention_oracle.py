@@ -1,0 +1,89 @@
+"""The fp32 attention restatement (oracle) against gemma.c's own attention.
+
+tests/golden/attention.npz holds the outputs of the reference's decode
+attention (gemma.c:4836-4848) and prefill attention loop (gemma.c:5160-5295)
+on seeded inputs (make_attention_golden.py).  The reference is compiled with
+-ffast-math and vectorizes its fp32 dot products, so agreement is to fp32
+reassociation: max |oracle - reference| <= 1e-5 * max |reference| (measured
+1e-7 .. 3e-6 on these cases).  Host only.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+import oracle as O
+import synth
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+GOLD = np.load(os.path.join(HERE, "golden", "attention.npz"))
+META = json.loads(str(GOLD["meta"]))
+TOL = 1e-5  # of the output's largest magnitude
+
+
+def assert_attn_close(got, want, tol=TOL):
+    got, want = np.asarray(got, np.float32), np.asarray(want, np.float32)
+    assert got.shape == want.shape
+    err = float(np.max(np.abs(got - want)))
+    scale = float(np.max(np.abs(want)))
+    assert np.all(np.isfinite(got)) and err <= tol * scale, f"max err {err:.3g} vs {tol} x {scale:.3g}"
+
+
+@pytest.mark.parametrize("case", META["decode"], ids=lambda c: f"decode{c[0]}")
+def test_oracle_decode_matches_reference_fixture(case):
+    tid, nh, nkv, hd, clen, spos, attlen, sc = case
+    xq, kc, vc = synth.attention_inputs(tid, nh, nkv, hd, clen)
+    got = O.attention_decode(xq, kc, vc, spos, attlen, np.float32(1.0 / np.sqrt(hd)), sc)
+    assert_attn_close(got, GOLD[f"decode_{tid}"])
+
+
+@pytest.mark.parametrize("case", META["prefill"], ids=lambda c: f"prefill{c[0]}")
+def test_oracle_prefill_matches_reference_fixture(case):
+    tid, nh, nkv, hd, spos, ntok, slide, sc, mask = case
+    xq, kc, vc = synth.attention_inputs(tid, nh, nkv, hd, spos + ntok + 3, ntok)
+    got = O.attention_prefill(xq, kc, vc, spos, slide, sc, bool(mask))
+    assert_attn_close(got, GOLD[f"prefill_{tid}"])
+
+
+def _ref():
+    try:
+        lib = O.ref()
+    except OSError:
+        return None
+    if lib is None or not hasattr(lib, "ref_attention_decode"):
+        return None
+    return O.Ref(threads=4)
+
+
+@pytest.mark.parametrize("nh,nkv,hd,clen,spos,attlen,sc", [(4, 1, 256, 700, 200, 300, 0.0),
+                                                          (16, 8, 256, 1500, 0, 1500, 30.0),
+                                                          (6, 3, 64, 90, 17, 73, 0.0)])
+def test_oracle_decode_matches_live_reference(nh, nkv, hd, clen, spos, attlen, sc):
+    R = _ref()
+    if R is None:
+        pytest.skip("reference build not available")
+    xq, kc, vc = synth.attention_inputs(7 + attlen, nh, nkv, hd, clen)
+    asc = np.float32(1.0 / np.sqrt(hd))
+    assert_attn_close(O.attention_decode(xq, kc, vc, spos, attlen, asc, sc),
+                      R.attention_decode(xq, kc, vc, spos, attlen, asc, sc))
+
+
+@pytest.mark.parametrize("nh,nkv,hd,spos,ntok,slide,sc,mask", [(4, 1, 256, 0, 150, 64, 0.0, True),
+                                                               (8, 2, 128, 64, 96, 0, 20.0, True),
+                                                               (2, 1, 64, 30, 45, 16, 0.0, False)])
+def test_oracle_prefill_matches_live_reference(nh, nkv, hd, spos, ntok, slide, sc, mask):
+    R = _ref()
+    if R is None:
+        pytest.skip("reference build not available")
+    xq, kc, vc = synth.attention_inputs(9 + ntok, nh, nkv, hd, spos + ntok, ntok)
+    assert_attn_close(O.attention_prefill(xq, kc, vc, spos, slide, sc, mask),
+                      R.attention_prefill(xq, kc, vc, spos, slide, sc, mask))
+
+
+def test_oracle_single_position_returns_the_value_row():
+    # one visible position: weight fast_expf(0) = 1, so xo is V's row exactly
+    xq, kc, vc = synth.attention_inputs(3, 4, 2, 64, 10)
+    got = O.attention_decode(xq, kc, vc, 6, 1, np.float32(0.125))
+    want = np.repeat(vc[:, 6, :], 2, axis=0)
+    assert np.array_equal(got, want)

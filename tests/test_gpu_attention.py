@@ -1,0 +1,152 @@
+"""GPU attention kernels (k_attention.cu) against the reference and the oracle.
+
+Decode (gemma.c:4836-4848) and prefill (gemma.c:5160-5295) attention in fp32
+through the C ABI.  The reference's dot products are vectorized under
+-ffast-math, so agreement is to fp32 reassociation: max |gpu - reference|
+<= 1e-5 * max |reference|, against the golden fixture made by the compiled
+reference and against the oracle on larger seeded cases.  Size-independent
+checks: all-ones V gives ones (the weights sum to one), a single visible
+position returns its V row exactly.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+import oracle as O
+import synth
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+import gcu  # noqa: E402
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+GOLD = np.load(os.path.join(HERE, "golden", "attention.npz"))
+META = json.loads(str(GOLD["meta"]))
+TOL = 1e-5
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _gpu():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    gcu.init(0)
+    yield
+    gcu.check_device()
+
+
+def assert_attn_close(got, want, tol=TOL):
+    got, want = np.asarray(got, np.float32), np.asarray(want, np.float32)
+    assert got.shape == want.shape
+    err = float(np.max(np.abs(got - want)))
+    scale = float(np.max(np.abs(want)))
+    assert np.all(np.isfinite(got)) and err <= tol * scale, f"max err {err:.3g} vs {tol} x {scale:.3g}"
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def run_decode(xq, kc, vc, spos, attlen, asc, sc=0.0):
+    xo = torch.empty(xq.shape, device="cuda")
+    gcu.dev_attention_decode(xo, dev(xq), dev(kc), dev(vc), spos, attlen, float(asc), sc)
+    torch.cuda.synchronize()
+    return xo.cpu().numpy()
+
+
+def run_prefill(xq, kc, vc, spos, slide=0, sc=0.0, mask=True):
+    nh, ntok, hd = xq.shape
+    xo = torch.empty((ntok, nh * hd), device="cuda")
+    gcu.dev_attention_prefill(xo, dev(xq), dev(kc), dev(vc), spos, slide, sc, mask)
+    torch.cuda.synchronize()
+    return xo.cpu().numpy()
+
+
+@pytest.mark.parametrize("case", META["decode"], ids=lambda c: f"decode{c[0]}")
+def test_decode_matches_reference_fixture(case):
+    tid, nh, nkv, hd, clen, spos, attlen, sc = case
+    xq, kc, vc = synth.attention_inputs(tid, nh, nkv, hd, clen)
+    assert_attn_close(run_decode(xq, kc, vc, spos, attlen, np.float32(1.0 / np.sqrt(hd)), sc),
+                      GOLD[f"decode_{tid}"])
+
+
+@pytest.mark.parametrize("case", META["prefill"], ids=lambda c: f"prefill{c[0]}")
+def test_prefill_matches_reference_fixture(case):
+    tid, nh, nkv, hd, spos, ntok, slide, sc, mask = case
+    xq, kc, vc = synth.attention_inputs(tid, nh, nkv, hd, spos + ntok + 3, ntok)
+    assert_attn_close(run_prefill(xq, kc, vc, spos, slide, sc, bool(mask)), GOLD[f"prefill_{tid}"])
+
+
+# Gemma 3 decode shapes (heads, kv heads, head size) at several window lengths,
+# including windows that split over many CTAs and a sliding-window start
+@pytest.mark.parametrize("nh,nkv,hd,clen,spos,attlen,sc", [
+    (4, 1, 256, 64, 0, 64, 0.0), (4, 1, 256, 65, 0, 65, 0.0), (4, 1, 256, 4096, 3000, 512, 0.0),
+    (8, 4, 256, 8192, 0, 8192, 0.0), (16, 8, 256, 6000, 0, 6000, 50.0), (16, 8, 128, 777, 11, 700, 0.0),
+    (5, 1, 64, 3000, 0, 2999, 0.0)])
+def test_decode_matches_oracle(nh, nkv, hd, clen, spos, attlen, sc):
+    xq, kc, vc = synth.attention_inputs(300 + attlen, nh, nkv, hd, clen)
+    asc = np.float32(1.0 / np.sqrt(hd))
+    assert_attn_close(run_decode(xq, kc, vc, spos, attlen, asc, sc),
+                      O.attention_decode(xq, kc, vc, spos, attlen, asc, sc))
+
+
+@pytest.mark.parametrize("nh,nkv,hd,spos,ntok,slide,sc,mask", [
+    (4, 1, 256, 0, 512, 512, 0.0, True),     # Gemma-3-1B prefill chunk (config 1 shape)
+    (4, 1, 256, 600, 200, 512, 0.0, True),   # a later chunk on a sliding layer
+    (8, 4, 256, 0, 300, 0, 0.0, True),       # 4B heads, global layer
+    (8, 4, 128, 13, 77, 20, 30.0, True),
+    (2, 1, 64, 0, 100, 0, 0.0, False)])
+def test_prefill_matches_oracle(nh, nkv, hd, spos, ntok, slide, sc, mask):
+    xq, kc, vc = synth.attention_inputs(400 + ntok, nh, nkv, hd, spos + ntok, ntok)
+    assert_attn_close(run_prefill(xq, kc, vc, spos, slide, sc, mask),
+                      O.attention_prefill(xq, kc, vc, spos, slide, sc, mask))
+
+
+def test_weights_sum_to_one():
+    # all-ones V: every output is sum(p_t)/sum(p_t), 1 to rounding, at any length
+    xq, kc, _ = synth.attention_inputs(500, 4, 2, 256, 32768)
+    ones = np.ones_like(kc)
+    out = run_decode(xq, kc, ones, 0, 32768, np.float32(1 / 16))
+    assert np.max(np.abs(out - 1.0)) < 1e-5
+    xq, kc, _ = synth.attention_inputs(501, 4, 1, 256, 2048, 1024)
+    out = run_prefill(xq, kc, np.ones_like(kc), 1024, 512)
+    assert np.max(np.abs(out - 1.0)) < 1e-5
+
+
+def test_single_position_returns_value_row():
+    xq, kc, vc = synth.attention_inputs(502, 4, 2, 64, 10)
+    got = run_decode(xq, kc, vc, 6, 1, np.float32(0.125))
+    assert np.array_equal(got, np.repeat(vc[:, 6, :], 2, axis=0))
+    xq, kc, vc = synth.attention_inputs(503, 2, 1, 128, 1, 1)
+    assert np.array_equal(run_prefill(xq, kc, vc, 0), np.concatenate([vc[0, 0], vc[0, 0]])[None])
+
+
+def test_prefill_output_stride():
+    xq, kc, vc = synth.attention_inputs(504, 2, 1, 64, 20, 20)
+    xo = torch.full((20, 200), 7.0, device="cuda")
+    gcu.dev_attention_prefill(xo, dev(xq), dev(kc), dev(vc), 0, xostr=200)
+    torch.cuda.synchronize()
+    got = xo.cpu().numpy()
+    assert_attn_close(got[:, :128], O.attention_prefill(xq, kc, vc, 0))
+    assert np.all(got[:, 128:] == 7.0)
+
+
+def test_rejections():
+    xq, kc, vc = (dev(a) for a in synth.attention_inputs(505, 4, 1, 96, 10))
+    xo = torch.empty_like(xq)
+    with pytest.raises(gcu.GcuError, match="head size"):
+        gcu.dev_attention_decode(xo, xq, kc, vc, 0, 10, 0.1)
+    xq, kc, vc = (dev(a) for a in synth.attention_inputs(506, 4, 1, 64, 10))
+    with pytest.raises(gcu.GcuError, match="window"):
+        gcu.dev_attention_decode(torch.empty_like(xq), xq, kc, vc, 5, 6, 0.1)
+    with pytest.raises(gcu.GcuError, match="window"):
+        gcu.dev_attention_decode(torch.empty_like(xq), xq, kc, vc, 0, 0, 0.1)
+    xq9, kc9, vc9 = (dev(a) for a in synth.attention_inputs(507, 18, 2, 64, 10))
+    with pytest.raises(gcu.GcuError, match="per kv head"):
+        gcu.dev_attention_decode(torch.empty_like(xq9), xq9, kc9, vc9, 0, 10, 0.1)
+    xqp, kcp, vcp = (dev(a) for a in synth.attention_inputs(508, 2, 1, 64, 8, 8))
+    with pytest.raises(gcu.GcuError, match="outside a cache"):
+        gcu.dev_attention_prefill(torch.empty((8, 128), device="cuda"), xqp, kcp, vcp, 4)
+    gcu.check_device()
