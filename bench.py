@@ -965,6 +965,185 @@ def run_upload(args):
 
 
 # ---------------------------------------------------------------------------
+# attention (gcu_dev_attention_decode / _prefill), the fp32 layer around the
+# matmuls: Gemma 3's pattern of 5 sliding-window layers then 1 global layer
+# ---------------------------------------------------------------------------
+ATTN = {
+    "attn_decode12b": dict(title="Gemma-3-12B decode attention at position 32767, 48 layers "
+                                 "(40 sliding-window 1024, 8 global)", kind="decode", n_heads=16, nkv=8, hd=256,
+                           layers=48, pos=32767, slide=1024),
+    "attn_prefill1b": dict(title="Gemma-3-1B prefill attention, M=512 tokens from position 0, 26 layers "
+                                 "(sliding window 512 / global)", kind="prefill", n_heads=4, nkv=1, hd=256,
+                           layers=26, ntok=512, spos=0, slide=512),
+}
+
+
+def _attn_layers(c):
+    """Per layer: (global, spos, attlen or ntok, slide).  Layer l is global
+    when (l + 1) % 6 == 0 (Gemma 3's 5:1 pattern)."""
+    out = []
+    for l in range(c["layers"]):
+        glob = (l + 1) % 6 == 0
+        if c["kind"] == "decode":
+            pos = c["pos"]
+            spos = 0 if glob or pos < c["slide"] else pos + 1 - c["slide"]
+            out.append((glob, spos, pos + 1 - spos, 0 if glob else c["slide"]))
+        else:
+            out.append((glob, c["spos"], c["ntok"], 0 if glob else c["slide"]))
+    return out
+
+
+def run_attention(args):
+    """Decode: one step = every layer's attention of one token at `pos` (K/V
+    windows streamed from HBM; roofline: measured HBM copy bandwidth).
+    Prefill: one step = every layer's causal attention of an M-token chunk
+    (roofline: the fp32 FMA peak derived from the SM count and clock).
+    Inputs resident in HBM, each layer its own cache, one CUDA graph replay
+    per step, CUDA events on the launching stream."""
+    import numpy as np
+    import torch
+
+    import gcu
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    gcu.init(0)
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    peaks = load_peaks()
+    c = ATTN[args.workload]
+    nh, nkv, hd = c["n_heads"], c["nkv"], c["hd"]
+    lay = _attn_layers(c)
+    gen = torch.Generator(device=dev).manual_seed(5)
+    clen = c["pos"] + 1 if c["kind"] == "decode" else c["spos"] + c["ntok"]
+    bufs = []
+    for glob, spos, n, slide in lay:
+        kc = torch.randn((nkv, clen, hd), generator=gen, device=dev)
+        vc = torch.randn((nkv, clen, hd), generator=gen, device=dev)
+        if c["kind"] == "decode":
+            xq = torch.randn((nh, hd), generator=gen, device=dev)
+            xo = torch.empty((nh, hd), device=dev)
+        else:
+            xq = torch.randn((nh, n, hd), generator=gen, device=dev) / hd ** 0.5
+            xo = torch.empty((n, nh * hd), device=dev)
+        bufs.append((xq, kc, vc, xo))
+    asc = 1.0 / hd ** 0.5
+    stream = torch.cuda.Stream(dev)
+
+    def step():
+        for (glob, spos, n, slide), (xq, kc, vc, xo) in zip(lay, bufs):
+            if c["kind"] == "decode":
+                gcu.dev_attention_decode(xo, xq, kc, vc, spos, n, asc, stream=stream)
+            else:
+                gcu.dev_attention_prefill(xo, xq, kc, vc, spos, slide, stream=stream)
+
+    with torch.cuda.stream(stream):
+        step()
+    stream.synchronize()
+    gcu.check_device()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            graph.replay()
+    torch.cuda.synchronize()
+    clocks = Clocks(0)
+    clocks.start()
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    clk = clocks.stop()
+    gcu.check_device()
+
+    if c["kind"] == "decode":
+        kv = sum(2 * nkv * n * hd * 4 for _, _, n, _ in lay)
+        nbytes = kv + len(lay) * 2 * nh * hd * 4
+        value = nbytes / (ms * 1e-3) / 1e9
+        splits = [1 if n <= 64 else None for _, _, n, _ in lay]
+        roof = {"bound": "hbm", "achieved": value, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": value / peaks["hbm_gbs"], "peak_src": f"{peaks['src']} copy bandwidth",
+                "bytes_per_step": nbytes, "traffic": None}
+        unit, metric = "GB/s", "decode attention: K/V window bytes streamed from HBM per second"
+        launches = sum(1 if s == 1 else 2 for s in splits)
+    else:
+        flops = 0
+        for _, spos, n, slide in lay:
+            vis = 0
+            for i in range(n):
+                pos = spos + i
+                t0 = pos + 1 - slide if slide and pos >= slide else 0
+                vis += pos - t0 + 1
+            flops += 4 * nh * hd * vis  # q.k and p.v, 2 flops per multiply-add
+        value = flops / (ms * 1e-3) / 1e12
+        mhz = clk.get("sm_max_mhz") or 1965.0
+        peak = 148 * 128 * 2 * mhz * 1e6 / 1e12
+        roof = {"bound": "fp32", "achieved": value, "peak": peak, "unit": "TFLOP/s", "frac": value / peak,
+                "peak_src": "derived fp32 FMA peak: 148 SMs x 128 lanes x 2 flops x max SM clock",
+                "flops_per_step": flops, "note": "the kernel scores every key twice (max pass, weight pass): "
+                "1.5x the counted flops", "traffic": None}
+        unit, metric = "TFLOP/s", "prefill attention: causal fp32 flops per second"
+        launches = len(lay)
+    out = {"metric": metric, "value": value, "unit": unit, "n_gpus": 1, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "none",
+           "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "ours",
+           "config": {"workload": f"{args.workload}: {c['title']}", "heads": nh, "kv_heads": nkv, "head_dim": hd,
+                      "inputs": "each layer its own K/V cache in HBM (no L2 reuse across layers)"},
+           "roofline": roof, "clocks": clk, "gpu_launches": launches * args.steps,
+           "e2e": None, "e2e_note": "attention has no host-pointer entry point: it runs between device-resident "
+                                  "matmuls"}
+    if not args.no_cpu:
+        out["cpu_baseline"] = _attn_cpu_baseline(c, lay)
+    del graph
+    print(json.dumps(out), flush=True)
+
+
+def _attn_cpu_baseline(c, lay):
+    """gemma.c's own attention (oracle/_ref build, all host threads) on one
+    period of the layer pattern (5 sliding + 1 global), scaled to the step."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    variant = oracle.ref_variant()
+    lib = oracle.ref(variant) if variant else None
+    threads = os.cpu_count() or 1
+    if lib is None or not hasattr(lib, "ref_attention_decode"):
+        return {"value": None, "cores": threads, "kind": "reference", "sample": "reference build not available"}
+    R = oracle.Ref(variant, threads=threads)
+    nh, nkv, hd = c["n_heads"], c["nkv"], c["hd"]
+    rng = np.random.default_rng(0)
+    period = lay[:6]
+    clen = max(spos + n for _, spos, n, _ in period)
+    kc = rng.standard_normal((nkv, clen, hd), dtype=np.float32)
+    vc = rng.standard_normal((nkv, clen, hd), dtype=np.float32)
+    t = 0.0
+    for _, spos, n, slide in period:
+        if c["kind"] == "decode":
+            xq = rng.standard_normal((nh, hd), dtype=np.float32)
+            R.attention_decode(xq, kc, vc, spos, n, np.float32(1 / hd ** 0.5))
+            t0 = time.perf_counter()
+            R.attention_decode(xq, kc, vc, spos, n, np.float32(1 / hd ** 0.5))
+        else:
+            xq = rng.standard_normal((nh, n, hd), dtype=np.float32) / np.float32(hd ** 0.5)
+            R.attention_prefill(xq, kc, vc, spos, slide)
+            t0 = time.perf_counter()
+            R.attention_prefill(xq, kc, vc, spos, slide)
+        t += time.perf_counter() - t0
+    scale = len(lay) / len(period)
+    step_s = t * scale
+    return {"ms_per_step": step_s * 1e3, "cores": threads, "kind": "reference",
+            "sample": f"one period of the layer pattern (6 layers, gemma.c's attention, {variant}/{R.isa}), "
+                      f"scaled x{scale:.1f} to the step",
+            "speedup_note": "GPU step time vs this CPU step time"}
+
+
+# ---------------------------------------------------------------------------
 # reference arm: the reference's own CPU implementation of the path
 # ---------------------------------------------------------------------------
 def run_reference(args):
@@ -1009,7 +1188,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="prefill1b",
-                    choices=list(PREFILL) + list(DECODE) + ["lmhead4b"] + list(UPLOAD))
+                    choices=list(PREFILL) + list(DECODE) + ["lmhead4b"] + list(UPLOAD) + list(ATTN))
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--unfused", action="store_true",
                     help="decode: quantize and GEMV as separate launches (the reference's call split)")
@@ -1023,7 +1202,13 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.workload in UPLOAD:
+    if args.workload in ATTN:
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the attention lines carry the reference's "
+                              "attention timing as their cpu_baseline"}))
+        else:
+            run_attention(args)
+    elif args.workload in UPLOAD:
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "the model-upload line carries the reference's "
                               "read_gemma_model timing as its cpu_baseline"}))

@@ -327,6 +327,17 @@ __device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap *m, int x, 
                "r"(y)
                : "memory");
 }
+// 1D bulk copy of `bytes` (a multiple of 16) from a 16-byte aligned global
+// address into this CTA's shared memory (16-byte aligned), completing on
+// `bar` (complete_tx).  No multicast.
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
+                                          uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
 // L2 prefetch of `bytes` (a multiple of 16) from a 16-byte aligned address
 __device__ __forceinline__ void bulk_prefetch_l2(const void *p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");

@@ -87,6 +87,7 @@ struct DecodeArgs {
   int n_heads, nkv, spos, attlen, chunk, splits;
   float asc, sc_att;
   float *part;  // [splits][n_heads][HD] sums, then [splits][n_heads] max, then weight sums
+  unsigned int *err;
 };
 
 // query heads [h0, h1) of kv head hk (gqa_head_of, gemma.c:2861-2863)
@@ -116,27 +117,64 @@ __device__ __forceinline__ void load_lane(float (&v)[PL], const float *p) {
   }
 }
 
-// smem: scores / weights [G][chunk], then (HD < 256) [R][G][HD] partials
+// Cache tiles move by 1D bulk copies (positions of one kv head are
+// contiguous in the cache) through a ring of kStages shared-memory stages:
+// the K tiles of the CTA's slice, then its V tiles.  Thread 0 keeps kStages
+// copies in flight; every thread waits on a tile's mbarrier, and one CTA
+// barrier per tile both agrees on the outcome of the (bounded) wait and
+// frees the previous tile's stage for the next copy.
+constexpr int kTR = 16;     // cache rows per copy
+constexpr int kStages = 4;  // copies in flight per CTA
+
+template <int HD>
+struct DecSmem {
+  static constexpr int C4 = HD / 4;            // float4 columns of a row
+  static constexpr int R = kDecThreads / C4;   // row groups of the value phase
+  static constexpr size_t region = (size_t)kStages * kTR * HD > (size_t)R * kMaxGroup * HD
+                                       ? (size_t)kStages * kTR * HD
+                                       : (size_t)R * kMaxGroup * HD;
+  static size_t bytes(int chunk) { return (region + (size_t)kMaxGroup * chunk) * sizeof(float); }
+};
+
+// smem: the stage ring (reused at the end for the row groups' partial sums),
+// then the scores / weights [kMaxGroup][chunk]
 template <int HD>
 __global__ void __launch_bounds__(kDecThreads) k_attn_decode(DecodeArgs a) {
-  extern __shared__ float sm[];
+  extern __shared__ __align__(128) float sm[];
+  __shared__ __align__(8) uint64_t full[kStages];
   __shared__ float red[kDecThreads / 32][kMaxGroup];
   __shared__ float stat[2][kMaxGroup];  // row max, weight sum
+  using S = DecSmem<HD>;
   constexpr int PL = HD / 32;
-  constexpr int R = kDecThreads / HD;  // thread rows in the value phase
+  float *stage = sm, *sc = sm + S::region;
   ptx::griddep_launch();
   const int split = blockIdx.x, hk = blockIdx.y;
   const int h0 = gqa_head_of(hk, a.n_heads, a.nkv);
   const int G = gqa_head_of(hk + 1, a.n_heads, a.nkv) - h0;
   const int c0 = split * a.chunk;
   const int n = min(a.attlen, c0 + a.chunk) - c0;
+  const int nt = (n + kTR - 1) / kTR, nload = 2 * nt;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float *kh = a.kc + (size_t)hk * a.kv_stride + (size_t)(a.spos + c0) * HD;
   const float *vh = a.vc + (size_t)hk * a.kv_stride + (size_t)(a.spos + c0) * HD;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) ptx::mbar_init(&full[s], 1);
+    ptx::fence_mbar_init();
+  }
+  __syncthreads();
   ptx::griddep_wait();
+  const uint64_t pol = ptx::policy_evict_first();
+  int issued = 0;  // thread 0 only
+  auto issue = [&](int j) {
+    const int tile = j < nt ? j : j - nt;
+    const uint32_t bytes = (uint32_t)min(kTR, n - tile * kTR) * HD * sizeof(float);
+    ptx::mbar_arrive_expect_tx(&full[j % kStages], bytes);
+    ptx::bulk_load(stage + (size_t)(j % kStages) * kTR * HD, (j < nt ? kh : vh) + (size_t)tile * kTR * HD, bytes,
+                   &full[j % kStages], pol);
+  };
+  if (threadIdx.x == 0)
+    for (; issued < kStages && issued < nload; ++issued) issue(issued);
 
-  // scores: each warp takes every 8th position; a K row is read once for
-  // all G query heads of the group (att_scores_gqa's order of work)
   float q[kMaxGroup][PL];
 #pragma unroll
   for (int g = 0; g < kMaxGroup; ++g)
@@ -144,101 +182,133 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(DecodeArgs a) {
   float wmax[kMaxGroup];
 #pragma unroll
   for (int g = 0; g < kMaxGroup; ++g) wmax[g] = -INFINITY;
-  for (int t = warp; t < n; t += kDecThreads / 32) {
-    float k[PL];
-    load_lane<PL>(k, kh + (size_t)t * HD + lane * PL);
+  const int c = threadIdx.x % S::C4, r = threadIdx.x / S::C4;  // value phase: float4 column, row group
+  float4 acc[kMaxGroup];
 #pragma unroll
-    for (int g = 0; g < kMaxGroup; ++g) {
-      if (g < G) {
-        float d = 0.0f;
-#pragma unroll
-        for (int i = 0; i < PL; ++i) d += q[g][i] * k[i];
-        d = warp_sum(d);
-        const float s = softcap(d * a.asc, a.sc_att);  // att_finalize: *asc, then the cap
-        wmax[g] = fmaxf(wmax[g], s);
-        if (lane == 0) sm[g * a.chunk + t] = s;
-      }
-    }
-  }
-  if (lane == 0)
-#pragma unroll
-    for (int g = 0; g < kMaxGroup; ++g) red[warp][g] = wmax[g];
-  __syncthreads();
-  if (threadIdx.x < G) {
-    float m = red[0][threadIdx.x];
-    for (int w = 1; w < kDecThreads / 32; ++w) m = fmaxf(m, red[w][threadIdx.x]);
-    stat[0][threadIdx.x] = m;
-  }
-  __syncthreads();
+  for (int g = 0; g < kMaxGroup; ++g) acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
 
-  // softmax weights fast_expf(s - max) (gemma.c:4094-4105) and their sums
-  for (int g = 0; g < G; ++g) {
-    const float m = stat[0][g];
-    float l = 0.0f;
-    for (int t = threadIdx.x; t < n; t += kDecThreads) {
-      const float p = dev_fast_expf(sm[g * a.chunk + t] - m);
-      sm[g * a.chunk + t] = p;
-      l += p;
+  int j = 0;
+  for (; j < nload; ++j) {
+    const bool ok = ptx::mbar_wait(&full[j % kStages], (j / kStages) & 1, a.err, DEV_TIMEOUT_FULL);
+    if (__syncthreads_or(!ok)) break;  // also: every thread is done with tile j - 1
+    if (threadIdx.x == 0 && j >= 1 && issued < nload) {
+      ptx::fence_proxy_async_smem();
+      issue(issued++);
     }
-    l = warp_sum(l);
-    if (lane == 0) red[warp][g] = l;
+    const float *tl = stage + (size_t)(j % kStages) * kTR * HD;
+    const int tile = j < nt ? j : j - nt;
+    const int rows = min(kTR, n - tile * kTR);
+    if (j < nt) {
+      // scores of this tile's rows: warp w takes rows w and w + 8; a row is
+      // read once for every query head of the group
+#pragma unroll
+      for (int rr = 0; rr < kTR / (kDecThreads / 32); ++rr) {
+        const int row = warp + rr * (kDecThreads / 32);
+        if (row < rows) {
+          float k[PL];
+#pragma unroll
+          for (int i = 0; i < PL; ++i) k[i] = tl[row * HD + lane * PL + i];
+#pragma unroll
+          for (int g = 0; g < kMaxGroup; ++g) {
+            if (g < G) {
+              float d = 0.0f;
+#pragma unroll
+              for (int i = 0; i < PL; ++i) d += q[g][i] * k[i];
+              d = warp_sum(d);
+              const float s = softcap(d * a.asc, a.sc_att);  // att_finalize: *asc, then the cap
+              wmax[g] = fmaxf(wmax[g], s);
+              if (lane == 0) sc[g * a.chunk + tile * kTR + row] = s;
+            }
+          }
+        }
+      }
+      if (j == nt - 1) {
+        // softmax weights fast_expf(s - max) (gemma.c:4094-4105) and sums
+        if (lane == 0)
+#pragma unroll
+          for (int g = 0; g < kMaxGroup; ++g) red[warp][g] = wmax[g];
+        __syncthreads();
+        if (threadIdx.x < G) {
+          float m = red[0][threadIdx.x];
+          for (int w = 1; w < kDecThreads / 32; ++w) m = fmaxf(m, red[w][threadIdx.x]);
+          stat[0][threadIdx.x] = m;
+        }
+        __syncthreads();
+        for (int g = 0; g < G; ++g) {
+          const float m = stat[0][g];
+          float l = 0.0f;
+          for (int t = threadIdx.x; t < n; t += kDecThreads) {
+            const float p = dev_fast_expf(sc[g * a.chunk + t] - m);
+            sc[g * a.chunk + t] = p;
+            l += p;
+          }
+          l = warp_sum(l);
+          if (lane == 0) red[warp][g] = l;
+        }
+        __syncthreads();
+        if (threadIdx.x < G) {
+          float l = 0.0f;
+          for (int w = 0; w < kDecThreads / 32; ++w) l += red[w][threadIdx.x];
+          stat[1][threadIdx.x] = l;
+        }
+      }
+    } else {
+      // weighted V rows: thread (r, c) takes rows r, r + R, ... of the tile
+      for (int row = r; row < rows; row += S::R) {
+        const float4 v = *reinterpret_cast<const float4 *>(tl + row * HD + c * 4);
+        const int t = tile * kTR + row;
+#pragma unroll
+        for (int g = 0; g < kMaxGroup; ++g) {
+          if (g < G) {
+            const float p = sc[g * a.chunk + t];
+            acc[g].x += p * v.x;
+            acc[g].y += p * v.y;
+            acc[g].z += p * v.z;
+            acc[g].w += p * v.w;
+          }
+        }
+      }
+    }
   }
+  if (j < nload) {
+    // a copy never completed: the error word says so; wait (bounded) for the
+    // copies still in flight into this CTA's shared memory, then leave
+    if (threadIdx.x == 0)
+      for (int jj = j; jj < issued; ++jj)
+        ptx::mbar_wait(&full[jj % kStages], (jj / kStages) & 1, a.err, DEV_TIMEOUT_DRAIN);
+    return;
+  }
+  // merge the row groups' sums in row-group order (the ring is free now)
   __syncthreads();
-  if (threadIdx.x < G) {
-    float l = 0.0f;
-    for (int w = 0; w < kDecThreads / 32; ++w) l += red[w][threadIdx.x];
-    stat[1][threadIdx.x] = l;
-  }
-
-  // values: thread (r, d) sums weight * V[t][d] over t = r, r + R, ...
-  const int d = threadIdx.x % HD, r = threadIdx.x / HD;
-  float acc[kMaxGroup];
+  float *rs = sm;  // [R][kMaxGroup][HD]
 #pragma unroll
-  for (int g = 0; g < kMaxGroup; ++g) acc[g] = 0.0f;
-  int t = r;
-  for (; t + 3 * R < n; t += 4 * R) {
-    const float v0 = __ldg(vh + (size_t)t * HD + d), v1 = __ldg(vh + (size_t)(t + R) * HD + d);
-    const float v2 = __ldg(vh + (size_t)(t + 2 * R) * HD + d), v3 = __ldg(vh + (size_t)(t + 3 * R) * HD + d);
+  for (int g = 0; g < kMaxGroup; ++g)
+    if (g < G) *reinterpret_cast<float4 *>(rs + ((size_t)r * kMaxGroup + g) * HD + c * 4) = acc[g];
+  __syncthreads();
+  if (r != 0) return;
 #pragma unroll
-    for (int g = 0; g < kMaxGroup; ++g) {
-      if (g < G) {
-        const float *p = sm + g * a.chunk + t;
-        acc[g] += p[0] * v0;
-        acc[g] += p[R] * v1;
-        acc[g] += p[2 * R] * v2;
-        acc[g] += p[3 * R] * v3;
+  for (int g = 0; g < kMaxGroup; ++g) {
+    if (g < G) {
+      float4 s = *reinterpret_cast<const float4 *>(rs + (size_t)g * HD + c * 4);
+      for (int rr = 1; rr < S::R; ++rr) {
+        const float4 u = *reinterpret_cast<const float4 *>(rs + ((size_t)rr * kMaxGroup + g) * HD + c * 4);
+        s.x += u.x;
+        s.y += u.y;
+        s.z += u.z;
+        s.w += u.w;
       }
+      acc[g] = s;
     }
-  }
-  for (; t < n; t += R) {
-    const float v = __ldg(vh + (size_t)t * HD + d);
-#pragma unroll
-    for (int g = 0; g < kMaxGroup; ++g)
-      if (g < G) acc[g] += sm[g * a.chunk + t] * v;
-  }
-  if constexpr (R > 1) {
-    float *rs = sm + kMaxGroup * a.chunk;  // [R][G][HD]
-    __syncthreads();                       // every thread is done with the weights' smem neighbours
-#pragma unroll
-    for (int g = 0; g < kMaxGroup; ++g)
-      if (g < G) rs[(r * kMaxGroup + g) * HD + d] = acc[g];
-    __syncthreads();
-    if (r != 0) return;
-#pragma unroll
-    for (int g = 0; g < kMaxGroup; ++g) {
-      if (g < G) {
-        float s = rs[g * HD + d];
-        for (int rr = 1; rr < R; ++rr) s += rs[(rr * kMaxGroup + g) * HD + d];
-        acc[g] = s;
-      }
-    }
-  } else {
-    __syncthreads();  // stat[1] is written
   }
   if (a.splits == 1) {
 #pragma unroll
-    for (int g = 0; g < kMaxGroup; ++g)
-      if (g < G) a.xo[(size_t)(h0 + g) * HD + d] = acc[g] / stat[1][g];
+    for (int g = 0; g < kMaxGroup; ++g) {
+      if (g < G) {
+        const float l = stat[1][g];
+        *reinterpret_cast<float4 *>(a.xo + (size_t)(h0 + g) * HD + c * 4) =
+            make_float4(acc[g].x / l, acc[g].y / l, acc[g].z / l, acc[g].w / l);
+      }
+    }
     return;
   }
   float *po = a.part + (size_t)split * a.n_heads * HD;
@@ -247,8 +317,8 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(DecodeArgs a) {
 #pragma unroll
   for (int g = 0; g < kMaxGroup; ++g) {
     if (g < G) {
-      po[(size_t)(h0 + g) * HD + d] = acc[g];
-      if (d == 0) {
+      *reinterpret_cast<float4 *>(po + (size_t)(h0 + g) * HD + c * 4) = acc[g];
+      if (c == 0) {
         pm[h0 + g] = stat[0][g];
         pl[h0 + g] = stat[1][g];
       }
@@ -442,8 +512,21 @@ __global__ void __launch_bounds__(kPreThreads) k_attn_prefill(PrefillArgs a) {
 
 template <int HD>
 cudaError_t launch_decode(const DecodeArgs &a, cudaStream_t st) {
-  constexpr int R = kDecThreads / HD;
-  const size_t smem = ((size_t)kMaxGroup * a.chunk + (R > 1 ? (size_t)R * kMaxGroup * HD : 0)) * sizeof(float);
+  const size_t smem = DecSmem<HD>::bytes(a.chunk);
+  static std::mutex mu;
+  static unsigned long long done_mask = 0;
+  {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lk(mu);
+    if (!(done_mask & (1ull << (dev & 63)))) {
+      e = cudaFuncSetAttribute(k_attn_decode<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)DecSmem<HD>::bytes(kMaxChunk));
+      if (e != cudaSuccess) return e;
+      done_mask |= 1ull << (dev & 63);
+    }
+  }
   cudaError_t e = launch_k(k_attn_decode<HD>, dim3(a.splits, a.nkv), dim3(kDecThreads), smem, st, a);
   if (e != cudaSuccess || a.splits == 1) return e;
   return launch_k(k_attn_combine<HD>, dim3(a.n_heads), dim3(HD), 0, st, a.xo, (const float *)a.part, a.n_heads,
@@ -499,7 +582,8 @@ GCU_EXPORT int gcu_dev_attention_decode(float *xo, const float *xq, const float 
     return set_error("attention_decode: window [%d, %d) outside a cache of %ld floats per head", spos,
                      spos + attlen, kv_stride);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  DecodeArgs a{xo, xq, k_cache, v_cache, kv_stride, n_heads, nkv, spos, attlen, 0, 1, asc, sc_att, nullptr};
+  DecodeArgs a{xo, xq, k_cache, v_cache, kv_stride, n_heads, nkv, spos, attlen, 0, 1, asc, sc_att, nullptr,
+               dev_error_word()};
   // splits of the window: enough CTAs to stream it at full bandwidth, at
   // least 64 positions each, at most kMaxChunk
   const int target = 2 * num_sms();

@@ -303,7 +303,7 @@ def ref(variant: str | None = None) -> ctypes.CDLL | None:
             [ctypes.c_float, ctypes.c_float, _f32p, ctypes.c_int]
         lib.ref_attention_prefill.restype = ctypes.c_int
         lib.ref_attention_prefill.argtypes = [_f32p, ctypes.c_int, _f32p, _f32p, _f32p, ctypes.c_long] + \
-            [ctypes.c_int] * 6 + [ctypes.c_float, ctypes.c_int, _f32p]
+            [ctypes.c_int] * 6 + [ctypes.c_float, ctypes.c_int, _f32p, ctypes.c_int]
     if hasattr(lib, "ref_read_model_seconds"):
         lib.ref_read_model_seconds.restype = ctypes.c_double
         lib.ref_read_model_seconds.argtypes = [ctypes.c_char_p, ctypes.c_int]
@@ -385,7 +385,7 @@ class Ref:
         att = np.zeros(n_heads * ntok * (spos + ntok), np.float32)
         if self.lib.ref_attention_prefill(_ptr(xo, _f32p), n_heads * hdim, _ptr(xq, _f32p), _ptr(kc, _f32p),
                                           _ptr(vc, _f32p), stride, n_heads, kc.shape[0], hdim, spos, ntok, slide,
-                                          sc_att, int(mask), _ptr(att, _f32p)):
+                                          sc_att, int(mask), _ptr(att, _f32p), self.threads):
             raise RuntimeError("reference attention_prefill failed")
         return xo
 

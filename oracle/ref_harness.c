@@ -175,15 +175,19 @@ void ref_attention_decode(float *xo, const float *xq, const float *kc, const flo
  * gemm_fpx, softmax and gemm_fpx_nn.  xq [n_heads][ntok][hdim] (rotated and
  * scaled); slide > 0 marks a sliding-window layer (tc->swa[l], tc->slide);
  * xo row i of head h at xo + i*xostr + h*hdim.  att: n_heads*ntok*(spos+ntok)
- * floats.  Single-threaded calls, as each OpenMP task of the reference is. */
+ * floats.  `threads` OpenMP threads over the (head, query block) tasks, as
+ * the reference runs them; each task calls the GEMMs single-threaded. */
 int ref_attention_prefill(float *xo, int xostr, const float *xq, const float *kc, const float *vc,
                           long kv_stride, int n_heads, int nkv, int hdim, int spos, int ntok,
-                          int slide, float sc_att, int mask, float *att) {
+                          int slide, float sc_att, int mask, float *att, int threads) {
   const bool sliding = slide > 0;
   const int epos = spos + ntok - 1, max_k = epos + 1;
   const int qk = g_rt.qk_blk;
   const int n_qb = mask ? (ntok + qk - 1) / qk : 1;
-  for (int qidx = 0; qidx < n_heads * n_qb; qidx++) {
+  bool quit = false;
+  int qidx;
+#pragma omp parallel for private(qidx) schedule(dynamic) reduction(|| : quit) num_threads(threads)
+  for (qidx = 0; qidx < n_heads * n_qb; qidx++) {
     const int h = qidx / n_qb, qbi = qidx % n_qb;
     const int h_kv = h * nkv / n_heads;
     float *att_h = att + (size_t)h * ntok * max_k;
@@ -205,7 +209,7 @@ int ref_attention_prefill(float *xo, int xostr, const float *xq, const float *kc
         const int k_end = min(k_start + qk, max_k);
         float *att_b = att_h + (size_t)q_start * max_k + k_start;
         if (gemm_fpx(att_b, max_k, kb, 0, qb, 0, q_end - q_start, k_end - k_start, hdim, false, 1, NULL))
-          return 1;
+          quit = true;
         for (int qi = q_start; qi < q_end; qi++) {
           const int pos_i = spos + qi;
           const int spos_i = (sliding && pos_i >= slide) ? (pos_i + 1 - slide) : 0;
@@ -227,7 +231,7 @@ int ref_attention_prefill(float *xo, int xostr, const float *xq, const float *kc
     } else {
       const float *xq_head = xq + (size_t)h * ntok * hdim;
       const float *xk_head = kc + (size_t)h_kv * kv_stride;
-      if (gemm_fpx(att_h, max_k, xk_head, 0, xq_head, 0, ntok, max_k, hdim, false, 1, NULL)) return 1;
+      if (gemm_fpx(att_h, max_k, xk_head, 0, xq_head, 0, ntok, max_k, hdim, false, 1, NULL)) quit = true;
       for (int qi = 0; qi < ntok; qi++) {
         float *att_row = att_h + (size_t)qi * max_k;
         if (sc_att != 0.0f)
@@ -237,5 +241,5 @@ int ref_attention_prefill(float *xo, int xostr, const float *xq, const float *kc
       gemm_fpx_nn(xo_head, xostr, xv_head, 0, att_h, max_k, ntok, hdim, max_k, false, 1, NULL);
     }
   }
-  return 0;
+  return quit ? 1 : 0;
 }
