@@ -1144,6 +1144,106 @@ def _attn_cpu_baseline(c, lay):
 
 
 # ---------------------------------------------------------------------------
+# SigLIP head (gcu_dev_patch_embed, gcu_dev_vision_pool_quantize, then the
+# projection gcu_dev_gemm_int8): one 896 px image of Gemma-3-4B
+# ---------------------------------------------------------------------------
+def run_siglip_head(args):
+    """One step = patch embedding of an (896, 896, 3) image (4096 patches of
+    14 px -> 1152, the int8 position embedding added), LayerNorm -> 4x4
+    average pool -> RMSNorm -> quantize (256 tokens), and the int8 projection
+    to the 4B text width 2560.  Inputs resident in HBM, one CUDA graph replay
+    per step, CUDA events; roofline of the dominant kernel (patch embedding,
+    fp32 FMA-bound) against the fp32 FMA peak derived from SMs and clock."""
+    import numpy as np
+    import torch
+
+    import gcu
+    import synth
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    gcu.init(0)
+    torch.cuda.set_device(0)
+    v = synth.vision_head_inputs(700, 896, 14, 1152, 256, 2560)
+    ppi, side, dim, tdim = 64, 16, 1152, 2560
+    d = {k: torch.from_numpy(np.ascontiguousarray(v[k])).cuda() for k in
+         ("img", "pe", "pe_b", "pos_q", "pos_s", "post_n", "post_nb", "norm", "proj_q", "proj_s")}
+    x = torch.empty((ppi * ppi, dim), device="cuda")
+    q = torch.empty((side * side, dim), dtype=torch.int8, device="cuda")
+    sc = torch.empty(side * side, device="cuda")
+    y = torch.empty((side * side, tdim), device="cuda")
+    stream = torch.cuda.Stream()
+
+    def step(which=("pe", "pool", "proj")):
+        if "pe" in which:
+            gcu.dev_patch_embed(x, d["img"], d["pe"], d["pe_b"], d["pos_q"], d["pos_s"], 896, 14, dim, stream=stream)
+        if "pool" in which:
+            gcu.dev_vision_pool_quantize(q, sc, x, d["post_n"], d["post_nb"], d["norm"], v["eps"], ppi, side, dim,
+                                         stream=stream)
+        if "proj" in which:
+            gcu.dev_gemm_int8(y, d["proj_q"], d["proj_s"], q, sc, side * side, tdim, dim, stream=stream)
+
+    def timed(which):
+        with torch.cuda.stream(stream):
+            step(which)
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            step(which)
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(args.steps):
+                g.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        del g
+        return e0.elapsed_time(e1) / args.steps
+
+    clocks = Clocks(0)
+    clocks.start()
+    ms = timed(("pe", "pool", "proj"))
+    parts = {k: timed((k,)) for k in ("pe", "pool", "proj")}
+    clk = clocks.stop()
+    gcu.check_device()
+    pe_flops = 2 * ppi * ppi * dim * 3 * 14 * 14
+    mhz = clk.get("sm_max_mhz") or 1965.0
+    peak = 148 * 128 * 2 * mhz * 1e6 / 1e12
+    ach = pe_flops / (parts["pe"] * 1e-3) / 1e12
+    out = {"metric": "SigLIP head: images per second (patch embedding, pool, int8 projection)",
+           "value": 1e3 / ms, "unit": "images/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": ms, "higher_is_better": True, "scaling": "none", "vs_baseline": None,
+           "dtype": "f32 (patch embedding, norms), int8 (projection)", "data": "synthetic", "impl": "ours",
+           "config": {"workload": "siglip_head: Gemma-3-4B vision head, 896 px image, 4096 patches -> 256 tokens -> "
+                                  "2560", "inputs": "seeded image and weights resident in HBM"},
+           "stage_ms": parts,
+           "roofline": {"bound": "fp32", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
+                        "kernel": "k_patch_embed", "flops_per_launch": pe_flops,
+                        "peak_src": "derived fp32 FMA peak: 148 SMs x 128 lanes x 2 flops x max SM clock",
+                        "traffic": None},
+           "clocks": clk, "gpu_launches": 3 * args.steps, "e2e": None,
+           "e2e_note": "no host-pointer entry point: the head runs between device-resident tower layers"}
+    if not args.no_cpu:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle
+        variant = oracle.ref_variant()
+        lib = oracle.ref(variant) if variant else None
+        if lib is not None and hasattr(lib, "ref_vision_head"):
+            R = oracle.Ref(variant, threads=os.cpu_count() or 1)
+            R.vision_head(v)
+            t0 = time.perf_counter()
+            R.vision_head(v)
+            t = time.perf_counter() - t0
+            out["cpu_baseline"] = {"value": 1.0 / t, "unit": "images/s", "cores": R.threads, "kind": "reference",
+                                   "sample": f"gemma.c forward_vision on an encoder with no layers (the same head), "
+                                             f"{variant}/{R.isa}", "ms_per_step": t * 1e3}
+    print(json.dumps(out), flush=True)
+
+
+# ---------------------------------------------------------------------------
 # reference arm: the reference's own CPU implementation of the path
 # ---------------------------------------------------------------------------
 def run_reference(args):
@@ -1188,7 +1288,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="prefill1b",
-                    choices=list(PREFILL) + list(DECODE) + ["lmhead4b"] + list(UPLOAD) + list(ATTN))
+                    choices=list(PREFILL) + list(DECODE) + ["lmhead4b"] + list(UPLOAD) + list(ATTN) +
+                    ["siglip_head"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--unfused", action="store_true",
                     help="decode: quantize and GEMV as separate launches (the reference's call split)")
@@ -1202,7 +1303,13 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.workload in ATTN:
+    if args.workload == "siglip_head":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the SigLIP-head line carries the reference's "
+                              "forward_vision timing as its cpu_baseline"}))
+        else:
+            run_siglip_head(args)
+    elif args.workload in ATTN:
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "the attention lines carry the reference's "
                               "attention timing as their cpu_baseline"}))

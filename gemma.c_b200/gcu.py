@@ -85,6 +85,9 @@ SIGNATURES = {
                                         ctypes.c_float, ctypes.c_float, _vp]),
     "gcu_dev_attention_prefill": (_int, [_vp, _int, _vp, _vp, _vp, ctypes.c_long, _int, _int, _int, _int, _int,
                                          _int, ctypes.c_float, _int, _vp]),
+    "gcu_dev_patch_embed": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _int, _vp]),
+    "gcu_dev_vision_pool_quantize": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_float, _int, _int, _int,
+                                            _vp]),
 }
 # exported but not part of the public header (benchmark sweeps, self-test)
 EXTRA = {
@@ -422,3 +425,19 @@ def dev_attention_prefill(xo, xq, kc, vc, spos, slide=0, sc_att=0.0, mask=True, 
                                            clen * hdim, n_heads, nkv, hdim, spos, ntok, slide, sc_att, int(mask),
                                            _stream(stream)),
            "dev_attention_prefill")
+
+
+def dev_patch_embed(x, img, pe, pe_b, pos_q, pos_s, img_px, psize, dim, stream=None):
+    """gemma.c:4411-4466 on CUDA tensors: x (npatch, dim) from the image
+    (img_px, img_px, 3), pe (dim, 3, psize, psize), pe_b and the int8
+    position embedding (pos_q, pos_s)."""
+    _check(lib().gcu_dev_patch_embed(x.data_ptr(), img.data_ptr(), pe.data_ptr(), pe_b.data_ptr(), pos_q.data_ptr(),
+                                     pos_s.data_ptr(), img_px, psize, dim, _stream(stream)), "dev_patch_embed")
+
+
+def dev_vision_pool_quantize(q, s, x, post_n, post_nb, norm, eps, ppi, side, dim, out=None, stream=None):
+    """gemma.c:4660-4705 + 4714 on CUDA tensors: codes q (side*side, dim),
+    scales s, optional fp32 rows out, from the patch rows x (ppi*ppi, dim)."""
+    _check(lib().gcu_dev_vision_pool_quantize(q.data_ptr(), s.data_ptr(), out.data_ptr() if out is not None else None,
+                                              x.data_ptr(), post_n.data_ptr(), post_nb.data_ptr(), norm.data_ptr(),
+                                              eps, ppi, side, dim, _stream(stream)), "dev_vision_pool_quantize")

@@ -77,6 +77,26 @@ def attention_inputs(tensor_id: int, n_heads: int, nkv: int, hdim: int, clen: in
     return xq, kc, vc
 
 
+def vision_head_inputs(tensor_id: int, img_px: int, psize: int, dim: int, img_tok: int, tdim: int):
+    """Seeded operands of the SigLIP head (gemma.c:4411-4716): an
+    (img_px, img_px, 3) image of N(0, 0.5^2) pixels, patch-embedding weights
+    pe (dim, 3, psize, psize) and bias of N(0, 0.02^2), the int8 position
+    embedding (npatch rows of dim) and projection (tdim rows of dim)
+    quantized per row as the exporter does, LayerNorm weight 1 + N(0, 0.1^2)
+    and bias N(0, 0.1^2), RMSNorm weight N(0, 0.1^2)."""
+    ppi = img_px // psize
+    pos_q, pos_s = weight(tensor_id + 3, ppi * ppi, dim)
+    proj_q, proj_s = weight(tensor_id + 4, tdim, dim)
+    return {"img_px": img_px, "psize": psize, "dim": dim, "img_tok": img_tok, "tdim": tdim, "eps": 1e-6,
+            "img": normal(tensor_id, (img_px, img_px, 3), 0.5),
+            "pe": normal(tensor_id + 1, (dim, 3, psize, psize), 0.02),
+            "pe_b": normal(tensor_id + 2, (dim,), 0.02),
+            "pos_q": pos_q, "pos_s": pos_s, "proj_q": proj_q, "proj_s": proj_s,
+            "post_n": 1.0 + normal(tensor_id + 5, (dim,), 0.1),
+            "post_nb": normal(tensor_id + 6, (dim,), 0.1),
+            "norm": normal(tensor_id + 7, (dim,), 0.1)}
+
+
 def quantize_weight_rows(w: np.ndarray):
     """Exporter quantizer (model.py:151-161) in numpy fp32 arithmetic."""
     w = np.asarray(w, np.float32)

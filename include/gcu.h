@@ -247,6 +247,25 @@ int gcu_dev_attention_prefill(float *xo, int xostr, const float *xq, const float
                               const float *v_cache, long kv_stride, int n_heads, int nkv, int hdim,
                               int spos, int ntok, int slide, float sc_att, int mask, void *stream);
 
+/* ---- SigLIP head (fp32) around the vision tower's matmuls ------------------
+ * gemma.c:4411-4466: the patch embedding, Conv2d(3, dim, kernel = stride =
+ * psize, bias) of the (img_px, img_px, 3) image img, then the int8 position
+ * embedding (pos_q rows of dim, scales pos_s; the -q model's QTensor) added
+ * dequantized; each step clamped to the float range.  pe [dim][3][psize][psize],
+ * pe_b [dim]; x [(img_px/psize)^2][dim].  psize <= 16. */
+int gcu_dev_patch_embed(float *x, const float *img, const float *pe, const float *pe_b,
+                        const int8_t *pos_q, const float *pos_s, int img_px, int psize, int dim,
+                        void *stream);
+/* gemma.c:4660-4705 + the quantize_acts of 4714: LayerNorm (post_n, post_nb)
+ * of every patch row of x [ppi*ppi][dim], the average of each
+ * (ppi/side) x (ppi/side) block, gemma-style RMSNorm (norm), then the int8
+ * codes q [side*side][dim] and scales s of the pooled rows -- the input of the
+ * projection gcu_dev_gemm_int8.  out (may be NULL) receives the fp32 rows.
+ * dim a multiple of 4, at most 4096. */
+int gcu_dev_vision_pool_quantize(int8_t *q, float *s, float *out, const float *x, const float *post_n,
+                                 const float *post_nb, const float *norm, float eps, int ppi, int side,
+                                 int dim, void *stream);
+
 /* ---- row-sharded entry points (NCCL over NVLink) ---------------------------
  * No counterpart in the reference, which is single-process (README.md:614).
  * Rank r of `world` owns weight rows [r*n/world, (r+1)*n/world) of an n-row

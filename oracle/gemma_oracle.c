@@ -330,3 +330,77 @@ void orc_attention_prefill(float *xo, int xostr, const float *xq, const float *k
     }
   }
 }
+
+/* ---- SigLIP head: patch embedding, pooling --------------------------------- */
+
+static float orc_clamp(float v) { /* clamp_fpx for floatx = float, gemma.c:2504-2506 */
+  const float m = 3.402823466e38f;
+  return v > m ? m : (v < -m ? -m : v);
+}
+
+/* gemma.c:4411-4466: Conv2d(3, dim, kernel = stride = psize, bias) over the
+ * (img_px, img_px, 3) image, one row of x per patch (row-major patches), then
+ * the dequantized int8 position embedding added per element.
+ *   x[p][oc] = clamp(sum_{py,px,c} pe[oc][c][py][px] * img[oy*P+py][ox*P+px][c] + pe_b[oc])
+ *   x[p][oc] = clamp(x[p][oc] + (float)pos_q[p][oc] * pos_s[p]) */
+void orc_patch_embed(float *x, const float *img, const float *pe, const float *pe_b, const int8_t *pos_q,
+                     const float *pos_s, int img_px, int psize, int dim) {
+  const int ppi = img_px / psize, idim = 3 * psize * psize;
+  for (int pi = 0; pi < ppi * ppi; pi++) {
+    const int oy = pi / ppi, ox = pi - oy * ppi;
+    for (int oc = 0; oc < dim; oc++) {
+      float sum = 0.0f;
+      for (int py = 0; py < psize; py++)
+        for (int px = 0; px < psize; px++)
+          for (int c = 0; c < 3; c++)
+            sum += pe[(size_t)oc * idim + c * psize * psize + py * psize + px] *
+                   img[((size_t)(oy * psize + py) * img_px + (ox * psize + px)) * 3 + c];
+      float v = orc_clamp(sum + pe_b[oc]);
+      v = orc_clamp(v + (float)pos_q[(size_t)pi * dim + oc] * pos_s[pi]);
+      x[(size_t)pi * dim + oc] = v;
+    }
+  }
+}
+
+/* gemma.c:4660-4705, 4714: LayerNorm of every patch row (weight post_n, bias
+ * post_nb, gemma.c:2526-2551), average pooling of ksize x ksize patches
+ * (ksize = ppi / side) in (ky, kx) order, gemma-style RMSNorm (norm,
+ * gemma.c:2509-2523), then quantize_acts of the pooled rows.  out (optional)
+ * [side*side][dim]; q [side*side][dim], s [side*side]. */
+void orc_vision_pool(int8_t *q, float *s, float *out, const float *x, const float *post_n,
+                     const float *post_nb, const float *norm, float eps, int ppi, int side, int dim,
+                     float *scratch /* dim floats */) {
+  const int ks = ppi / side;
+  for (int oy = 0; oy < side; oy++) {
+    for (int ox = 0; ox < side; ox++) {
+      float *acc = scratch;
+      for (int d = 0; d < dim; d++) acc[d] = 0.0f;
+      for (int ky = 0; ky < ks; ky++) {
+        for (int kx = 0; kx < ks; kx++) {
+          const float *row = x + ((size_t)(oy * ks + ky) * ppi + (ox * ks + kx)) * dim;
+          float mean = 0.0f;
+          for (int d = 0; d < dim; d++) mean += row[d];
+          mean /= (float)dim;
+          float var = 0.0f;
+          for (int d = 0; d < dim; d++) {
+            const float df = row[d] - mean;
+            var += df * df;
+          }
+          var /= (float)dim;
+          const float inv_std = 1.0f / sqrtf(var + eps);
+          for (int d = 0; d < dim; d++) acc[d] += (row[d] - mean) * inv_std * post_n[d] + post_nb[d];
+        }
+      }
+      const int o = oy * side + ox;
+      float sq = 0.0f;
+      for (int d = 0; d < dim; d++) {
+        acc[d] = acc[d] / (float)(ks * ks);
+        sq += acc[d] * acc[d];
+      }
+      const float rms = 1.0f / sqrtf(sq / (float)dim + eps);
+      for (int d = 0; d < dim; d++) acc[d] = acc[d] * rms * (norm[d] + 1.0f);
+      if (out) memcpy(out + (size_t)o * dim, acc, (size_t)dim * sizeof(float));
+      s[o] = orc_quantize_act(q + (size_t)o * dim, acc, dim);
+    }
+  }
+}

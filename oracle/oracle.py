@@ -90,6 +90,12 @@ def orc() -> ctypes.CDLL:
         lib.orc_attention_prefill.restype = None
         lib.orc_attention_prefill.argtypes = [_f32p, ctypes.c_int, _f32p, _f32p, _f32p, ctypes.c_long] + \
             [ctypes.c_int] * 6 + [ctypes.c_float, ctypes.c_int, _f32p]
+        lib.orc_patch_embed.restype = None
+        lib.orc_patch_embed.argtypes = [_f32p, _f32p, _f32p, _f32p, _i8p, _f32p, ctypes.c_int, ctypes.c_int,
+                                        ctypes.c_int]
+        lib.orc_vision_pool.restype = None
+        lib.orc_vision_pool.argtypes = [_i8p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, ctypes.c_float,
+                                        ctypes.c_int, ctypes.c_int, ctypes.c_int, _f32p]
         _orc = lib
     return _orc
 
@@ -237,6 +243,32 @@ def attention_prefill(xq, kc, vc, spos, slide=0, sc_att=0.0, mask=True):
     return xo
 
 
+def patch_embed(v: dict):
+    """gemma.c:4411-4466 on synth.vision_head_inputs: (npatch, dim) fp32."""
+    ppi = v["img_px"] // v["psize"]
+    dim = v["dim"]
+    x = np.empty((ppi * ppi, dim), np.float32)
+    orc().orc_patch_embed(_ptr(x, _f32p), _ptr(v["img"], _f32p), _ptr(v["pe"], _f32p), _ptr(v["pe_b"], _f32p),
+                          _ptr(v["pos_q"], _i8p), _ptr(v["pos_s"], _f32p), v["img_px"], v["psize"], dim)
+    return x
+
+
+def vision_pool(x: np.ndarray, v: dict):
+    """gemma.c:4660-4705 + the quantize of 4714: pooled rows, codes, scales."""
+    x = np.ascontiguousarray(x, np.float32)
+    ppi = v["img_px"] // v["psize"]
+    side = int(round(np.sqrt(v["img_tok"])))
+    dim = v["dim"]
+    out = np.empty((side * side, dim), np.float32)
+    q = np.empty((side * side, dim), np.int8)
+    s = np.empty(side * side, np.float32)
+    scratch = np.empty(dim, np.float32)
+    orc().orc_vision_pool(_ptr(q, _i8p), _ptr(s, _f32p), _ptr(out, _f32p), _ptr(x, _f32p), _ptr(v["post_n"], _f32p),
+                          _ptr(v["post_nb"], _f32p), _ptr(v["norm"], _f32p), v["eps"], ppi, side, dim,
+                          _ptr(scratch, _f32p))
+    return out, q, s
+
+
 # --------------------------------------------------------------------------
 # the compiled reference (gemma.c's own functions)
 # --------------------------------------------------------------------------
@@ -304,6 +336,10 @@ def ref(variant: str | None = None) -> ctypes.CDLL | None:
         lib.ref_attention_prefill.restype = ctypes.c_int
         lib.ref_attention_prefill.argtypes = [_f32p, ctypes.c_int, _f32p, _f32p, _f32p, ctypes.c_long] + \
             [ctypes.c_int] * 6 + [ctypes.c_float, ctypes.c_int, _f32p, ctypes.c_int]
+    if hasattr(lib, "ref_vision_head"):
+        lib.ref_vision_head.restype = ctypes.c_int
+        lib.ref_vision_head.argtypes = [_f32p, _f32p, _i8p, _f32p, _f32p] + [ctypes.c_int] * 5 + \
+            [ctypes.c_float, _f32p, _f32p, _i8p, _f32p, _f32p, _f32p, _f32p, _i8p, _f32p, ctypes.c_int]
     if hasattr(lib, "ref_read_model_seconds"):
         lib.ref_read_model_seconds.restype = ctypes.c_double
         lib.ref_read_model_seconds.argtypes = [ctypes.c_char_p, ctypes.c_int]
@@ -388,6 +424,25 @@ class Ref:
                                           sc_att, int(mask), _ptr(att, _f32p), self.threads):
             raise RuntimeError("reference attention_prefill failed")
         return xo
+
+    def vision_head(self, v: dict):
+        """gemma.c's forward_vision with no encoder layers on
+        synth.vision_head_inputs: (projection output, pooled rows, codes, scales)."""
+        side = int(round(np.sqrt(v["img_tok"])))
+        n, dim, tdim = side * side, v["dim"], v["tdim"]
+        out = np.empty((n, tdim), np.float32)
+        pooled = np.empty((n, dim), np.float32)
+        q = np.empty((n, dim), np.int8)
+        s = np.empty(n, np.float32)
+        rc = self.lib.ref_vision_head(_ptr(out, _f32p), _ptr(pooled, _f32p), _ptr(q, _i8p), _ptr(s, _f32p),
+                                      _ptr(v["img"], _f32p), v["img_px"], v["psize"], dim, v["img_tok"], tdim,
+                                      v["eps"], _ptr(v["pe"], _f32p), _ptr(v["pe_b"], _f32p), _ptr(v["pos_q"], _i8p),
+                                      _ptr(v["pos_s"], _f32p), _ptr(v["post_n"], _f32p), _ptr(v["post_nb"], _f32p),
+                                      _ptr(v["norm"], _f32p), _ptr(v["proj_q"], _i8p), _ptr(v["proj_s"], _f32p),
+                                      self.threads)
+        if rc:
+            raise RuntimeError("reference forward_vision failed")
+        return out, pooled, q, s
 
     def read_model_seconds(self, path: str, allow_mm: bool = True) -> float:
         """Seconds gemma.c's read_gemma_model takes to load the file."""

@@ -243,3 +243,72 @@ int ref_attention_prefill(float *xo, int xostr, const float *xq, const float *kc
   }
   return quit ? 1 : 0;
 }
+
+/* gemma.c:4391 forward_vision on an encoder with no layers: the patch
+ * embedding and position embedding (gemma.c:4411-4466), the post LayerNorm,
+ * average pooling and RMSNorm (gemma.c:4660-4705), then quantize_acts and the
+ * int8 projection (gemma.c:4714-4716) -- the reference's own code end to end.
+ * img [img_px][img_px][3]; pe [dim][3][psize][psize]; pos_q/pos_s the
+ * position embedding QTensor (npatch rows of dim); proj_q/proj_s the
+ * projection QTensor (tdim rows of dim).  Outputs: out [img_tok][tdim] (the
+ * projection), and when non-null the pooled RMSNorm'd rows pooled
+ * [img_tok][dim] with their codes q and scales s. */
+int ref_vision_head(float *out, float *pooled, int8_t *q, float *s, const float *img, int img_px,
+                    int psize, int dim, int img_tok, int tdim, float eps, const float *pe,
+                    const float *pe_b, const int8_t *pos_q, const float *pos_s, const float *post_n,
+                    const float *post_nb, const float *norm, const int8_t *proj_q,
+                    const float *proj_s, int threads) {
+  const int ppi = img_px / psize, npatch = ppi * ppi;
+  VisionConfig vc;
+  memset(&vc, 0, sizeof(vc));
+  vc.nl = 0;
+  vc.n_heads = 1;
+  vc.img_px = (uint16_t)img_px;
+  vc.psize = (uint16_t)psize;
+  vc.dim = (uint16_t)dim;
+  vc.mlp_dim = (uint16_t)dim;
+  vc.eps = eps;
+  TextConfig tc;
+  memset(&tc, 0, sizeof(tc));
+  tc.img_tok = (uint16_t)img_tok;
+  tc.dim = (uint16_t)tdim;
+  QTensor pos, proj;
+  memset(&pos, 0, sizeof(pos));
+  memset(&proj, 0, sizeof(proj));
+  pos.quant = true;
+  pos.i8.q = (int8_t *)pos_q;
+  pos.i8.scales = (floatx *)pos_s;
+  proj.quant = true;
+  proj.i8.q = (int8_t *)proj_q;
+  proj.i8.scales = (floatx *)proj_s;
+  VisionEncoder enc;
+  memset(&enc, 0, sizeof(enc));
+  enc.config = &vc;
+  enc.pe = (floatx *)pe;
+  enc.pe_b = (floatx *)pe_b;
+  enc.pos_emb = &pos;
+  enc.layers = NULL;
+  enc.post_n = (floatx *)post_n;
+  enc.post_nb = (floatx *)post_nb;
+  enc.norm = (floatx *)norm;
+  enc.proj = &proj;
+  VisionBuffer vb;
+  memset(&vb, 0, sizeof(vb));
+  vb.x = malloc((size_t)npatch * dim * sizeof(floatx));
+  vb.x_i8 = malloc((size_t)npatch * dim);
+  vb.xsc = malloc((size_t)npatch * sizeof(floatx));
+  TextBuffer tb;
+  memset(&tb, 0, sizeof(tb));
+  tb.x = out;
+  int rc = 1;
+  if (vb.x && vb.x_i8 && vb.xsc) {
+    rc = forward_vision(&enc, &tc, &tb, &vb, img, true, threads, NULL);
+    if (pooled) memcpy(pooled, vb.x, (size_t)img_tok * dim * sizeof(floatx));
+    if (q) memcpy(q, vb.x_i8, (size_t)img_tok * dim);
+    if (s) memcpy(s, vb.xsc, (size_t)img_tok * sizeof(floatx));
+  }
+  free(vb.x);
+  free(vb.x_i8);
+  free(vb.xsc);
+  return rc;
+}
