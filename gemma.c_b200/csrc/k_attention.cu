@@ -360,6 +360,8 @@ struct PrefillArgs {
   long kv_stride;
   int n_heads, nkv, spos, ntok, slide, mask;
   float sc_att;
+  int kpc, maxch;  // key tiles per chunk, chunks per query tile (grid z)
+  float *part;     // maxch > 1: [n_heads][ntok][maxch][HD] sums, then maxima, then weight sums
 };
 
 template <int HD>
@@ -436,7 +438,12 @@ __global__ void __launch_bounds__(kPreThreads) k_attn_prefill(PrefillArgs a) {
   row_window(a, i0 + min(qi, nrows - 1), t0, t1);
   row_window(a, i0, lo, unused);              // windows only move right with i
   row_window(a, i0 + nrows - 1, unused, hi);
-  const int kend = hi + 1;
+  // this CTA's chunk of the tile's key range: kpc key tiles
+  const int ntiles = (hi + 1 - lo + kBK - 1) / kBK, nch = (ntiles + a.kpc - 1) / a.kpc;
+  const int chunk = blockIdx.z;
+  if (chunk >= nch) return;
+  const int kbeg = lo + chunk * a.kpc * kBK;
+  const int kend = min(hi + 1, kbeg + a.kpc * kBK);
   ptx::griddep_wait();
 
   for (int idx = threadIdx.x; idx < kBQ * HD / 4; idx += kPreThreads) {
@@ -449,7 +456,7 @@ __global__ void __launch_bounds__(kPreThreads) k_attn_prefill(PrefillArgs a) {
 
   // pass 1: the maximum capped score of each row over its window
   float m = -INFINITY;
-  for (int k0 = lo; k0 < kend; k0 += kBK) {
+  for (int k0 = kbeg; k0 < kend; k0 += kBK) {
     __syncthreads();  // the previous tile (and the Q tile's stores) are done
     load_tile<HD>(ks, S::KS, kh, k0, kend);
     __syncthreads();
@@ -458,7 +465,7 @@ __global__ void __launch_bounds__(kPreThreads) k_attn_prefill(PrefillArgs a) {
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       const int t = k0 + kq + 16 * c;
-      if (t >= t0 && t <= t1) m = fmaxf(m, softcap(s[c], a.sc_att));
+      if (t >= t0 && t <= t1 && t < kend) m = fmaxf(m, softcap(s[c], a.sc_att));
     }
   }
 #pragma unroll
@@ -470,7 +477,7 @@ __global__ void __launch_bounds__(kPreThreads) k_attn_prefill(PrefillArgs a) {
   float4 acc[HD / 64];
 #pragma unroll
   for (int c = 0; c < HD / 64; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int k0 = lo; k0 < kend; k0 += kBK) {
+  for (int k0 = kbeg; k0 < kend; k0 += kBK) {
     __syncthreads();
     load_tile<HD>(ks, S::KS, kh, k0, kend);
     load_tile<HD>(vs, HD, vh, k0, kend);
@@ -480,7 +487,7 @@ __global__ void __launch_bounds__(kPreThreads) k_attn_prefill(PrefillArgs a) {
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       const int t = k0 + kq + 16 * c;
-      const float p = (t >= t0 && t <= t1) ? dev_fast_expf(softcap(s[c], a.sc_att) - m) : 0.0f;
+      const float p = (t >= t0 && t <= t1 && t < kend) ? dev_fast_expf(softcap(s[c], a.sc_att) - m) : 0.0f;
       ps[qi * kBK + kq + 16 * c] = p;
       l += p;
     }
@@ -503,11 +510,58 @@ __global__ void __launch_bounds__(kPreThreads) k_attn_prefill(PrefillArgs a) {
 #pragma unroll
   for (int o = 8; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
   if (qi >= nrows) return;
-  float *out = a.xo + (size_t)(i0 + qi) * a.xostr + (size_t)h * HD + kq * 4;
+  if (nch == 1) {
+    float *out = a.xo + (size_t)(i0 + qi) * a.xostr + (size_t)h * HD + kq * 4;
 #pragma unroll
-  for (int c = 0; c < HD / 64; ++c)
-    *reinterpret_cast<float4 *>(out + 64 * c) =
-        make_float4(acc[c].x / l, acc[c].y / l, acc[c].z / l, acc[c].w / l);
+    for (int c = 0; c < HD / 64; ++c)
+      *reinterpret_cast<float4 *>(out + 64 * c) =
+          make_float4(acc[c].x / l, acc[c].y / l, acc[c].z / l, acc[c].w / l);
+    return;
+  }
+  // a chunk of several: leave the unnormalised sums, the maximum and the
+  // weight sum (a row with no key in this chunk leaves -inf, 0, zeros)
+  const size_t r = ((size_t)h * a.ntok + i0 + qi) * a.maxch + chunk;
+  const size_t nrec = (size_t)a.n_heads * a.ntok * a.maxch;
+  float *po = a.part + r * HD + kq * 4;
+#pragma unroll
+  for (int c = 0; c < HD / 64; ++c) *reinterpret_cast<float4 *>(po + 64 * c) = acc[c];
+  if (kq == 0) {
+    a.part[nrec * HD + r] = m;
+    a.part[nrec * (HD + 1) + r] = l;
+  }
+}
+
+// merges the chunks of token i, head h in chunk order:
+// m = max m_c, xo = sum e_c O_c / sum e_c l_c, e_c = fast_expf(m_c - m)
+template <int HD>
+__global__ void __launch_bounds__(HD / 4) k_attn_prefill_merge(PrefillArgs a) {
+  ptx::griddep_launch();
+  const int i = blockIdx.x, h = blockIdx.y, c = threadIdx.x;
+  const int i0 = (i / kBQ) * kBQ, nrows = min(kBQ, a.ntok - i0);
+  int lo, hi, unused;
+  row_window(a, i0, lo, unused);
+  row_window(a, i0 + nrows - 1, unused, hi);
+  const int nch = ((hi + 1 - lo + kBK - 1) / kBK + a.kpc - 1) / a.kpc;
+  if (nch == 1) return;  // the chunk kernel wrote this row
+  const size_t r0 = ((size_t)h * a.ntok + i) * a.maxch;
+  const size_t nrec = (size_t)a.n_heads * a.ntok * a.maxch;
+  const float *pm = a.part + nrec * HD, *pl = a.part + nrec * (HD + 1);
+  ptx::griddep_wait();
+  float m = -INFINITY;
+  for (int ch = 0; ch < nch; ++ch) m = fmaxf(m, pm[r0 + ch]);
+  float l = 0.0f;
+  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int ch = 0; ch < nch; ++ch) {
+    const float e = dev_fast_expf(pm[r0 + ch] - m);
+    l += e * pl[r0 + ch];
+    const float4 u = *reinterpret_cast<const float4 *>(a.part + (r0 + ch) * HD + c * 4);
+    o.x += e * u.x;
+    o.y += e * u.y;
+    o.z += e * u.z;
+    o.w += e * u.w;
+  }
+  *reinterpret_cast<float4 *>(a.xo + (size_t)i * a.xostr + (size_t)h * HD + c * 4) =
+      make_float4(o.x / l, o.y / l, o.z / l, o.w / l);
 }
 
 template <int HD>
@@ -550,8 +604,10 @@ cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t st) {
       done_mask |= 1ull << (dev & 63);
     }
   }
-  const dim3 grid((a.ntok + kBQ - 1) / kBQ, a.n_heads);
-  return launch_k(k_attn_prefill<HD>, grid, dim3(kPreThreads), PreSmem<HD>::bytes, st, a);
+  const dim3 grid((a.ntok + kBQ - 1) / kBQ, a.n_heads, a.maxch);
+  cudaError_t e = launch_k(k_attn_prefill<HD>, grid, dim3(kPreThreads), PreSmem<HD>::bytes, st, a);
+  if (e != cudaSuccess || a.maxch == 1) return e;
+  return launch_k(k_attn_prefill_merge<HD>, dim3(a.ntok, a.n_heads), dim3(HD / 4), 0, st, a);
 }
 
 bool aligned16(const void *p) { return ((uintptr_t)p & 15) == 0; }
@@ -618,7 +674,29 @@ GCU_EXPORT int gcu_dev_attention_prefill(float *xo, int xostr, const float *xq, 
     return set_error("attention_prefill: chunk [%d, %d) outside a cache of %ld floats per head", spos, spos + ntok,
                      kv_stride);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  PrefillArgs a{xo, xostr, xq, k_cache, v_cache, kv_stride, n_heads, nkv, spos, ntok, slide, mask ? 1 : 0, sc_att};
+  PrefillArgs a{xo, xostr, xq, k_cache, v_cache, kv_stride, n_heads, nkv, spos, ntok, slide, mask ? 1 : 0, sc_att,
+                1, 1, nullptr};
+  // the causal triangle gives late query tiles many key tiles and early ones
+  // few: split every tile's key range into chunks of kpc key tiles (at most 8
+  // chunks), so the longest CTA does kpc tiles, not the whole range
+  int max_tiles = 1;
+  for (int i0 = 0; i0 < ntok; i0 += kBQ) {
+    const int i1 = std::min(ntok, i0 + kBQ) - 1;
+    int lo = 0, hi = spos + ntok - 1;
+    if (a.mask) {
+      lo = (slide > 0 && spos + i0 >= slide) ? spos + i0 + 1 - slide : 0;
+      hi = spos + i1;
+    }
+    max_tiles = std::max(max_tiles, (hi + 1 - lo + kBK - 1) / kBK);
+  }
+  a.kpc = std::max(2, (max_tiles + 7) / 8);
+  a.maxch = (max_tiles + a.kpc - 1) / a.kpc;
+  if (a.maxch > 1) {
+    void *ws;
+    int *cnt;
+    if (gemm_workspace((size_t)n_heads * ntok * a.maxch * (hdim + 2) * sizeof(float), &ws, &cnt, 0, st)) return 1;
+    a.part = static_cast<float *>(ws);
+  }
   cudaError_t e = hdim == 256 ? launch_prefill<256>(a, st) : hdim == 128 ? launch_prefill<128>(a, st)
                                                                          : launch_prefill<64>(a, st);
   GCU_CUDA(e);
