@@ -454,18 +454,23 @@ __global__ void __launch_bounds__(kPreThreads) k_attn_prefill(PrefillArgs a) {
     *reinterpret_cast<float4 *>(qs + row * S::KS + c * 4) = v;
   }
 
-  // pass 1: the maximum capped score of each row over its window
-  float m = -INFINITY;
+  // pass 1: the maximum capped score of each row over its window.  A chunk
+  // of one key tile keeps that tile and its scores for pass 2.
+  const bool one = kend - kbeg <= kBK;
+  float m = -INFINITY, keep[4];
   for (int k0 = kbeg; k0 < kend; k0 += kBK) {
     __syncthreads();  // the previous tile (and the Q tile's stores) are done
     load_tile<HD>(ks, S::KS, kh, k0, kend);
+    if (one) load_tile<HD>(vs, HD, vh, k0, kend);
     __syncthreads();
     float s[4];
     tile_scores<HD>(qs, ks, qi, kq, s);
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       const int t = k0 + kq + 16 * c;
-      if (t >= t0 && t <= t1 && t < kend) m = fmaxf(m, softcap(s[c], a.sc_att));
+      s[c] = softcap(s[c], a.sc_att);
+      keep[c] = s[c];
+      if (t >= t0 && t <= t1 && t < kend) m = fmaxf(m, s[c]);
     }
   }
 #pragma unroll
@@ -478,16 +483,23 @@ __global__ void __launch_bounds__(kPreThreads) k_attn_prefill(PrefillArgs a) {
 #pragma unroll
   for (int c = 0; c < HD / 64; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int k0 = kbeg; k0 < kend; k0 += kBK) {
-    __syncthreads();
-    load_tile<HD>(ks, S::KS, kh, k0, kend);
-    load_tile<HD>(vs, HD, vh, k0, kend);
-    __syncthreads();
     float s[4];
-    tile_scores<HD>(qs, ks, qi, kq, s);
+    if (one) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) s[c] = keep[c];
+    } else {
+      __syncthreads();
+      load_tile<HD>(ks, S::KS, kh, k0, kend);
+      load_tile<HD>(vs, HD, vh, k0, kend);
+      __syncthreads();
+      tile_scores<HD>(qs, ks, qi, kq, s);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) s[c] = softcap(s[c], a.sc_att);
+    }
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       const int t = k0 + kq + 16 * c;
-      const float p = (t >= t0 && t <= t1 && t < kend) ? dev_fast_expf(softcap(s[c], a.sc_att) - m) : 0.0f;
+      const float p = (t >= t0 && t <= t1 && t < kend) ? dev_fast_expf(s[c] - m) : 0.0f;
       ps[qi * kBK + kq + 16 * c] = p;
       l += p;
     }
@@ -677,8 +689,9 @@ GCU_EXPORT int gcu_dev_attention_prefill(float *xo, int xostr, const float *xq, 
   PrefillArgs a{xo, xostr, xq, k_cache, v_cache, kv_stride, n_heads, nkv, spos, ntok, slide, mask ? 1 : 0, sc_att,
                 1, 1, nullptr};
   // the causal triangle gives late query tiles many key tiles and early ones
-  // few: split every tile's key range into chunks of kpc key tiles (at most 8
-  // chunks), so the longest CTA does kpc tiles, not the whole range
+  // few: split every tile's key range into chunks of kpc key tiles (one tile
+  // per chunk up to 8 tiles, at most 8 chunks beyond), so the longest CTA
+  // does kpc tiles, not the whole range
   int max_tiles = 1;
   for (int i0 = 0; i0 < ntok; i0 += kBQ) {
     const int i1 = std::min(ntok, i0 + kBQ) - 1;
@@ -689,7 +702,7 @@ GCU_EXPORT int gcu_dev_attention_prefill(float *xo, int xostr, const float *xq, 
     }
     max_tiles = std::max(max_tiles, (hi + 1 - lo + kBK - 1) / kBK);
   }
-  a.kpc = std::max(2, (max_tiles + 7) / 8);
+  a.kpc = std::max(1, (max_tiles + 7) / 8);
   a.maxch = (max_tiles + a.kpc - 1) / a.kpc;
   if (a.maxch > 1) {
     void *ws;
