@@ -369,8 +369,7 @@ struct PreSmem {
   static constexpr int KS = HD + 4;  // padded K / Q row: conflict-free 16-byte reads
   static constexpr size_t q = 0;
   static constexpr size_t k = q + (size_t)kBQ * KS;
-  static constexpr size_t v = k + (size_t)kBK * KS;
-  static constexpr size_t p = v + (size_t)kBK * HD;
+  static constexpr size_t p = k + (size_t)kBK * KS;
   static constexpr size_t floats = p + (size_t)kBQ * kBK;
   static constexpr size_t bytes = floats * sizeof(float);
 };
@@ -424,10 +423,10 @@ __device__ __forceinline__ void tile_scores(const float *qs, const float *ks, in
 // row qi against keys kq + 16c of each tile and, in the value phase, owns
 // columns kq*4 + 64c of row qi.
 template <int HD>
-__global__ void __launch_bounds__(kPreThreads) k_attn_prefill(PrefillArgs a) {
+__global__ void __launch_bounds__(kPreThreads, 2) k_attn_prefill(PrefillArgs a) {
   extern __shared__ __align__(16) float smem[];
   using S = PreSmem<HD>;
-  float *qs = smem + S::q, *ks = smem + S::k, *vs = smem + S::v, *ps = smem + S::p;
+  float *qs = smem + S::q, *ks = smem + S::k, *ps = smem + S::p;
   ptx::griddep_launch();
   const int h = blockIdx.y, i0 = blockIdx.x * kBQ;
   const int nrows = min(kBQ, a.ntok - i0);
@@ -461,7 +460,6 @@ __global__ void __launch_bounds__(kPreThreads) k_attn_prefill(PrefillArgs a) {
   for (int k0 = kbeg; k0 < kend; k0 += kBK) {
     __syncthreads();  // the previous tile (and the Q tile's stores) are done
     load_tile<HD>(ks, S::KS, kh, k0, kend);
-    if (one) load_tile<HD>(vs, HD, vh, k0, kend);
     __syncthreads();
     float s[4];
     tile_scores<HD>(qs, ks, qi, kq, s);
@@ -490,7 +488,6 @@ __global__ void __launch_bounds__(kPreThreads) k_attn_prefill(PrefillArgs a) {
     } else {
       __syncthreads();
       load_tile<HD>(ks, S::KS, kh, k0, kend);
-      load_tile<HD>(vs, HD, vh, k0, kend);
       __syncthreads();
       tile_scores<HD>(qs, ks, qi, kq, s);
 #pragma unroll
@@ -506,12 +503,15 @@ __global__ void __launch_bounds__(kPreThreads) k_attn_prefill(PrefillArgs a) {
     __syncthreads();
     const int jn = min(kBK, kend - k0);
     const float *pr = ps + qi * kBK;
+    // V rows straight from L2 / L1: the 16 threads of a row read 256
+    // contiguous bytes, the two rows of a warp the same ones
+#pragma unroll 4
     for (int j = 0; j < jn; ++j) {
       const float p = pr[j];
-      const float *vr = vs + j * HD + kq * 4;
+      const float *vr = vh + (size_t)(k0 + j) * HD + kq * 4;
 #pragma unroll
       for (int c = 0; c < HD / 64; ++c) {
-        const float4 v = *reinterpret_cast<const float4 *>(vr + 64 * c);
+        const float4 v = __ldg(reinterpret_cast<const float4 *>(vr + 64 * c));
         acc[c].x += p * v.x;
         acc[c].y += p * v.y;
         acc[c].z += p * v.z;
