@@ -1014,6 +1014,8 @@ def run_attention(args):
     c = ATTN[args.workload]
     nh, nkv, hd = c["n_heads"], c["nkv"], c["hd"]
     lay = _attn_layers(c)
+    if args.layers > 0:  # profiling captures of a small case
+        lay = lay[:args.layers]
     gen = torch.Generator(device=dev).manual_seed(5)
     clen = c["pos"] + 1 if c["kind"] == "decode" else c["spos"] + c["ntok"]
     bufs = []
@@ -1094,7 +1096,9 @@ def run_attention(args):
            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "none",
            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "ours",
            "config": {"workload": f"{args.workload}: {c['title']}", "heads": nh, "kv_heads": nkv, "head_dim": hd,
-                      "inputs": "each layer its own K/V cache in HBM (no L2 reuse across layers)"},
+                      "inputs": "each layer its own K/V cache in HBM (no L2 reuse across layers)",
+                      **({"reduced": f"--layers {args.layers}: a profiling case, not the benchmark workload"}
+                         if args.layers > 0 else {})},
            "roofline": roof, "clocks": clk, "gpu_launches": launches * args.steps,
            "e2e": None, "e2e_note": "attention has no host-pointer entry point: it runs between device-resident "
                                   "matmuls"}
