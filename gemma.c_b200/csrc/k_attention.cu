@@ -101,22 +101,6 @@ __device__ __forceinline__ int gqa_head_of(int hk, int n_heads, int nkv) {
 constexpr int kDecThreads = 256;
 constexpr int kMaxChunk = 1024;  // window positions per CTA
 
-template <int PL>
-__device__ __forceinline__ void load_lane(float (&v)[PL], const float *p) {
-  if constexpr (PL == 8) {
-    const float4 a = __ldg(reinterpret_cast<const float4 *>(p));
-    const float4 b = __ldg(reinterpret_cast<const float4 *>(p + 4));
-    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-  } else if constexpr (PL == 4) {
-    const float4 a = __ldg(reinterpret_cast<const float4 *>(p));
-    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-  } else {
-    const float2 a = __ldg(reinterpret_cast<const float2 *>(p));
-    v[0] = a.x; v[1] = a.y;
-  }
-}
-
 // Cache tiles move by 1D bulk copies (positions of one kv head are
 // contiguous in the cache) through a ring of kStages shared-memory stages:
 // the K tiles of the CTA's slice, then its V tiles.  Thread 0 keeps kStages
@@ -126,26 +110,25 @@ __device__ __forceinline__ void load_lane(float (&v)[PL], const float *p) {
 constexpr int kTR = 16;     // cache rows per copy
 constexpr int kStages = 4;  // copies in flight per CTA
 
-template <int HD>
+template <int HD, int GM>
 struct DecSmem {
   static constexpr int C4 = HD / 4;            // float4 columns of a row
   static constexpr int R = kDecThreads / C4;   // row groups of the value phase
-  static constexpr size_t region = (size_t)kStages * kTR * HD > (size_t)R * kMaxGroup * HD
+  static constexpr size_t region = (size_t)kStages * kTR * HD > (size_t)R * GM * HD
                                        ? (size_t)kStages * kTR * HD
-                                       : (size_t)R * kMaxGroup * HD;
-  static size_t bytes(int chunk) { return (region + (size_t)kMaxGroup * chunk) * sizeof(float); }
+                                       : (size_t)R * GM * HD;
+  static size_t bytes(int chunk) { return (region + (size_t)GM * chunk) * sizeof(float); }
 };
 
 // smem: the stage ring (reused at the end for the row groups' partial sums),
-// then the scores / weights [kMaxGroup][chunk]
-template <int HD>
-__global__ void __launch_bounds__(kDecThreads) k_attn_decode(DecodeArgs a) {
+// then the scores / weights [GM][chunk]
+template <int HD, int GM>
+__global__ void __launch_bounds__(kDecThreads, GM <= 2 ? 3 : GM <= 4 ? 2 : 1) k_attn_decode(DecodeArgs a) {
   extern __shared__ __align__(128) float sm[];
   __shared__ __align__(8) uint64_t full[kStages];
-  __shared__ float red[kDecThreads / 32][kMaxGroup];
-  __shared__ float stat[2][kMaxGroup];  // row max, weight sum
-  using S = DecSmem<HD>;
-  constexpr int PL = HD / 32;
+  __shared__ float red[kDecThreads / 32][GM];
+  __shared__ float stat[2][GM];  // row max, weight sum
+  using S = DecSmem<HD, GM>;
   float *stage = sm, *sc = sm + S::region;
   ptx::griddep_launch();
   const int split = blockIdx.x, hk = blockIdx.y;
@@ -175,17 +158,26 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(DecodeArgs a) {
   if (threadIdx.x == 0)
     for (; issued < kStages && issued < nload; ++issued) issue(issued);
 
-  float q[kMaxGroup][PL];
+  // scores: each half warp takes one row of a tile (16 lanes x HD/64
+  // interleaved float4, conflict-free), two rows per warp at a time; a K row
+  // is read once for every query head of the group (att_scores_gqa's order
+  // of work)
+  constexpr int Q4 = HD / 64;  // float4 per lane of a row
+  const int half = lane >> 4, l16 = lane & 15;
+  float4 q[GM][Q4];
 #pragma unroll
-  for (int g = 0; g < kMaxGroup; ++g)
-    if (g < G) load_lane<PL>(q[g], a.xq + (size_t)(h0 + g) * HD + lane * PL);
-  float wmax[kMaxGroup];
+  for (int g = 0; g < GM; ++g)
 #pragma unroll
-  for (int g = 0; g < kMaxGroup; ++g) wmax[g] = -INFINITY;
+    for (int i = 0; i < Q4; ++i)
+      q[g][i] = g < G ? __ldg(reinterpret_cast<const float4 *>(a.xq + (size_t)(h0 + g) * HD) + i * 16 + l16)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+  float wmax[GM];
+#pragma unroll
+  for (int g = 0; g < GM; ++g) wmax[g] = -INFINITY;
   const int c = threadIdx.x % S::C4, r = threadIdx.x / S::C4;  // value phase: float4 column, row group
-  float4 acc[kMaxGroup];
+  float4 acc[GM];
 #pragma unroll
-  for (int g = 0; g < kMaxGroup; ++g) acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int g = 0; g < GM; ++g) acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
 
   int j = 0;
   for (; j < nload; ++j) {
@@ -199,34 +191,41 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(DecodeArgs a) {
     const int tile = j < nt ? j : j - nt;
     const int rows = min(kTR, n - tile * kTR);
     if (j < nt) {
-      // scores of this tile's rows: warp w takes rows w and w + 8; a row is
-      // read once for every query head of the group
 #pragma unroll
-      for (int rr = 0; rr < kTR / (kDecThreads / 32); ++rr) {
-        const int row = warp + rr * (kDecThreads / 32);
-        if (row < rows) {
-          float k[PL];
+      for (int rr = 0; rr < kTR / (kDecThreads / 16); ++rr) {
+        const int row = warp * 2 + half + rr * (kDecThreads / 16);
+        const bool live = row < rows;  // the shuffles below run on every lane
+        float4 k[Q4];
 #pragma unroll
-          for (int i = 0; i < PL; ++i) k[i] = tl[row * HD + lane * PL + i];
+        for (int i = 0; i < Q4; ++i)
+          k[i] = live ? reinterpret_cast<const float4 *>(tl + row * HD)[i * 16 + l16]
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-          for (int g = 0; g < kMaxGroup; ++g) {
-            if (g < G) {
-              float d = 0.0f;
+        for (int g = 0; g < GM; ++g) {
+          float d = 0.0f;
 #pragma unroll
-              for (int i = 0; i < PL; ++i) d += q[g][i] * k[i];
-              d = warp_sum(d);
-              const float s = softcap(d * a.asc, a.sc_att);  // att_finalize: *asc, then the cap
-              wmax[g] = fmaxf(wmax[g], s);
-              if (lane == 0) sc[g * a.chunk + tile * kTR + row] = s;
-            }
+          for (int i = 0; i < Q4; ++i) {
+            d += q[g][i].x * k[i].x;
+            d += q[g][i].y * k[i].y;
+            d += q[g][i].z * k[i].z;
+            d += q[g][i].w * k[i].w;
+          }
+#pragma unroll
+          for (int o = 8; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+          if (live && g < G) {
+            const float s = softcap(d * a.asc, a.sc_att);  // att_finalize: *asc, then the cap
+            wmax[g] = fmaxf(wmax[g], s);
+            if (l16 == 0) sc[g * a.chunk + tile * kTR + row] = s;
           }
         }
       }
       if (j == nt - 1) {
         // softmax weights fast_expf(s - max) (gemma.c:4094-4105) and sums
+#pragma unroll
+        for (int g = 0; g < GM; ++g) wmax[g] = fmaxf(wmax[g], __shfl_xor_sync(0xffffffffu, wmax[g], 16));
         if (lane == 0)
 #pragma unroll
-          for (int g = 0; g < kMaxGroup; ++g) red[warp][g] = wmax[g];
+          for (int g = 0; g < GM; ++g) red[warp][g] = wmax[g];
         __syncthreads();
         if (threadIdx.x < G) {
           float m = red[0][threadIdx.x];
@@ -258,7 +257,7 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(DecodeArgs a) {
         const float4 v = *reinterpret_cast<const float4 *>(tl + row * HD + c * 4);
         const int t = tile * kTR + row;
 #pragma unroll
-        for (int g = 0; g < kMaxGroup; ++g) {
+        for (int g = 0; g < GM; ++g) {
           if (g < G) {
             const float p = sc[g * a.chunk + t];
             acc[g].x += p * v.x;
@@ -280,18 +279,18 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(DecodeArgs a) {
   }
   // merge the row groups' sums in row-group order (the ring is free now)
   __syncthreads();
-  float *rs = sm;  // [R][kMaxGroup][HD]
+  float *rs = sm;  // [R][GM][HD]
 #pragma unroll
-  for (int g = 0; g < kMaxGroup; ++g)
-    if (g < G) *reinterpret_cast<float4 *>(rs + ((size_t)r * kMaxGroup + g) * HD + c * 4) = acc[g];
+  for (int g = 0; g < GM; ++g)
+    if (g < G) *reinterpret_cast<float4 *>(rs + ((size_t)r * GM + g) * HD + c * 4) = acc[g];
   __syncthreads();
   if (r != 0) return;
 #pragma unroll
-  for (int g = 0; g < kMaxGroup; ++g) {
+  for (int g = 0; g < GM; ++g) {
     if (g < G) {
       float4 s = *reinterpret_cast<const float4 *>(rs + (size_t)g * HD + c * 4);
       for (int rr = 1; rr < S::R; ++rr) {
-        const float4 u = *reinterpret_cast<const float4 *>(rs + ((size_t)rr * kMaxGroup + g) * HD + c * 4);
+        const float4 u = *reinterpret_cast<const float4 *>(rs + ((size_t)rr * GM + g) * HD + c * 4);
         s.x += u.x;
         s.y += u.y;
         s.z += u.z;
@@ -302,7 +301,7 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(DecodeArgs a) {
   }
   if (a.splits == 1) {
 #pragma unroll
-    for (int g = 0; g < kMaxGroup; ++g) {
+    for (int g = 0; g < GM; ++g) {
       if (g < G) {
         const float l = stat[1][g];
         *reinterpret_cast<float4 *>(a.xo + (size_t)(h0 + g) * HD + c * 4) =
@@ -315,7 +314,7 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(DecodeArgs a) {
   float *pm = a.part + (size_t)a.splits * a.n_heads * HD + (size_t)split * a.n_heads;
   float *pl = pm + (size_t)a.splits * a.n_heads;
 #pragma unroll
-  for (int g = 0; g < kMaxGroup; ++g) {
+  for (int g = 0; g < GM; ++g) {
     if (g < G) {
       *reinterpret_cast<float4 *>(po + (size_t)(h0 + g) * HD + c * 4) = acc[g];
       if (c == 0) {
@@ -576,9 +575,9 @@ __global__ void __launch_bounds__(HD / 4) k_attn_prefill_merge(PrefillArgs a) {
       make_float4(o.x / l, o.y / l, o.z / l, o.w / l);
 }
 
-template <int HD>
+template <int HD, int GM>
 cudaError_t launch_decode(const DecodeArgs &a, cudaStream_t st) {
-  const size_t smem = DecSmem<HD>::bytes(a.chunk);
+  const size_t smem = DecSmem<HD, GM>::bytes(a.chunk);
   static std::mutex mu;
   static unsigned long long done_mask = 0;
   {
@@ -587,13 +586,13 @@ cudaError_t launch_decode(const DecodeArgs &a, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     std::lock_guard<std::mutex> lk(mu);
     if (!(done_mask & (1ull << (dev & 63)))) {
-      e = cudaFuncSetAttribute(k_attn_decode<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)DecSmem<HD>::bytes(kMaxChunk));
+      e = cudaFuncSetAttribute(k_attn_decode<HD, GM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)DecSmem<HD, GM>::bytes(kMaxChunk));
       if (e != cudaSuccess) return e;
       done_mask |= 1ull << (dev & 63);
     }
   }
-  cudaError_t e = launch_k(k_attn_decode<HD>, dim3(a.splits, a.nkv), dim3(kDecThreads), smem, st, a);
+  cudaError_t e = launch_k(k_attn_decode<HD, GM>, dim3(a.splits, a.nkv), dim3(kDecThreads), smem, st, a);
   if (e != cudaSuccess || a.splits == 1) return e;
   return launch_k(k_attn_combine<HD>, dim3(a.n_heads), dim3(HD), 0, st, a.xo, (const float *)a.part, a.n_heads,
                   a.splits);
@@ -665,8 +664,17 @@ GCU_EXPORT int gcu_dev_attention_decode(float *xo, const float *xq, const float 
     if (gemm_workspace((size_t)a.splits * n_heads * (hdim + 2) * sizeof(float), &ws, &cnt, 0, st)) return 1;
     a.part = static_cast<float *>(ws);
   }
-  cudaError_t e = hdim == 256 ? launch_decode<256>(a, st) : hdim == 128 ? launch_decode<128>(a, st)
-                                                                        : launch_decode<64>(a, st);
+  // the group size as a compile-time bound: registers and score storage
+  const int gmax = (n_heads + nkv - 1) / nkv;
+  cudaError_t e;
+  if (gmax <= 1)
+    e = hdim == 256 ? launch_decode<256, 1>(a, st) : hdim == 128 ? launch_decode<128, 1>(a, st) : launch_decode<64, 1>(a, st);
+  else if (gmax <= 2)
+    e = hdim == 256 ? launch_decode<256, 2>(a, st) : hdim == 128 ? launch_decode<128, 2>(a, st) : launch_decode<64, 2>(a, st);
+  else if (gmax <= 4)
+    e = hdim == 256 ? launch_decode<256, 4>(a, st) : hdim == 128 ? launch_decode<128, 4>(a, st) : launch_decode<64, 4>(a, st);
+  else
+    e = hdim == 256 ? launch_decode<256, 8>(a, st) : hdim == 128 ? launch_decode<128, 8>(a, st) : launch_decode<64, 8>(a, st);
   GCU_CUDA(e);
   return 0;
 }
