@@ -58,7 +58,8 @@ def _ref():
 
 @pytest.mark.parametrize("nh,nkv,hd,clen,spos,attlen,sc", [(4, 1, 256, 700, 200, 300, 0.0),
                                                           (16, 8, 256, 1500, 0, 1500, 30.0),
-                                                          (6, 3, 64, 90, 17, 73, 0.0)])
+                                                          (6, 3, 64, 90, 17, 73, 0.0),
+                                                          (6, 4, 128, 300, 0, 300, 0.0)])  # uneven groups
 def test_oracle_decode_matches_live_reference(nh, nkv, hd, clen, spos, attlen, sc):
     R = _ref()
     if R is None:
@@ -71,7 +72,8 @@ def test_oracle_decode_matches_live_reference(nh, nkv, hd, clen, spos, attlen, s
 
 @pytest.mark.parametrize("nh,nkv,hd,spos,ntok,slide,sc,mask", [(4, 1, 256, 0, 150, 64, 0.0, True),
                                                                (8, 2, 128, 64, 96, 0, 20.0, True),
-                                                               (2, 1, 64, 30, 45, 16, 0.0, False)])
+                                                               (2, 1, 64, 30, 45, 16, 0.0, False),
+                                                               (6, 4, 64, 0, 70, 0, 0.0, True)])  # uneven
 def test_oracle_prefill_matches_live_reference(nh, nkv, hd, spos, ntok, slide, sc, mask):
     R = _ref()
     if R is None:

@@ -84,7 +84,7 @@ def test_prefill_matches_reference_fixture(case):
 @pytest.mark.parametrize("nh,nkv,hd,clen,spos,attlen,sc", [
     (4, 1, 256, 64, 0, 64, 0.0), (4, 1, 256, 65, 0, 65, 0.0), (4, 1, 256, 4096, 3000, 512, 0.0),
     (8, 4, 256, 8192, 0, 8192, 0.0), (16, 8, 256, 6000, 0, 6000, 50.0), (16, 8, 128, 777, 11, 700, 0.0),
-    (5, 1, 64, 3000, 0, 2999, 0.0)])
+    (5, 1, 64, 3000, 0, 2999, 0.0), (6, 4, 128, 2000, 0, 2000, 0.0)])  # last: uneven groups
 def test_decode_matches_oracle(nh, nkv, hd, clen, spos, attlen, sc):
     xq, kc, vc = synth.attention_inputs(300 + attlen, nh, nkv, hd, clen)
     asc = np.float32(1.0 / np.sqrt(hd))
@@ -97,7 +97,8 @@ def test_decode_matches_oracle(nh, nkv, hd, clen, spos, attlen, sc):
     (4, 1, 256, 600, 200, 512, 0.0, True),   # a later chunk on a sliding layer
     (8, 4, 256, 0, 300, 0, 0.0, True),       # 4B heads, global layer
     (8, 4, 128, 13, 77, 20, 30.0, True),
-    (2, 1, 64, 0, 100, 0, 0.0, False)])
+    (2, 1, 64, 0, 100, 0, 0.0, False),
+    (6, 4, 64, 0, 70, 0, 0.0, True)])      # uneven query-head groups
 def test_prefill_matches_oracle(nh, nkv, hd, spos, ntok, slide, sc, mask):
     xq, kc, vc = synth.attention_inputs(400 + ntok, nh, nkv, hd, spos + ntok, ntok)
     assert_attn_close(run_prefill(xq, kc, vc, spos, slide, sc, mask),
