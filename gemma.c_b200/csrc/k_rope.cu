@@ -1,0 +1,122 @@
+// k_rope.cu -- the steps between the Q/K/V matmuls and attention.
+//
+// gemma.c runs, per layer (decode gemma.c:4775-4818, prefill 5095-5145):
+//   - RMSNorm of every query and key head row (qk_norm models), weight nq / nk
+//     (x * rms * (w + 1), gemma.c:2509-2523);
+//   - RoPE (rope_apply, gemma.c:4223-4245): pairs (d, d + hdim/2) rotated by
+//     the position's (cos, sin) table entry d, the queries also scaled (1 at
+//     decode, the attention scale at prefill);
+//   - the chunk's rotated keys and its values copied into the KV cache.
+// One warp per head row.  The frequency table is an input: gemma.c builds it
+// on the host (rope_freqs, gemma.c:4178-4216, libm powf / cosf / sinf), and
+// the same table is used here.  Lane l holds elements [l*P, l*P + P) of a
+// row (P = hdim/32), so the partner of element d < hdim/2 sits in lane l ^ 16.
+#include "gcu_internal.cuh"
+
+#define GCU_EXPORT extern "C" __attribute__((visibility("default")))
+
+namespace gcu {
+namespace {
+
+constexpr int kRopeThreads = 256;
+
+struct RopeArgs {
+  float *xq;
+  const float *xk, *xv;
+  float *kc, *vc;
+  long kv_stride;
+  const float *nq, *nk;
+  float eps;
+  const float *freqs;
+  float q_scale;
+  int n_heads, nkv, spos, ntok;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(kRopeThreads) k_qk_norm_rope_cache(RopeArgs a) {
+  constexpr int P = HD / 32;
+  ptx::griddep_launch();
+  const int lane = threadIdx.x & 31;
+  const long row = (long)blockIdx.x * (kRopeThreads / 32) + (threadIdx.x >> 5);
+  const long nq_rows = (long)a.n_heads * a.ntok, nk_rows = (long)a.nkv * a.ntok;
+  if (row >= nq_rows + 2 * nk_rows) return;  // whole warp
+  ptx::griddep_wait();
+  if (row >= nq_rows + nk_rows) {  // a value row: straight into the cache
+    const long r = row - nq_rows - nk_rows;
+    const int h = (int)(r / a.ntok), t = (int)(r - (long)h * a.ntok);
+    const float *src = a.xv + r * HD + lane * P;
+    float *dst = a.vc + (size_t)h * a.kv_stride + (size_t)(a.spos + t) * HD + lane * P;
+#pragma unroll
+    for (int i = 0; i < P; i += 2)
+      *reinterpret_cast<float2 *>(dst + i) = __ldg(reinterpret_cast<const float2 *>(src + i));
+    return;
+  }
+  const bool isq = row < nq_rows;
+  const long r = isq ? row : row - nq_rows;
+  const int h = (int)(r / a.ntok), t = (int)(r - (long)h * a.ntok);
+  const float *src = (isq ? a.xq : a.xk) + r * HD + lane * P;
+  const float *w = isq ? a.nq : a.nk;
+  float v[P];
+#pragma unroll
+  for (int i = 0; i < P; i += 2) {
+    const float2 u = *reinterpret_cast<const float2 *>(src + i);
+    v[i] = u.x;
+    v[i + 1] = u.y;
+  }
+  if (w) {  // gemma.c:2513-2521
+    float sq = 0.0f;
+#pragma unroll
+    for (int i = 0; i < P; ++i) sq += v[i] * v[i];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    const float rms = 1.0f / sqrtf(sq / (float)HD + a.eps);
+#pragma unroll
+    for (int i = 0; i < P; ++i) v[i] = v[i] * rms * (__ldg(w + lane * P + i) + 1.0f);
+  }
+  // rope_apply: first-half lanes hold a (element d), second-half lanes b
+  // (element d + hdim/2); both use table entry d
+  const float scale = isq ? a.q_scale : 1.0f;
+  const float *fr = a.freqs + (size_t)t * HD + 2 * ((lane & 15) * P);
+  const bool first = lane < 16;
+#pragma unroll
+  for (int i = 0; i < P; ++i) {
+    const float other = __shfl_xor_sync(0xffffffffu, v[i], 16);
+    const float c = __ldg(fr + 2 * i), s = __ldg(fr + 2 * i + 1);
+    const float aa = first ? v[i] : other, bb = first ? other : v[i];
+    v[i] = first ? (aa * c - bb * s) * scale : (aa * s + bb * c) * scale;
+  }
+  float *dst = isq ? a.xq + r * HD + lane * P
+                   : a.kc + (size_t)h * a.kv_stride + (size_t)(a.spos + t) * HD + lane * P;
+#pragma unroll
+  for (int i = 0; i < P; i += 2) *reinterpret_cast<float2 *>(dst + i) = make_float2(v[i], v[i + 1]);
+}
+
+}  // namespace
+}  // namespace gcu
+
+using namespace gcu;
+
+GCU_EXPORT int gcu_dev_qk_norm_rope_cache(float *xq, const float *xk, const float *xv, float *k_cache,
+                                          float *v_cache, long kv_stride, const float *nq, const float *nk,
+                                          float eps, const float *freqs, float q_scale, int n_heads, int nkv,
+                                          int hdim, int spos, int ntok, void *stream) {
+  if (ntok == 0) return 0;
+  if (!xq || !xk || !xv || !k_cache || !v_cache || !freqs) return set_error("qk_norm_rope_cache: null pointer");
+  if (hdim != 64 && hdim != 128 && hdim != 256)
+    return set_error("qk_norm_rope_cache: head size %d (64, 128 or 256 supported)", hdim);
+  if (n_heads < 1 || nkv < 1 || ntok < 0 || spos < 0 || kv_stride < (long)(spos + ntok) * hdim || kv_stride % 2)
+    return set_error("qk_norm_rope_cache: chunk [%d, %d) outside a cache of %ld floats per head", spos, spos + ntok,
+                     kv_stride);
+  const void *ptrs[] = {xq, xk, xv, k_cache, v_cache};
+  for (const void *p : ptrs)
+    if ((uintptr_t)p % 8) return set_error("qk_norm_rope_cache: buffers must be 8-byte aligned");
+  RopeArgs a{xq, xk, xv, k_cache, v_cache, kv_stride, nq, nk, eps, freqs, q_scale, n_heads, nkv, spos, ntok};
+  const long rows = (long)(n_heads + 2 * nkv) * ntok;
+  const dim3 grid((unsigned)((rows + kRopeThreads / 32 - 1) / (kRopeThreads / 32)));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = hdim == 256 ? launch_k(k_qk_norm_rope_cache<256>, grid, dim3(kRopeThreads), 0, st, a)
+                  : hdim == 128 ? launch_k(k_qk_norm_rope_cache<128>, grid, dim3(kRopeThreads), 0, st, a)
+                                : launch_k(k_qk_norm_rope_cache<64>, grid, dim3(kRopeThreads), 0, st, a);
+  GCU_CUDA(e);
+  return 0;
+}

@@ -85,6 +85,8 @@ SIGNATURES = {
                                         ctypes.c_float, ctypes.c_float, _vp]),
     "gcu_dev_attention_prefill": (_int, [_vp, _int, _vp, _vp, _vp, ctypes.c_long, _int, _int, _int, _int, _int,
                                          _int, ctypes.c_float, _int, _vp]),
+    "gcu_dev_qk_norm_rope_cache": (_int, [_vp, _vp, _vp, _vp, _vp, ctypes.c_long, _vp, _vp, ctypes.c_float, _vp,
+                                          ctypes.c_float, _int, _int, _int, _int, _int, _vp]),
     "gcu_dev_patch_embed": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _int, _vp]),
     "gcu_dev_vision_pool_quantize": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_float, _int, _int, _int,
                                             _vp]),
@@ -441,3 +443,17 @@ def dev_vision_pool_quantize(q, s, x, post_n, post_nb, norm, eps, ppi, side, dim
     _check(lib().gcu_dev_vision_pool_quantize(q.data_ptr(), s.data_ptr(), out.data_ptr() if out is not None else None,
                                               x.data_ptr(), post_n.data_ptr(), post_nb.data_ptr(), norm.data_ptr(),
                                               eps, ppi, side, dim, _stream(stream)), "dev_vision_pool_quantize")
+
+
+def dev_qk_norm_rope_cache(xq, xk, xv, kc, vc, freqs, spos, q_scale=1.0, nq=None, nk=None, eps=1e-6, stream=None):
+    """gemma.c:4775-4818 / 5095-5145 on CUDA tensors: xq (n_heads, ntok, hdim)
+    rotated in place; xk, xv (nkv, ntok, hdim) normed/rotated keys and the
+    values written into kc, vc (nkv, clen, hdim) at [spos, spos+ntok);
+    freqs (ntok, hdim)."""
+    n_heads, ntok, hdim = xq.shape
+    nkv, clen, _ = kc.shape
+    _check(lib().gcu_dev_qk_norm_rope_cache(xq.data_ptr(), xk.data_ptr(), xv.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+                                            clen * hdim, nq.data_ptr() if nq is not None else None,
+                                            nk.data_ptr() if nk is not None else None, eps, freqs.data_ptr(),
+                                            q_scale, n_heads, nkv, hdim, spos, ntok, _stream(stream)),
+           "dev_qk_norm_rope_cache")

@@ -77,6 +77,20 @@ def attention_inputs(tensor_id: int, n_heads: int, nkv: int, hdim: int, clen: in
     return xq, kc, vc
 
 
+def rope_inputs(tensor_id: int, n_heads: int, nkv: int, hdim: int, clen: int, ntok: int, qk_norm: bool):
+    """Seeded operands of the QK-norm / RoPE / KV-cache step: head rows xq
+    (n_heads, ntok, hdim), xk and xv (nkv, ntok, hdim) of N(0, 1), caches
+    (nkv, clen, hdim), and when qk_norm the norm weights N(0, 0.1^2)."""
+    xq = normal(tensor_id, (n_heads, ntok, hdim))
+    xk = normal(tensor_id + 1, (nkv, ntok, hdim))
+    xv = normal(tensor_id + 2, (nkv, ntok, hdim))
+    kc = normal(tensor_id + 3, (nkv, clen, hdim))
+    vc = normal(tensor_id + 4, (nkv, clen, hdim))
+    nq = normal(tensor_id + 5, (hdim,), 0.1) if qk_norm else None
+    nk = normal(tensor_id + 6, (hdim,), 0.1) if qk_norm else None
+    return xq, xk, xv, kc, vc, nq, nk
+
+
 def vision_head_inputs(tensor_id: int, img_px: int, psize: int, dim: int, img_tok: int, tdim: int):
     """Seeded operands of the SigLIP head (gemma.c:4411-4716): an
     (img_px, img_px, 3) image of N(0, 0.5^2) pixels, patch-embedding weights

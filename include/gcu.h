@@ -229,6 +229,19 @@ int gcu_dev_geglu_quantize(int8_t *q, float *s, float *out, const float *gate, c
  * gemma.c's fast_expf softmax; results agree with the reference to fp32
  * reassociation (the reference's dot products are vectorized). */
 
+/* gemma.c:4775-4818 (decode, ntok = 1) and 5095-5145 (prefill): the steps
+ * between the Q/K/V matmuls and attention.  Per-head RMSNorm of the query and
+ * key rows (weights nq / nk; NULL = the model has no qk_norm), RoPE with
+ * freqs, the position's (cos, sin) table [ntok][hdim] exactly as gemma.c's
+ * rope_freqs builds it for the layer kind, queries also scaled by q_scale (1
+ * at decode, the attention scale at prefill), then the chunk's rotated keys
+ * and its values written to the cache at [spos, spos+ntok).  xq
+ * [n_heads][ntok][hdim] is rotated in place; xk, xv [nkv][ntok][hdim] are
+ * only read.  8-byte aligned buffers. */
+int gcu_dev_qk_norm_rope_cache(float *xq, const float *xk, const float *xv, float *k_cache,
+                               float *v_cache, long kv_stride, const float *nq, const float *nk,
+                               float eps, const float *freqs, float q_scale, int n_heads, int nkv,
+                               int hdim, int spos, int ntok, void *stream);
 /* gemma.c:4836-4848 (att_scores_gqa, att_finalize, att_values_gqa): one
  * decode step of one layer.  xq [n_heads][hdim] (normed and rotated), the
  * window [spos, spos+attlen) of the cache, scores scaled by asc

@@ -404,3 +404,49 @@ void orc_vision_pool(int8_t *q, float *s, float *out, const float *x, const floa
     }
   }
 }
+
+/* ---- between the Q/K/V matmuls and attention ------------------------------- */
+
+/* gemma.c:2509-2523 rmsnorm of one row in place: x * rms * (w + 1). */
+static void orc_rmsnorm_row(float *x, const float *w, int n, float eps) {
+  float sq = 0.0f;
+  for (int i = 0; i < n; i++) sq += x[i] * x[i];
+  const float rms = 1.0f / sqrtf(sq / (float)n + eps);
+  for (int i = 0; i < n; i++) x[i] = x[i] * rms * (w[i] + 1.0f);
+}
+
+/* gemma.c:4223-4245 rope_apply on one vector: pairs (d, d + hdim/2) rotated
+ * by the table's (cos, sin) for d, times scale. */
+static void orc_rope_row(float *x, const float *fr, int hdim, float scale) {
+  for (int d = 0; d < hdim / 2; d++) {
+    const float c = fr[2 * d], s = fr[2 * d + 1];
+    const float a = x[d], b = x[d + hdim / 2];
+    x[d] = (a * c - b * s) * scale;
+    x[d + hdim / 2] = (a * s + b * c) * scale;
+  }
+}
+
+/* QK RMSNorm (when nq / nk are given), RoPE (q scaled by q_scale) and the
+ * K/V cache writes of a chunk of ntok tokens at [spos, spos+ntok), as
+ * gemma.c:4775-4818 (decode) and 5095-5145 (prefill) run them.  xq
+ * [n_heads][ntok][hdim] rotated in place; xk [nkv][ntok][hdim] normed and
+ * rotated in place (then copied to the cache); freqs [ntok][hdim]. */
+void orc_qk_norm_rope_cache(float *xq, float *xk, const float *xv, float *kc, float *vc, long kv_stride,
+                            const float *nq, const float *nk, float eps, const float *freqs, float q_scale,
+                            int n_heads, int nkv, int hdim, int spos, int ntok) {
+  for (int h = 0; h < n_heads; h++)
+    for (int t = 0; t < ntok; t++) {
+      float *row = xq + ((size_t)h * ntok + t) * hdim;
+      if (nq) orc_rmsnorm_row(row, nq, hdim, eps);
+      orc_rope_row(row, freqs + (size_t)t * hdim, hdim, q_scale);
+    }
+  for (int h = 0; h < nkv; h++)
+    for (int t = 0; t < ntok; t++) {
+      float *row = xk + ((size_t)h * ntok + t) * hdim;
+      if (nk) orc_rmsnorm_row(row, nk, hdim, eps);
+      orc_rope_row(row, freqs + (size_t)t * hdim, hdim, 1.0f);
+      memcpy(kc + (size_t)h * kv_stride + (size_t)(spos + t) * hdim, row, (size_t)hdim * sizeof(float));
+      memcpy(vc + (size_t)h * kv_stride + (size_t)(spos + t) * hdim, xv + ((size_t)h * ntok + t) * hdim,
+             (size_t)hdim * sizeof(float));
+    }
+}

@@ -90,6 +90,9 @@ def orc() -> ctypes.CDLL:
         lib.orc_attention_prefill.restype = None
         lib.orc_attention_prefill.argtypes = [_f32p, ctypes.c_int, _f32p, _f32p, _f32p, ctypes.c_long] + \
             [ctypes.c_int] * 6 + [ctypes.c_float, ctypes.c_int, _f32p]
+        lib.orc_qk_norm_rope_cache.restype = None
+        lib.orc_qk_norm_rope_cache.argtypes = [_f32p, _f32p, _f32p, _f32p, _f32p, ctypes.c_long, _f32p, _f32p,
+                                               ctypes.c_float, _f32p, ctypes.c_float] + [ctypes.c_int] * 5
         lib.orc_patch_embed.restype = None
         lib.orc_patch_embed.argtypes = [_f32p, _f32p, _f32p, _f32p, _i8p, _f32p, ctypes.c_int, ctypes.c_int,
                                         ctypes.c_int]
@@ -243,6 +246,25 @@ def attention_prefill(xq, kc, vc, spos, slide=0, sc_att=0.0, mask=True):
     return xo
 
 
+def qk_norm_rope_cache(xq, xk, xv, kc, vc, freqs, spos, q_scale=1.0, nq=None, nk=None, eps=1e-6):
+    """gemma.c:4775-4818 / 5095-5145: returns (rotated xq, k cache, v cache)
+    after writing the chunk at [spos, spos+ntok); inputs are not modified."""
+    xq = np.array(xq, np.float32, copy=True)
+    xk = np.array(xk, np.float32, copy=True)
+    xv = np.ascontiguousarray(xv, np.float32)
+    kc = np.array(kc, np.float32, copy=True)
+    vc = np.array(vc, np.float32, copy=True)
+    freqs = np.ascontiguousarray(freqs, np.float32)
+    n_heads, ntok, hdim = xq.shape
+    nq = None if nq is None else np.ascontiguousarray(nq, np.float32)
+    nk = None if nk is None else np.ascontiguousarray(nk, np.float32)
+    orc().orc_qk_norm_rope_cache(_ptr(xq, _f32p), _ptr(xk, _f32p), _ptr(xv, _f32p), _ptr(kc, _f32p), _ptr(vc, _f32p),
+                                 kc.shape[1] * hdim, _ptr(nq, _f32p) if nq is not None else None,
+                                 _ptr(nk, _f32p) if nk is not None else None, eps, _ptr(freqs, _f32p), q_scale,
+                                 n_heads, kc.shape[0], hdim, spos, ntok)
+    return xq, kc, vc
+
+
 def patch_embed(v: dict):
     """gemma.c:4411-4466 on synth.vision_head_inputs: (npatch, dim) fp32."""
     ppi = v["img_px"] // v["psize"]
@@ -340,6 +362,13 @@ def ref(variant: str | None = None) -> ctypes.CDLL | None:
         lib.ref_vision_head.restype = ctypes.c_int
         lib.ref_vision_head.argtypes = [_f32p, _f32p, _i8p, _f32p, _f32p] + [ctypes.c_int] * 5 + \
             [ctypes.c_float, _f32p, _f32p, _i8p, _f32p, _f32p, _f32p, _f32p, _i8p, _f32p, ctypes.c_int]
+    if hasattr(lib, "ref_qk_norm_rope_cache"):
+        lib.ref_rope_freqs.restype = None
+        lib.ref_rope_freqs.argtypes = [_f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_float,
+                                       ctypes.c_int, ctypes.c_int]
+        lib.ref_qk_norm_rope_cache.restype = None
+        lib.ref_qk_norm_rope_cache.argtypes = [_f32p, _f32p, _f32p, _f32p, _f32p, ctypes.c_long, _f32p, _f32p,
+                                               ctypes.c_float, _f32p, ctypes.c_float] + [ctypes.c_int] * 5
     if hasattr(lib, "ref_read_model_seconds"):
         lib.ref_read_model_seconds.restype = ctypes.c_double
         lib.ref_read_model_seconds.argtypes = [ctypes.c_char_p, ctypes.c_int]
@@ -424,6 +453,31 @@ class Ref:
                                           sc_att, int(mask), _ptr(att, _f32p), self.threads):
             raise RuntimeError("reference attention_prefill failed")
         return xo
+
+    def rope_freqs(self, hdim, theta_l, theta_g, pos, n):
+        """gemma.c's rope_freqs: (sliding, full) tables, (n, hdim) each."""
+        slid = np.empty((n, hdim), np.float32)
+        full = np.empty((n, hdim), np.float32)
+        self.lib.ref_rope_freqs(_ptr(slid, _f32p), _ptr(full, _f32p), hdim, hdim, theta_l, theta_g, pos, n)
+        return slid, full
+
+    def qk_norm_rope_cache(self, xq, xk, xv, kc, vc, freqs, spos, q_scale=1.0, nq=None, nk=None, eps=1e-6):
+        """The reference's rmsnorm / rope_apply / cache copies on the same
+        arguments as oracle.qk_norm_rope_cache."""
+        xq = np.array(xq, np.float32, copy=True)
+        xk = np.array(xk, np.float32, copy=True)
+        xv = np.ascontiguousarray(xv, np.float32)
+        kc = np.array(kc, np.float32, copy=True)
+        vc = np.array(vc, np.float32, copy=True)
+        freqs = np.ascontiguousarray(freqs, np.float32)
+        n_heads, ntok, hdim = xq.shape
+        nq = None if nq is None else np.ascontiguousarray(nq, np.float32)
+        nk = None if nk is None else np.ascontiguousarray(nk, np.float32)
+        self.lib.ref_qk_norm_rope_cache(_ptr(xq, _f32p), _ptr(xk, _f32p), _ptr(xv, _f32p), _ptr(kc, _f32p),
+                                        _ptr(vc, _f32p), kc.shape[1] * hdim, _ptr(nq, _f32p) if nq is not None else None,
+                                        _ptr(nk, _f32p) if nk is not None else None, eps, _ptr(freqs, _f32p), q_scale,
+                                        n_heads, kc.shape[0], hdim, spos, ntok)
+        return xq, kc, vc
 
     def vision_head(self, v: dict):
         """gemma.c's forward_vision with no encoder layers on

@@ -312,3 +312,41 @@ int ref_vision_head(float *out, float *pooled, int8_t *q, float *s, const float 
   free(vb.xsc);
   return rc;
 }
+
+/* gemma.c:4198-4216 rope_freqs: the cos/sin tables (hdim floats per
+ * position, `stride` apart) for n positions from pos, sliding and full. */
+void ref_rope_freqs(float *slid, float *full, int hdim, int stride, float theta_l, float theta_g, int pos, int n) {
+  rope_freqs(slid, full, hdim, stride, theta_l, theta_g, pos, n, 1, NULL);
+}
+
+/* The steps between the Q/K/V matmuls and attention, as the call sites run
+ * them: per-head QK RMSNorm (gemma.c:4778-4790 decode, 5095-5113 prefill;
+ * skipped when nq / nk are NULL), rope_apply on q (scaled by q_scale: 1 at
+ * decode, the attention scale at prefill, gemma.c:4796-4797, 5121-5133) and
+ * on k, then the K/V cache writes (gemma.c:4806-4818, 5136-5145).  xq
+ * [n_heads][ntok][hdim] and xk [nkv][ntok][hdim] are changed in place, as in
+ * gemma.c; freqs is one table block per position (stride hdim). */
+void ref_qk_norm_rope_cache(float *xq, float *xk, const float *xv, float *kc, float *vc, long kv_stride,
+                            const float *nq, const float *nk, float eps, const float *freqs, float q_scale,
+                            int n_heads, int nkv, int hdim, int spos, int ntok) {
+  if (nq)
+    for (int h = 0; h < n_heads; h++)
+      for (int t = 0; t < ntok; t++) {
+        float *row = xq + ((size_t)h * ntok + t) * hdim;
+        rmsnorm(row, row, nq, hdim, eps, NULL);
+      }
+  if (nk)
+    for (int h = 0; h < nkv; h++)
+      for (int t = 0; t < ntok; t++) {
+        float *row = xk + ((size_t)h * ntok + t) * hdim;
+        rmsnorm(row, row, nk, hdim, eps, NULL);
+      }
+  for (int h = 0; h < n_heads; h++) rope_apply(xq + (size_t)h * ntok * hdim, ntok, hdim, freqs, hdim, q_scale, NULL);
+  for (int h = 0; h < nkv; h++) rope_apply(xk + (size_t)h * ntok * hdim, ntok, hdim, freqs, hdim, 1.0f, NULL);
+  for (int h = 0; h < nkv; h++) {
+    memcpy(kc + (size_t)h * kv_stride + (size_t)spos * hdim, xk + (size_t)h * ntok * hdim,
+           (size_t)ntok * hdim * sizeof(float));
+    memcpy(vc + (size_t)h * kv_stride + (size_t)spos * hdim, xv + (size_t)h * ntok * hdim,
+           (size_t)ntok * hdim * sizeof(float));
+  }
+}

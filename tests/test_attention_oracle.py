@@ -89,3 +89,29 @@ def test_oracle_single_position_returns_the_value_row():
     got = O.attention_decode(xq, kc, vc, 6, 1, np.float32(0.125))
     want = np.repeat(vc[:, 6, :], 2, axis=0)
     assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("case", META.get("rope", []), ids=lambda c: f"rope{c[0]}")
+def test_oracle_rope_matches_reference_fixture(case):
+    # QK norm + RoPE + cache write (gemma.c:4775-4818, 5095-5145) on the
+    # reference's own rope_freqs table
+    tid, nh, nkv, hd, clen, spos, ntok, qs, norm, _, _ = case
+    xq, xk, xv, kc, vc, nq, nk = synth.rope_inputs(tid, nh, nkv, hd, clen, ntok, norm)
+    gq, gk, gv = O.qk_norm_rope_cache(xq, xk, xv, kc, vc, GOLD[f"rope_{tid}_freqs"], spos, qs, nq, nk)
+    assert_attn_close(gq, GOLD[f"rope_{tid}_xq"])
+    assert_attn_close(gk[:, spos:spos + ntok], GOLD[f"rope_{tid}_k"])
+    assert np.array_equal(gv[:, spos:spos + ntok], xv)  # values are copied
+    assert np.array_equal(gk[:, :spos], kc[:, :spos]) and np.array_equal(gk[:, spos + ntok:], kc[:, spos + ntok:])
+
+
+def test_oracle_rope_matches_live_reference():
+    R = _ref()
+    if R is None or not hasattr(R.lib, "ref_qk_norm_rope_cache"):
+        pytest.skip("reference build not available")
+    slid, full = R.rope_freqs(128, 10000.0, 1e6, 700, 33)
+    xq, xk, xv, kc, vc, nq, nk = synth.rope_inputs(340, 6, 2, 128, 800, 33, True)
+    for fr in (slid, full):
+        a = O.qk_norm_rope_cache(xq, xk, xv, kc, vc, fr, 700, 0.088, nq, nk)
+        b = R.qk_norm_rope_cache(xq, xk, xv, kc, vc, fr, 700, 0.088, nq, nk)
+        for x, y in zip(a, b):
+            assert_attn_close(x, y)

@@ -151,3 +151,58 @@ def test_rejections():
     with pytest.raises(gcu.GcuError, match="outside a cache"):
         gcu.dev_attention_prefill(torch.empty((8, 128), device="cuda"), xqp, kcp, vcp, 4)
     gcu.check_device()
+
+
+def run_rope(xq, xk, xv, kc, vc, freqs, spos, qs, nq, nk):
+    q, k, v = dev(xq), dev(xk), dev(xv)
+    kcd, vcd = dev(kc), dev(vc)
+    gcu.dev_qk_norm_rope_cache(q, k, v, kcd, vcd, dev(freqs), spos, qs, None if nq is None else dev(nq),
+                               None if nk is None else dev(nk))
+    torch.cuda.synchronize()
+    return q.cpu().numpy(), kcd.cpu().numpy(), vcd.cpu().numpy(), k.cpu().numpy()
+
+
+@pytest.mark.parametrize("case", META.get("rope", []), ids=lambda c: f"rope{c[0]}")
+def test_rope_matches_reference_fixture(case):
+    tid, nh, nkv, hd, clen, spos, ntok, qs, norm, _, _ = case
+    xq, xk, xv, kc, vc, nq, nk = synth.rope_inputs(tid, nh, nkv, hd, clen, ntok, norm)
+    gq, gk, gv, k_after = run_rope(xq, xk, xv, kc, vc, GOLD[f"rope_{tid}_freqs"], spos, qs, nq, nk)
+    assert_attn_close(gq, GOLD[f"rope_{tid}_xq"])
+    assert_attn_close(gk[:, spos:spos + ntok], GOLD[f"rope_{tid}_k"])
+    assert np.array_equal(gv[:, spos:spos + ntok], xv)
+    assert np.array_equal(gk[:, :spos], kc[:, :spos]) and np.array_equal(gk[:, spos + ntok:], kc[:, spos + ntok:])
+    assert np.array_equal(k_after, xk)  # the keys are read, not changed
+
+
+@pytest.mark.parametrize("nh,nkv,hd,clen,spos,ntok,qs,norm", [
+    (16, 8, 256, 4096, 4000, 1, 1.0, True),     # 12B decode step
+    (4, 1, 256, 512, 0, 512, 0.0625, True),     # 1B prefill chunk
+    (8, 4, 128, 300, 37, 200, 0.088, False),
+    (3, 3, 64, 100, 99, 1, 1.0, True)])
+def test_rope_matches_oracle(nh, nkv, hd, clen, spos, ntok, qs, norm):
+    xq, xk, xv, kc, vc, nq, nk = synth.rope_inputs(800 + ntok, nh, nkv, hd, clen, ntok, norm)
+    pos = np.arange(spos, spos + ntok, dtype=np.float64)[:, None]
+    inv = 10000.0 ** (-np.arange(0, hd, 2, dtype=np.float64) / hd)
+    freqs = np.empty((ntok, hd), np.float32)
+    freqs[:, 0::2] = np.cos(pos * inv)
+    freqs[:, 1::2] = np.sin(pos * inv)
+    got = run_rope(xq, xk, xv, kc, vc, freqs, spos, qs, nq, nk)
+    want = O.qk_norm_rope_cache(xq, xk, xv, kc, vc, freqs, spos, qs, nq, nk)
+    for g, w in zip(got[:3], want):
+        assert_attn_close(g, w)
+
+
+def test_rope_then_decode_attention_matches_oracle_chain():
+    # QK norm + RoPE + cache write, then the decode attention over the cache
+    nh, nkv, hd, clen, spos = 8, 4, 256, 2048, 2047
+    xq, xk, xv, kc, vc, nq, nk = synth.rope_inputs(900, nh, nkv, hd, clen, 1, True)
+    freqs = np.tile(np.float32([1.0, 0.0]), (1, hd // 2))  # position 0 angles: the identity rotation
+    q, k, v = dev(xq), dev(xk), dev(xv)
+    kcd, vcd = dev(kc), dev(vc)
+    gcu.dev_qk_norm_rope_cache(q, k, v, kcd, vcd, dev(freqs), spos, 1.0, dev(nq), dev(nk))
+    xo = torch.empty((nh, hd), device="cuda")
+    gcu.dev_attention_decode(xo, q[:, 0, :].contiguous(), kcd, vcd, 0, clen, 1.0 / 16)
+    torch.cuda.synchronize()
+    oq, okc, ovc = O.qk_norm_rope_cache(xq, xk, xv, kc, vc, freqs, spos, 1.0, nq, nk)
+    want = O.attention_decode(oq[:, 0, :], okc, ovc, 0, clen, np.float32(1.0 / 16))
+    assert_attn_close(xo.cpu().numpy(), want)
