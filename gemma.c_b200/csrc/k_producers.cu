@@ -23,6 +23,8 @@
 // warp path: WPR warps per row, 8/WPR rows per 256-thread CTA.
 #include "gcu_internal.cuh"
 
+#include <algorithm>
+
 #define GCU_EXPORT extern "C" __attribute__((visibility("default")))
 
 namespace gcu {
@@ -193,4 +195,93 @@ GCU_EXPORT int gcu_dev_geglu_quantize(int8_t *q, float *s, float *h, const float
                                       const float *up, int m, int dim, void *stream) {
   return launch_producer<GEGLU>(q, s, h, gate, up, 0.0f, dim, m, dim, static_cast<cudaStream_t>(stream),
                                 "geglu_quantize");
+}
+
+// ---------------------------------------------------------------------------
+// residual stream: x = clamp(resid + rmsnorm(y)), and the logit softcap
+// ---------------------------------------------------------------------------
+namespace gcu {
+namespace {
+
+// gemma.c:4862-4881 (attention) and 4950-4962 (feedforward): the block's
+// output y, RMSNorm'd with w when the model has post-norms (NULL: as is),
+// added to the residual and clamped to the floatx range.  x may alias resid.
+// One CTA of 256 threads per row, float4 columns, NC per thread.
+template <int NC>
+__global__ void __launch_bounds__(256) k_rmsnorm_residual(float *x, const float *__restrict__ y, const float *resid,
+                                                          const float *__restrict__ w, float eps, int dim) {
+  __shared__ float red[8];
+  ptx::griddep_launch();
+  const size_t row = blockIdx.x;
+  const int d4 = dim >> 2, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  ptx::griddep_wait();
+  float4 v[NC];
+  float sq = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    const int c = threadIdx.x + i * 256;
+    v[i] = c < d4 ? __ldg(reinterpret_cast<const float4 *>(y + row * dim) + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    sq += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+  }
+  float rms = 1.0f;
+  if (w) {  // gemma.c:2513-2521
+    sq = row_reduce<8, false>(sq, red, warp, 0, lane);
+    rms = 1.0f / sqrtf(sq / (float)dim + eps);
+  }
+  const float m = 3.402823466e38f;  // FLT_MAX: clamp_fpx, gemma.c:2504-2506
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    const int c = threadIdx.x + i * 256;
+    if (c >= d4) continue;
+    float4 a = v[i];
+    if (w) {
+      const float4 g = __ldg(reinterpret_cast<const float4 *>(w) + c);
+      a = make_float4(a.x * rms * (g.x + 1.0f), a.y * rms * (g.y + 1.0f), a.z * rms * (g.z + 1.0f),
+                      a.w * rms * (g.w + 1.0f));
+    }
+    const float4 r = reinterpret_cast<const float4 *>(resid + row * dim)[c];
+    reinterpret_cast<float4 *>(x + row * dim)[c] =
+        make_float4(fminf(m, fmaxf(-m, a.x + r.x)), fminf(m, fmaxf(-m, a.y + r.y)), fminf(m, fmaxf(-m, a.z + r.z)),
+                    fminf(m, fmaxf(-m, a.w + r.w)));
+  }
+}
+
+// gemma.c:4971-4976: logits = tanh(logits / cap) * cap
+__global__ void k_softcap(float *x, long n, float cap) {
+  ptx::griddep_launch();
+  ptx::griddep_wait();
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+    x[i] = tanhf(x[i] / cap) * cap;
+}
+
+}  // namespace
+}  // namespace gcu
+
+GCU_EXPORT int gcu_dev_rmsnorm_residual(float *x, const float *y, const float *resid, const float *weight, float eps,
+                                        int m, int dim, void *stream) {
+  if (m <= 0) return 0;
+  if (!x || !y || !resid) return set_error("rmsnorm_residual: null pointer");
+  if (dim <= 0 || dim % 4 || dim > 4 * 256 * 4)
+    return set_error("rmsnorm_residual: row length %d must be a positive multiple of 4 up to 4096", dim);
+  if ((uintptr_t)x % 16 || (uintptr_t)y % 16 || (uintptr_t)resid % 16 || (weight && (uintptr_t)weight % 16))
+    return set_error("rmsnorm_residual: rows must be 16-byte aligned");
+  const int nc = (dim / 4 + 255) / 256;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  switch (nc) {
+    case 1: e = launch_k(k_rmsnorm_residual<1>, m, 256, 0, st, x, y, resid, weight, eps, dim); break;
+    case 2: e = launch_k(k_rmsnorm_residual<2>, m, 256, 0, st, x, y, resid, weight, eps, dim); break;
+    case 3: e = launch_k(k_rmsnorm_residual<3>, m, 256, 0, st, x, y, resid, weight, eps, dim); break;
+    default: e = launch_k(k_rmsnorm_residual<4>, m, 256, 0, st, x, y, resid, weight, eps, dim); break;
+  }
+  GCU_CUDA(e);
+  return 0;
+}
+
+GCU_EXPORT int gcu_dev_softcap(float *x, long n, float cap, void *stream) {
+  if (n <= 0) return 0;
+  if (!x || cap == 0.0f) return set_error("softcap: null pointer or zero cap");
+  const int grid = (int)std::min<long>((n + 255) / 256, 4L * num_sms());
+  GCU_CUDA(launch_k(k_softcap, grid, 256, 0, static_cast<cudaStream_t>(stream), x, n, cap));
+  return 0;
 }

@@ -1,0 +1,158 @@
+"""decode.py -- a device-resident W8A8 decode step through libgcu.so.
+
+`Decoder.step` runs gemma.c's forward_text_decode (gemma.c:4727-4978) for one
+token with every activation, weight and the KV cache in GPU memory, one C-ABI
+call per step of the reference:
+
+    per layer (gemma.c:4750-4962)
+      rmsnorm(x, n1) + quantize_act            gcu_dev_rmsnorm_quantize
+      q, k, v = gemv_int8_multi                gcu_dev_gemv_int8_multi
+      QK norm, RoPE, KV-cache write            gcu_dev_qk_norm_rope_cache
+      attention (scores, softmax, values)      gcu_dev_attention_decode
+      quantize_act(xo) + gemv_int8(wo)         gcu_dev_quantize_gemm_int8_multi
+      x = clamp(resid + rmsnorm(o, n2))        gcu_dev_rmsnorm_residual
+      rmsnorm(x, n3) + quantize_act            gcu_dev_rmsnorm_quantize
+      gate, up = gemv_int8_multi               gcu_dev_gemv_int8_multi
+      gelu(gate) * up + quantize_act           gcu_dev_geglu_quantize
+      down = gemv_int8(w3)                     gcu_dev_gemv_int8
+      x = clamp(resid + rmsnorm(down, n4))     gcu_dev_rmsnorm_residual
+    final rmsnorm + quantize_act, lm_head gemv_int8, logit softcap
+
+Weights follow gemma.c's TextDecoder (gemma.c:1174-1301); torch only holds
+the device memory and the stream.  The RoPE tables are computed on the host
+per position as rope_freqs does (gemma.c:4178-4216) unless the caller passes
+its own.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+import gcu
+
+
+def rope_tables(hdim: int, theta_l: float, theta_g: float, pos: int):
+    """gemma.c:4178-4193 in float32: (cos, sin) interleaved per frequency, for
+    sliding-window and full-attention layers."""
+    d = np.arange(hdim // 2, dtype=np.float32)
+    e = (np.float32(-2.0) * d) / np.float32(hdim)
+    out = []
+    for theta in (theta_l, theta_g):
+        freq = np.power(np.float32(theta), e, dtype=np.float32)
+        ang = (freq * np.float32(pos)).astype(np.float32)
+        t = np.empty(hdim, np.float32)
+        t[0::2] = np.cos(ang)
+        t[1::2] = np.sin(ang)
+        out.append(t)
+    return out[0], out[1]
+
+
+class Decoder:
+    """A W8A8 Gemma text decoder resident on one GPU.
+
+    cfg: nl, n_heads, nkv, hdim, dim, mlp_dim, nvocab, q_scale, slide, swa
+    (per-layer sliding flags), qk_norm, mlp_pre, mlp_pst, theta_l, theta_g,
+    eps, sc_att, sc_log.  layers: per layer a dict of (q, scales) numpy pairs
+    wq, wk, wv, wo, w1 (up), w2 (gate), w3 (down) and norm vectors n1..n4, nq,
+    nk.  emb: the tied embedding (q, scales) used as lm_head; fnorm: the final
+    norm.  clen: KV-cache positions."""
+
+    def __init__(self, cfg: dict, layers: list, emb, fnorm, clen: int, device="cuda"):
+        import torch
+        self.torch = torch
+        self.cfg = cfg
+        self.dev = device
+        self.clen = clen
+        c = cfg
+        t = lambda a: a.to(device).contiguous() if torch.is_tensor(a) else torch.from_numpy(np.ascontiguousarray(a)).to(device)
+        self.L = []
+        for lay in layers:
+            d = {k: (t(lay[k][0]), t(lay[k][1])) for k in ("wq", "wk", "wv", "wo", "w1", "w2", "w3")}
+            for k in ("n1", "n2", "n3", "n4", "nq", "nk"):
+                d[k] = t(lay[k]) if lay.get(k) is not None else None
+            self.L.append(d)
+        self.emb = (t(emb[0]), t(emb[1]))
+        self.fnorm = t(fnorm)
+        q_sz, kv_sz = c["n_heads"] * c["hdim"], c["nkv"] * c["hdim"]
+        f32 = dict(dtype=torch.float32, device=device)
+        i8 = dict(dtype=torch.int8, device=device)
+        self.kv = torch.zeros((c["nl"], 2, c["nkv"], clen, c["hdim"]), **f32)
+        self.x = torch.empty((1, c["dim"]), **f32)
+        self.out = torch.empty((1, c["dim"]), **f32)
+        self.xq = torch.empty((c["n_heads"], 1, c["hdim"]), **f32)
+        self.xk = torch.empty((c["nkv"], 1, c["hdim"]), **f32)
+        self.xv = torch.empty((c["nkv"], 1, c["hdim"]), **f32)
+        self.xo = torch.empty((1, q_sz), **f32)
+        self.xg = torch.empty((1, c["mlp_dim"]), **f32)
+        self.xu = torch.empty((1, c["mlp_dim"]), **f32)
+        self.q = torch.empty((1, max(c["dim"], q_sz, c["mlp_dim"])), **i8)
+        self.s = torch.empty(1, **f32)
+        self.logits = torch.empty((1, c["nvocab"]), **f32)
+        self.freqs = torch.empty((2, c["hdim"]), **f32)  # sliding, full
+        del kv_sz
+
+    def set_freqs(self, slid, full, stream=None):
+        """Upload the RoPE tables of the position about to be decoded."""
+        torch = self.torch
+        host = torch.from_numpy(np.stack([np.asarray(slid, np.float32), np.asarray(full, np.float32)]))
+        with torch.cuda.stream(stream) if stream is not None else _null():
+            self.freqs.copy_(host, non_blocking=False)
+
+    def step(self, pos: int, stream=None):
+        """Decode position `pos` from the embedding already in self.x (dim,);
+        leaves the logits in self.logits and the final hidden state in self.x.
+        The RoPE tables for `pos` must be set (set_freqs) beforehand."""
+        c = self.cfg
+        dim, mlp, hdim = c["dim"], c["mlp_dim"], c["hdim"]
+        nh, nkv = c["n_heads"], c["nkv"]
+        q_sz = nh * hdim
+        asc = float(np.float32(1.0) / np.sqrt(np.float32(c["q_scale"])))
+        eps = c["eps"]
+        q = self.q
+        for l, w in enumerate(self.L):
+            # gemma.c:4750-4773: rmsnorm(x, n1) -> quantize_act -> q, k, v
+            gcu.dev_rmsnorm_quantize(q, self.s, self.x, w["n1"], eps, 1, dim, stream=stream)
+            gcu.dev_gemv_int8_multi([(w["wq"][0], w["wq"][1], self.xq), (w["wk"][0], w["wk"][1], self.xk),
+                                     (w["wv"][0], w["wv"][1], self.xv)], q, self.s, dim, stream=stream)
+            # gemma.c:4775-4818: QK norm, RoPE, cache write
+            kc, vc = self.kv[l, 0], self.kv[l, 1]
+            sliding = bool(c["swa"][l])
+            gcu.dev_qk_norm_rope_cache(self.xq, self.xk, self.xv, kc, vc, self.freqs[0 if sliding else 1], pos, 1.0,
+                                       w["nq"] if c["qk_norm"] else None, w["nk"] if c["qk_norm"] else None, eps,
+                                       stream=stream)
+            # gemma.c:4820-4848: attention over [spos, pos]
+            spos = pos + 1 - c["slide"] if sliding and pos >= c["slide"] else 0
+            gcu.dev_attention_decode(self.xo.view(nh, hdim), self.xq.view(nh, hdim), kc, vc, spos, pos + 1 - spos,
+                                     asc, c["sc_att"], stream=stream)
+            # gemma.c:4855-4881: O projection, post-attention norm, residual
+            gcu.dev_quantize_gemm_int8_multi([(w["wo"][0], w["wo"][1], self.out)], q, self.s, self.xo, 1, q_sz,
+                                             stream=stream)
+            gcu.dev_rmsnorm_residual(self.x, self.out, self.x, w["n2"] if c["mlp_pre"] else None, eps, 1, dim,
+                                     stream=stream)
+            # gemma.c:4885-4930: pre-FFN norm, gate/up, GeGLU, down
+            gcu.dev_rmsnorm_quantize(q, self.s, self.x, w["n3"] if c["mlp_pre"] else w["n2"], eps, 1, dim,
+                                     stream=stream)
+            gcu.dev_gemv_int8_multi([(w["w2"][0], w["w2"][1], self.xg), (w["w1"][0], w["w1"][1], self.xu)], q,
+                                    self.s, dim, stream=stream)
+            gcu.dev_geglu_quantize(q, self.s, self.xg, self.xu, 1, mlp, stream=stream)
+            gcu.dev_gemv_int8(self.out, w["w3"][0], w["w3"][1], q, self.s, dim, mlp, stream=stream)
+            # gemma.c:4934-4962: post-FFN norm, residual
+            gcu.dev_rmsnorm_residual(self.x, self.out, self.x, w["n4"] if c["mlp_pst"] else None, eps, 1, dim,
+                                     stream=stream)
+        # gemma.c:4965-4976: final norm, tied lm_head, logit softcap
+        gcu.dev_rmsnorm_quantize(q, self.s, self.x, self.fnorm, eps, 1, dim, out=self.x, stream=stream)
+        gcu.dev_gemv_int8(self.logits, self.emb[0], self.emb[1], q, self.s, c["nvocab"], dim, stream=stream)
+        if c["sc_log"]:
+            gcu.dev_softcap(self.logits, c["sc_log"], stream=stream)
+
+    def launches_per_step(self) -> int:
+        """Kernel launches of one step (attention over a split window adds its
+        combine launch; counted as one here)."""
+        return 11 * self.cfg["nl"] + 2 + (1 if self.cfg["sc_log"] else 0)
+
+
+class _null:
+    def __enter__(self):
+        return None
+
+    def __exit__(self, *a):
+        return False

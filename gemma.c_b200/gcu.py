@@ -85,6 +85,8 @@ SIGNATURES = {
                                         ctypes.c_float, ctypes.c_float, _vp]),
     "gcu_dev_attention_prefill": (_int, [_vp, _int, _vp, _vp, _vp, ctypes.c_long, _int, _int, _int, _int, _int,
                                          _int, ctypes.c_float, _int, _vp]),
+    "gcu_dev_rmsnorm_residual": (_int, [_vp, _vp, _vp, _vp, ctypes.c_float, _int, _int, _vp]),
+    "gcu_dev_softcap": (_int, [_vp, ctypes.c_long, ctypes.c_float, _vp]),
     "gcu_dev_qk_norm_rope_cache": (_int, [_vp, _vp, _vp, _vp, _vp, ctypes.c_long, _vp, _vp, ctypes.c_float, _vp,
                                           ctypes.c_float, _int, _int, _int, _int, _int, _vp]),
     "gcu_dev_patch_embed": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _int, _vp]),
@@ -457,3 +459,16 @@ def dev_qk_norm_rope_cache(xq, xk, xv, kc, vc, freqs, spos, q_scale=1.0, nq=None
                                             nk.data_ptr() if nk is not None else None, eps, freqs.data_ptr(),
                                             q_scale, n_heads, nkv, hdim, spos, ntok, _stream(stream)),
            "dev_qk_norm_rope_cache")
+
+
+def dev_rmsnorm_residual(x, y, resid, weight, eps, m, dim, stream=None):
+    """gemma.c:4862-4881 / 4950-4962 on CUDA tensors: x = clamp(resid + rmsnorm(y, weight)),
+    weight None = no post-norm."""
+    _check(lib().gcu_dev_rmsnorm_residual(x.data_ptr(), y.data_ptr(), resid.data_ptr(),
+                                          weight.data_ptr() if weight is not None else None, eps, m, dim,
+                                          _stream(stream)), "dev_rmsnorm_residual")
+
+
+def dev_softcap(x, cap, stream=None):
+    """gemma.c:4971-4976 on a CUDA tensor, in place."""
+    _check(lib().gcu_dev_softcap(x.data_ptr(), x.numel(), cap, _stream(stream)), "dev_softcap")

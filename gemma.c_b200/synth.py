@@ -91,6 +91,29 @@ def rope_inputs(tensor_id: int, n_heads: int, nkv: int, hdim: int, clen: int, nt
     return xq, xk, xv, kc, vc, nq, nk
 
 
+def decoder_model(tensor_id: int, cfg: dict):
+    """Seeded W8A8 text decoder for decode-step tests: per layer the QTensors
+    wq, wk, wv, wo, w1 (up), w2 (gate), w3 (down) quantized per row like the
+    exporter, norm weights N(0, 0.1^2) (n1..n4, and nq, nk of head size);
+    the tied embedding (nvocab rows of dim) and the final norm."""
+    dim, mlp, hd = cfg["dim"], cfg["mlp_dim"], cfg["hdim"]
+    q_sz, kv_sz = cfg["n_heads"] * hd, cfg["nkv"] * hd
+    layers = []
+    for l in range(cfg["nl"]):
+        b = tensor_id + 100 * l
+        lay = {"wq": weight(b + 1, q_sz, dim), "wk": weight(b + 2, kv_sz, dim), "wv": weight(b + 3, kv_sz, dim),
+               "wo": weight(b + 4, dim, q_sz), "w1": weight(b + 5, mlp, dim), "w2": weight(b + 6, mlp, dim),
+               "w3": weight(b + 7, dim, mlp)}
+        for i, k in enumerate(("n1", "n2", "n3", "n4")):
+            lay[k] = normal(b + 10 + i, (dim,), 0.1)
+        lay["nq"] = normal(b + 20, (hd,), 0.1)
+        lay["nk"] = normal(b + 21, (hd,), 0.1)
+        layers.append(lay)
+    emb = weight(tensor_id + 90, cfg["nvocab"], dim)
+    fnorm = normal(tensor_id + 91, (dim,), 0.1)
+    return layers, emb, fnorm
+
+
 def vision_head_inputs(tensor_id: int, img_px: int, psize: int, dim: int, img_tok: int, tdim: int):
     """Seeded operands of the SigLIP head (gemma.c:4411-4716): an
     (img_px, img_px, 3) image of N(0, 0.5^2) pixels, patch-embedding weights

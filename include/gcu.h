@@ -221,6 +221,15 @@ int gcu_dev_rmsnorm_quantize(int8_t *q, float *s, float *out, const float *x, in
 int gcu_dev_geglu_quantize(int8_t *q, float *s, float *out, const float *gate, const float *up,
                            int m, int dim, void *stream);
 
+/* gemma.c:4862-4881, 4950-4962: the residual update after a block, m rows
+ * of dim: x = clamp(resid + rmsnorm(y, weight)) (weight NULL: no post-norm,
+ * x = clamp(resid + y)); clamp to the float range as clamp_fpx does.  x may
+ * be resid.  dim a multiple of 4, at most 4096. */
+int gcu_dev_rmsnorm_residual(float *x, const float *y, const float *resid, const float *weight,
+                             float eps, int m, int dim, void *stream);
+/* gemma.c:4971-4976: x[i] = tanh(x[i] / cap) * cap (the final logit softcap). */
+int gcu_dev_softcap(float *x, long n, float cap, void *stream);
+
 /* ---- attention (fp32) between the Q/K/V and O matmuls ----------------------
  * gemma.c's KV cache layout (gemma.c:4806-4808): kv head hk's position t at
  * cache + hk*kv_stride + t*hdim (kv_stride = clen*hdim), K and V separate;

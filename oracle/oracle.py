@@ -369,6 +369,11 @@ def ref(variant: str | None = None) -> ctypes.CDLL | None:
         lib.ref_qk_norm_rope_cache.restype = None
         lib.ref_qk_norm_rope_cache.argtypes = [_f32p, _f32p, _f32p, _f32p, _f32p, ctypes.c_long, _f32p, _f32p,
                                                ctypes.c_float, _f32p, ctypes.c_float] + [ctypes.c_int] * 5
+    if hasattr(lib, "ref_decode_steps"):
+        lib.ref_decode_steps.restype = ctypes.c_int
+        lib.ref_decode_steps.argtypes = [_f32p, _f32p, _f32p] + [ctypes.c_int] * 10 + \
+            [ctypes.POINTER(ctypes.c_int)] + [ctypes.c_int] * 3 + [ctypes.c_float] * 5 + \
+            [ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p), _i8p, _f32p, _f32p, ctypes.c_int]
     if hasattr(lib, "ref_read_model_seconds"):
         lib.ref_read_model_seconds.restype = ctypes.c_double
         lib.ref_read_model_seconds.argtypes = [ctypes.c_char_p, ctypes.c_int]
@@ -478,6 +483,39 @@ class Ref:
                                         _ptr(nk, _f32p) if nk is not None else None, eps, _ptr(freqs, _f32p), q_scale,
                                         n_heads, kc.shape[0], hdim, spos, ntok)
         return xq, kc, vc
+
+    def decode_steps(self, cfg: dict, layers: list, emb, fnorm, x0):
+        """gemma.c's forward_text_decode for positions 0 .. len(x0)-1 on a
+        decoder built from synth.decoder_model-style tensors; returns the
+        logits (npos, nvocab) and final hidden states (npos, dim)."""
+        x0 = np.ascontiguousarray(x0, np.float32)
+        npos, dim = x0.shape
+        keep = []
+        qt = (ctypes.c_void_p * (14 * cfg["nl"]))()
+        nrm = (ctypes.c_void_p * (6 * cfg["nl"]))()
+        for l, lay in enumerate(layers):
+            for j, k in enumerate(("wq", "wk", "wv", "wo", "w1", "w2", "w3")):
+                q, s = np.ascontiguousarray(lay[k][0], np.int8), np.ascontiguousarray(lay[k][1], np.float32)
+                keep += [q, s]
+                qt[14 * l + 2 * j], qt[14 * l + 2 * j + 1] = q.ctypes.data, s.ctypes.data
+            for j, k in enumerate(("n1", "n2", "n3", "n4", "nq", "nk")):
+                v = np.ascontiguousarray(lay[k], np.float32)
+                keep.append(v)
+                nrm[6 * l + j] = v.ctypes.data
+        swa = (ctypes.c_int * cfg["nl"])(*[int(b) for b in cfg["swa"]])
+        eq, es = np.ascontiguousarray(emb[0], np.int8), np.ascontiguousarray(emb[1], np.float32)
+        fn = np.ascontiguousarray(fnorm, np.float32)
+        logits = np.empty((npos, cfg["nvocab"]), np.float32)
+        hid = np.empty((npos, dim), np.float32)
+        rc = self.lib.ref_decode_steps(_ptr(logits, _f32p), _ptr(hid, _f32p), _ptr(x0, _f32p), npos, cfg["nl"],
+                                       cfg["n_heads"], cfg["nkv"], cfg["hdim"], dim, cfg["mlp_dim"], cfg["nvocab"],
+                                       cfg["q_scale"], cfg["slide"], swa, int(cfg["qk_norm"]), int(cfg["mlp_pre"]),
+                                       int(cfg["mlp_pst"]), cfg["theta_l"], cfg["theta_g"], cfg["eps"], cfg["sc_att"],
+                                       cfg["sc_log"], qt, nrm, _ptr(eq, _i8p), _ptr(es, _f32p), _ptr(fn, _f32p),
+                                       self.threads)
+        if rc:
+            raise RuntimeError("reference forward_text_decode failed")
+        return logits, hid
 
     def vision_head(self, v: dict):
         """gemma.c's forward_vision with no encoder layers on

@@ -350,3 +350,129 @@ void ref_qk_norm_rope_cache(float *xq, float *xk, const float *xv, float *kc, fl
            (size_t)ntok * hdim * sizeof(float));
   }
 }
+
+/* gemma.c:4727-4978 forward_text_decode, the reference's whole decode step,
+ * on a W8A8 text decoder built from the given tensors: npos steps at
+ * positions 0 .. npos-1, step p's input embedding x0[p] placed in tb->x as
+ * its caller does (gemma.c:5470-5490).  Outputs per step: the logits
+ * (after the optional softcap) and the final hidden state (after the final
+ * RMSNorm).  qt: 14 pointers per layer (wq, wk, wv, wo, w1 = up, w2 = gate,
+ * w3 = down; int8 values then fp32 scales each); nrm: 6 per layer (n1, n2,
+ * n3, n4, nq, nk); swa: sliding-window flag per layer. */
+int ref_decode_steps(float *logits, float *hid, const float *x0, int npos, int nl, int n_heads, int nkv,
+                     int hdim, int dim, int mlp_dim, int nvocab, int q_scale, int slide, const int *swa,
+                     int qk_norm, int mlp_pre, int mlp_pst, float theta_l, float theta_g, float eps, float sc_att,
+                     float sc_log, void *const *qt, float *const *nrm, const int8_t *emb_q, const float *emb_s,
+                     const float *fnorm, int threads) {
+  TextConfig tc;
+  memset(&tc, 0, sizeof(tc));
+  tc.nl = (uint8_t)nl;
+  tc.n_heads = (uint8_t)n_heads;
+  tc.nkv = (uint8_t)nkv;
+  tc.hdim = (uint16_t)hdim;
+  tc.dim = (uint16_t)dim;
+  tc.mlp_dim = (uint16_t)mlp_dim;
+  tc.q_scale = (uint16_t)q_scale;
+  tc.slide = (uint16_t)slide;
+  tc.max_seq = (uint32_t)npos;
+  tc.nvocab = (uint32_t)nvocab;
+  tc.theta_l = theta_l;
+  tc.theta_g = theta_g;
+  tc.eps = eps;
+  tc.sc_att = sc_att;
+  tc.sc_log = sc_log;
+  tc.qk_norm = qk_norm != 0;
+  tc.mlp_pre = mlp_pre != 0;
+  tc.mlp_pst = mlp_pst != 0;
+  bool *flags = calloc((size_t)nl, sizeof(bool));
+  QTensor *qts = calloc((size_t)nl * 7 + 1, sizeof(QTensor));
+  TextDecoderLayer *lay = calloc((size_t)nl, sizeof(TextDecoderLayer));
+  TextDecoderLayer **lp = calloc((size_t)nl, sizeof(TextDecoderLayer *));
+  const int q_sz = n_heads * hdim, kv_sz = nkv * hdim;
+  TextBuffer tb;
+  memset(&tb, 0, sizeof(tb));
+  tb.clen = npos;
+  tb.x_i8 = malloc((size_t)(mlp_dim > dim ? mlp_dim : dim) + q_sz);
+  tb.xo_i8 = malloc((size_t)q_sz);
+  tb.xg_i8 = malloc((size_t)mlp_dim);
+  tb.cs_slid = malloc((size_t)hdim * sizeof(float));
+  tb.cs_full = malloc((size_t)hdim * sizeof(float));
+  tb.x = malloc((size_t)dim * sizeof(float));
+  tb.resid = malloc((size_t)dim * sizeof(float));
+  tb.xq = malloc((size_t)q_sz * sizeof(float));
+  tb.xk = malloc((size_t)kv_sz * sizeof(float));
+  tb.xv = malloc((size_t)kv_sz * sizeof(float));
+  tb.xo = malloc((size_t)q_sz * sizeof(float));
+  tb.att = malloc((size_t)n_heads * npos * sizeof(float));
+  tb.kvc = calloc((size_t)nl * 2 * npos * kv_sz, sizeof(float));
+  tb.xg = malloc((size_t)mlp_dim * sizeof(float));
+  tb.xu = malloc((size_t)mlp_dim * sizeof(float));
+  tb.logits = malloc((size_t)nvocab * sizeof(float));
+  int rc = 1;
+  if (!flags || !qts || !lay || !lp || !tb.x_i8 || !tb.xo_i8 || !tb.xg_i8 || !tb.cs_slid || !tb.cs_full || !tb.x ||
+      !tb.resid || !tb.xq || !tb.xk || !tb.xv || !tb.xo || !tb.att || !tb.kvc || !tb.xg || !tb.xu || !tb.logits)
+    goto done;
+  for (int l = 0; l < nl; l++) {
+    flags[l] = swa[l] != 0;
+    QTensor *t = qts + (size_t)l * 7;
+    for (int j = 0; j < 7; j++) {
+      t[j].quant = true;
+      t[j].i8.q = (int8_t *)qt[(size_t)l * 14 + 2 * j];
+      t[j].i8.scales = (floatx *)qt[(size_t)l * 14 + 2 * j + 1];
+    }
+    lay[l].wq = t + 0;
+    lay[l].wk = t + 1;
+    lay[l].wv = t + 2;
+    lay[l].wo = t + 3;
+    lay[l].w1 = t + 4;
+    lay[l].w2 = t + 5;
+    lay[l].w3 = t + 6;
+    lay[l].n1 = nrm[(size_t)l * 6 + 0];
+    lay[l].n2 = nrm[(size_t)l * 6 + 1];
+    lay[l].n3 = nrm[(size_t)l * 6 + 2];
+    lay[l].n4 = nrm[(size_t)l * 6 + 3];
+    lay[l].nq = nrm[(size_t)l * 6 + 4];
+    lay[l].nk = nrm[(size_t)l * 6 + 5];
+    lp[l] = lay + l;
+  }
+  tc.swa = flags;
+  QTensor *emb = qts + (size_t)nl * 7;
+  emb->quant = true;
+  emb->i8.q = (int8_t *)emb_q;
+  emb->i8.scales = (floatx *)emb_s;
+  TextDecoder dec;
+  memset(&dec, 0, sizeof(dec));
+  dec.config = &tc;
+  dec.emb = emb;
+  dec.layers = lp;
+  dec.fnorm = (floatx *)fnorm;
+  rc = 0;
+  for (int p = 0; p < npos && rc == 0; p++) {
+    memcpy(tb.x, x0 + (size_t)p * dim, (size_t)dim * sizeof(float));
+    rc = forward_text_decode(&dec, &tb, p, true, true, threads, NULL);
+    memcpy(logits + (size_t)p * nvocab, tb.logits, (size_t)nvocab * sizeof(float));
+    memcpy(hid + (size_t)p * dim, tb.x, (size_t)dim * sizeof(float));
+  }
+done:
+  free(flags);
+  free(qts);
+  free(lay);
+  free(lp);
+  free(tb.x_i8);
+  free(tb.xo_i8);
+  free(tb.xg_i8);
+  free(tb.cs_slid);
+  free(tb.cs_full);
+  free(tb.x);
+  free(tb.resid);
+  free(tb.xq);
+  free(tb.xk);
+  free(tb.xv);
+  free(tb.xo);
+  free(tb.att);
+  free(tb.kvc);
+  free(tb.xg);
+  free(tb.xu);
+  free(tb.logits);
+  return rc;
+}

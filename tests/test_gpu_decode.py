@@ -1,0 +1,105 @@
+"""A device-resident decode step (decode.Decoder) against gemma.c's own.
+
+tests/golden/decode.npz holds what gemma.c's forward_text_decode computes for
+positions 0..7 on small seeded W8A8 decoders (make_decode_golden.py): logits
+and final hidden states per step, and its RoPE tables.  The GPU decoder runs
+the same step as one chain of C-ABI calls (norm+quantize, multi-GEMV, QK
+norm/RoPE/cache, attention, fused quantize+GEMV, residual, GeGLU+quantize,
+lm_head), with the KV cache on the device across the 8 steps.
+
+Each stage is checked exactly or to fp32 reassociation by its own tests; the
+chain adds int8 rounding boundaries: an fp32 value a few ulps from a
+quantization boundary can round to the neighbouring code, which moves that
+product by one code step.  So the bound here is max |gpu - ref| <= 2e-3 of
+the largest |ref| per step, and the median difference within 1e-5 of it
+(the typical element agrees to fp32 rounding).
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+import synth
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+import decode  # noqa: E402
+import gcu  # noqa: E402
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+GOLD = np.load(os.path.join(HERE, "golden", "decode.npz"))
+META = json.loads(str(GOLD["meta"]))
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _gpu():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    gcu.init(0)
+    yield
+    gcu.check_device()
+
+
+def close(got, want):
+    err = np.abs(got - want)
+    scale = float(np.max(np.abs(want)))
+    return float(err.max()) <= 2e-3 * scale and float(np.median(err)) <= 1e-5 * scale, float(err.max()) / scale
+
+
+@pytest.mark.parametrize("name", list(META["cases"]))
+def test_decode_steps_match_reference(name):
+    cfg = META["cases"][name]
+    layers, emb, fnorm = synth.decoder_model(cfg["tid"], cfg)
+    npos = META["npos"]
+    x0 = synth.normal(cfg["tid"] + 999, (npos, cfg["dim"]))
+    dec = decode.Decoder(cfg, layers, emb, fnorm, clen=npos)
+    for p in range(npos):
+        dec.set_freqs(GOLD[f"{name}_slid"][p], GOLD[f"{name}_full"][p])
+        dec.x.copy_(torch.from_numpy(x0[p][None]))
+        dec.step(p)
+        torch.cuda.synchronize()
+        ok, rel = close(dec.logits.cpu().numpy()[0], GOLD[f"{name}_logits"][p])
+        assert ok, f"logits at position {p}: max diff {rel:.3g} of the largest"
+        ok, rel = close(dec.x.cpu().numpy()[0], GOLD[f"{name}_hid"][p])
+        assert ok, f"hidden state at position {p}: max diff {rel:.3g} of the largest"
+    gcu.check_device()
+
+
+def test_decode_step_graph_replay_matches_eager():
+    # the whole step is capturable: a CUDA graph replay gives the eager result bit for bit
+    name = "gemma3"
+    cfg = META["cases"][name]
+    layers, emb, fnorm = synth.decoder_model(cfg["tid"], cfg)
+    x0 = synth.normal(cfg["tid"] + 999, (2, cfg["dim"]))
+    outs = []
+    for use_graph in (False, True):
+        dec = decode.Decoder(cfg, layers, emb, fnorm, clen=4)
+        dec.set_freqs(GOLD[f"{name}_slid"][0], GOLD[f"{name}_full"][0])
+        dec.x.copy_(torch.from_numpy(x0[0][None]))
+        dec.step(0)  # position 0 eagerly (also warms the library)
+        dec.set_freqs(GOLD[f"{name}_slid"][1], GOLD[f"{name}_full"][1])
+        dec.x.copy_(torch.from_numpy(x0[1][None]))
+        st = torch.cuda.Stream()
+        torch.cuda.synchronize()
+        if use_graph:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=st):
+                dec.step(1, stream=st)
+            g.replay()
+        else:
+            with torch.cuda.stream(st):
+                dec.step(1, stream=st)
+        torch.cuda.synchronize()
+        outs.append(dec.logits.cpu().numpy().copy())
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+
+
+def test_rope_tables_follow_rope_freqs():
+    # the host tables (numpy float32) against the reference's own for the fixture positions
+    cfg = META["cases"]["gemma3"]
+    for p in range(META["npos"]):
+        slid, full = decode.rope_tables(cfg["hdim"], cfg["theta_l"], cfg["theta_g"], p)
+        assert np.max(np.abs(slid - GOLD["gemma3_slid"][p])) <= 2e-6
+        assert np.max(np.abs(full - GOLD["gemma3_full"][p])) <= 2e-6
