@@ -1148,6 +1148,138 @@ def _attn_cpu_baseline(c, lay):
 
 
 # ---------------------------------------------------------------------------
+# device-resident decode step (decode.Decoder): every layer of a Gemma 3
+# text decoder plus the lm_head for one token, activations and KV cache in HBM
+# ---------------------------------------------------------------------------
+DECODE_STEP = {
+    "decode_step1b": dict(title="Gemma-3-1B decode step at position 1023 (26 layers + lm_head)", nl=26, n_heads=4,
+                          nkv=1, hdim=256, dim=1152, mlp_dim=6912, nvocab=262144, q_scale=256, slide=512, pos=1023),
+    "decode_step4b": dict(title="Gemma-3-4B decode step at position 1023 (34 layers + lm_head)", nl=34, n_heads=8,
+                          nkv=4, hdim=256, dim=2560, mlp_dim=10240, nvocab=262144, q_scale=256, slide=1024, pos=1023),
+}
+
+
+def run_decode_step(args):
+    """One step = decode.Decoder.step: per layer RMSNorm+quantize, Q/K/V
+    multi-GEMV, QK norm/RoPE/cache write, attention over the window, fused
+    quantize+O GEMV, post-norm residual, pre-FFN norm+quantize, gate/up
+    multi-GEMV, GeGLU+quantize, down GEMV, post-norm residual; then the final
+    norm and the 262144-row lm_head.  Weights and a KV cache of `pos`
+    positions resident in HBM, one CUDA graph replay per step, CUDA events.
+    Roofline: HBM bytes the step must read (all weights + the K/V windows)
+    over the measured copy bandwidth."""
+    import numpy as np
+    import torch
+
+    import decode
+    import gcu
+    import synth
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    gcu.init(0)
+    torch.cuda.set_device(0)
+    peaks = load_peaks()
+    spec = DECODE_STEP[args.workload]
+    nl = spec["nl"] if args.layers <= 0 else min(spec["nl"], args.layers)
+    cfg = dict(spec, nl=nl, swa=[(l + 1) % 6 != 0 for l in range(nl)], qk_norm=True, mlp_pre=True, mlp_pst=True,
+               theta_l=10000.0, theta_g=1000000.0, eps=1e-6, sc_att=0.0, sc_log=0.0)
+    pos = cfg["pos"]
+    dim, mlp, hd = cfg["dim"], cfg["mlp_dim"], cfg["hdim"]
+    q_sz, kv_sz = cfg["n_heads"] * hd, cfg["nkv"] * hd
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    wt = lambda n, k: synth.weight_torch(n, k, gen, "cuda")
+    nv = lambda n: torch.randn(n, generator=gen, device="cuda") * 0.1
+    layers = [{"wq": wt(q_sz, dim), "wk": wt(kv_sz, dim), "wv": wt(kv_sz, dim), "wo": wt(dim, q_sz),
+               "w1": wt(mlp, dim), "w2": wt(mlp, dim), "w3": wt(dim, mlp), "n1": nv(dim), "n2": nv(dim),
+               "n3": nv(dim), "n4": nv(dim), "nq": nv(hd), "nk": nv(hd)} for _ in range(nl)]
+    emb = wt(cfg["nvocab"], dim)
+    fnorm = nv(dim)
+    dec = decode.Decoder(cfg, layers, emb, fnorm, clen=pos + 1)
+    dec.kv.normal_(generator=gen)  # positions 0 .. pos-1 as if decoded before
+    slid, full = decode.rope_tables(hd, cfg["theta_l"], cfg["theta_g"], pos)
+    dec.set_freqs(slid, full)
+    dec.x.normal_(generator=gen)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        dec.step(pos, stream=stream)  # eager: allocates the attention split scratch
+    stream.synchronize()
+    gcu.check_device()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        dec.step(pos, stream=stream)
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            g.replay()
+    torch.cuda.synchronize()
+    clocks = Clocks(0)
+    clocks.start()
+    time.sleep(0.2)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps):
+            g.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    clk = clocks.stop()
+    gcu.check_device()
+    wbytes = sum(t[0].numel() + 4 * t[1].numel() for lay in dec.L for k, t in lay.items()
+                 if isinstance(t, tuple)) + emb[0].numel() + 4 * emb[1].numel()
+    kvbytes = 0
+    for l in range(nl):
+        n = min(pos + 1, cfg["slide"]) if cfg["swa"][l] else pos + 1
+        kvbytes += 2 * kv_sz * n * 4
+    nbytes = wbytes + kvbytes
+    ach = nbytes / (ms * 1e-3) / 1e9
+    out = {"metric": "device-resident decode: tokens per second (all layers + lm_head, batch 1)",
+           "value": 1e3 / ms, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": ms, "higher_is_better": True, "scaling": "none", "vs_baseline": None,
+           "dtype": "int8 matmuls (int32 accum), fp32 norms/attention", "data": "synthetic", "impl": "ours",
+           "config": {"workload": f"{args.workload}: {cfg['title']}", "layers": nl, "kv_cache_positions": pos + 1,
+                      "layer_pattern": "5 sliding-window layers then 1 global",
+                      **({"reduced": f"--layers {args.layers}: a profiling case, not the benchmark workload"}
+                         if args.layers > 0 else {})},
+           "roofline": {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                        "frac": ach / peaks["hbm_gbs"], "peak_src": f"{peaks['src']} copy bandwidth",
+                        "bytes_per_step": nbytes, "weight_bytes": wbytes, "kv_bytes": kvbytes, "traffic": None},
+           "clocks": clk, "gpu_launches": dec.launches_per_step() * args.steps, "e2e": None,
+           "e2e_note": "device-resident by design: the step reads no host memory"}
+    if not args.no_cpu and args.layers <= 0 and args.workload == "decode_step1b":
+        out["cpu_baseline"] = _decode_cpu_baseline(cfg, dec, emb, fnorm)
+    del g
+    print(json.dumps(out), flush=True)
+
+
+def _decode_cpu_baseline(cfg, dec, emb, fnorm):
+    """gemma.c's forward_text_decode on the same weights (copied to the host),
+    positions 0..15, all host threads: seconds per token."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    variant = oracle.ref_variant()
+    lib = oracle.ref(variant) if variant else None
+    threads = os.cpu_count() or 1
+    if lib is None or not hasattr(lib, "ref_decode_steps"):
+        return {"value": None, "cores": threads, "kind": "reference", "sample": "reference build not available"}
+    R = oracle.Ref(variant, threads=threads)
+    host = lambda t: t.cpu().numpy()
+    layers = []
+    for w in dec.L:
+        lay = {k: (host(w[k][0]), host(w[k][1])) for k in ("wq", "wk", "wv", "wo", "w1", "w2", "w3")}
+        lay.update({k: host(w[k]) for k in ("n1", "n2", "n3", "n4", "nq", "nk")})
+        layers.append(lay)
+    e = (host(emb[0]), host(emb[1]))
+    x0 = np.random.default_rng(0).standard_normal((16, cfg["dim"]), dtype=np.float32)
+    R.decode_steps(cfg, layers, e, host(fnorm), x0[:2])  # warm-up (pages the weights in)
+    t0 = time.perf_counter()
+    R.decode_steps(cfg, layers, e, host(fnorm), x0)
+    dt = (time.perf_counter() - t0) / len(x0)
+    return {"value": 1.0 / dt, "unit": "tokens/s", "cores": threads, "kind": "reference", "ms_per_step": dt * 1e3,
+            "sample": f"gemma.c forward_text_decode on the same weights, positions 0..15, {variant}/{R.isa}"}
+
+
+# ---------------------------------------------------------------------------
 # SigLIP head (gcu_dev_patch_embed, gcu_dev_vision_pool_quantize, then the
 # projection gcu_dev_gemm_int8): one 896 px image of Gemma-3-4B
 # ---------------------------------------------------------------------------
@@ -1293,7 +1425,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="prefill1b",
                     choices=list(PREFILL) + list(DECODE) + ["lmhead4b"] + list(UPLOAD) + list(ATTN) +
-                    ["siglip_head"])
+                    ["siglip_head"] + list(DECODE_STEP))
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--unfused", action="store_true",
                     help="decode: quantize and GEMV as separate launches (the reference's call split)")
@@ -1307,7 +1439,13 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.workload == "siglip_head":
+    if args.workload in DECODE_STEP:
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the decode-step line carries the reference's "
+                              "forward_text_decode timing as its cpu_baseline"}))
+        else:
+            run_decode_step(args)
+    elif args.workload == "siglip_head":
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "the SigLIP-head line carries the reference's "
                               "forward_vision timing as its cpu_baseline"}))
