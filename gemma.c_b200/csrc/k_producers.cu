@@ -285,3 +285,105 @@ GCU_EXPORT int gcu_dev_softcap(float *x, long n, float cap, void *stream) {
   GCU_CUDA(launch_k(k_softcap, grid, 256, 0, static_cast<cudaStream_t>(stream), x, n, cap));
   return 0;
 }
+
+// ---------------------------------------------------------------------------
+// the residual update fused with the next block's norm + quantize
+// ---------------------------------------------------------------------------
+namespace gcu {
+namespace {
+
+// x = clamp(resid + rmsnorm(y, w_post))            gemma.c:4862-4881 / 4950-4962
+// q, s = quantize_act(rmsnorm(x, w_next))          gemma.c:4885-4910 / 4754-4768
+// One CTA per row: the two RMSNorms and the quantize step are the same
+// arithmetic as gcu_dev_rmsnorm_residual followed by gcu_dev_rmsnorm_quantize
+// (one launch instead of two).  w_post NULL: no post-norm.
+template <int NC>
+__global__ void __launch_bounds__(256) k_residual_norm_quant(float *x, int8_t *__restrict__ q, float *__restrict__ s,
+                                                             const float *__restrict__ y, const float *resid,
+                                                             const float *__restrict__ w_post,
+                                                             const float *__restrict__ w_next, float eps, int dim) {
+  __shared__ float red[8];
+  ptx::griddep_launch();
+  const size_t row = blockIdx.x;
+  const int d4 = dim >> 2, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float big = 3.402823466e38f;
+  ptx::griddep_wait();
+  float4 v[NC];
+  float sq = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    const int c = threadIdx.x + i * 256;
+    v[i] = c < d4 ? __ldg(reinterpret_cast<const float4 *>(y + row * dim) + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    sq += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+  }
+  float rms = 1.0f;
+  if (w_post) {
+    sq = row_reduce<8, false>(sq, red, warp, 0, lane);
+    rms = 1.0f / sqrtf(sq / (float)dim + eps);
+  }
+  float sq2 = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    const int c = threadIdx.x + i * 256;
+    if (c >= d4) continue;
+    float4 a = v[i];
+    if (w_post) {
+      const float4 g = __ldg(reinterpret_cast<const float4 *>(w_post) + c);
+      a = make_float4(a.x * rms * (g.x + 1.0f), a.y * rms * (g.y + 1.0f), a.z * rms * (g.z + 1.0f),
+                      a.w * rms * (g.w + 1.0f));
+    }
+    const float4 r = reinterpret_cast<const float4 *>(resid + row * dim)[c];
+    v[i] = make_float4(fminf(big, fmaxf(-big, a.x + r.x)), fminf(big, fmaxf(-big, a.y + r.y)),
+                       fminf(big, fmaxf(-big, a.z + r.z)), fminf(big, fmaxf(-big, a.w + r.w)));
+    reinterpret_cast<float4 *>(x + row * dim)[c] = v[i];
+    sq2 += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+  }
+  sq2 = row_reduce<8, false>(sq2, red, warp, 0, lane);
+  const float rms2 = 1.0f / sqrtf(sq2 / (float)dim + eps);
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    const int c = threadIdx.x + i * 256;
+    if (c >= d4) continue;
+    const float4 g = __ldg(reinterpret_cast<const float4 *>(w_next) + c);
+    v[i] = make_float4(v[i].x * rms2 * (g.x + 1.0f), v[i].y * rms2 * (g.y + 1.0f), v[i].z * rms2 * (g.z + 1.0f),
+                       v[i].w * rms2 * (g.w + 1.0f));
+    amax = ptx::absmax4(v[i], amax);
+  }
+  amax = row_reduce<8, true>(amax, red, warp, 0, lane);
+  float scale, inv;
+  ptx::quant_scale(amax, scale, inv);
+  int *qr = reinterpret_cast<int *>(q + row * dim);
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    const int c = threadIdx.x + i * 256;
+    if (c < d4) qr[c] = ptx::quant_pack4(v[i], inv);
+  }
+  if (threadIdx.x == 0) s[row] = scale;
+}
+
+}  // namespace
+}  // namespace gcu
+
+GCU_EXPORT int gcu_dev_residual_norm_quantize(float *x, int8_t *q, float *s, const float *y, const float *resid,
+                                              const float *w_post, const float *w_next, float eps, int m, int dim,
+                                              void *stream) {
+  if (m <= 0) return 0;
+  if (!x || !q || !s || !y || !resid || !w_next) return set_error("residual_norm_quantize: null pointer");
+  if (dim <= 0 || dim % 4 || dim > 4 * 256 * 4)
+    return set_error("residual_norm_quantize: row length %d must be a positive multiple of 4 up to 4096", dim);
+  if ((uintptr_t)x % 16 || (uintptr_t)y % 16 || (uintptr_t)resid % 16 || (uintptr_t)w_next % 16 ||
+      (w_post && (uintptr_t)w_post % 16) || (uintptr_t)q % 4)
+    return set_error("residual_norm_quantize: rows must be 16-byte aligned (codes 4-byte)");
+  const int nc = (dim / 4 + 255) / 256;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  switch (nc) {
+    case 1: e = launch_k(k_residual_norm_quant<1>, m, 256, 0, st, x, q, s, y, resid, w_post, w_next, eps, dim); break;
+    case 2: e = launch_k(k_residual_norm_quant<2>, m, 256, 0, st, x, q, s, y, resid, w_post, w_next, eps, dim); break;
+    case 3: e = launch_k(k_residual_norm_quant<3>, m, 256, 0, st, x, q, s, y, resid, w_post, w_next, eps, dim); break;
+    default: e = launch_k(k_residual_norm_quant<4>, m, 256, 0, st, x, q, s, y, resid, w_post, w_next, eps, dim); break;
+  }
+  GCU_CUDA(e);
+  return 0;
+}

@@ -5,17 +5,19 @@ token with every activation, weight and the KV cache in GPU memory, one C-ABI
 call per step of the reference:
 
     per layer (gemma.c:4750-4962)
-      rmsnorm(x, n1) + quantize_act            gcu_dev_rmsnorm_quantize
+      rmsnorm(x, n1) + quantize_act            gcu_dev_rmsnorm_quantize (first layer)
       q, k, v = gemv_int8_multi                gcu_dev_gemv_int8_multi
       QK norm, RoPE, KV-cache write            gcu_dev_qk_norm_rope_cache
       attention (scores, softmax, values)      gcu_dev_attention_decode
       quantize_act(xo) + gemv_int8(wo)         gcu_dev_quantize_gemm_int8_multi
-      x = clamp(resid + rmsnorm(o, n2))        gcu_dev_rmsnorm_residual
-      rmsnorm(x, n3) + quantize_act            gcu_dev_rmsnorm_quantize
+      x = clamp(resid + rmsnorm(o, n2)),
+        rmsnorm(x, n3) + quantize_act          gcu_dev_residual_norm_quantize
       gate, up = gemv_int8_multi               gcu_dev_gemv_int8_multi
       gelu(gate) * up + quantize_act           gcu_dev_geglu_quantize
       down = gemv_int8(w3)                     gcu_dev_gemv_int8
-      x = clamp(resid + rmsnorm(down, n4))     gcu_dev_rmsnorm_residual
+      x = clamp(resid + rmsnorm(down, n4)),
+        next layer's rmsnorm(x, n1) + quantize gcu_dev_residual_norm_quantize
+                                               (last layer: gcu_dev_rmsnorm_residual)
     final rmsnorm + quantize_act, lm_head gemv_int8, logit softcap
 
 Weights follow gemma.c's TextDecoder (gemma.c:1174-1301); torch only holds
@@ -108,9 +110,12 @@ class Decoder:
         asc = float(np.float32(1.0) / np.sqrt(np.float32(c["q_scale"])))
         eps = c["eps"]
         q = self.q
+        nl = len(self.L)
+        # gemma.c:4750-4768: the first layer's rmsnorm(x, n1) -> quantize_act
+        # (every later layer's is fused into the previous layer's last residual)
+        gcu.dev_rmsnorm_quantize(q, self.s, self.x, self.L[0]["n1"], eps, 1, dim, stream=stream)
         for l, w in enumerate(self.L):
-            # gemma.c:4750-4773: rmsnorm(x, n1) -> quantize_act -> q, k, v
-            gcu.dev_rmsnorm_quantize(q, self.s, self.x, w["n1"], eps, 1, dim, stream=stream)
+            # gemma.c:4769-4773: q, k, v
             gcu.dev_gemv_int8_multi([(w["wq"][0], w["wq"][1], self.xq), (w["wk"][0], w["wk"][1], self.xk),
                                      (w["wv"][0], w["wv"][1], self.xv)], q, self.s, dim, stream=stream)
             # gemma.c:4775-4818: QK norm, RoPE, cache write
@@ -123,21 +128,25 @@ class Decoder:
             spos = pos + 1 - c["slide"] if sliding and pos >= c["slide"] else 0
             gcu.dev_attention_decode(self.xo.view(nh, hdim), self.xq.view(nh, hdim), kc, vc, spos, pos + 1 - spos,
                                      asc, c["sc_att"], stream=stream)
-            # gemma.c:4855-4881: O projection, post-attention norm, residual
+            # gemma.c:4855-4910: O projection; post-attention norm + residual and
+            # the pre-FFN norm + quantize in one launch
             gcu.dev_quantize_gemm_int8_multi([(w["wo"][0], w["wo"][1], self.out)], q, self.s, self.xo, 1, q_sz,
                                              stream=stream)
-            gcu.dev_rmsnorm_residual(self.x, self.out, self.x, w["n2"] if c["mlp_pre"] else None, eps, 1, dim,
-                                     stream=stream)
-            # gemma.c:4885-4930: pre-FFN norm, gate/up, GeGLU, down
-            gcu.dev_rmsnorm_quantize(q, self.s, self.x, w["n3"] if c["mlp_pre"] else w["n2"], eps, 1, dim,
-                                     stream=stream)
+            gcu.dev_residual_norm_quantize(self.x, q, self.s, self.out, self.x, w["n2"] if c["mlp_pre"] else None,
+                                           w["n3"] if c["mlp_pre"] else w["n2"], eps, 1, dim, stream=stream)
+            # gemma.c:4911-4930: gate/up, GeGLU, down
             gcu.dev_gemv_int8_multi([(w["w2"][0], w["w2"][1], self.xg), (w["w1"][0], w["w1"][1], self.xu)], q,
                                     self.s, dim, stream=stream)
             gcu.dev_geglu_quantize(q, self.s, self.xg, self.xu, 1, mlp, stream=stream)
             gcu.dev_gemv_int8(self.out, w["w3"][0], w["w3"][1], q, self.s, dim, mlp, stream=stream)
-            # gemma.c:4934-4962: post-FFN norm, residual
-            gcu.dev_rmsnorm_residual(self.x, self.out, self.x, w["n4"] if c["mlp_pst"] else None, eps, 1, dim,
-                                     stream=stream)
+            # gemma.c:4934-4962: post-FFN norm + residual, with the next layer's
+            # rmsnorm(x, n1) + quantize_act in the same launch
+            post = w["n4"] if c["mlp_pst"] else None
+            if l + 1 < nl:
+                gcu.dev_residual_norm_quantize(self.x, q, self.s, self.out, self.x, post, self.L[l + 1]["n1"], eps, 1,
+                                               dim, stream=stream)
+            else:
+                gcu.dev_rmsnorm_residual(self.x, self.out, self.x, post, eps, 1, dim, stream=stream)
         # gemma.c:4965-4976: final norm, tied lm_head, logit softcap
         gcu.dev_rmsnorm_quantize(q, self.s, self.x, self.fnorm, eps, 1, dim, out=self.x, stream=stream)
         gcu.dev_gemv_int8(self.logits, self.emb[0], self.emb[1], q, self.s, c["nvocab"], dim, stream=stream)
@@ -147,7 +156,7 @@ class Decoder:
     def launches_per_step(self) -> int:
         """Kernel launches of one step (attention over a split window adds its
         combine launch; counted as one here)."""
-        return 11 * self.cfg["nl"] + 2 + (1 if self.cfg["sc_log"] else 0)
+        return 9 * self.cfg["nl"] + 3 + (1 if self.cfg["sc_log"] else 0)
 
 
 class _null:

@@ -87,6 +87,7 @@ SIGNATURES = {
                                          _int, ctypes.c_float, _int, _vp]),
     "gcu_dev_rmsnorm_residual": (_int, [_vp, _vp, _vp, _vp, ctypes.c_float, _int, _int, _vp]),
     "gcu_dev_softcap": (_int, [_vp, ctypes.c_long, ctypes.c_float, _vp]),
+    "gcu_dev_residual_norm_quantize": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_float, _int, _int, _vp]),
     "gcu_dev_qk_norm_rope_cache": (_int, [_vp, _vp, _vp, _vp, _vp, ctypes.c_long, _vp, _vp, ctypes.c_float, _vp,
                                           ctypes.c_float, _int, _int, _int, _int, _int, _vp]),
     "gcu_dev_patch_embed": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _int, _vp]),
@@ -472,3 +473,11 @@ def dev_rmsnorm_residual(x, y, resid, weight, eps, m, dim, stream=None):
 def dev_softcap(x, cap, stream=None):
     """gemma.c:4971-4976 on a CUDA tensor, in place."""
     _check(lib().gcu_dev_softcap(x.data_ptr(), x.numel(), cap, _stream(stream)), "dev_softcap")
+
+
+def dev_residual_norm_quantize(x, q, s, y, resid, w_post, w_next, eps, m, dim, stream=None):
+    """x = clamp(resid + rmsnorm(y, w_post)); q, s = quantize(rmsnorm(x, w_next)), one launch."""
+    _check(lib().gcu_dev_residual_norm_quantize(x.data_ptr(), q.data_ptr(), s.data_ptr(), y.data_ptr(),
+                                                resid.data_ptr(), w_post.data_ptr() if w_post is not None else None,
+                                                w_next.data_ptr(), eps, m, dim, _stream(stream)),
+           "dev_residual_norm_quantize")

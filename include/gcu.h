@@ -227,6 +227,15 @@ int gcu_dev_geglu_quantize(int8_t *q, float *s, float *out, const float *gate, c
  * be resid.  dim a multiple of 4, at most 4096. */
 int gcu_dev_rmsnorm_residual(float *x, const float *y, const float *resid, const float *weight,
                              float eps, int m, int dim, void *stream);
+/* The residual update fused with the next block's norm + quantize: x =
+ * clamp(resid + rmsnorm(y, w_post)) as gcu_dev_rmsnorm_residual, then the
+ * codes q (dense [m][dim]) and scales s of rmsnorm(x, w_next) as
+ * gcu_dev_rmsnorm_quantize -- one launch.  gemma.c runs the pair after the
+ * attention block (n2, then n3: gemma.c:4862-4910) and across a layer
+ * boundary (n4, then the next layer's n1: 4950-4962, 4754-4768). */
+int gcu_dev_residual_norm_quantize(float *x, int8_t *q, float *s, const float *y, const float *resid,
+                                   const float *w_post, const float *w_next, float eps, int m, int dim,
+                                   void *stream);
 /* gemma.c:4971-4976: x[i] = tanh(x[i] / cap) * cap (the final logit softcap). */
 int gcu_dev_softcap(float *x, long n, float cap, void *stream);
 
