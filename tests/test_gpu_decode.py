@@ -103,3 +103,58 @@ def test_rope_tables_follow_rope_freqs():
         slid, full = decode.rope_tables(cfg["hdim"], cfg["theta_l"], cfg["theta_g"], p)
         assert np.max(np.abs(slid - GOLD["gemma3_slid"][p])) <= 2e-6
         assert np.max(np.abs(full - GOLD["gemma3_full"][p])) <= 2e-6
+
+
+# ---- the residual / softcap kernels on their own
+
+import oracle as O  # noqa: E402
+
+
+def _d(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.mark.parametrize("m,dim", [(1, 1152), (3, 2560), (2, 96), (1, 4096)])
+def test_rmsnorm_residual(m, dim):
+    y, r = synth.normal(50 + dim, (m, dim)), synth.normal(51 + dim, (m, dim))
+    w = synth.normal(52 + dim, (dim,), 0.1)
+    x = torch.empty((m, dim), device="cuda")
+    gcu.dev_rmsnorm_residual(x, _d(y), _d(r), None, 1e-6, m, dim)  # no post-norm: an exact add
+    torch.cuda.synchronize()
+    assert np.array_equal(x.cpu().numpy(), y + r)
+    gcu.dev_rmsnorm_residual(x, _d(y), _d(r), _d(w), 1e-6, m, dim)
+    torch.cuda.synchronize()
+    y64 = y.astype(np.float64)
+    want = r + y64 / np.sqrt((y64 ** 2).mean(axis=1, keepdims=True) + 1e-6) * (w + 1.0)
+    assert np.max(np.abs(x.cpu().numpy() - want)) <= 1e-5 * np.max(np.abs(want))
+
+
+@pytest.mark.parametrize("m,dim,post", [(1, 1152, True), (2, 2560, False), (1, 96, True)])
+def test_residual_norm_quantize_equals_the_two_step_path(m, dim, post):
+    y, r = synth.normal(60 + dim, (m, dim)), synth.normal(61 + dim, (m, dim))
+    wp = synth.normal(62 + dim, (dim,), 0.1) if post else None
+    wn = synth.normal(63 + dim, (dim,), 0.1)
+    x1 = _d(r.copy())
+    q = torch.empty((m, dim), dtype=torch.int8, device="cuda")
+    s = torch.empty(m, device="cuda")
+    gcu.dev_residual_norm_quantize(x1, q, s, _d(y), x1, None if wp is None else _d(wp), _d(wn), 1e-6, m, dim)
+    x2 = _d(r.copy())
+    gcu.dev_rmsnorm_residual(x2, _d(y), x2, None if wp is None else _d(wp), 1e-6, m, dim)
+    torch.cuda.synchronize()
+    xg = x1.cpu().numpy()
+    assert np.array_equal(xg.view(np.uint32), x2.cpu().numpy().view(np.uint32))  # same residual update
+    _, qo, so = O.rmsnorm_quantize(xg, wn, 1e-6)
+    d = np.abs(q.cpu().numpy().astype(np.int32) - qo.astype(np.int32))
+    assert d.max() <= 1 and (d != 0).sum() <= max(2, d.size // 1000)
+    assert np.max(np.abs(s.cpu().numpy() - so)) <= 1e-6 * np.max(so)
+
+
+def test_softcap():
+    x = synth.normal(70, (5, 1000), 40.0)
+    t = _d(x)
+    gcu.dev_softcap(t, 30.0)
+    torch.cuda.synchronize()
+    want = np.tanh(x.astype(np.float64) / 30.0) * 30.0
+    assert np.max(np.abs(t.cpu().numpy() - want)) <= 1e-5 * 30.0
+    with pytest.raises(gcu.GcuError, match="zero cap"):
+        gcu.dev_softcap(t, 0.0)
