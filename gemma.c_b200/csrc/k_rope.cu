@@ -30,6 +30,11 @@ struct RopeArgs {
   const float *freqs;
   float q_scale;
   int n_heads, nkv, spos, ntok;
+  // token-major input (ld > 0): row t of the fused Q|K|V projection at
+  // qkv + t*ld, q heads first, then k, then v; rotated queries go to xq
+  // ([n_heads][ntok][hdim]).  ld == 0: head-major xq (in place), xk, xv.
+  const float *qkv;
+  long ld;
 };
 
 template <int HD>
@@ -44,7 +49,7 @@ __global__ void __launch_bounds__(kRopeThreads) k_qk_norm_rope_cache(RopeArgs a)
   if (row >= nq_rows + nk_rows) {  // a value row: straight into the cache
     const long r = row - nq_rows - nk_rows;
     const int h = (int)(r / a.ntok), t = (int)(r - (long)h * a.ntok);
-    const float *src = a.xv + r * HD + lane * P;
+    const float *src = (a.ld ? a.qkv + t * a.ld + (long)(a.n_heads + a.nkv + h) * HD : a.xv + r * HD) + lane * P;
     float *dst = a.vc + (size_t)h * a.kv_stride + (size_t)(a.spos + t) * HD + lane * P;
 #pragma unroll
     for (int i = 0; i < P; i += 2)
@@ -54,7 +59,8 @@ __global__ void __launch_bounds__(kRopeThreads) k_qk_norm_rope_cache(RopeArgs a)
   const bool isq = row < nq_rows;
   const long r = isq ? row : row - nq_rows;
   const int h = (int)(r / a.ntok), t = (int)(r - (long)h * a.ntok);
-  const float *src = (isq ? a.xq : a.xk) + r * HD + lane * P;
+  const float *src = (a.ld ? a.qkv + t * a.ld + (long)((isq ? 0 : a.n_heads) + h) * HD
+                           : (isq ? a.xq : a.xk) + r * HD) + lane * P;
   const float *w = isq ? a.nq : a.nk;
   float v[P];
 #pragma unroll
@@ -96,21 +102,25 @@ __global__ void __launch_bounds__(kRopeThreads) k_qk_norm_rope_cache(RopeArgs a)
 
 using namespace gcu;
 
-GCU_EXPORT int gcu_dev_qk_norm_rope_cache(float *xq, const float *xk, const float *xv, float *k_cache,
-                                          float *v_cache, long kv_stride, const float *nq, const float *nk,
-                                          float eps, const float *freqs, float q_scale, int n_heads, int nkv,
-                                          int hdim, int spos, int ntok, void *stream) {
+static int qk_norm_rope_cache(float *xq, const float *xk, const float *xv, const float *qkv, long ld, float *k_cache,
+                              float *v_cache, long kv_stride, const float *nq, const float *nk, float eps,
+                              const float *freqs, float q_scale, int n_heads, int nkv, int hdim, int spos, int ntok,
+                              void *stream) {
   if (ntok == 0) return 0;
-  if (!xq || !xk || !xv || !k_cache || !v_cache || !freqs) return set_error("qk_norm_rope_cache: null pointer");
+  if (!xq || (!ld && (!xk || !xv)) || (ld && !qkv) || !k_cache || !v_cache || !freqs)
+    return set_error("qk_norm_rope_cache: null pointer");
+  if (ld && (ld < (long)(n_heads + 2 * nkv) * hdim || ld % 2))
+    return set_error("qk_norm_rope_cache: row stride %ld below the %d fused q/k/v columns", ld,
+                     (n_heads + 2 * nkv) * hdim);
   if (hdim != 64 && hdim != 128 && hdim != 256)
     return set_error("qk_norm_rope_cache: head size %d (64, 128 or 256 supported)", hdim);
   if (n_heads < 1 || nkv < 1 || ntok < 0 || spos < 0 || kv_stride < (long)(spos + ntok) * hdim || kv_stride % 2)
     return set_error("qk_norm_rope_cache: chunk [%d, %d) outside a cache of %ld floats per head", spos, spos + ntok,
                      kv_stride);
-  const void *ptrs[] = {xq, xk, xv, k_cache, v_cache};
+  const void *ptrs[] = {xq, ld ? qkv : xk, ld ? qkv : xv, k_cache, v_cache};
   for (const void *p : ptrs)
     if ((uintptr_t)p % 8) return set_error("qk_norm_rope_cache: buffers must be 8-byte aligned");
-  RopeArgs a{xq, xk, xv, k_cache, v_cache, kv_stride, nq, nk, eps, freqs, q_scale, n_heads, nkv, spos, ntok};
+  RopeArgs a{xq, xk, xv, k_cache, v_cache, kv_stride, nq, nk, eps, freqs, q_scale, n_heads, nkv, spos, ntok, qkv, ld};
   const long rows = (long)(n_heads + 2 * nkv) * ntok;
   const dim3 grid((unsigned)((rows + kRopeThreads / 32 - 1) / (kRopeThreads / 32)));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -119,4 +129,20 @@ GCU_EXPORT int gcu_dev_qk_norm_rope_cache(float *xq, const float *xk, const floa
                                 : launch_k(k_qk_norm_rope_cache<64>, grid, dim3(kRopeThreads), 0, st, a);
   GCU_CUDA(e);
   return 0;
+}
+
+GCU_EXPORT int gcu_dev_qk_norm_rope_cache(float *xq, const float *xk, const float *xv, float *k_cache,
+                                          float *v_cache, long kv_stride, const float *nq, const float *nk,
+                                          float eps, const float *freqs, float q_scale, int n_heads, int nkv,
+                                          int hdim, int spos, int ntok, void *stream) {
+  return qk_norm_rope_cache(xq, xk, xv, nullptr, 0, k_cache, v_cache, kv_stride, nq, nk, eps, freqs, q_scale,
+                            n_heads, nkv, hdim, spos, ntok, stream);
+}
+
+GCU_EXPORT int gcu_dev_qkv_norm_rope_cache(float *xq, const float *qkv, long ld, float *k_cache, float *v_cache,
+                                           long kv_stride, const float *nq, const float *nk, float eps,
+                                           const float *freqs, float q_scale, int n_heads, int nkv, int hdim,
+                                           int spos, int ntok, void *stream) {
+  return qk_norm_rope_cache(xq, nullptr, nullptr, qkv, ld, k_cache, v_cache, kv_stride, nq, nk, eps, freqs, q_scale,
+                            n_heads, nkv, hdim, spos, ntok, stream);
 }

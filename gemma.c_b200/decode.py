@@ -1,4 +1,4 @@
-"""decode.py -- a device-resident W8A8 decode step through libgcu.so.
+"""decode.py -- device-resident W8A8 decode steps and prefill chunks through libgcu.so.
 
 `Decoder.step` runs gemma.c's forward_text_decode (gemma.c:4727-4978) for one
 token with every activation, weight and the KV cache in GPU memory, one C-ABI
@@ -19,6 +19,11 @@ call per step of the reference:
         next layer's rmsnorm(x, n1) + quantize gcu_dev_residual_norm_quantize
                                                (last layer: gcu_dev_rmsnorm_residual)
     final rmsnorm + quantize_act, lm_head gemv_int8, logit softcap
+
+`Decoder.prefill` runs gemma.c's forward_text_chunk (gemma.c:4985-5455) for
+a chunk of tokens the same way, with one GEMM over wq|wk|wv (the values of
+gemma.c's per-head GEMMs), the tensor-core GEMMs for the projections, and
+the causal attention kernel.
 
 Weights follow gemma.c's TextDecoder (gemma.c:1174-1301); torch only holds
 the device memory and the stream.  The RoPE tables are computed on the host
@@ -150,6 +155,99 @@ class Decoder:
         # gemma.c:4965-4976: final norm, tied lm_head, logit softcap
         gcu.dev_rmsnorm_quantize(q, self.s, self.x, self.fnorm, eps, 1, dim, out=self.x, stream=stream)
         gcu.dev_gemv_int8(self.logits, self.emb[0], self.emb[1], q, self.s, c["nvocab"], dim, stream=stream)
+        if c["sc_log"]:
+            gcu.dev_softcap(self.logits, c["sc_log"], stream=stream)
+
+    # ---- prefill ---------------------------------------------------------------
+    def _prefill_buffers(self, nmax: int):
+        torch = self.torch
+        c = self.cfg
+        if getattr(self, "_pmax", 0) >= nmax:
+            return
+        self._pmax = nmax
+        dim, mlp, hd = c["dim"], c["mlp_dim"], c["hdim"]
+        q_sz, kv_sz = c["n_heads"] * hd, c["nkv"] * hd
+        f32 = dict(dtype=torch.float32, device=self.dev)
+        i8 = dict(dtype=torch.int8, device=self.dev)
+        self.px = torch.empty((nmax, dim), **f32)           # residual stream, one row per token
+        self.pqkv = torch.empty((nmax, q_sz + 2 * kv_sz), **f32)
+        self.pxq = torch.empty(c["n_heads"] * nmax * hd, **f32)
+        self.pxo = torch.empty((nmax, q_sz), **f32)
+        self.pout = torch.empty((nmax, dim), **f32)
+        self.pxg = torch.empty((nmax, mlp), **f32)
+        self.pxu = torch.empty((nmax, mlp), **f32)
+        self.pq_dim = torch.empty((nmax, dim), **i8)
+        self.pq_qsz = torch.empty((nmax, q_sz), **i8)
+        self.pq_mlp = torch.empty((nmax, mlp), **i8)
+        self.ps = torch.empty(nmax, **f32)
+        self.pfreq = torch.empty((2, nmax, hd), **f32)        # sliding, full
+        if not hasattr(self, "wqkv"):
+            # one GEMM over wq|wk|wv: the same values as gemma.c's per-head GEMMs
+            self.wqkv = [(torch.cat([w["wq"][0], w["wk"][0], w["wv"][0]]).contiguous(),
+                          torch.cat([w["wq"][1], w["wk"][1], w["wv"][1]]).contiguous()) for w in self.L]
+
+    def set_prefill_freqs(self, slid, full):
+        """Upload the RoPE tables (ntok, hdim) of the chunk about to be prefilled."""
+        torch = self.torch
+        n = len(slid)
+        self._prefill_buffers(n)
+        self.pfreq[0, :n].copy_(torch.from_numpy(np.ascontiguousarray(slid, np.float32)))
+        self.pfreq[1, :n].copy_(torch.from_numpy(np.ascontiguousarray(full, np.float32)))
+
+    def prefill(self, spos: int, ntok: int, stream=None):
+        """gemma.c's forward_text_chunk (gemma.c:4985-5455) for the ntok input
+        embeddings in self.px[:ntok] at positions spos .. spos+ntok-1 (causal):
+        every layer, the final norm of every row (left in self.px) and the
+        last token's logits (self.logits).  set_prefill_freqs first."""
+        c = self.cfg
+        self._prefill_buffers(ntok)
+        dim, mlp, hd = c["dim"], c["mlp_dim"], c["hdim"]
+        nh, nkv = c["n_heads"], c["nkv"]
+        q_sz, kv_sz = nh * hd, nkv * hd
+        asc = float(np.float32(1.0) / np.sqrt(np.float32(c["q_scale"])))
+        eps = c["eps"]
+        n = ntok
+        px, ps, pout = self.px[:n], self.ps[:n], self.pout[:n]
+        q_dim, q_qsz, q_mlp = self.pq_dim[:n], self.pq_qsz[:n], self.pq_mlp[:n]
+        xq = self.pxq[:nh * n * hd].view(nh, n, hd)
+        nl = len(self.L)
+        # gemma.c:5019-5034: the first layer's rmsnorm(x, n1) -> quantize_acts
+        gcu.dev_rmsnorm_quantize(q_dim, ps, px, self.L[0]["n1"], eps, n, dim, stream=stream)
+        for l, w in enumerate(self.L):
+            # gemma.c:5036-5091: q, k, v of every token (one fused GEMM)
+            gcu.dev_gemm_int8(self.pqkv[:n], self.wqkv[l][0], self.wqkv[l][1], q_dim, ps, n, q_sz + 2 * kv_sz, dim,
+                              stream=stream)
+            # gemma.c:5095-5145: QK norm, RoPE (queries scaled), cache write
+            kc, vc = self.kv[l, 0], self.kv[l, 1]
+            sliding = bool(c["swa"][l])
+            gcu.dev_qkv_norm_rope_cache(xq, self.pqkv[:n], kc, vc, self.pfreq[0 if sliding else 1, :n], spos, nh,
+                                        asc, w["nq"] if c["qk_norm"] else None, w["nk"] if c["qk_norm"] else None,
+                                        eps, stream=stream)
+            # gemma.c:5160-5295: causal attention, sliding window on local layers
+            gcu.dev_attention_prefill(self.pxo[:n], xq, kc, vc, spos, c["slide"] if sliding else 0, c["sc_att"],
+                                      True, stream=stream)
+            # gemma.c:5296-5340: O projection, post-attention norm + residual,
+            # pre-FFN norm + quantize
+            gcu.dev_quantize_gemm_int8_multi([(w["wo"][0], w["wo"][1], pout)], q_qsz, ps, self.pxo[:n], n, q_sz,
+                                             stream=stream)
+            gcu.dev_residual_norm_quantize(px, q_dim, ps, pout, px, w["n2"] if c["mlp_pre"] else None,
+                                           w["n3"] if c["mlp_pre"] else w["n2"], eps, n, dim, stream=stream)
+            # gemma.c:5357-5392: gate/up, GeGLU + quantize, down
+            gcu.dev_gemm_int8_multi([(w["w2"][0], w["w2"][1], self.pxg[:n]), (w["w1"][0], w["w1"][1], self.pxu[:n])],
+                                    q_dim, ps, n, dim, stream=stream)
+            gcu.dev_geglu_quantize(q_mlp, ps, self.pxg[:n], self.pxu[:n], n, mlp, stream=stream)
+            gcu.dev_gemm_int8(pout, w["w3"][0], w["w3"][1], q_mlp, ps, n, dim, mlp, stream=stream)
+            # gemma.c:5399-5418: post-FFN norm + residual (+ the next layer's input norm)
+            post = w["n4"] if c["mlp_pst"] else None
+            if l + 1 < nl:
+                gcu.dev_residual_norm_quantize(px, q_dim, ps, pout, px, post, self.L[l + 1]["n1"], eps, n, dim,
+                                               stream=stream)
+            else:
+                gcu.dev_rmsnorm_residual(px, pout, px, post, eps, n, dim, stream=stream)
+        # gemma.c:5420-5450: final norm of every row, the last token's logits
+        gcu.dev_rmsnorm_quantize(q_dim, ps, px, self.fnorm, eps, n, dim, out=px, stream=stream)
+        gcu.dev_gemv_int8(self.logits, self.emb[0], self.emb[1], q_dim[n - 1:n], ps[n - 1:n], c["nvocab"], dim,
+                          stream=stream)
         if c["sc_log"]:
             gcu.dev_softcap(self.logits, c["sc_log"], stream=stream)
 

@@ -90,6 +90,8 @@ SIGNATURES = {
     "gcu_dev_residual_norm_quantize": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_float, _int, _int, _vp]),
     "gcu_dev_qk_norm_rope_cache": (_int, [_vp, _vp, _vp, _vp, _vp, ctypes.c_long, _vp, _vp, ctypes.c_float, _vp,
                                           ctypes.c_float, _int, _int, _int, _int, _int, _vp]),
+    "gcu_dev_qkv_norm_rope_cache": (_int, [_vp, _vp, ctypes.c_long, _vp, _vp, ctypes.c_long, _vp, _vp, ctypes.c_float,
+                                           _vp, ctypes.c_float, _int, _int, _int, _int, _int, _vp]),
     "gcu_dev_patch_embed": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _int, _vp]),
     "gcu_dev_vision_pool_quantize": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_float, _int, _int, _int,
                                             _vp]),
@@ -481,3 +483,17 @@ def dev_residual_norm_quantize(x, q, s, y, resid, w_post, w_next, eps, m, dim, s
                                                 resid.data_ptr(), w_post.data_ptr() if w_post is not None else None,
                                                 w_next.data_ptr(), eps, m, dim, _stream(stream)),
            "dev_residual_norm_quantize")
+
+
+def dev_qkv_norm_rope_cache(xq, qkv, kc, vc, freqs, spos, n_heads, q_scale=1.0, nq=None, nk=None, eps=1e-6,
+                            stream=None):
+    """Token-major variant: qkv (ntok, >= (n_heads+2*nkv)*hdim) rows of the fused
+    projection; rotated queries to xq (n_heads, ntok, hdim), keys/values to the
+    caches kc, vc (nkv, clen, hdim)."""
+    nkv, clen, hdim = kc.shape
+    ntok = qkv.shape[0]
+    _check(lib().gcu_dev_qkv_norm_rope_cache(xq.data_ptr(), qkv.data_ptr(), qkv.stride(0), kc.data_ptr(),
+                                             vc.data_ptr(), clen * hdim, nq.data_ptr() if nq is not None else None,
+                                             nk.data_ptr() if nk is not None else None, eps, freqs.data_ptr(),
+                                             q_scale, n_heads, nkv, hdim, spos, ntok, _stream(stream)),
+           "dev_qkv_norm_rope_cache")

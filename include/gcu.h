@@ -260,6 +260,15 @@ int gcu_dev_qk_norm_rope_cache(float *xq, const float *xk, const float *xv, floa
                                float *v_cache, long kv_stride, const float *nq, const float *nk,
                                float eps, const float *freqs, float q_scale, int n_heads, int nkv,
                                int hdim, int spos, int ntok, void *stream);
+/* The same step on the fused projection of a prefill chunk: row t of qkv
+ * (row stride ld floats) holds the token's query heads, then its key heads,
+ * then its value heads (one GEMM over wq|wk|wv gives exactly the values of
+ * gemma.c's per-head GEMMs, gemma.c:5045-5091); the rotated queries go to xq
+ * [n_heads][ntok][hdim], the rotated keys and the values to the cache. */
+int gcu_dev_qkv_norm_rope_cache(float *xq, const float *qkv, long ld, float *k_cache, float *v_cache,
+                                long kv_stride, const float *nq, const float *nk, float eps,
+                                const float *freqs, float q_scale, int n_heads, int nkv, int hdim,
+                                int spos, int ntok, void *stream);
 /* gemma.c:4836-4848 (att_scores_gqa, att_finalize, att_values_gqa): one
  * decode step of one layer.  xq [n_heads][hdim] (normed and rotated), the
  * window [spos, spos+attlen) of the cache, scores scaled by asc

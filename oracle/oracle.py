@@ -369,11 +369,15 @@ def ref(variant: str | None = None) -> ctypes.CDLL | None:
         lib.ref_qk_norm_rope_cache.restype = None
         lib.ref_qk_norm_rope_cache.argtypes = [_f32p, _f32p, _f32p, _f32p, _f32p, ctypes.c_long, _f32p, _f32p,
                                                ctypes.c_float, _f32p, ctypes.c_float] + [ctypes.c_int] * 5
+    _model_args = [ctypes.POINTER(ctypes.c_int)] + [ctypes.c_int] * 3 + [ctypes.c_float] * 5 + \
+        [ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p), _i8p, _f32p, _f32p, ctypes.c_int]
     if hasattr(lib, "ref_decode_steps"):
         lib.ref_decode_steps.restype = ctypes.c_int
-        lib.ref_decode_steps.argtypes = [_f32p, _f32p, _f32p] + [ctypes.c_int] * 10 + \
-            [ctypes.POINTER(ctypes.c_int)] + [ctypes.c_int] * 3 + [ctypes.c_float] * 5 + \
-            [ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p), _i8p, _f32p, _f32p, ctypes.c_int]
+        lib.ref_decode_steps.argtypes = [_f32p, _f32p, _f32p] + [ctypes.c_int] * 10 + _model_args
+    if hasattr(lib, "ref_prefill_chunks"):
+        lib.ref_prefill_chunks.restype = ctypes.c_int
+        lib.ref_prefill_chunks.argtypes = [_f32p, _f32p, _f32p, ctypes.POINTER(ctypes.c_int)] + \
+            [ctypes.c_int] * 10 + _model_args
     if hasattr(lib, "ref_read_model_seconds"):
         lib.ref_read_model_seconds.restype = ctypes.c_double
         lib.ref_read_model_seconds.argtypes = [ctypes.c_char_p, ctypes.c_int]
@@ -484,12 +488,8 @@ class Ref:
                                         n_heads, kc.shape[0], hdim, spos, ntok)
         return xq, kc, vc
 
-    def decode_steps(self, cfg: dict, layers: list, emb, fnorm, x0):
-        """gemma.c's forward_text_decode for positions 0 .. len(x0)-1 on a
-        decoder built from synth.decoder_model-style tensors; returns the
-        logits (npos, nvocab) and final hidden states (npos, dim)."""
-        x0 = np.ascontiguousarray(x0, np.float32)
-        npos, dim = x0.shape
+    def _model(self, cfg, layers, emb, fnorm):
+        """ctypes arguments describing a decoder (and the arrays they point into)."""
         keep = []
         qt = (ctypes.c_void_p * (14 * cfg["nl"]))()
         nrm = (ctypes.c_void_p * (6 * cfg["nl"]))()
@@ -505,16 +505,44 @@ class Ref:
         swa = (ctypes.c_int * cfg["nl"])(*[int(b) for b in cfg["swa"]])
         eq, es = np.ascontiguousarray(emb[0], np.int8), np.ascontiguousarray(emb[1], np.float32)
         fn = np.ascontiguousarray(fnorm, np.float32)
+        keep += [eq, es, fn, swa]
+        dims = [cfg["nl"], cfg["n_heads"], cfg["nkv"], cfg["hdim"], cfg["dim"], cfg["mlp_dim"], cfg["nvocab"],
+                cfg["q_scale"], cfg["slide"]]
+        rest = [swa, int(cfg["qk_norm"]), int(cfg["mlp_pre"]), int(cfg["mlp_pst"]), cfg["theta_l"], cfg["theta_g"],
+                cfg["eps"], cfg["sc_att"], cfg["sc_log"], qt, nrm, _ptr(eq, _i8p), _ptr(es, _f32p), _ptr(fn, _f32p),
+                self.threads]
+        return dims, rest, keep
+
+    def decode_steps(self, cfg: dict, layers: list, emb, fnorm, x0):
+        """gemma.c's forward_text_decode for positions 0 .. len(x0)-1 on a
+        decoder built from synth.decoder_model-style tensors; returns the
+        logits (npos, nvocab) and final hidden states (npos, dim)."""
+        x0 = np.ascontiguousarray(x0, np.float32)
+        npos = x0.shape[0]
+        dims, rest, keep = self._model(cfg, layers, emb, fnorm)
         logits = np.empty((npos, cfg["nvocab"]), np.float32)
-        hid = np.empty((npos, dim), np.float32)
-        rc = self.lib.ref_decode_steps(_ptr(logits, _f32p), _ptr(hid, _f32p), _ptr(x0, _f32p), npos, cfg["nl"],
-                                       cfg["n_heads"], cfg["nkv"], cfg["hdim"], dim, cfg["mlp_dim"], cfg["nvocab"],
-                                       cfg["q_scale"], cfg["slide"], swa, int(cfg["qk_norm"]), int(cfg["mlp_pre"]),
-                                       int(cfg["mlp_pst"]), cfg["theta_l"], cfg["theta_g"], cfg["eps"], cfg["sc_att"],
-                                       cfg["sc_log"], qt, nrm, _ptr(eq, _i8p), _ptr(es, _f32p), _ptr(fn, _f32p),
-                                       self.threads)
+        hid = np.empty((npos, cfg["dim"]), np.float32)
+        rc = self.lib.ref_decode_steps(_ptr(logits, _f32p), _ptr(hid, _f32p), _ptr(x0, _f32p), npos, *dims, *rest)
+        del keep
         if rc:
             raise RuntimeError("reference forward_text_decode failed")
+        return logits, hid
+
+    def prefill_chunks(self, cfg: dict, layers: list, emb, fnorm, x0, chunks):
+        """gemma.c's forward_text_chunk over consecutive chunks from position
+        0; returns each chunk's last-token logits (len(chunks), nvocab) and
+        every token's final hidden state (sum(chunks), dim)."""
+        x0 = np.ascontiguousarray(x0, np.float32)
+        assert x0.shape[0] == sum(chunks)
+        dims, rest, keep = self._model(cfg, layers, emb, fnorm)
+        ch = (ctypes.c_int * len(chunks))(*chunks)
+        logits = np.empty((len(chunks), cfg["nvocab"]), np.float32)
+        hid = np.empty((x0.shape[0], cfg["dim"]), np.float32)
+        rc = self.lib.ref_prefill_chunks(_ptr(logits, _f32p), _ptr(hid, _f32p), _ptr(x0, _f32p), ch, len(chunks), *dims,
+                                         *rest)
+        del keep
+        if rc:
+            raise RuntimeError("reference forward_text_chunk failed")
         return logits, hid
 
     def vision_head(self, v: dict):

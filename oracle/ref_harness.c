@@ -351,128 +351,198 @@ void ref_qk_norm_rope_cache(float *xq, float *xk, const float *xv, float *kc, fl
   }
 }
 
-/* gemma.c:4727-4978 forward_text_decode, the reference's whole decode step,
- * on a W8A8 text decoder built from the given tensors: npos steps at
- * positions 0 .. npos-1, step p's input embedding x0[p] placed in tb->x as
- * its caller does (gemma.c:5470-5490).  Outputs per step: the logits
- * (after the optional softcap) and the final hidden state (after the final
- * RMSNorm).  qt: 14 pointers per layer (wq, wk, wv, wo, w1 = up, w2 = gate,
- * w3 = down; int8 values then fp32 scales each); nrm: 6 per layer (n1, n2,
- * n3, n4, nq, nk); swa: sliding-window flag per layer. */
-int ref_decode_steps(float *logits, float *hid, const float *x0, int npos, int nl, int n_heads, int nkv,
-                     int hdim, int dim, int mlp_dim, int nvocab, int q_scale, int slide, const int *swa,
-                     int qk_norm, int mlp_pre, int mlp_pst, float theta_l, float theta_g, float eps, float sc_att,
-                     float sc_log, void *const *qt, float *const *nrm, const int8_t *emb_q, const float *emb_s,
-                     const float *fnorm, int threads) {
+/* A W8A8 text decoder (gemma.c:1174-1301) around caller-owned tensors, and
+ * a TextBuffer (gemma.c:2241-2273) for chunks of up to ntok tokens. */
+typedef struct {
   TextConfig tc;
-  memset(&tc, 0, sizeof(tc));
-  tc.nl = (uint8_t)nl;
-  tc.n_heads = (uint8_t)n_heads;
-  tc.nkv = (uint8_t)nkv;
-  tc.hdim = (uint16_t)hdim;
-  tc.dim = (uint16_t)dim;
-  tc.mlp_dim = (uint16_t)mlp_dim;
-  tc.q_scale = (uint16_t)q_scale;
-  tc.slide = (uint16_t)slide;
-  tc.max_seq = (uint32_t)npos;
-  tc.nvocab = (uint32_t)nvocab;
-  tc.theta_l = theta_l;
-  tc.theta_g = theta_g;
-  tc.eps = eps;
-  tc.sc_att = sc_att;
-  tc.sc_log = sc_log;
-  tc.qk_norm = qk_norm != 0;
-  tc.mlp_pre = mlp_pre != 0;
-  tc.mlp_pst = mlp_pst != 0;
-  bool *flags = calloc((size_t)nl, sizeof(bool));
-  QTensor *qts = calloc((size_t)nl * 7 + 1, sizeof(QTensor));
-  TextDecoderLayer *lay = calloc((size_t)nl, sizeof(TextDecoderLayer));
-  TextDecoderLayer **lp = calloc((size_t)nl, sizeof(TextDecoderLayer *));
-  const int q_sz = n_heads * hdim, kv_sz = nkv * hdim;
-  TextBuffer tb;
-  memset(&tb, 0, sizeof(tb));
-  tb.clen = npos;
-  tb.x_i8 = malloc((size_t)(mlp_dim > dim ? mlp_dim : dim) + q_sz);
-  tb.xo_i8 = malloc((size_t)q_sz);
-  tb.xg_i8 = malloc((size_t)mlp_dim);
-  tb.cs_slid = malloc((size_t)hdim * sizeof(float));
-  tb.cs_full = malloc((size_t)hdim * sizeof(float));
-  tb.x = malloc((size_t)dim * sizeof(float));
-  tb.resid = malloc((size_t)dim * sizeof(float));
-  tb.xq = malloc((size_t)q_sz * sizeof(float));
-  tb.xk = malloc((size_t)kv_sz * sizeof(float));
-  tb.xv = malloc((size_t)kv_sz * sizeof(float));
-  tb.xo = malloc((size_t)q_sz * sizeof(float));
-  tb.att = malloc((size_t)n_heads * npos * sizeof(float));
-  tb.kvc = calloc((size_t)nl * 2 * npos * kv_sz, sizeof(float));
-  tb.xg = malloc((size_t)mlp_dim * sizeof(float));
-  tb.xu = malloc((size_t)mlp_dim * sizeof(float));
-  tb.logits = malloc((size_t)nvocab * sizeof(float));
-  int rc = 1;
-  if (!flags || !qts || !lay || !lp || !tb.x_i8 || !tb.xo_i8 || !tb.xg_i8 || !tb.cs_slid || !tb.cs_full || !tb.x ||
-      !tb.resid || !tb.xq || !tb.xk || !tb.xv || !tb.xo || !tb.att || !tb.kvc || !tb.xg || !tb.xu || !tb.logits)
-    goto done;
+  bool *flags;
+  QTensor *qts;
+  TextDecoderLayer *lay;
+  TextDecoderLayer **lp;
+  TextDecoder dec;
+} RefDecoder;
+
+static void ref_free_decoder(RefDecoder *m) {
+  free(m->flags);
+  free(m->qts);
+  free(m->lay);
+  free(m->lp);
+}
+
+/* qt: 14 pointers per layer (wq, wk, wv, wo, w1 = up, w2 = gate, w3 = down;
+ * int8 values then fp32 scales each); nrm: 6 per layer (n1, n2, n3, n4, nq,
+ * nk); swa: the sliding-window flag per layer. */
+static int ref_build_decoder(RefDecoder *m, int nl, int n_heads, int nkv, int hdim, int dim, int mlp_dim,
+                             int nvocab, int q_scale, int slide, int max_seq, const int *swa, int qk_norm,
+                             int mlp_pre, int mlp_pst, float theta_l, float theta_g, float eps, float sc_att,
+                             float sc_log, void *const *qt, float *const *nrm, const int8_t *emb_q,
+                             const float *emb_s, const float *fnorm) {
+  memset(m, 0, sizeof(*m));
+  TextConfig *tc = &m->tc;
+  tc->nl = (uint8_t)nl;
+  tc->n_heads = (uint8_t)n_heads;
+  tc->nkv = (uint8_t)nkv;
+  tc->hdim = (uint16_t)hdim;
+  tc->dim = (uint16_t)dim;
+  tc->mlp_dim = (uint16_t)mlp_dim;
+  tc->q_scale = (uint16_t)q_scale;
+  tc->slide = (uint16_t)slide;
+  tc->max_seq = (uint32_t)max_seq;
+  tc->nvocab = (uint32_t)nvocab;
+  tc->theta_l = theta_l;
+  tc->theta_g = theta_g;
+  tc->eps = eps;
+  tc->sc_att = sc_att;
+  tc->sc_log = sc_log;
+  tc->qk_norm = qk_norm != 0;
+  tc->mlp_pre = mlp_pre != 0;
+  tc->mlp_pst = mlp_pst != 0;
+  m->flags = calloc((size_t)nl, sizeof(bool));
+  m->qts = calloc((size_t)nl * 7 + 1, sizeof(QTensor));
+  m->lay = calloc((size_t)nl, sizeof(TextDecoderLayer));
+  m->lp = calloc((size_t)nl, sizeof(TextDecoderLayer *));
+  if (!m->flags || !m->qts || !m->lay || !m->lp) return 1;
   for (int l = 0; l < nl; l++) {
-    flags[l] = swa[l] != 0;
-    QTensor *t = qts + (size_t)l * 7;
+    m->flags[l] = swa[l] != 0;
+    QTensor *t = m->qts + (size_t)l * 7;
     for (int j = 0; j < 7; j++) {
       t[j].quant = true;
       t[j].i8.q = (int8_t *)qt[(size_t)l * 14 + 2 * j];
       t[j].i8.scales = (floatx *)qt[(size_t)l * 14 + 2 * j + 1];
     }
-    lay[l].wq = t + 0;
-    lay[l].wk = t + 1;
-    lay[l].wv = t + 2;
-    lay[l].wo = t + 3;
-    lay[l].w1 = t + 4;
-    lay[l].w2 = t + 5;
-    lay[l].w3 = t + 6;
-    lay[l].n1 = nrm[(size_t)l * 6 + 0];
-    lay[l].n2 = nrm[(size_t)l * 6 + 1];
-    lay[l].n3 = nrm[(size_t)l * 6 + 2];
-    lay[l].n4 = nrm[(size_t)l * 6 + 3];
-    lay[l].nq = nrm[(size_t)l * 6 + 4];
-    lay[l].nk = nrm[(size_t)l * 6 + 5];
-    lp[l] = lay + l;
+    TextDecoderLayer *L = m->lay + l;
+    L->wq = t + 0;
+    L->wk = t + 1;
+    L->wv = t + 2;
+    L->wo = t + 3;
+    L->w1 = t + 4;
+    L->w2 = t + 5;
+    L->w3 = t + 6;
+    L->n1 = nrm[(size_t)l * 6 + 0];
+    L->n2 = nrm[(size_t)l * 6 + 1];
+    L->n3 = nrm[(size_t)l * 6 + 2];
+    L->n4 = nrm[(size_t)l * 6 + 3];
+    L->nq = nrm[(size_t)l * 6 + 4];
+    L->nk = nrm[(size_t)l * 6 + 5];
+    m->lp[l] = L;
   }
-  tc.swa = flags;
-  QTensor *emb = qts + (size_t)nl * 7;
+  tc->swa = m->flags;
+  QTensor *emb = m->qts + (size_t)nl * 7;
   emb->quant = true;
   emb->i8.q = (int8_t *)emb_q;
   emb->i8.scales = (floatx *)emb_s;
-  TextDecoder dec;
-  memset(&dec, 0, sizeof(dec));
-  dec.config = &tc;
-  dec.emb = emb;
-  dec.layers = lp;
-  dec.fnorm = (floatx *)fnorm;
-  rc = 0;
+  m->dec.config = tc;
+  m->dec.emb = emb;
+  m->dec.layers = m->lp;
+  m->dec.fnorm = (floatx *)fnorm;
+  return 0;
+}
+
+static void ref_free_tb(TextBuffer *tb) {
+  free(tb->x_i8);
+  free(tb->xsc);
+  free(tb->xo_i8);
+  free(tb->xosc);
+  free(tb->xg_i8);
+  free(tb->xgsc);
+  free(tb->cs_slid);
+  free(tb->cs_full);
+  free(tb->x);
+  free(tb->resid);
+  free(tb->xq);
+  free(tb->xk);
+  free(tb->xv);
+  free(tb->xo);
+  free(tb->att);
+  free(tb->kvc);
+  free(tb->xg);
+  free(tb->xu);
+  free(tb->logits);
+}
+
+static int ref_alloc_tb(TextBuffer *tb, const TextConfig *tc, int ntok, int clen) {
+  memset(tb, 0, sizeof(*tb));
+  const size_t dim = tc->dim, mlp = tc->mlp_dim, q_sz = (size_t)tc->n_heads * tc->hdim,
+               kv_sz = (size_t)tc->nkv * tc->hdim, n = (size_t)ntok;
+  tb->clen = clen;
+  tb->x_i8 = malloc(n * (dim > q_sz ? dim : q_sz));
+  tb->xsc = malloc(n * sizeof(float));
+  tb->xo_i8 = malloc(n * q_sz);
+  tb->xosc = malloc(n * sizeof(float));
+  tb->xg_i8 = malloc(n * mlp);
+  tb->xgsc = malloc(n * sizeof(float));
+  tb->cs_slid = malloc(n * tc->hdim * sizeof(float));
+  tb->cs_full = malloc(n * tc->hdim * sizeof(float));
+  tb->x = malloc(n * dim * sizeof(float));
+  tb->resid = malloc(n * dim * sizeof(float));
+  tb->xq = malloc(n * q_sz * sizeof(float));
+  tb->xk = malloc(n * kv_sz * sizeof(float));
+  tb->xv = malloc(n * kv_sz * sizeof(float));
+  tb->xo = malloc(n * q_sz * sizeof(float));
+  tb->att = malloc((size_t)tc->n_heads * n * clen * sizeof(float));
+  tb->kvc = calloc((size_t)tc->nl * 2 * clen * kv_sz, sizeof(float));
+  tb->xg = malloc(n * mlp * sizeof(float));
+  tb->xu = malloc(n * mlp * sizeof(float));
+  tb->logits = malloc((size_t)tc->nvocab * sizeof(float));
+  return !(tb->x_i8 && tb->xsc && tb->xo_i8 && tb->xosc && tb->xg_i8 && tb->xgsc && tb->cs_slid && tb->cs_full &&
+           tb->x && tb->resid && tb->xq && tb->xk && tb->xv && tb->xo && tb->att && tb->kvc && tb->xg && tb->xu &&
+           tb->logits);
+}
+
+/* gemma.c:4727-4978 forward_text_decode, the reference's whole decode step,
+ * on a decoder built from the given tensors: npos steps at positions
+ * 0 .. npos-1, step p's input embedding x0[p] placed in tb->x as its caller
+ * does (gemma.c:5470-5490).  Outputs per step: the logits (after the
+ * optional softcap) and the final hidden state (after the final RMSNorm). */
+int ref_decode_steps(float *logits, float *hid, const float *x0, int npos, int nl, int n_heads, int nkv,
+                     int hdim, int dim, int mlp_dim, int nvocab, int q_scale, int slide, const int *swa,
+                     int qk_norm, int mlp_pre, int mlp_pst, float theta_l, float theta_g, float eps, float sc_att,
+                     float sc_log, void *const *qt, float *const *nrm, const int8_t *emb_q, const float *emb_s,
+                     const float *fnorm, int threads) {
+  RefDecoder m;
+  TextBuffer tb;
+  int rc = ref_build_decoder(&m, nl, n_heads, nkv, hdim, dim, mlp_dim, nvocab, q_scale, slide, npos, swa, qk_norm,
+                             mlp_pre, mlp_pst, theta_l, theta_g, eps, sc_att, sc_log, qt, nrm, emb_q, emb_s, fnorm);
+  rc = rc || ref_alloc_tb(&tb, &m.tc, 1, npos);
   for (int p = 0; p < npos && rc == 0; p++) {
     memcpy(tb.x, x0 + (size_t)p * dim, (size_t)dim * sizeof(float));
-    rc = forward_text_decode(&dec, &tb, p, true, true, threads, NULL);
+    rc = forward_text_decode(&m.dec, &tb, p, true, true, threads, NULL);
     memcpy(logits + (size_t)p * nvocab, tb.logits, (size_t)nvocab * sizeof(float));
     memcpy(hid + (size_t)p * dim, tb.x, (size_t)dim * sizeof(float));
   }
-done:
-  free(flags);
-  free(qts);
-  free(lay);
-  free(lp);
-  free(tb.x_i8);
-  free(tb.xo_i8);
-  free(tb.xg_i8);
-  free(tb.cs_slid);
-  free(tb.cs_full);
-  free(tb.x);
-  free(tb.resid);
-  free(tb.xq);
-  free(tb.xk);
-  free(tb.xv);
-  free(tb.xo);
-  free(tb.att);
-  free(tb.kvc);
-  free(tb.xg);
-  free(tb.xu);
-  free(tb.logits);
+  ref_free_tb(&tb);
+  ref_free_decoder(&m);
+  return rc;
+}
+
+/* gemma.c:4985-5455 forward_text_chunk, the reference's prefill of a chunk,
+ * on the same kind of decoder: chunks[c] tokens at a time from position 0
+ * (causal mask, as prompt processing calls it), chunk c's input embeddings
+ * the next chunks[c] rows of x0.  Outputs: each chunk's last-token logits,
+ * and every token's final hidden state (after the final RMSNorm). */
+int ref_prefill_chunks(float *logits, float *hid, const float *x0, const int *chunks, int nchunks, int nl,
+                       int n_heads, int nkv, int hdim, int dim, int mlp_dim, int nvocab, int q_scale, int slide,
+                       const int *swa, int qk_norm, int mlp_pre, int mlp_pst, float theta_l, float theta_g,
+                       float eps, float sc_att, float sc_log, void *const *qt, float *const *nrm,
+                       const int8_t *emb_q, const float *emb_s, const float *fnorm, int threads) {
+  int total = 0, maxc = 1;
+  for (int c = 0; c < nchunks; c++) {
+    total += chunks[c];
+    maxc = chunks[c] > maxc ? chunks[c] : maxc;
+  }
+  RefDecoder m;
+  TextBuffer tb;
+  int rc = ref_build_decoder(&m, nl, n_heads, nkv, hdim, dim, mlp_dim, nvocab, q_scale, slide, total, swa,
+                             qk_norm, mlp_pre, mlp_pst, theta_l, theta_g, eps, sc_att, sc_log, qt, nrm, emb_q,
+                             emb_s, fnorm);
+  rc = rc || ref_alloc_tb(&tb, &m.tc, maxc, total);
+  for (int c = 0, spos = 0; c < nchunks && rc == 0; spos += chunks[c], c++) {
+    memcpy(tb.x, x0 + (size_t)spos * dim, (size_t)chunks[c] * dim * sizeof(float));
+    rc = forward_text_chunk(&m.dec, &tb, spos, chunks[c], true, true, true, threads, NULL);
+    memcpy(logits + (size_t)c * nvocab, tb.logits, (size_t)nvocab * sizeof(float));
+    memcpy(hid + (size_t)spos * dim, tb.x, (size_t)chunks[c] * dim * sizeof(float));
+  }
+  ref_free_tb(&tb);
+  ref_free_decoder(&m);
   return rc;
 }

@@ -2,8 +2,9 @@
 
 gemma.c's forward_text_decode (gemma.c:4727-4978) runs, through
 oracle/ref_harness.c's ref_decode_steps, on small seeded W8A8 decoders
-(synth.decoder_model) for positions 0..7 with seeded input embeddings.  The
-fixture keeps every step's logits and final hidden state, and the RoPE
+(synth.decoder_model) for positions 0..7 with seeded input embeddings, and
+its forward_text_chunk (gemma.c:4985-5455) over chunks of 5 and 11 tokens.
+The fixture keeps every step's logits and final hidden state, and the RoPE
 tables gemma.c's rope_freqs builds for each position, so the GPU decoder can
 be fed the same angles.  Needs the reference sources (run where they are
 mounted):
@@ -27,6 +28,7 @@ import oracle  # noqa: E402
 import synth  # noqa: E402
 
 NPOS = 8
+CHUNKS = [5, 11]  # forward_text_chunk calls from position 0
 CASES = {
     # Gemma 3 style: QK norm, pre/post norms, a sliding layer (window 4) and a global one
     "gemma3": dict(tid=1000, nl=2, n_heads=2, nkv=1, hdim=64, dim=128, mlp_dim=256, nvocab=500, q_scale=64,
@@ -43,7 +45,7 @@ def main() -> None:
     if not oracle.build_ref():
         raise SystemExit("reference sources not found; cannot generate fixtures")
     R = oracle.Ref("native", threads=2)
-    out = {"meta": np.array(json.dumps({"cases": CASES, "npos": NPOS, "isa": R.isa}))}
+    out = {"meta": np.array(json.dumps({"cases": CASES, "npos": NPOS, "chunks": CHUNKS, "isa": R.isa}))}
     for name, cfg in CASES.items():
         layers, emb, fnorm = synth.decoder_model(cfg["tid"], cfg)
         x0 = synth.normal(cfg["tid"] + 999, (NPOS, cfg["dim"]))
@@ -54,6 +56,12 @@ def main() -> None:
             s, f = R.rope_freqs(cfg["hdim"], cfg["theta_l"], cfg["theta_g"], p, 1)
             slid[p], full[p] = s[0], f[0]
         out.update({f"{name}_logits": logits, f"{name}_hid": hid, f"{name}_slid": slid, f"{name}_full": full})
+        # prefill: the same decoder over chunks of CHUNKS tokens
+        total = sum(CHUNKS)
+        xp = synth.normal(cfg["tid"] + 777, (total, cfg["dim"]))
+        plog, phid = R.prefill_chunks(cfg, layers, emb, fnorm, xp, CHUNKS)
+        ps, pf = R.rope_freqs(cfg["hdim"], cfg["theta_l"], cfg["theta_g"], 0, total)
+        out.update({f"{name}_pre_logits": plog, f"{name}_pre_hid": phid, f"{name}_pslid": ps, f"{name}_pfull": pf})
     np.savez_compressed(os.path.join(HERE, "decode.npz"), **out)
     print(f"{len(CASES)} decoders x {NPOS} positions")
 

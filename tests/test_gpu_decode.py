@@ -158,3 +158,55 @@ def test_softcap():
     assert np.max(np.abs(t.cpu().numpy() - want)) <= 1e-5 * 30.0
     with pytest.raises(gcu.GcuError, match="zero cap"):
         gcu.dev_softcap(t, 0.0)
+
+
+@pytest.mark.parametrize("name", list(META["cases"]))
+def test_prefill_chunks_match_reference(name):
+    # forward_text_chunk over chunks of 5 and 11 tokens, the KV cache carried
+    # from the first chunk to the second
+    cfg = META["cases"][name]
+    layers, emb, fnorm = synth.decoder_model(cfg["tid"], cfg)
+    chunks = META["chunks"]
+    total = sum(chunks)
+    xp = synth.normal(cfg["tid"] + 777, (total, cfg["dim"]))
+    dec = decode.Decoder(cfg, layers, emb, fnorm, clen=total)
+    spos = 0
+    for c, n in enumerate(chunks):
+        dec.set_prefill_freqs(GOLD[f"{name}_pslid"][spos:spos + n], GOLD[f"{name}_pfull"][spos:spos + n])
+        dec.px[:n].copy_(torch.from_numpy(xp[spos:spos + n]))
+        dec.prefill(spos, n)
+        torch.cuda.synchronize()
+        ok, rel = close(dec.logits.cpu().numpy()[0], GOLD[f"{name}_pre_logits"][c])
+        assert ok, f"chunk {c} logits: max diff {rel:.3g} of the largest"
+        ok, rel = close(dec.px[:n].cpu().numpy(), GOLD[f"{name}_pre_hid"][spos:spos + n])
+        assert ok, f"chunk {c} hidden states: max diff {rel:.3g} of the largest"
+        spos += n
+    gcu.check_device()
+
+
+def test_prefill_then_decode_continues_the_cache():
+    # prefill 16 tokens, then decode position 16 on the same KV cache: the
+    # reference decode of 17 positions gives the same last logits
+    name = "gemma3"
+    cfg = META["cases"][name]
+    layers, emb, fnorm = synth.decoder_model(cfg["tid"], cfg)
+    xp = synth.normal(cfg["tid"] + 777, (17, cfg["dim"]))
+    dec = decode.Decoder(cfg, layers, emb, fnorm, clen=17)
+    dec.set_prefill_freqs(GOLD[f"{name}_pslid"][:16], GOLD[f"{name}_pfull"][:16])
+    dec.px[:16].copy_(torch.from_numpy(xp[:16]))
+    dec.prefill(0, 16)
+    slid, full = decode.rope_tables(cfg["hdim"], cfg["theta_l"], cfg["theta_g"], 16)
+    dec.set_freqs(slid, full)
+    dec.x.copy_(torch.from_numpy(xp[16][None]))
+    dec.step(16)
+    torch.cuda.synchronize()
+    got = dec.logits.cpu().numpy()[0]
+    dec2 = decode.Decoder(cfg, layers, emb, fnorm, clen=17)
+    for p in range(17):
+        s_, f_ = (GOLD[f"{name}_pslid"][p], GOLD[f"{name}_pfull"][p]) if p < 16 else (slid, full)
+        dec2.set_freqs(s_, f_)
+        dec2.x.copy_(torch.from_numpy(xp[p][None]))
+        dec2.step(p)
+    torch.cuda.synchronize()
+    ok, rel = close(got, dec2.logits.cpu().numpy()[0])
+    assert ok, f"prefill+decode vs decode only: {rel:.3g}"
