@@ -1156,6 +1156,9 @@ DECODE_STEP = {
                           nkv=1, hdim=256, dim=1152, mlp_dim=6912, nvocab=262144, q_scale=256, slide=512, pos=1023),
     "decode_step4b": dict(title="Gemma-3-4B decode step at position 1023 (34 layers + lm_head)", nl=34, n_heads=8,
                           nkv=4, hdim=256, dim=2560, mlp_dim=10240, nvocab=262144, q_scale=256, slide=1024, pos=1023),
+    "prefill_chunk1b": dict(title="Gemma-3-1B prefill of a 512-token chunk from position 0 (26 layers + last-token "
+                                  "lm_head)", nl=26, n_heads=4, nkv=1, hdim=256, dim=1152, mlp_dim=6912,
+                            nvocab=262144, q_scale=256, slide=512, pos=0, ntok=512),
 }
 
 
@@ -1194,19 +1197,28 @@ def run_decode_step(args):
                "n3": nv(dim), "n4": nv(dim), "nq": nv(hd), "nk": nv(hd)} for _ in range(nl)]
     emb = wt(cfg["nvocab"], dim)
     fnorm = nv(dim)
-    dec = decode.Decoder(cfg, layers, emb, fnorm, clen=pos + 1)
-    dec.kv.normal_(generator=gen)  # positions 0 .. pos-1 as if decoded before
-    slid, full = decode.rope_tables(hd, cfg["theta_l"], cfg["theta_g"], pos)
-    dec.set_freqs(slid, full)
-    dec.x.normal_(generator=gen)
+    ntok = cfg.get("ntok", 0)
+    prefill = ntok > 0
+    dec = decode.Decoder(cfg, layers, emb, fnorm, clen=pos + max(ntok, 1))
     stream = torch.cuda.Stream()
+    if prefill:
+        tabs = [decode.rope_tables(hd, cfg["theta_l"], cfg["theta_g"], pos + t) for t in range(ntok)]
+        dec.set_prefill_freqs(np.stack([t[0] for t in tabs]), np.stack([t[1] for t in tabs]))
+        dec.px[:ntok].normal_(generator=gen)
+        run = lambda: dec.prefill(pos, ntok, stream=stream)
+    else:
+        dec.kv.normal_(generator=gen)  # positions 0 .. pos-1 as if decoded before
+        slid, full = decode.rope_tables(hd, cfg["theta_l"], cfg["theta_g"], pos)
+        dec.set_freqs(slid, full)
+        dec.x.normal_(generator=gen)
+        run = lambda: dec.step(pos, stream=stream)
     with torch.cuda.stream(stream):
-        dec.step(pos, stream=stream)  # eager: allocates the attention split scratch
+        run()  # eager: allocates the split scratch
     stream.synchronize()
     gcu.check_device()
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, stream=stream):
-        dec.step(pos, stream=stream)
+        run()
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
             g.replay()
@@ -1232,20 +1244,30 @@ def run_decode_step(args):
         kvbytes += 2 * kv_sz * n * 4
     nbytes = wbytes + kvbytes
     ach = nbytes / (ms * 1e-3) / 1e9
-    out = {"metric": "device-resident decode: tokens per second (all layers + lm_head, batch 1)",
-           "value": 1e3 / ms, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+    if prefill:
+        ops = ntok * sum(2 * t[0].numel() for lay in dec.L for t in lay.values() if isinstance(t, tuple))
+        ach_t = ops / (ms * 1e-3) / 1e12
+        roof = {"bound": "tensor", "achieved": ach_t, "peak": 2.0 * peaks["bf16_tflops"], "unit": "TOPS",
+                "frac": ach_t / (2.0 * peaks["bf16_tflops"]), "peak_src": f"2 x {peaks['src']} bf16 dense",
+                "int8_ops_per_step": ops, "note": "layer matmuls only; attention and norms are fp32", "traffic": None}
+    else:
+        roof = {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": ach / peaks["hbm_gbs"], "peak_src": f"{peaks['src']} copy bandwidth",
+                "bytes_per_step": nbytes, "weight_bytes": wbytes, "kv_bytes": kvbytes, "traffic": None}
+    out = {"metric": ("device-resident prefill: tokens per second (all layers, last-token lm_head)" if prefill else
+                      "device-resident decode: tokens per second (all layers + lm_head, batch 1)"),
+           "value": (ntok if prefill else 1) * 1e3 / ms, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+           "warmup": args.warmup,
            "ms_per_step": ms, "higher_is_better": True, "scaling": "none", "vs_baseline": None,
            "dtype": "int8 matmuls (int32 accum), fp32 norms/attention", "data": "synthetic", "impl": "ours",
            "config": {"workload": f"{args.workload}: {cfg['title']}", "layers": nl, "kv_cache_positions": pos + 1,
                       "layer_pattern": "5 sliding-window layers then 1 global",
                       **({"reduced": f"--layers {args.layers}: a profiling case, not the benchmark workload"}
                          if args.layers > 0 else {})},
-           "roofline": {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                        "frac": ach / peaks["hbm_gbs"], "peak_src": f"{peaks['src']} copy bandwidth",
-                        "bytes_per_step": nbytes, "weight_bytes": wbytes, "kv_bytes": kvbytes, "traffic": None},
-           "clocks": clk, "gpu_launches": dec.launches_per_step() * args.steps, "e2e": None,
+           "roofline": roof,
+           "clocks": clk, "gpu_launches": dec.launches_per_step(prefill) * args.steps, "e2e": None,
            "e2e_note": "device-resident by design: the step reads no host memory"}
-    if not args.no_cpu and args.layers <= 0 and args.workload == "decode_step1b":
+    if not args.no_cpu and args.layers <= 0 and args.workload in ("decode_step1b", "prefill_chunk1b"):
         out["cpu_baseline"] = _decode_cpu_baseline(cfg, dec, emb, fnorm)
     del g
     print(json.dumps(out), flush=True)
@@ -1270,6 +1292,17 @@ def _decode_cpu_baseline(cfg, dec, emb, fnorm):
         lay.update({k: host(w[k]) for k in ("n1", "n2", "n3", "n4", "nq", "nk")})
         layers.append(lay)
     e = (host(emb[0]), host(emb[1]))
+    ntok = cfg.get("ntok", 0)
+    if ntok:
+        x0 = np.random.default_rng(0).standard_normal((ntok, cfg["dim"]), dtype=np.float32)
+        R.prefill_chunks(cfg, layers, e, host(fnorm), x0[:16], [16])  # warm-up (pages the weights in)
+        t0 = time.perf_counter()
+        R.prefill_chunks(cfg, layers, e, host(fnorm), x0, [ntok])
+        dt = time.perf_counter() - t0
+        return {"value": ntok / dt, "unit": "tokens/s", "cores": threads, "kind": "reference",
+                "ms_per_step": dt * 1e3,
+                "sample": f"gemma.c forward_text_chunk of the same {ntok} tokens on the same weights, "
+                          f"{variant}/{R.isa}"}
     x0 = np.random.default_rng(0).standard_normal((16, cfg["dim"]), dtype=np.float32)
     R.decode_steps(cfg, layers, e, host(fnorm), x0[:2])  # warm-up (pages the weights in)
     t0 = time.perf_counter()

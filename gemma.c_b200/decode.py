@@ -251,10 +251,13 @@ class Decoder:
         if c["sc_log"]:
             gcu.dev_softcap(self.logits, c["sc_log"], stream=stream)
 
-    def launches_per_step(self) -> int:
-        """Kernel launches of one step (attention over a split window adds its
-        combine launch; counted as one here)."""
-        return 9 * self.cfg["nl"] + 3 + (1 if self.cfg["sc_log"] else 0)
+    def launches_per_step(self, prefill: bool = False) -> int:
+        """Kernel launches of one decode step (9 per layer) or one prefill
+        chunk (11 per layer: the chunk merge of the attention and the separate
+        quantize of the O projection's input at m > 8); an attention window
+        split over CTAs adds its merge launch to the decode count."""
+        per = 11 if prefill else 9
+        return per * self.cfg["nl"] + 3 + (1 if self.cfg["sc_log"] else 0)
 
 
 class _null:
