@@ -1088,8 +1088,9 @@ def run_attention(args):
         peak = 148 * 128 * 2 * mhz * 1e6 / 1e12
         roof = {"bound": "fp32", "achieved": value, "peak": peak, "unit": "TFLOP/s", "frac": value / peak,
                 "peak_src": "derived fp32 FMA peak: 148 SMs x 128 lanes x 2 flops x max SM clock",
-                "flops_per_step": flops, "note": "the kernel scores every key twice (max pass, weight pass): "
-                "1.5x the counted flops", "traffic": None}
+                "flops_per_step": flops, "note": "a chunk of one 64-key tile keeps its scores between the max and "
+                "weight passes; a longer chunk scores its keys twice (up to 1.5x the counted flops)",
+                "traffic": None}
         unit, metric = "TFLOP/s", "prefill attention: causal fp32 flops per second"
         launches = len(lay)
     out = {"metric": metric, "value": value, "unit": unit, "n_gpus": 1, "steps": args.steps,

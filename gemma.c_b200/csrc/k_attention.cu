@@ -349,7 +349,7 @@ __global__ void __launch_bounds__(HD) k_attn_combine(float *xo, const float *par
 // prefill
 // ---------------------------------------------------------------------------
 constexpr int kPreThreads = 256;
-constexpr int kBQ = 16;  // queries per CTA
+constexpr int kBQ = 64;  // queries per CTA
 constexpr int kBK = 64;  // keys per tile
 
 struct PrefillArgs {
@@ -365,11 +365,12 @@ struct PrefillArgs {
 
 template <int HD>
 struct PreSmem {
-  static constexpr int KS = HD + 4;  // padded K / Q row: conflict-free 16-byte reads
-  static constexpr size_t q = 0;
-  static constexpr size_t k = q + (size_t)kBQ * KS;
-  static constexpr size_t p = k + (size_t)kBK * KS;
-  static constexpr size_t floats = p + (size_t)kBQ * kBK;
+  static constexpr int KS = HD + 4;   // padded Q / K / V rows: conflict-free 16-byte reads
+  static constexpr int PS = kBK + 4;  // padded weight rows
+  static constexpr size_t q = 0;                      // [kBQ][KS]
+  static constexpr size_t kv = q + (size_t)kBQ * KS;  // [kBK][KS]: a K tile, then its V tile
+  static constexpr size_t p = kv + (size_t)kBK * KS;  // [kBQ][PS]
+  static constexpr size_t floats = p + (size_t)kBQ * PS;
   static constexpr size_t bytes = floats * sizeof(float);
 };
 
@@ -398,43 +399,52 @@ __device__ __forceinline__ void load_tile(float *dst, int ld, const float *src, 
   }
 }
 
-// s[c] = q(row qi) . k(row kq + 16c), c < 4, from smem
+// s[i][c] = q(row ty*4 + i) . k(row tx + 16c), i, c < 4, from smem: per
+// 16-byte step 4 query and 4 key loads feed 64 multiply-adds
 template <int HD>
-__device__ __forceinline__ void tile_scores(const float *qs, const float *ks, int qi, int kq, float (&s)[4]) {
+__device__ __forceinline__ void tile_scores(const float *qs, const float *ks, int ty, int tx, float (&s)[4][4]) {
   constexpr int KS = PreSmem<HD>::KS;
-  s[0] = s[1] = s[2] = s[3] = 0.0f;
-  const float *qr = qs + qi * KS;
-#pragma unroll 8
-  for (int d = 0; d < HD; d += 4) {
-    const float4 q = *reinterpret_cast<const float4 *>(qr + d);
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const float4 k = *reinterpret_cast<const float4 *>(ks + (kq + 16 * c) * KS + d);
-      s[c] += q.x * k.x;
-      s[c] += q.y * k.y;
-      s[c] += q.z * k.z;
-      s[c] += q.w * k.w;
-    }
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) s[i][c] = 0.0f;
+#pragma unroll 4
+  for (int d = 0; d < HD; d += 4) {
+    float4 q[4], k[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q[i] = *reinterpret_cast<const float4 *>(qs + (ty * 4 + i) * KS + d);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) k[c] = *reinterpret_cast<const float4 *>(ks + (tx + 16 * c) * KS + d);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        s[i][c] += q[i].x * k[c].x;
+        s[i][c] += q[i].y * k[c].y;
+        s[i][c] += q[i].z * k[c].z;
+        s[i][c] += q[i].w * k[c].w;
+      }
   }
 }
 
-// CTA (query tile, head).  Thread (qi, kq) = (tid / 16, tid % 16) scores
-// row qi against keys kq + 16c of each tile and, in the value phase, owns
-// columns kq*4 + 64c of row qi.
+// CTA (64-query tile, head, chunk of the tile's key range).  Thread (ty, tx)
+// = (tid / 16, tid % 16) scores query rows ty*4 .. +3 against keys tx + 16c
+// of each 64-key tile (c < 4) and, in the weight pass, owns value columns
+// tx*4 + 64c of the same rows.  The V tile replaces the K tile in shared
+// memory once the tile's scores are done.
 template <int HD>
-__global__ void __launch_bounds__(kPreThreads, 2) k_attn_prefill(PrefillArgs a) {
+__global__ void __launch_bounds__(kPreThreads, 1) k_attn_prefill(PrefillArgs a) {
   extern __shared__ __align__(16) float smem[];
   using S = PreSmem<HD>;
-  float *qs = smem + S::q, *ks = smem + S::k, *ps = smem + S::p;
+  float *qs = smem + S::q, *kv = smem + S::kv, *ps = smem + S::p;
   ptx::griddep_launch();
   const int h = blockIdx.y, i0 = blockIdx.x * kBQ;
   const int nrows = min(kBQ, a.ntok - i0);
   const int hk = h * a.nkv / a.n_heads;  // gemma.c:5172
   const float *kh = a.kc + (size_t)hk * a.kv_stride, *vh = a.vc + (size_t)hk * a.kv_stride;
-  const int qi = threadIdx.x >> 4, kq = threadIdx.x & 15;
-  int t0, t1, lo, hi, unused;
-  row_window(a, i0 + min(qi, nrows - 1), t0, t1);
-  row_window(a, i0, lo, unused);              // windows only move right with i
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  int lo, hi, unused;
+  row_window(a, i0, lo, unused);  // windows only move right with i
   row_window(a, i0 + nrows - 1, unused, hi);
   // this CTA's chunk of the tile's key range: kpc key tiles
   const int ntiles = (hi + 1 - lo + kBK - 1) / kBK, nch = (ntiles + a.kpc - 1) / a.kpc;
@@ -442,6 +452,9 @@ __global__ void __launch_bounds__(kPreThreads, 2) k_attn_prefill(PrefillArgs a) 
   if (chunk >= nch) return;
   const int kbeg = lo + chunk * a.kpc * kBK;
   const int kend = min(hi + 1, kbeg + a.kpc * kBK);
+  int t0[4], t1[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) row_window(a, i0 + min(ty * 4 + i, nrows - 1), t0[i], t1[i]);
   ptx::griddep_wait();
 
   for (int idx = threadIdx.x; idx < kBQ * HD / 4; idx += kPreThreads) {
@@ -453,92 +466,105 @@ __global__ void __launch_bounds__(kPreThreads, 2) k_attn_prefill(PrefillArgs a) 
   }
 
   // pass 1: the maximum capped score of each row over its window.  A chunk
-  // of one key tile keeps that tile and its scores for pass 2.
+  // of one key tile keeps its scores for pass 2.
   const bool one = kend - kbeg <= kBK;
-  float m = -INFINITY, keep[4];
+  float m[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY}, keep[4][4];
   for (int k0 = kbeg; k0 < kend; k0 += kBK) {
     __syncthreads();  // the previous tile (and the Q tile's stores) are done
-    load_tile<HD>(ks, S::KS, kh, k0, kend);
+    load_tile<HD>(kv, S::KS, kh, k0, kend);
     __syncthreads();
-    float s[4];
-    tile_scores<HD>(qs, ks, qi, kq, s);
+    tile_scores<HD>(qs, kv, ty, tx, keep);
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const int t = k0 + kq + 16 * c;
-      s[c] = softcap(s[c], a.sc_att);
-      keep[c] = s[c];
-      if (t >= t0 && t <= t1 && t < kend) m = fmaxf(m, s[c]);
-    }
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int t = k0 + tx + 16 * c;
+        keep[i][c] = softcap(keep[i][c], a.sc_att);
+        if (t >= t0[i] && t <= t1[i] && t < kend) m[i] = fmaxf(m[i], keep[i][c]);
+      }
   }
 #pragma unroll
-  for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) m[i] = fmaxf(m[i], __shfl_xor_sync(0xffffffffu, m[i], o));
 
-  // pass 2: weights fast_expf(s - max) (gemma.c:4094-4105), their sum, and
+  // pass 2: weights fast_expf(s - max) (gemma.c:4094-4105), their sums, and
   // the weighted V rows
-  float l = 0.0f;
-  float4 acc[HD / 64];
+  float l[4] = {0.f, 0.f, 0.f, 0.f};
+  float4 acc[4][HD / 64];
 #pragma unroll
-  for (int c = 0; c < HD / 64; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int c = 0; c < HD / 64; ++c) acc[i][c] = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int k0 = kbeg; k0 < kend; k0 += kBK) {
-    float s[4];
-    if (one) {
-#pragma unroll
-      for (int c = 0; c < 4; ++c) s[c] = keep[c];
-    } else {
+    if (!one) {
       __syncthreads();
-      load_tile<HD>(ks, S::KS, kh, k0, kend);
+      load_tile<HD>(kv, S::KS, kh, k0, kend);
       __syncthreads();
-      tile_scores<HD>(qs, ks, qi, kq, s);
+      tile_scores<HD>(qs, kv, ty, tx, keep);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) s[c] = softcap(s[c], a.sc_att);
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) keep[i][c] = softcap(keep[i][c], a.sc_att);
     }
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const int t = k0 + kq + 16 * c;
-      const float p = (t >= t0 && t <= t1 && t < kend) ? dev_fast_expf(s[c] - m) : 0.0f;
-      ps[qi * kBK + kq + 16 * c] = p;
-      l += p;
-    }
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int t = k0 + tx + 16 * c;
+        const float p = (t >= t0[i] && t <= t1[i] && t < kend) ? dev_fast_expf(keep[i][c] - m[i]) : 0.0f;
+        ps[(ty * 4 + i) * S::PS + tx + 16 * c] = p;
+        l[i] += p;
+      }
+    __syncthreads();  // every thread is done with the K tile; the weights are written
+    load_tile<HD>(kv, S::KS, vh, k0, kend);
     __syncthreads();
     const int jn = min(kBK, kend - k0);
-    const float *pr = ps + qi * kBK;
-    // V rows straight from L2 / L1: the 16 threads of a row read 256
-    // contiguous bytes, the two rows of a warp the same ones
-#pragma unroll 4
     for (int j = 0; j < jn; ++j) {
-      const float p = pr[j];
-      const float *vr = vh + (size_t)(k0 + j) * HD + kq * 4;
+      float p[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) p[i] = ps[(ty * 4 + i) * S::PS + j];
+      const float *vr = kv + j * S::KS + tx * 4;
 #pragma unroll
       for (int c = 0; c < HD / 64; ++c) {
-        const float4 v = __ldg(reinterpret_cast<const float4 *>(vr + 64 * c));
-        acc[c].x += p * v.x;
-        acc[c].y += p * v.y;
-        acc[c].z += p * v.z;
-        acc[c].w += p * v.w;
+        const float4 v = *reinterpret_cast<const float4 *>(vr + 64 * c);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          acc[i][c].x += p[i] * v.x;
+          acc[i][c].y += p[i] * v.y;
+          acc[i][c].z += p[i] * v.z;
+          acc[i][c].w += p[i] * v.w;
+        }
       }
     }
   }
 #pragma unroll
-  for (int o = 8; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-  if (qi >= nrows) return;
-  if (nch == 1) {
-    float *out = a.xo + (size_t)(i0 + qi) * a.xostr + (size_t)h * HD + kq * 4;
+  for (int i = 0; i < 4; ++i)
 #pragma unroll
-    for (int c = 0; c < HD / 64; ++c)
-      *reinterpret_cast<float4 *>(out + 64 * c) =
-          make_float4(acc[c].x / l, acc[c].y / l, acc[c].z / l, acc[c].w / l);
-    return;
-  }
-  // a chunk of several: leave the unnormalised sums, the maximum and the
-  // weight sum (a row with no key in this chunk leaves -inf, 0, zeros)
-  const size_t r = ((size_t)h * a.ntok + i0 + qi) * a.maxch + chunk;
+    for (int o = 8; o > 0; o >>= 1) l[i] += __shfl_xor_sync(0xffffffffu, l[i], o);
   const size_t nrec = (size_t)a.n_heads * a.ntok * a.maxch;
-  float *po = a.part + r * HD + kq * 4;
 #pragma unroll
-  for (int c = 0; c < HD / 64; ++c) *reinterpret_cast<float4 *>(po + 64 * c) = acc[c];
-  if (kq == 0) {
-    a.part[nrec * HD + r] = m;
-    a.part[nrec * (HD + 1) + r] = l;
+  for (int i = 0; i < 4; ++i) {
+    const int row = ty * 4 + i;
+    if (row >= nrows) continue;
+    if (nch == 1) {
+      float *out = a.xo + (size_t)(i0 + row) * a.xostr + (size_t)h * HD + tx * 4;
+#pragma unroll
+      for (int c = 0; c < HD / 64; ++c)
+        *reinterpret_cast<float4 *>(out + 64 * c) =
+            make_float4(acc[i][c].x / l[i], acc[i][c].y / l[i], acc[i][c].z / l[i], acc[i][c].w / l[i]);
+    } else {
+      // a chunk of several: the unnormalised sums, the maximum and the weight
+      // sum (a row with no key in this chunk leaves -inf, 0, zeros)
+      const size_t r = ((size_t)h * a.ntok + i0 + row) * a.maxch + chunk;
+      float *po = a.part + r * HD + tx * 4;
+#pragma unroll
+      for (int c = 0; c < HD / 64; ++c) *reinterpret_cast<float4 *>(po + 64 * c) = acc[i][c];
+      if (tx == 0) {
+        a.part[nrec * HD + r] = m[i];
+        a.part[nrec * (HD + 1) + r] = l[i];
+      }
+    }
   }
 }
 
