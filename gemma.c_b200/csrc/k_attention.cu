@@ -361,17 +361,28 @@ struct PrefillArgs {
   float sc_att;
   int kpc, maxch;  // key tiles per chunk, chunks per query tile (grid z)
   float *part;     // maxch > 1: [n_heads][ntok][maxch][HD] sums, then maxima, then weight sums
+  unsigned int *err;
 };
 
+// Q, K and V tiles move by 1D bulk copies, one per row (rows of one head
+// are contiguous in xq and in the cache), issued by warp 0 and completing on
+// one mbarrier per buffer.  Each buffer has at most one copy in flight, so a
+// buffer's completed-copy count gives the parity of its next wait.
 template <int HD>
 struct PreSmem {
   static constexpr int KS = HD + 4;   // padded Q / K / V rows: conflict-free 16-byte reads
   static constexpr int PS = kBK + 4;  // padded weight rows
   static constexpr size_t q = 0;                      // [kBQ][KS]
-  static constexpr size_t kv = q + (size_t)kBQ * KS;  // [kBK][KS]: a K tile, then its V tile
-  static constexpr size_t p = kv + (size_t)kBK * KS;  // [kBQ][PS]
+  static constexpr size_t k = q + (size_t)kBQ * KS;   // [kBK][KS]
+  static constexpr size_t v = k + (size_t)kBK * KS;   // [kBK][KS]
+  static constexpr size_t p = v + (size_t)kBK * KS;   // [kBQ][PS]
   static constexpr size_t floats = p + (size_t)kBQ * PS;
   static constexpr size_t bytes = floats * sizeof(float);
+};
+
+struct TileRing {
+  uint64_t *bar;  // [3]: Q, K, V
+  int issued[3], done[3];
 };
 
 // the window of token i (gemma.c:5187-5199 / 5232-5236): [t0, t1]
@@ -386,57 +397,90 @@ __device__ __forceinline__ void row_window(const PrefillArgs &a, int i, int &t0,
   }
 }
 
-// rows [k0, k0 + kBK) of one kv head's cache into smem (row stride `ld`),
-// rows at or past `kend` zero
+// n rows of HD floats at src (contiguous) into smem rows of stride KS; every
+// thread of the CTA calls it (the issue counts stay uniform), warp 0 issues.
+// The issuing lanes order their earlier shared-memory reads of the buffer
+// (made before the caller's CTA barrier) before the async writes.
 template <int HD>
-__device__ __forceinline__ void load_tile(float *dst, int ld, const float *src, int k0, int kend) {
-  constexpr int V4 = HD / 4;
-  for (int idx = threadIdx.x; idx < kBK * V4; idx += kPreThreads) {
-    const int row = idx / V4, c = idx - row * V4;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (k0 + row < kend) v = __ldg(reinterpret_cast<const float4 *>(src + (size_t)(k0 + row) * HD) + c);
-    *reinterpret_cast<float4 *>(dst + row * ld + c * 4) = v;
-  }
+__device__ __forceinline__ void ring_copy(TileRing &r, int b, float *dst, const float *src, int n, uint64_t pol) {
+  ++r.issued[b];
+  if (threadIdx.x >= 32) return;
+  ptx::fence_proxy_async_smem();
+  if (threadIdx.x == 0) ptx::mbar_arrive_expect_tx(&r.bar[b], (uint32_t)n * HD * sizeof(float));
+  __syncwarp();
+  for (int row = threadIdx.x; row < n; row += 32)
+    ptx::bulk_load(dst + (size_t)row * PreSmem<HD>::KS, src + (size_t)row * HD, HD * sizeof(float), &r.bar[b], pol);
+}
+
+// every thread waits (bounded) for buffer b's copy in flight; the CTA barrier
+// both agrees on the outcome and orders the threads' earlier work before
+// what follows.  false: a copy never completed (the error word says which).
+__device__ __forceinline__ bool ring_wait(TileRing &r, int b, unsigned int *err) {
+  const bool ok = ptx::mbar_wait(&r.bar[b], r.done[b] & 1, err, DEV_TIMEOUT_FULL);
+  if (__syncthreads_or(!ok)) return false;
+  ++r.done[b];
+  return true;
 }
 
 // s[i][c] = q(row ty*4 + i) . k(row tx + 16c), i, c < 4, from smem: per
-// 16-byte step 4 query and 4 key loads feed 64 multiply-adds
+// 16-byte step 4 query and 4 key loads feed 64 multiply-adds.  The loads of
+// step d + 4 are issued before the multiply-adds of step d, and the 16
+// accumulators advance one component at a time (16 independent chains).
 template <int HD>
 __device__ __forceinline__ void tile_scores(const float *qs, const float *ks, int ty, int tx, float (&s)[4][4]) {
   constexpr int KS = PreSmem<HD>::KS;
+  const float *qb = qs + ty * 4 * KS, *kb = ks + tx * KS;
+  auto load = [&](float4 (&q)[4], float4 (&k)[4], int d) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q[i] = *reinterpret_cast<const float4 *>(qb + i * KS + d);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) k[c] = *reinterpret_cast<const float4 *>(kb + 16 * c * KS + d);
+  };
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int c = 0; c < 4; ++c) s[i][c] = 0.0f;
+  float4 q[4], k[4];
+  load(q, k, 0);
 #pragma unroll 4
   for (int d = 0; d < HD; d += 4) {
-    float4 q[4], k[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) q[i] = *reinterpret_cast<const float4 *>(qs + (ty * 4 + i) * KS + d);
-#pragma unroll
-    for (int c = 0; c < 4; ++c) k[c] = *reinterpret_cast<const float4 *>(ks + (tx + 16 * c) * KS + d);
+    float4 qn[4], kn[4];
+    load(qn, kn, d + 4 < HD ? d + 4 : d);
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        s[i][c] += q[i].x * k[c].x;
-        s[i][c] += q[i].y * k[c].y;
-        s[i][c] += q[i].z * k[c].z;
-        s[i][c] += q[i].w * k[c].w;
-      }
+      for (int c = 0; c < 4; ++c) s[i][c] += q[i].x * k[c].x;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) s[i][c] += q[i].y * k[c].y;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) s[i][c] += q[i].z * k[c].z;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) s[i][c] += q[i].w * k[c].w;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      q[i] = qn[i];
+      k[i] = kn[i];
+    }
   }
 }
 
 // CTA (64-query tile, head, chunk of the tile's key range).  Thread (ty, tx)
 // = (tid / 16, tid % 16) scores query rows ty*4 .. +3 against keys tx + 16c
 // of each 64-key tile (c < 4) and, in the weight pass, owns value columns
-// tx*4 + 64c of the same rows.  The V tile replaces the K tile in shared
-// memory once the tile's scores are done.
+// tx*4 + 64c of the same rows.  The first V tile loads while the first pass
+// runs; each later K or V tile is issued as soon as its buffer is free.
 template <int HD>
 __global__ void __launch_bounds__(kPreThreads, 1) k_attn_prefill(PrefillArgs a) {
-  extern __shared__ __align__(16) float smem[];
+  extern __shared__ __align__(128) float smem[];
+  __shared__ __align__(8) uint64_t bars[3];
   using S = PreSmem<HD>;
-  float *qs = smem + S::q, *kv = smem + S::kv, *ps = smem + S::p;
+  float *qs = smem + S::q, *ks = smem + S::k, *vs = smem + S::v, *ps = smem + S::p;
   ptx::griddep_launch();
   const int h = blockIdx.y, i0 = blockIdx.x * kBQ;
   const int nrows = min(kBQ, a.ntok - i0);
@@ -452,91 +496,128 @@ __global__ void __launch_bounds__(kPreThreads, 1) k_attn_prefill(PrefillArgs a) 
   if (chunk >= nch) return;
   const int kbeg = lo + chunk * a.kpc * kBK;
   const int kend = min(hi + 1, kbeg + a.kpc * kBK);
+  const int ntl = (kend - kbeg + kBK - 1) / kBK;  // key tiles of this chunk
+  const bool one = ntl == 1;  // a one-tile chunk keeps its scores for pass 2
   int t0[4], t1[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) row_window(a, i0 + min(ty * 4 + i, nrows - 1), t0[i], t1[i]);
+  TileRing ring{bars, {0, 0, 0}, {0, 0, 0}};
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < 3; ++b) ptx::mbar_init(&bars[b], 1);
+    ptx::fence_mbar_init();
+  }
+  __syncthreads();
   ptx::griddep_wait();
+  const uint64_t pol = ptx::policy_evict_last();  // K/V tiles are read by every query tile of the head
+  auto krows = [&](int k0) { return min(kBK, kend - k0); };
+  ring_copy<HD>(ring, 0, qs, a.xq + ((size_t)h * a.ntok + i0) * HD, nrows, pol);
+  ring_copy<HD>(ring, 1, ks, kh + (size_t)kbeg * HD, krows(kbeg), pol);
+  ring_copy<HD>(ring, 2, vs, vh + (size_t)kbeg * HD, krows(kbeg), pol);
 
-  for (int idx = threadIdx.x; idx < kBQ * HD / 4; idx += kPreThreads) {
-    const int row = idx / (HD / 4), c = idx - row * (HD / 4);
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (row < nrows)
-      v = __ldg(reinterpret_cast<const float4 *>(a.xq + ((size_t)h * a.ntok + i0 + row) * HD) + c);
-    *reinterpret_cast<float4 *>(qs + row * S::KS + c * 4) = v;
-  }
-
-  // pass 1: the maximum capped score of each row over its window.  A chunk
-  // of one key tile keeps its scores for pass 2.
-  const bool one = kend - kbeg <= kBK;
-  float m[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY}, keep[4][4];
-  for (int k0 = kbeg; k0 < kend; k0 += kBK) {
-    __syncthreads();  // the previous tile (and the Q tile's stores) are done
-    load_tile<HD>(kv, S::KS, kh, k0, kend);
-    __syncthreads();
-    tile_scores<HD>(qs, kv, ty, tx, keep);
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int t = k0 + tx + 16 * c;
-        keep[i][c] = softcap(keep[i][c], a.sc_att);
-        if (t >= t0[i] && t <= t1[i] && t < kend) m[i] = fmaxf(m[i], keep[i][c]);
-      }
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) m[i] = fmaxf(m[i], __shfl_xor_sync(0xffffffffu, m[i], o));
-
-  // pass 2: weights fast_expf(s - max) (gemma.c:4094-4105), their sums, and
-  // the weighted V rows
-  float l[4] = {0.f, 0.f, 0.f, 0.f};
+  // Rows of a buffer past its copy hold stale values: a key past kend is
+  // masked by a select (never multiplied), a V row past it is never read,
+  // and a query row past nrows is never written out.
+  float m[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY}, s[4][4], l[4] = {0.f, 0.f, 0.f, 0.f};
   float4 acc[4][HD / 64];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int c = 0; c < HD / 64; ++c) acc[i][c] = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int k0 = kbeg; k0 < kend; k0 += kBK) {
-    if (!one) {
-      __syncthreads();
-      load_tile<HD>(kv, S::KS, kh, k0, kend);
-      __syncthreads();
-      tile_scores<HD>(qs, kv, ty, tx, keep);
+  auto scores = [&](int k0) {
+    tile_scores<HD>(qs, ks, ty, tx, s);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) s[i][c] = softcap(s[i][c], a.sc_att);
+  };
+  auto valid = [&](int i, int t) { return t >= t0[i] && t <= t1[i] && t < kend; };
+
+  auto body = [&]() -> bool {
+    if (!ring_wait(ring, 0, a.err)) return false;
+    // pass 1: the maximum capped score of each row over its window
+    for (int k0 = kbeg; k0 < kend; k0 += kBK) {
+      if (!ring_wait(ring, 1, a.err)) return false;
+      scores(k0);
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) keep[i][c] = softcap(keep[i][c], a.sc_att);
+        for (int c = 0; c < 4; ++c)
+          if (valid(i, k0 + tx + 16 * c)) m[i] = fmaxf(m[i], s[i][c]);
+      if (!one) {  // the next pass-1 tile, or pass 2's first
+        __syncthreads();
+        const int kn = k0 + kBK < kend ? k0 + kBK : kbeg;
+        ring_copy<HD>(ring, 1, ks, kh + (size_t)kn * HD, krows(kn), pol);
+      }
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int t = k0 + tx + 16 * c;
-        const float p = (t >= t0[i] && t <= t1[i] && t < kend) ? dev_fast_expf(keep[i][c] - m[i]) : 0.0f;
-        ps[(ty * 4 + i) * S::PS + tx + 16 * c] = p;
-        l[i] += p;
+      for (int o = 8; o > 0; o >>= 1) m[i] = fmaxf(m[i], __shfl_xor_sync(0xffffffffu, m[i], o));
+
+    // pass 2: weights fast_expf(s - max) (gemma.c:4094-4105), their sums,
+    // and the weighted V rows
+    for (int k0 = kbeg; k0 < kend; k0 += kBK) {
+      if (!one) {
+        if (!ring_wait(ring, 1, a.err)) return false;
+        scores(k0);
       }
-    __syncthreads();  // every thread is done with the K tile; the weights are written
-    load_tile<HD>(kv, S::KS, vh, k0, kend);
-    __syncthreads();
-    const int jn = min(kBK, kend - k0);
-    for (int j = 0; j < jn; ++j) {
-      float p[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) p[i] = ps[(ty * 4 + i) * S::PS + j];
-      const float *vr = kv + j * S::KS + tx * 4;
+      for (int i = 0; i < 4; ++i)
 #pragma unroll
-      for (int c = 0; c < HD / 64; ++c) {
-        const float4 v = *reinterpret_cast<const float4 *>(vr + 64 * c);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          acc[i][c].x += p[i] * v.x;
-          acc[i][c].y += p[i] * v.y;
-          acc[i][c].z += p[i] * v.z;
-          acc[i][c].w += p[i] * v.w;
+        for (int c = 0; c < 4; ++c) {
+          const float p = valid(i, k0 + tx + 16 * c) ? dev_fast_expf(s[i][c] - m[i]) : 0.0f;
+          ps[(ty * 4 + i) * S::PS + tx + 16 * c] = p;
+          l[i] += p;
         }
+      // V tile: its barrier also publishes the weights and frees the K buffer
+      if (!ring_wait(ring, 2, a.err)) return false;
+      const bool last = k0 + kBK >= kend;
+      if (!one && !last) ring_copy<HD>(ring, 1, ks, kh + (size_t)(k0 + kBK) * HD, krows(k0 + kBK), pol);
+      // weighted V rows, row j + 1's weights and values loaded ahead of row j's multiply-adds
+      const int jn = krows(k0);
+      auto pv_load = [&](float (&p)[4], float4 (&v)[HD / 64], int j) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) p[i] = ps[(ty * 4 + i) * S::PS + j];
+#pragma unroll
+        for (int c = 0; c < HD / 64; ++c) v[c] = *reinterpret_cast<const float4 *>(vs + j * S::KS + tx * 4 + 64 * c);
+      };
+      float p[4];
+      float4 v[HD / 64];
+      pv_load(p, v, 0);
+#pragma unroll 2
+      for (int j = 0; j < jn; ++j) {
+        float pn[4];
+        float4 vn[HD / 64];
+        pv_load(pn, vn, j + 1 < jn ? j + 1 : j);
+#pragma unroll
+        for (int c = 0; c < HD / 64; ++c)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            acc[i][c].x += p[i] * v[c].x;
+            acc[i][c].y += p[i] * v[c].y;
+            acc[i][c].z += p[i] * v[c].z;
+            acc[i][c].w += p[i] * v[c].w;
+          }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) p[i] = pn[i];
+#pragma unroll
+        for (int c = 0; c < HD / 64; ++c) v[c] = vn[c];
+      }
+      if (!last) {
+        __syncthreads();  // every thread is done with this V tile and its weights
+        ring_copy<HD>(ring, 2, vs, vh + (size_t)(k0 + kBK) * HD, krows(k0 + kBK), pol);
       }
     }
+    return true;
+  };
+  if (!body()) {
+    // a copy never completed: wait (bounded) for the copies still in flight
+    // into this CTA's shared memory, then leave
+    if (threadIdx.x == 0)
+      for (int b = 0; b < 3; ++b)
+        if (ring.issued[b] > ring.done[b])
+          ptx::mbar_wait(&bars[b], ring.done[b] & 1, a.err, DEV_TIMEOUT_DRAIN);
+    return;
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i)
@@ -721,7 +802,7 @@ GCU_EXPORT int gcu_dev_attention_prefill(float *xo, int xostr, const float *xq, 
                      kv_stride);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   PrefillArgs a{xo, xostr, xq, k_cache, v_cache, kv_stride, n_heads, nkv, spos, ntok, slide, mask ? 1 : 0, sc_att,
-                1, 1, nullptr};
+                1, 1, nullptr, dev_error_word()};
   // the causal triangle gives late query tiles many key tiles and early ones
   // few: split every tile's key range into chunks of kpc key tiles (one tile
   // per chunk up to 8 tiles, at most 8 chunks beyond), so the longest CTA

@@ -98,7 +98,9 @@ def test_decode_matches_oracle(nh, nkv, hd, clen, spos, attlen, sc):
     (8, 4, 256, 0, 300, 0, 0.0, True),       # 4B heads, global layer
     (8, 4, 128, 13, 77, 20, 30.0, True),
     (2, 1, 64, 0, 100, 0, 0.0, False),
-    (6, 4, 64, 0, 70, 0, 0.0, True)])      # uneven query-head groups
+    (6, 4, 64, 0, 70, 0, 0.0, True),       # uneven query-head groups
+    (4, 1, 256, 0, 2048, 0, 0.0, True),    # 32 key tiles: chunks of 4 tiles each
+    (2, 1, 128, 0, 700, 0, 0.0, False)])   # 11 tiles: chunks of 2, the last of one
 def test_prefill_matches_oracle(nh, nkv, hd, spos, ntok, slide, sc, mask):
     xq, kc, vc = synth.attention_inputs(400 + ntok, nh, nkv, hd, spos + ntok, ntok)
     assert_attn_close(run_prefill(xq, kc, vc, spos, slide, sc, mask),
