@@ -79,7 +79,7 @@ class Decoder:
             self.L.append(d)
         self.emb = (t(emb[0]), t(emb[1]))
         self.fnorm = t(fnorm)
-        q_sz, kv_sz = c["n_heads"] * c["hdim"], c["nkv"] * c["hdim"]
+        q_sz = c["n_heads"] * c["hdim"]
         f32 = dict(dtype=torch.float32, device=device)
         i8 = dict(dtype=torch.int8, device=device)
         self.kv = torch.zeros((c["nl"], 2, c["nkv"], clen, c["hdim"]), **f32)
@@ -95,7 +95,6 @@ class Decoder:
         self.s = torch.empty(1, **f32)
         self.logits = torch.empty((1, c["nvocab"]), **f32)
         self.freqs = torch.empty((2, c["hdim"]), **f32)  # sliding, full
-        del kv_sz
 
     def set_freqs(self, slid, full, stream=None):
         """Upload the RoPE tables of the position about to be decoded."""
@@ -200,7 +199,13 @@ class Decoder:
         every layer, the final norm of every row (left in self.px) and the
         last token's logits (self.logits).  set_prefill_freqs first."""
         c = self.cfg
-        self._prefill_buffers(ntok)
+        if not 0 < ntok <= getattr(self, "_pmax", 0):
+            # the chunk's embeddings and RoPE tables live in buffers that
+            # set_prefill_freqs sized; growing them here would drop both
+            raise ValueError(f"prefill of {ntok} tokens: call set_prefill_freqs with the chunk's "
+                             f"{ntok} rows of tables first")
+        if spos < 0 or spos + ntok > self.clen:
+            raise ValueError(f"prefill of positions [{spos}, {spos + ntok}) outside a cache of {self.clen}")
         dim, mlp, hd = c["dim"], c["mlp_dim"], c["hdim"]
         nh, nkv = c["n_heads"], c["nkv"]
         q_sz, kv_sz = nh * hd, nkv * hd
