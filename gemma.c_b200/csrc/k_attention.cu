@@ -24,10 +24,11 @@
 //   split the CTA normalises and writes xo itself; otherwise it leaves an
 //   unnormalised partial (sum, row max, weight sum) that k_attn_combine
 //   merges in split order.
-// prefill: fp32 FMA-bound.  CTA = (head, 16-query tile); two passes over the
-//   key tiles the tile's rows can see: the first finds each row's maximum
-//   score, the second forms fast_expf(s - max) exactly as softmax does and
-//   accumulates the weights and the weighted V rows in registers.
+// prefill: fp32 FMA-bound.  CTA = (head, 64-query tile, chunk of the key
+//   range); two passes over the chunk's 64-key tiles: the first finds each
+//   row's maximum score, the second forms fast_expf(s - max) exactly as
+//   softmax does and accumulates the weights and the weighted V rows in
+//   registers.  Chunks of one query tile are merged in chunk order.
 #include "gcu_internal.cuh"
 
 #include <algorithm>
