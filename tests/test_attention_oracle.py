@@ -115,3 +115,40 @@ def test_oracle_rope_matches_live_reference():
         b = R.qk_norm_rope_cache(xq, xk, xv, kc, vc, fr, 700, 0.088, nq, nk)
         for x, y in zip(a, b):
             assert_attn_close(x, y)
+
+
+# ---- size-independent properties of the two restatements
+
+@pytest.mark.parametrize("nh,nkv,hd,spos,ntok,slide,sc", [(4, 1, 256, 0, 40, 0, 0.0), (6, 2, 64, 30, 50, 16, 0.0),
+                                                          (4, 4, 128, 100, 20, 64, 25.0)])
+def test_oracle_prefill_row_is_decode_over_its_window(nh, nkv, hd, spos, ntok, slide, sc):
+    # causal prefill row i (queries pre-scaled) attends to exactly the window
+    # decode attention sees at position spos + i with a unit score scale
+    xq, kc, vc = synth.attention_inputs(40 + ntok, nh, nkv, hd, spos + ntok, ntok)
+    pre = O.attention_prefill(xq, kc, vc, spos, slide, sc, True)
+    for i in range(ntok):
+        pos = spos + i
+        t0 = pos + 1 - slide if slide > 0 and pos >= slide else 0
+        dec = O.attention_decode(np.ascontiguousarray(xq[:, i, :]), kc, vc, t0, pos + 1 - t0, np.float32(1.0), sc)
+        assert_attn_close(pre[i].reshape(nh, hd), dec)
+
+
+def test_oracle_output_is_linear_in_values():
+    # weights do not depend on V: scaling V by a power of two scales the output exactly
+    xq, kc, vc = synth.attention_inputs(77, 8, 2, 128, 300)
+    a = O.attention_decode(xq, kc, vc, 10, 250, np.float32(0.088))
+    b = O.attention_decode(xq, kc, (vc * np.float32(4.0)).astype(np.float32), 10, 250, np.float32(0.088))
+    assert np.array_equal(b, a * np.float32(4.0))
+    xq, kc, vc = synth.attention_inputs(78, 4, 1, 64, 60, 60)
+    a = O.attention_prefill(xq, kc, vc, 0, 16)
+    b = O.attention_prefill(xq, kc, (vc * np.float32(0.5)).astype(np.float32), 0, 16)
+    assert np.array_equal(b, a * np.float32(0.5))
+
+
+def test_oracle_weights_sum_to_one():
+    xq, kc, _ = synth.attention_inputs(79, 4, 2, 256, 2000)
+    out = O.attention_decode(xq, kc, np.ones_like(kc), 0, 2000, np.float32(1 / 16), 30.0)
+    assert np.max(np.abs(out - 1.0)) < 1e-5
+    xq, kc, _ = synth.attention_inputs(80, 2, 1, 64, 300, 300)
+    out = O.attention_prefill(xq, kc, np.ones_like(kc), 0, 100)
+    assert np.max(np.abs(out - 1.0)) < 1e-5
