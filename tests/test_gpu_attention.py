@@ -208,3 +208,43 @@ def test_rope_then_decode_attention_matches_oracle_chain():
     oq, okc, ovc = O.qk_norm_rope_cache(xq, xk, xv, kc, vc, freqs, spos, 1.0, nq, nk)
     want = O.attention_decode(oq[:, 0, :], okc, ovc, 0, clen, np.float32(1.0 / 16))
     assert_attn_close(xo.cpu().numpy(), want)
+
+
+# ---- size-independent properties at full size (no oracle needed)
+
+def test_decode_full_window_is_linear_in_values():
+    # Gemma-3-12B global layer (16 query heads over 8 kv heads, a 32768-position
+    # window split over many CTAs and merged): the weights do not depend on V,
+    # so scaling V by a power of two scales every output exactly
+    nh, nkv, hd, clen = 16, 8, 256, 32768
+    g = torch.Generator(device="cuda").manual_seed(5)
+    q = torch.randn((nh, hd), generator=g, device="cuda")
+    kc = torch.randn((nkv, clen, hd), generator=g, device="cuda")
+    vc = torch.randn((nkv, clen, hd), generator=g, device="cuda")
+    a, b = torch.empty((nh, hd), device="cuda"), torch.empty((nh, hd), device="cuda")
+    gcu.dev_attention_decode(a, q, kc, vc, 0, clen, 1.0 / 16)
+    vc.mul_(4.0)
+    gcu.dev_attention_decode(b, q, kc, vc, 0, clen, 1.0 / 16)
+    torch.cuda.synchronize()
+    assert torch.equal(b, a * 4.0)
+    gcu.check_device()
+
+
+def test_prefill_rows_equal_decode_over_their_windows():
+    # a full Gemma-3-1B chunk (512 tokens, 4 heads over 1 kv head) with a
+    # 128-position sliding window: sampled rows of the causal prefill equal
+    # decode attention over the same window (queries pre-scaled, unit scale)
+    nh, nkv, hd, ntok, slide = 4, 1, 256, 512, 128
+    g = torch.Generator(device="cuda").manual_seed(6)
+    xq = torch.randn((nh, ntok, hd), generator=g, device="cuda") * 0.0625
+    kc = torch.randn((nkv, ntok, hd), generator=g, device="cuda")
+    vc = torch.randn((nkv, ntok, hd), generator=g, device="cuda")
+    pre = torch.empty((ntok, nh * hd), device="cuda")
+    gcu.dev_attention_prefill(pre, xq, kc, vc, 0, slide)
+    for i in (0, 1, 63, 64, 127, 128, 129, 300, 511):
+        t0 = i + 1 - slide if i >= slide else 0
+        dec = torch.empty((nh, hd), device="cuda")
+        gcu.dev_attention_decode(dec, xq[:, i, :].contiguous(), kc, vc, t0, i + 1 - t0, 1.0)
+        torch.cuda.synchronize()
+        assert_attn_close(pre[i].view(nh, hd).cpu().numpy(), dec.cpu().numpy())
+    gcu.check_device()
