@@ -25,3 +25,29 @@ def test_prefill_flop_count():
             vis += pos - t0 + 1
         brute = sum(min(spos + i + 1, slide if slide else 10 ** 9) for i in range(n))
         assert vis == brute
+
+
+def test_reference_arm_prints_the_contract_line():
+    # the reference arm runs gemma.c's own functions on host cores: no GPU
+    import json
+    import os
+    import subprocess
+    import sys
+
+    import oracle as O
+    if O.ref() is None:
+        import pytest
+        pytest.skip("reference build not available")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    out = subprocess.run([sys.executable, os.path.join(root, "bench.py"), "--impl", "reference", "--steps", "3",
+                          "--warmup", "3"], capture_output=True, text=True, timeout=300, cwd=root)
+    assert out.returncode == 0, out.stderr[-2000:]
+    line = json.loads(out.stdout.strip().splitlines()[-1])
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                "config", "cpu_baseline", "e2e"):
+        assert key in line, key
+    assert line["impl"] == "reference" and line["steps"] == 3 and line["value"] > 0
+    assert line["e2e"]["value"] == line["value"]
+    assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
+    assert line["cpu_baseline"]["kind"] in ("reference", "port") and line["cpu_baseline"]["cores"] >= 1
+    assert line["config"]["workload"].startswith("prefill1b")
