@@ -12,6 +12,9 @@ any input, so hypothesis draws the shapes and values:
   gemv_int8 of activation row m bit for bit (both dequantize (float)acc *
   (xs * ws)); gemv_int8_multi equals its jobs run one by one; the int32
   sums are linear in the activation codes.
+- where the reference build is present: drawn inputs (values on rounding
+  boundaries among them) give the same bits through the restatement and
+  through gemma.c's own compiled quantize_acts, gemv_int8 and gemm_int8.
 """
 import numpy as np
 import pytest
@@ -100,3 +103,27 @@ def test_int32_sums_are_linear_in_the_codes(data, m, n, k):
     b = data.draw(hnp.arrays(np.int8, (m, k), elements=half))
     lhs = O.acc_int8(mat, (a.astype(np.int16) + b).astype(np.int8))
     assert np.array_equal(lhs, O.acc_int8(mat, a) + O.acc_int8(mat, b))
+
+
+_REF = O.ref()
+
+
+@pytest.mark.skipif(_REF is None, reason="reference build not present on this host")
+@settings(max_examples=30, deadline=None, derandomize=True)
+@given(st.data(), st.integers(1, 6), st.integers(1, 24), st.integers(1, 260))
+def test_oracle_matches_live_reference_on_drawn_inputs(data, m, n, k):
+    # drawn activations (no subnormals: the reference is built with fast math)
+    # through quantize_acts, gemv_int8 and gemm_int8 of the compiled
+    # reference and of the restatement: the same bits
+    R = O.Ref(threads=2)
+    el = st.one_of(st.floats(min_value=-1e4, max_value=1e4, allow_nan=False, allow_subnormal=False, width=32),
+                   st.sampled_from([0.0, 0.5, -0.5, 1.5, -2.5, 127.0]))
+    x = data.draw(hnp.arrays(np.float32, (m, k), elements=el))
+    q1, s1 = O.quantize_acts(x)
+    q2, s2 = R.quantize_acts(x)
+    assert np.array_equal(q1, q2) and np.array_equal(bits(s1), bits(s2))
+    w = data.draw(hnp.arrays(np.int8, (n, k), elements=st.integers(-127, 127)))
+    pos = st.floats(min_value=float(np.float32(1e-4)), max_value=4.0, allow_nan=False, width=32)
+    ws = data.draw(hnp.arrays(np.float32, n, elements=pos))
+    assert np.array_equal(bits(O.gemm_int8(w, ws, q1, s1)), bits(R.gemm_int8(w, ws, q2, s2)))
+    assert np.array_equal(bits(O.gemv_int8(w, ws, q1[0], s1[0])), bits(R.gemv_int8(w, ws, q2[0], s2[0])))
