@@ -1,4 +1,4 @@
-"""Host logic of the row-sharded path on CPU ranks (gloo, world size 2).
+"""Host logic of the row-sharded path on CPU ranks (gloo, world sizes 2 and 4).
 
 Each rank computes its row slice of a W8A8 GEMM/GEMV with the oracle, the
 slices are all-gathered over gloo in rank order, and the re-layout must give
@@ -47,9 +47,9 @@ def _worker(rank, world, port, m, n, k, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("m", [1, 4, 9])
-def test_rowshard_gather_matches_unsharded(m):
-    world, n, k = 2, 96, 640
+@pytest.mark.parametrize("m,world", [(1, 2), (4, 2), (9, 2), (1, 4), (9, 4)])
+def test_rowshard_gather_matches_unsharded(m, world):
+    n, k = 96, 640
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -60,7 +60,7 @@ def test_rowshard_gather_matches_unsharded(m):
         p.join(120)
     assert all(p.exitcode == 0 for p in procs)
     res = dict(q.get(timeout=10) for _ in range(world))
-    assert res == {0: True, 1: True}
+    assert res == {r: True for r in range(world)}
 
 
 def test_row_slice_rejects_uneven():
