@@ -152,3 +152,38 @@ def test_oracle_weights_sum_to_one():
     xq, kc, _ = synth.attention_inputs(80, 2, 1, 64, 300, 300)
     out = O.attention_prefill(xq, kc, np.ones_like(kc), 0, 100)
     assert np.max(np.abs(out - 1.0)) < 1e-5
+
+
+def test_oracle_matches_live_reference_on_drawn_shapes():
+    # hypothesis draws head layouts (uneven groups included), head sizes,
+    # windows, sliding spans, softcaps and the dense path; the restatement
+    # stays within the fp32 bound of gemma.c's own compiled attention
+    hyp = pytest.importorskip("hypothesis")
+    from hypothesis import given, settings, strategies as st
+    R = _ref()
+    if R is None:
+        pytest.skip("reference build not available")
+
+    @settings(max_examples=25, deadline=None, derandomize=True)
+    @given(st.data())
+    def run(data):
+        nkv = data.draw(st.integers(1, 4))
+        nh = data.draw(st.integers(nkv, 4 * nkv))
+        hd = data.draw(st.sampled_from([64, 128, 256]))
+        sc = data.draw(st.sampled_from([0.0, 30.0]))
+        clen = data.draw(st.integers(1, 600))
+        spos = data.draw(st.integers(0, clen - 1))
+        attlen = data.draw(st.integers(1, clen - spos))
+        xq, kc, vc = synth.attention_inputs(1000 + clen, nh, nkv, hd, clen)
+        asc = np.float32(1.0 / np.sqrt(hd))
+        assert_attn_close(O.attention_decode(xq, kc, vc, spos, attlen, asc, sc),
+                          R.attention_decode(xq, kc, vc, spos, attlen, asc, sc))
+        ntok = data.draw(st.integers(1, 120))
+        pspos = data.draw(st.integers(0, 150))
+        slide = data.draw(st.sampled_from([0, 16, 64]))
+        mask = data.draw(st.booleans())
+        xq, kc, vc = synth.attention_inputs(2000 + ntok, nh, nkv, hd, pspos + ntok, ntok)
+        assert_attn_close(O.attention_prefill(xq, kc, vc, pspos, slide, sc, mask),
+                          R.attention_prefill(xq, kc, vc, pspos, slide, sc, mask))
+
+    run()
