@@ -75,3 +75,35 @@ def test_pooling_identity_window():
     ln = (x - mu) / np.sqrt(((x - mu) ** 2).mean(axis=1, keepdims=True) + v["eps"]) * v["post_n"] + v["post_nb"]
     rms = ln / np.sqrt((ln ** 2).mean(axis=1, keepdims=True) + v["eps"]) * (v["norm"] + 1.0)
     assert np.max(np.abs(pooled - rms)) <= 1e-5 * np.max(np.abs(rms))
+
+
+def test_oracle_head_matches_live_reference_on_drawn_shapes():
+    # hypothesis draws patch sizes, patch grids, pooling windows and widths;
+    # the restatement stays within the fp32 bound of gemma.c's forward_vision
+    # head, with at most a few +-1 codes on rounding boundaries
+    pytest.importorskip("hypothesis")
+    from hypothesis import given, settings, strategies as st
+    try:
+        lib = O.ref()
+    except OSError:
+        lib = None
+    if lib is None or not hasattr(lib, "ref_vision_head"):
+        pytest.skip("reference build not available")
+    R = O.Ref(threads=4)
+
+    @settings(max_examples=15, deadline=None, derandomize=True)
+    @given(st.data())
+    def run(data):
+        psize = data.draw(st.integers(1, 16))
+        side = data.draw(st.integers(1, 6))
+        ppi = side * data.draw(st.integers(1, 4))
+        dim = 4 * data.draw(st.integers(1, 48))
+        tdim = data.draw(st.integers(1, 40))
+        v = synth.vision_head_inputs(700 + ppi * psize, ppi * psize, psize, dim, side * side, tdim)
+        _, pooled, q, s = R.vision_head(v)
+        po, qo, so = O.vision_pool(O.patch_embed(v), v)
+        assert_rows_close(po, pooled)
+        assert_codes_close(qo, q)
+        assert_rows_close(so, s)
+
+    run()
