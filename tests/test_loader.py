@@ -114,3 +114,39 @@ def test_capacity_and_counting():
     recs = (gcu.QTensor * 3)()
     assert gcu.lib().gcu_bin_qtensors(buf.ctypes.data, buf.nbytes, 1, recs, 3) == n
     assert [r.kind for r in recs] == [0, 1, 2]
+
+
+def test_parser_matches_live_reference_on_drawn_configs():
+    # hypothesis draws decoder and SigLIP configurations (head layouts, odd
+    # widths and vocabularies, every norm flag, with and without a vision
+    # tower); the parser and gemma.c's mmap_gemma_model must find the same
+    # records in the same bytes
+    pytest.importorskip("hypothesis")
+    from hypothesis import given, settings, strategies as st
+    R = _ref_with_layout()
+    if R is None:
+        pytest.skip("reference build not available")
+
+    @settings(max_examples=12, deadline=None, derandomize=True)
+    @given(st.data())
+    def run(data):
+        nkv = data.draw(st.integers(1, 3))
+        text = dict(nl=data.draw(st.integers(1, 3)), n_heads=nkv * data.draw(st.integers(1, 3)), nkv=nkv,
+                    hdim=2 * data.draw(st.integers(2, 16)), dim=data.draw(st.integers(8, 80)),
+                    mlp_dim=data.draw(st.integers(4, 64)), nvocab=data.draw(st.integers(20, 700)),
+                    qk_norm=data.draw(st.booleans()), mlp_pre=data.draw(st.booleans()),
+                    mlp_pst=data.draw(st.booleans()))
+        vision = None
+        if data.draw(st.booleans()):
+            psize = data.draw(st.integers(1, 8))
+            vision = dict(nl=data.draw(st.integers(0, 2)), n_heads=data.draw(st.integers(1, 2)),
+                          mlp_dim=data.draw(st.integers(4, 40)), dim=data.draw(st.integers(4, 40)),
+                          img_px=psize * data.draw(st.integers(1, 6)), psize=psize)
+        buf, _ = binfmt.image(text, vision, seed=data.draw(st.integers(0, 99)))
+        with tempfile.TemporaryDirectory() as d:
+            path = os.path.join(d, "m.bin")
+            buf.tofile(path)
+            for allow_mm in (True, False):
+                assert gcu.bin_qtensors(buf, allow_mm) == R.bin_layout(path, allow_mm)
+
+    run()
