@@ -187,3 +187,34 @@ def test_oracle_matches_live_reference_on_drawn_shapes():
                           R.attention_prefill(xq, kc, vc, pspos, slide, sc, mask))
 
     run()
+
+
+def test_oracle_rope_matches_live_reference_on_drawn_shapes():
+    # QK norm + RoPE + cache write on drawn head layouts, head sizes,
+    # positions, chunk lengths and norm settings, with the reference's own
+    # rope_freqs tables (local and global theta)
+    pytest.importorskip("hypothesis")
+    from hypothesis import given, settings, strategies as st
+    R = _ref()
+    if R is None or not hasattr(R.lib, "ref_qk_norm_rope_cache"):
+        pytest.skip("reference build not available")
+
+    @settings(max_examples=15, deadline=None, derandomize=True)
+    @given(st.data())
+    def run(data):
+        nkv = data.draw(st.integers(1, 4))
+        nh = data.draw(st.integers(nkv, 3 * nkv))
+        hd = data.draw(st.sampled_from([64, 128, 256]))
+        ntok = data.draw(st.integers(1, 40))
+        spos = data.draw(st.integers(0, 3000))
+        norm = data.draw(st.booleans())
+        qs = data.draw(st.sampled_from([1.0, 0.0625, 0.088]))
+        slid, full = R.rope_freqs(hd, 10000.0, 1e6, spos, ntok)
+        xq, xk, xv, kc, vc, nq, nk = synth.rope_inputs(3000 + ntok, nh, nkv, hd, spos + ntok + 2, ntok, norm)
+        for fr in (slid, full):
+            a = O.qk_norm_rope_cache(xq, xk, xv, kc, vc, fr, spos, qs, nq, nk)
+            b = R.qk_norm_rope_cache(xq, xk, xv, kc, vc, fr, spos, qs, nq, nk)
+            for x, y in zip(a, b):
+                assert_attn_close(x, y)
+
+    run()
