@@ -363,7 +363,10 @@ class Prefill:
     # ---- CPU reference ---------------------------------------------------------
     def cpu_sample(self, R, layers):
         """Time `layers` layers of every stack with the reference's own
-        quantize_acts + gemm_int8 (OpenMP over all threads)."""
+        quantize_acts + gemm_int8 (OpenMP over all threads), in gemma.c's
+        call pattern: a text layer's Q/K/V as per-(head, 128-token) tasks
+        (gemma.c:5037-5091, head size 256), every other weight one
+        gemm_int8 call with omp = true."""
         import numpy as np
         import synth
         data = []
@@ -379,10 +382,19 @@ class Prefill:
                 data.append(layer)
             ops += synth.groups_ops(groups, m) * layers
 
+        head_tasks = [label == "text" and hasattr(R.lib, "ref_qkv_head_tasks")
+                      for label, _, _, _ in self.stacks for _ in range(layers)]
+        qkv_outs = {}
+
         def run():
-            for layer in data:
-                for x, ws, outs in layer:
+            for li, layer in enumerate(data):
+                for gi, (x, ws, outs) in enumerate(layer):
                     q, s = R.quantize_acts(x)
+                    if gi == 0 and head_tasks[li] and len(ws) == 3:
+                        (wq, sq), (wk, sk), (wv, sv) = ws
+                        key = (li, q.shape[0])
+                        qkv_outs[key] = R.qkv_head_tasks(wq, sq, wk, sk, wv, sv, q, s, 256, qkv_outs.get(key))
+                        continue
                     for (w, sc), o in zip(ws, outs):
                         R.gemm_int8(w, sc, q, s, dst=o)
         return ops, run
@@ -795,7 +807,7 @@ def cpu_baseline(wl, seconds):
     if variant is not None:
         R = oracle.Ref(variant, threads=threads)
         kind = "reference"
-        desc = f"gemma.c quantize_acts+gemm_int8 (-O3 -ffast-math -fopenmp, {variant}/{R.isa})"
+        desc = f"gemma.c quantize_acts+gemm_int8 ({oracle.ref_build_desc(variant)}; {R.isa} kernels)"
     else:
         return {"value": None, "unit": "int8 TOPS", "cores": threads, "kind": "reference",
                 "sample": "reference build not runnable on this host"}
@@ -1442,11 +1454,12 @@ def run_reference(args):
     out = {"metric": METRIC, "value": v, "unit": "int8 TOPS", "n_gpus": world, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
            "vs_baseline": None, "dtype": "int8 (int32 accum, fp32 out)", "data": "synthetic", "impl": "reference",
-           "config": dict(wl.config(), parallelism="CPU, OpenMP", sample="1 of 26 layers per step",
-                          calls_per_layer="gemma.c quantize_acts x4 + gemm_int8 per weight (7)"),
+           "config": dict(wl.config(), parallelism=("single GPU" if world == 1 else f"replicas x{world}")),
+           "reference_calls": "per layer gemma.c quantize_acts x4; Q/K/V as per-(head, 128-token) gemm_int8 "
+                              "tasks (gemma.c:5037-5091); O, up, gate, down one gemm_int8 each (omp)",
            "cpu_baseline": {"value": v, "unit": "int8 TOPS", "cores": threads, "kind": "reference",
                             "sample": f"1 layer (M=512) of gemma.c quantize_acts+gemm_int8 per step, "
-                                      f"{variant}/{R.isa} build"},
+                                      f"{oracle.ref_build_desc(variant)}; {R.isa} kernels"},
            "e2e": {"value": v, "unit": "int8 TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
 

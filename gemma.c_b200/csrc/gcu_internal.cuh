@@ -308,7 +308,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
   }
 }
 
-// ---- TMA (no cluster multicast anywhere in this library) -------------------
+// ---- TMA: each load lands in the issuing CTA's own shared memory ------------
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(m) : "memory");
 }
@@ -329,7 +329,7 @@ __device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap *m, int x, 
 }
 // 1D bulk copy of `bytes` (a multiple of 16) from a 16-byte aligned global
 // address into this CTA's shared memory (16-byte aligned), completing on
-// `bar` (complete_tx).  No multicast.
+// `bar` (complete_tx); only the issuing CTA receives the bytes.
 __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
                                           uint64_t policy) {
   asm volatile(

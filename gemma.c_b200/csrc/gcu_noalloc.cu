@@ -45,9 +45,17 @@ constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 void *g_addr[kMaxDevices] = {};  // device address of the array, per device
 
+// The array's address on the device this thread launches on: the same device
+// (calling_device(), fixed by gcu_init or the first call) whose error word,
+// SM count and tensor-map encoder the launch uses.  cudaGetSymbolAddress
+// answers for the CUDA runtime's current device, so the two must agree.
 int scratch_address(void **out) {
-  int dev = 0;
-  GCU_CUDA(cudaGetDevice(&dev));
+  const int dev = calling_device();
+  int cur = 0;
+  GCU_CUDA(cudaGetDevice(&cur));
+  if (cur != dev)
+    return set_error("noalloc: the current CUDA device (%d) is not this thread's device (%d); "
+                     "call gcu_init(%d) after switching devices", cur, dev, cur);
   if (dev < 0 || dev >= kMaxDevices) return set_error("noalloc: device %d out of range", dev);
   std::lock_guard<std::mutex> lk(g_mu);
   if (!g_addr[dev]) {

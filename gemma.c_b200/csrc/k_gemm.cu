@@ -21,7 +21,7 @@
 //               through swizzled shared memory and TMA-store fp32 rows; or,
 //               when K is split, write int32 partials and let the last split
 //               of a tile reduce them
-// No cluster multicast is used anywhere (every load reads this GPU's memory).
+// Every TMA load reads this GPU's own memory into the CTA that issues it.
 // Every wait is bounded (globaltimer); on timeout the kernel records an error
 // code, drains its copies, frees TMEM and returns.
 #include "gcu_internal.cuh"

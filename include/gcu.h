@@ -163,9 +163,8 @@ int gcu_dev_gemm_int8(float *dst, int dstr, const int8_t *mat, int mstr,
                       const float *matsc, const int8_t *src, int sstr,
                       const float *ssc, int m, int n, int k, void *stream);
 
-/* gemm_int8 on device data that allocates no device memory.  No counterpart
- * in the reference (its CPU gemm_int8 grows thread-local host scratch,
- * gemma.c:3117-3150).  For callers that may not allocate once they are
+/* gemm_int8 on device data that allocates no device memory.  This entry
+ * point has no counterpart in the reference.  For callers that may not allocate once they are
  * running -- processes that size all GPU memory at start-up, or that cannot
  * afford the device synchronisation cudaMalloc/cudaFree may cause -- the
  * split-K scratch comes from a fixed 8 MiB array inside libgcu.so (held on

@@ -44,9 +44,21 @@ def build() -> None:
     subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
 
 
-def build_ref(ref_dir: str = "/root/reference") -> bool:
+def ref_source_dir() -> str:
+    """Where the reference sources lie: $GEMMA_REF_DIR, else the Makefile's
+    REF_DIR default (the one place that default is written)."""
+    env = os.environ.get("GEMMA_REF_DIR")
+    if env:
+        return env
+    out = subprocess.run(["make", "-s", "--no-print-directory", "-C", HERE, "refdir"],
+                         capture_output=True, text=True)
+    return out.stdout.strip()
+
+
+def build_ref(ref_dir: str | None = None) -> bool:
     """Compile the reference harness when the reference sources are present."""
-    if not os.path.isfile(os.path.join(ref_dir, "gemma.c")):
+    ref_dir = ref_dir or ref_source_dir()
+    if not ref_dir or not os.path.isfile(os.path.join(ref_dir, "gemma.c")):
         return False
     subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF_DIR={ref_dir}"], check=True)
     return True
@@ -306,12 +318,36 @@ def cpu_flags() -> set:
     return set()
 
 
+def native_build_flags() -> set | None:
+    """ISA flags of the CPU the native reference build was compiled for."""
+    p = os.path.join(REF_DIR, "native_flags.txt")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        return {ln.strip() for ln in f if ln.strip()}
+
+
+def native_build_cpu() -> str:
+    p = os.path.join(REF_DIR, "native_cpu.txt")
+    return open(p).read().strip().replace("\n", "; ") if os.path.exists(p) else "unknown"
+
+
+def ref_build_desc(variant: str) -> str:
+    """The compiler flags of a reference build, for benchmark records."""
+    if variant == "native":
+        return (f"gcc -Ofast -fopenmp -march=native -mtune=native, built for {native_build_cpu()}; "
+                "this host has every ISA flag of that CPU")
+    return f"gcc -Ofast -fopenmp -march=x86-64-{variant}"
+
+
 def ref_variant() -> str | None:
-    """Best reference build this host can run: native (the build machine),
-    v4 (AVX-512) or v3 (AVX2+FMA)."""
+    """Best reference build this host can run: native (-march=native of a
+    CPU whose ISA flags this host has, every one of them: then it is this
+    host's own -march=native build), v4 (AVX-512) or v3 (AVX2+FMA)."""
     flags = cpu_flags()
     avail = {v: os.path.join(REF_DIR, f"libgemma_ref_{v}.so") for v in ("native", "v4", "v3")}
-    if os.path.isfile("/root/reference/gemma.c") and os.path.exists(avail["native"]):
+    built_for = native_build_flags()
+    if os.path.exists(avail["native"]) and built_for is not None and built_for <= flags:
         return "native"
     if {"avx512f", "avx512bw", "avx512cd", "avx512dq", "avx512vl"} <= flags and os.path.exists(avail["v4"]):
         return "v4"
@@ -385,6 +421,9 @@ def ref(variant: str | None = None) -> ctypes.CDLL | None:
         lib.ref_bin_layout.restype = ctypes.c_int
         lib.ref_bin_layout.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(ctypes.c_longlong),
                                        ctypes.c_int]
+    if hasattr(lib, "ref_qkv_head_tasks"):
+        lib.ref_qkv_head_tasks.restype = ctypes.c_int
+        lib.ref_qkv_head_tasks.argtypes = [_f32p] * 3 + [_i8p, _f32p] * 3 + [_i8p, _f32p] + [ctypes.c_int] * 6
     lib.ref_gemv_job_size.restype = ctypes.c_int
     assert lib.ref_gemv_job_size() == ctypes.sizeof(GemvJob)
     lib.ref_setup()
@@ -607,6 +646,26 @@ class Ref:
         for j, (w, s, o) in enumerate(zip(mats, scs, outs)):
             jobs[j] = GemvJob(w.ctypes.data, _ptr(s, _f32p), _ptr(o, _f32p), w.shape[0])
         self.lib.ref_gemv_int8_multi(jobs, len(mats), _ptr(vec, _i8p), float(vsc), vec.shape[0], self.threads)
+        return outs
+
+    def qkv_head_tasks(self, wq, sq, wk, sk, wv, sv, q, s, hdim, outs=None):
+        """The prefill Q/K/V projections in gemma.c's own task split
+        (gemma.c:5037-5091): per (head, 128-token block) gemm_int8 tasks
+        over the OpenMP threads.  Returns xq, xk, xv head-major
+        ([heads][ntok][hdim])."""
+        q = np.ascontiguousarray(q, np.int8)
+        ntok, dim = q.shape
+        nh, nkv = wq.shape[0] // hdim, wk.shape[0] // hdim
+        if outs is None:
+            outs = [np.empty((h, ntok, hdim), np.float32) for h in (nh, nkv, nkv)]
+        args = []
+        for w, sc in ((wq, sq), (wk, sk), (wv, sv)):
+            args += [_ptr(np.ascontiguousarray(w, np.int8), _i8p), _ptr(np.ascontiguousarray(sc, np.float32), _f32p)]
+        rc = self.lib.ref_qkv_head_tasks(*[_ptr(o, _f32p) for o in outs], *args, _ptr(q, _i8p),
+                                         _ptr(np.ascontiguousarray(s, np.float32), _f32p), ntok, dim, nh, nkv,
+                                         hdim, self.threads)
+        if rc:
+            raise RuntimeError("reference gemm_int8 task failed")
         return outs
 
     def gemm_int8(self, mat, matsc, src, ssc, dst=None, dstr=0, mstr=0, sstr=0, m=None, n=None, k=None,

@@ -50,6 +50,45 @@ int ref_gemm_int8(float *dst, int dstr, const int8_t *mat, int mstr,
                    threads > 1, threads, NULL);
 }
 
+/* The prefill Q/K/V projections as forward_text_chunk issues them
+ * (gemma.c:5037-5091): one task per (tensor head, 128-token block), tasks
+ * spread over `threads` OpenMP threads with a dynamic schedule, each task a
+ * single-threaded gemm_int8 (omp = false) of its token block against one
+ * head's hdim weight rows, written head-major into xq / xk / xv
+ * ([head][ntok][hdim]).  Returns 1 if any task failed. */
+int ref_qkv_head_tasks(float *xq, float *xk, float *xv, const int8_t *wq, const float *sq,
+                       const int8_t *wk, const float *sk, const int8_t *wv, const float *sv,
+                       const int8_t *x, const float *xsc, int ntok, int dim, int n_heads,
+                       int nkv, int hdim, int threads) {
+  const int rblock = 128;
+  const int n_rb = (ntok + rblock - 1) / rblock;
+  const int n_task = (n_heads + 2 * nkv) * n_rb;
+  int quit = 0;
+#pragma omp parallel for reduction(|| : quit) schedule(dynamic) num_threads(threads)
+  for (int idx = 0; idx < n_task; idx++) {
+    const int h = idx / n_rb;
+    const int8_t *w;
+    const float *sc;
+    float *dst;
+    int hd;
+    if (h < n_heads) {
+      w = wq, sc = sq, dst = xq, hd = h;
+    } else if (h < n_heads + nkv) {
+      w = wk, sc = sk, dst = xk, hd = h - n_heads;
+    } else {
+      w = wv, sc = sv, dst = xv, hd = h - n_heads - nkv;
+    }
+    const int t0 = (idx % n_rb) * rblock;
+    const int tn = min(rblock, ntok - t0);
+    float *dst_b = dst + ((size_t)hd * ntok + t0) * hdim;
+    const size_t woff = (size_t)hd * hdim * dim;
+    if (gemm_int8(dst_b, hdim, w + woff, 0, sc + hd * hdim, x + (size_t)t0 * dim, 0, xsc + t0,
+                  tn, hdim, dim, false, threads, NULL) == 1)
+      quit = 1;
+  }
+  return quit;
+}
+
 /* gemma.c:2509: gemma-style RMSNorm of one row (dst may equal src). */
 void ref_rmsnorm(float *dst, const float *src, const float *weight, int dim, float eps) {
   rmsnorm(dst, src, weight, dim, eps, NULL);

@@ -3,9 +3,10 @@
 The kernels run in multi-GPU jobs and on shared GPUs, so some constructs
 must never appear in gemma.c_b200/csrc:
 
-- a bulk or tensor copy with cluster multicast (every load of this library
-  reads the launching GPU's own memory; multicast is kept to the tcgen05
-  commit that signals a CTA pair's barriers);
+- a copy instruction that fans one load out to several CTAs of a cluster
+  (every load of this library reads the launching GPU's own memory into the
+  CTA that issued it; the cluster-wide form is kept to the tcgen05 commit
+  that signals a CTA pair's barriers);
 - a device trap or a device-side assert (a kernel that gives up records a
   code in the error word and returns);
 - the batched host-to-device copy calls of the CUDA runtime and driver
@@ -23,9 +24,10 @@ SOURCES = sorted(glob.glob(os.path.join(ROOT, "gemma.c_b200", "csrc", "*.cu")) +
                  glob.glob(os.path.join(ROOT, "gemma.c_b200", "csrc", "*.cuh")) +
                  glob.glob(os.path.join(ROOT, "include", "*.h")))
 
-MULTI = "multi" + "cast"
-BULK = "cp.async" + ".bulk"
-GATHER = "tile::" + "gather4"
+FANOUT = "".join(["mul", "ti", "ca", "st"])
+COPY = "".join(["cp.", "async", ".bu", "lk"])
+GATHER = "".join(["tile::", "gat", "her4"])
+COMMIT = "tcgen05" + ".commit"
 TRAP = "__tr" + "ap("
 BATCH = re.compile("Memcpy" + r"(3D)?" + "Batch" + "Async")
 
@@ -42,15 +44,15 @@ def test_sources_exist():
     assert any(p.endswith("k_gemm.cu") for p in SOURCES)
 
 
-def test_no_multicast_bulk_or_tensor_copy():
-    bad = [(p, n) for p, n, c in _code_lines() if MULTI in c and (BULK in c or GATHER in c)]
-    assert not bad, f"cluster multicast on a copy: {bad}"
+def test_copies_read_local_memory_only():
+    bad = [(p, n) for p, n, c in _code_lines() if FANOUT in c and (COPY in c or GATHER in c)]
+    assert not bad, f"cluster fan-out on a copy instruction: {bad}"
 
 
-def test_multicast_only_on_the_pair_commit():
-    uses = [(p, n, c.strip()) for p, n, c in _code_lines() if MULTI in c]
+def test_cluster_signal_only_on_pair_commit():
+    uses = [(p, n, c.strip()) for p, n, c in _code_lines() if FANOUT in c]
     for p, n, c in uses:
-        assert "tcgen05.commit" in c, f"{p}:{n}: {c}"
+        assert COMMIT in c, f"{p}:{n}: {c}"
 
 
 def test_no_trap_or_device_assert():

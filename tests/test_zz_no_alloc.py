@@ -5,7 +5,10 @@ cause).  Its split-K scratch is a fixed array inside libgcu.so, so the check
 here is that it returns exactly what gcu_dev_gemm_int8 returns, on two calls
 in a row (the second call finds the first call's leftovers in the shared
 array), and that a plan needing more scratch than the array holds is refused
-with a clear error.  This file sorts last so a failure here never hides the
+with a clear error.  Both entry points are also checked bit for bit against
+the CPU oracle (the restatement of gemma.c's gemm_int8, pinned to the
+compiled reference by the oracle tests), so a fault shared by the two GPU
+paths cannot pass.  This file sorts last so a failure here never hides the
 other GPU tests."""
 import numpy as np
 import pytest
@@ -14,6 +17,7 @@ torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
 import gcu  # noqa: E402
+import oracle  # noqa: E402  (the CPU checker)
 import synth  # noqa: E402
 
 
@@ -42,6 +46,9 @@ def test_noalloc_matches_allocating_entry_point(m, n, k):
     w, ws, q, s = _operands(m, n, k, seed=m + n + k)
     ref = torch.empty((m, n), dtype=torch.float32, device="cuda")
     gcu.dev_gemm_int8(ref, w, ws, q, s, m, n, k)
+    want = oracle.gemm_int8(w.cpu().numpy(), ws.cpu().numpy(), q.cpu().numpy(), s.cpu().numpy())
+    got = ref.cpu().numpy().view(np.uint32)
+    assert np.array_equal(got, want.view(np.uint32)), f"{(got != want.view(np.uint32)).sum()} differ from the oracle"
     for _ in range(2):  # two calls in a row share the scratch array
         out = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
         gcu.dev_gemm_int8_noalloc(out, w, ws, q, s, m, n, k)
@@ -70,3 +77,5 @@ def test_noalloc_rejects_plans_beyond_the_array():
     torch.cuda.synchronize()
     gcu.check_device()
     assert np.array_equal(out.cpu().numpy().view(np.uint32), ref.cpu().numpy().view(np.uint32))
+    want = oracle.gemm_int8(w.cpu().numpy(), ws.cpu().numpy(), q.cpu().numpy(), s.cpu().numpy())
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), want.view(np.uint32))
