@@ -44,6 +44,8 @@ import sys
 import threading
 import time
 
+import numpy as np
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "gemma.c_b200"))
 
@@ -321,6 +323,12 @@ class Prefill:
             for g in hl:
                 for w, s in g["w"]:
                     gcu.register_weight(w, s)
+
+    def unregister_host(self, gcu):
+        for hl in self.H:
+            for g in hl:
+                for w, _ in g["w"]:
+                    gcu.unregister_weight(w)
 
     def step_host(self, gcu, rec=None):
         """One step through the host-pointer ABI in gemma.c's call order.
@@ -601,38 +609,23 @@ class LmHead:
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
-def run_ours(args):
-    import torch
-    world, rank, local = dist_setup(args)
-    device = torch.device("cuda", local)
-    torch.cuda.set_device(device)
-    import gcu
-    gcu.init(local)
-    peaks = load_peaks()
-    if args.workload in PREFILL:
-        wl = Prefill(args.workload, seed=rank, fused=args.fused, world=world, rank=rank, layers=args.layers)
-    elif args.workload in DECODE:
-        wl = Decode(args.workload, seed=rank, fused=not args.unfused, world=world, rank=rank, layers=args.layers)
-    else:
-        wl = LmHead(world, rank)
-    if wl.needs_comm:
-        uid = bytearray(128)
-        if rank == 0:
-            uid = bytearray(gcu.comm_unique_id())
-        import torch.distributed as dist
-        obj = [bytes(uid)]
-        dist.broadcast_object_list(obj, src=0)
-        gcu.comm_init(rank, world, obj[0])
-    wl.build(device)
-    torch.cuda.synchronize()
+def make_workload(name, args, world, rank, batch=1):
+    if name in PREFILL:
+        return Prefill(name, seed=rank, fused=args.fused, world=world, rank=rank, layers=args.layers)
+    if name in DECODE:
+        return Decode(name, seed=rank, fused=not args.unfused, world=world, rank=rank, layers=args.layers)
+    return LmHead(world, rank, batch=batch)
 
-    stream = torch.cuda.Stream(device)
-    # eager warm-up (allocates the split-K workspace before capture)
+
+def time_workload(wl, gcu, stream, args, world):
+    """Eager warm-up, CUDA-graph capture where the step holds no NCCL call,
+    `warmup` untimed steps, then `steps` timed steps between CUDA events on
+    the launching stream.  Returns (ms per step, max over ranks; graph)."""
+    import torch
     with torch.cuda.stream(stream):
-        wl.step(gcu)
+        wl.step(gcu)  # allocates the split-K workspace before capture
     stream.synchronize()
     gcu.check_device()
-
     # a sharded step is graph-captured only when every all-gather is the fused
     # peer-load GEMV (no NCCL call inside the step): sharded decode with the
     # peers mapped, never sharded prefill (m > 8 all-gathers through NCCL)
@@ -656,11 +649,6 @@ def run_ours(args):
             one()
     torch.cuda.synchronize()
     barrier(world)
-    clocks = Clocks(local)
-    clocks.start()
-    time.sleep(0.3)
-    torch.cuda.synchronize()
-    barrier(world)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
@@ -670,49 +658,110 @@ def run_ours(args):
         e1.record(stream)
     torch.cuda.synchronize()
     barrier(world)
-    ms = e0.elapsed_time(e1) / args.steps
-    ms = max_over_ranks(ms, world)
-    clk = clocks.stop()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
     gcu.check_device()
+    return ms, graph
 
-    # per-kernel-class durations: the step's launches of one kernel class
-    # only (same inputs, same order), captured as a CUDA graph and replayed
-    # `steps` times between CUDA events on the launching stream; the
-    # average launch duration includes the graph's inter-kernel gap
+
+def class_profile(wl, gcu, stream, steps):
+    """Per-kernel-class durations: the step's launches of one kernel class
+    only (same inputs, same order), captured as a CUDA graph and replayed
+    `steps` times between CUDA events on the launching stream; the average
+    launch duration includes the graph's inter-kernel gap."""
+    import torch
     prof = {}
-    if use_graph:
-        for kind in wl.kinds:
-            acc = {"launches": 0, "bytes": 0, "ops": 0}
+    for kind in wl.kinds:
+        acc = {"launches": 0, "bytes": 0, "ops": 0}
 
-            def want(k, nbytes, ops, kind=kind, acc=acc):
-                if k != kind:
-                    return False
-                acc["launches"] += 1
-                acc["bytes"] += nbytes
-                acc["ops"] += ops
-                return True
+        def want(k, nbytes, ops, kind=kind, acc=acc):
+            if k != kind:
+                return False
+            acc["launches"] += 1
+            acc["bytes"] += nbytes
+            acc["ops"] += ops
+            return True
 
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=stream):
-                wl.step(gcu, want=want)
-            with torch.cuda.stream(stream):
-                for _ in range(2):
-                    g.replay()
-                k0 = torch.cuda.Event(enable_timing=True)
-                k1 = torch.cuda.Event(enable_timing=True)
-                k0.record(stream)
-                for _ in range(args.steps):
-                    g.replay()
-                k1.record(stream)
-            torch.cuda.synchronize()
-            prof[kind] = {"launches": acc["launches"] * args.steps, "ms": k0.elapsed_time(k1),
-                          "bytes": acc["bytes"] * args.steps, "ops": acc["ops"] * args.steps}
-            del g
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            wl.step(gcu, want=want)
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                g.replay()
+            k0 = torch.cuda.Event(enable_timing=True)
+            k1 = torch.cuda.Event(enable_timing=True)
+            k0.record(stream)
+            for _ in range(steps):
+                g.replay()
+            k1.record(stream)
+        torch.cuda.synchronize()
+        prof[kind] = {"launches": acc["launches"] * steps, "ms": k0.elapsed_time(k1),
+                      "bytes": acc["bytes"] * steps, "ops": acc["ops"] * steps}
+        del g
+    return prof
+
+
+def roofline_of(prof, peaks, traffic_file=None, kind=None):
+    """Roofline of the dominant kernel class (or of `kind`) from class_profile
+    numbers: algorithmic bytes (ops) per launch over the average launch."""
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+    dom = kind or max(prof, key=lambda k: prof[k]["ms"])
+    d = prof[dom]
+    t = d["ms"] * 1e-3
+    t_hbm = d["bytes"] / (peaks["hbm_gbs"] * 1e9)
+    t_tc = d["ops"] / (int8_peak * 1e12) if d["ops"] else 0.0
+    if t_tc > t_hbm:
+        roof = {"bound": "tensor", "achieved": d["ops"] / t / 1e12, "peak": int8_peak, "unit": "TOPS",
+                "peak_src": f"2 x {peaks['src']} bf16 dense"}
+    else:
+        roof = {"bound": "hbm", "achieved": d["bytes"] / t / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "peak_src": f"{peaks['src']} copy bandwidth"}
+    roof.update(frac=roof["achieved"] / roof["peak"], kernel=dom, launches=d["launches"],
+                avg_launch_us=d["ms"] * 1e3 / d["launches"],
+                bytes_per_launch=d["bytes"] / d["launches"], ops_per_launch=d["ops"] / d["launches"],
+                roofline_time_frac=max(t_hbm, t_tc) / t, traffic=None)
+    if traffic_file and os.path.exists(traffic_file):
+        # ncu dram__bytes_read.sum + dram__bytes_write.sum per launch of this
+        # class, from a capture of the same build (profiles/); the fp32
+        # outputs usually leave L2 after the kernel ends, so the in-kernel
+        # write counter can read ~0 and the figure is then reads-only, to be
+        # set against the algorithmic READ bytes recorded beside it
+        rec = json.load(open(traffic_file)).get("kernels", {}).get(dom)
+        if rec is not None:
+            roof["traffic"] = rec["read_bytes"] + rec["write_bytes"]
+            roof["traffic_detail"] = rec
+    kernels = {k: {"launches": v["launches"], "share": v["ms"] / sum(x["ms"] for x in prof.values()),
+                   "avg_us": v["ms"] * 1e3 / v["launches"]} for k, v in prof.items()}
+    return roof, kernels
+
+
+def run_ours(args):
+    import torch
+    world, rank, local = dist_setup(args)
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    import gcu
+    gcu.init(local)
+    peaks = load_peaks()
+    wl = make_workload(args.workload, args, world, rank)
+    comm_on = False
+    if wl.needs_comm or (args.workload == "prefill1b" and world > 1 and not args.no_decode):
+        comm_init(gcu, rank, world)
+        comm_on = True
+    wl.build(device)
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.Stream(device)
+    barrier(world)
+    clocks = Clocks(local)
+    clocks.start()
+    time.sleep(0.3)
+    ms, graph = time_workload(wl, gcu, stream, args, world)
+    clk = clocks.stop()
+    prof = class_profile(wl, gcu, stream, args.steps) if graph is not None else {}
 
     out = {"metric": METRIC, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
            "ms_per_step": ms, "higher_is_better": True, "vs_baseline": None, "data": "synthetic",
            "impl": "ours"}
-    int8_peak = 2.0 * peaks["bf16_tflops"]
     # replicas: every rank runs the whole workload (weak scaling, value sums
     # them); sharded: the ranks share one workload (strong scaling)
     copies = 1 if wl.needs_comm else world
@@ -740,29 +789,8 @@ def run_ours(args):
 
     # roofline of the dominant kernel
     if prof:
-        dom = max(prof, key=lambda k: prof[k]["ms"])
-        d = prof[dom]
-        t = d["ms"] * 1e-3
-        t_hbm = d["bytes"] / (peaks["hbm_gbs"] * 1e9)
-        t_tc = d["ops"] / (int8_peak * 1e12) if d["ops"] else 0.0
-        if t_tc > t_hbm:
-            ach = d["ops"] / t / 1e12
-            roof = {"bound": "tensor", "achieved": ach, "peak": int8_peak, "unit": "TOPS",
-                    "peak_src": f"2 x {peaks['src']} bf16 dense"}
-        else:
-            ach = d["bytes"] / t / 1e9
-            roof = {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                    "peak_src": f"{peaks['src']} copy bandwidth"}
-        roof.update(frac=roof["achieved"] / roof["peak"], kernel=dom, launches=d["launches"],
-                    avg_launch_us=d["ms"] * 1e3 / d["launches"],
-                    bytes_per_launch=d["bytes"] / d["launches"], ops_per_launch=d["ops"] / d["launches"],
-                    roofline_time_frac=max(t_hbm, t_tc) / t, traffic=None)
-        tr = os.path.join(ROOT, "profiles", f"traffic_{wl.name}.json")
-        if os.path.exists(tr):
-            roof["traffic"] = json.load(open(tr)).get(dom)
-        out["roofline"] = roof
-        out["kernels"] = {k: {"launches": v["launches"], "share": v["ms"] / sum(x["ms"] for x in prof.values()),
-                              "avg_us": v["ms"] * 1e3 / v["launches"]} for k, v in prof.items()}
+        out["roofline"], out["kernels"] = roofline_of(
+            prof, peaks, os.path.join(ROOT, "profiles", f"traffic_{wl.name}.json"))
 
     # end to end through the host-pointer ABI
     if isinstance(wl, Prefill) and wl.name == "prefill1b" and not args.no_e2e:
@@ -783,6 +811,7 @@ def run_ours(args):
                       "path": "gcu_quantize_acts + gcu_gemm_int8 host-pointer ABI, registered weights, "
                               "pinned host activations, wall clock around synchronous calls",
                       "calls": wl.host_call_breakdown(gcu)}
+        wl.unregister_host(gcu)
 
     # CPU baseline on rank 0 at N=1 (bounded sample)
     if world == 1 and not args.no_cpu and isinstance(wl, Prefill) and wl.name == "prefill1b":
@@ -790,13 +819,136 @@ def run_ours(args):
 
     if graph is not None:
         del graph
-    if wl.needs_comm:
+    # the decode half of the metric (configs[2] and configs[0] at N=1; the
+    # row-sharded lm_head and 12B decode at N>1), each with its roofline
+    if args.workload == "prefill1b" and not args.no_decode and args.layers == 0:
+        del wl
+        torch.cuda.empty_cache()
+        out["decode"] = decode_records(args, gcu, world, rank, device, stream, peaks)
+    if comm_on:
         gcu.comm_destroy()
     if rank == 0:
         print(json.dumps(out), flush=True)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+def comm_init(gcu, rank, world):
+    import torch.distributed as dist
+    uid = gcu.comm_unique_id() if rank == 0 else None
+    obj = [uid]
+    dist.broadcast_object_list(obj, src=0)
+    gcu.comm_init(rank, world, obj[0])
+
+
+def decode_records(args, gcu, world, rank, device, stream, peaks):
+    """The decode-GEMV half of BASELINE's metric, in HBM GB/s with its
+    roofline.  N=1: configs[2]'s lm_head GEMV 262144 x 2560 at batch 1 and
+    8, and configs[0]'s Gemma-3-270m decode step, each beside the reference's
+    own gemv_int8 / gemv_int8_multi (gemma.c:2765-2837) on the host cores.
+    N>1: the row-sharded lm_head and the 12B decode step with
+    FFN and lm_head rows sharded, with the share of the step
+    spent in the launches that carry the all-gather."""
+    import torch
+    rec = {}
+    if world == 1:
+        cases = [("lmhead4b_b1", "lmhead4b", 1), ("lmhead4b_b8", "lmhead4b", 8), ("decode270m", "decode270m", 1)]
+    else:
+        cases = [("lmhead4b_b1", "lmhead4b", 1), ("decode12b", "decode12b", 1)]
+    for key, name, batch in cases:
+        wl = make_workload(name, args, world, rank, batch=batch)
+        wl.build(device)
+        torch.cuda.synchronize()
+        ms, graph = time_workload(wl, gcu, stream, args, world)
+        prof = class_profile(wl, gcu, stream, args.steps) if graph is not None else {}
+        r = {"workload": wl.config()["workload"], "unit": "GB/s", "ms_per_step": ms,
+             "value": wl.bytes / (ms * 1e-3) / 1e9 * (1 if wl.needs_comm else world),
+             "scaling": "strong" if wl.needs_comm else "weak"}
+        if prof:
+            gemv_kind = max((k for k in wl.kinds if "gemv" in k), key=lambda k: prof[k]["ms"])
+            tf = os.path.join(ROOT, "profiles", f"traffic_{name}.json") if batch == 1 and world == 1 else None
+            r["roofline"], r["kernels"] = roofline_of(prof, peaks, tf, kind=gemv_kind)
+            if world > 1:
+                ag = {k: v for k, v in prof.items() if "allgather" in k}
+                tot = sum(v["ms"] for v in prof.values())
+                r["allgather_launch_share"] = sum(v["ms"] for v in ag.values()) / tot if tot else None
+                for k, v in ag.items():
+                    # time over the HBM floor of the rank's own rows: the
+                    # cross-rank hand-off and the NVLink pull of the others'
+                    floor_us = v["bytes"] / v["launches"] / (peaks["hbm_gbs"] * 1e9) * 1e6
+                    r.setdefault("allgather_overhead_us_per_launch", {})[k] = \
+                        v["ms"] * 1e3 / v["launches"] - floor_us
+        if world == 1 and rank == 0 and not args.no_cpu:
+            r["cpu_baseline"] = decode_cpu_baseline(wl, args.cpu_seconds / 4)
+        rec[key] = r
+        del graph, wl, prof
+        torch.cuda.empty_cache()
+    return rec
+
+
+def decode_cpu_baseline(wl, seconds):
+    """The reference's own GEMV code on the host cores (all threads) over the
+    same weights: gemv_int8 (batch 1) or gemm_int8 (batch 8) for the
+    lm_head; for a decode step, per layer quantize_act + gemv_int8_multi for
+    Q/K/V and gate/up, gemv_int8 for O and down, then the lm_head, as
+    forward_text_decode issues them (gemma.c:4768-4966)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    threads = os.cpu_count() or 1
+    variant = oracle.ref_variant()
+    if variant is None:
+        return {"value": None, "unit": "GB/s", "cores": threads, "kind": "reference",
+                "sample": "reference build not runnable on this host"}
+    R = oracle.Ref(variant, threads=threads)
+    if isinstance(wl, LmHead):
+        w, ws = wl.w.cpu().numpy(), wl.ws.cpu().numpy()
+        x = wl.x.cpu().numpy()
+        q, s = R.quantize_acts(x)
+        out = np.empty((wl.b, w.shape[0]), np.float32)
+        if wl.b == 1:
+            def run():
+                qq, ss = R.quantize_act(x[0])
+                R.gemv_int8(w, ws, qq, ss, dst=out[0])
+            what = "gemma.c quantize_act + gemv_int8 (gemma.c:2765-2788)"
+        else:
+            def run():
+                R.quantize_acts(x)
+                R.gemm_int8(w, ws, q, s, dst=out)
+            what = "gemma.c quantize_acts + gemm_int8 at m = 8 (gemma.c:3937-4054)"
+        nbytes = wl.bytes
+    else:
+        layers = [[(g["x"].cpu().numpy()[0], [(w.cpu().numpy(), sc.cpu().numpy()) for w, sc in g["w"]])
+                   for g in layer] for layer in wl.L]
+        hw, hs = wl.head["w"][0].cpu().numpy(), wl.head["w"][1].cpu().numpy()
+        hx = wl.head["x"].cpu().numpy()[0]
+        outs = [[[np.empty(w.shape[0], np.float32) for w, _ in ws] for _, ws in layer] for layer in layers]
+        hout = np.empty(hw.shape[0], np.float32)
+
+        def run():
+            for layer, lo in zip(layers, outs):
+                for (x, ws), o in zip(layer, lo):
+                    q, s = R.quantize_act(x)
+                    if len(ws) > 1:
+                        R.gemv_int8_multi([w for w, _ in ws], [sc for _, sc in ws], q, s, outs=o)
+                    else:
+                        R.gemv_int8(ws[0][0], ws[0][1], q, s, dst=o[0])
+            q, s = R.quantize_act(hx)
+            R.gemv_int8(hw, hs, q, s, dst=hout)
+        what = ("gemma.c per layer quantize_act + gemv_int8_multi (Q/K/V, gate/up) / gemv_int8 (O, down), "
+                "then the lm_head (gemma.c:4768-4966)")
+        nbytes = wl.bytes
+    run()  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        run()
+        n += 1
+        if time.perf_counter() - t0 > seconds or n >= 20:
+            break
+    dt = (time.perf_counter() - t0) / n
+    return {"value": nbytes / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "reference",
+            "sample": f"{what}, {n} reps of the whole step, {oracle.ref_build_desc(variant)}; {R.isa} kernels",
+            "ms_per_step": dt * 1e3}
 
 
 def cpu_baseline(wl, seconds):
@@ -1479,6 +1631,8 @@ def main():
     ap.add_argument("--fused", action="store_true",
                     help="prefill: issue each quantize+GEMM pair through gcu_dev_quantize_gemm_int8_multi")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-decode", action="store_true",
+                    help="default workload: skip the decode-GEMV sub-records")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--layers", type=int, default=0,
                     help="cut every stack to this many layers (small cases for ncu captures; the line "

@@ -61,6 +61,9 @@ def build_ref(ref_dir: str | None = None) -> bool:
     if not ref_dir or not os.path.isfile(os.path.join(ref_dir, "gemma.c")):
         return False
     subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF_DIR={ref_dir}"], check=True)
+    # gemma.c with the CUDA drop-in, when libgcu.so has been built
+    if os.path.exists(os.path.join(HERE, "..", "gemma.c_b200", "libgcu.so")):
+        subprocess.run(["make", "-s", "-C", HERE, "dropin", f"REF_DIR={ref_dir}"], check=True)
     return True
 
 

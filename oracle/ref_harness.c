@@ -585,3 +585,63 @@ int ref_prefill_chunks(float *logits, float *hid, const float *x0, const int *ch
   ref_free_decoder(&m);
   return rc;
 }
+
+/* 1 when this build routes the hot path through the CUDA drop-in
+ * (gemma_gcu.h, built with -DGEMMA_CUDA), 0 for the reference's own code. */
+int ref_dropin(void) {
+#if defined(GEMMA_CUDA)
+  return 1;
+#else
+  return 0;
+#endif
+}
+
+/* gemma.c's own model path, end to end: setup_gemma_model (gemma.c:6867,
+ * read_gemma_model or mmap_gemma_model, plus the registration hook in a
+ * GEMMA_CUDA build), then optionally forward_gemma_image (gemma.c:5561: the
+ * SigLIP tower, its projection and the image tokens' prefill), then
+ * forward_gemma_prefill (gemma.c:5497) of nprompt tokens in chunks of `chunk`
+ * with logits, then ndecode forward_gemma_decode steps (gemma.c:5456), and
+ * cleanup_gemma_model (gemma.c:6909).  logits receives (1 + ndecode) rows of
+ * nvocab: the prompt's last logits, then each decode step's.  Returns 0, or
+ * 1 when any stage fails (the message is in gemma.c's g_err). */
+int ref_model_run(const char *path, int mmap_on, int allow_mm, int seqlen, int chunk, const float *image,
+                  const int *tokens, int nprompt, int ndecode, float *logits, int nvocab, int threads) {
+  GemmaModel *model = NULL;
+  TextBuffer *tb = NULL;
+  VisionBuffer *vb = NULL;
+  int rc = setup_gemma_model(path, mmap_on != 0, allow_mm != 0, seqlen, chunk, &model, &tb, &vb);
+  int pos = 0;
+  if (rc == 0 && (int)model->decoder->config->nvocab != nvocab) rc = 1;
+  if (rc == 0 && image != NULL)
+    rc = forward_gemma_image(model, tb, vb, image, &pos, false, threads, NULL);
+  if (rc == 0) {
+    rc = forward_gemma_prefill(model, tb, (int *)tokens, nprompt, &pos, chunk, NULL, true, threads, NULL);
+    if (rc == 0) memcpy(logits, tb->logits, (size_t)nvocab * sizeof(float));
+  }
+  for (int i = 0; i < ndecode && rc == 0; i++, pos++) {
+    rc = forward_gemma_decode(model, tb, tokens[nprompt + i], pos, threads, NULL);
+    if (rc == 0) memcpy(logits + (size_t)(1 + i) * nvocab, tb->logits, (size_t)nvocab * sizeof(float));
+  }
+  if (model != NULL) cleanup_gemma_model(model, tb, vb, mmap_on != 0);
+  return rc;
+}
+
+/* Device bytes the registration hook holds while the model is set up
+ * (GEMMA_CUDA builds; -1 elsewhere): setup_gemma_model, gcu_registered_bytes,
+ * cleanup_gemma_model. */
+long long ref_model_registered_bytes(const char *path, int mmap_on, int allow_mm, int seqlen, int chunk) {
+#if defined(GEMMA_CUDA)
+  GemmaModel *model = NULL;
+  TextBuffer *tb = NULL;
+  VisionBuffer *vb = NULL;
+  long long held = -1;
+  if (setup_gemma_model(path, mmap_on != 0, allow_mm != 0, seqlen, chunk, &model, &tb, &vb) == 0)
+    held = (long long)gcu_registered_bytes();
+  if (model != NULL) cleanup_gemma_model(model, tb, vb, mmap_on != 0);
+  return held;
+#else
+  (void)path, (void)mmap_on, (void)allow_mm, (void)seqlen, (void)chunk;
+  return -1;
+#endif
+}
