@@ -64,6 +64,7 @@ enum DevErr : unsigned int {
   DEV_TIMEOUT_PEER = 6,   // a rank of a fused all-gather never signalled
   DEV_TIMEOUT_SPLIT = 7,  // a split-K CTA waited too long for the other splits
   DEV_TIMEOUT_SELFTEST = 8,  // gcu_selftest_bounded_wait's wait (nothing ever completes it)
+  DEV_TIMEOUT_CHAIN = 9,     // a chain launch's grid-wide hand-off between two steps
 };
 unsigned int *dev_error_word();  // device address of the error word
 
@@ -172,6 +173,16 @@ int launch_gemm_tc_jobs(const int8_t *src, long sstr, const float *ssc, int m,
 // split-K workspace and tile counters (device memory owned by the runtime)
 int gemm_workspace(size_t bytes, void **ws, int **counters, int ncounters,
                    cudaStream_t st);
+
+// Shared with the chain kernel (k_chain.cu): TMA tensor maps of the GEMM's
+// operand layouts (int8 [rows][k], box 128 B x box_rows, 128-byte swizzle;
+// fp32 [rows][n], box 32 x 32), and the one-CTA tile planner ((128*mb) x bn
+// tiles, K split) over the cost model of the GEMM launcher.
+int gemm_tmap_i8(CUtensorMap *m, const int8_t *base, int k, int rows, long stride, int box_rows);
+int gemm_tmap_f32(CUtensorMap *m, float *base, int n, int rows, long stride_elems);
+int gemm_plan_one_cta(int m, int k, const int *n, int njobs, int sms, int *bn, int *mb,
+                      int *splits);
+int gemm_split_for(int tiles, int k, int sms);
 
 }  // namespace gcu
 

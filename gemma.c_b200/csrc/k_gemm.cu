@@ -986,11 +986,12 @@ int run_plan(const Plan &pl, const int8_t *src, long sstr, const float *ssc, int
              const GemmArgs *jobs, int njobs, cudaStream_t st, const ExtWorkspace *ext);
 
 // Planner's pick without running anything: the cost model above.
-Plan model_plan(int m, int k, const GemmArgs *jobs, int njobs, int sms) {
+Plan model_plan(int m, int k, const GemmArgs *jobs, int njobs, int sms, bool allow_pair = true) {
   const int kb_total = (k + BK - 1) / BK;
   Plan best{128, 1, 1};
   double best_t = 1e30;
   for (const Shape &sh : kShapes) {
+    if (!allow_pair && sh.mb == kPairMB) continue;
     const int tiles = (m + tile_rows(sh.mb) - 1) / tile_rows(sh.mb) * ntiles_n(jobs, njobs, sh.bn);
     const int sp = sh.mb == kPairMB ? 1 : split_for(tiles, kb_total, sms);
     const double t = estimate_us(m, ntiles_n(jobs, njobs, sh.bn), kb_total, sh.bn, sh.mb, sp, sms);
@@ -1219,5 +1220,29 @@ int launch_gemm_tc(const GemmArgs &a, cudaStream_t st, int force_bn, int force_s
   return launch_gemm_tc_jobs(a.src, a.sstr, a.ssc, a.m, a.k, &a, 1, st, force_bn, force_split,
                              nullptr, force_mb);
 }
+
+// ---- helpers shared with the chain kernel (k_chain.cu) ----------------------
+int gemm_tmap_i8(CUtensorMap *m, const int8_t *base, int k, int rows, long stride, int box_rows) {
+  if (get_encode()) return 1;
+  return make_map_i8(m, base, k, rows, stride, box_rows);
+}
+
+int gemm_tmap_f32(CUtensorMap *m, float *base, int n, int rows, long stride_elems) {
+  if (get_encode()) return 1;
+  return make_map_f32(m, base, n, rows, stride_elems);
+}
+
+int gemm_plan_one_cta(int m, int k, const int *n, int njobs, int sms, int *bn, int *mb, int *splits) {
+  if (njobs < 1 || njobs > kMaxJobs) return set_error("gemm plan: 1..%d jobs (got %d)", kMaxJobs, njobs);
+  GemmArgs jobs[kMaxJobs] = {};
+  for (int j = 0; j < njobs; ++j) jobs[j].n = n[j];
+  const Plan pl = model_plan(m, k, jobs, njobs, sms, false);
+  *bn = pl.bn;
+  *mb = pl.mb;
+  *splits = pl.splits;
+  return 0;
+}
+
+int gemm_split_for(int tiles, int k, int sms) { return split_for(tiles, (k + BK - 1) / BK, sms); }
 
 }  // namespace gcu

@@ -29,6 +29,12 @@ class GemvJob(ctypes.Structure):
     _fields_ = [("w", ctypes.c_void_p), ("sc", ctypes.c_void_p), ("dst", ctypes.c_void_p), ("m", ctypes.c_int)]
 
 
+class QGemmStep(ctypes.Structure):
+    """gcu_qgemm_step: one quantize_acts -> gemm_int8 step of a chain."""
+    _fields_ = [("x", ctypes.c_void_p), ("xstr", ctypes.c_int), ("q", ctypes.c_void_p), ("s", ctypes.c_void_p),
+                ("m", ctypes.c_int), ("k", ctypes.c_int), ("njobs", ctypes.c_int), ("jobs", GemvJob * 4)]
+
+
 class QTensor(ctypes.Structure):
     """gcu_qtensor: one matmul weight of a model image (gemma.c:1102 QTensor
     plus its shape and which weight it is)."""
@@ -72,6 +78,10 @@ SIGNATURES = {
     "gcu_dev_gemm_int8_noalloc": (_int, [_vp, _int, _vp, _int, _vp, _vp, _int, _vp, _int, _int, _int, _vp]),
     "gcu_dev_quantize_gemm_int8_multi": (_int, [ctypes.POINTER(GemvJob), _int, _vp, _vp, _vp, _int, _int, _int,
                                                 _vp]),
+    "gcu_gemm_chain_create": (_int, [ctypes.POINTER(QGemmStep), _int, ctypes.POINTER(_int), ctypes.POINTER(_int)]),
+    "gcu_gemm_chain_run": (_int, [_int, _vp]),
+    "gcu_gemm_chain_plan": (_int, [_int, ctypes.POINTER(_int), _int]),
+    "gcu_gemm_chain_destroy": (_int, [_int]),
     "gcu_comm_unique_id": (_int, [ctypes.c_char_p]),
     "gcu_comm_init": (_int, [_int, _int, ctypes.c_char_p]),
     "gcu_comm_destroy": (_int, []),
@@ -358,6 +368,50 @@ def dev_gemm_int8_multi_tuned(jobs_t, src, ssc, m, k, bn, split, mb=1, stream=No
         jobs[j] = GemvJob(w.data_ptr(), s.data_ptr(), o.data_ptr(), w.shape[0])
     _check(lib().gcu_dev_gemm_int8_multi_tuned(jobs, len(jobs_t), src.data_ptr(), 0, ssc.data_ptr(), m, k, bn,
                                                split, mb, _stream(stream)), "dev_gemm_int8_multi_tuned")
+
+
+class GemmChain:
+    """A chain of quantize_acts -> gemm_int8 steps run as one launch
+    (gcu_gemm_chain_*).  steps: list of (x, q, s, jobs) with device tensors
+    x [m][k] fp32, q [m][k] int8, s [m] fp32 and jobs [(w, sc, dst), ...];
+    force: None or per step (bn, mb, splits)."""
+
+    def __init__(self, steps, force=None):
+        self.handle = 0
+        arr = (QGemmStep * len(steps))()
+        for i, (x, q, s, jobs) in enumerate(steps):
+            st = arr[i]
+            st.x, st.xstr, st.q, st.s = x.data_ptr(), 0, q.data_ptr(), s.data_ptr()
+            st.m, st.k, st.njobs = x.shape[0], x.shape[1], len(jobs)
+            for j, (w, sc, o) in enumerate(jobs[:4]):  # more than 4: the library refuses njobs
+                st.jobs[j] = GemvJob(w.data_ptr(), sc.data_ptr(), o.data_ptr(), w.shape[0])
+        self._keep = steps
+        self.n = len(steps)
+        f = None
+        if force is not None:
+            f = (_int * (3 * len(steps)))(*[v for t in force for v in t])
+        h = _int(0)
+        _check(lib().gcu_gemm_chain_create(arr, len(steps), f, ctypes.byref(h)), "gemm_chain_create")
+        self.handle = h.value
+
+    def run(self, stream=None):
+        _check(lib().gcu_gemm_chain_run(self.handle, _stream(stream)), "gemm_chain_run")
+
+    def plan(self):
+        out = (_int * (3 * self.n))()
+        _check(lib().gcu_gemm_chain_plan(self.handle, out, self.n), "gemm_chain_plan")
+        return [tuple(out[3 * i:3 * i + 3]) for i in range(self.n)]
+
+    def close(self):
+        if self.handle:
+            _check(lib().gcu_gemm_chain_destroy(self.handle), "gemm_chain_destroy")
+            self.handle = 0
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def comm_unique_id() -> bytes:

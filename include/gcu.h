@@ -198,6 +198,40 @@ int gcu_dev_quantize_gemm_int8_multi(const gcu_gemv_job *jobs, int njobs,
                                      int8_t *q, float *s, const float *x,
                                      int xstr, int m, int k, void *stream);
 
+/* ---- chains of quantize_acts -> gemm_int8 steps, one launch -----------------
+ * gemma.c's prefill is a sequence of such pairs (gemma.c:5034-5091 Q/K/V,
+ * 5302-5304 O, 5365-5372 up/gate, 5389-5391 down; the vision tower at
+ * 4497-4633).  A chain runs a list of them in order in ONE persistent
+ * launch: step i quantizes x_i (m_i fp32 rows, row stride xstr floats, 0 =
+ * k) into q_i (dense [m][k]) and s_i, then computes every job's gemm_int8
+ * on them into its dst (dense [m][rows]).  Each step sees everything the
+ * earlier steps wrote (x_i may be an earlier step's dst); weights and their
+ * scales must not be written by the chain.  The bits are those of
+ * gcu_dev_quantize_acts + gcu_dev_gemm_int8_multi called step by step.
+ * Device pointers; m >= 1; k % 16 == 0, k <= 16384; 16-byte aligned x rows,
+ * q and weights; 1..4 jobs per step.
+ * create: plans every step's tiles and encodes its descriptors once (device
+ * memory owned by the handle); the pointers are fixed from then on.
+ * force: NULL, or per step {bn, mb, splits} to pin the tile shape
+ * ((128*mb) x bn, mb 1 with bn 64/128/256 or mb 2 with bn 128/192/256) and
+ * K split (0 = planner's).  run: enqueues cooperative launches on `stream`
+ * (one CTA per SM, all resident at once).  plan: the chosen {bn, mb,
+ * splits} per step.  No single counterpart in the reference. */
+typedef struct {
+  const float *x;
+  int xstr;
+  int8_t *q;
+  float *s;
+  int m, k;
+  int njobs;
+  gcu_gemv_job jobs[4];
+} gcu_qgemm_step;
+int gcu_gemm_chain_create(const gcu_qgemm_step *steps, int nsteps,
+                          const int *force, int *handle);
+int gcu_gemm_chain_run(int handle, void *stream);
+int gcu_gemm_chain_plan(int handle, int *plan, int nsteps);
+int gcu_gemm_chain_destroy(int handle);
+
 /* ---- producers fused with quantize_acts -------------------------------------
  * gemma.c quantizes each block input right after its RMSNorm (rmsnorm,
  * gemma.c:2509-2524, at 4754 / 5026, then quantize_act(s) at 4768 / 5034) and
