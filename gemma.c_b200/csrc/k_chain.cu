@@ -31,7 +31,7 @@
 //   warps 2-9   quantize worker (rows of the pair's x), then GEMM epilogue:
 //               tcgen05.ld, dequant (float)acc * (xs*ws), fp32 out by TMA store;
 //               split-K partials and their reduction as in k_gemm.cu
-// Every wait is bounded (globaltimer); a wait that has run long also gives up
+// Every wait is bounded (cycle counter); a wait that has run long also gives up
 // once any CTA has recorded an error; on error the kernel drains its copies,
 // frees TMEM and returns.  Every TMA load reads this GPU's own memory into the
 // issuing CTA.
@@ -81,25 +81,23 @@ struct alignas(64) PairDesc {
   int wpr, vpt;             // quantize: warps per row, float4 per lane
 };
 
-// The tensor maps travel as kernel parameters (a grid constant), where the
-// TMA unit finds them through the parameter bank; a launch therefore covers
-// at most kParamPairs steps and a longer chain is several launches.
-constexpr int kParamPairs = 24;
-struct PairMaps {
-  CUtensorMap A;
-  CUtensorMap B[kJobs];
-  CUtensorMap D[kJobs];
-};
+// The step descriptors travel as kernel parameters (a grid constant): their
+// fields are read through the constant cache, and the TMA unit finds the
+// tensor maps in the parameter bank.  (Descriptors in global memory cost a
+// dependent L2 round trip per field read in the quantize and epilogue code,
+// about a microsecond each.)  A launch therefore covers at most kParamPairs
+// steps; a longer chain is several launches.
+constexpr int kParamPairs = 22;
 
 struct alignas(64) ChainParams {
-  PairMaps pm[kParamPairs];
-  const PairDesc *pairs;  // this launch's steps
+  PairDesc pd[kParamPairs];
   int npairs;             // <= kParamPairs
   int *sync;       // [2i] CTAs done quantizing pair i, [2i+1] done with its GEMM, [2n] exits
   int32_t *ws;     // split-K partials (pairs run one after another and share it)
   int *counters;   // split-K tile counters (zero between launches)
   unsigned int *err;
 };
+static_assert(sizeof(ChainParams) <= 32764, "kernel parameter limit");
 
 // A pair's geometry, copied to registers at the start of each pair.
 struct Geo {
@@ -144,19 +142,22 @@ __device__ __forceinline__ bool err_set(const unsigned int *err) {
   return *reinterpret_cast<const volatile unsigned int *>(err) != 0u;
 }
 
-// Waits give up after 2 s, or -- once they have waited kErrPollNs, longer
-// than any hand-off of a healthy launch at these sizes takes -- as soon as
-// another wait has recorded an error.  The error word is only read after
-// that point: a load from global memory stalls the waiting thread for about
-// a microsecond, which the MMA issuer cannot afford on every stage.
-constexpr uint64_t kBudgetNs = 2000000000ull;
-constexpr uint64_t kErrPollNs = 20000ull;
+// Waits are timed on the SM's cycle counter: reading %globaltimer costs
+// about 0.1 us on B200, and a waiter that reads it between polls notices a
+// landed stage that much later, on every stage.  A wait gives up after
+// kBudgetCycles (2 s at 2 GHz, longer at lower clocks), or -- once it has
+// waited kErrPollCycles, longer than any hand-off of a healthy launch at these
+// sizes takes -- as soon as another wait has recorded an error.  The error
+// word is only read after that point: a load from global memory stalls the
+// waiting thread for about a microsecond.
+constexpr long long kBudgetCycles = 4000000000ll;
+constexpr long long kErrPollCycles = 40000ll;
 
-__device__ __forceinline__ bool give_up(uint64_t t0, unsigned int *err, unsigned int code) {
-  const uint64_t dt = ptx::globaltimer() - t0;
-  if (dt < kErrPollNs) return false;
+__device__ __forceinline__ bool give_up(long long t0, unsigned int *err, unsigned int code) {
+  const long long dt = clock64() - t0;
+  if (dt < kErrPollCycles) return false;
   if (err_set(err)) return true;
-  if (dt > kBudgetNs) {
+  if (dt > kBudgetCycles) {
     atomicCAS(err, 0u, code);
     return true;
   }
@@ -168,33 +169,35 @@ __device__ __forceinline__ int ld_relaxed_gpu(const int *p) {
   asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void fence_acq_rel_gpu() {
-  asm volatile("fence.acq_rel.gpu;" ::: "memory");
-}
 
 // Wait until *flag >= target, then acquire at gpu scope; bounded.  The spin
-// is relaxed loads with a short back-off and one fence at the end.
-__device__ __forceinline__ bool chain_wait(const int *flag, int target, unsigned int *err) {
+// is relaxed loads with a short back-off; one acquire load at the end.
+__device__ __forceinline__ bool chain_wait(const int *flag, int target, unsigned int *err,
+                                           unsigned int code = DEV_TIMEOUT_CHAIN) {
   if (ld_relaxed_gpu(flag) < target) {
-    const uint64_t t0 = ptx::globaltimer();
+    const long long t0 = clock64();
     int n = 0;
     while (ld_relaxed_gpu(flag) < target) {
       __nanosleep(64);
-      if ((++n & 15) == 0 && give_up(t0, err, DEV_TIMEOUT_CHAIN)) return false;
+      if ((++n & 15) == 0 && give_up(t0, err, code)) return false;
     }
   }
-  fence_acq_rel_gpu();
+  (void)ptx::ld_acquire_gpu(flag);
   return true;
 }
 
-// mbarrier wait, bounded.
+// mbarrier wait, bounded.  `nap` > 0: sleep that many ns between polls, for
+// the 256 epilogue threads, whose spinning would otherwise take issue slots
+// from the producer and MMA threads on the same SM sub-partitions.
 __device__ __forceinline__ bool bar_wait(uint64_t *bar, uint32_t parity, unsigned int *err,
-                                         unsigned int code) {
+                                         unsigned int code, int nap = 0) {
   if (ptx::mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = ptx::globaltimer();
+  const long long t0 = clock64();
   while (true) {
-    for (int i = 0; i < 16; ++i)
+    for (int i = 0; i < 16; ++i) {
       if (ptx::mbar_try_wait(bar, parity)) return true;
+      if (nap) __nanosleep(nap);
+    }
     if (give_up(t0, err, code)) return false;
   }
 }
@@ -206,6 +209,13 @@ __device__ __forceinline__ void red_release_add(int *p, int v) {
   asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// K rotation: every CTA leaves a hand-off at the same moment, and the CTAs
+// that share an operand tile (the N tiles of one M block, the M blocks of one
+// N tile) would all request the same K block at once and queue on the same
+// L2 lines, stage after stage (measured: half the per-SM operand rate).  Each
+// unit therefore starts its K loop at block (tile % nk) and wraps around; the
+// int32 sums are exact, so the order cannot change a bit.
+//
 // The stage ring: stages are placed one after another, wrapping to offset 0
 // when the next stage would run past the end.  The producer and the MMA warp
 // step through the same sequence of stage sizes, so they agree on offsets.
@@ -213,6 +223,57 @@ __device__ __forceinline__ uint32_t ring_place(uint32_t &head, uint32_t bytes) {
   const uint32_t off = head + bytes > (uint32_t)kRingBytes ? 0u : head;
   head = off + bytes;
   return off;
+}
+
+// L2 prefetch of the rows of x this CTA will quantize.  A prefetch returns no
+// data to the CTA, so it may run before the hand-off that orders the step
+// after its producers: a line written later is read fresh from L2.
+__device__ __forceinline__ void prefetch_x_rows(const PairDesc &D) {
+  const int gpc = kEpiWarps / D.wpr;
+  const int total = gridDim.x * gpc;
+  const uint32_t bytes = (uint32_t)D.k * 4u;
+  for (int grp = 0; grp < gpc; ++grp)
+    for (int row = grp * gridDim.x + blockIdx.x; row < D.m; row += total)
+      ptx::bulk_prefetch_l2(D.x + (size_t)row * D.xstr, bytes);
+}
+
+// ---- MMA issue of one stage --------------------------------------------------
+// The K steps of a stage (4 x 32 bytes) go to `nc` accumulators round robin:
+// consecutive tcgen05.mma into one accumulator wait for each other (~170
+// cycles apiece on B200 for N <= 128, measured), while MMAs into different
+// accumulators pipeline.  A one-M-block tile of bn <= 128 columns therefore
+// keeps 256/bn accumulators side by side in its 256-column TMEM slot, and the
+// epilogue adds them (exact int32 adds: the bits do not change).
+template <int MB>
+__device__ __forceinline__ void mma_stage(uint32_t d_tmem, uint32_t a0, uint32_t b0, uint32_t idesc,
+                                          int bn, int nc, bool first) {
+#pragma unroll
+  for (int j = 0; j < BK / 32; ++j) {
+    const int c = MB == 1 ? (j & (nc - 1)) : 0;
+    const uint32_t acc = (!first || j >= (MB == 1 ? nc : 1)) ? 1u : 0u;
+#pragma unroll
+    for (int mb = 0; mb < MB; ++mb)
+      ptx::mma_i8(d_tmem + (uint32_t)((c + mb) * bn), ptx::smem_desc_k128(a0 + mb * BM * BK + 32 * j),
+                  ptx::smem_desc_k128(b0 + 32 * j), idesc, acc);
+  }
+}
+
+// accumulators of a tile: 256/bn for one M block of bn <= 128, else 1
+__device__ __forceinline__ int n_chains(int mb, int bn) { return mb == 1 && bn <= 128 ? 256 / bn : 1; }
+
+// 32 columns of a warp's lane quarter, summed over the tile's nc accumulators
+// (nc - 1 more loads bn columns apart)
+__device__ __forceinline__ void tmem_ld_sum(uint32_t taddr, int bn, int nc, uint32_t (&r)[32]) {
+  ptx::tmem_ld_32x32(taddr, r);
+  ptx::tmem_ld_wait();
+#pragma unroll 1
+  for (int c = 1; c < nc; ++c) {
+    uint32_t t[32];
+    ptx::tmem_ld_32x32(taddr + (uint32_t)(c * bn), t);
+    ptx::tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 32; ++i) r[i] += t[i];
+  }
 }
 
 // ---- quantize step (epilogue warps of every CTA) ----------------------------
@@ -395,17 +456,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
       const uint64_t pol_b = ptx::policy_evict_first();
       uint32_t head = 0;
       int it = 0, lo = 0;  // stages [lo, it) are issued and not yet known consumed
-      uint32_t soff[kNB], ssz[kNB];
-      int pa_x[kNB], pa_y[kNB];  // A coordinates of stages still waiting for their codes
+      prefetch_x_rows(p.pd[0]);
+      // ring bookkeeping in shared memory (local memory would miss in the
+      // small L1 this kernel leaves): stage offsets and sizes, and the A
+      // coordinates of stages still waiting for their codes
+      uint32_t *soff = reinterpret_cast<uint32_t *>(smem + kBarOff + 512);
+      uint32_t *ssz = soff + kNB;
+      int *pa_x = reinterpret_cast<int *>(ssz + kNB);
+      int *pa_y = pa_x + kNB;
       bool ok = true;
       for (int pi = 0; pi < p.npairs && ok; ++pi) {
-        const PairDesc &D = p.pairs[pi];
-        const PairMaps &M = p.pm[pi];
+        const PairDesc &D = p.pd[pi];
         Geo g;
         g.load(D);
         const uint32_t S = g.stage_bytes(), AB = g.a_bytes();
-        for (int j = 0; j < g.njobs; ++j) ptx::prefetch_tmap(&M.B[j]);
-        ptx::prefetch_tmap(&M.A);
+        for (int j = 0; j < g.njobs; ++j) ptx::prefetch_tmap(&D.tmB[j]);
+        ptx::prefetch_tmap(&D.tmA);
         bool dep = false;   // codes of pair pi published by every CTA
         int pend_lo = it;   // stages [pend_lo, it) wait for their A tile while !dep
         auto publish_wait = [&]() -> bool {
@@ -413,15 +479,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
           fence_proxy_async_global();  // generic-proxy codes before async-proxy reads
           for (int j = pend_lo; j < it; ++j) {
             const int sl = j % kNB;
-            ptx::tma_load_2d(&M.A, &full[sl], ring + soff[sl], pa_x[sl], pa_y[sl], pol_a);
+            ptx::tma_load_2d(&D.tmA, &full[sl], ring + soff[sl], pa_x[sl], pa_y[sl], pol_a);
           }
           return true;
         };
         for (int u = blockIdx.x; u < g.units && ok; u += G) {
           const Unit w = decode_unit(g, u);
           const int kb0 = w.s * g.kb_per_split;
-          const int kb1 = min(kb0 + g.kb_per_split, g.kb_total);
-          for (int kb = kb0; kb < kb1; ++kb) {
+          const int nk = min(kb0 + g.kb_per_split, g.kb_total) - kb0;
+          const int rot = w.tile % nk;
+          for (int i = 0; i < nk; ++i) {
+            const int kb = kb0 + (rot + i) % nk;  // see k_rotation below
             uint32_t h2 = head;
             const uint32_t off = ring_place(h2, S);
             // free the stages this one would overwrite (and a barrier slot)
@@ -451,9 +519,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
             soff[sl] = off;
             ssz[sl] = S;
             ptx::mbar_arrive_expect_tx(&full[sl], S);
-            ptx::tma_load_2d(&M.B[w.job], &full[sl], ring + off + AB, kb * BK, w.n_t * g.bn, pol_b);
+            ptx::tma_load_2d(&D.tmB[w.job], &full[sl], ring + off + AB, kb * BK, w.n_t * g.bn, pol_b);
             if (dep) {
-              ptx::tma_load_2d(&M.A, &full[sl], ring + off, kb * BK, w.m_t * g.tile_m(), pol_a);
+              ptx::tma_load_2d(&D.tmA, &full[sl], ring + off, kb * BK, w.m_t * g.tile_m(), pol_a);
             } else {
               pa_x[sl] = kb * BK;
               pa_y[sl] = w.m_t * g.tile_m();
@@ -471,21 +539,24 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
           // that their barriers complete and the drain below sees them land
           for (int j = pend_lo; j < it; ++j) {
             const int sl = j % kNB;
-            ptx::tma_load_2d(&M.A, &full[sl], ring + soff[sl], pa_x[sl], pa_y[sl], pol_a);
+            ptx::tma_load_2d(&D.tmA, &full[sl], ring + soff[sl], pa_x[sl], pa_y[sl], pol_a);
           }
           break;
         }
-        // warm L2 with the next pair's first weight tiles of this CTA
+        // warm L2 with the next pair's activation rows and first weight tiles
         if (pi + 1 < p.npairs && ok) {
+          prefetch_x_rows(p.pd[pi + 1]);
           Geo gn;
-          gn.load(p.pairs[pi + 1]);
+          gn.load(p.pd[pi + 1]);
           if ((int)blockIdx.x < gn.units) {
             const Unit w = decode_unit(gn, blockIdx.x);
             const int kb0 = w.s * gn.kb_per_split;
-            const int kb1 = min(kb0 + gn.kb_per_split, gn.kb_total);
-            const int kbn = min(kb1 - kb0, max(4, (64 * 1024) / (gn.bn * BK)));
-            for (int kb = kb0; kb < kb0 + kbn; ++kb)
-              ptx::tma_prefetch_l2_2d(&p.pm[pi + 1].B[w.job], kb * BK, w.n_t * gn.bn);
+            const int nk = min(kb0 + gn.kb_per_split, gn.kb_total) - kb0;
+            const int rot = w.tile % nk;
+            const int kbn = min(nk, max(4, (64 * 1024) / (gn.bn * BK)));
+            for (int i = 0; i < kbn; ++i)
+              ptx::tma_prefetch_l2_2d(&p.pd[pi + 1].tmB[w.job], (kb0 + (rot + i) % nk) * BK,
+                                      w.n_t * gn.bn);
           }
         }
       }
@@ -503,14 +574,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
       bool ok = true;
       for (int pi = 0; pi < p.npairs && ok; ++pi) {
         Geo g;
-        g.load(p.pairs[pi]);
+        g.load(p.pd[pi]);
         const uint32_t S = g.stage_bytes(), AB = g.a_bytes();
         const uint32_t idesc = ptx::idesc_i8(BM, g.bn);
         const bool wide = g.mb * g.bn > 256;
+        const int nc = n_chains(g.mb, g.bn);
         for (int u = blockIdx.x; u < g.units && ok; u += G) {
           const Unit w = decode_unit(g, u);
           const int kb0 = w.s * g.kb_per_split;
-          const int kb1 = min(kb0 + g.kb_per_split, g.kb_total);
+          const int nk = min(kb0 + g.kb_per_split, g.kb_total) - kb0;
           int slot;
           if (wide) {  // the tile needs both 256-column slots
             slot = 0;
@@ -532,7 +604,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
           }
           ptx::tc_fence_after();
           const uint32_t d_tmem = tmem_base + (uint32_t)slot * 256u;
-          for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          for (int i = 0; i < nk; ++i, ++it) {
             const uint32_t off = ring_place(head, S);
             const int sl = it % kNB;
             if (!bar_wait(&full[sl], (it / kNB) & 1, p.err, DEV_TIMEOUT_FULL)) {
@@ -542,11 +614,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
             ptx::tc_fence_after();
             const uint32_t a0 = ptx::smem_u32(ring + off);
             const uint32_t b0 = ptx::smem_u32(ring + off + AB);
-#pragma unroll
-            for (int j = 0; j < BK / 32; ++j)
-              for (int mb = 0; mb < g.mb; ++mb)
-                ptx::mma_i8(d_tmem + mb * g.bn, ptx::smem_desc_k128(a0 + mb * BM * BK + 32 * j),
-                            ptx::smem_desc_k128(b0 + 32 * j), idesc, (kb > kb0 || j > 0) ? 1u : 0u);
+            if (g.mb == 1)
+              mma_stage<1>(d_tmem, a0, b0, idesc, g.bn, nc, i == 0);
+            else
+              mma_stage<2>(d_tmem, a0, b0, idesc, g.bn, nc, i == 0);
             ptx::mma_commit(&empty[sl]);
           }
           if (!ok) break;
@@ -567,7 +638,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
     int nxt = 0;
     bool ok = true;
     for (int pi = 0; pi < p.npairs && ok; ++pi) {
-      const PairDesc &D = p.pairs[pi];
+      const PairDesc &D = p.pd[pi];
       Geo g;
       g.load(D);
       // 1. the previous pair's outputs are complete on every CTA
@@ -581,8 +652,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
       }
       // 2. quantize this CTA's rows of x_pi, then publish the codes
       quantize_rows(D, red);
-      __threadfence();
-      fence_proxy_async_global();
+      // publish: the CTA barrier orders every thread's stores before thread
+      // 0's release at gpu scope (cumulative); the readers acquire, then
+      // fence the async proxy before their TMA loads of the codes
       ptx::named_bar_sync(1, kEpiThreads);
       if (et == 0) red_release_add(p.sync + 2 * pi, 1);
       // the epilogue reads activation scales that other CTAs wrote: observe
@@ -605,6 +677,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
       // the kernel outgrows the instruction cache and every phase slows down.
       const int ch0 = g.mb == 2 ? 0 : half;
       const int chs = g.mb == 2 ? 1 : 2;
+      const int nc = n_chains(g.mb, g.bn);
       for (int u = blockIdx.x; u < g.units; u += G) {
         const Unit w = decode_unit(g, u);
         const int job = w.job;
@@ -630,7 +703,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
         // chunk ahead)
         const float xs = row < g.m ? __ldcg(D.s + row) : 0.0f;
         float ws_cur = ws_of(ch0);
-        if (!bar_wait(&tfull[slot], fills[slot] & 1, p.err, DEV_TIMEOUT_TMEM)) {
+        if (!bar_wait(&tfull[slot], fills[slot] & 1, p.err, DEV_TIMEOUT_TMEM, 100)) {
           ok = false;
           break;
         }
@@ -644,11 +717,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
             const float ws_nxt = ws_of(ch + chs);
             __syncwarp();
             uint32_t r[32];
-            ptx::tmem_ld_32x32(taddr + ch * 32, r);
-            ptx::tmem_ld_wait();
+            tmem_ld_sum(taddr + ch * 32, g.bn, nc, r);
             const int col0 = n0 + ch * 32;
             if (col0 < n)
-              emit_chunk(D, &p.pm[pi].D[job], job, reinterpret_cast<const int(&)[32]>(r), xs, ws_cur,
+              emit_chunk(D, &D.tmD[job], job, reinterpret_cast<const int(&)[32]>(r), xs, ws_cur,
                          row, col0, lane, stage, tile_row0, g.m);
             ws_cur = ws_nxt;
           }
@@ -666,8 +738,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
         for (int ch = ch0; ch < nch; ch += chs) {
           __syncwarp();
           uint32_t r[32];
-          ptx::tmem_ld_32x32(taddr + ch * 32, r);
-          ptx::tmem_ld_wait();
+          tmem_ld_sum(taddr + ch * 32, g.bn, nc, r);
 #pragma unroll
           for (int c = 0; c < 8; ++c)
             __stcg(part + (ch * 8 + c) * 32, make_int4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]));
@@ -682,10 +753,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
           // each split reduces its share of the tile's 32x32 blocks
           if (et == 0) {
             atomicAdd(p.counters + w.tile, 1);
-            *s_last = ptx::flag_wait_geq<false>(p.counters + w.tile, g.splits, ptx::globaltimer(),
-                                                p.err, DEV_TIMEOUT_SPLIT)
-                          ? 1
-                          : 0;
+            *s_last = chain_wait(p.counters + w.tile, g.splits, p.err, DEV_TIMEOUT_SPLIT) ? 1 : 0;
           }
           ptx::named_bar_sync(1, kEpiThreads);
           if (!*s_last) {
@@ -730,17 +798,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
               }
             }
             __syncwarp();
-            emit_chunk(D, &p.pm[pi].D[job], job, acc, xs, ws_ch, row, col0, lane, stage, tile_row0, g.m);
+            emit_chunk(D, &D.tmD[job], job, acc, xs, ws_ch, row, col0, lane, stage, tile_row0, g.m);
           }
           ptx::named_bar_sync(1, kEpiThreads);
           if (et == 0) p.counters[w.tile] = 0;  // ready for the next pair or launch
         }
       }
       if (!ok) break;
-      // 4. this CTA's outputs of pair pi are written: publish
-      if (lane == 0) ptx::bulk_wait<0>();
+      // 4. this CTA's outputs of pair pi are written: publish (the TMA
+      // stores complete, ordered before the generic release by a proxy fence)
+      if (lane == 0) {
+        ptx::bulk_wait<0>();
+        fence_proxy_async_global();
+      }
       __syncwarp();
-      __threadfence();
       ptx::named_bar_sync(1, kEpiThreads);
       if (et == 0) red_release_add(p.sync + 2 * pi + 1, 1);
     }
@@ -773,8 +844,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
 struct Chain {
   int device = -1;
   int npairs = 0;
-  std::vector<PairDesc> h;  // host copy (the tensor maps go into each launch's parameters)
-  PairDesc *d_pairs = nullptr;
+  std::vector<PairDesc> h;  // descriptors (they go into each launch's parameters)
   int *d_sync = nullptr;
   int32_t *d_ws = nullptr;
   int *d_cnt = nullptr;
@@ -785,7 +855,6 @@ std::map<int, Chain> g_chains;
 int g_next_chain = 1;
 
 void free_chain(Chain &c) {
-  if (c.d_pairs) cudaFree(c.d_pairs);
   if (c.d_sync) cudaFree(c.d_sync);
   if (c.d_ws) cudaFree(c.d_ws);
   if (c.d_cnt) cudaFree(c.d_cnt);
@@ -927,11 +996,9 @@ GCU_EXPORT int gcu_gemm_chain_create(const gcu_qgemm_step *steps, int nsteps, co
   }
   c.h = h;
   const int nsync = 2 * (nsteps < kParamPairs ? nsteps : kParamPairs) + 1;
-  cudaError_t e = cudaMalloc(&c.d_pairs, sizeof(PairDesc) * nsteps);
-  if (e == cudaSuccess) e = cudaMalloc(&c.d_sync, sizeof(int) * nsync);
+  cudaError_t e = cudaMalloc(&c.d_sync, sizeof(int) * nsync);
   if (e == cudaSuccess && ws_need) e = cudaMalloc(&c.d_ws, ws_need);
   if (e == cudaSuccess && cnt_need) e = cudaMalloc(&c.d_cnt, sizeof(int) * cnt_need);
-  if (e == cudaSuccess) e = cudaMemcpy(c.d_pairs, h.data(), sizeof(PairDesc) * nsteps, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemset(c.d_sync, 0, sizeof(int) * nsync);
   if (e == cudaSuccess && cnt_need) e = cudaMemset(c.d_cnt, 0, sizeof(int) * cnt_need);
   if (e != cudaSuccess) {
@@ -972,15 +1039,7 @@ GCU_EXPORT int gcu_gemm_chain_run(int handle, void *stream) {
   for (int b = 0; b < c.npairs; b += kParamPairs) {
     const int n = c.npairs - b < kParamPairs ? c.npairs - b : kParamPairs;
     memset(&p, 0, sizeof(p));
-    for (int i = 0; i < n; ++i) {
-      const PairDesc &D = c.h[b + i];
-      p.pm[i].A = D.tmA;
-      for (int j = 0; j < kJobs; ++j) {
-        p.pm[i].B[j] = D.tmB[j];
-        p.pm[i].D[j] = D.tmD[j];
-      }
-    }
-    p.pairs = c.d_pairs + b;
+    for (int i = 0; i < n; ++i) p.pd[i] = c.h[b + i];
     p.npairs = n;
     p.sync = c.d_sync;
     p.ws = c.d_ws;
