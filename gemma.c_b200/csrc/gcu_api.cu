@@ -57,9 +57,16 @@ static int current_device() {
   return t_device;
 }
 
+// The device error word.  Two homes: a __device__ variable (looked up with no
+// allocation, for callers that never set up the library), and once gcu_init
+// or a host entry point has run on the device, a word of mapped pinned host
+// memory, which kernels write directly and host calls read after their
+// stream wait without a device-to-host copy (each copy costs ~10 us here).
 struct DeviceInfo {
   int sms = 0;
-  unsigned int *err = nullptr;
+  unsigned int *err_sym = nullptr;              // device variable
+  unsigned int *err_map = nullptr;              // mapped host word, device view
+  volatile unsigned int *err_host = nullptr;    // the same word, host view
 };
 static std::mutex g_dev_mu;
 static std::unordered_map<int, DeviceInfo> g_dev;
@@ -71,9 +78,46 @@ static DeviceInfo &device_info() {
   if (di.sms == 0) {
     cudaDeviceGetAttribute(&di.sms, cudaDevAttrMultiProcessorCount, d);
     void *p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_dev_err) == cudaSuccess) di.err = (unsigned int *)p;
+    if (cudaGetSymbolAddress(&p, g_dev_err) == cudaSuccess) di.err_sym = (unsigned int *)p;
   }
   return di;
+}
+
+// Create the mapped host error word of the calling thread's device (once).
+static int map_error_word() {
+  const int d = current_device();
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DeviceInfo &di = g_dev[d];
+  if (di.err_map) return 0;
+  void *h = nullptr, *dp = nullptr;
+  GCU_CUDA(cudaHostAlloc(&h, 64, cudaHostAllocMapped | cudaHostAllocPortable));
+  memset(h, 0, 64);
+  if (cudaHostGetDevicePointer(&dp, h, 0) != cudaSuccess) {
+    cudaFreeHost(h);
+    return set_error("cudaHostGetDevicePointer failed for the error word");
+  }
+  di.err_host = static_cast<volatile unsigned int *>(h);
+  di.err_map = static_cast<unsigned int *>(dp);
+  return 0;
+}
+
+// Read and clear every home of the error word (device variable by copy).
+static unsigned int take_error_code(bool read_symbol) {
+  DeviceInfo &di = device_info();
+  unsigned int code = 0;
+  if (di.err_host) {
+    code = *di.err_host;
+    if (code) *di.err_host = 0;
+  }
+  if (read_symbol && di.err_sym) {
+    unsigned int c2 = 0;
+    if (cudaMemcpy(&c2, di.err_sym, sizeof(c2), cudaMemcpyDeviceToHost) == cudaSuccess && c2) {
+      unsigned int zero = 0;
+      cudaMemcpy(di.err_sym, &zero, sizeof(zero), cudaMemcpyHostToDevice);
+      if (!code) code = c2;
+    }
+  }
+  return code;
 }
 
 int num_sms() { return device_info().sms; }
@@ -85,7 +129,10 @@ bool pdl_enabled() {
   }();
   return on;
 }
-unsigned int *dev_error_word() { return device_info().err; }
+unsigned int *dev_error_word() {
+  DeviceInfo &di = device_info();
+  return di.err_map ? di.err_map : di.err_sym;
+}
 
 // ---------------------------------------------------------------------------
 // per-thread context: stream and device buffers for the host entry points
@@ -112,20 +159,52 @@ struct DevBuf {
   }
 };
 
+// Mapped pinned host memory that kernels read or write directly over PCIe
+// (zero-copy).  The host entry points pass per-row scales this way: a 2 KB
+// vector costs a host memcpy instead of a copy-engine transfer, and every
+// transfer costs ~10 us of fixed latency on these machines.
+struct MappedBuf {
+  void *h = nullptr;  // host view
+  void *d = nullptr;  // device view
+  size_t cap = 0;
+  int get(size_t bytes) {
+    if (bytes <= cap) return 0;
+    if (h) cudaFreeHost(h);
+    h = d = nullptr;
+    cap = 0;
+    const size_t want = bytes + bytes / 4 + 256;
+    GCU_CUDA(cudaHostAlloc(&h, want, cudaHostAllocMapped | cudaHostAllocPortable));
+    if (cudaHostGetDevicePointer(&d, h, 0) != cudaSuccess) {
+      cudaFreeHost(h);
+      h = nullptr;
+      return set_error("cudaHostGetDevicePointer failed for a scale buffer");
+    }
+    cap = want;
+    return 0;
+  }
+  void release() {
+    if (h) cudaFreeHost(h);
+    h = d = nullptr;
+    cap = 0;
+  }
+};
+
 // Host entry points that move several MB split their rows into chunks and
 // pipeline them: chunk i's host->device copy (stream s_in), its kernel
 // (stream), and its device->host copy (s_out) overlap chunk i+1's, so the
 // two PCIe directions and the GPU work at the same time.
 constexpr int kMaxChunks = 4;
-constexpr size_t kChunkMinBytes = 4u << 20;  // smaller transfers go in one piece
+// smaller transfers go in one piece: every transfer or launch costs ~10 us
+// of fixed latency on these machines, more than overlapping saves below this
+constexpr size_t kChunkMinBytes = 4u << 20;
 
 struct ThreadCtx {
   int device = -1;
   cudaStream_t stream = nullptr;  // kernels (and everything of unchunked calls)
   cudaStream_t s_in = nullptr, s_out = nullptr;
   cudaEvent_t ev_in[kMaxChunks] = {}, ev_done[kMaxChunks] = {};
-  unsigned int *h_err = nullptr;  // pinned landing slot of the device error word
   DevBuf in, in2, out, sc, sc2, wtmp, wstmp;
+  MappedBuf hs;  // per-row scales, read or written by the kernels in place
   ~ThreadCtx() {
     // process teardown may already have unloaded the driver: leak quietly
   }
@@ -144,8 +223,7 @@ static int ctx(ThreadCtx **out) {
       GCU_CUDA(cudaEventCreateWithFlags(&c.ev_in[i], cudaEventDisableTiming));
       GCU_CUDA(cudaEventCreateWithFlags(&c.ev_done[i], cudaEventDisableTiming));
     }
-    GCU_CUDA(cudaHostAlloc(reinterpret_cast<void **>(&c.h_err), sizeof(unsigned int),
-                           cudaHostAllocDefault));
+    if (map_error_word()) return 1;
     c.device = d;
   }
   *out = &c;
@@ -334,21 +412,14 @@ static int scales_dev(ThreadCtx *c, DevBuf &buf, const float *host, size_t count
 }
 
 // Wait for `st`, the last stream of a host call, and report a device-side
-// error word set by its kernels.  The word is read back on `st` itself, so
-// the wait covers it (no extra synchronous copy).
+// error word set by its kernels.  The host entry points run with the mapped
+// error word (ctx() creates it), which the kernels wrote before the stream's
+// work completed: reading it after the wait needs no copy.
 static int sync_and_check(ThreadCtx *c, cudaStream_t st) {
-  unsigned int *ew = dev_error_word();
-  if (ew) {
-    *c->h_err = 0;
-    GCU_CUDA(cudaMemcpyAsync(c->h_err, ew, sizeof(unsigned int), cudaMemcpyDeviceToHost, st));
-  }
+  (void)c;
   GCU_CUDA(cudaStreamSynchronize(st));
-  const unsigned int code = ew ? *c->h_err : 0u;
-  if (code) {
-    unsigned int zero = 0;
-    cudaMemcpy(ew, &zero, sizeof(zero), cudaMemcpyHostToDevice);
-    return set_error("device-side wait gave up (code %u)", code);
-  }
+  const unsigned int code = take_error_code(false);
+  if (code) return set_error("device-side wait gave up (code %u)", code);
   return 0;
 }
 static int sync_and_check(ThreadCtx *c) { return sync_and_check(c, c->stream); }
@@ -392,18 +463,13 @@ GCU_EXPORT int gcu_init(int device) {
   GCU_CUDA(cudaSetDevice(device));
   t_device = device;
   device_info();
-  return 0;
+  return map_error_word();
 }
 
 GCU_EXPORT int gcu_check_device(void) {
   GCU_CUDA(cudaDeviceSynchronize());
-  unsigned int *ew = dev_error_word();
-  if (!ew) return 0;
-  unsigned int code = 0;
-  GCU_CUDA(cudaMemcpy(&code, ew, sizeof(code), cudaMemcpyDeviceToHost));
+  const unsigned int code = take_error_code(true);
   if (code) {
-    unsigned int zero = 0;
-    cudaMemcpy(ew, &zero, sizeof(zero), cudaMemcpyHostToDevice);
     set_error("device-side wait gave up (code %u)", code);
     return 1;
   }
@@ -521,6 +587,7 @@ GCU_EXPORT int gcu_shutdown(void) {
   c.sc2.release();
   c.wtmp.release();
   c.wstmp.release();
+  c.hs.release();
   if (c.stream) {
     cudaStreamDestroy(c.stream);
     cudaStreamDestroy(c.s_in);
@@ -529,10 +596,8 @@ GCU_EXPORT int gcu_shutdown(void) {
       cudaEventDestroy(c.ev_in[i]);
       cudaEventDestroy(c.ev_done[i]);
     }
-    cudaFreeHost(c.h_err);
   }
   c.stream = c.s_in = c.s_out = nullptr;
-  c.h_err = nullptr;
   c.device = -1;
   return 0;
 }
@@ -548,10 +613,13 @@ GCU_EXPORT int gcu_quantize_acts(int8_t *dst, float *dsc, const float *src, int 
   ThreadCtx *c;
   if (ctx(&c)) return 1;
   const size_t in_elems = (size_t)(m - 1) * sstr + n;
-  void *din, *dout, *dsc_d;
+  // (the scales come back by a transfer too: kernel writes into mapped host
+  // memory would queue behind the previous chunk's copy and delay the kernel)
+  void *din, *dout, *dsc_v;
   if (c->in.get(in_elems * 4, &din) || c->out.get((size_t)m * n, &dout) ||
-      c->sc.get((size_t)m * 4, &dsc_d))
+      c->sc.get((size_t)m * 4, &dsc_v))
     return 1;
+  float *dsc_d = static_cast<float *>(dsc_v);
   const int rows = chunk_rows(m, (size_t)sstr * 4, 1);
   const bool piped = rows < m;
   cudaStream_t s_in = piped ? c->s_in : c->stream, s_out = piped ? c->s_out : c->stream;
@@ -564,7 +632,7 @@ GCU_EXPORT int gcu_quantize_acts(int8_t *dst, float *dsc, const float *src, int 
       GCU_CUDA(cudaEventRecord(c->ev_in[i], s_in));
       GCU_CUDA(cudaStreamWaitEvent(c->stream, c->ev_in[i], 0));
     }
-    if (launch_quantize_rows((int8_t *)dout + (size_t)r0 * n, (float *)dsc_d + r0,
+    if (launch_quantize_rows((int8_t *)dout + (size_t)r0 * n, dsc_d + r0,
                              (const float *)din + off, sstr, mr, n, c->stream))
       return 1;
     if (piped) {
@@ -573,8 +641,7 @@ GCU_EXPORT int gcu_quantize_acts(int8_t *dst, float *dsc, const float *src, int 
     }
     GCU_CUDA(cudaMemcpyAsync(dst + (size_t)r0 * n, (int8_t *)dout + (size_t)r0 * n, (size_t)mr * n,
                              cudaMemcpyDeviceToHost, s_out));
-    GCU_CUDA(cudaMemcpyAsync(dsc + r0, (float *)dsc_d + r0, (size_t)mr * 4, cudaMemcpyDeviceToHost,
-                             s_out));
+    GCU_CUDA(cudaMemcpyAsync(dsc + r0, dsc_d + r0, (size_t)mr * 4, cudaMemcpyDeviceToHost, s_out));
   }
   GCU_CUDA(cudaStreamSynchronize(s_out));
   return 0;
@@ -597,10 +664,11 @@ static int host_gemv_jobs(const gcu_gemv_job *jobs, int njobs, const int8_t *vec
   int rows = 0;
   size_t out_elems = 0;
   for (int j = 0; j < njobs; ++j) out_elems += jobs[j].m > 0 ? jobs[j].m : 0;
-  void *dx, *dy, *dxs;
-  if (c->in.get((size_t)n + 16, &dx) || c->out.get(out_elems * 4 + 16, &dy) ||
-      c->sc.get(16, &dxs))
+  void *dx, *dy;
+  if (c->in.get((size_t)n + 16, &dx) || c->out.get(out_elems * 4 + 16, &dy) || c->hs.get(16))
     return 1;
+  *static_cast<float *>(c->hs.h) = vsc;  // read by the kernel in place
+  const void *dxs = c->hs.d;
   // weights of unregistered jobs share one transient buffer: size it once
   size_t wt = 0, st = 0;
   for (int j = 0; j < njobs; ++j) {
@@ -637,7 +705,6 @@ static int host_gemv_jobs(const gcu_gemv_job *jobs, int njobs, const int8_t *vec
     yoff += m;
   }
   GCU_CUDA(cudaMemcpyAsync(dx, vec, (size_t)n, cudaMemcpyHostToDevice, c->stream));
-  GCU_CUDA(cudaMemcpyAsync(dxs, &vsc, 4, cudaMemcpyHostToDevice, c->stream));
   if (launch_gemv(J, (const int8_t *)dx, 0, (const float *)dxs, 1, 0, n, c->stream)) return 1;
   yoff = 0;
   for (int j = 0; j < njobs; ++j) {
@@ -646,7 +713,7 @@ static int host_gemv_jobs(const gcu_gemv_job *jobs, int njobs, const int8_t *vec
                              cudaMemcpyDeviceToHost, c->stream));
     yoff += jobs[j].m;
   }
-  // vsc lives on this stack frame: the copies must finish before returning
+  // the outputs are host memory the caller owns: wait for them
   GCU_CUDA(cudaStreamSynchronize(c->stream));
   return 0;
 }
@@ -675,17 +742,27 @@ GCU_EXPORT int gcu_gemm_int8(float *dst, int dstr, const int8_t *mat, int mstr,
   const int k16 = (k + 15) / 16 * 16;  // device row stride of packed operands
   const int n4 = (n + 3) / 4 * 4;      // device row stride of the output
   // activations: pack to rows of k16 bytes (TMA wants 16-byte strides)
-  void *dsrc, *dssc, *dout;
-  if (c->in.get((size_t)m * k16, &dsrc) || c->sc.get((size_t)m * 4, &dssc) ||
-      c->out.get((size_t)m * n4 * 4, &dout))
+  void *dsrc, *dout, *dssc;
+  if (c->in.get((size_t)m * k16, &dsrc) || c->out.get((size_t)m * n4 * 4, &dout)) return 1;
+  // Activation scales: small outputs read them in place from mapped host
+  // memory (no transfer); every N tile reads each row's scale, so large ones
+  // (over ~16k PCIe reads) get them by a transfer like the activations.
+  const bool scales_in_place = (size_t)m * n <= ((size_t)1 << 20);
+  if (scales_in_place) {
+    if (c->hs.get((size_t)m * 4)) return 1;
+    memcpy(c->hs.h, ssc, (size_t)m * 4);
+    dssc = c->hs.d;
+  } else if (c->sc.get((size_t)m * 4, &dssc)) {
     return 1;
+  }
   // row chunks of whole 128-row tiles when the output is large: chunk i's
   // output copy overlaps the GEMM and input copy of chunk i+1
   const int rows = m <= 8 ? m : chunk_rows(m, (size_t)n * 4, 128);
   const bool piped = rows < m;
   if (!piped) {
     GCU_CUDA(copy_rows(dsrc, k16, src, sstr, k, m, cudaMemcpyHostToDevice, c->stream));
-    GCU_CUDA(cudaMemcpyAsync(dssc, ssc, (size_t)m * 4, cudaMemcpyHostToDevice, c->stream));
+    if (!scales_in_place)
+      GCU_CUDA(cudaMemcpyAsync(dssc, ssc, (size_t)m * 4, cudaMemcpyHostToDevice, c->stream));
   }
   // weights: registered copy if the whole strided range is inside one
   const size_t wbytes = (size_t)(n - 1) * mstr + k;
@@ -727,8 +804,9 @@ GCU_EXPORT int gcu_gemm_int8(float *dst, int dstr, const int8_t *mat, int mstr,
       // this chunk's activation rows, on the input stream
       GCU_CUDA(copy_rows((int8_t *)dsrc + (size_t)r0 * k16, k16, src + (size_t)r0 * sstr,
                                  sstr, k, mr, cudaMemcpyHostToDevice, c->s_in));
-      GCU_CUDA(cudaMemcpyAsync((float *)dssc + r0, ssc + r0, (size_t)mr * 4,
-                               cudaMemcpyHostToDevice, c->s_in));
+      if (!scales_in_place)
+        GCU_CUDA(cudaMemcpyAsync((float *)dssc + r0, ssc + r0, (size_t)mr * 4,
+                                 cudaMemcpyHostToDevice, c->s_in));
       GCU_CUDA(cudaEventRecord(c->ev_in[i], c->s_in));
       GCU_CUDA(cudaStreamWaitEvent(c->stream, c->ev_in[i], 0));
     }

@@ -214,6 +214,16 @@ __device__ __forceinline__ uint64_t globaltimer() {
   return t;
 }
 
+// Record a device-side error code.  The word may live in mapped pinned host
+// memory (the host entry points read it there after their stream wait, with
+// no copy), so it is written with a plain store rather than an atomic: any
+// nonzero code reports the failure, and the first writer usually wins.
+__device__ __forceinline__ void record_err(unsigned int *err, unsigned int code) {
+  volatile unsigned int *e = err;
+  if (*e == 0u) *e = code;
+  __threadfence_system();
+}
+
 __device__ __forceinline__ int ld_acquire_sys(const int *p) {
   int v;
   asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -234,7 +244,7 @@ __device__ __forceinline__ bool flag_wait_geq(const int *flag, int target, uint6
                                               uint64_t budget_ns = 2000000000ull) {
   while ((SYS ? ld_acquire_sys(flag) : ld_acquire_gpu(flag)) < target) {
     if (globaltimer() - t0 > budget_ns) {
-      atomicCAS(err, 0u, code);
+      record_err(err, code);
       return false;
     }
     __nanosleep(32);
@@ -299,7 +309,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait_cluster(bar, parity)) return true;
     if (globaltimer() - t0 > budget_ns) {
-      atomicCAS(err, 0u, code);
+      record_err(err, code);
       return false;
     }
   }
@@ -313,7 +323,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(bar, parity)) return true;
     if (globaltimer() - t0 > budget_ns) {
-      atomicCAS(err, 0u, code);
+      record_err(err, code);
       return false;
     }
   }

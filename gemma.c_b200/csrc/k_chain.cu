@@ -158,7 +158,7 @@ __device__ __forceinline__ bool give_up(long long t0, unsigned int *err, unsigne
   if (dt < kErrPollCycles) return false;
   if (err_set(err)) return true;
   if (dt > kBudgetCycles) {
-    atomicCAS(err, 0u, code);
+    ptx::record_err(err, code);
     return true;
   }
   return false;
