@@ -15,6 +15,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <map>
+#include <atomic>
 #include <mutex>
 #include <shared_mutex>
 #include <unordered_map>
@@ -101,6 +102,23 @@ static int map_error_word() {
   return 0;
 }
 
+// Every nonzero code the host has observed (bit `code`), whoever read it:
+// a call that must not run after a given failure checks this.
+static std::atomic<unsigned int> g_codes_seen{0};
+
+unsigned int error_codes_seen() {
+  DeviceInfo &di = device_info();
+  if (di.err_host) {
+    const unsigned int code = *di.err_host;  // peek: a later check still reports it
+    if (code && code < 32) g_codes_seen.fetch_or(1u << code);
+  }
+  return g_codes_seen.load();
+}
+
+void forget_error_code(unsigned int code) {
+  if (code < 32) g_codes_seen.fetch_and(~(1u << code));
+}
+
 // Read and clear every home of the error word (device variable by copy).
 static unsigned int take_error_code(bool read_symbol) {
   DeviceInfo &di = device_info();
@@ -117,6 +135,7 @@ static unsigned int take_error_code(bool read_symbol) {
       if (!code) code = c2;
     }
   }
+  if (code && code < 32) g_codes_seen.fetch_or(1u << code);
   return code;
 }
 

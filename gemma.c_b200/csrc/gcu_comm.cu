@@ -197,6 +197,7 @@ GCU_EXPORT int gcu_comm_init(int rank, int world, const unsigned char id[128]) {
   g_comm.world = world;
   // all ranks synchronise here anyway (the NCCL init above is collective)
   if (setup_p2p(g_comm)) return 1;
+  forget_error_code(DEV_TIMEOUT_PEER);  // fresh buffers and counters
   return 0;
 }
 
@@ -212,6 +213,21 @@ GCU_EXPORT int gcu_comm_destroy(void) {
   ncclResult_t r = g_nccl.commDestroy(g_comm.comm);
   g_comm.comm = nullptr;
   if (r != ncclSuccess) return nccl_err(r, "ncclCommDestroy");
+  return 0;
+}
+
+// A rank whose fused all-gather gave up waiting for its peers (device code
+// 6) leaves the arrival counters of every rank out of step: a late arrival
+// would count toward the next launch, which could then read a half of a
+// peer's buffer that is not yet written.  Row-sharded calls are therefore
+// refused from then on, until gcu_comm_destroy and gcu_comm_init (on every
+// rank) rebuild the buffers and counters.  They are refused rather than sent
+// to NCCL: ranks that disagree on the path would wait for each other forever.
+static int refuse_after_peer_timeout(const char *what) {
+  if (error_codes_seen() & (1u << DEV_TIMEOUT_PEER))
+    return set_error("%s: refused after a fused all-gather gave up waiting for a peer (device code %d); "
+                     "call gcu_comm_destroy and gcu_comm_init on every rank",
+                     what, (int)DEV_TIMEOUT_PEER);
   return 0;
 }
 
@@ -236,6 +252,7 @@ GCU_EXPORT int gcu_dev_gemm_int8_rowshard(float *dst, float *work, const int8_t 
                                           const float *matsc_local, const int8_t *src,
                                           const float *ssc, int m, int n, int k, void *stream) {
   if (!g_comm.comm) return set_error("gcu_dev_gemm_int8_rowshard: gcu_comm_init first");
+  if (refuse_after_peer_timeout("gcu_dev_gemm_int8_rowshard")) return 1;
   const int world = g_comm.world, rank = g_comm.rank;
   if (n % world) return set_error("rowshard: n %d not divisible by world %d", n, world);
   if (m <= 0) return 0;
@@ -287,6 +304,7 @@ GCU_EXPORT int gcu_dev_quantize_gemm_int8_rowshard_multi(const gcu_gemv_job *job
                                                          int xstr, int m, int k, float *work,
                                                          void *stream) {
   if (!g_comm.comm) return set_error("gcu_dev_quantize_gemm_int8_rowshard_multi: gcu_comm_init first");
+  if (refuse_after_peer_timeout("gcu_dev_quantize_gemm_int8_rowshard_multi")) return 1;
   if (njobs < 1 || njobs > GCU_MAX_JOBS)
     return set_error("quantize_gemm_rowshard_multi: 1..%d jobs (got %d)", GCU_MAX_JOBS, njobs);
   if (m <= 0) return 0;

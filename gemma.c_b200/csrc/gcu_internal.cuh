@@ -67,6 +67,11 @@ enum DevErr : unsigned int {
   DEV_TIMEOUT_CHAIN = 9,     // a chain launch's grid-wide hand-off between two steps
 };
 unsigned int *dev_error_word();  // device address of the error word
+// Bit mask of the device error codes the host has observed since start-up
+// (1u << code), including a code now sitting in the error word unread;
+// forget_error_code clears one (after the state it poisoned is rebuilt).
+unsigned int error_codes_seen();
+void forget_error_code(unsigned int code);
 
 // ---------------------------------------------------------------------------
 // weight registry (gcu_api.cu)

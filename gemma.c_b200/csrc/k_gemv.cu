@@ -118,6 +118,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, cons
   __shared__ float red[kThreads / 32];
   __shared__ float s_scale[MB];
   __shared__ float s_xsc[MB];  // activation scales, indexed by reduced-sum slot
+  __shared__ int s_peers_ok;
   const int C = k >> 4;
   constexpr int kRowsPerWarp = (32 / LPR) * R;
   const int lane = threadIdx.x & 31;
@@ -304,9 +305,13 @@ __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, cons
         __threadfence_system();
         for (int pr = 0; pr < po.world; ++pr) atomicAdd_system(po.flag_peer[pr], 1);
       }
-      ptx::flag_wait_geq<true>(po.flag_local, (epoch0 + 1) * po.world, t0, po.err, DEV_TIMEOUT_PEER);
+      s_peers_ok = ptx::flag_wait_geq<true>(po.flag_local, (epoch0 + 1) * po.world, t0, po.err,
+                                            DEV_TIMEOUT_PEER);
     }
     __syncthreads();
+    // a peer that never arrived: its half may be unwritten, pull nothing (the
+    // host reports code 6 and refuses further row-sharded calls)
+    if (!s_peers_ok) return;
     // every rank's slices are ready in its own half: pull them into dst, 16
     // bytes at a time (a 4-float group never straddles two ranks' slices)
     for (int j = 0; j < po.njobs; ++j) {

@@ -12,7 +12,10 @@ chain adds int8 rounding boundaries: an fp32 value a few ulps from a
 quantization boundary can round to the neighbouring code, which moves that
 product by one code step.  So the bound here is max |gpu - ref| <= 2e-3 of
 the largest |ref| per step, and the median difference within 1e-5 of it
-(the typical element agrees to fp32 rounding).
+(the typical element agrees to fp32 rounding).  The last link is then checked
+exactly: the logits equal the lm_head of the quantized final hidden state on
+both sides, and the two quantizations are counted code by code (on these
+fixtures no code flips, and the logits are bit-identical without a softcap).
 """
 import json
 import os
@@ -65,6 +68,54 @@ def test_decode_steps_match_reference(name):
         ok, rel = close(dec.x.cpu().numpy()[0], GOLD[f"{name}_hid"][p])
         assert ok, f"hidden state at position {p}: max diff {rel:.3g} of the largest"
     gcu.check_device()
+
+
+@pytest.mark.parametrize("name", list(META["cases"]))
+def test_decode_logit_error_is_last_quantize_code_flips(name):
+    # The logit bound above is a tolerance; this accounts for it at the last
+    # link of the chain.  The fixture's hidden state is the final RMSNorm's
+    # output, the input of the lm_head's quantize_act (gemma.c:4965-4966).
+    # (1) the GPU's logits are exactly lm_head(quantize(GPU hidden)), (2) the
+    # reference's are exactly lm_head(quantize(reference hidden)) -- so the
+    # logit difference IS the difference of those two int8 inputs -- and (3)
+    # the two quantizations differ only by codes flipped by one step at a
+    # rounding boundary (counted per step) and a scale within fp32 rounding.
+    import oracle as O
+    cfg = META["cases"][name]
+    layers, emb, fnorm = synth.decoder_model(cfg["tid"], cfg)
+    npos = META["npos"]
+    x0 = synth.normal(cfg["tid"] + 999, (npos, cfg["dim"]))
+    dec = decode.Decoder(cfg, layers, emb, fnorm, clen=npos)
+    cap = cfg["sc_log"]
+
+    def lm_head(q, sc):
+        y = O.gemv_int8(emb[0], emb[1], q, sc)
+        # gemma.c:4971-4976: tanhf(logit / cap) * cap
+        return (np.tanh(y / np.float32(cap)) * np.float32(cap)).astype(np.float32) if cap else y
+
+    flips = []
+    for p in range(npos):
+        dec.set_freqs(GOLD[f"{name}_slid"][p], GOLD[f"{name}_full"][p])
+        dec.x.copy_(torch.from_numpy(x0[p][None]))
+        dec.step(p)
+        torch.cuda.synchronize()
+        hid_g, log_g = dec.x.cpu().numpy()[0], dec.logits.cpu().numpy()[0]
+        hid_r, log_r = GOLD[f"{name}_hid"][p], GOLD[f"{name}_logits"][p]
+        qg, sg = O.quantize_act(hid_g)
+        qr, sr = O.quantize_act(hid_r)
+        tol = 0.0 if not cap else 2e-6 * float(np.max(np.abs(log_r)))  # tanhf vs numpy's tanh
+        assert np.max(np.abs(lm_head(qg, sg) - log_g)) <= tol, f"GPU lm_head at position {p}"
+        assert np.max(np.abs(lm_head(qr, sr) - log_r)) <= tol, f"reference lm_head at position {p}"
+        d = qg.astype(np.int32) - qr.astype(np.int32)
+        assert np.max(np.abs(d)) <= 1, f"position {p}: a code moved by {np.max(np.abs(d))} steps"
+        assert abs(float(sg) - float(sr)) <= 1e-5 * float(sr), f"position {p}: scales {sg} vs {sr}"
+        flips.append(int(np.count_nonzero(d)))
+        assert flips[-1] <= max(2, cfg["dim"] // 50), f"position {p}: {flips[-1]} codes flipped"
+        if flips[-1] == 0 and sg == sr:  # the same int8 input: the same logits
+            assert np.max(np.abs(log_g - log_r)) <= 2 * tol, f"position {p}: equal codes, different logits"
+            if not cap:
+                assert np.array_equal(log_g.view(np.uint32), log_r.view(np.uint32))
+    print(f"{name}: codes flipped at the lm_head quantize per step: {flips}")
 
 
 def test_decode_step_graph_replay_matches_eager():
