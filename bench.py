@@ -157,7 +157,8 @@ PREFILL = {
                   lambda S: [("vision", S.vision_layer_groups(S.CONFIGS["siglip"]), 4096, 27),
                              ("projector", S.projector_groups(S.CONFIGS["siglip"], S.CONFIGS["4b"]), 256, 1),
                              ("text", S.layer_groups(S.CONFIGS["4b"]), 2048, 34)], False),
-    "prefill12b": (4, "Gemma-3-12B-shaped W8A8 prefill matmul set, FFN rows sharded over the GPUs",
+    "prefill12b": (4, "Gemma-3-12B-shaped W8A8 prefill matmul set; each layer's FFN as one block (up/gate, "
+                      "GeGLU, quantize, down) with its hidden dimension sharded over the GPUs",
                    lambda S: [("text", S.layer_groups(S.CONFIGS["12b"]), 4096, 48)], True),
 }
 
@@ -169,9 +170,12 @@ def is_ffn(name):
 class Prefill:
     """Prefill GEMM sets (configs[1], [3], [4]): stacks of identical layers,
     each layer the quantize_acts -> GEMM pairs of gemma.c (5034-5391 text,
-    4497-4633 vision, 4714-4716 projector).  Sharded workloads split the FFN
-    weights' rows over the ranks and all-gather each FFN output
-    (gcu_dev_gemm_int8_rowshard); Q/K/V/O stay replicated."""
+    4497-4633 vision, 4714-4716 projector).  configs[4] runs each layer's FFN
+    as one block (gcu_dev_ffn_rowshard: up/gate, GeGLU, quantize, down,
+    gemma.c:5365-5391): unsharded on one GPU; at N > 1 its hidden dimension
+    is split over the ranks (rows of up/gate, columns of down) and the ranks
+    exchange row maxima and int32 partial sums, bit-exact; Q/K/V/O stay
+    replicated."""
 
     def __init__(self, name="prefill1b", seed=0, fused=False, world=1, rank=0, layers=0):
         import synth
@@ -182,6 +186,7 @@ class Prefill:
             self.stacks = [(lb, g, m, min(nl, layers)) for lb, g, m, nl in self.stacks]
         self.fused, self.world, self.rank = fused, world, rank
         self.shard = shard and world > 1
+        self.ffn_block = name == "prefill12b"
         self.needs_comm = self.shard
         self.m = self.stacks[-1][2]
         self.layers = sum(st[3] for st in self.stacks)
@@ -216,6 +221,11 @@ class Prefill:
             for _ in range(nl):
                 layer = []
                 for k, jobs in groups:
+                    if self.ffn_block and jobs[0][0] == "w3_down":
+                        continue  # part of the FFN block built with up/gate
+                    if self.ffn_block and jobs[0][0] == "w1_up":
+                        layer.append(self._ffn_record(synth, gen, wgen, device, m, k, jobs[0][1]))
+                        continue
                     x = synth.activations_torch(m, k, gen, device, outliers=True)
                     q = torch.empty((m, k), dtype=torch.int8, device=device)
                     s = torch.empty(m, dtype=torch.float32, device=device)
@@ -236,13 +246,36 @@ class Prefill:
             self.L.append(stack)
             # output buffers (fp32) per group, shared by the stack's layers
             self.out.append([[torch.empty((m, n), dtype=torch.float32, device=device) for _, n in jobs]
-                             for _, jobs in groups])
+                             for _, jobs in groups if not (self.ffn_block and jobs[0][0] == "w3_down")])
             self.work.append([[torch.empty((m, n), dtype=torch.float32, device=device) for _, n in jobs]
-                              if self.shard and all(is_ffn(nm) for nm, _ in jobs) else None
-                              for _, jobs in groups])
+                              if self.shard and not self.ffn_block and all(is_ffn(nm) for nm, _ in jobs) else None
+                              for _, jobs in groups if not (self.ffn_block and jobs[0][0] == "w3_down")])
+
+    def _ffn_record(self, synth, gen, wgen, device, m, d, f):
+        """One layer's FFN block: its input, the up/gate rows and the down
+        columns this rank holds (all of them on one GPU)."""
+        import torch
+        x = synth.activations_torch(m, d, gen, device, outliers=True)
+        src = wgen if self.shard else gen  # identical weights on every rank
+        w1, s1 = synth.weight_torch(f, d, src, device)
+        w2, s2 = synth.weight_torch(f, d, src, device)
+        w3, s3 = synth.weight_torch(d, f, src, device)
+        if self.shard:
+            fl = f // self.world
+            r0 = self.rank * fl
+            w1, s1 = w1[r0:r0 + fl].contiguous(), s1[r0:r0 + fl].contiguous()
+            w2, s2 = w2[r0:r0 + fl].contiguous(), s2[r0:r0 + fl].contiguous()
+            w3 = w3[:, r0:r0 + fl].contiguous()
+        return {"ffn": True, "x": x, "k": d, "f": f,
+                "q": torch.empty((m, d), dtype=torch.int8, device=device),
+                "s": torch.empty(m, dtype=torch.float32, device=device),
+                "w1": (w1, s1), "w2": (w2, s2), "w3": (w3, s3),
+                "out": torch.empty((m, d), dtype=torch.float32, device=device), "shard": False}
 
     @property
     def kinds(self):
+        if self.ffn_block:
+            return ("quant", "gemm", "ffn")
         if self.shard:
             return ("quant", "gemm", "gemm_allgather")
         return ("qgemm",) if self.fused else ("quant", "gemm")
@@ -254,6 +287,18 @@ class Prefill:
             for layer in self.L[si]:
                 for gi, g in enumerate(layer):
                     k = g["k"]
+                    if g.get("ffn"):
+                        f, (w1, s1), (w2, s2), (w3, s3) = g["f"], g["w1"], g["w2"], g["w3"]
+                        if want is None or want("quant", 5 * m * k + 4 * m, 0):
+                            gcu.dev_quantize_acts(g["q"], g["s"], g["x"], m, k, stream=stream)
+                        fl = w1.shape[0]
+                        # this rank's weights, the block's activations (up, gate, h in fp32, its
+                        # codes) and output; ops of up, gate and down over this rank's slice
+                        fb = 3 * (fl * k + 4 * fl) + m * k + 4 * m + 3 * 4 * m * fl + m * fl + 4 * m * k
+                        if want is None or want("ffn", fb, 3 * 2 * m * fl * k):
+                            gcu.dev_ffn_rowshard(g["out"], g["q"], g["s"], m, k, f, w1, s1, w2, s2, w3, s3,
+                                                 stream=stream)
+                        continue
                     outs = self.out[si][gi]
                     if g["shard"]:
                         if want is None or want("quant", 5 * m * k + 4 * m, 0):
@@ -288,6 +333,13 @@ class Prefill:
         n = 0
         for si, (_, groups, _, nl) in enumerate(self.stacks):
             for k, jobs in groups:
+                if self.ffn_block and jobs[0][0] == "w3_down":
+                    continue
+                if self.ffn_block and jobs[0][0] == "w1_up":
+                    # quantize; up/gate GEMM, GeGLU(+quantize), down GEMM; sharded: the two
+                    # all-reduces, the separate quantize and the dequant
+                    n += nl * (1 + (3 if not self.shard else 7))
+                    continue
                 sh = self.shard and all(is_ffn(nm) for nm, _ in jobs)
                 n += nl * ((1 + len(jobs)) if sh else (1 if self.fused else 2))
         return n

@@ -15,6 +15,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -29,6 +30,8 @@ struct Nccl {
   ncclResult_t (*getUniqueId)(ncclUniqueId *) = nullptr;
   ncclResult_t (*commInitRank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
   ncclResult_t (*allGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t,
+                            cudaStream_t) = nullptr;
+  ncclResult_t (*allReduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                             cudaStream_t) = nullptr;
   ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
   const char *(*getErrorString)(ncclResult_t) = nullptr;
@@ -47,11 +50,12 @@ int nccl() {
     g_nccl.getUniqueId = (decltype(g_nccl.getUniqueId))dlsym(g_nccl.lib, "ncclGetUniqueId");
     g_nccl.commInitRank = (decltype(g_nccl.commInitRank))dlsym(g_nccl.lib, "ncclCommInitRank");
     g_nccl.allGather = (decltype(g_nccl.allGather))dlsym(g_nccl.lib, "ncclAllGather");
+    g_nccl.allReduce = (decltype(g_nccl.allReduce))dlsym(g_nccl.lib, "ncclAllReduce");
     g_nccl.commDestroy = (decltype(g_nccl.commDestroy))dlsym(g_nccl.lib, "ncclCommDestroy");
     g_nccl.getErrorString = (decltype(g_nccl.getErrorString))dlsym(g_nccl.lib, "ncclGetErrorString");
   });
   if (!g_nccl.lib || !g_nccl.getUniqueId || !g_nccl.commInitRank || !g_nccl.allGather ||
-      !g_nccl.commDestroy)
+      !g_nccl.allReduce || !g_nccl.commDestroy)
     return set_error("NCCL (libnccl.so.2) could not be loaded");
   return 0;
 }
@@ -349,5 +353,123 @@ GCU_EXPORT int gcu_dev_quantize_gemm_int8_rowshard_multi(const gcu_gemv_job *job
     if (gcu_dev_gemm_int8_rowshard(jobs[j].dst, work, static_cast<const int8_t *>(jobs[j].w), jobs[j].sc,
                                    q, s, m, jobs[j].m, k, stream))
       return 1;
+  return 0;
+}
+
+// ---------------------------------------------------------------------------
+// Gemma's feed-forward block over a hidden dimension sharded across the ranks
+// ---------------------------------------------------------------------------
+namespace gcu {
+namespace {
+
+// out[r][c] = (float)acc[r][c] * (hs[r] * ws[c]): the dequant of gemm_int8
+// (gemma.c:3859-3862 under -ffast-math), on int32 sums summed over the ranks
+__global__ void k_dequant_i32(float *__restrict__ out, const int *__restrict__ acc,
+                              const float *__restrict__ hs, const float *__restrict__ ws, int m, int n) {
+  const long total = (long)m * n;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int r = (int)(i / n), c = (int)(i - (long)r * n);
+    out[i] = __fmul_rn(__int2float_rn(acc[i]), __fmul_rn(__ldg(hs + r), __ldg(ws + c)));
+  }
+}
+
+// per-device scratch of the FFN entry point (grown, never shrunk)
+struct FfnScratch {
+  void *p = nullptr;
+  size_t cap = 0;
+};
+std::mutex g_ffn_mu;
+FfnScratch g_ffn[64];
+
+size_t align256(size_t b) { return (b + 255) / 256 * 256; }
+
+}  // namespace
+}  // namespace gcu
+
+// Gemma's FFN for m > 8 tokens (gemma.c:5365-5391 and the GeGLU between,
+// 4139-4170), the hidden dimension `ffn` split over the ranks of gcu_comm_init:
+// rank r holds rows [r*fl, (r+1)*fl) of the up and gate weights (fl =
+// ffn/world) and the same columns of the down weight (a [dim][fl] slice with
+// row stride w_down_stride bytes).  Every rank computes its slice of up and
+// gate, h = gelu(gate)*up on it, and the row maxima of h over its slice; an
+// all-reduce(max) gives every rank the maxima of the full rows, so each
+// quantizes its slice into exactly the codes and scales of the unsharded
+// quantize_acts; its K slice of the down projection gives int32 partial sums,
+// an all-reduce(sum) adds them -- integer addition is exact -- and one
+// dequant forms out [m][dim], the same on every rank and bit for bit the
+// unsharded block's.  The collectives move m floats and m*dim int32 values
+// instead of the 2*m*ffn floats of gathering up and gate.  With one rank (or
+// none initialised) the same block runs unsharded.
+GCU_EXPORT int gcu_dev_ffn_rowshard(float *out, const int8_t *xq, const float *xs, int m, int dim,
+                                    int ffn, const int8_t *w_up, const float *s_up,
+                                    const int8_t *w_gate, const float *s_gate,
+                                    const int8_t *w_down, int w_down_stride, const float *s_down,
+                                    void *stream) {
+  const int world = g_comm.comm ? g_comm.world : 1;
+  if (g_comm.comm && refuse_after_peer_timeout("gcu_dev_ffn_rowshard")) return 1;
+  if (m <= 8) return set_error("gcu_dev_ffn_rowshard: m %d (needs m > 8: tensor-core path)", m);
+  if (dim <= 0 || ffn <= 0 || ffn % world)
+    return set_error("gcu_dev_ffn_rowshard: ffn %d not a positive multiple of world %d", ffn, world);
+  const int fl = ffn / world;
+  if (fl % 16 || dim % 16) return set_error("gcu_dev_ffn_rowshard: ffn/world %d and dim %d must be multiples of 16", fl, dim);
+  if (w_down_stride == 0) w_down_stride = fl;
+  if (w_down_stride < fl || w_down_stride % 16) return set_error("gcu_dev_ffn_rowshard: bad down stride %d", w_down_stride);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int dev = calling_device();
+  if (dev < 0 || dev >= 64) return set_error("gcu_dev_ffn_rowshard: device %d", dev);
+  // scratch: up, h (over gate), row maxima, codes, scales, int32 sums
+  const size_t b_up = align256((size_t)m * fl * 4), b_amax = align256((size_t)m * 4),
+               b_q = align256((size_t)m * fl), b_acc = align256((size_t)m * dim * 4);
+  const size_t need = 2 * b_up + 2 * b_amax + b_q + b_acc;
+  char *base;
+  {
+    std::lock_guard<std::mutex> lk(g_ffn_mu);
+    FfnScratch &fs = g_ffn[dev];
+    if (fs.cap < need) {
+      if (fs.p) {
+        GCU_CUDA(cudaStreamSynchronize(st));
+        cudaFree(fs.p);
+      }
+      fs.p = nullptr;
+      fs.cap = 0;
+      GCU_CUDA(cudaMalloc(&fs.p, need));
+      fs.cap = need;
+    }
+    base = static_cast<char *>(fs.p);
+  }
+  float *up = reinterpret_cast<float *>(base);
+  float *gate = reinterpret_cast<float *>(base + b_up);
+  float *amax = reinterpret_cast<float *>(base + 2 * b_up);
+  float *hs = reinterpret_cast<float *>(base + 2 * b_up + b_amax);
+  int8_t *hq = reinterpret_cast<int8_t *>(base + 2 * b_up + 2 * b_amax);
+  int *acc = reinterpret_cast<int *>(base + 2 * b_up + 2 * b_amax + b_q);
+  // 1. this rank's slice of up (w1) and gate (w2), one launch
+  GemmArgs jobs[2] = {};
+  jobs[0] = GemmArgs{up, fl, w_up, dim, s_up, xq, dim, xs, m, fl, dim};
+  jobs[1] = GemmArgs{gate, fl, w_gate, dim, s_gate, xq, dim, xs, m, fl, dim};
+  if (launch_gemm_tc_jobs(xq, dim, xs, m, dim, jobs, 2, st, 0, 0)) return 1;
+  if (world == 1) {
+    // 2-4 unsharded: the fused GeGLU + quantize, the down projection with its dequant
+    if (gcu_dev_geglu_quantize(hq, hs, nullptr, gate, up, m, fl, stream)) return 1;
+    GemmArgs a{out, dim, w_down, w_down_stride, s_down, hq, fl, hs, m, dim, fl};
+    return launch_gemm_tc(a, st, 0, 0);
+  }
+  // 2. h = gelu(gate)*up over the slice (in place of gate), row maxima of the slice
+  if (launch_geglu_amax(gate, amax, gate, up, m, fl, st)) return 1;
+  // 3. maxima of the full rows: every rank now forms the unsharded codes
+  ncclResult_t r = g_nccl.allReduce(amax, amax, (size_t)m, ncclFloat32, ncclMax, g_comm.comm, st);
+  if (r != ncclSuccess) return nccl_err(r, "ncclAllReduce (row maxima)");
+  if (launch_quantize_given_amax(hq, hs, gate, amax, m, fl, st)) return 1;
+  // 4. this rank's K slice of down: int32 partial sums, summed over the ranks
+  GemmArgs d{reinterpret_cast<float *>(acc), dim, w_down, w_down_stride, nullptr, hq, fl, nullptr, m, dim, fl};
+  d.raw = 1;
+  if (launch_gemm_tc_jobs(hq, fl, nullptr, m, fl, &d, 1, st, 0, 0)) return 1;
+  r = g_nccl.allReduce(acc, acc, (size_t)m * dim, ncclInt32, ncclSum, g_comm.comm, st);
+  if (r != ncclSuccess) return nccl_err(r, "ncclAllReduce (int32 partial sums)");
+  // 5. one dequant of the summed int32 values
+  const long total = (long)m * dim;
+  const int grid = (int)std::min<long>((total + 255) / 256, (long)num_sms() * 8);
+  k_dequant_i32<<<grid, 256, 0, st>>>(out, acc, hs, s_down, m, dim);
+  GCU_CUDA(cudaGetLastError());
   return 0;
 }

@@ -138,6 +138,15 @@ int launch_gemv_p2p(const GemvJobs &jobs, const int8_t *x, long xstride, const f
                     const float *xf, int8_t *qout, float *sout, int mb, int k,
                     const PeerOut &po, cudaStream_t st);
 
+// GeGLU over a slice of the hidden dimension (k_producers.cu): h and each
+// row's |max| over the slice; then the codes of h given each row's max over
+// every slice (scales as quantize_acts writes them).  Rows 16-byte aligned,
+// n % 4 == 0.
+int launch_geglu_amax(float *h, float *amax, const float *gate, const float *up, int m, int n,
+                      cudaStream_t st);
+int launch_quantize_given_amax(int8_t *q, float *s, const float *h, const float *amax, int m, int n,
+                               cudaStream_t st);
+
 // quantize_acts + GEMV in one launch (mb <= 8 rows of fp32 xf); writes the
 // codes (qout, dense [mb][k]) and scales (sout) as quantize_acts would.
 int launch_quantize_gemv(const GemvJobs &jobs, const float *xf, long xfstride,
@@ -154,6 +163,7 @@ struct GemmArgs {
   long sstr;
   const float *ssc;
   int m, n, k;
+  int raw = 0;  // 1: dst receives the int32 sums (as their bit patterns), scales unused
 };
 // force_bn / force_mb / force_split = 0 let the planner choose the tile
 // shape ((128*mb) x bn) and the K split.

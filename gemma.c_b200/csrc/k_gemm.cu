@@ -116,6 +116,7 @@ struct alignas(64) TcJob {
   int n;
   int tn_begin;  // first global n-tile of this job
   int tma_store;
+  int raw;       // write the int32 sums themselves (bit patterns), no dequant
 };
 
 struct alignas(64) TcParams {
@@ -166,7 +167,7 @@ __device__ __forceinline__ void emit_chunk(const TcParams &p, const TcJob &job, 
   float out[32];
 #pragma unroll
   for (int i = 0; i < 32; ++i)
-    out[i] = dequant(acc[i], xs, __shfl_sync(0xffffffffu, ws_lane, i));
+    out[i] = job.raw ? __int_as_float(acc[i]) : dequant(acc[i], xs, __shfl_sync(0xffffffffu, ws_lane, i));
   if (TMA) {
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
@@ -216,9 +217,10 @@ __device__ __forceinline__ void share_scales(const TcParams &p, const TcJob &job
     const int row = w.m_t * C::TILE_M + rb * 32 + lane;
     const int col = w.n_t * BN + ch * 32 + 4 * c;
     const bool ok = r0 + i < my_nb;
-    sc.xs[i] = ok && row < p.m ? __ldg(p.ssc + row) : 0.0f;
+    sc.xs[i] = ok && !job.raw && row < p.m ? __ldg(p.ssc + row) : 0.0f;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) sc.ws[i][e] = ok && col + e < job.n ? __ldg(job.matsc + col + e) : 0.0f;
+    for (int e = 0; e < 4; ++e)
+      sc.ws[i][e] = ok && !job.raw && col + e < job.n ? __ldg(job.matsc + col + e) : 0.0f;
   }
 }
 
@@ -263,10 +265,12 @@ __device__ __forceinline__ void reduce_share(const TcParams &p, const TcJob &job
       const int row = w.m_t * C::TILE_M + rb * 32 + lane;
       const int col = w.n_t * BN + ch * 32 + 4 * c;
       if (row >= p.m || col >= job.n) continue;
-      const float4 o = make_float4(dequant(acc[i].x, sc.xs[i], sc.ws[i][0]),
-                                   dequant(acc[i].y, sc.xs[i], sc.ws[i][1]),
-                                   dequant(acc[i].z, sc.xs[i], sc.ws[i][2]),
-                                   dequant(acc[i].w, sc.xs[i], sc.ws[i][3]));
+      const float4 o = job.raw ? make_float4(__int_as_float(acc[i].x), __int_as_float(acc[i].y),
+                                             __int_as_float(acc[i].z), __int_as_float(acc[i].w))
+                               : make_float4(dequant(acc[i].x, sc.xs[i], sc.ws[i][0]),
+                                             dequant(acc[i].y, sc.xs[i], sc.ws[i][1]),
+                                             dequant(acc[i].z, sc.xs[i], sc.ws[i][2]),
+                                             dequant(acc[i].w, sc.xs[i], sc.ws[i][3]));
       float *d = job.dst + (size_t)row * job.dstr + col;
       if (job.tma_store && col + 3 < job.n) {  // 16-byte aligned rows
         *reinterpret_cast<float4 *>(d) = o;
@@ -442,12 +446,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_tc(const __grid_constan
       // operand scales of this tile, fetched while its MMAs still run: the
       // row's activation scale, and lane i holds column (32*ch + i)'s weight
       // scale for chunk ch
-      const float xs = row < p.m ? __ldg(p.ssc + row) : 0.0f;
+      const float xs = !job.raw && row < p.m ? __ldg(p.ssc + row) : 0.0f;
       float wsl[NCH];
 #pragma unroll
       for (int ch = 0; ch < NCH; ++ch) {
         const int col = n0 + ch * 32 + lane;
-        wsl[ch] = col < job.n ? __ldg(job.matsc + col) : 0.0f;
+        wsl[ch] = !job.raw && col < job.n ? __ldg(job.matsc + col) : 0.0f;
       }
       if (!ptx::mbar_wait(&tfull[buf], use & 1, p.err, DEV_TIMEOUT_TMEM)) break;
       ptx::tc_fence_after();
@@ -747,12 +751,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_pair(const __grid_const
       const int tile_row0 = w.m_t * C::TILE_M + crank * BM + q * 32;
       const int row = tile_row0 + lane;
       const int n0 = w.n_t * BN;
-      const float xs = row < p.m ? __ldg(p.ssc + row) : 0.0f;
+      const float xs = !job.raw && row < p.m ? __ldg(p.ssc + row) : 0.0f;
       float wsl[NCH];
 #pragma unroll
       for (int ch = 0; ch < NCH; ++ch) {
         const int col = n0 + ch * 32 + lane;
-        wsl[ch] = col < job.n ? __ldg(job.matsc + col) : 0.0f;
+        wsl[ch] = !job.raw && col < job.n ? __ldg(job.matsc + col) : 0.0f;
       }
       if (!ptx::mbar_wait(&tfull[buf], use & 1, p.err, DEV_TIMEOUT_TMEM)) break;
       ptx::tc_fence_after();
@@ -1158,6 +1162,7 @@ int run_plan(const Plan &pl, const int8_t *src, long sstr, const float *ssc, int
     TcJob &J = p.jobs[j];
     if (make_map_i8(&J.tmB, jobs[j].mat, k, jobs[j].n, jobs[j].mstr, pair ? bn / 2 : bn)) return 1;
     J.tma_store = ((uintptr_t)jobs[j].dst % 16 == 0) && (jobs[j].dstr % 4 == 0);
+    J.raw = jobs[j].raw;
     if (J.tma_store && make_map_f32(&J.tmD, jobs[j].dst, jobs[j].n, m, jobs[j].dstr)) return 1;
     J.matsc = jobs[j].matsc;
     J.dst = jobs[j].dst;
@@ -1246,3 +1251,17 @@ int gemm_plan_one_cta(int m, int k, const int *n, int njobs, int sms, int *bn, i
 int gemm_split_for(int tiles, int k, int sms) { return split_for(tiles, (k + BK - 1) / BK, sms); }
 
 }  // namespace gcu
+
+// Test hook (not in the public header): gemm_int8's int32 sums themselves,
+// dst[i][j] = sum_l src[i][l] * mat[j][l] as int32 bit patterns, with a forced
+// tile shape and K split -- the mode the sharded FFN's down projection uses.
+extern "C" __attribute__((visibility("default"))) int gcu_dev_gemm_int8_raw_tuned(
+    int32_t *dst, const int8_t *mat, const int8_t *src, int m, int n, int k, int bn, int split, int mb,
+    void *stream) {
+  using namespace gcu;
+  if (m <= 8) return set_error("gemm_int8_raw: m > 8 only (tensor-core path)");
+  GemmArgs a{reinterpret_cast<float *>(dst), n, mat, k, nullptr, src, k, nullptr, m, n, k};
+  a.raw = 1;
+  return launch_gemm_tc_jobs(src, k, nullptr, m, k, &a, 1, static_cast<cudaStream_t>(stream), bn, split,
+                             nullptr, mb);
+}

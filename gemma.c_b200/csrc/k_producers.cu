@@ -30,7 +30,11 @@
 namespace gcu {
 namespace {
 
-enum Producer { RMSNORM = 0, GEGLU = 1 };
+// GEGLU_AMAX and QUANT_GIVEN split GEGLU in two for a hidden dimension
+// sharded over ranks: the first writes h and each row's local |max| (in place
+// of the scale), the second quantizes h with the row maxima all ranks agreed
+// on (b = amax per row), so every rank forms the codes of the unsharded row.
+enum Producer { RMSNORM = 0, GEGLU = 1, GEGLU_AMAX = 2, QUANT_GIVEN = 3 };
 
 template <int WPR, bool MAX>
 __device__ __forceinline__ float row_reduce(float v, float *red, int warp, int grp, int lane) {
@@ -74,13 +78,13 @@ __global__ void __launch_bounds__(256) k_producer_quant(int8_t *__restrict__ dst
   float4 v[VPT];
   if (live) {
     const float4 *ar = reinterpret_cast<const float4 *>(a + (size_t)row * astr);
-    const float4 *br = reinterpret_cast<const float4 *>(P == GEGLU ? b + (size_t)row * astr : b);
+    const float4 *br = reinterpret_cast<const float4 *>(P == GEGLU || P == GEGLU_AMAX ? b + (size_t)row * astr : b);
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int idx = (i * WPR + wi) * 32 + lane;
       if (idx < n4) {
         v[i] = __ldcs(ar + idx);
-        if (P == GEGLU) {
+        if (P == GEGLU || P == GEGLU_AMAX) {
           const float4 u = __ldcs(br + idx);
           v[i] = make_float4(__fmul_rn(gelu_tanh(v[i].x), u.x), __fmul_rn(gelu_tanh(v[i].y), u.y),
                              __fmul_rn(gelu_tanh(v[i].z), u.z), __fmul_rn(gelu_tanh(v[i].w), u.w));
@@ -114,13 +118,27 @@ __global__ void __launch_bounds__(256) k_producer_quant(int8_t *__restrict__ dst
     }
   }
   float amax = 0.0f;
-  if (live) {
+  if (P == QUANT_GIVEN) {
+    if (live) amax = __ldg(b + row);  // the row's max over every rank's slice
+  } else {
+    if (live) {
 #pragma unroll
-    for (int i = 0; i < VPT; ++i)
-      if ((i * WPR + wi) * 32 + lane < n4) amax = ptx::absmax4(v[i], amax);
+      for (int i = 0; i < VPT; ++i)
+        if ((i * WPR + wi) * 32 + lane < n4) amax = ptx::absmax4(v[i], amax);
+    }
+    amax = row_reduce<WPR, true>(amax, red, warp, grp, lane);
   }
-  amax = row_reduce<WPR, true>(amax, red, warp, grp, lane);
   if (!live) return;
+  if (P == GEGLU_AMAX) {
+    float4 *o = reinterpret_cast<float4 *>(out + (size_t)row * n);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int idx = (i * WPR + wi) * 32 + lane;
+      if (idx < n4) o[idx] = v[i];
+    }
+    if (wi == 0 && lane == 0) dsc[row] = amax;
+    return;
+  }
   float scale, inv;
   ptx::quant_scale(amax, scale, inv);
   int *q = reinterpret_cast<int *>(dst + (size_t)row * n);
@@ -154,7 +172,8 @@ int launch_producer(int8_t *dst, float *dsc, float *out, const float *a, const f
   if (n <= 0 || n % 4 || n > 16384)
     return set_error("%s: row length %d must be a positive multiple of 4 up to 16384", what, n);
   if (astr < n || astr % 4) return set_error("%s: row stride %ld must be >= %d and a multiple of 4", what, astr, n);
-  if (!dst || !dsc || !a || !b) return set_error("%s: null pointer", what);
+  if ((P != GEGLU_AMAX && !dst) || !dsc || !a || !b || (P == GEGLU_AMAX && !out))
+    return set_error("%s: null pointer", what);
   if ((uintptr_t)a % 16 || (uintptr_t)b % 16 || (uintptr_t)dst % 4 || (out && (uintptr_t)out % 16))
     return set_error("%s: rows must be 16-byte aligned (codes 4-byte)", what);
   const int n4 = n / 4;
@@ -196,6 +215,20 @@ GCU_EXPORT int gcu_dev_geglu_quantize(int8_t *q, float *s, float *h, const float
   return launch_producer<GEGLU>(q, s, h, gate, up, 0.0f, dim, m, dim, static_cast<cudaStream_t>(stream),
                                 "geglu_quantize");
 }
+
+namespace gcu {
+// The two halves of gcu_dev_geglu_quantize for a sharded hidden dimension
+// (gcu_comm.cu): h = gelu(gate) * up and each row's |max| over this slice;
+// then the codes of h given every row's max over all slices.
+int launch_geglu_amax(float *h, float *amax, const float *gate, const float *up, int m, int n,
+                      cudaStream_t st) {
+  return launch_producer<GEGLU_AMAX>(nullptr, amax, h, gate, up, 0.0f, n, m, n, st, "geglu_amax");
+}
+int launch_quantize_given_amax(int8_t *q, float *s, const float *h, const float *amax, int m, int n,
+                               cudaStream_t st) {
+  return launch_producer<QUANT_GIVEN>(q, s, nullptr, h, amax, 0.0f, n, m, n, st, "quantize_given_amax");
+}
+}  // namespace gcu
 
 // ---------------------------------------------------------------------------
 // residual stream: x = clamp(resid + rmsnorm(y)), and the logit softcap

@@ -82,6 +82,7 @@ SIGNATURES = {
     "gcu_gemm_chain_run": (_int, [_int, _vp]),
     "gcu_gemm_chain_plan": (_int, [_int, ctypes.POINTER(_int), _int]),
     "gcu_gemm_chain_destroy": (_int, [_int]),
+    "gcu_dev_ffn_rowshard": (_int, [_vp, _vp, _vp, _int, _int, _int, _vp, _vp, _vp, _vp, _vp, _int, _vp, _vp]),
     "gcu_comm_unique_id": (_int, [ctypes.c_char_p]),
     "gcu_comm_init": (_int, [_int, _int, ctypes.c_char_p]),
     "gcu_comm_destroy": (_int, []),
@@ -113,6 +114,7 @@ EXTRA = {
                                              _int, _int, _vp]),
     "gcu_dev_gemm_int8_tuned": (_int, [_vp, _int, _vp, _int, _vp, _vp, _int, _vp, _int, _int, _int,
                                        _int, _int, _int, _vp]),
+    "gcu_dev_gemm_int8_raw_tuned": (_int, [_vp, _vp, _vp, _int, _int, _int, _int, _int, _int, _vp]),
     "gcu_dev_gemm_int8_noalloc_tuned": (_int, [_vp, _int, _vp, _int, _vp, _vp, _int, _vp, _int, _int,
                                                _int, _int, _int, _int, _vp]),
 }
@@ -412,6 +414,21 @@ class GemmChain:
             self.close()
         except Exception:
             pass
+
+
+def dev_ffn_rowshard(out, xq, xs, m, dim, ffn, w_up, s_up, w_gate, s_gate, w_down, s_down, w_down_stride=0,
+                     stream=None):
+    """Gemma's FFN (up, gate, GeGLU, quantize, down) with the hidden dimension
+    split over the ranks of comm_init; unsharded without it."""
+    _check(lib().gcu_dev_ffn_rowshard(out.data_ptr(), xq.data_ptr(), xs.data_ptr(), m, dim, ffn, w_up.data_ptr(),
+                                      s_up.data_ptr(), w_gate.data_ptr(), s_gate.data_ptr(), w_down.data_ptr(),
+                                      w_down_stride, s_down.data_ptr(), _stream(stream)), "dev_ffn_rowshard")
+
+
+def dev_gemm_int8_raw_tuned(dst, mat, src, m, n, k, bn=0, split=0, mb=0, stream=None):
+    """The int32 sums of gemm_int8 (dst: int32 tensor), forced tile shape (tests)."""
+    _check(lib().gcu_dev_gemm_int8_raw_tuned(dst.data_ptr(), mat.data_ptr(), src.data_ptr(), m, n, k, bn, split, mb,
+                                             _stream(stream)), "dev_gemm_int8_raw_tuned")
 
 
 def comm_unique_id() -> bytes:

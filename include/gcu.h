@@ -386,6 +386,26 @@ int gcu_dev_quantize_gemm_int8_rowshard_multi(const gcu_gemv_job *jobs, int njob
                                               int xstr, int m, int k, float *work,
                                               void *stream);
 
+/* Gemma's feed-forward block for m > 8 tokens (gemma.c:5365-5391 with the
+ * GeGLU of 4139-4170 between), the hidden dimension `ffn` split over the
+ * ranks of gcu_comm_init (fl = ffn/world, a multiple of 16; dim % 16 == 0):
+ *   up   = gemm_int8(w_up, xq, xs), gate = gemm_int8(w_gate, xq, xs)   rows [r*fl, (r+1)*fl) of w1 / w2
+ *   h    = gelu(gate) * up;  (hq, hs) = quantize_acts(h)
+ *   out  = gemm_int8(w_down, hq, hs)           w_down: columns [r*fl, (r+1)*fl) of w3, [dim][fl],
+ *                                               row stride w_down_stride bytes (0 = fl)
+ * s_down holds all dim scales of w3.  Each rank quantizes its slice of h with
+ * the maxima of the full rows (an all-reduce of m floats) and sums its int32
+ * partial products of down with the other ranks' (an all-reduce of m*dim
+ * int32, exact), so `out` [m][dim] is the same on every rank and bit for
+ * bit the unsharded block's.  Without gcu_comm_init it runs unsharded (the
+ * same bits as gcu_dev_gemm_int8_multi + gcu_dev_geglu_quantize +
+ * gcu_dev_gemm_int8).  No single counterpart in the reference (it is the
+ * sharded form of three of its calls). */
+int gcu_dev_ffn_rowshard(float *out, const int8_t *xq, const float *xs, int m, int dim, int ffn,
+                         const int8_t *w_up, const float *s_up, const int8_t *w_gate,
+                         const float *s_gate, const int8_t *w_down, int w_down_stride,
+                         const float *s_down, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
