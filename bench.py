@@ -877,6 +877,7 @@ def run_ours(args):
         del wl
         torch.cuda.empty_cache()
         out["decode"] = decode_records(args, gcu, world, rank, device, stream, peaks)
+        out["ffn12b"] = ffn_record(args, gcu, world, rank, device, stream)
     if comm_on:
         gcu.comm_destroy()
     if rank == 0:
@@ -936,6 +937,66 @@ def decode_records(args, gcu, world, rank, device, stream, peaks):
         rec[key] = r
         del graph, wl, prof
         torch.cuda.empty_cache()
+    return rec
+
+
+def ffn_record(args, gcu, world, rank, device, stream, layers=4):
+    """The Gemma-3-12B FFN block of configs[4] (M = 4096 tokens, dim 3840,
+    ffn 15360) through gcu_dev_ffn_rowshard over `layers` layers: unsharded at
+    N = 1; at N > 1 the hidden dimension split over the ranks, with the row
+    maxima and the int32 partial sums all-reduced (bit-exact, strong scaling:
+    the same total work at every N).  A block-level record (the full 48-layer
+    prefill12b step is `--workload prefill12b`)."""
+    import torch
+    import synth
+    m, d, f = 4096, 3840, 15360
+    fl = f // world
+    r0 = rank * fl
+    wgen = torch.Generator(device=device).manual_seed(4321)
+    L = []
+    for _ in range(layers):
+        x = synth.activations_torch(m, d, wgen, device, outliers=True)
+        q = torch.empty((m, d), dtype=torch.int8, device=device)
+        s = torch.empty(m, dtype=torch.float32, device=device)
+        gcu.dev_quantize_acts(q, s, x, m, d)
+        del x
+        w1, s1 = synth.weight_torch(f, d, wgen, device)
+        w2, s2 = synth.weight_torch(f, d, wgen, device)
+        w3, s3 = synth.weight_torch(d, f, wgen, device)
+        L.append((q, s, w1[r0:r0 + fl].contiguous(), s1[r0:r0 + fl].contiguous(), w2[r0:r0 + fl].contiguous(),
+                  s2[r0:r0 + fl].contiguous(), w3[:, r0:r0 + fl].contiguous(), s3,
+                  torch.empty((m, d), dtype=torch.float32, device=device)))
+        del w1, w2, w3
+    torch.cuda.synchronize()
+
+    def step():
+        for q, s, w1, s1, w2, s2, w3, s3, out in L:
+            gcu.dev_ffn_rowshard(out, q, s, m, d, f, w1, s1, w2, s2, w3, s3, stream=stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = max(1, min(args.steps, 10))
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(reps):
+            step()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / reps / layers, world)
+    gcu.check_device()
+    ops = 3 * 2 * m * f * d
+    rec = {"workload": "Gemma-3-12B FFN block (configs[4]): M=4096, dim 3840, ffn 15360; up/gate, GeGLU, "
+                       "quantize, down per layer",
+           "sharding": ("hidden dimension over %d GPUs: row maxima and int32 partial sums all-reduced (exact)"
+                        % world) if world > 1 else "single GPU, unsharded",
+           "unit": "int8 TOPS", "ms_per_layer": ms, "value": ops / (ms * 1e-3) / 1e12, "layers_timed": layers,
+           "scaling": "strong"}
+    del L
+    torch.cuda.empty_cache()
     return rec
 
 

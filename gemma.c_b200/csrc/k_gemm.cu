@@ -116,7 +116,6 @@ struct alignas(64) TcJob {
   int n;
   int tn_begin;  // first global n-tile of this job
   int tma_store;
-  int raw;       // write the int32 sums themselves (bit patterns), no dequant
 };
 
 struct alignas(64) TcParams {
@@ -160,14 +159,18 @@ __device__ __forceinline__ Unit decode_unit(const TcParams &p, int u) {
 // warp's swizzled staging buffer for a TMA store, or straight to global.
 // Lane i of the warp holds the weight scale of column col0 + i in `ws_lane`
 // (loaded before the accumulator was ready); shuffles broadcast it.
-template <bool TMA>
+template <bool TMA, bool RAW = false>
 __device__ __forceinline__ void emit_chunk(const TcParams &p, const TcJob &job, const int (&acc)[32],
                                            float xs, float ws_lane, int row, int col0, int lane,
                                            uint8_t *stage, int tile_row0) {
   float out[32];
 #pragma unroll
   for (int i = 0; i < 32; ++i)
-    out[i] = job.raw ? __int_as_float(acc[i]) : dequant(acc[i], xs, __shfl_sync(0xffffffffu, ws_lane, i));
+    out[i] = dequant(acc[i], xs, __shfl_sync(0xffffffffu, ws_lane, i));
+  if (RAW) {  // the int32 sums themselves, as their bit patterns
+#pragma unroll
+    for (int i = 0; i < 32; ++i) out[i] = __int_as_float(acc[i]);
+  }
   if (TMA) {
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
@@ -204,7 +207,7 @@ struct ShareScales {
   float ws[4][4];
 };
 
-template <typename C, int BN>
+template <typename C, int BN, bool RAW = false>
 __device__ __forceinline__ void share_scales(const TcParams &p, const TcJob &job, const Unit &w,
                                              int r0, int my_nb, ShareScales &sc) {
   constexpr int NCH = BN / 32;
@@ -217,14 +220,14 @@ __device__ __forceinline__ void share_scales(const TcParams &p, const TcJob &job
     const int row = w.m_t * C::TILE_M + rb * 32 + lane;
     const int col = w.n_t * BN + ch * 32 + 4 * c;
     const bool ok = r0 + i < my_nb;
-    sc.xs[i] = ok && !job.raw && row < p.m ? __ldg(p.ssc + row) : 0.0f;
+    sc.xs[i] = ok && !RAW && row < p.m ? __ldg(p.ssc + row) : 0.0f;
 #pragma unroll
     for (int e = 0; e < 4; ++e)
-      sc.ws[i][e] = ok && !job.raw && col + e < job.n ? __ldg(job.matsc + col + e) : 0.0f;
+      sc.ws[i][e] = ok && !RAW && col + e < job.n ? __ldg(job.matsc + col + e) : 0.0f;
   }
 }
 
-template <typename C, int BN>
+template <typename C, int BN, bool RAW = false>
 __device__ __forceinline__ void reduce_share(const TcParams &p, const TcJob &job, const Unit &w,
                                              size_t part_int4, int my_nb, ShareScales &sc) {
   constexpr int NCH = BN / 32;
@@ -232,7 +235,7 @@ __device__ __forceinline__ void reduce_share(const TcParams &p, const TcJob &job
   const int lane = et & 31, c = et >> 5;
   const int4 *tbase = reinterpret_cast<const int4 *>(p.ws) + (size_t)w.tile * p.splits * part_int4;
   for (int r0 = 0; r0 < my_nb; r0 += 4) {
-    if (r0 > 0) share_scales<C, BN>(p, job, w, r0, my_nb, sc);
+    if (r0 > 0) share_scales<C, BN, RAW>(p, job, w, r0, my_nb, sc);
     int4 acc[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[i] = make_int4(0, 0, 0, 0);
@@ -265,7 +268,7 @@ __device__ __forceinline__ void reduce_share(const TcParams &p, const TcJob &job
       const int row = w.m_t * C::TILE_M + rb * 32 + lane;
       const int col = w.n_t * BN + ch * 32 + 4 * c;
       if (row >= p.m || col >= job.n) continue;
-      const float4 o = job.raw ? make_float4(__int_as_float(acc[i].x), __int_as_float(acc[i].y),
+      const float4 o = RAW ? make_float4(__int_as_float(acc[i].x), __int_as_float(acc[i].y),
                                              __int_as_float(acc[i].z), __int_as_float(acc[i].w))
                                : make_float4(dequant(acc[i].x, sc.xs[i], sc.ws[i][0]),
                                              dequant(acc[i].y, sc.xs[i], sc.ws[i][1]),
@@ -284,7 +287,7 @@ __device__ __forceinline__ void reduce_share(const TcParams &p, const TcJob &job
   }
 }
 
-template <int BN, int MB>
+template <int BN, int MB, bool RAW = false>
 __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_tc(const __grid_constant__ TcParams p) {
   using C = Cfg<BN, MB>;
   extern __shared__ uint8_t smem_raw[];
@@ -446,12 +449,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_tc(const __grid_constan
       // operand scales of this tile, fetched while its MMAs still run: the
       // row's activation scale, and lane i holds column (32*ch + i)'s weight
       // scale for chunk ch
-      const float xs = !job.raw && row < p.m ? __ldg(p.ssc + row) : 0.0f;
+      const float xs = !RAW && row < p.m ? __ldg(p.ssc + row) : 0.0f;
       float wsl[NCH];
 #pragma unroll
       for (int ch = 0; ch < NCH; ++ch) {
         const int col = n0 + ch * 32 + lane;
-        wsl[ch] = !job.raw && col < job.n ? __ldg(job.matsc + col) : 0.0f;
+        wsl[ch] = !RAW && col < job.n ? __ldg(job.matsc + col) : 0.0f;
       }
       if (!ptx::mbar_wait(&tfull[buf], use & 1, p.err, DEV_TIMEOUT_TMEM)) break;
       ptx::tc_fence_after();
@@ -470,10 +473,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_tc(const __grid_constan
           if (job.tma_store) {
             if (lane == 0) ptx::bulk_wait_read<0>();
             __syncwarp();
-            emit_chunk<true>(p, job, reinterpret_cast<const int(&)[32]>(r), xs, wsl[ch], row, col0,
+            emit_chunk<true, RAW>(p, job, reinterpret_cast<const int(&)[32]>(r), xs, wsl[ch], row, col0,
                              lane, stage, tile_row0);
           } else {
-            emit_chunk<false>(p, job, reinterpret_cast<const int(&)[32]>(r), xs, wsl[ch], row, col0,
+            emit_chunk<false, RAW>(p, job, reinterpret_cast<const int(&)[32]>(r), xs, wsl[ch], row, col0,
                               lane, nullptr, tile_row0);
           }
         }
@@ -511,14 +514,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_tc(const __grid_constan
           constexpr int NB = C::TILE_M / 32 * NCH;
           const int my_nb = (NB - w.s + p.splits - 1) / p.splits;
           ShareScales sc;
-          share_scales<C, BN>(p, job, w, 0, my_nb, sc);
+          share_scales<C, BN, RAW>(p, job, w, 0, my_nb, sc);
           if (threadIdx.x == 64) {
             atomicAdd(p.counters + w.tile, 1);
             ptx::flag_wait_geq<false>(p.counters + w.tile, p.splits, ptx::globaltimer(), p.err,
                                       DEV_TIMEOUT_SPLIT);
           }
           ptx::named_bar_sync(1, kEpiThreads);
-          reduce_share<C, BN>(p, job, w, kPartInt4, my_nb, sc);
+          reduce_share<C, BN, RAW>(p, job, w, kPartInt4, my_nb, sc);
           ptx::named_bar_sync(1, kEpiThreads);
           if (threadIdx.x == 64) {
             // the last split done reading resets both counters for the next launch
@@ -564,9 +567,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_tc(const __grid_constan
             if (job.tma_store) {
               if (lane == 0) ptx::bulk_wait_read<0>();
               __syncwarp();
-              emit_chunk<true>(p, job, acc, xs, wsl[ch], row, col0, lane, stage, tile_row0);
+              emit_chunk<true, RAW>(p, job, acc, xs, wsl[ch], row, col0, lane, stage, tile_row0);
             } else {
-              emit_chunk<false>(p, job, acc, xs, wsl[ch], row, col0, lane, nullptr, tile_row0);
+              emit_chunk<false, RAW>(p, job, acc, xs, wsl[ch], row, col0, lane, nullptr, tile_row0);
             }
           }
           ptx::named_bar_sync(1, kEpiThreads);
@@ -751,12 +754,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_pair(const __grid_const
       const int tile_row0 = w.m_t * C::TILE_M + crank * BM + q * 32;
       const int row = tile_row0 + lane;
       const int n0 = w.n_t * BN;
-      const float xs = !job.raw && row < p.m ? __ldg(p.ssc + row) : 0.0f;
+      const float xs = row < p.m ? __ldg(p.ssc + row) : 0.0f;
       float wsl[NCH];
 #pragma unroll
       for (int ch = 0; ch < NCH; ++ch) {
         const int col = n0 + ch * 32 + lane;
-        wsl[ch] = !job.raw && col < job.n ? __ldg(job.matsc + col) : 0.0f;
+        wsl[ch] = col < job.n ? __ldg(job.matsc + col) : 0.0f;
       }
       if (!ptx::mbar_wait(&tfull[buf], use & 1, p.err, DEV_TIMEOUT_TMEM)) break;
       ptx::tc_fence_after();
@@ -847,7 +850,7 @@ int make_map_f32(CUtensorMap *m, float *base, int n, int rows, long stride_elems
   return 0;
 }
 
-template <int BN, int MB>
+template <int BN, int MB, bool RAW = false>
 int launch_cfg(TcParams &p, cudaStream_t st) {
   using C = Cfg<BN, MB>;
   // the shared-memory opt-in is per device; set it once, outside any capture
@@ -858,13 +861,13 @@ int launch_cfg(TcParams &p, cudaStream_t st) {
   {
     std::lock_guard<std::mutex> lk(mu);
     if (!(done_mask & (1ull << (dev & 63)))) {
-      GCU_CUDA(cudaFuncSetAttribute(k_gemm_i8_tc<BN, MB>,
+      GCU_CUDA(cudaFuncSetAttribute(k_gemm_i8_tc<BN, MB, RAW>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
       done_mask |= 1ull << (dev & 63);
     }
   }
   int grid = p.units < num_sms() ? p.units : num_sms();
-  GCU_CUDA(launch_k(k_gemm_i8_tc<BN, MB>, grid, kThreads, C::SMEM, st, p));
+  GCU_CUDA(launch_k(k_gemm_i8_tc<BN, MB, RAW>, grid, kThreads, C::SMEM, st, p));
   GCU_CUDA(cudaGetLastError());
   return 0;
 }
@@ -1126,10 +1129,12 @@ int launch_gemm_tc_jobs(const int8_t *src, long sstr, const float *ssc, int m, i
     if (pl.mb == kPairMB && pl.splits > 1) return set_error("gemm: the CTA-pair tiles take no K split");
     return run_plan(pl, src, sstr, ssc, m, k, jobs, njobs, st, ext);
   }
-  pl = model_plan(m, k, jobs, njobs, sms);
+  // int32-sum output exists for the one-CTA tiles only
+  const bool raw = jobs[0].raw != 0;
+  pl = model_plan(m, k, jobs, njobs, sms, !raw);
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
   GCU_CUDA(cudaStreamIsCapturing(st, &cap));
-  if (!ext && autotune_enabled() && cap == cudaStreamCaptureStatusNone &&
+  if (!ext && !raw && autotune_enabled() && cap == cudaStreamCaptureStatusNone &&
       tuned_plan(&pl, src, sstr, ssc, m, k, jobs, njobs, st, sms))
     return 1;
   if (force_split > 0) pl.splits = force_split;
@@ -1142,6 +1147,9 @@ int run_plan(const Plan &pl, const int8_t *src, long sstr, const float *ssc, int
              const GemmArgs *jobs, int njobs, cudaStream_t st, const ExtWorkspace *ext) {
   const int bn = pl.bn, mb = pl.mb;
   const bool pair = mb == kPairMB;
+  for (int j = 1; j < njobs; ++j)
+    if (jobs[j].raw != jobs[0].raw) return set_error("gemm: int32-sum output is all jobs or none");
+  if (jobs[0].raw && pair) return set_error("gemm: int32-sum output has no CTA-pair tile");
   const int kb_total = (k + BK - 1) / BK;
   const int tile_m = tile_rows(mb);
   const int tiles_m = (m + tile_m - 1) / tile_m;
@@ -1162,7 +1170,6 @@ int run_plan(const Plan &pl, const int8_t *src, long sstr, const float *ssc, int
     TcJob &J = p.jobs[j];
     if (make_map_i8(&J.tmB, jobs[j].mat, k, jobs[j].n, jobs[j].mstr, pair ? bn / 2 : bn)) return 1;
     J.tma_store = ((uintptr_t)jobs[j].dst % 16 == 0) && (jobs[j].dstr % 4 == 0);
-    J.raw = jobs[j].raw;
     if (J.tma_store && make_map_f32(&J.tmD, jobs[j].dst, jobs[j].n, m, jobs[j].dstr)) return 1;
     J.matsc = jobs[j].matsc;
     J.dst = jobs[j].dst;
@@ -1207,6 +1214,16 @@ int run_plan(const Plan &pl, const int8_t *src, long sstr, const float *ssc, int
     if (bn == 128) return launch_pair<128>(p, st);
     if (bn == 192) return launch_pair<192>(p, st);
     return launch_pair<256>(p, st);
+  }
+  if (jobs[0].raw) {  // int32 sums out (one-CTA tiles only)
+    if (mb == 2) {
+      if (bn == 128) return launch_cfg<128, 2, true>(p, st);
+      if (bn == 192) return launch_cfg<192, 2, true>(p, st);
+      return launch_cfg<256, 2, true>(p, st);
+    }
+    if (bn == 256) return launch_cfg<256, 1, true>(p, st);
+    if (bn == 128) return launch_cfg<128, 1, true>(p, st);
+    return launch_cfg<64, 1, true>(p, st);
   }
   if (mb == 2) {
     if (bn == 128) return launch_cfg<128, 2>(p, st);

@@ -5,7 +5,7 @@ quantize_acts, down) with the hidden dimension split over the ranks of
 gcu_comm_init; without it, unsharded.  The sharded form sums the down
 projection's int32 partial products over the ranks, so the GEMM must be able
 to write the int32 sums themselves: those are checked against the oracle's
-exact accumulators on every tile shape, K split and CTA-pair plan, and the
+exact accumulators on every one-CTA tile shape and K split, and the
 unsharded block against the step-by-step calls bit for bit.  The two-rank
 form is tests/test_gpu_ffn_rowshard.py.
 """
@@ -32,7 +32,7 @@ def _gpu():
 
 @pytest.mark.parametrize("m,n,k,bn,split,mb", [
     (300, 1000, 1168, 64, 1, 1), (512, 1152, 7680, 128, 4, 1), (512, 1152, 7680, 0, 0, 0),
-    (256, 2048, 1920, 192, 1, 2), (1024, 3840, 1920, 256, 1, 4), (130, 480, 3840, 128, 3, 1),
+    (256, 2048, 1920, 192, 1, 2), (1024, 3840, 1920, 256, 1, 2), (130, 480, 3840, 128, 3, 1),
     (4096, 3840, 7680, 0, 0, 0)])
 def test_raw_int32_sums_are_exact(m, n, k, bn, split, mb):
     # the sums past 2^24 (k = 7680: up to 1.2e8) that an fp32 output could not hold
@@ -53,6 +53,14 @@ def test_raw_int32_sums_are_exact(m, n, k, bn, split, mb):
     got = acc[rows].cpu().numpy()
     assert np.array_equal(got, want), f"{int((got != want).sum())} of {got.size} sums differ"
     assert abs(int(want[0, 0])) == k * 127 * 127 and (k * 127 * 127 > (1 << 24) or k < 1100)
+
+
+def test_raw_int32_sums_have_no_pair_tile():
+    w = torch.zeros((256, 1024), dtype=torch.int8, device="cuda")
+    x = torch.zeros((256, 1024), dtype=torch.int8, device="cuda")
+    acc = torch.empty((256, 256), dtype=torch.int32, device="cuda")
+    with pytest.raises(gcu.GcuError, match="CTA-pair"):
+        gcu.dev_gemm_int8_raw_tuned(acc, w, x, 256, 256, 1024, 256, 1, 4)
 
 
 def _ffn_weights(gen, dim, ffn):
