@@ -177,7 +177,7 @@ class Prefill:
     exchange row maxima and int32 partial sums, bit-exact; Q/K/V/O stay
     replicated."""
 
-    def __init__(self, name="prefill1b", seed=0, fused=False, world=1, rank=0, layers=0):
+    def __init__(self, name="prefill1b", seed=0, fused=False, world=1, rank=0, layers=0, chain=False):
         import synth
         self.name = name
         self.index, self.title, stacks, shard = PREFILL[name]
@@ -187,6 +187,8 @@ class Prefill:
         self.fused, self.world, self.rank = fused, world, rank
         self.shard = shard and world > 1
         self.ffn_block = name == "prefill12b"
+        self.chain = chain and not self.shard and not self.ffn_block
+        self._chain = None
         self.needs_comm = self.shard
         self.m = self.stacks[-1][2]
         self.layers = sum(st[3] for st in self.stacks)
@@ -205,9 +207,14 @@ class Prefill:
              "inputs": "1% outlier channels x20; per-layer weights+activations exceed L2 (no flush)"}
         if self.name == "prefill1b":
             c.update(tokens_m=self.m, layers=self.layers, d_model=self.groups[0][0], ffn=self.groups[3][0])
+        if self.chain:
+            c["calls_per_layer"] = "every quantize_acts -> GEMM pair of the step in chain launches (<= 22 pairs each)"
+        if self.ffn_block:
+            c["calls_per_layer"] = ("quantize_acts + one GEMM launch for Q/K/V and O; the FFN as one block "
+                                    "(gcu_dev_ffn_rowshard)")
         if self.shard:
-            c["sharding"] = (f"FFN rows over {self.world} GPUs, outputs all-gathered; "
-                             "Q/K/V/O replicated (counted once in value)")
+            c["sharding"] = (f"FFN hidden dimension over {self.world} GPUs (row maxima and int32 partial "
+                             "sums all-reduced); Q/K/V/O replicated (counted once in value)")
         return c
 
     def build(self, device):
@@ -274,6 +281,8 @@ class Prefill:
 
     @property
     def kinds(self):
+        if self.chain:
+            return ("chain",)
         if self.ffn_block:
             return ("quant", "gemm", "ffn")
         if self.shard:
@@ -283,6 +292,26 @@ class Prefill:
     def step(self, gcu, stream=None, want=None):
         """Enqueue one step.  `want(kind, bytes, ops)` filters the launches
         (and accounts their algorithmic work) for per-kernel timing."""
+        if self.chain:
+            # every quantize_acts -> GEMM pair of the step through the chain launch
+            # (gcu_gemm_chain_*): built on the first (eager) step, outside any capture
+            if self._chain is None:
+                steps = []
+                for si, (_, _, m, _) in enumerate(self.stacks):
+                    for layer in self.L[si]:
+                        for gi, g in enumerate(layer):
+                            steps.append([g["x"], g["q"], g["s"],
+                                          [(w, sc, o) for (w, sc), o in zip(g["w"], self.out[si][gi])]])
+                self._chain = gcu.GemmChain(steps)
+            nb = ops = 0
+            for si, (_, groups, m, nl) in enumerate(self.stacks):
+                for k, jobs in groups:
+                    ns = sum(n for _, n in jobs)
+                    nb += nl * (5 * m * k + 4 * m + ns * k + 4 * ns + m * k + 4 * m + 4 * m * ns)
+                    ops += nl * 2 * m * ns * k
+            if want is None or want("chain", nb, ops):
+                self._chain.run(stream)
+            return
         for si, (_, _, m, _) in enumerate(self.stacks):
             for layer in self.L[si]:
                 for gi, g in enumerate(layer):
@@ -330,6 +359,9 @@ class Prefill:
 
     @property
     def launches_per_step(self):
+        if self.chain:
+            npairs = sum(nl * len(groups) for _, groups, _, nl in self.stacks)
+            return -(-npairs // 22)
         n = 0
         for si, (_, groups, _, nl) in enumerate(self.stacks):
             for k, jobs in groups:
@@ -663,7 +695,8 @@ class LmHead:
 # ---------------------------------------------------------------------------
 def make_workload(name, args, world, rank, batch=1):
     if name in PREFILL:
-        return Prefill(name, seed=rank, fused=args.fused, world=world, rank=rank, layers=args.layers)
+        return Prefill(name, seed=rank, fused=args.fused, world=world, rank=rank, layers=args.layers,
+                       chain=getattr(args, "chain", False))
     if name in DECODE:
         return Decode(name, seed=rank, fused=not args.unfused, world=world, rank=rank, layers=args.layers)
     return LmHead(world, rank, batch=batch)
@@ -1739,6 +1772,9 @@ def main():
                     choices=list(PREFILL) + list(DECODE) + ["lmhead4b"] + list(UPLOAD) + list(ATTN) +
                     ["siglip_head"] + list(DECODE_STEP))
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--chain", action="store_true",
+                    help="prefill workloads: the step's quantize_acts -> GEMM pairs as chain launches "
+                         "(gcu_gemm_chain_*, at most 22 pairs per launch)")
     ap.add_argument("--unfused", action="store_true",
                     help="decode: quantize and GEMV as separate launches (the reference's call split)")
     ap.add_argument("--fused", action="store_true",

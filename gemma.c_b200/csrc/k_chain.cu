@@ -92,12 +92,19 @@ constexpr int kParamPairs = 22;
 struct alignas(64) ChainParams {
   PairDesc pd[kParamPairs];
   int npairs;             // <= kParamPairs
-  int *sync;       // [2i] CTAs done quantizing pair i, [2i+1] done with its GEMM, [2n] exits
+  int *sync;       // counters kSyncStride ints apart: [2i] CTAs done quantizing pair i,
+                   // [2i+1] done with its GEMM, [2n] exits
+  int *abort;      // nonzero once a wait of this launch has given up (device memory)
   int32_t *ws;     // split-K partials (pairs run one after another and share it)
   int *counters;   // split-K tile counters (zero between launches)
   unsigned int *err;
 };
 static_assert(sizeof(ChainParams) <= 32764, "kernel parameter limit");
+
+// Each hand-off counter sits in its own 128-byte line: the CTAs that count in
+// and the threads that poll one counter then do not queue behind another's.
+constexpr int kSyncStride = 32;
+__device__ __forceinline__ int *slot(const ChainParams &p, int i) { return p.sync + i * kSyncStride; }
 
 // A pair's geometry, copied to registers at the start of each pair.
 struct Geo {
@@ -138,27 +145,34 @@ __device__ __forceinline__ float dequant(int acc, float xs, float ws) {
   return __fmul_rn(__int2float_rn(acc), __fmul_rn(xs, ws));
 }
 
-__device__ __forceinline__ bool err_set(const unsigned int *err) {
-  return *reinterpret_cast<const volatile unsigned int *>(err) != 0u;
-}
+// Where a wait that gives up reports: the library's error word (which may be
+// mapped host memory, so it is written once and never polled) and the
+// launch's abort word in device memory, which the other waits poll.
+struct Fail {
+  unsigned int *err;
+  int *abort;
+};
 
 // Waits are timed on the SM's cycle counter: reading %globaltimer costs
 // about 0.1 us on B200, and a waiter that reads it between polls notices a
 // landed stage that much later, on every stage.  A wait gives up after
 // kBudgetCycles (2 s at 2 GHz, longer at lower clocks), or -- once it has
-// waited kErrPollCycles, longer than any hand-off of a healthy launch at these
-// sizes takes -- as soon as another wait has recorded an error.  The error
+// waited kErrPollCycles -- as soon as another wait has given up.  The abort
 // word is only read after that point: a load from global memory stalls the
-// waiting thread for about a microsecond.
+// waiting thread for about a microsecond.  (Polling the error word itself
+// was measured to stall whole launches: in mapped host memory each poll is a
+// PCIe read, and hundreds of waiters flood the link.)
 constexpr long long kBudgetCycles = 4000000000ll;
 constexpr long long kErrPollCycles = 40000ll;
 
-__device__ __forceinline__ bool give_up(long long t0, unsigned int *err, unsigned int code) {
+__device__ __forceinline__ bool give_up(long long t0, Fail f, unsigned int code) {
   const long long dt = clock64() - t0;
   if (dt < kErrPollCycles) return false;
-  if (err_set(err)) return true;
+  if (*reinterpret_cast<volatile int *>(f.abort) != 0) return true;
   if (dt > kBudgetCycles) {
-    ptx::record_err(err, code);
+    ptx::record_err(f.err, code);
+    *reinterpret_cast<volatile int *>(f.abort) = 1;
+    __threadfence();
     return true;
   }
   return false;
@@ -172,13 +186,15 @@ __device__ __forceinline__ int ld_relaxed_gpu(const int *p) {
 
 // Wait until *flag >= target, then acquire at gpu scope; bounded.  The spin
 // is relaxed loads with a short back-off; one acquire load at the end.
-__device__ __forceinline__ bool chain_wait(const int *flag, int target, unsigned int *err,
+__device__ __forceinline__ bool chain_wait(const int *flag, int target, Fail err,
                                            unsigned int code = DEV_TIMEOUT_CHAIN) {
   if (ld_relaxed_gpu(flag) < target) {
     const long long t0 = clock64();
     int n = 0;
+    int nap = 32;
     while (ld_relaxed_gpu(flag) < target) {
-      __nanosleep(64);
+      __nanosleep(nap);
+      if (nap < 256) nap += 16;  // long waits poll the shared line less often
       if ((++n & 15) == 0 && give_up(t0, err, code)) return false;
     }
   }
@@ -189,7 +205,7 @@ __device__ __forceinline__ bool chain_wait(const int *flag, int target, unsigned
 // mbarrier wait, bounded.  `nap` > 0: sleep that many ns between polls, for
 // the 256 epilogue threads, whose spinning would otherwise take issue slots
 // from the producer and MMA threads on the same SM sub-partitions.
-__device__ __forceinline__ bool bar_wait(uint64_t *bar, uint32_t parity, unsigned int *err,
+__device__ __forceinline__ bool bar_wait(uint64_t *bar, uint32_t parity, Fail err,
                                          unsigned int code, int nap = 0) {
   if (ptx::mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
@@ -427,6 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int G = gridDim.x;
+  const Fail fail{p.err, p.abort};
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kNB; ++s) {
@@ -475,7 +492,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
         bool dep = false;   // codes of pair pi published by every CTA
         int pend_lo = it;   // stages [pend_lo, it) wait for their A tile while !dep
         auto publish_wait = [&]() -> bool {
-          if (!chain_wait(p.sync + 2 * pi, G, p.err)) return false;
+          if (!chain_wait(slot(p, 2 * pi), G, fail)) return false;
           fence_proxy_async_global();  // generic-proxy codes before async-proxy reads
           for (int j = pend_lo; j < it; ++j) {
             const int sl = j % kNB;
@@ -507,7 +524,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
                 }
                 dep = true;
               }
-              if (!bar_wait(&empty[lo % kNB], (lo / kNB) & 1, p.err, DEV_TIMEOUT_EMPTY)) {
+              if (!bar_wait(&empty[lo % kNB], (lo / kNB) & 1, fail, DEV_TIMEOUT_EMPTY)) {
                 ok = false;
                 break;
               }
@@ -586,8 +603,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
           int slot;
           if (wide) {  // the tile needs both 256-column slots
             slot = 0;
-            if (!bar_wait(&tempty[0], (uses[0] & 1) ^ 1, p.err, DEV_TIMEOUT_TMEM) ||
-                !bar_wait(&tempty[1], (uses[1] & 1) ^ 1, p.err, DEV_TIMEOUT_TMEM)) {
+            if (!bar_wait(&tempty[0], (uses[0] & 1) ^ 1, fail, DEV_TIMEOUT_TMEM) ||
+                !bar_wait(&tempty[1], (uses[1] & 1) ^ 1, fail, DEV_TIMEOUT_TMEM)) {
               ok = false;
               break;
             }
@@ -596,7 +613,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
           } else {
             slot = nxt;
             nxt ^= 1;
-            if (!bar_wait(&tempty[slot], (uses[slot] & 1) ^ 1, p.err, DEV_TIMEOUT_TMEM)) {
+            if (!bar_wait(&tempty[slot], (uses[slot] & 1) ^ 1, fail, DEV_TIMEOUT_TMEM)) {
               ok = false;
               break;
             }
@@ -607,7 +624,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
           for (int i = 0; i < nk; ++i, ++it) {
             const uint32_t off = ring_place(head, S);
             const int sl = it % kNB;
-            if (!bar_wait(&full[sl], (it / kNB) & 1, p.err, DEV_TIMEOUT_FULL)) {
+            if (!bar_wait(&full[sl], (it / kNB) & 1, fail, DEV_TIMEOUT_FULL)) {
               ok = false;
               break;
             }
@@ -643,7 +660,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
       g.load(D);
       // 1. the previous pair's outputs are complete on every CTA
       if (pi > 0) {
-        if (et == 0) *s_last = chain_wait(p.sync + 2 * pi - 1, G, p.err) ? 1 : 0;
+        if (et == 0) *s_last = chain_wait(slot(p, 2 * pi - 1), G, fail) ? 1 : 0;
         ptx::named_bar_sync(1, kEpiThreads);
         if (!*s_last) {
           ok = false;
@@ -656,11 +673,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
       // 0's release at gpu scope (cumulative); the readers acquire, then
       // fence the async proxy before their TMA loads of the codes
       ptx::named_bar_sync(1, kEpiThreads);
-      if (et == 0) red_release_add(p.sync + 2 * pi, 1);
+      if (et == 0) red_release_add(slot(p, 2 * pi), 1);
       // the epilogue reads activation scales that other CTAs wrote: observe
       // their publication (long complete by the time a tile is ready)
       if ((int)blockIdx.x < g.units) {
-        if (et == 0) *s_last = chain_wait(p.sync + 2 * pi, G, p.err) ? 1 : 0;
+        if (et == 0) *s_last = chain_wait(slot(p, 2 * pi), G, fail) ? 1 : 0;
         ptx::named_bar_sync(1, kEpiThreads);
         if (!*s_last) {
           ok = false;
@@ -703,7 +720,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
         // chunk ahead)
         const float xs = row < g.m ? __ldcg(D.s + row) : 0.0f;
         float ws_cur = ws_of(ch0);
-        if (!bar_wait(&tfull[slot], fills[slot] & 1, p.err, DEV_TIMEOUT_TMEM, 100)) {
+        if (!bar_wait(&tfull[slot], fills[slot] & 1, fail, DEV_TIMEOUT_TMEM, 100)) {
           ok = false;
           break;
         }
@@ -753,7 +770,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
           // each split reduces its share of the tile's 32x32 blocks
           if (et == 0) {
             atomicAdd(p.counters + w.tile, 1);
-            *s_last = chain_wait(p.counters + w.tile, g.splits, p.err, DEV_TIMEOUT_SPLIT) ? 1 : 0;
+            *s_last = chain_wait(p.counters + w.tile, g.splits, fail, DEV_TIMEOUT_SPLIT) ? 1 : 0;
           }
           ptx::named_bar_sync(1, kEpiThreads);
           if (!*s_last) {
@@ -813,7 +830,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
       }
       __syncwarp();
       ptx::named_bar_sync(1, kEpiThreads);
-      if (et == 0) red_release_add(p.sync + 2 * pi + 1, 1);
+      if (et == 0) red_release_add(slot(p, 2 * pi + 1), 1);
     }
     if (lane == 0) ptx::bulk_wait<0>();
     __syncwarp();
@@ -829,9 +846,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(const __grid_constant__ C
   // CTA has finished all of its waits before it counts itself out)
   if (threadIdx.x == 0) {
     __threadfence();
-    int *exits = p.sync + 2 * p.npairs;
+    int *exits = slot(p, 2 * p.npairs);
     if (atomicAdd(exits, 1) == G - 1) {
-      for (int i = 0; i < 2 * p.npairs; ++i) p.sync[i] = 0;
+      for (int i = 0; i < 2 * p.npairs; ++i) *slot(p, i) = 0;
+      *p.abort = 0;
       __threadfence();
       *exits = 0;
     }
@@ -995,7 +1013,8 @@ GCU_EXPORT int gcu_gemm_chain_create(const gcu_qgemm_step *steps, int nsteps, co
     c.plan.push_back(h[i].splits);
   }
   c.h = h;
-  const int nsync = 2 * (nsteps < kParamPairs ? nsteps : kParamPairs) + 1;
+  // [2 per step of a launch][exits], kSyncStride ints apart; then the abort word
+  const int nsync = (2 * kParamPairs + 1) * kSyncStride + 1;
   cudaError_t e = cudaMalloc(&c.d_sync, sizeof(int) * nsync);
   if (e == cudaSuccess && ws_need) e = cudaMalloc(&c.d_ws, ws_need);
   if (e == cudaSuccess && cnt_need) e = cudaMalloc(&c.d_cnt, sizeof(int) * cnt_need);
@@ -1045,6 +1064,7 @@ GCU_EXPORT int gcu_gemm_chain_run(int handle, void *stream) {
     p.ws = c.d_ws;
     p.counters = c.d_cnt;
     p.err = dev_error_word();
+    p.abort = c.d_sync + (2 * kParamPairs + 1) * kSyncStride;
     GCU_CUDA(cudaLaunchKernelEx(&cfg, k_chain, p));
   }
   GCU_CUDA(cudaGetLastError());
