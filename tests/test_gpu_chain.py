@@ -120,7 +120,7 @@ def test_chain_prefill1b_layers():
 
 def test_chain_longer_than_one_launch():
     # 26 layers of the 1B prefill (104 steps): several launches of at most
-    # 24 steps each, sharing the hand-off counters
+    # 22 steps each, sharing the hand-off counters
     gen = torch.Generator(device="cuda").manual_seed(3)
     steps = [make_step(gen, 512, k, ns) for _ in range(7) for k, ns in LAYER_1B[:2]]
     steps += [make_step(gen, 256, k, ns) for _ in range(6) for k, ns in LAYER_1B[2:]]
