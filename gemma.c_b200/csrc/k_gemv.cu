@@ -84,6 +84,38 @@ __device__ __forceinline__ void job_of(const GemvJobs &jobs, int row, int &j, in
   local = row - (j > 0 ? jobs.row_end[j - 1] : 0);
 }
 
+// One lane's share of a row group: the R weight rows from `row0`, their
+// scales, and the first U chunks of each row (lane `sub` of LPR takes chunks
+// sub, sub + LPR, ...).  Rows past the end read the last row and are not
+// written.
+template <int R, int U, int LPR>
+__device__ __forceinline__ void load_chunks(const int8_t *const (&wp)[R], const bool (&valid)[R], int c0,
+                                            int C, int4 (&wv)[U][R]) {
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int c = c0 + u * LPR;
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+      wv[u][r] = (c < C && valid[r]) ? ptx::ld_stream_v4(wp[r] + (size_t)c * 16) : make_int4(0, 0, 0, 0);
+  }
+}
+
+template <int R, int U, int LPR>
+__device__ __forceinline__ void load_rows(const GemvJobs &jobs, int row0, int sub, int k, int C,
+                                          int total_rows, const int8_t *(&wp)[R], bool (&valid)[R],
+                                          float (&wsc)[R], int4 (&wv)[U][R]) {
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int row = row0 + r;
+    valid[r] = row < total_rows;
+    int j, local;
+    job_of(jobs, valid[r] ? row : total_rows - 1, j, local);
+    wp[r] = jobs.w[j] + (size_t)local * k;
+    wsc[r] = __ldg(jobs.ws[j] + local);
+  }
+  load_chunks<R, U, LPR>(wp, valid, sub, C, wv);
+}
+
 // Activation source of the GEMV: already-quantized int8 rows with their
 // scales, or (fused) fp32 rows that every CTA quantizes itself while staging
 // them -- gemma.c's quantize_act + gemv_int8 pair in one launch.  CTA 0 also
@@ -135,6 +167,10 @@ __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, cons
       ptx::bulk_prefetch_l2(jobs.w[j] + (size_t)local * k, (uint32_t)k);
     }
   }
+  // and the fp32 activation rows (the previous kernel may still be writing
+  // them; a prefetch only moves lines into L2, where those writes land)
+  if (FQ && blockIdx.x == 0 && threadIdx.x < mb)
+    ptx::bulk_prefetch_l2(X.xf + (size_t)threadIdx.x * X.xstride, (uint32_t)k * 4u);
   ptx::griddep_wait();
   // fused all-gather: this launch's epoch picks the symmetric buffer half
   int epoch0 = 0;
@@ -143,6 +179,17 @@ __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, cons
     epoch0 = *reinterpret_cast<volatile int *>(po.flag_local + 1);
     half_off = (epoch0 & 1) ? po.half_elems : 0;
   }
+  // The first row group's weight chunks and scales do not depend on the
+  // activation: they are requested before it is staged or quantized, so
+  // their latency overlaps that work.
+  const int slot = lane / LPR, sub = lane % LPR;
+  const int nwarps = gridDim.x * (kThreads / 32);
+  const int base0 = (blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5)) * kRowsPerWarp;
+  const int8_t *wp[R];
+  bool valid[R];
+  float wsc[R];
+  int4 wv[U][R];
+  if (base0 < total_rows) load_rows<R, U, LPR>(jobs, base0 + slot * R, sub, k, C, total_rows, wp, valid, wsc, wv);
   float xsc[MB];
   if (FQ) {
     for (int b = 0; b < MB; ++b) {
@@ -217,20 +264,8 @@ __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, cons
   if (threadIdx.x < MB) s_xsc[threadIdx.x] = xsc[threadIdx.x];
   __syncthreads();
 
-  const int slot = lane / LPR, sub = lane % LPR;
-  const int nwarps = gridDim.x * (kThreads / 32);
-  for (int base = (blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5)) * kRowsPerWarp;
-       base < total_rows; base += nwarps * kRowsPerWarp) {
-    const int8_t *wp[R];
-    bool valid[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int row = base + slot * R + r;
-      valid[r] = row < total_rows;
-      int j, local;
-      job_of(jobs, valid[r] ? row : total_rows - 1, j, local);
-      wp[r] = jobs.w[j] + (size_t)local * k;
-    }
+  for (int base = base0; base < total_rows; base += nwarps * kRowsPerWarp) {
+    if (base != base0) load_rows<R, U, LPR>(jobs, base + slot * R, sub, k, C, total_rows, wp, valid, wsc, wv);
     int acc[R][MB];
 #pragma unroll
     for (int r = 0; r < R; ++r)
@@ -238,15 +273,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, cons
       for (int b = 0; b < MB; ++b) acc[r][b] = 0;
 
     for (int c0 = sub; c0 < C; c0 += LPR * U) {
-      int4 wv[U][R];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int c = c0 + u * LPR;
-#pragma unroll
-        for (int r = 0; r < R; ++r)
-          wv[u][r] = (c < C && valid[r]) ? ptx::ld_stream_v4(wp[r] + (size_t)c * 16)
-                                         : make_int4(0, 0, 0, 0);
-      }
+      if (c0 != sub) load_chunks<R, U, LPR>(wp, valid, c0, C, wv);
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int c = c0 + u * LPR;
@@ -277,7 +304,11 @@ __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, cons
         if (row < total_rows && b < mb) {
           int j, local;
           job_of(jobs, row, j, local);
-          const float val = dequant(v[t], s_xsc[b], jobs.ws[j][local]);
+          float ws = wsc[0];
+#pragma unroll
+          for (int rr = 1; rr < R; ++rr)
+            if (r == rr) ws = wsc[rr];
+          const float val = dequant(v[t], s_xsc[b], ws);
           if (P2P) {
             // this rank's slice of job j in the current half
             po.sym[half_off + po.off[j] + (size_t)b * po.n[j] + (size_t)po.rank * po.n_local[j] + local] = val;
