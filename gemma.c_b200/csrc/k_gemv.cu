@@ -393,11 +393,10 @@ __global__ void __launch_bounds__(kThreads) k_gemv_any(const GemvJobs jobs,
   }
 }
 
-template <int MB, int LPR, bool FQ, bool P2P = false>
+template <int MB, int LPR, bool FQ, bool P2P = false, int U = (MB >= 4) ? 2 : 4>
 int launch_v16(const GemvJobs &jobs, const GemvX &X, int mb, long ystride, int k, int total_rows,
                cudaStream_t st, const PeerOut *po = nullptr) {
   constexpr int R = 2;
-  constexpr int U = (MB >= 4) ? 2 : 4;
   auto kern = k_gemv_v16<MB, LPR, R, U, FQ, P2P>;
   PeerOut pz{};
   const PeerOut &pout = po ? *po : pz;
@@ -435,8 +434,18 @@ int launch_mb(const GemvJobs &jobs, const GemvX &X, int mb, long ystride, int k,
   const int C = k / 16;
   // many activation rows: narrower lane groups keep the reduction short
   if (MB >= 8) return launch_v16<MB, 8, FQ, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
-  if (C >= 128 && MB <= 2)
-    return launch_v16<MB, 32, FQ, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
+  if (MB <= 2) {
+    // One or two rows (decode): a weight set that fits the L2 prefetch is
+    // read from L2 after the dependency wait, where each round of loads a
+    // lane waits for costs a round trip.  As many lanes per row as make one
+    // round of U chunks cover the row (the first round is requested before
+    // the activation is quantized), and rounds of 8 chunks past 128 chunks.
+    if (C > 128 && (long)total_rows * k <= kPrefetchMaxBytes)
+      return launch_v16<MB, 32, FQ, P2P, 8>(jobs, X, mb, ystride, k, total_rows, st, po);
+    if (C > 64) return launch_v16<MB, 32, FQ, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
+    if (C > 32) return launch_v16<MB, 16, FQ, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
+    return launch_v16<MB, 8, FQ, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
+  }
   if (C >= 64) return launch_v16<MB, 16, FQ, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
   return launch_v16<MB, 8, FQ, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
 }
