@@ -129,6 +129,7 @@ struct GemvX {
   float *sout;       // fused: scales out [mb] (may be null)
 };
 
+// Block-wide max; `red` (one slot per warp) is not reused by the caller.
 __device__ __forceinline__ float block_max256(float v, float *red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -137,7 +138,6 @@ __device__ __forceinline__ float block_max256(float v, float *red) {
   float r = red[0];
 #pragma unroll
   for (int w = 1; w < kThreads / 32; ++w) r = fmaxf(r, red[w]);
-  __syncthreads();
   return r;
 }
 
@@ -147,8 +147,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, cons
                                                        long ystride, int k, int total_rows,
                                                        const PeerOut po) {
   extern __shared__ int4 xsm[];  // [MB][C] 16-byte chunks of x
-  __shared__ float red[kThreads / 32];
-  __shared__ float s_scale[MB];
+  __shared__ float red[MB][kThreads / 32];  // per activation row: no reuse, no second barrier
   __shared__ float s_xsc[MB];  // activation scales, indexed by reduced-sum slot
   __shared__ int s_peers_ok;
   const int C = k >> 4;
@@ -190,11 +189,13 @@ __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, cons
   float wsc[R];
   int4 wv[U][R];
   if (base0 < total_rows) load_rows<R, U, LPR>(jobs, base0 + slot * R, sub, k, C, total_rows, wp, valid, wsc, wv);
-  float xsc[MB];
+  // One barrier publishes the staged codes and the scales (every thread
+  // derives the scale from the same block max).
   if (FQ) {
     for (int b = 0; b < MB; ++b) {
       if (b >= mb) {  // uniform: padding rows are zero
         for (int i = threadIdx.x; i < C; i += kThreads) xsm[b * C + i] = make_int4(0, 0, 0, 0);
+        if (threadIdx.x == 0) s_xsc[b] = 0.0f;
         continue;
       }
       const float4 *xr = reinterpret_cast<const float4 *>(X.xf + (size_t)b * X.xstride);
@@ -212,7 +213,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, cons
             amax = ptx::absmax4(xv[i], amax);
           }
         }
-        amax = block_max256(amax, red);
+        amax = block_max256(amax, red[b]);
         ptx::quant_scale(amax, scale, inv);
         // float4 idx -> 32-bit word idx of the row's codes (word 4c + j of
         // 16-byte chunk c holds elements 16c + 4j .. 16c + 4j + 3)
@@ -229,7 +230,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, cons
         }
       } else {
         for (int i = threadIdx.x; i < 4 * C; i += kThreads) amax = ptx::absmax4(__ldg(xr + i), amax);
-        amax = block_max256(amax, red);
+        amax = block_max256(amax, red[b]);
         ptx::quant_scale(amax, scale, inv);
         for (int i = threadIdx.x; i < C; i += kThreads) {
           int4 v;
@@ -243,13 +244,10 @@ __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, cons
         }
       }
       if (threadIdx.x == 0) {
-        s_scale[b] = scale;
+        s_xsc[b] = scale;
         if (blockIdx.x == 0 && X.sout) X.sout[b] = scale;
       }
     }
-    __syncthreads();
-#pragma unroll
-    for (int b = 0; b < MB; ++b) xsc[b] = b < mb ? s_scale[b] : 0.0f;
   } else {
     for (int i = threadIdx.x; i < MB * C; i += kThreads) {
       const int b = i / C, c = i - b * C;
@@ -257,11 +255,8 @@ __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, cons
       if (b < mb) v = *reinterpret_cast<const int4 *>(X.x + (size_t)b * X.xstride + (size_t)c * 16);
       xsm[i] = v;
     }
-#pragma unroll
-    for (int b = 0; b < MB; ++b) xsc[b] = b < mb ? X.xs[b] : 0.0f;
-    __syncthreads();
+    if (threadIdx.x < MB) s_xsc[threadIdx.x] = threadIdx.x < mb ? X.xs[threadIdx.x] : 0.0f;
   }
-  if (threadIdx.x < MB) s_xsc[threadIdx.x] = xsc[threadIdx.x];
   __syncthreads();
 
   for (int base = base0; base < total_rows; base += nwarps * kRowsPerWarp) {
