@@ -982,6 +982,39 @@ GCU_EXPORT int gcu_dev_quantize_gemm_int8_multi(const gcu_gemv_job *jobs, int nj
   return launch_gemm_tc_jobs(q, k, s, m, k, a, njobs, st, 0, 0);
 }
 
+static int gemv_jobs_of(const gcu_gemv_job *jobs, int njobs, GemvJobs &J, const char *what) {
+  if (!jobs || njobs <= 0 || njobs > GCU_MAX_JOBS) return set_error("%s: 1..%d jobs", what, GCU_MAX_JOBS);
+  J = GemvJobs{};
+  int rows = 0;
+  for (int j = 0; j < njobs; ++j) {
+    if (!jobs[j].w || !jobs[j].sc || !jobs[j].dst || jobs[j].m <= 0)
+      return set_error("%s: job %d has a null pointer or no rows", what, j);
+    J.w[j] = (const int8_t *)jobs[j].w;
+    J.ws[j] = jobs[j].sc;
+    J.y[j] = jobs[j].dst;
+    rows += jobs[j].m;
+    J.row_end[j] = rows;
+  }
+  J.njobs = njobs;
+  return 0;
+}
+
+GCU_EXPORT int gcu_dev_geglu_quantize_gemv_multi(const gcu_gemv_job *jobs, int njobs, int8_t *q, float *s,
+                                                 const float *gate, const float *up, int k, void *stream) {
+  GemvJobs J;
+  if (gemv_jobs_of(jobs, njobs, J, "geglu_quantize_gemv")) return 1;
+  return launch_geglu_gemv(J, gate, up, q, s, k, as_stream(stream));
+}
+
+GCU_EXPORT int gcu_dev_residual_norm_quantize_gemv_multi(const gcu_gemv_job *jobs, int njobs, float *x, int8_t *q,
+                                                         float *s, const float *y, const float *resid,
+                                                         const float *w_post, const float *w_next, float eps,
+                                                         int dim, void *stream) {
+  GemvJobs J;
+  if (gemv_jobs_of(jobs, njobs, J, "residual_norm_quantize_gemv")) return 1;
+  return launch_resnorm_gemv(J, y, resid, w_post, w_next, eps, x, q, s, dim, as_stream(stream));
+}
+
 // Tuning hook (not in gcu.h): the multi-job GEMM with a forced tile shape
 // ((128*mb) x bn) and K split.  Used by the benchmark's sweeps.
 GCU_EXPORT int gcu_dev_gemm_int8_multi_tuned(const gcu_gemv_job *jobs, int njobs, const int8_t *src,

@@ -153,6 +153,15 @@ int launch_quantize_gemv(const GemvJobs &jobs, const float *xf, long xfstride,
                          int8_t *qout, float *sout, int mb, long ystride, int k,
                          cudaStream_t st);
 
+// A producer row + GEMV in one launch (one token): h = gelu(gate) * up, or
+// x = clamp(resid + rmsnorm(y, w_post)) then rmsnorm(x, w_next), quantized
+// and multiplied; codes, scale and (residual form) x are written out.
+int launch_geglu_gemv(const GemvJobs &jobs, const float *gate, const float *up, int8_t *qout, float *sout,
+                      int k, cudaStream_t st);
+int launch_resnorm_gemv(const GemvJobs &jobs, const float *y, const float *resid, const float *w_post,
+                        const float *w_next, float eps, float *xout, int8_t *qout, float *sout, int dim,
+                        cudaStream_t st);
+
 struct GemmArgs {
   float *dst;
   long dstr;

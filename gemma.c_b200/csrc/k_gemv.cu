@@ -17,6 +17,7 @@
 // shuffles reduce.  CTAs are persistent-ish (grid = SMs x occupancy) and
 // stride over row groups.
 #include "gcu_internal.cuh"
+#include "producers.cuh"
 
 #include <mutex>
 
@@ -116,17 +117,31 @@ __device__ __forceinline__ void load_rows(const GemvJobs &jobs, int row0, int su
   load_chunks<R, U, LPR>(wp, valid, sub, C, wv);
 }
 
-// Activation source of the GEMV: already-quantized int8 rows with their
-// scales, or (fused) fp32 rows that every CTA quantizes itself while staging
-// them -- gemma.c's quantize_act + gemv_int8 pair in one launch.  CTA 0 also
-// writes the codes and scales out, as quantize_act would.
+// Activation source of the GEMV (the kernel's SRC):
+//   SRC_I8      already-quantized int8 rows with their scales;
+//   SRC_QUANT   fp32 rows that every CTA quantizes itself while staging them
+//               -- gemma.c's quantize_act + gemv_int8 pair in one launch;
+//   SRC_GEGLU   one row h = gelu(gate) * up, quantized (the down projection's
+//               input, gemma.c:4921-4927);
+//   SRC_RESNORM one row: x = clamp(resid + rmsnorm(y, w_post)), then
+//               rmsnorm(x, w_next), quantized (gemma.c:4862-4910 and
+//               4950-4962 + 4754-4768); CTA 0 writes x to xout, which must
+//               not alias resid (every CTA reads resid).
+// The producer arithmetic is producers.cuh's, shared with the standalone
+// producer kernels, so the codes are those of the two-launch sequence.  CTA 0
+// also writes the codes and scales out, as quantize_act would.
+enum { SRC_I8 = 0, SRC_QUANT = 1, SRC_GEGLU = 2, SRC_RESNORM = 3 };
 struct GemvX {
-  const int8_t *x;   // int8 rows (not fused)
+  const int8_t *x;   // int8 rows (SRC_I8)
   long xstride;      // elements between rows (int8 or fp32)
-  const float *xs;   // their scales (not fused)
-  const float *xf;   // fp32 rows (fused)
-  int8_t *qout;      // fused: codes out [mb][k] dense (may be null)
-  float *sout;       // fused: scales out [mb] (may be null)
+  const float *xs;   // their scales (SRC_I8)
+  const float *xf;   // fp32 rows (SRC_QUANT), the gate (SRC_GEGLU), y (SRC_RESNORM)
+  int8_t *qout;      // codes out [mb][k] dense (may be null)
+  float *sout;       // scales out [mb] (may be null)
+  const float *xb;   // up (SRC_GEGLU), resid (SRC_RESNORM)
+  const float *w_post, *w_next;  // SRC_RESNORM norm weights (w_post may be null)
+  float *xout;       // SRC_RESNORM: the updated residual row
+  float eps;
 };
 
 // Block-wide max; `red` (one slot per warp) is not reused by the caller.
@@ -142,10 +157,13 @@ __device__ __forceinline__ float block_max256(float v, float *red) {
 }
 
 // Vector kernel: k % 16 == 0, every weight row and x row 16-byte aligned.
-template <int MB, int LPR, int R, int U, bool FQ, bool P2P>
+// VPT: float4 per thread of the producer row (SRC_GEGLU, SRC_RESNORM).
+template <int MB, int LPR, int R, int U, int SRC, bool P2P, int VPT>
 __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, const GemvX X, int mb,
                                                        long ystride, int k, int total_rows,
                                                        const PeerOut po) {
+  constexpr bool FQ = SRC == SRC_QUANT;
+  static_assert(SRC < SRC_GEGLU || (MB == 1 && VPT > 0 && !P2P), "producer staging: one row");
   extern __shared__ int4 xsm[];  // [MB][C] 16-byte chunks of x
   __shared__ float red[MB][kThreads / 32];  // per activation row: no reuse, no second barrier
   __shared__ float s_xsc[MB];  // activation scales, indexed by reduced-sum slot
@@ -170,6 +188,10 @@ __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, cons
   // them; a prefetch only moves lines into L2, where those writes land)
   if (FQ && blockIdx.x == 0 && threadIdx.x < mb)
     ptx::bulk_prefetch_l2(X.xf + (size_t)threadIdx.x * X.xstride, (uint32_t)k * 4u);
+  if (SRC >= SRC_GEGLU && blockIdx.x == 0 && threadIdx.x < 4) {
+    const float *row = threadIdx.x == 0 ? X.xf : threadIdx.x == 1 ? X.xb : threadIdx.x == 2 ? X.w_post : X.w_next;
+    if (row && (SRC == SRC_RESNORM || threadIdx.x < 2)) ptx::bulk_prefetch_l2(row, (uint32_t)k * 4u);
+  }
   ptx::griddep_wait();
   // fused all-gather: this launch's epoch picks the symmetric buffer half
   int epoch0 = 0;
@@ -247,6 +269,43 @@ __global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, cons
         s_xsc[b] = scale;
         if (blockIdx.x == 0 && X.sout) X.sout[b] = scale;
       }
+    }
+  } else if constexpr (SRC >= SRC_GEGLU) {
+    // the producer row (thread t holds float4 columns t, t + 256, ...), then
+    // its codes in the same layout as above
+    float4 v[VPT];
+    float amax = 0.0f;
+    if constexpr (SRC == SRC_GEGLU) {
+      const float4 *g4 = reinterpret_cast<const float4 *>(X.xf);
+      const float4 *u4 = reinterpret_cast<const float4 *>(X.xb);
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int idx = threadIdx.x + i * kThreads;
+        if (idx < 4 * C) {
+          v[i] = prod::geglu4(__ldg(g4 + idx), __ldg(u4 + idx));
+          amax = ptx::absmax4(v[i], amax);
+        }
+      }
+      amax = block_max256(amax, red[0]);
+    } else {
+      amax = prod::residual_norm_row<VPT>(v, X.xf, X.xb, X.w_post, X.w_next, X.eps, k, red[0],
+                                          blockIdx.x == 0 ? X.xout : nullptr);
+    }
+    float scale, inv;
+    ptx::quant_scale(amax, scale, inv);
+    int *xw = reinterpret_cast<int *>(xsm);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int idx = threadIdx.x + i * kThreads;
+      if (idx < 4 * C) {
+        const int w = ptx::quant_pack4(v[i], inv);
+        xw[idx] = w;
+        if (blockIdx.x == 0 && X.qout) reinterpret_cast<int *>(X.qout)[idx] = w;
+      }
+    }
+    if (threadIdx.x == 0) {
+      s_xsc[0] = scale;
+      if (blockIdx.x == 0 && X.sout) X.sout[0] = scale;
     }
   } else {
     for (int i = threadIdx.x; i < MB * C; i += kThreads) {
@@ -388,11 +447,11 @@ __global__ void __launch_bounds__(kThreads) k_gemv_any(const GemvJobs jobs,
   }
 }
 
-template <int MB, int LPR, bool FQ, bool P2P = false, int U = (MB >= 4) ? 2 : 4>
+template <int MB, int LPR, int SRC, bool P2P = false, int U = (MB >= 4) ? 2 : 4, int VPT = 0>
 int launch_v16(const GemvJobs &jobs, const GemvX &X, int mb, long ystride, int k, int total_rows,
                cudaStream_t st, const PeerOut *po = nullptr) {
   constexpr int R = 2;
-  auto kern = k_gemv_v16<MB, LPR, R, U, FQ, P2P>;
+  auto kern = k_gemv_v16<MB, LPR, R, U, SRC, P2P, VPT>;
   PeerOut pz{};
   const PeerOut &pout = po ? *po : pz;
   const size_t smem = (size_t)MB * k;
@@ -423,12 +482,12 @@ int launch_v16(const GemvJobs &jobs, const GemvX &X, int mb, long ystride, int k
   return 0;
 }
 
-template <int MB, bool FQ, bool P2P = false>
+template <int MB, int SRC, bool P2P = false>
 int launch_mb(const GemvJobs &jobs, const GemvX &X, int mb, long ystride, int k, int total_rows,
               cudaStream_t st, const PeerOut *po = nullptr) {
   const int C = k / 16;
   // many activation rows: narrower lane groups keep the reduction short
-  if (MB >= 8) return launch_v16<MB, 8, FQ, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
+  if (MB >= 8) return launch_v16<MB, 8, SRC, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
   if (MB <= 2) {
     // One or two rows (decode): a weight set that fits the L2 prefetch is
     // read from L2 after the dependency wait, where each round of loads a
@@ -436,22 +495,34 @@ int launch_mb(const GemvJobs &jobs, const GemvX &X, int mb, long ystride, int k,
     // round of U chunks cover the row (the first round is requested before
     // the activation is quantized), and rounds of 8 chunks past 128 chunks.
     if (C > 128 && (long)total_rows * k <= kPrefetchMaxBytes)
-      return launch_v16<MB, 32, FQ, P2P, 8>(jobs, X, mb, ystride, k, total_rows, st, po);
-    if (C > 64) return launch_v16<MB, 32, FQ, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
-    if (C > 32) return launch_v16<MB, 16, FQ, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
-    return launch_v16<MB, 8, FQ, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
+      return launch_v16<MB, 32, SRC, P2P, 8>(jobs, X, mb, ystride, k, total_rows, st, po);
+    if (C > 64) return launch_v16<MB, 32, SRC, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
+    if (C > 32) return launch_v16<MB, 16, SRC, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
+    return launch_v16<MB, 8, SRC, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
   }
-  if (C >= 64) return launch_v16<MB, 16, FQ, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
-  return launch_v16<MB, 8, FQ, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
+  if (C >= 64) return launch_v16<MB, 16, SRC, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
+  return launch_v16<MB, 8, SRC, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
 }
 
-template <bool FQ>
+template <int SRC>
 int launch_vec(const GemvJobs &jobs, const GemvX &X, int mb, long ystride, int k, int total_rows,
                cudaStream_t st) {
-  if (mb == 1) return launch_mb<1, FQ>(jobs, X, mb, ystride, k, total_rows, st);
-  if (mb == 2) return launch_mb<2, FQ>(jobs, X, mb, ystride, k, total_rows, st);
-  if (mb <= 4) return launch_mb<4, FQ>(jobs, X, mb, ystride, k, total_rows, st);
-  return launch_mb<8, FQ>(jobs, X, mb, ystride, k, total_rows, st);
+  if (mb == 1) return launch_mb<1, SRC>(jobs, X, mb, ystride, k, total_rows, st);
+  if (mb == 2) return launch_mb<2, SRC>(jobs, X, mb, ystride, k, total_rows, st);
+  if (mb <= 4) return launch_mb<4, SRC>(jobs, X, mb, ystride, k, total_rows, st);
+  return launch_mb<8, SRC>(jobs, X, mb, ystride, k, total_rows, st);
+}
+
+// One producer row staged in front of the GEMV (SRC_GEGLU / SRC_RESNORM):
+// the lane split of launch_mb<1> for this k, VPT float4 of the row per thread.
+template <int SRC, int VPT>
+int launch_staged(const GemvJobs &jobs, const GemvX &X, int k, int total_rows, cudaStream_t st) {
+  const int C = k / 16;
+  if (C > 128 && (long)total_rows * k <= kPrefetchMaxBytes)
+    return launch_v16<1, 32, SRC, false, 8, VPT>(jobs, X, 1, 0, k, total_rows, st);
+  if (C > 64) return launch_v16<1, 32, SRC, false, 4, VPT>(jobs, X, 1, 0, k, total_rows, st);
+  if (C > 32) return launch_v16<1, 16, SRC, false, 4, VPT>(jobs, X, 1, 0, k, total_rows, st);
+  return launch_v16<1, 8, SRC, false, 4, VPT>(jobs, X, 1, 0, k, total_rows, st);
 }
 
 }  // namespace
@@ -469,7 +540,7 @@ int launch_gemv(const GemvJobs &jobs, const int8_t *x, long xstride, const float
   for (int j = 0; j < jobs.njobs && vec; ++j) vec = ((uintptr_t)jobs.w[j] % 16 == 0);
   if (vec) {
     GemvX X{x, xstride, xs, nullptr, nullptr, nullptr};
-    return launch_vec<false>(jobs, X, mb, ystride, k, total_rows, st);
+    return launch_vec<SRC_I8>(jobs, X, mb, ystride, k, total_rows, st);
   }
   long need = ((long)total_rows + 7) / 8;
   long cap = (long)num_sms() * 8;
@@ -496,16 +567,16 @@ int launch_gemv_p2p(const GemvJobs &jobs, const int8_t *x, long xstride, const f
   if (!vec) return set_error("gemv p2p: needs k %% 16 == 0, 16-byte aligned operands and outputs");
   if (xf) {
     GemvX X{nullptr, xstride, nullptr, xf, qout, sout};
-    if (mb == 1) return launch_mb<1, true, true>(jobs, X, mb, 0, k, total_rows, st, &po);
-    if (mb == 2) return launch_mb<2, true, true>(jobs, X, mb, 0, k, total_rows, st, &po);
-    if (mb <= 4) return launch_mb<4, true, true>(jobs, X, mb, 0, k, total_rows, st, &po);
-    return launch_mb<8, true, true>(jobs, X, mb, 0, k, total_rows, st, &po);
+    if (mb == 1) return launch_mb<1, SRC_QUANT, true>(jobs, X, mb, 0, k, total_rows, st, &po);
+    if (mb == 2) return launch_mb<2, SRC_QUANT, true>(jobs, X, mb, 0, k, total_rows, st, &po);
+    if (mb <= 4) return launch_mb<4, SRC_QUANT, true>(jobs, X, mb, 0, k, total_rows, st, &po);
+    return launch_mb<8, SRC_QUANT, true>(jobs, X, mb, 0, k, total_rows, st, &po);
   }
   GemvX X{x, xstride, xs, nullptr, nullptr, nullptr};
-  if (mb == 1) return launch_mb<1, false, true>(jobs, X, mb, 0, k, total_rows, st, &po);
-  if (mb == 2) return launch_mb<2, false, true>(jobs, X, mb, 0, k, total_rows, st, &po);
-  if (mb <= 4) return launch_mb<4, false, true>(jobs, X, mb, 0, k, total_rows, st, &po);
-  return launch_mb<8, false, true>(jobs, X, mb, 0, k, total_rows, st, &po);
+  if (mb == 1) return launch_mb<1, SRC_I8, true>(jobs, X, mb, 0, k, total_rows, st, &po);
+  if (mb == 2) return launch_mb<2, SRC_I8, true>(jobs, X, mb, 0, k, total_rows, st, &po);
+  if (mb <= 4) return launch_mb<4, SRC_I8, true>(jobs, X, mb, 0, k, total_rows, st, &po);
+  return launch_mb<8, SRC_I8, true>(jobs, X, mb, 0, k, total_rows, st, &po);
 }
 
 // Fused quantize_acts + GEMV: xf holds mb fp32 rows (row stride xfstride
@@ -526,7 +597,75 @@ int launch_quantize_gemv(const GemvJobs &jobs, const float *xf, long xfstride, i
   }
   if (total_rows <= 0) return launch_quantize_rows(qout, sout, xf, xfstride, mb, k, st);
   GemvX X{nullptr, xfstride, nullptr, xf, qout, sout};
-  return launch_vec<true>(jobs, X, mb, ystride, k, total_rows, st);
+  return launch_vec<SRC_QUANT>(jobs, X, mb, ystride, k, total_rows, st);
+}
+
+// Producer row + GEMV in one launch (decode, one token): the codes, scale and
+// (SRC_RESNORM) the updated residual row are also written out, as the
+// standalone producer kernels write them.
+int launch_geglu_gemv(const GemvJobs &jobs, const float *gate, const float *up, int8_t *qout, float *sout,
+                      int k, cudaStream_t st) {
+  if (jobs.njobs <= 0 || jobs.njobs > GCU_MAX_JOBS) return set_error("geglu_quantize_gemv: 1..%d jobs", GCU_MAX_JOBS);
+  const int total_rows = jobs.row_end[jobs.njobs - 1];
+  if (total_rows <= 0 || k <= 0 || k % 16 || k > 16384)
+    return set_error("geglu_quantize_gemv: k %d must be a positive multiple of 16 up to 16384", k);
+  if (!gate || !up || (uintptr_t)gate % 16 || (uintptr_t)up % 16 || (uintptr_t)qout % 16)
+    return set_error("geglu_quantize_gemv: gate, up and the codes must be 16-byte aligned");
+  for (int j = 0; j < jobs.njobs; ++j)
+    if ((uintptr_t)jobs.w[j] % 16) return set_error("geglu_quantize_gemv: weight rows must be 16-byte aligned");
+  GemvX X{};
+  X.xf = gate;
+  X.xb = up;
+  X.xstride = k;
+  X.qout = qout;
+  X.sout = sout;
+  const int vpt = (k / 4 + kThreads - 1) / kThreads;
+  if (vpt <= 2) return launch_staged<SRC_GEGLU, 2>(jobs, X, k, total_rows, st);
+  if (vpt <= 4) return launch_staged<SRC_GEGLU, 4>(jobs, X, k, total_rows, st);
+  if (vpt <= 8) return launch_staged<SRC_GEGLU, 8>(jobs, X, k, total_rows, st);
+  return launch_staged<SRC_GEGLU, 16>(jobs, X, k, total_rows, st);
+}
+
+int launch_resnorm_gemv(const GemvJobs &jobs, const float *y, const float *resid, const float *w_post,
+                        const float *w_next, float eps, float *xout, int8_t *qout, float *sout, int dim,
+                        cudaStream_t st) {
+  if (jobs.njobs <= 0 || jobs.njobs > GCU_MAX_JOBS)
+    return set_error("residual_norm_quantize_gemv: 1..%d jobs", GCU_MAX_JOBS);
+  const int total_rows = jobs.row_end[jobs.njobs - 1];
+  if (total_rows <= 0 || dim <= 0 || dim % 16 || dim > 4096)
+    return set_error("residual_norm_quantize_gemv: dim %d must be a positive multiple of 16 up to 4096", dim);
+  if (!y || !resid || !w_next || !xout)
+    return set_error("residual_norm_quantize_gemv: null pointer");
+  if ((uintptr_t)y % 16 || (uintptr_t)resid % 16 || (uintptr_t)w_next % 16 || (w_post && (uintptr_t)w_post % 16) ||
+      (uintptr_t)xout % 16 || (uintptr_t)qout % 16)
+    return set_error("residual_norm_quantize_gemv: rows must be 16-byte aligned");
+  // every CTA reads y and resid while CTA 0 writes x: x must be another buffer
+  const char *xo = reinterpret_cast<const char *>(xout);
+  const size_t bytes = (size_t)dim * sizeof(float);
+  auto overlaps = [&](const float *p) {
+    const char *c = reinterpret_cast<const char *>(p);
+    return xo < c + bytes && c < xo + bytes;
+  };
+  if (overlaps(resid) || overlaps(y))
+    return set_error("residual_norm_quantize_gemv: x must not overlap resid or y (every CTA reads them)");
+  for (int j = 0; j < jobs.njobs; ++j)
+    if ((uintptr_t)jobs.w[j] % 16)
+      return set_error("residual_norm_quantize_gemv: weight rows must be 16-byte aligned");
+  GemvX X{};
+  X.xf = y;
+  X.xb = resid;
+  X.w_post = w_post;
+  X.w_next = w_next;
+  X.eps = eps;
+  X.xout = xout;
+  X.xstride = dim;
+  X.qout = qout;
+  X.sout = sout;
+  const int nc = (dim / 4 + kThreads - 1) / kThreads;
+  if (nc == 1) return launch_staged<SRC_RESNORM, 1>(jobs, X, dim, total_rows, st);
+  if (nc == 2) return launch_staged<SRC_RESNORM, 2>(jobs, X, dim, total_rows, st);
+  if (nc == 3) return launch_staged<SRC_RESNORM, 3>(jobs, X, dim, total_rows, st);
+  return launch_staged<SRC_RESNORM, 4>(jobs, X, dim, total_rows, st);
 }
 
 }  // namespace gcu

@@ -22,6 +22,7 @@
 // one int8 write (plus the optional fp32 write).  Same work split as K1's
 // warp path: WPR warps per row, 8/WPR rows per 256-thread CTA.
 #include "gcu_internal.cuh"
+#include "producers.cuh"
 
 #include <algorithm>
 
@@ -36,28 +37,7 @@ namespace {
 // on (b = amax per row), so every rank forms the codes of the unsharded row.
 enum Producer { RMSNORM = 0, GEGLU = 1, GEGLU_AMAX = 2, QUANT_GIVEN = 3 };
 
-template <int WPR, bool MAX>
-__device__ __forceinline__ float row_reduce(float v, float *red, int warp, int grp, int lane) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float u = __shfl_xor_sync(0xffffffffu, v, o);
-    v = MAX ? fmaxf(v, u) : v + u;
-  }
-  if (WPR == 1) return v;
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  float r = red[grp * WPR];
-#pragma unroll
-  for (int w = 1; w < WPR; ++w) r = MAX ? fmaxf(r, red[grp * WPR + w]) : r + red[grp * WPR + w];
-  __syncthreads();  // red is written again by the next reduction
-  return r;
-}
-
-__device__ __forceinline__ float gelu_tanh(float x) {
-  const float c = 0.79788456080287f;  // sqrt(2 / pi)
-  const float t = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, x), x), x);
-  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(__fmul_rn(c, __fadd_rn(x, t)))));
-}
+using prod::row_reduce;
 
 // a: the row source (x, or the gate), b: the norm weight [n] (RMSNORM) or the
 // up rows (GEGLU, same stride as a); out: optional fp32 result rows [m][n].
@@ -86,8 +66,7 @@ __global__ void __launch_bounds__(256) k_producer_quant(int8_t *__restrict__ dst
         v[i] = __ldcs(ar + idx);
         if (P == GEGLU || P == GEGLU_AMAX) {
           const float4 u = __ldcs(br + idx);
-          v[i] = make_float4(__fmul_rn(gelu_tanh(v[i].x), u.x), __fmul_rn(gelu_tanh(v[i].y), u.y),
-                             __fmul_rn(gelu_tanh(v[i].z), u.z), __fmul_rn(gelu_tanh(v[i].w), u.w));
+          v[i] = prod::geglu4(v[i], u);
         }
       }
     }
@@ -338,52 +317,11 @@ __global__ void __launch_bounds__(256) k_residual_norm_quant(float *x, int8_t *_
   __shared__ float red[8];
   ptx::griddep_launch();
   const size_t row = blockIdx.x;
-  const int d4 = dim >> 2, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const float big = 3.402823466e38f;
+  const int d4 = dim >> 2;
   ptx::griddep_wait();
   float4 v[NC];
-  float sq = 0.0f;
-#pragma unroll
-  for (int i = 0; i < NC; ++i) {
-    const int c = threadIdx.x + i * 256;
-    v[i] = c < d4 ? __ldg(reinterpret_cast<const float4 *>(y + row * dim) + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-    sq += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
-  }
-  float rms = 1.0f;
-  if (w_post) {
-    sq = row_reduce<8, false>(sq, red, warp, 0, lane);
-    rms = 1.0f / sqrtf(sq / (float)dim + eps);
-  }
-  float sq2 = 0.0f;
-#pragma unroll
-  for (int i = 0; i < NC; ++i) {
-    const int c = threadIdx.x + i * 256;
-    if (c >= d4) continue;
-    float4 a = v[i];
-    if (w_post) {
-      const float4 g = __ldg(reinterpret_cast<const float4 *>(w_post) + c);
-      a = make_float4(a.x * rms * (g.x + 1.0f), a.y * rms * (g.y + 1.0f), a.z * rms * (g.z + 1.0f),
-                      a.w * rms * (g.w + 1.0f));
-    }
-    const float4 r = reinterpret_cast<const float4 *>(resid + row * dim)[c];
-    v[i] = make_float4(fminf(big, fmaxf(-big, a.x + r.x)), fminf(big, fmaxf(-big, a.y + r.y)),
-                       fminf(big, fmaxf(-big, a.z + r.z)), fminf(big, fmaxf(-big, a.w + r.w)));
-    reinterpret_cast<float4 *>(x + row * dim)[c] = v[i];
-    sq2 += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
-  }
-  sq2 = row_reduce<8, false>(sq2, red, warp, 0, lane);
-  const float rms2 = 1.0f / sqrtf(sq2 / (float)dim + eps);
-  float amax = 0.0f;
-#pragma unroll
-  for (int i = 0; i < NC; ++i) {
-    const int c = threadIdx.x + i * 256;
-    if (c >= d4) continue;
-    const float4 g = __ldg(reinterpret_cast<const float4 *>(w_next) + c);
-    v[i] = make_float4(v[i].x * rms2 * (g.x + 1.0f), v[i].y * rms2 * (g.y + 1.0f), v[i].z * rms2 * (g.z + 1.0f),
-                       v[i].w * rms2 * (g.w + 1.0f));
-    amax = ptx::absmax4(v[i], amax);
-  }
-  amax = row_reduce<8, true>(amax, red, warp, 0, lane);
+  const float amax = prod::residual_norm_row<NC>(v, y + row * dim, resid + row * dim, w_post, w_next, eps, dim, red,
+                                                 x + row * dim);
   float scale, inv;
   ptx::quant_scale(amax, scale, inv);
   int *qr = reinterpret_cast<int *>(q + row * dim);

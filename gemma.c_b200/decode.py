@@ -84,6 +84,7 @@ class Decoder:
         i8 = dict(dtype=torch.int8, device=device)
         self.kv = torch.zeros((c["nl"], 2, c["nkv"], clen, c["hdim"]), **f32)
         self.x = torch.empty((1, c["dim"]), **f32)
+        self.x2 = torch.empty((1, c["dim"]), **f32)  # the residual stream alternates between x and x2
         self.out = torch.empty((1, c["dim"]), **f32)
         self.xq = torch.empty((c["n_heads"], 1, c["hdim"]), **f32)
         self.xk = torch.empty((c["nkv"], 1, c["hdim"]), **f32)
@@ -116,12 +117,16 @@ class Decoder:
         q = self.q
         nl = len(self.L)
         # gemma.c:4750-4768: the first layer's rmsnorm(x, n1) -> quantize_act
-        # (every later layer's is fused into the previous layer's last residual)
+        # (every later layer's runs in front of its Q/K/V projection, in the
+        # launch that also adds the previous layer's FFN output to the residual)
         gcu.dev_rmsnorm_quantize(q, self.s, self.x, self.L[0]["n1"], eps, 1, dim, stream=stream)
+        # The residual stream alternates between x and x2: a launch whose CTAs
+        # all read the residual writes the updated one to the other buffer.
+        xa, xb = self.x, self.x2
+        qkv = lambda w: [(w["wq"][0], w["wq"][1], self.xq), (w["wk"][0], w["wk"][1], self.xk),
+                         (w["wv"][0], w["wv"][1], self.xv)]
+        gcu.dev_gemv_int8_multi(qkv(self.L[0]), q, self.s, dim, stream=stream)  # gemma.c:4769-4773
         for l, w in enumerate(self.L):
-            # gemma.c:4769-4773: q, k, v
-            gcu.dev_gemv_int8_multi([(w["wq"][0], w["wq"][1], self.xq), (w["wk"][0], w["wk"][1], self.xk),
-                                     (w["wv"][0], w["wv"][1], self.xv)], q, self.s, dim, stream=stream)
             # gemma.c:4775-4818: QK norm, RoPE, cache write
             kc, vc = self.kv[l, 0], self.kv[l, 1]
             sliding = bool(c["swa"][l])
@@ -132,27 +137,30 @@ class Decoder:
             spos = pos + 1 - c["slide"] if sliding and pos >= c["slide"] else 0
             gcu.dev_attention_decode(self.xo.view(nh, hdim), self.xq.view(nh, hdim), kc, vc, spos, pos + 1 - spos,
                                      asc, c["sc_att"], stream=stream)
-            # gemma.c:4855-4910: O projection; post-attention norm + residual and
-            # the pre-FFN norm + quantize in one launch
+            # gemma.c:4855-4860: O projection (quantize_act of the attention
+            # output in the same launch)
             gcu.dev_quantize_gemm_int8_multi([(w["wo"][0], w["wo"][1], self.out)], q, self.s, self.xo, 1, q_sz,
                                              stream=stream)
-            gcu.dev_residual_norm_quantize(self.x, q, self.s, self.out, self.x, w["n2"] if c["mlp_pre"] else None,
-                                           w["n3"] if c["mlp_pre"] else w["n2"], eps, 1, dim, stream=stream)
-            # gemma.c:4911-4930: gate/up, GeGLU, down
-            gcu.dev_gemv_int8_multi([(w["w2"][0], w["w2"][1], self.xg), (w["w1"][0], w["w1"][1], self.xu)], q,
-                                    self.s, dim, stream=stream)
-            gcu.dev_geglu_quantize(q, self.s, self.xg, self.xu, 1, mlp, stream=stream)
-            gcu.dev_gemv_int8(self.out, w["w3"][0], w["w3"][1], q, self.s, dim, mlp, stream=stream)
+            # gemma.c:4862-4915: post-attention norm + residual, pre-FFN norm +
+            # quantize, and the gate/up projections -- one launch
+            gcu.dev_residual_norm_quantize_gemv_multi(
+                [(w["w2"][0], w["w2"][1], self.xg), (w["w1"][0], w["w1"][1], self.xu)], xb, q, self.s, self.out, xa,
+                w["n2"] if c["mlp_pre"] else None, w["n3"] if c["mlp_pre"] else w["n2"], eps, dim, stream=stream)
+            xa, xb = xb, xa
+            # gemma.c:4921-4930: GeGLU + quantize and the down projection -- one launch
+            gcu.dev_geglu_quantize_gemv_multi([(w["w3"][0], w["w3"][1], self.out)], q, self.s, self.xg, self.xu,
+                                              mlp, stream=stream)
             # gemma.c:4934-4962: post-FFN norm + residual, with the next layer's
-            # rmsnorm(x, n1) + quantize_act in the same launch
+            # rmsnorm(x, n1) + quantize_act and its Q/K/V projections (4754-4773)
             post = w["n4"] if c["mlp_pst"] else None
             if l + 1 < nl:
-                gcu.dev_residual_norm_quantize(self.x, q, self.s, self.out, self.x, post, self.L[l + 1]["n1"], eps, 1,
-                                               dim, stream=stream)
+                gcu.dev_residual_norm_quantize_gemv_multi(qkv(self.L[l + 1]), xb, q, self.s, self.out, xa, post,
+                                                          self.L[l + 1]["n1"], eps, dim, stream=stream)
             else:
-                gcu.dev_rmsnorm_residual(self.x, self.out, self.x, post, eps, 1, dim, stream=stream)
-        # gemma.c:4965-4976: final norm, tied lm_head, logit softcap
-        gcu.dev_rmsnorm_quantize(q, self.s, self.x, self.fnorm, eps, 1, dim, out=self.x, stream=stream)
+                gcu.dev_rmsnorm_residual(xb, self.out, xa, post, eps, 1, dim, stream=stream)
+            xa, xb = xb, xa
+        # gemma.c:4965-4976: final norm (into x), tied lm_head, logit softcap
+        gcu.dev_rmsnorm_quantize(q, self.s, xa, self.fnorm, eps, 1, dim, out=self.x, stream=stream)
         gcu.dev_gemv_int8(self.logits, self.emb[0], self.emb[1], q, self.s, c["nvocab"], dim, stream=stream)
         if c["sc_log"]:
             gcu.dev_softcap(self.logits, c["sc_log"], stream=stream)
@@ -257,12 +265,15 @@ class Decoder:
             gcu.dev_softcap(self.logits, c["sc_log"], stream=stream)
 
     def launches_per_step(self, prefill: bool = False) -> int:
-        """Kernel launches of one decode step (9 per layer) or one prefill
-        chunk (11 per layer: the chunk merge of the attention and the separate
-        quantize of the O projection's input at m > 8); an attention window
-        split over CTAs adds its merge launch to the decode count."""
-        per = 11 if prefill else 9
-        return per * self.cfg["nl"] + 3 + (1 if self.cfg["sc_log"] else 0)
+        """Kernel launches of one decode step (6 per layer: the residual
+        updates, norms, GeGLU and quantize steps run in front of the GEMVs
+        that consume them, plus the first layer's norm and Q/K/V) or one
+        prefill chunk (11 per layer: the chunk merge of the attention and the
+        separate quantize of the O projection's input at m > 8); an attention
+        window split over CTAs adds its merge launch to the decode count."""
+        if prefill:
+            return 11 * self.cfg["nl"] + 3 + (1 if self.cfg["sc_log"] else 0)
+        return 6 * self.cfg["nl"] + 4 + (1 if self.cfg["sc_log"] else 0)
 
 
 class _null:

@@ -99,6 +99,9 @@ SIGNATURES = {
     "gcu_dev_rmsnorm_residual": (_int, [_vp, _vp, _vp, _vp, ctypes.c_float, _int, _int, _vp]),
     "gcu_dev_softcap": (_int, [_vp, ctypes.c_long, ctypes.c_float, _vp]),
     "gcu_dev_residual_norm_quantize": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_float, _int, _int, _vp]),
+    "gcu_dev_geglu_quantize_gemv_multi": (_int, [ctypes.POINTER(GemvJob), _int, _vp, _vp, _vp, _vp, _int, _vp]),
+    "gcu_dev_residual_norm_quantize_gemv_multi": (_int, [ctypes.POINTER(GemvJob), _int, _vp, _vp, _vp, _vp, _vp,
+                                                         _vp, _vp, ctypes.c_float, _int, _vp]),
     "gcu_dev_qk_norm_rope_cache": (_int, [_vp, _vp, _vp, _vp, _vp, ctypes.c_long, _vp, _vp, ctypes.c_float, _vp,
                                           ctypes.c_float, _int, _int, _int, _int, _int, _vp]),
     "gcu_dev_qkv_norm_rope_cache": (_int, [_vp, _vp, ctypes.c_long, _vp, _vp, ctypes.c_long, _vp, _vp, ctypes.c_float,
@@ -554,6 +557,32 @@ def dev_residual_norm_quantize(x, q, s, y, resid, w_post, w_next, eps, m, dim, s
                                                 resid.data_ptr(), w_post.data_ptr() if w_post is not None else None,
                                                 w_next.data_ptr(), eps, m, dim, _stream(stream)),
            "dev_residual_norm_quantize")
+
+
+def _gemv_jobs(jobs_t):
+    jobs = (GemvJob * len(jobs_t))()
+    for j, (w, sc, o) in enumerate(jobs_t):
+        jobs[j] = GemvJob(w.data_ptr(), sc.data_ptr(), o.data_ptr(), w.shape[0])
+    return jobs
+
+
+def dev_geglu_quantize_gemv_multi(jobs_t, q, s, gate, up, k, stream=None):
+    """One token: h = gelu(gate) * up quantized into (q, s) and every job's
+    GEMV on it, in one launch.  jobs_t: list of (w, sc, dst) device tensors."""
+    jobs = _gemv_jobs(jobs_t)
+    _check(lib().gcu_dev_geglu_quantize_gemv_multi(jobs, len(jobs_t), q.data_ptr(), s.data_ptr(), gate.data_ptr(),
+                                                   up.data_ptr(), k, _stream(stream)), "dev_geglu_quantize_gemv_multi")
+
+
+def dev_residual_norm_quantize_gemv_multi(jobs_t, x, q, s, y, resid, w_post, w_next, eps, dim, stream=None):
+    """One token: x = clamp(resid + rmsnorm(y, w_post)), then rmsnorm(x, w_next)
+    quantized into (q, s) and every job's GEMV on it, in one launch.  x must
+    be a buffer other than resid and y."""
+    jobs = _gemv_jobs(jobs_t)
+    _check(lib().gcu_dev_residual_norm_quantize_gemv_multi(
+        jobs, len(jobs_t), x.data_ptr(), q.data_ptr(), s.data_ptr(), y.data_ptr(), resid.data_ptr(),
+        w_post.data_ptr() if w_post is not None else None, w_next.data_ptr(), eps, dim, _stream(stream)),
+        "dev_residual_norm_quantize_gemv_multi")
 
 
 def dev_qkv_norm_rope_cache(xq, qkv, kc, vc, freqs, spos, n_heads, q_scale=1.0, nq=None, nk=None, eps=1e-6,

@@ -269,6 +269,25 @@ int gcu_dev_rmsnorm_residual(float *x, const float *y, const float *resid, const
 int gcu_dev_residual_norm_quantize(float *x, int8_t *q, float *s, const float *y, const float *resid,
                                    const float *w_post, const float *w_next, float eps, int m, int dim,
                                    void *stream);
+
+/* One token (m = 1): a producer and the decode projection that consumes it in
+ * one launch, every CTA of the GEMV computing the producer row itself.  The
+ * codes, scale and outputs are bit for bit those of the producer call above
+ * followed by gcu_dev_gemv_int8_multi on the same jobs; q and s receive the
+ * codes and scale as the producer call writes them.
+ *   geglu:    h = gelu_tanh(gate) * up over k (gemma.c:4921-4927 then the down
+ *             projection 4929); k % 16 == 0, k <= 16384.
+ *   residual: x = clamp(resid + rmsnorm(y, w_post)), then rmsnorm(x, w_next)
+ *             quantized and multiplied (gemma.c:4862-4915 / 4950-4962 with
+ *             4754-4773); dim % 16 == 0, dim <= 4096.  x must not overlap
+ *             resid or y: every CTA reads those while one CTA writes x.
+ * 16-byte aligned rows and codes.  No single counterpart in the reference. */
+int gcu_dev_geglu_quantize_gemv_multi(const gcu_gemv_job *jobs, int njobs, int8_t *q, float *s,
+                                      const float *gate, const float *up, int k, void *stream);
+int gcu_dev_residual_norm_quantize_gemv_multi(const gcu_gemv_job *jobs, int njobs, float *x, int8_t *q,
+                                              float *s, const float *y, const float *resid,
+                                              const float *w_post, const float *w_next, float eps, int dim,
+                                              void *stream);
 /* gemma.c:4971-4976: x[i] = tanh(x[i] / cap) * cap (the final logit softcap). */
 int gcu_dev_softcap(float *x, long n, float cap, void *stream);
 
