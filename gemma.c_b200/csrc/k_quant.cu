@@ -61,6 +61,9 @@ __global__ void __launch_bounds__(256) k_quant_warps(int8_t *__restrict__ dst,
   const int row = blockIdx.x * kRows + grp;
   const bool live = row < m;  // uniform per warp
   const int n4 = n >> 2;
+  // Start the row's trip from DRAM while the previous kernel finishes: a
+  // prefetch only moves lines into L2, where that kernel's writes land too.
+  if (live && wi == 0 && lane == 0) ptx::bulk_prefetch_l2(src + (size_t)row * sstr, (uint32_t)n * 4u);
   ptx::griddep_wait();
   float4 v[VPT];
   float amax = 0.0f;
@@ -105,6 +108,7 @@ __global__ void __launch_bounds__(1024) k_quant_rows_v4(int8_t *__restrict__ dst
   __shared__ float red[32];
   const int n4 = n >> 2;
   ptx::griddep_launch();
+  if (threadIdx.x == 0 && blockIdx.x < m) ptx::bulk_prefetch_l2(src + (size_t)blockIdx.x * sstr, (uint32_t)n * 4u);
   ptx::griddep_wait();
   for (int row = blockIdx.x; row < m; row += gridDim.x) {
     const float4 *x = reinterpret_cast<const float4 *>(src + (size_t)row * sstr);
