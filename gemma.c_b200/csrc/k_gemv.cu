@@ -488,18 +488,20 @@ int launch_mb(const GemvJobs &jobs, const GemvX &X, int mb, long ystride, int k,
   const int C = k / 16;
   // many activation rows: narrower lane groups keep the reduction short
   if (MB >= 8) return launch_v16<MB, 8, SRC, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
-  if (MB <= 2) {
-    // One or two rows (decode): a weight set that fits the L2 prefetch is
-    // read from L2 after the dependency wait, where each round of loads a
-    // lane waits for costs a round trip.  As many lanes per row as make one
-    // round of U chunks cover the row (the first round is requested before
-    // the activation is quantized), and rounds of 8 chunks past 128 chunks.
-    if (C > 128 && (long)total_rows * k <= kPrefetchMaxBytes)
-      return launch_v16<MB, 32, SRC, P2P, 8>(jobs, X, mb, ystride, k, total_rows, st, po);
+  if (MB <= 2 && (long)total_rows * k <= kPrefetchMaxBytes) {
+    // One or two rows (decode) and a weight set that fits the L2 prefetch:
+    // the rows are read from L2 after the dependency wait, where each round
+    // of loads a lane waits for costs a round trip.  As many lanes per row as
+    // make one round of U chunks cover the row (the first round is requested
+    // before the activation is quantized), and rounds of 8 chunks past 128
+    // chunks.  (A set streamed from DRAM keeps the split below: fewer lanes
+    // per row keep more bytes in flight per warp.)
+    if (C > 128) return launch_v16<MB, 32, SRC, P2P, 8>(jobs, X, mb, ystride, k, total_rows, st, po);
     if (C > 64) return launch_v16<MB, 32, SRC, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
     if (C > 32) return launch_v16<MB, 16, SRC, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
     return launch_v16<MB, 8, SRC, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
   }
+  if (C >= 128 && MB <= 2) return launch_v16<MB, 32, SRC, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
   if (C >= 64) return launch_v16<MB, 16, SRC, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
   return launch_v16<MB, 8, SRC, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
 }
