@@ -159,7 +159,7 @@ __device__ __forceinline__ float block_max256(float v, float *red) {
 // Vector kernel: k % 16 == 0, every weight row and x row 16-byte aligned.
 // VPT: float4 per thread of the producer row (SRC_GEGLU, SRC_RESNORM).
 template <int MB, int LPR, int R, int U, int SRC, bool P2P, int VPT>
-__global__ void __launch_bounds__(kThreads) k_gemv_v16(const GemvJobs jobs, const GemvX X, int mb,
+__global__ void __launch_bounds__(kThreads, (MB == 1 && U == 4 && SRC <= SRC_QUANT) ? 4 : 1) k_gemv_v16(const GemvJobs jobs, const GemvX X, int mb,
                                                        long ystride, int k, int total_rows,
                                                        const PeerOut po) {
   constexpr bool FQ = SRC == SRC_QUANT;
