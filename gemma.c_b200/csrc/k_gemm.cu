@@ -54,17 +54,22 @@ __host__ __device__ constexpr int pow2_at_least(int v) {
   return p;
 }
 
+// A stage holds KG consecutive 128-byte K blocks under one pair of
+// barriers: the MMA issuer's wait on a landed stage and its commit cost a
+// few hundred cycles apiece, so tiles small enough to keep three double
+// stages resident take two K blocks per stage.
 template <int BN, int MB>
 struct Cfg {
   static constexpr int TILE_M = BM * MB;
-  static constexpr int A_BYTES = TILE_M * BK;
+  static constexpr int A_BYTES = TILE_M * BK;  // one K block
   static constexpr int B_BYTES = BN * BK;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int ACC_COLS = MB * BN;  // TMEM columns of one tile
   static constexpr int NBUF = 2 * ACC_COLS <= 512 ? 2 : 1;
   static constexpr int TMEM_COLS = pow2_at_least(NBUF * ACC_COLS);
   static constexpr int EPI_BYTES = kEpiWarps * kEpiStageBytes;
   static constexpr int FIXED = 1024 + EPI_BYTES + 512;
+  static constexpr int KG = (kSmemMax - FIXED) / (2 * (A_BYTES + B_BYTES)) >= 3 ? 2 : 1;
+  static constexpr int STAGE_BYTES = KG * (A_BYTES + B_BYTES);
   static constexpr int STAGES_FIT = (kSmemMax - FIXED) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
@@ -294,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_tc(const __grid_constan
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *smA = smem;
-  uint8_t *smB = smem + C::STAGES * C::A_BYTES;
+  uint8_t *smB = smem + C::STAGES * C::KG * C::A_BYTES;
   uint8_t *epi = smem + C::EPI_OFF;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
   uint64_t *full = bars;
@@ -362,18 +367,23 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_tc(const __grid_constan
         const Unit w = u == (int)blockIdx.x ? w_first : decode_unit(p, u);
         const int kb0 = w.s * p.kb_per_split;
         const int kb1 = min(kb0 + p.kb_per_split, p.kb_total);
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; kb += C::KG, ++it) {
           const int st = it % C::STAGES;
           const uint32_t round = it / C::STAGES;
+          const int nk = min(C::KG, kb1 - kb);  // K blocks in this stage
           if (!ptx::mbar_wait(&empty[st], (round & 1) ^ 1, p.err, DEV_TIMEOUT_EMPTY)) {
             ok = false;
             break;
           }
-          ptx::mbar_arrive_expect_tx(&full[st], C::STAGE_BYTES);
-          ptx::tma_load_2d(&p.tmA, &full[st], smA + st * C::A_BYTES, kb * BK, w.m_t * C::TILE_M,
-                           pol_a);
-          ptx::tma_load_2d(&p.jobs[w.job].tmB, &full[st], smB + st * C::B_BYTES, kb * BK,
-                           w.n_t * BN, pol_b);
+          ptx::mbar_arrive_expect_tx(&full[st], (uint32_t)nk * (C::A_BYTES + C::B_BYTES));
+#pragma unroll
+          for (int g = 0; g < C::KG; ++g) {
+            if (g >= nk) break;
+            ptx::tma_load_2d(&p.tmA, &full[st], smA + (st * C::KG + g) * C::A_BYTES, (kb + g) * BK,
+                             w.m_t * C::TILE_M, pol_a);
+            ptx::tma_load_2d(&p.jobs[w.job].tmB, &full[st], smB + (st * C::KG + g) * C::B_BYTES,
+                             (kb + g) * BK, w.n_t * BN, pol_b);
+          }
         }
       }
       // drain: the last load issued into each stage must have landed before
@@ -401,22 +411,27 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_i8_tc(const __grid_constan
         }
         ptx::tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * C::ACC_COLS;
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; kb += C::KG, ++it) {
           const int st = it % C::STAGES;
           const uint32_t round = it / C::STAGES;
+          const int nk = min(C::KG, kb1 - kb);
           if (!ptx::mbar_wait(&full[st], round & 1, p.err, DEV_TIMEOUT_FULL)) {
             ok = false;
             break;
           }
           ptx::tc_fence_after();
-          const uint32_t a0 = ptx::smem_u32(smA + st * C::A_BYTES);
-          const uint32_t b0 = ptx::smem_u32(smB + st * C::B_BYTES);
 #pragma unroll
-          for (int j = 0; j < BK / 32; ++j)
+          for (int g = 0; g < C::KG; ++g) {
+            if (g >= nk) break;
+            const uint32_t a0 = ptx::smem_u32(smA + (st * C::KG + g) * C::A_BYTES);
+            const uint32_t b0 = ptx::smem_u32(smB + (st * C::KG + g) * C::B_BYTES);
 #pragma unroll
-            for (int mb = 0; mb < MB; ++mb)  // M block mb: A rows 128*mb.., TMEM columns BN*mb..
-              ptx::mma_i8(d_tmem + mb * BN, ptx::smem_desc_k128(a0 + mb * BM * BK + 32 * j),
-                          ptx::smem_desc_k128(b0 + 32 * j), idesc, (kb > kb0 || j > 0) ? 1u : 0u);
+            for (int j = 0; j < BK / 32; ++j)
+#pragma unroll
+              for (int mb = 0; mb < MB; ++mb)  // M block mb: A rows 128*mb.., TMEM columns BN*mb..
+                ptx::mma_i8(d_tmem + mb * BN, ptx::smem_desc_k128(a0 + mb * BM * BK + 32 * j),
+                            ptx::smem_desc_k128(b0 + 32 * j), idesc, (kb + g > kb0 || j > 0) ? 1u : 0u);
+          }
           ptx::mma_commit(&empty[st]);
         }
         ptx::mma_commit(&tfull[buf]);

@@ -158,8 +158,13 @@ __device__ __forceinline__ float block_max256(float v, float *red) {
 
 // Vector kernel: k % 16 == 0, every weight row and x row 16-byte aligned.
 // VPT: float4 per thread of the producer row (SRC_GEGLU, SRC_RESNORM).
+// Register bounds, as measured on the decode steps: the producer-staging
+// variants compile with a minimum of one CTA per SM (more registers, faster
+// staging: 1B step 1023 -> 986 us), the one-row int8 variants with four
+// (64 registers, no spills); the quantize-staging variants keep the
+// compiler's default (one CTA per SM doubled their registers and cost 14 %).
 template <int MB, int LPR, int R, int U, int SRC, bool P2P, int VPT>
-__global__ void __launch_bounds__(kThreads, (MB == 1 && U == 4 && SRC <= SRC_QUANT) ? 4 : 1) k_gemv_v16(const GemvJobs jobs, const GemvX X, int mb,
+__global__ void __launch_bounds__(kThreads, (MB == 1 && U == 4 && SRC == SRC_I8) ? 4 : SRC >= SRC_GEGLU ? 1 : 0) k_gemv_v16(const GemvJobs jobs, const GemvX X, int mb,
                                                        long ystride, int k, int total_rows,
                                                        const PeerOut po) {
   constexpr bool FQ = SRC == SRC_QUANT;
