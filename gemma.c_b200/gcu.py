@@ -248,13 +248,16 @@ def quantize_act(vec: np.ndarray):
     return dst, np.float32(sc)
 
 
-def quantize_acts(src: np.ndarray, n: int | None = None, sstr: int = 0):
-    """gemma.c:2656 on an (m, sstr) fp32 array -> int8 (m, n), fp32 (m,)."""
+def quantize_acts(src: np.ndarray, n: int | None = None, sstr: int = 0, dst=None, dsc=None):
+    """gemma.c:2656 on an (m, sstr) fp32 array -> int8 (m, n), fp32 (m,);
+    dst / dsc: optional output arrays (for instance views of pinned memory)."""
     src = np.ascontiguousarray(src, np.float32)
     m = src.shape[0]
     n = src.shape[1] if n is None else n
-    dst = np.empty((m, n), np.int8)
-    dsc = np.empty(m, np.float32)
+    if dst is None:
+        dst = np.empty((m, n), np.int8)
+    if dsc is None:
+        dsc = np.empty(m, np.float32)
     _check(lib().gcu_quantize_acts(_p(dst), _p(dsc), _p(src), sstr, m, n), "quantize_acts")
     return dst, dsc
 

@@ -181,6 +181,34 @@ def test_gemm_random(m, n, k):
     assert_bits(y, O.gemm_int8(w, ws, xq, xs))
 
 
+@pytest.mark.parametrize("m,n,k,pad", [(4, 4096, 2560, 2), (1, 640, 1024, 0), (300, 1000, 1168, 3),
+                                       (512, 1024, 1152, 0), (512, 1152, 6912, 0), (130, 24, 160, 1),
+                                       (77, 100, 4304, 0), (512, 6912, 1152, 0)])
+def test_host_calls_write_pinned_outputs(m, n, k, pad):
+    # the host-pointer entry points with page-locked caller buffers (the
+    # transfers then run straight from and into them), a padded output
+    # stride, the GEMV, one-CTA, split-K and row-chunked GEMM paths
+    x = synth.activations(3700 + m + k, m, k, outliers=True)
+    w, ws = synth.weight(3701 + n + k, n, k)
+    gcu.register_weight(w, ws)
+    try:
+        q = torch.empty((m, k), dtype=torch.int8, pin_memory=True).numpy()
+        s = torch.empty(m, dtype=torch.float32, pin_memory=True).numpy()
+        dst = torch.full((m, n + pad), float("nan"), dtype=torch.float32, pin_memory=True).numpy()
+        q0, s0 = O.quantize_acts(x)
+        y0 = O.gemm_int8(w, ws, q0, s0)
+        for _ in range(2):
+            q[:] = 99
+            gcu.quantize_acts(x, dst=q, dsc=s)
+            assert np.array_equal(q, q0) and np.array_equal(bits(s), bits(s0))
+            dst[:, :n] = float("nan")
+            gcu.gemm_int8(w, ws, q, s, dst=dst, dstr=n + pad, m=m, n=n, k=k)
+            assert_bits(dst[:, :n], y0)
+            assert np.isnan(dst[:, n:]).all()  # the padding columns are left alone
+    finally:
+        gcu.unregister_weight(w)
+
+
 @pytest.mark.parametrize("m,n,k,pad", [(600, 2500, 640, 0), (300, 4000, 640, 5), (129, 9000, 128, 3)])
 def test_gemm_host_pipelined(m, n, k, pad):
     # > 4 MB of output: the host call runs 128-row chunks whose copies overlap
