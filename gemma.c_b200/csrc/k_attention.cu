@@ -30,6 +30,7 @@
 //   softmax does and accumulates the weights and the weighted V rows in
 //   registers.  Chunks of one query tile are merged in chunk order.
 #include "gcu_internal.cuh"
+#include "rope.cuh"
 
 #include <algorithm>
 #include <cmath>
@@ -89,6 +90,12 @@ struct DecodeArgs {
   float asc, sc_att;
   float *part;  // [splits][n_heads][HD] sums, then [splits][n_heads] max, then weight sums
   unsigned int *err;
+  // ROPE form: xq, xk, xv are the Q/K/V projections as they come out of the
+  // GEMV; every CTA normalises and rotates its group's query heads itself,
+  // and the kv head's last split the new key (and the value) of position
+  // spos + attlen - 1, which it writes into the cache before reading it back
+  const float *xk, *xv, *nq, *nk, *freqs;
+  float eps;
 };
 
 // query heads [h0, h1) of kv head hk (gqa_head_of, gemma.c:2861-2863)
@@ -123,9 +130,10 @@ struct DecSmem {
 
 // smem: the stage ring (reused at the end for the row groups' partial sums),
 // then the scores / weights [GM][chunk]
-template <int HD, int GM>
+template <int HD, int GM, bool ROPE = false>
 __global__ void __launch_bounds__(kDecThreads, GM <= 2 ? 3 : GM <= 4 ? 2 : 1) k_attn_decode(DecodeArgs a) {
   extern __shared__ __align__(128) float sm[];
+  __shared__ __align__(16) float qs[ROPE ? GM * HD : 4];  // the rotated query heads (ROPE form)
   __shared__ __align__(8) uint64_t full[kStages];
   __shared__ float red[kDecThreads / 32][GM];
   __shared__ float stat[2][GM];  // row max, weight sum
@@ -147,6 +155,27 @@ __global__ void __launch_bounds__(kDecThreads, GM <= 2 ? 3 : GM <= 4 ? 2 : 1) k_
   }
   __syncthreads();
   ptx::griddep_wait();
+  if constexpr (ROPE) {
+    // tasks of this CTA, one warp each: the G query heads, then (last split:
+    // it holds the window's last position) the new key and value rows
+    const bool last = split == a.splits - 1;
+    const int pos = a.spos + a.attlen - 1;
+    for (int t = warp; t < G + (last ? 2 : 0); t += kDecThreads / 32) {
+      if (t < G) {
+        rope::norm_rope_row<HD>(a.xq + (size_t)(h0 + t) * HD, a.nq, a.eps, a.freqs, 1.0f, qs + t * HD, lane);
+      } else if (t == G) {
+        rope::norm_rope_row<HD>(a.xk + (size_t)hk * HD, a.nk, a.eps, a.freqs, 1.0f,
+                                const_cast<float *>(a.kc) + (size_t)hk * a.kv_stride + (size_t)pos * HD, lane);
+      } else {
+        rope::copy_row<HD>(a.xv + (size_t)hk * HD,
+                           const_cast<float *>(a.vc) + (size_t)hk * a.kv_stride + (size_t)pos * HD, lane);
+      }
+    }
+    // the cache rows just stored (generic proxy) are read back by this CTA's
+    // bulk copies (async proxy)
+    if (last) asm volatile("fence.proxy.async.global;" ::: "memory");
+    __syncthreads();
+  }
   const uint64_t pol = ptx::policy_evict_first();
   int issued = 0;  // thread 0 only
   auto issue = [&](int j) {
@@ -170,8 +199,9 @@ __global__ void __launch_bounds__(kDecThreads, GM <= 2 ? 3 : GM <= 4 ? 2 : 1) k_
   for (int g = 0; g < GM; ++g)
 #pragma unroll
     for (int i = 0; i < Q4; ++i)
-      q[g][i] = g < G ? __ldg(reinterpret_cast<const float4 *>(a.xq + (size_t)(h0 + g) * HD) + i * 16 + l16)
-                      : make_float4(0.f, 0.f, 0.f, 0.f);
+      q[g][i] = g >= G ? make_float4(0.f, 0.f, 0.f, 0.f)
+                : ROPE ? reinterpret_cast<const float4 *>(qs + g * HD)[i * 16 + l16]
+                       : __ldg(reinterpret_cast<const float4 *>(a.xq + (size_t)(h0 + g) * HD) + i * 16 + l16);
   float wmax[GM];
 #pragma unroll
   for (int g = 0; g < GM; ++g) wmax[g] = -INFINITY;
@@ -683,7 +713,7 @@ __global__ void __launch_bounds__(HD / 4) k_attn_prefill_merge(PrefillArgs a) {
       make_float4(o.x / l, o.y / l, o.z / l, o.w / l);
 }
 
-template <int HD, int GM>
+template <int HD, int GM, bool ROPE>
 cudaError_t launch_decode(const DecodeArgs &a, cudaStream_t st) {
   const size_t smem = DecSmem<HD, GM>::bytes(a.chunk);
   static std::mutex mu;
@@ -694,13 +724,13 @@ cudaError_t launch_decode(const DecodeArgs &a, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     std::lock_guard<std::mutex> lk(mu);
     if (!(done_mask & (1ull << (dev & 63)))) {
-      e = cudaFuncSetAttribute(k_attn_decode<HD, GM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      e = cudaFuncSetAttribute(k_attn_decode<HD, GM, ROPE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)DecSmem<HD, GM>::bytes(kMaxChunk));
       if (e != cudaSuccess) return e;
       done_mask |= 1ull << (dev & 63);
     }
   }
-  cudaError_t e = launch_k(k_attn_decode<HD, GM>, dim3(a.splits, a.nkv), dim3(kDecThreads), smem, st, a);
+  cudaError_t e = launch_k(k_attn_decode<HD, GM, ROPE>, dim3(a.splits, a.nkv), dim3(kDecThreads), smem, st, a);
   if (e != cudaSuccess || a.splits == 1) return e;
   return launch_k(k_attn_combine<HD>, dim3(a.n_heads), dim3(HD), 0, st, a.xo, (const float *)a.part, a.n_heads,
                   a.splits);
@@ -746,19 +776,26 @@ int check_heads(const char *what, int n_heads, int nkv, int hdim) {
 
 using namespace gcu;
 
-GCU_EXPORT int gcu_dev_attention_decode(float *xo, const float *xq, const float *k_cache, const float *v_cache,
-                                        long kv_stride, int n_heads, int nkv, int hdim, int spos, int attlen,
-                                        float asc, float sc_att, void *stream) {
-  if (check_heads("attention_decode", n_heads, nkv, hdim)) return 1;
-  if (!xo || !xq || !k_cache || !v_cache) return set_error("attention_decode: null pointer");
-  if (!aligned16(xo) || !aligned16(xq) || !aligned16(k_cache) || !aligned16(v_cache) || kv_stride % 4)
-    return set_error("attention_decode: buffers must be 16-byte aligned, kv_stride a multiple of 4");
-  if (spos < 0 || attlen < 1 || kv_stride < (long)(spos + attlen) * hdim)
-    return set_error("attention_decode: window [%d, %d) outside a cache of %ld floats per head", spos,
-                     spos + attlen, kv_stride);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  DecodeArgs a{xo, xq, k_cache, v_cache, kv_stride, n_heads, nkv, spos, attlen, 0, 1, asc, sc_att, nullptr,
-               dev_error_word()};
+namespace {
+
+template <bool ROPE>
+cudaError_t launch_decode_hd(const DecodeArgs &a, int hdim, int gmax, cudaStream_t st) {
+  // the group size as a compile-time bound: registers and score storage
+  if (gmax <= 1)
+    return hdim == 256 ? launch_decode<256, 1, ROPE>(a, st) : hdim == 128 ? launch_decode<128, 1, ROPE>(a, st)
+                                                            : launch_decode<64, 1, ROPE>(a, st);
+  if (gmax <= 2)
+    return hdim == 256 ? launch_decode<256, 2, ROPE>(a, st) : hdim == 128 ? launch_decode<128, 2, ROPE>(a, st)
+                                                            : launch_decode<64, 2, ROPE>(a, st);
+  if (gmax <= 4)
+    return hdim == 256 ? launch_decode<256, 4, ROPE>(a, st) : hdim == 128 ? launch_decode<128, 4, ROPE>(a, st)
+                                                            : launch_decode<64, 4, ROPE>(a, st);
+  return hdim == 256 ? launch_decode<256, 8, ROPE>(a, st) : hdim == 128 ? launch_decode<128, 8, ROPE>(a, st)
+                                                          : launch_decode<64, 8, ROPE>(a, st);
+}
+
+int attention_decode(DecodeArgs a, int hdim, cudaStream_t st) {
+  const int n_heads = a.n_heads, nkv = a.nkv, attlen = a.attlen;
   // splits of the window: enough CTAs to stream it at full bandwidth, at
   // least 64 positions each, at most kMaxChunk
   const int target = 2 * num_sms();
@@ -772,19 +809,45 @@ GCU_EXPORT int gcu_dev_attention_decode(float *xo, const float *xq, const float 
     if (gemm_workspace((size_t)a.splits * n_heads * (hdim + 2) * sizeof(float), &ws, &cnt, 0, st)) return 1;
     a.part = static_cast<float *>(ws);
   }
-  // the group size as a compile-time bound: registers and score storage
   const int gmax = (n_heads + nkv - 1) / nkv;
-  cudaError_t e;
-  if (gmax <= 1)
-    e = hdim == 256 ? launch_decode<256, 1>(a, st) : hdim == 128 ? launch_decode<128, 1>(a, st) : launch_decode<64, 1>(a, st);
-  else if (gmax <= 2)
-    e = hdim == 256 ? launch_decode<256, 2>(a, st) : hdim == 128 ? launch_decode<128, 2>(a, st) : launch_decode<64, 2>(a, st);
-  else if (gmax <= 4)
-    e = hdim == 256 ? launch_decode<256, 4>(a, st) : hdim == 128 ? launch_decode<128, 4>(a, st) : launch_decode<64, 4>(a, st);
-  else
-    e = hdim == 256 ? launch_decode<256, 8>(a, st) : hdim == 128 ? launch_decode<128, 8>(a, st) : launch_decode<64, 8>(a, st);
-  GCU_CUDA(e);
+  GCU_CUDA(a.xk ? launch_decode_hd<true>(a, hdim, gmax, st) : launch_decode_hd<false>(a, hdim, gmax, st));
   return 0;
+}
+
+}  // namespace
+
+GCU_EXPORT int gcu_dev_attention_decode(float *xo, const float *xq, const float *k_cache, const float *v_cache,
+                                        long kv_stride, int n_heads, int nkv, int hdim, int spos, int attlen,
+                                        float asc, float sc_att, void *stream) {
+  if (check_heads("attention_decode", n_heads, nkv, hdim)) return 1;
+  if (!xo || !xq || !k_cache || !v_cache) return set_error("attention_decode: null pointer");
+  if (!aligned16(xo) || !aligned16(xq) || !aligned16(k_cache) || !aligned16(v_cache) || kv_stride % 4)
+    return set_error("attention_decode: buffers must be 16-byte aligned, kv_stride a multiple of 4");
+  if (spos < 0 || attlen < 1 || kv_stride < (long)(spos + attlen) * hdim)
+    return set_error("attention_decode: window [%d, %d) outside a cache of %ld floats per head", spos,
+                     spos + attlen, kv_stride);
+  DecodeArgs a{xo, xq, k_cache, v_cache, kv_stride, n_heads, nkv, spos, attlen, 0, 1, asc, sc_att, nullptr,
+               dev_error_word()};
+  return attention_decode(a, hdim, static_cast<cudaStream_t>(stream));
+}
+
+GCU_EXPORT int gcu_dev_attention_decode_rope(float *xo, const float *xq, const float *xk, const float *xv,
+                                             float *k_cache, float *v_cache, long kv_stride, const float *nq,
+                                             const float *nk, float eps, const float *freqs, int n_heads, int nkv,
+                                             int hdim, int spos, int attlen, float asc, float sc_att,
+                                             void *stream) {
+  if (check_heads("attention_decode_rope", n_heads, nkv, hdim)) return 1;
+  if (!xo || !xq || !xk || !xv || !k_cache || !v_cache || !freqs)
+    return set_error("attention_decode_rope: null pointer");
+  if (!aligned16(xo) || !aligned16(xq) || !aligned16(xk) || !aligned16(xv) || !aligned16(k_cache) ||
+      !aligned16(v_cache) || kv_stride % 4 || (uintptr_t)freqs % 8)
+    return set_error("attention_decode_rope: buffers must be 16-byte aligned, kv_stride a multiple of 4");
+  if (spos < 0 || attlen < 1 || kv_stride < (long)(spos + attlen) * hdim)
+    return set_error("attention_decode_rope: window [%d, %d) outside a cache of %ld floats per head", spos,
+                     spos + attlen, kv_stride);
+  DecodeArgs a{xo, xq, k_cache, v_cache, kv_stride, n_heads, nkv, spos, attlen, 0, 1, asc, sc_att, nullptr,
+               dev_error_word(), xk, xv, nq, nk, freqs, eps};
+  return attention_decode(a, hdim, static_cast<cudaStream_t>(stream));
 }
 
 GCU_EXPORT int gcu_dev_attention_prefill(float *xo, int xostr, const float *xq, const float *k_cache,

@@ -12,6 +12,7 @@
 // the same table is used here.  Lane l holds elements [l*P, l*P + P) of a
 // row (P = hdim/32), so the partner of element d < hdim/2 sits in lane l ^ 16.
 #include "gcu_internal.cuh"
+#include "rope.cuh"
 
 #define GCU_EXPORT extern "C" __attribute__((visibility("default")))
 
@@ -39,7 +40,6 @@ struct RopeArgs {
 
 template <int HD>
 __global__ void __launch_bounds__(kRopeThreads) k_qk_norm_rope_cache(RopeArgs a) {
-  constexpr int P = HD / 32;
   ptx::griddep_launch();
   const int lane = threadIdx.x & 31;
   const long row = (long)blockIdx.x * (kRopeThreads / 32) + (threadIdx.x >> 5);
@@ -49,52 +49,18 @@ __global__ void __launch_bounds__(kRopeThreads) k_qk_norm_rope_cache(RopeArgs a)
   if (row >= nq_rows + nk_rows) {  // a value row: straight into the cache
     const long r = row - nq_rows - nk_rows;
     const int h = (int)(r / a.ntok), t = (int)(r - (long)h * a.ntok);
-    const float *src = (a.ld ? a.qkv + t * a.ld + (long)(a.n_heads + a.nkv + h) * HD : a.xv + r * HD) + lane * P;
-    float *dst = a.vc + (size_t)h * a.kv_stride + (size_t)(a.spos + t) * HD + lane * P;
-#pragma unroll
-    for (int i = 0; i < P; i += 2)
-      *reinterpret_cast<float2 *>(dst + i) = __ldg(reinterpret_cast<const float2 *>(src + i));
+    const float *src = a.ld ? a.qkv + t * a.ld + (long)(a.n_heads + a.nkv + h) * HD : a.xv + r * HD;
+    rope::copy_row<HD>(src, a.vc + (size_t)h * a.kv_stride + (size_t)(a.spos + t) * HD, lane);
     return;
   }
   const bool isq = row < nq_rows;
   const long r = isq ? row : row - nq_rows;
   const int h = (int)(r / a.ntok), t = (int)(r - (long)h * a.ntok);
-  const float *src = (a.ld ? a.qkv + t * a.ld + (long)((isq ? 0 : a.n_heads) + h) * HD
-                           : (isq ? a.xq : a.xk) + r * HD) + lane * P;
-  const float *w = isq ? a.nq : a.nk;
-  float v[P];
-#pragma unroll
-  for (int i = 0; i < P; i += 2) {
-    const float2 u = *reinterpret_cast<const float2 *>(src + i);
-    v[i] = u.x;
-    v[i + 1] = u.y;
-  }
-  if (w) {  // gemma.c:2513-2521
-    float sq = 0.0f;
-#pragma unroll
-    for (int i = 0; i < P; ++i) sq += v[i] * v[i];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-    const float rms = 1.0f / sqrtf(sq / (float)HD + a.eps);
-#pragma unroll
-    for (int i = 0; i < P; ++i) v[i] = v[i] * rms * (__ldg(w + lane * P + i) + 1.0f);
-  }
-  // rope_apply: first-half lanes hold a (element d), second-half lanes b
-  // (element d + hdim/2); both use table entry d
-  const float scale = isq ? a.q_scale : 1.0f;
-  const float *fr = a.freqs + (size_t)t * HD + 2 * ((lane & 15) * P);
-  const bool first = lane < 16;
-#pragma unroll
-  for (int i = 0; i < P; ++i) {
-    const float other = __shfl_xor_sync(0xffffffffu, v[i], 16);
-    const float c = __ldg(fr + 2 * i), s = __ldg(fr + 2 * i + 1);
-    const float aa = first ? v[i] : other, bb = first ? other : v[i];
-    v[i] = first ? (aa * c - bb * s) * scale : (aa * s + bb * c) * scale;
-  }
-  float *dst = isq ? a.xq + r * HD + lane * P
-                   : a.kc + (size_t)h * a.kv_stride + (size_t)(a.spos + t) * HD + lane * P;
-#pragma unroll
-  for (int i = 0; i < P; i += 2) *reinterpret_cast<float2 *>(dst + i) = make_float2(v[i], v[i + 1]);
+  const float *src = a.ld ? a.qkv + t * a.ld + (long)((isq ? 0 : a.n_heads) + h) * HD
+                          : (isq ? a.xq : a.xk) + r * HD;
+  float *dst = isq ? a.xq + r * HD : a.kc + (size_t)h * a.kv_stride + (size_t)(a.spos + t) * HD;
+  rope::norm_rope_row<HD>(src, isq ? a.nq : a.nk, a.eps, a.freqs + (size_t)t * HD, isq ? a.q_scale : 1.0f, dst,
+                          lane);
 }
 
 }  // namespace

@@ -127,16 +127,16 @@ class Decoder:
                          (w["wv"][0], w["wv"][1], self.xv)]
         gcu.dev_gemv_int8_multi(qkv(self.L[0]), q, self.s, dim, stream=stream)  # gemma.c:4769-4773
         for l, w in enumerate(self.L):
-            # gemma.c:4775-4818: QK norm, RoPE, cache write
+            # gemma.c:4775-4848: QK norm, RoPE and the cache write of position
+            # pos, then attention over [spos, pos] -- one launch
             kc, vc = self.kv[l, 0], self.kv[l, 1]
             sliding = bool(c["swa"][l])
-            gcu.dev_qk_norm_rope_cache(self.xq, self.xk, self.xv, kc, vc, self.freqs[0 if sliding else 1], pos, 1.0,
-                                       w["nq"] if c["qk_norm"] else None, w["nk"] if c["qk_norm"] else None, eps,
-                                       stream=stream)
-            # gemma.c:4820-4848: attention over [spos, pos]
             spos = pos + 1 - c["slide"] if sliding and pos >= c["slide"] else 0
-            gcu.dev_attention_decode(self.xo.view(nh, hdim), self.xq.view(nh, hdim), kc, vc, spos, pos + 1 - spos,
-                                     asc, c["sc_att"], stream=stream)
+            gcu.dev_attention_decode_rope(self.xo.view(nh, hdim), self.xq.view(nh, hdim), self.xk.view(nkv, hdim),
+                                          self.xv.view(nkv, hdim), kc, vc, self.freqs[0 if sliding else 1], spos,
+                                          pos + 1 - spos, asc, c["sc_att"],
+                                          nq=w["nq"] if c["qk_norm"] else None,
+                                          nk=w["nk"] if c["qk_norm"] else None, eps=eps, stream=stream)
             # gemma.c:4855-4860: O projection (quantize_act of the attention
             # output in the same launch)
             gcu.dev_quantize_gemm_int8_multi([(w["wo"][0], w["wo"][1], self.out)], q, self.s, self.xo, 1, q_sz,
@@ -265,15 +265,16 @@ class Decoder:
             gcu.dev_softcap(self.logits, c["sc_log"], stream=stream)
 
     def launches_per_step(self, prefill: bool = False) -> int:
-        """Kernel launches of one decode step (6 per layer: the residual
+        """Kernel launches of one decode step (5 per layer: the residual
         updates, norms, GeGLU and quantize steps run in front of the GEMVs
-        that consume them, plus the first layer's norm and Q/K/V) or one
-        prefill chunk (11 per layer: the chunk merge of the attention and the
-        separate quantize of the O projection's input at m > 8); an attention
-        window split over CTAs adds its merge launch to the decode count."""
+        that consume them, QK norm and RoPE inside the attention kernel, plus
+        the first layer's norm and Q/K/V) or one prefill chunk (11 per layer:
+        the chunk merge of the attention and the separate quantize of the O
+        projection's input at m > 8); an attention window split over CTAs adds
+        its merge launch to the decode count."""
         if prefill:
             return 11 * self.cfg["nl"] + 3 + (1 if self.cfg["sc_log"] else 0)
-        return 6 * self.cfg["nl"] + 4 + (1 if self.cfg["sc_log"] else 0)
+        return 5 * self.cfg["nl"] + 4 + (1 if self.cfg["sc_log"] else 0)
 
 
 class _null:

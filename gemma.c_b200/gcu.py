@@ -96,6 +96,8 @@ SIGNATURES = {
                                         ctypes.c_float, ctypes.c_float, _vp]),
     "gcu_dev_attention_prefill": (_int, [_vp, _int, _vp, _vp, _vp, ctypes.c_long, _int, _int, _int, _int, _int,
                                          _int, ctypes.c_float, _int, _vp]),
+    "gcu_dev_attention_decode_rope": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_long, _vp, _vp, ctypes.c_float,
+                                             _vp, _int, _int, _int, _int, _int, ctypes.c_float, ctypes.c_float, _vp]),
     "gcu_dev_rmsnorm_residual": (_int, [_vp, _vp, _vp, _vp, ctypes.c_float, _int, _int, _vp]),
     "gcu_dev_softcap": (_int, [_vp, ctypes.c_long, ctypes.c_float, _vp]),
     "gcu_dev_residual_norm_quantize": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_float, _int, _int, _vp]),
@@ -497,6 +499,22 @@ def dev_attention_decode(xo, xq, kc, vc, spos, attlen, asc, sc_att=0.0, stream=N
     _check(lib().gcu_dev_attention_decode(xo.data_ptr(), xq.data_ptr(), kc.data_ptr(), vc.data_ptr(), clen * hdim,
                                           n_heads, nkv, hdim, spos, attlen, asc, sc_att, _stream(stream)),
            "dev_attention_decode")
+
+
+def dev_attention_decode_rope(xo, xq, xk, xv, kc, vc, freqs, spos, attlen, asc, sc_att=0.0, nq=None, nk=None,
+                              eps=1e-6, stream=None):
+    """dev_qk_norm_rope_cache at position spos + attlen - 1 and
+    dev_attention_decode in one launch: xq (n_heads, hdim), xk / xv (nkv,
+    hdim) as the Q/K/V GEMVs wrote them; kc, vc (nkv, clen, hdim); freqs the
+    position's (hdim,) table.  xq is not rotated in place."""
+    n_heads, hdim = xq.shape[-2], xq.shape[-1]
+    nkv, clen, _ = kc.shape
+    _check(lib().gcu_dev_attention_decode_rope(xo.data_ptr(), xq.data_ptr(), xk.data_ptr(), xv.data_ptr(),
+                                               kc.data_ptr(), vc.data_ptr(), clen * hdim,
+                                               nq.data_ptr() if nq is not None else None,
+                                               nk.data_ptr() if nk is not None else None, eps, freqs.data_ptr(),
+                                               n_heads, nkv, hdim, spos, attlen, asc, sc_att, _stream(stream)),
+           "dev_attention_decode_rope")
 
 
 def dev_attention_prefill(xo, xq, kc, vc, spos, slide=0, sc_att=0.0, mask=True, xostr=0, stream=None):

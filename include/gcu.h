@@ -328,6 +328,19 @@ int gcu_dev_qkv_norm_rope_cache(float *xq, const float *qkv, long ld, float *k_c
 int gcu_dev_attention_decode(float *xo, const float *xq, const float *k_cache, const float *v_cache,
                              long kv_stride, int n_heads, int nkv, int hdim, int spos, int attlen,
                              float asc, float sc_att, void *stream);
+/* gcu_dev_qk_norm_rope_cache for one token at position pos = spos+attlen-1
+ * (q_scale 1) followed by gcu_dev_attention_decode, in one launch: xq, xk, xv
+ * are the Q/K/V projections as the GEMVs wrote them ([n_heads][hdim],
+ * [nkv][hdim], [nkv][hdim]); each CTA normalises (nq / nk, NULL = no qk_norm)
+ * and rotates its query heads with freqs (the position's table, hdim floats),
+ * and the last CTA over each kv head's window writes the rotated key and the
+ * value to cache row pos before reading it.  xo, and the cache rows, are bit
+ * for bit those of the two calls; xq is left as it is (the two-call form
+ * rotates it in place).  gemma.c:4775-4848. */
+int gcu_dev_attention_decode_rope(float *xo, const float *xq, const float *xk, const float *xv,
+                                  float *k_cache, float *v_cache, long kv_stride, const float *nq,
+                                  const float *nk, float eps, const float *freqs, int n_heads, int nkv,
+                                  int hdim, int spos, int attlen, float asc, float sc_att, void *stream);
 /* gemma.c:5160-5295: a prefill chunk of ntok tokens at positions
  * [spos, spos+ntok) whose keys and values are already in the cache.  xq
  * [n_heads][ntok][hdim], rotated and scaled by the attention scale

@@ -210,6 +210,43 @@ def test_rope_then_decode_attention_matches_oracle_chain():
     assert_attn_close(xo.cpu().numpy(), want)
 
 
+@pytest.mark.parametrize("nh,nkv,hd,clen,spos,attlen,sc,norm", [
+    (4, 1, 256, 1024, 0, 1024, 0.0, True),       # 1B global layer at position 1023 (split window)
+    (4, 1, 256, 1024, 512, 512, 0.0, True),      # 1B sliding layer: window [512, 1023]
+    (16, 8, 256, 4096, 3072, 1024, 50.0, True),  # 12B-like sliding layer with a score softcap
+    (8, 4, 128, 300, 0, 37, 0.0, False),         # one CTA per kv head, no qk_norm
+    (3, 3, 64, 100, 0, 1, 0.0, True)])           # the new position alone
+def test_fused_rope_decode_equals_two_calls(nh, nkv, hd, clen, spos, attlen, sc, norm):
+    # gcu_dev_attention_decode_rope: QK norm + RoPE + cache write inside the
+    # attention launch; output and cache bit for bit those of the two calls
+    xq, xk, xv, kc, vc, nq, nk = synth.rope_inputs(1000 + attlen, nh, nkv, hd, clen, 1, norm)
+    pos = spos + attlen - 1
+    inv = 10000.0 ** (-np.arange(0, hd, 2, dtype=np.float64) / hd)
+    freqs = np.empty((1, hd), np.float32)
+    freqs[0, 0::2] = np.cos(pos * inv)
+    freqs[0, 1::2] = np.sin(pos * inv)
+    asc = float(np.float32(1.0) / np.sqrt(np.float32(hd)))
+    nqd = dev(nq) if norm else None
+    nkd = dev(nk) if norm else None
+    # two calls
+    q1, k1, v1, kc1, vc1 = dev(xq), dev(xk), dev(xv), dev(kc), dev(vc)
+    gcu.dev_qk_norm_rope_cache(q1, k1, v1, kc1, vc1, dev(freqs), pos, 1.0, nqd, nkd)
+    xo1 = torch.empty((nh, hd), device="cuda")
+    gcu.dev_attention_decode(xo1, q1[:, 0, :].contiguous(), kc1, vc1, spos, attlen, asc, sc)
+    # one launch, twice (the cache row is rewritten with the same values)
+    xq2, kc2, vc2 = dev(xq[:, 0, :]), dev(kc), dev(vc)
+    xo2 = torch.full((nh, hd), float("nan"), device="cuda")
+    for _ in range(2):
+        gcu.dev_attention_decode_rope(xo2, xq2, dev(xk[:, 0, :]), dev(xv[:, 0, :]), kc2, vc2, dev(freqs[0]), spos,
+                                      attlen, asc, sc, nq=nqd, nk=nkd)
+    torch.cuda.synchronize()
+    gcu.check_device()
+    assert torch.equal(xo2.view(torch.int32), xo1.view(torch.int32))
+    assert torch.equal(kc2.view(torch.int32), kc1.view(torch.int32))
+    assert torch.equal(vc2.view(torch.int32), vc1.view(torch.int32))
+    assert np.array_equal(xq2.cpu().numpy(), xq[:, 0, :])  # the projections are inputs only
+
+
 # ---- size-independent properties at full size (no oracle needed)
 
 def test_decode_full_window_is_linear_in_values():
