@@ -467,10 +467,13 @@ __device__ __forceinline__ void tile_scores(const float *qs, const float *ks, in
 #pragma unroll
     for (int c = 0; c < 4; ++c) k[c] = *reinterpret_cast<const float4 *>(kb + 16 * c * KS + d);
   };
+  // packed fp32 multiply-adds (two per instruction): each score keeps the
+  // partial sums over even and odd dimensions, added at the end
+  float2 s2[4][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
-    for (int c = 0; c < 4; ++c) s[i][c] = 0.0f;
+    for (int c = 0; c < 4; ++c) s2[i][c] = make_float2(0.0f, 0.0f);
   float4 q[4], k[4];
   load(q, k, 0);
 #pragma unroll 4
@@ -480,25 +483,23 @@ __device__ __forceinline__ void tile_scores(const float *qs, const float *ks, in
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) s[i][c] += q[i].x * k[c].x;
+      for (int c = 0; c < 4; ++c)
+        s2[i][c] = __ffma2_rn(make_float2(q[i].x, q[i].y), make_float2(k[c].x, k[c].y), s2[i][c]);
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) s[i][c] += q[i].y * k[c].y;
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) s[i][c] += q[i].z * k[c].z;
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) s[i][c] += q[i].w * k[c].w;
+      for (int c = 0; c < 4; ++c)
+        s2[i][c] = __ffma2_rn(make_float2(q[i].z, q[i].w), make_float2(k[c].z, k[c].w), s2[i][c]);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       q[i] = qn[i];
       k[i] = kn[i];
     }
   }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) s[i][c] = s2[i][c].x + s2[i][c].y;
 }
 
 // CTA (64-query tile, head, chunk of the tile's key range).  Thread (ty, tx)
@@ -621,14 +622,15 @@ __global__ void __launch_bounds__(kPreThreads, 1) k_attn_prefill(PrefillArgs a) 
         float4 vn[HD / 64];
         pv_load(pn, vn, j + 1 < jn ? j + 1 : j);
 #pragma unroll
-        for (int c = 0; c < HD / 64; ++c)
+        for (int i = 0; i < 4; ++i) {
+          const float2 pp = make_float2(p[i], p[i]);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            acc[i][c].x += p[i] * v[c].x;
-            acc[i][c].y += p[i] * v[c].y;
-            acc[i][c].z += p[i] * v[c].z;
-            acc[i][c].w += p[i] * v[c].w;
+          for (int c = 0; c < HD / 64; ++c) {  // packed fp32 multiply-adds, two columns each
+            const float2 lo = __ffma2_rn(pp, make_float2(v[c].x, v[c].y), make_float2(acc[i][c].x, acc[i][c].y));
+            const float2 hi = __ffma2_rn(pp, make_float2(v[c].z, v[c].w), make_float2(acc[i][c].z, acc[i][c].w));
+            acc[i][c] = make_float4(lo.x, lo.y, hi.x, hi.y);
           }
+        }
 #pragma unroll
         for (int i = 0; i < 4; ++i) p[i] = pn[i];
 #pragma unroll
