@@ -155,6 +155,21 @@ __global__ void __launch_bounds__(kDecThreads, GM <= 2 ? 3 : GM <= 4 ? 2 : 1) k_
   }
   __syncthreads();
   ptx::griddep_wait();
+  const uint64_t pol = ptx::policy_evict_first();
+  int issued = 0;  // thread 0 only
+  auto issue = [&](int j) {
+    const int tile = j < nt ? j : j - nt;
+    const uint32_t bytes = (uint32_t)min(kTR, n - tile * kTR) * HD * sizeof(float);
+    ptx::mbar_arrive_expect_tx(&full[j % kStages], bytes);
+    ptx::bulk_load(stage + (size_t)(j % kStages) * kTR * HD, (j < nt ? kh : vh) + (size_t)tile * kTR * HD, bytes,
+                   &full[j % kStages], pol);
+  };
+  // The first copies go out before the ROPE form's rotation work, except in
+  // the last split the tile that holds the new position (its last K tile),
+  // which waits until that row is written.
+  const int first = (ROPE && split == a.splits - 1) ? min(kStages, nt - 1) : kStages;
+  if (threadIdx.x == 0)
+    for (; issued < first && issued < nload; ++issued) issue(issued);
   if constexpr (ROPE) {
     // tasks of this CTA, one warp each: the G query heads, then (last split:
     // it holds the window's last position) the new key and value rows
@@ -175,18 +190,9 @@ __global__ void __launch_bounds__(kDecThreads, GM <= 2 ? 3 : GM <= 4 ? 2 : 1) k_
     // bulk copies (async proxy)
     if (last) asm volatile("fence.proxy.async.global;" ::: "memory");
     __syncthreads();
+    if (threadIdx.x == 0)
+      for (; issued < kStages && issued < nload; ++issued) issue(issued);
   }
-  const uint64_t pol = ptx::policy_evict_first();
-  int issued = 0;  // thread 0 only
-  auto issue = [&](int j) {
-    const int tile = j < nt ? j : j - nt;
-    const uint32_t bytes = (uint32_t)min(kTR, n - tile * kTR) * HD * sizeof(float);
-    ptx::mbar_arrive_expect_tx(&full[j % kStages], bytes);
-    ptx::bulk_load(stage + (size_t)(j % kStages) * kTR * HD, (j < nt ? kh : vh) + (size_t)tile * kTR * HD, bytes,
-                   &full[j % kStages], pol);
-  };
-  if (threadIdx.x == 0)
-    for (; issued < kStages && issued < nload; ++issued) issue(issued);
 
   // scores: each half warp takes one row of a tile (16 lanes x HD/64
   // interleaved float4, conflict-free), two rows per warp at a time; a K row
