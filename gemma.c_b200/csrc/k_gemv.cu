@@ -507,6 +507,19 @@ int launch_mb(const GemvJobs &jobs, const GemvX &X, int mb, long ystride, int k,
     return launch_v16<MB, 8, SRC, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
   }
   if (C >= 128 && MB <= 2) return launch_v16<MB, 32, SRC, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
+  if constexpr (MB <= 2 && !P2P) {
+    // A streamed set of narrow rows: enough chunks per lane that one round
+    // of loads covers a row, so each row group waits on one DRAM round trip
+    // (at four a 640-byte row took a second round for its last 8 chunks).
+    const int lpr = C >= 64 ? 16 : 8;
+    const int u = (C + lpr - 1) / lpr;
+    if (u == 5)
+      return lpr == 16 ? launch_v16<MB, 16, SRC, P2P, 5>(jobs, X, mb, ystride, k, total_rows, st, po)
+                       : launch_v16<MB, 8, SRC, P2P, 5>(jobs, X, mb, ystride, k, total_rows, st, po);
+    if (u > 5)
+      return lpr == 16 ? launch_v16<MB, 16, SRC, P2P, 8>(jobs, X, mb, ystride, k, total_rows, st, po)
+                       : launch_v16<MB, 8, SRC, P2P, 8>(jobs, X, mb, ystride, k, total_rows, st, po);
+  }
   if (C >= 64) return launch_v16<MB, 16, SRC, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
   return launch_v16<MB, 8, SRC, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
 }

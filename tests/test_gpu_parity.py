@@ -125,7 +125,9 @@ def test_gemv_multi_golden(golden):
 
 
 @pytest.mark.parametrize("n,k", [(262144, 640), (262144, 2560), (2048, 640), (640, 2048), (1536, 1152),
-                                 (3840, 15360), (1000, 4304), (257, 1024), (77, 48)])
+                                 (3840, 15360), (1000, 4304), (257, 1024), (77, 48),
+                                 # streamed sets whose row fits one round of 5 / 8 chunks per lane
+                                 (262144, 1152), (40000, 896), (20000, 1920)])
 def test_gemv_registered(n, k):
     w, ws = big_weight(2000 + n % 997 + k, n, k)
     gcu.register_weight(w, ws)
@@ -491,7 +493,8 @@ def test_error_reported_for_unsupported_device_call():
 @pytest.mark.parametrize("m,k,rows", [(1, 640, (1024, 256, 256)), (1, 2560, (262144,)), (4, 1152, (2048,)),
                                       (3, 1152, (512, 256)), (300, 1152, (1024, 256, 256)),
                                       (512, 1152, (6912, 6912)), (512, 6912, (1152,)), (1000, 2560, (640,)),
-                                      (6, 40, (48,)), (77, 4304, (100, 60))])
+                                      (6, 40, (48,)), (77, 4304, (100, 60)), (1, 640, (262144,)),
+                                      (2, 1152, (40000,))])
 def test_fused_quantize_gemm(m, k, rows):
     x = synth.activations(9100 + m + k, m, k, outliers=True)
     ws_np = [big_weight(9200 + i + k, n, k) for i, n in enumerate(rows)]
