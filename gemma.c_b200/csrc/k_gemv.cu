@@ -452,10 +452,9 @@ __global__ void __launch_bounds__(kThreads) k_gemv_any(const GemvJobs jobs,
   }
 }
 
-template <int MB, int LPR, int SRC, bool P2P = false, int U = (MB >= 4) ? 2 : 4, int VPT = 0>
+template <int MB, int LPR, int SRC, bool P2P = false, int U = (MB >= 4) ? 2 : 4, int VPT = 0, int R = 2>
 int launch_v16(const GemvJobs &jobs, const GemvX &X, int mb, long ystride, int k, int total_rows,
                cudaStream_t st, const PeerOut *po = nullptr) {
-  constexpr int R = 2;
   auto kern = k_gemv_v16<MB, LPR, R, U, SRC, P2P, VPT>;
   PeerOut pz{};
   const PeerOut &pout = po ? *po : pz;
@@ -487,6 +486,25 @@ int launch_v16(const GemvJobs &jobs, const GemvX &X, int mb, long ystride, int k
   return 0;
 }
 
+// An L2-resident weight set at one activation row: one weight row per lane
+// group instead of two when two would leave half the SMs idle and give each
+// CTA 64 KB or more of weights -- twice the CTAs, each staging the same
+// activation and loading half the weight bytes (1B GeGLU + down, k = 6912:
+// decode step 0.957 -> 0.940 ms).  CTAs with less to load gain nothing from
+// the split (one round of loads either way) and pay for the extra staging
+// (270m decode, 20-32 KB per CTA: 0.2046 -> 0.2080 ms).  Integer sums are
+// exact, so the split does not change the bits.
+template <int MB, int LPR, int SRC, bool P2P, int U = (MB >= 4) ? 2 : 4, int VPT = 0>
+int launch_fill(const GemvJobs &jobs, const GemvX &X, int mb, long ystride, int k, int total_rows,
+                cudaStream_t st, const PeerOut *po = nullptr) {
+  if constexpr (MB == 1 && !P2P) {
+    constexpr long kRowsR1 = (32 / LPR) * (kThreads / 32);
+    if (total_rows <= kRowsR1 * num_sms() && 2 * kRowsR1 * k >= (64L << 10))
+      return launch_v16<MB, LPR, SRC, P2P, U, VPT, 1>(jobs, X, mb, ystride, k, total_rows, st, po);
+  }
+  return launch_v16<MB, LPR, SRC, P2P, U, VPT>(jobs, X, mb, ystride, k, total_rows, st, po);
+}
+
 template <int MB, int SRC, bool P2P = false>
 int launch_mb(const GemvJobs &jobs, const GemvX &X, int mb, long ystride, int k, int total_rows,
               cudaStream_t st, const PeerOut *po = nullptr) {
@@ -501,7 +519,7 @@ int launch_mb(const GemvJobs &jobs, const GemvX &X, int mb, long ystride, int k,
     // before the activation is quantized), and rounds of 8 chunks past 128
     // chunks.  (A set streamed from DRAM keeps the split below: fewer lanes
     // per row keep more bytes in flight per warp.)
-    if (C > 128) return launch_v16<MB, 32, SRC, P2P, 8>(jobs, X, mb, ystride, k, total_rows, st, po);
+    if (C > 128) return launch_fill<MB, 32, SRC, P2P, 8>(jobs, X, mb, ystride, k, total_rows, st, po);
     if (C > 64) return launch_v16<MB, 32, SRC, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
     if (C > 32) return launch_v16<MB, 16, SRC, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
     return launch_v16<MB, 8, SRC, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
@@ -539,7 +557,7 @@ template <int SRC, int VPT>
 int launch_staged(const GemvJobs &jobs, const GemvX &X, int k, int total_rows, cudaStream_t st) {
   const int C = k / 16;
   if (C > 128 && (long)total_rows * k <= kPrefetchMaxBytes)
-    return launch_v16<1, 32, SRC, false, 8, VPT>(jobs, X, 1, 0, k, total_rows, st);
+    return launch_fill<1, 32, SRC, false, 8, VPT>(jobs, X, 1, 0, k, total_rows, st);
   if (C > 64) return launch_v16<1, 32, SRC, false, 4, VPT>(jobs, X, 1, 0, k, total_rows, st);
   if (C > 32) return launch_v16<1, 16, SRC, false, 4, VPT>(jobs, X, 1, 0, k, total_rows, st);
   return launch_v16<1, 8, SRC, false, 4, VPT>(jobs, X, 1, 0, k, total_rows, st);
