@@ -509,6 +509,16 @@ template <int MB, int SRC, bool P2P = false>
 int launch_mb(const GemvJobs &jobs, const GemvX &X, int mb, long ystride, int k, int total_rows,
               cudaStream_t st, const PeerOut *po = nullptr) {
   const int C = k / 16;
+  // A set streamed from DRAM at several activation rows: four chunks per
+  // lane in flight instead of two (the register budget of two was set by
+  // L2-resident sets, where a round trip is short).
+  const bool streamed = (long)total_rows * k > kPrefetchMaxBytes;
+  if constexpr (MB >= 4 && !P2P) {
+    if (streamed) {
+      if (MB >= 8 || C < 64) return launch_v16<MB, 8, SRC, P2P, 4>(jobs, X, mb, ystride, k, total_rows, st, po);
+      return launch_v16<MB, 16, SRC, P2P, 4>(jobs, X, mb, ystride, k, total_rows, st, po);
+    }
+  }
   // many activation rows: narrower lane groups keep the reduction short
   if (MB >= 8) return launch_v16<MB, 8, SRC, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
   if (MB <= 2 && (long)total_rows * k <= kPrefetchMaxBytes) {

@@ -152,6 +152,15 @@ def test_small_batch_gemm_uses_gemv_kernel(m):
     assert_bits(y, O.gemm_int8(w, ws, xq, xs))
 
 
+@pytest.mark.parametrize("m,n,k", [(3, 16384, 2560), (8, 16384, 2560), (6, 60000, 640)])
+def test_small_batch_gemm_streamed_set(m, n, k):
+    # weight sets above the L2 prefetch bound take the four-chunk streaming split
+    w, ws = big_weight(4200 + m + k, n, k)
+    xq, xs = O.quantize_acts(synth.activations(4300 + m, m, k))
+    y = gcu.gemm_int8(w, ws, xq, xs)
+    assert_bits(y, O.gemm_int8(w, ws, xq, xs))
+
+
 # ---------------------------------------------------------------- GEMM
 
 @pytest.mark.parametrize("name", ["gemm_a", "gemm_b", "gemm_d"])
