@@ -180,7 +180,9 @@ __global__ void __launch_bounds__(kThreads, (MB == 1 && U == 4 && SRC == SRC_I8)
   // still orders it after this grid completes.
   ptx::griddep_launch();
   // Small weight sets: warm L2 with this warp's first rows while the previous
-  // kernel finishes (an L2 prefetch cannot expose a stale value).
+  // kernel finishes (an L2 prefetch cannot expose a stale value).  Warming
+  // every row of a warp that reads two row groups measured slower (1B decode
+  // step 0.943 -> 0.951 ms).
   if ((long)total_rows * k <= kPrefetchMaxBytes) {
     const int row = (blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5)) * kRowsPerWarp + lane;
     if (lane < kRowsPerWarp && row < total_rows) {
