@@ -363,21 +363,55 @@ __global__ void __launch_bounds__(kDecThreads, GM <= 2 ? 3 : GM <= 4 ? 2 : 1) k_
 }
 
 // merge the splits of one head in split order: m = max over splits,
-// xo = sum_s e_s * O_s / sum_s e_s * l_s with e_s = fast_expf(m_s - m)
+// xo = sum_s e_s * O_s / sum_s e_s * l_s with e_s = fast_expf(m_s - m).
+// The split maxima and weight sums are read by all threads at once and the
+// e_s staged in shared memory, and each thread keeps eight splits' partial
+// loads in flight, so the merge costs a few L2 round trips rather than one
+// per split; the sums still run in split order.
 template <int HD>
 __global__ void __launch_bounds__(HD) k_attn_combine(float *xo, const float *part, int n_heads, int splits) {
+  __shared__ float s_e[HD], s_l[HD], s_red[HD / 32];
   ptx::griddep_launch();
   const int h = blockIdx.x, d = threadIdx.x;
   const float *pm = part + (size_t)splits * n_heads * HD;
   const float *pl = pm + (size_t)splits * n_heads;
   ptx::griddep_wait();
   float m = -INFINITY;
-  for (int s = 0; s < splits; ++s) m = fmaxf(m, pm[(size_t)s * n_heads + h]);
+  for (int s = d; s < splits; s += HD) m = fmaxf(m, pm[(size_t)s * n_heads + h]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((d & 31) == 0) s_red[d >> 5] = m;
+  __syncthreads();
+  m = s_red[0];
+#pragma unroll
+  for (int w = 1; w < HD / 32; ++w) m = fmaxf(m, s_red[w]);
   float o = 0.0f, l = 0.0f;
-  for (int s = 0; s < splits; ++s) {
-    const float e = dev_fast_expf(pm[(size_t)s * n_heads + h] - m);
-    l += e * pl[(size_t)s * n_heads + h];
-    o += e * part[((size_t)s * n_heads + h) * HD + d];
+  for (int s0 = 0; s0 < splits; s0 += HD) {
+    const int ns = min(HD, splits - s0);
+    __syncthreads();  // the previous group's weights are consumed
+    if (d < ns) {
+      s_e[d] = dev_fast_expf(pm[(size_t)(s0 + d) * n_heads + h] - m);
+      s_l[d] = pl[(size_t)(s0 + d) * n_heads + h];
+    }
+    __syncthreads();
+    const float *ps = part + ((size_t)s0 * n_heads + h) * HD + d;
+    int s = 0;
+    for (; s + 8 <= ns; s += 8) {
+      float v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = ps[(size_t)(s + i) * n_heads * HD];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float e = s_e[s + i];
+        l += e * s_l[s + i];
+        o += e * v[i];
+      }
+    }
+    for (; s < ns; ++s) {
+      const float e = s_e[s];
+      l += e * s_l[s];
+      o += e * ps[(size_t)s * n_heads * HD];
+    }
   }
   xo[(size_t)h * HD + d] = o / l;
 }
