@@ -738,18 +738,41 @@ __global__ void __launch_bounds__(HD / 4) k_attn_prefill_merge(PrefillArgs a) {
   const size_t nrec = (size_t)a.n_heads * a.ntok * a.maxch;
   const float *pm = a.part + nrec * HD, *pl = a.part + nrec * (HD + 1);
   ptx::griddep_wait();
+  // eight chunks' records are requested at a time (every CTA of the launch
+  // is resident at once, so each one's chain of L2 round trips is the
+  // launch's time); the sums still run in chunk order
   float m = -INFINITY;
-  for (int ch = 0; ch < nch; ++ch) m = fmaxf(m, pm[r0 + ch]);
+  for (int ch0 = 0; ch0 < nch; ch0 += 8) {
+    float mv[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) mv[t] = ch0 + t < nch ? pm[r0 + ch0 + t] : -INFINITY;
+#pragma unroll
+    for (int t = 0; t < 8; ++t) m = fmaxf(m, mv[t]);
+  }
   float l = 0.0f;
   float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int ch = 0; ch < nch; ++ch) {
-    const float e = dev_fast_expf(pm[r0 + ch] - m);
-    l += e * pl[r0 + ch];
-    const float4 u = *reinterpret_cast<const float4 *>(a.part + (r0 + ch) * HD + c * 4);
-    o.x += e * u.x;
-    o.y += e * u.y;
-    o.z += e * u.z;
-    o.w += e * u.w;
+  for (int ch0 = 0; ch0 < nch; ch0 += 8) {
+    float ev[8], lv[8];
+    float4 uv[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      if (ch0 + t < nch) {
+        ev[t] = pm[r0 + ch0 + t];
+        lv[t] = pl[r0 + ch0 + t];
+        uv[t] = *reinterpret_cast<const float4 *>(a.part + (r0 + ch0 + t) * HD + c * 4);
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      if (ch0 + t < nch) {
+        const float e = dev_fast_expf(ev[t] - m);
+        l += e * lv[t];
+        o.x += e * uv[t].x;
+        o.y += e * uv[t].y;
+        o.z += e * uv[t].z;
+        o.w += e * uv[t].w;
+      }
+    }
   }
   *reinterpret_cast<float4 *>(a.xo + (size_t)i * a.xostr + (size_t)h * HD + c * 4) =
       make_float4(o.x / l, o.y / l, o.z / l, o.w / l);
