@@ -118,26 +118,26 @@ constexpr int kMaxChunk = 1024;  // window positions per CTA
 constexpr int kTR = 16;     // cache rows per copy
 constexpr int kStages = 4;  // copies in flight per CTA
 
-template <int HD, int GM>
+template <int HD, int GM, int NS = kStages>
 struct DecSmem {
   static constexpr int C4 = HD / 4;            // float4 columns of a row
   static constexpr int R = kDecThreads / C4;   // row groups of the value phase
-  static constexpr size_t region = (size_t)kStages * kTR * HD > (size_t)R * GM * HD
-                                       ? (size_t)kStages * kTR * HD
+  static constexpr size_t region = (size_t)NS * kTR * HD > (size_t)R * GM * HD
+                                       ? (size_t)NS * kTR * HD
                                        : (size_t)R * GM * HD;
   static size_t bytes(int chunk) { return (region + (size_t)GM * chunk) * sizeof(float); }
 };
 
 // smem: the stage ring (reused at the end for the row groups' partial sums),
 // then the scores / weights [GM][chunk]
-template <int HD, int GM, bool ROPE = false>
+template <int HD, int GM, bool ROPE = false, int NS = kStages>
 __global__ void __launch_bounds__(kDecThreads, GM <= 2 ? 3 : GM <= 4 ? 2 : 1) k_attn_decode(DecodeArgs a) {
   extern __shared__ __align__(128) float sm[];
   __shared__ __align__(16) float qs[ROPE ? GM * HD : 4];  // the rotated query heads (ROPE form)
-  __shared__ __align__(8) uint64_t full[kStages];
+  __shared__ __align__(8) uint64_t full[NS];
   __shared__ float red[kDecThreads / 32][GM];
   __shared__ float stat[2][GM];  // row max, weight sum
-  using S = DecSmem<HD, GM>;
+  using S = DecSmem<HD, GM, NS>;
   float *stage = sm, *sc = sm + S::region;
   ptx::griddep_launch();
   const int split = blockIdx.x, hk = blockIdx.y;
@@ -150,7 +150,7 @@ __global__ void __launch_bounds__(kDecThreads, GM <= 2 ? 3 : GM <= 4 ? 2 : 1) k_
   const float *kh = a.kc + (size_t)hk * a.kv_stride + (size_t)(a.spos + c0) * HD;
   const float *vh = a.vc + (size_t)hk * a.kv_stride + (size_t)(a.spos + c0) * HD;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) ptx::mbar_init(&full[s], 1);
+    for (int s = 0; s < NS; ++s) ptx::mbar_init(&full[s], 1);
     ptx::fence_mbar_init();
   }
   __syncthreads();
@@ -160,14 +160,14 @@ __global__ void __launch_bounds__(kDecThreads, GM <= 2 ? 3 : GM <= 4 ? 2 : 1) k_
   auto issue = [&](int j) {
     const int tile = j < nt ? j : j - nt;
     const uint32_t bytes = (uint32_t)min(kTR, n - tile * kTR) * HD * sizeof(float);
-    ptx::mbar_arrive_expect_tx(&full[j % kStages], bytes);
-    ptx::bulk_load(stage + (size_t)(j % kStages) * kTR * HD, (j < nt ? kh : vh) + (size_t)tile * kTR * HD, bytes,
-                   &full[j % kStages], pol);
+    ptx::mbar_arrive_expect_tx(&full[j % NS], bytes);
+    ptx::bulk_load(stage + (size_t)(j % NS) * kTR * HD, (j < nt ? kh : vh) + (size_t)tile * kTR * HD, bytes,
+                   &full[j % NS], pol);
   };
   // The first copies go out before the ROPE form's rotation work, except in
   // the last split the tile that holds the new position (its last K tile),
   // which waits until that row is written.
-  const int first = (ROPE && split == a.splits - 1) ? min(kStages, nt - 1) : kStages;
+  const int first = (ROPE && split == a.splits - 1) ? min(NS, nt - 1) : NS;
   if (threadIdx.x == 0)
     for (; issued < first && issued < nload; ++issued) issue(issued);
   if constexpr (ROPE) {
@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(kDecThreads, GM <= 2 ? 3 : GM <= 4 ? 2 : 1) k_
     if (last) asm volatile("fence.proxy.async.global;" ::: "memory");
     __syncthreads();
     if (threadIdx.x == 0)
-      for (; issued < kStages && issued < nload; ++issued) issue(issued);
+      for (; issued < NS && issued < nload; ++issued) issue(issued);
   }
 
   // scores: each half warp takes one row of a tile (16 lanes x HD/64
@@ -218,13 +218,13 @@ __global__ void __launch_bounds__(kDecThreads, GM <= 2 ? 3 : GM <= 4 ? 2 : 1) k_
 
   int j = 0;
   for (; j < nload; ++j) {
-    const bool ok = ptx::mbar_wait(&full[j % kStages], (j / kStages) & 1, a.err, DEV_TIMEOUT_FULL);
+    const bool ok = ptx::mbar_wait(&full[j % NS], (j / NS) & 1, a.err, DEV_TIMEOUT_FULL);
     if (__syncthreads_or(!ok)) break;  // also: every thread is done with tile j - 1
     if (threadIdx.x == 0 && j >= 1 && issued < nload) {
       ptx::fence_proxy_async_smem();
       issue(issued++);
     }
-    const float *tl = stage + (size_t)(j % kStages) * kTR * HD;
+    const float *tl = stage + (size_t)(j % NS) * kTR * HD;
     const int tile = j < nt ? j : j - nt;
     const int rows = min(kTR, n - tile * kTR);
     if (j < nt) {
@@ -311,7 +311,7 @@ __global__ void __launch_bounds__(kDecThreads, GM <= 2 ? 3 : GM <= 4 ? 2 : 1) k_
     // copies still in flight into this CTA's shared memory, then leave
     if (threadIdx.x == 0)
       for (int jj = j; jj < issued; ++jj)
-        ptx::mbar_wait(&full[jj % kStages], (jj / kStages) & 1, a.err, DEV_TIMEOUT_DRAIN);
+        ptx::mbar_wait(&full[jj % NS], (jj / NS) & 1, a.err, DEV_TIMEOUT_DRAIN);
     return;
   }
   // merge the row groups' sums in row-group order (the ring is free now)
@@ -778,9 +778,9 @@ __global__ void __launch_bounds__(HD / 4) k_attn_prefill_merge(PrefillArgs a) {
       make_float4(o.x / l, o.y / l, o.z / l, o.w / l);
 }
 
-template <int HD, int GM, bool ROPE>
-cudaError_t launch_decode(const DecodeArgs &a, cudaStream_t st) {
-  const size_t smem = DecSmem<HD, GM>::bytes(a.chunk);
+template <int HD, int GM, bool ROPE, int NS>
+cudaError_t launch_decode_ns(const DecodeArgs &a, cudaStream_t st) {
+  const size_t smem = DecSmem<HD, GM, NS>::bytes(a.chunk);
   static std::mutex mu;
   static unsigned long long done_mask = 0;
   {
@@ -789,16 +789,26 @@ cudaError_t launch_decode(const DecodeArgs &a, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     std::lock_guard<std::mutex> lk(mu);
     if (!(done_mask & (1ull << (dev & 63)))) {
-      e = cudaFuncSetAttribute(k_attn_decode<HD, GM, ROPE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)DecSmem<HD, GM>::bytes(kMaxChunk));
+      e = cudaFuncSetAttribute(k_attn_decode<HD, GM, ROPE, NS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)DecSmem<HD, GM, NS>::bytes(kMaxChunk));
       if (e != cudaSuccess) return e;
       done_mask |= 1ull << (dev & 63);
     }
   }
-  cudaError_t e = launch_k(k_attn_decode<HD, GM, ROPE>, dim3(a.splits, a.nkv), dim3(kDecThreads), smem, st, a);
+  cudaError_t e = launch_k(k_attn_decode<HD, GM, ROPE, NS>, dim3(a.splits, a.nkv), dim3(kDecThreads), smem, st, a);
   if (e != cudaSuccess || a.splits == 1) return e;
   return launch_k(k_attn_combine<HD>, dim3(a.n_heads), dim3(HD), 0, st, a.xo, (const float *)a.part, a.n_heads,
                   a.splits);
+}
+
+// A launch of at most one CTA per two SMs (short windows over few kv heads,
+// as in a small model's decode step) takes a ring of eight stages, so all
+// the K and V copies of a 64-position split are in flight at once instead of
+// the V tiles waiting for a second round trip.
+template <int HD, int GM, bool ROPE>
+cudaError_t launch_decode(const DecodeArgs &a, cudaStream_t st) {
+  if (a.splits * a.nkv <= num_sms()) return launch_decode_ns<HD, GM, ROPE, 8>(a, st);
+  return launch_decode_ns<HD, GM, ROPE, kStages>(a, st);
 }
 
 template <int HD>
