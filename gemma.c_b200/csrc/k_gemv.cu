@@ -570,6 +570,12 @@ int launch_staged(const GemvJobs &jobs, const GemvX &X, int k, int total_rows, c
   const int C = k / 16;
   if (C > 128 && (long)total_rows * k <= kPrefetchMaxBytes)
     return launch_fill<1, 32, SRC, false, 8, VPT>(jobs, X, 1, 0, k, total_rows, st);
+  if constexpr (SRC == SRC_RESNORM) {
+    // a streamed set of model-width rows (the 4B / 12B gate + up): one round
+    // of loads per row group, 5 or 8 chunks per lane
+    if (C > 128 && C <= 160) return launch_v16<1, 32, SRC, false, 5, VPT>(jobs, X, 1, 0, k, total_rows, st);
+    if (C > 160 && C <= 256) return launch_v16<1, 32, SRC, false, 8, VPT>(jobs, X, 1, 0, k, total_rows, st);
+  }
   if (C > 64) return launch_v16<1, 32, SRC, false, 4, VPT>(jobs, X, 1, 0, k, total_rows, st);
   if (C > 32) return launch_v16<1, 16, SRC, false, 4, VPT>(jobs, X, 1, 0, k, total_rows, st);
   return launch_v16<1, 8, SRC, false, 4, VPT>(jobs, X, 1, 0, k, total_rows, st);

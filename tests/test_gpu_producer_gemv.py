@@ -86,7 +86,9 @@ def test_geglu_gemv_equals_two_launches(k, ns):
 
 @pytest.mark.parametrize("dim,ns,post", [(640, (2048, 2048), True), (1152, (1024, 256, 256), True),
                                          (1152, (6912, 6912), False), (2560, (2048, 1024, 1024), True),
-                                         (3840, (4096,), True), (4096, (32,), False), (48, (16,), True)])
+                                         (3840, (4096,), True), (4096, (32,), False), (48, (16,), True),
+                                         # streamed weight sets (over 32 MB): one round of 5 / 8 chunks
+                                         (2560, (10240, 10240), True), (3840, (15360,), False)])
 def test_residual_norm_gemv_equals_two_launches(dim, ns, post):
     gen = torch.Generator(device="cuda").manual_seed(dim + len(ns))
     y = synth.activations_torch(1, dim, gen, "cuda", outliers=True)
