@@ -536,6 +536,8 @@ int launch_mb(const GemvJobs &jobs, const GemvX &X, int mb, long ystride, int k,
     if (C > 32) return launch_v16<MB, 16, SRC, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
     return launch_v16<MB, 8, SRC, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
   }
+  // (rows of 129-160 chunks in one round of 5 chunks per lane measured the
+  // same on the 4B lm_head, already at the copy rate)
   if (C >= 128 && MB <= 2) return launch_v16<MB, 32, SRC, P2P>(jobs, X, mb, ystride, k, total_rows, st, po);
   if constexpr (MB <= 2 && !P2P) {
     // A streamed set of narrow rows: enough chunks per lane that one round
