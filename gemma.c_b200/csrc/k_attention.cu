@@ -111,8 +111,8 @@ constexpr int kMaxChunk = 1024;  // window positions per CTA
 
 // Cache tiles move by 1D bulk copies (positions of one kv head are
 // contiguous in the cache) through a ring of NS shared-memory stages (kStages,
-// or eight when the launch has at most one CTA per SM): the K tiles of the
-// CTA's slice, then its V tiles.  Thread 0 keeps NS copies in flight; every thread waits on a tile's mbarrier, and one CTA
+// or more when the launch has few CTAs per SM): the K tiles of the CTA's
+// slice, then its V tiles.  Thread 0 keeps NS copies in flight; every thread waits on a tile's mbarrier, and one CTA
 // barrier per tile both agrees on the outcome of the (bounded) wait and
 // frees the previous tile's stage for the next copy.
 constexpr int kTR = 16;     // cache rows per copy
@@ -801,13 +801,16 @@ cudaError_t launch_decode_ns(const DecodeArgs &a, cudaStream_t st) {
                   a.splits);
 }
 
-// A launch of at most one CTA per two SMs (short windows over few kv heads,
-// as in a small model's decode step) takes a ring of eight stages, so all
-// the K and V copies of a 64-position split are in flight at once instead of
-// the V tiles waiting for a second round trip.
+// A launch of at most one CTA per SM (short windows over few kv heads, as in
+// a small model's decode step) takes a ring of eight stages, so all the K and
+// V copies of a 64-position split are in flight at once instead of the V
+// tiles waiting for a second round trip; one of up to two CTAs per SM takes
+// six when two such CTAs still fit on an SM.
 template <int HD, int GM, bool ROPE>
 cudaError_t launch_decode(const DecodeArgs &a, cudaStream_t st) {
   if (a.splits * a.nkv <= num_sms()) return launch_decode_ns<HD, GM, ROPE, 8>(a, st);
+  if (a.splits * a.nkv <= 2 * num_sms() && 2 * (DecSmem<HD, GM, 6>::bytes(a.chunk) + 1024) <= 228 * 1024)
+    return launch_decode_ns<HD, GM, ROPE, 6>(a, st);
   return launch_decode_ns<HD, GM, ROPE, kStages>(a, st);
 }
 
