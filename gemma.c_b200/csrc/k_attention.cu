@@ -112,9 +112,10 @@ constexpr int kMaxChunk = 1024;  // window positions per CTA
 // Cache tiles move by 1D bulk copies (positions of one kv head are
 // contiguous in the cache) through a ring of NS shared-memory stages (kStages,
 // or more when the launch has few CTAs per SM): the K tiles of the CTA's
-// slice, then its V tiles.  Thread 0 keeps NS copies in flight; every thread waits on a tile's mbarrier, and one CTA
-// barrier per tile both agrees on the outcome of the (bounded) wait and
-// frees the previous tile's stage for the next copy.
+// slice, then its V tiles.  Thread 0 keeps NS copies in flight; every thread
+// waits on a tile's mbarrier, and one CTA barrier per tile both agrees on the
+// outcome of the (bounded) wait and frees the previous tile's stage for the
+// next copy.
 constexpr int kTR = 16;     // cache rows per copy
 constexpr int kStages = 4;  // copies in flight per CTA
 
