@@ -23,7 +23,8 @@ Workloads (synthetic seeded data, no checkpoints):
               FFN rows are sharded over the ranks and every FFN output is
               all-gathered (strong scaling).
   decode12b   configs[4] decode: Gemma-3-12B, batch 1, 48 layers + lm_head;
-              at N>1 the FFN and lm_head rows are sharded (strong scaling).
+              at N>1 the lm_head rows, and at N>=4 the FFN rows too, are
+              sharded (strong scaling).
   upload1b    not a BASELINE metric: gcu_register_model of a synthetic `-q`
   upload4b    model image (1B text / 4B text + SigLIP), GB/s of matmul
               weights into HBM against the measured PCIe copy rate.
@@ -492,8 +493,12 @@ class Prefill:
         return ops, run
 
 
+# The decode FFN rows are sharded from this many GPUs on: below it the
+# per-layer all-gathers cost more than the smaller FFN slices save.
+FFN_SHARD_MIN_GPUS = 4
+
 DECODE = {
-    # name: (configs index, model, layer count, FFN + lm_head rows sharded)
+    # name: (configs index, model, rows sharded at N > 1)
     "decode270m": (0, "270m", False),
     "decode12b": (4, "12b", True),
 }
@@ -502,9 +507,12 @@ DECODE = {
 class Decode:
     """Decode, batch 1 (configs[0], and configs[4]'s decode half): every
     layer's quantize_act -> Q/K/V, O, gate/up, down GEMVs, then the
-    262144-row lm_head.  Sharded workloads split the FFN and lm_head rows
-    over the ranks with the all-gather fused into the GEMV when the peers are
-    mapped (gcu_dev_gemm_int8_rowshard); Q/K/V/O stay replicated."""
+    262144-row lm_head.  Sharded workloads split the lm_head rows over the
+    ranks, and from FFN_SHARD_MIN_GPUS ranks on the FFN rows too, with the
+    all-gather fused into the GEMV when the peers are mapped
+    (gcu_dev_gemm_int8_rowshard); Q/K/V/O stay replicated.  (At 2 GPUs the
+    per-layer FFN all-gathers cost more than the halved FFN slices save:
+    12B step 2.69 ms with them against 2.565 ms on one GPU.)"""
 
     def __init__(self, name="decode270m", seed=0, fused=True, world=1, rank=0, layers=0):
         import synth
@@ -513,6 +521,7 @@ class Decode:
         self.fused = fused
         self.world, self.rank = world, rank
         self.shard = shard and world > 1
+        self.shard_ffn = self.shard and world >= FFN_SHARD_MIN_GPUS
         self.needs_comm = self.shard
         self.cfg = synth.CONFIGS[cfg]
         self.groups = synth.layer_groups(self.cfg)
@@ -531,7 +540,8 @@ class Decode:
                       "quantize_act and gemv_int8(_multi) as separate launches"}
         if self.shard:
             ag = "fused into the GEMV (NVLink peer loads)" if gcu.comm_fused_allgather() else "NCCL"
-            c["sharding"] = (f"FFN and lm_head rows over {self.world} GPUs, all-gather {ag}; "
+            rows = "FFN and lm_head rows" if self.shard_ffn else "lm_head rows (FFN replicated below 4 GPUs)"
+            c["sharding"] = (f"{rows} over {self.world} GPUs, all-gather {ag}; "
                              "Q/K/V/O replicated (counted once in value)")
         return c
 
@@ -553,7 +563,7 @@ class Decode:
         for _ in range(self.layers):
             layer = []
             for k, jobs in self.groups:
-                sh = self.shard and all(is_ffn(nm) for nm, _ in jobs)
+                sh = self.shard_ffn and all(is_ffn(nm) for nm, _ in jobs)
                 layer.append({"x": synth.activations_torch(1, k, gen, device),
                               "q": torch.empty(k, dtype=torch.int8, device=device),
                               "s": torch.empty(1, dtype=torch.float32, device=device), "k": k, "shard": sh,
@@ -633,7 +643,7 @@ class Decode:
             return (self.layers * len(self.groups) + 1) * (1 if self.fused else 2)
         n = 1  # lm_head: one fused quantize + sharded GEMV
         for k, jobs in self.groups:
-            if all(is_ffn(nm) for nm, _ in jobs):
+            if self.shard_ffn and all(is_ffn(nm) for nm, _ in jobs):
                 n += self.layers
             else:
                 n += self.layers * (1 if self.fused else 2)
