@@ -879,11 +879,11 @@ int attention_decode(DecodeArgs a, int hdim, cudaStream_t st) {
   // least 64 positions each, at most kMaxChunk
   const int target = 2 * num_sms();
   int splits = attlen <= 64 ? 1 : std::min((attlen + 63) / 64, std::max(1, (target + nkv - 1) / nkv));
-  // A launch that would fill at most half the SMs (a small model's windows
-  // over few kv heads) takes 32-position splits: twice the CTAs, each with
-  // four copies in flight (1B decode step 0.922 -> 0.868 ms, 4B 1.769 ->
-  // 1.742 ms).
-  if (attlen > 64 && 2 * splits * nkv <= num_sms())
+  // A launch that would have at most one CTA per SM (a small model's windows
+  // over few kv heads, the 12B sliding layers) takes 32-position splits:
+  // twice the CTAs, each with four copies in flight (1B decode step 0.922 ->
+  // 0.868 ms, 4B 1.769 -> 1.742 ms, 12B attention 1.139 -> 1.130 ms).
+  if (attlen > 64 && splits * nkv <= num_sms())
     splits = std::min((attlen + 31) / 32, std::max(1, (target + nkv - 1) / nkv));
   splits = std::max(splits, (attlen + kMaxChunk - 1) / kMaxChunk);
   a.chunk = (attlen + splits - 1) / splits;
